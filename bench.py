@@ -1,0 +1,410 @@
+#!/usr/bin/env python
+"""Embedding rows/s per round (pull + push + LazyAdam) on B200.
+
+One *round* (= one bench step) over the configured synthetic batch is: one
+lookup (gather + sum/mean pooling of every feature, occurrence list and its
+coalescing sort) and one push (gradient prescan, coalesced segment-sum fused
+with the sparse LazyAdam update, finalize).  rows = id occurrences processed per
+round (each is pulled once and contributes one gradient).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--config 1|2|4]
+
+value  : rows/s with inputs resident in HBM, device-timed with CUDA events on
+         the launching stream, L2 flushed (256 MiB write) before every timed
+         round, summed over the K rounds; max over ranks when N > 1.
+e2e    : the same rounds through the C ABI with HOST (pinned) buffers: keys and
+         offsets copied in, pooled outputs copied out, gradients copied in and
+         the push status read back, all inside the timed region.
+roofline: the dominant phase's algorithmic bytes per launch (per-row byte
+         counts below) over its event-timed duration, against the measured HBM
+         copy bandwidth in MEASURED_PEAKS.json.
+cpu_baseline / --impl reference: the UNMODIFIED reference CPU parameter server
+         (oracle/_ref, compiled from its own sources) with one shard per host
+         core behind its DistributedClient, timed wall-clock on the same batch.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "tests"))
+METRIC = "embedding rows/s per round (pull+push+Adam)"
+UNIT = "rows/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def _import_package():
+    import importlib.util
+    pkg = os.path.join(ROOT, "distributed-recommendation-model-training-system_b200")
+
+    def load(name, path, package=False):
+        if name in sys.modules:
+            return sys.modules[name]
+        kw = {"submodule_search_locations": [pkg]} if package else {}
+        spec = importlib.util.spec_from_file_location(name, path, **kw)
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules[name] = mod
+        spec.loader.exec_module(mod)
+        return mod
+
+    workloads = load("eps_b200_workloads", os.path.join(pkg, "workloads.py"))
+    if os.environ.get("EPS_B200_NO_PACKAGE"):
+        return workloads, None
+    return workloads, load("eps_b200", os.path.join(pkg, "__init__.py"), package=True)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 4])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+            int(os.environ.get("WORLD_SIZE", 1)))
+
+
+def workload_for(wl, config, rank):
+    if config == 1:
+        return wl.config1(seed=1 + 1000 * rank)
+    if config == 4:
+        return wl.config4(seed=4 + 1000 * rank)
+    return wl.config2(seed=2 + 1000 * rank)
+
+
+def byte_model(w):
+    """Compulsory bytes (each byte that must cross HBM once; sort scratch excluded)."""
+    N = w.occurrences
+    rows_out = w.bags                                    # output / gradient rows
+    pooled_offsets = sum(len(f.offsets) for f in w.features if f.pooling != 2)
+    dims = {t.id: t.dimension for t in w.tables}
+    U_by_dim = {}
+    for t in w.tables:
+        ks = [f.keys for f in w.features if f.table == t.id]
+        if ks:
+            U_by_dim[t.id] = len(np.unique(np.concatenate(ks)))
+    U = sum(U_by_dim.values())
+    row_bytes_u = sum(4 * dims[t] * u for t, u in U_by_dim.items())        # 4D per unique row
+    out_bytes = sum(4 * dims[f.table] * f.output_rows for f in w.features)  # 4D per output row
+    pull = 8 * N + 8 * pooled_offsets + row_bytes_u + out_bytes
+    push = out_bytes + 8 * N + 8 * pooled_offsets + 6 * row_bytes_u + 16 * U
+    lookup_kernel = pull
+    apply_kernel = out_bytes + 8 * N + 6 * row_bytes_u + 16 * U
+    prescan_kernel = out_bytes
+    return {"N": N, "U": U, "B": rows_out, "pull": pull, "push": push,
+            "lookup": lookup_kernel, "apply": apply_kernel, "prescan": prescan_kernel,
+            "sort": 0}
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def load_traffic():
+    """ncu DRAM bytes per launch of each phase, from the committed summary."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, local_rank):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        self.index = vis.split(",")[local_rank] if vis else str(local_rank)
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.out = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", self.index, f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.out, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.out.close()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 8:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[4:8]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# --------------------------------------------------------------- reference arm
+def reference_rounds(w, steps, warmup, threads):
+    """Times the reference's CPU path (oracle/_ref) on the batch; returns seconds per round."""
+    from oracle_lib import Feature, Reference, TableDef, reference_available
+    if not reference_available():
+        return None
+    tables = [TableDef(id=t.id, dimension=t.dimension, learning_rate=1e-3, init_min=-0.05,
+                       init_max=0.05, init_seed=42, rows=t.rows) for t in w.tables]
+    feats = [Feature(f.table, f.feature, f.pooling, f.keys, f.offsets) for f in w.features]
+    ref = Reference(tables, shards=threads, state_bytes=64 << 30)
+    times = []
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        batch, _ = ref.lookup(feats)
+        ref.push(batch, feats, w.gradients)
+        dt = time.perf_counter() - t0
+        if i >= warmup:
+            times.append(dt)
+    ref.close()
+    return times
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def run_reference(args):
+    rank, local_rank, world = dist_env()
+    if rank != 0:
+        return
+    wl, _ = _import_package()
+    w = workload_for(wl, args.config, 0)
+    threads = host_threads()
+    times = reference_rounds(w, args.steps, args.warmup, threads)
+    if times is None:
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "reference CPU build oracle/_ref/libeps_ref.so is missing"}))
+        return
+    total = sum(times)
+    value = w.occurrences * len(times) / total
+    sample = (f"{len(times)} full rounds of {w.name} ({w.occurrences} occurrences each) after "
+              f"{args.warmup} warm-up rounds, {threads} shards/threads")
+    print(json.dumps({
+        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+        "steps": len(times), "warmup": args.warmup, "ms_per_step": 1e3 * total / len(times),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": w.name, "parallelism": f"cpu x{threads}"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+
+
+# ------------------------------------------------------------------- B200 arm
+def run_b200(args):
+    import torch
+    rank, local_rank, world = dist_env()
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device(f"cuda:{local_rank}"))
+    wl, eps = _import_package()
+    w = workload_for(wl, args.config, rank)
+    bm = byte_model(w)
+    dev = torch.device(f"cuda:{local_rank}")
+    store = eps.ParameterStore(device=local_rank, state_bytes=150 << 30)
+    for t in w.tables:
+        store.create_table(eps.TableDefinition(id=t.id, dimension=t.dimension, key_space=t.rows,
+                                               learning_rate=1e-3))
+    stream = torch.cuda.current_stream()
+
+    # ---- device-resident inputs
+    feats = [eps.FeatureInput(f.table, f.feature, f.pooling,
+                              torch.from_numpy(f.keys.astype(np.int64)).to(dev),
+                              torch.from_numpy(f.offsets.astype(np.int64)).to(dev))
+             for f in w.features]
+    dims = {t.id: t.dimension for t in w.tables}
+    outs = [torch.empty((f.output_rows, dims[f.table]), dtype=torch.float32, device=dev)
+            for f in w.features]
+    grads = [torch.from_numpy(g).to(dev) for g in w.gradients]
+    lookup = store.prepare_lookup(feats, outs)
+    push = store.prepare_push(grads)
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)   # 256 MiB > 126 MB L2
+
+    def one_round():
+        ticket = lookup(stream)
+        push(ticket, stream, wait=False)
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        one_round()
+    store.synchronize()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks = Clocks(local_rank)
+    clocks.start()
+    store.profile(1)
+    launches0 = store.stats()["kernel_launches"]
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    for a, b in events:
+        flush.zero_()
+        a.record(stream)
+        one_round()
+        b.record(stream)
+    torch.cuda.synchronize()
+    store.synchronize()
+    if dist:
+        dist.barrier()
+    clk = clocks.stop()
+    prof = store.profile(0)
+    launches = store.stats()["kernel_launches"] - launches0
+    total_ms = sum(a.elapsed_time(b) for a, b in events)
+    if dist:
+        t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    value = bm["N"] * args.steps * world / (total_ms / 1e3)
+
+    # ---- roofline of the dominant phase
+    peak, peak_kind = load_peaks()
+    dom = max((p for p in prof if p in ("lookup", "apply", "sort", "prescan")),
+              key=lambda p: prof[p]["ms"])
+    calls = max(1, prof[dom]["calls"])
+    per_call_ms = prof[dom]["ms"] / calls
+    alg = bm[dom]
+    achieved = alg / (per_call_ms / 1e3) / 1e9 if alg else 0.0
+    traffic = load_traffic().get(f"cfg{args.config}", {}).get(dom)
+    phases = {p: {"ms_per_round": prof[p]["ms"] / max(1, prof[p]["calls"]),
+                  "launches_per_round": prof[p]["launches"] / max(1, prof[p]["calls"]),
+                  "alg_GBps": (bm[p] / (prof[p]["ms"] / max(1, prof[p]["calls"]) / 1e3) / 1e9)
+                  if bm.get(p) and prof[p]["ms"] else None} for p in prof}
+
+    # ---- e2e through the C ABI with pinned host buffers
+    def pinned(a):
+        t = torch.empty(a.shape, dtype=torch.from_numpy(a[:0]).dtype, pin_memory=True)
+        t.numpy()[...] = a
+        return t.numpy()
+
+    hfeats = [eps.FeatureInput(f.table, f.feature, f.pooling, pinned(f.keys), pinned(f.offsets))
+              for f in w.features]
+    houts = [pinned(np.zeros((f.output_rows, dims[f.table]), np.float32)) for f in w.features]
+    hgrads = [pinned(g) for g in w.gradients]
+    hlookup = store.prepare_lookup(hfeats, houts)
+    hpush = store.prepare_push(hgrads)
+    e2e_steps = max(3, args.steps // 2)
+    for _ in range(2):
+        hpush(hlookup(stream), stream, wait=True)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(e2e_steps)]
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    for a, b in ev:
+        flush.zero_()
+        a.record(stream)
+        hpush(hlookup(stream), stream, wait=True)
+        b.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = sum(a.elapsed_time(b) for a, b in ev)
+    if dist:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = bm["N"] * e2e_steps * world / (e2e_ms / 1e3)
+    h2d = sum(f.keys.nbytes + f.offsets.nbytes for f in w.features) + \
+        sum(g.nbytes for g in w.gradients)
+    d2h = sum(o.nbytes for o in houts) + 36      # pooled outputs + push status
+    store.close()
+
+    # ---- CPU baseline (rank 0, N = 1): reference CPU path, bounded sample
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = host_threads()
+        times = reference_rounds(w, steps=2, warmup=1, threads=threads)
+        if times:
+            cpu = {"value": w.occurrences * len(times) / sum(times), "unit": UNIT,
+                   "cores": threads, "kind": "reference",
+                   "sample": f"{len(times)} full rounds of the same batch after 1 warm-up round "
+                             f"(reference DistributedClient over {threads} CpuParameterService "
+                             f"shards, one per host thread)"}
+
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": w.name, "occurrences_per_round": bm["N"],
+                   "unique_rows_per_round": bm["U"], "output_rows_per_round": bm["B"],
+                   "compulsory_bytes_per_round": bm["pull"] + bm["push"],
+                   "l2": "flushed (256 MiB write) before every timed round",
+                   "parallelism": "single GPU" if world == 1 else f"{world} replicas"},
+        "unique_rows_per_s": bm["U"] * args.steps * world / (total_ms / 1e3),
+        "round_hbm_frac": ((bm["pull"] + bm["push"]) * args.steps / (total_ms / 1e3) / 1e9) / peak,
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": traffic, "alg_bytes_per_launch": alg},
+        "phases": phases,
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches,
+        "clocks": clk,
+    }
+    print(json.dumps(line))
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,434 @@
+"""Python binding of the B200 embedding parameter store (libeps_b200.so).
+
+Mirrors the reference parameter server's shard/client interface
+(include/eps/parameter_service.hpp, include/eps/distributed_client.hpp):
+
+    store = ParameterStore(device=0)
+    store.create_table(TableDefinition(id=1, dimension=64, ...))
+    ticket, outputs = store.lookup([FeatureInput(table=1, feature=0, pooling=SUM,
+                                                 keys=..., offsets=...)])
+    store.push(ticket, gradients)          # coalesce + segment-sum + LazyAdam
+    store.release(ticket)                  # for an abandoned lookup
+
+Host (numpy) and device (torch CUDA tensor) inputs are both accepted; the
+library itself runs only the hand-written sm_100a kernels.  There is no CPU
+fallback: importing this package fails loudly if the native library is missing,
+and every call fails with the library's own error when no GPU is present.
+Errors raise ``EpsError`` whose ``code`` is eps::Error::Code + 1
+(include/eps/types.hpp:17-25).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass
+from typing import Sequence
+
+import numpy as np
+
+__all__ = ["ParameterStore", "TableDefinition", "FeatureInput", "EpsError", "SUM", "MEAN",
+           "SEQUENCE", "library_path", "load_library"]
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(HERE, "libeps_b200.so")
+
+SUM, MEAN, SEQUENCE = 0, 1, 2
+INVALID_ARGUMENT, UNAVAILABLE, STALE_GENERATION, RETIRED_REQUEST, CAPACITY_EXCEEDED, RUN_FAILED = range(1, 7)
+
+
+def library_path() -> str:
+    return _LIB_PATH
+
+
+class EpsError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"[{code}] {message}")
+        self.code = code
+        self.message = message
+
+
+# ------------------------------------------------------------------ C structs
+class Status(C.Structure):
+    _fields_ = [("code", C.c_int32), ("message", C.c_char * 1024)]
+
+
+class Options(C.Structure):
+    _fields_ = [("device", C.c_int32), ("shard_id", C.c_uint32), ("shard_count", C.c_uint32),
+                ("max_live_tickets", C.c_uint32), ("partition_epoch", C.c_uint64),
+                ("state_bytes", C.c_uint64), ("flags", C.c_uint32), ("reserved", C.c_uint32)]
+
+
+FLAG_REFERENCE_ORDER = 1
+
+
+class Table(C.Structure):
+    _fields_ = [("id", C.c_uint32), ("dimension", C.c_uint32), ("shard_count", C.c_uint32),
+                ("has_weight_bounds", C.c_int32), ("partition_epoch", C.c_uint64),
+                ("learning_rate", C.c_float), ("beta1", C.c_float), ("beta2", C.c_float),
+                ("epsilon", C.c_float), ("initial_beta1_power", C.c_float),
+                ("initial_beta2_power", C.c_float), ("weight_min", C.c_float),
+                ("weight_max", C.c_float), ("initialization_min", C.c_float),
+                ("initialization_max", C.c_float), ("initialization_seed", C.c_uint64),
+                ("key_space", C.c_uint64)]
+
+
+class Feature(C.Structure):
+    _fields_ = [("table", C.c_uint32), ("feature", C.c_uint32), ("pooling", C.c_uint32),
+                ("reserved", C.c_uint32), ("keys", C.c_void_p), ("key_count", C.c_uint64),
+                ("offsets", C.c_void_p), ("offset_count", C.c_uint64),
+                ("valid_lengths", C.c_void_p)]
+
+
+class Buffer(C.Structure):
+    _fields_ = [("feature", C.c_uint32), ("reserved", C.c_uint32), ("rows", C.c_uint64),
+                ("columns", C.c_uint64), ("data", C.c_void_p), ("device", C.c_int32),
+                ("reserved2", C.c_int32)]
+
+
+class Stats(C.Structure):
+    _fields_ = [(n, C.c_uint64) for n in ("lookups", "updates", "rejected_updates",
+                                          "duplicate_requests", "live_tickets", "state_bytes",
+                                          "rows", "tables", "kernel_launches")]
+
+
+PHASES = ("lookup", "sort", "prescan", "apply", "finalize")
+
+
+_lib = None
+
+ENTRY_POINTS = ("eps_b200_abi_version", "eps_b200_create", "eps_b200_destroy",
+                "eps_b200_create_table", "eps_b200_lookup", "eps_b200_push", "eps_b200_release",
+                "eps_b200_synchronize", "eps_b200_read_state", "eps_b200_load_state",
+                "eps_b200_optimizer_state", "eps_b200_profile", "eps_b200_stats")
+
+
+def load_library() -> C.CDLL:
+    """Loads libeps_b200.so; raises if it has not been built (no fallback)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(_LIB_PATH):
+        raise ImportError(f"{_LIB_PATH} is missing: build it with `python build.py` "
+                          "(there is no non-CUDA fallback)")
+    lib = C.CDLL(_LIB_PATH)
+    P = C.POINTER
+    vp = C.c_void_p
+    lib.eps_b200_abi_version.restype = C.c_uint32
+    lib.eps_b200_create.argtypes = [P(Options), P(vp), P(Status)]
+    lib.eps_b200_destroy.argtypes = [vp]
+    lib.eps_b200_destroy.restype = None
+    lib.eps_b200_create_table.argtypes = [vp, P(Table), P(Status)]
+    lib.eps_b200_lookup.argtypes = [vp, P(Feature), C.c_uint64, C.c_int32, C.c_int32, C.c_int32,
+                                    P(Buffer), vp, P(C.c_uint64), P(Status)]
+    lib.eps_b200_push.argtypes = [vp, C.c_uint64, P(Buffer), C.c_uint64, vp, C.c_int32, P(Status)]
+    lib.eps_b200_release.argtypes = [vp, C.c_uint64, P(Status)]
+    lib.eps_b200_synchronize.argtypes = [vp, P(Status)]
+    lib.eps_b200_read_state.argtypes = [vp, C.c_uint32, vp, C.c_uint64, vp, vp, vp, vp, P(Status)]
+    lib.eps_b200_load_state.argtypes = [vp, C.c_uint32, vp, C.c_uint64, vp, vp, vp, vp, P(Status)]
+    lib.eps_b200_optimizer_state.argtypes = [vp, C.c_uint32, P(C.c_uint64), P(C.c_float),
+                                             P(C.c_float), P(Status)]
+    lib.eps_b200_stats.argtypes = [vp, P(Stats), P(Status)]
+    lib.eps_b200_profile.argtypes = [vp, C.c_int32, P(C.c_double), P(C.c_uint64), P(C.c_uint64),
+                                     P(Status)]
+    for name in ENTRY_POINTS[1:]:
+        if name != "eps_b200_destroy":
+            getattr(lib, name).restype = C.c_int
+    if lib.eps_b200_abi_version() != 1:
+        raise ImportError("libeps_b200.so ABI version mismatch")
+    _lib = lib
+    return lib
+
+
+load_library()
+
+
+# ----------------------------------------------------------- python mirror
+@dataclass
+class TableDefinition:
+    """eps::TableDefinition + OptimizerConfig (include/eps/types.hpp:76-97)."""
+    id: int
+    dimension: int
+    key_space: int
+    learning_rate: float = 1e-3
+    beta1: float = 0.9
+    beta2: float = 0.999
+    epsilon: float = 1e-8
+    initial_beta1_power: float = 0.9
+    initial_beta2_power: float = 0.999
+    weight_bounds: tuple | None = None
+    initialization_min: float = -0.05
+    initialization_max: float = 0.05
+    initialization_seed: int = 42
+    shard_count: int = 1
+    partition_epoch: int = 1
+
+
+@dataclass
+class FeatureInput:
+    """eps::FeatureInput (include/eps/types.hpp:99-107).
+
+    keys/offsets/valid_lengths are uint64 numpy arrays (host) or int64/uint64
+    torch CUDA tensors (device).  valid_lengths=None means offset differences.
+    """
+    table: int
+    feature: int
+    pooling: int
+    keys: object
+    offsets: object
+    valid_lengths: object = None
+
+    @property
+    def output_rows(self) -> int:
+        return _length(self.keys) if self.pooling == SEQUENCE else _length(self.offsets) - 1
+
+
+def _length(a) -> int:
+    return int(a.shape[0]) if hasattr(a, "shape") else len(a)
+
+
+def _is_device(a) -> bool:
+    return hasattr(a, "is_cuda") and a.is_cuda
+
+
+def _ptr(a):
+    if a is None:
+        return None
+    if _is_device(a):
+        return a.data_ptr()
+    return a.ctypes.data
+
+
+def _host_u64(a):
+    return np.ascontiguousarray(a, dtype=np.uint64)
+
+
+def _check(rc: int, status: Status):
+    if rc:
+        raise EpsError(rc, status.message.decode(errors="replace"))
+
+
+class ParameterStore:
+    """One shard of device-resident embedding tables (eps_b200_create)."""
+
+    def __init__(self, device: int = 0, shard_id: int = 0, shard_count: int = 1,
+                 state_bytes: int = 64 << 30, max_live_tickets: int = 1024,
+                 partition_epoch: int = 1, reference_order: bool = False):
+        self.lib = load_library()
+        self.device = device
+        self.shard_count = shard_count
+        self._tables: dict[int, TableDefinition] = {}
+        opt = Options(device, shard_id, shard_count, max_live_tickets, partition_epoch, state_bytes,
+                      FLAG_REFERENCE_ORDER if reference_order else 0, 0)
+        st = Status()
+        h = C.c_void_p()
+        _check(self.lib.eps_b200_create(C.byref(opt), C.byref(h), C.byref(st)), st)
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self.lib.eps_b200_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    # ParameterService::CreateTable (include/eps/parameter_service.hpp:16)
+    def create_table(self, t: TableDefinition):
+        b = t.weight_bounds
+        ct = Table(t.id, t.dimension, t.shard_count, 1 if b else 0, t.partition_epoch,
+                   t.learning_rate, t.beta1, t.beta2, t.epsilon, t.initial_beta1_power,
+                   t.initial_beta2_power, *(b if b else (0.0, 0.0)), t.initialization_min,
+                   t.initialization_max, t.initialization_seed, t.key_space)
+        st = Status()
+        _check(self.lib.eps_b200_create_table(self._h, C.byref(ct), C.byref(st)), st)
+        self._tables[t.id] = t
+
+    def _features(self, feats: Sequence[FeatureInput]):
+        on_device = None
+        keep = []
+        arr = (Feature * len(feats))()
+        for i, f in enumerate(feats):
+            dev = _is_device(f.keys)
+            if on_device is None:
+                on_device = dev
+            if dev != on_device or _is_device(f.offsets) != dev:
+                raise EpsError(INVALID_ARGUMENT, "mixed host/device lookup inputs")
+            keys, offs, lens = f.keys, f.offsets, f.valid_lengths
+            if not dev:
+                keys, offs = _host_u64(keys), _host_u64(offs)
+                lens = None if lens is None else _host_u64(lens)
+            keep += [keys, offs, lens]
+            arr[i] = Feature(f.table, f.feature, f.pooling, 0, _ptr(keys), _length(keys),
+                             _ptr(offs), _length(offs), _ptr(lens))
+        return arr, bool(on_device), keep
+
+    def lookup(self, feats: Sequence[FeatureInput], read_only: bool = False,
+               shard_partial: bool = False, outputs=None, stream=None, host_outputs=None):
+        """Pull.  Returns (ticket or None, outputs).  Device inputs give torch
+        CUDA outputs unless `outputs` is supplied; host inputs give numpy."""
+        arr, on_device, keep = self._features(feats)
+        if host_outputs is None:
+            host_outputs = not on_device
+        if outputs is None:
+            outputs = []
+            for f in feats:
+                shape = (f.output_rows, self._tables[f.table].dimension)
+                if host_outputs:
+                    outputs.append(np.empty(shape, np.float32))
+                else:
+                    import torch
+                    outputs.append(torch.empty(shape, dtype=torch.float32,
+                                               device=f"cuda:{self.device}"))
+        bufs = (Buffer * len(feats))()
+        for i, (f, o) in enumerate(zip(feats, outputs)):
+            dev = _is_device(o)
+            bufs[i] = Buffer(f.feature, 0, int(o.shape[0]), int(o.shape[1]), _ptr(o),
+                             self.device if dev else -1, 0)
+        ticket = C.c_uint64(0)
+        st = Status()
+        rc = self.lib.eps_b200_lookup(self._h, arr, len(feats), int(on_device), int(read_only),
+                                      int(shard_partial), bufs, _stream_ptr(stream),
+                                      C.byref(ticket), C.byref(st))
+        _check(rc, st)
+        del keep
+        return (None if read_only else ticket.value), outputs
+
+    def prepare_lookup(self, feats: Sequence[FeatureInput], outputs, read_only=False,
+                       shard_partial=False):
+        """Binds inputs/outputs once; the returned callable runs eps_b200_lookup
+        with no per-call Python marshalling (for steady-state loops)."""
+        arr, on_device, keep = self._features(feats)
+        bufs = (Buffer * len(feats))()
+        for i, (f, o) in enumerate(zip(feats, outputs)):
+            dev = _is_device(o)
+            bufs[i] = Buffer(f.feature, 0, int(o.shape[0]), int(o.shape[1]), _ptr(o),
+                             self.device if dev else -1, 0)
+        ticket = C.c_uint64(0)
+        st = Status()
+        lib, h, n = self.lib, self._h, len(feats)
+        ro, sp, od = int(read_only), int(shard_partial), int(on_device)
+
+        def run(stream=None):
+            rc = lib.eps_b200_lookup(h, arr, n, od, ro, sp, bufs, _stream_ptr(stream),
+                                     C.byref(ticket), C.byref(st))
+            _check(rc, st)
+            return ticket.value
+
+        run._keep = (arr, bufs, keep, outputs)
+        return run
+
+    def prepare_push(self, gradients, features: Sequence[int] | None = None):
+        """Binds gradient buffers once; returns push(ticket, stream=None, wait=False)."""
+        n = len(gradients)
+        bufs = (Buffer * n)()
+        keep = []
+        for i, g in enumerate(gradients):
+            dev = _is_device(g)
+            if not dev:
+                g = np.ascontiguousarray(g, dtype=np.float32)
+            keep.append(g)
+            fid = features[i] if features is not None else i
+            bufs[i] = Buffer(fid, 0, int(g.shape[0]), int(g.shape[1]), _ptr(g),
+                             self.device if dev else -1, 0)
+        st = Status()
+        lib, h = self.lib, self._h
+
+        def run(ticket, stream=None, wait=False):
+            _check(lib.eps_b200_push(h, ticket, bufs, n, _stream_ptr(stream), int(wait),
+                                     C.byref(st)), st)
+
+        run._keep = (bufs, keep)
+        return run
+
+    def push(self, ticket: int, gradients, features: Sequence[int] | None = None,
+             wait: bool = True, stream=None):
+        """Push feature gradients (ordered like the lookup's features, or with
+        explicit feature ids).  All-or-nothing; raises EpsError on rejection."""
+        n = len(gradients)
+        bufs = (Buffer * n)()
+        keep = []
+        for i, g in enumerate(gradients):
+            dev = _is_device(g)
+            if not dev:
+                g = np.ascontiguousarray(g, dtype=np.float32)
+            keep.append(g)
+            fid = features[i] if features is not None else i
+            bufs[i] = Buffer(fid, 0, int(g.shape[0]), int(g.shape[1]), _ptr(g),
+                             self.device if dev else -1, 0)
+        st = Status()
+        rc = self.lib.eps_b200_push(self._h, ticket, bufs, n, _stream_ptr(stream), int(wait),
+                                    C.byref(st))
+        _check(rc, st)
+
+    def release(self, ticket: int):
+        st = Status()
+        _check(self.lib.eps_b200_release(self._h, ticket, C.byref(st)), st)
+
+    def synchronize(self):
+        st = Status()
+        _check(self.lib.eps_b200_synchronize(self._h, C.byref(st)), st)
+
+    def read_state(self, table: int, keys):
+        keys = _host_u64(keys)
+        d = self._tables[table].dimension
+        w = np.empty((len(keys), d), np.float32)
+        m = np.empty_like(w)
+        v = np.empty_like(w)
+        upd = np.empty(len(keys), np.uint64)
+        st = Status()
+        _check(self.lib.eps_b200_read_state(self._h, table, _ptr(keys), len(keys), _ptr(w),
+                                            _ptr(m), _ptr(v), _ptr(upd), C.byref(st)), st)
+        return w, m, v, upd
+
+    def load_state(self, table: int, keys, weights, first, second, row_updates=None):
+        keys = _host_u64(keys)
+        w = np.ascontiguousarray(weights, np.float32)
+        m = np.ascontiguousarray(first, np.float32)
+        v = np.ascontiguousarray(second, np.float32)
+        u = None if row_updates is None else _host_u64(row_updates)
+        st = Status()
+        _check(self.lib.eps_b200_load_state(self._h, table, _ptr(keys), len(keys), _ptr(w),
+                                            _ptr(m), _ptr(v), _ptr(u), C.byref(st)), st)
+
+    def optimizer_state(self, table: int):
+        seq = C.c_uint64()
+        b1 = C.c_float()
+        b2 = C.c_float()
+        st = Status()
+        _check(self.lib.eps_b200_optimizer_state(self._h, table, C.byref(seq), C.byref(b1),
+                                                 C.byref(b2), C.byref(st)), st)
+        return seq.value, b1.value, b2.value
+
+    def profile(self, mode: int = -1) -> dict:
+        """Per-phase device milliseconds / kernel launches / calls; mode 1 resets
+        and starts recording, 0 stops (eps_b200_profile)."""
+        n = len(PHASES)
+        ms = (C.c_double * n)()
+        la = (C.c_uint64 * n)()
+        ca = (C.c_uint64 * n)()
+        st = Status()
+        _check(self.lib.eps_b200_profile(self._h, mode, ms, la, ca, C.byref(st)), st)
+        return {p: {"ms": ms[i], "launches": la[i], "calls": ca[i]} for i, p in enumerate(PHASES)}
+
+    def stats(self) -> dict:
+        s = Stats()
+        st = Status()
+        _check(self.lib.eps_b200_stats(self._h, C.byref(s), C.byref(st)), st)
+        return {n: getattr(s, n) for n, _ in Stats._fields_}
+
+
+def _stream_ptr(stream):
+    if stream is None:
+        return None
+    if hasattr(stream, "cuda_stream"):
+        return stream.cuda_stream
+    return int(stream)

@@ -1,0 +1,110 @@
+// device_types.h -- plain structs shared by the host runtime and the sm_100a kernels.
+//
+// HBM layout of one table shard (dense, direct-mapped):
+//   state   : float[rows][3][D]   row = [w(D) | m(D) | v(D)], the reference's row
+//             layout (src/store/shard_store.cpp:21-29), 12*D bytes per row
+//   updates : uint64[rows]        row_updates counter (RowState::row_updates)
+// A key k lives on shard k % shard_count at slot k / shard_count
+// (src/access/prepared_lookup.cpp:54, src/store/shard_store.cpp:77).
+#pragma once
+#include <stdint.h>
+
+namespace eps_b200 {
+
+// Device-resident optimizer bookkeeping of one table (TableState,
+// src/store/shard_store.hpp:11-16).  Kept on the GPU so that a rejected Push
+// (decided on the device) never advances the host's view of beta powers.
+struct DeviceTable {
+  float beta1_power;
+  float beta2_power;
+  unsigned long long optimizer_sequence;
+  // Upper bound of |w|, |m| and v over every row ever written (float bits).
+  // Used to prove that an update cannot overflow (see push kernels).
+  unsigned int state_absmax_bits;
+  unsigned int pad;
+};
+
+// One table as seen by a Push: constant optimizer parameters plus pointers.
+struct PushTable {
+  float* state;
+  unsigned long long* updates;
+  DeviceTable* dtable;
+  unsigned long long rows;
+  unsigned long long occurrences;   // occurrences of this table in the lookup
+  float learning_rate, beta1, beta2, epsilon;
+  float one_minus_beta1, one_minus_beta2;
+  float bound_min, bound_max;
+  int has_bounds;
+  unsigned int dim;
+  float lr_t;                       // bias-corrected rate, written on the device
+  unsigned int pad;
+};
+
+// One feature of a lookup.  `item` = one bag (for sequence features the bag
+// structure is kept; every position is its own output row).
+struct LookupFeature {
+  const unsigned long long* keys;
+  const unsigned long long* offsets;
+  const unsigned long long* lengths;  // original bag lengths, or null => offset diffs
+  float* out;
+  const float* state;
+  unsigned long long rows;             // slots of the table on this shard
+  unsigned long long key_count;
+  unsigned long long bag_count;
+  unsigned long long bag_base;         // prefix of bags over features (work items)
+  unsigned long long occ_base;         // first occurrence index in the ticket
+  unsigned long long scale_base;       // first gradient-row index in row_scale
+  unsigned int dim;
+  unsigned int pooling;                // 0 sum, 1 mean, 2 sequence
+  unsigned int table_rank;             // rank of the table inside this lookup
+  unsigned int feature_index;          // index inside the lookup (gradient slot)
+};
+
+// Gradient source of one feature for a Push.
+struct PushFeature {
+  const float* grad;                   // [rows][dim]
+  unsigned long long rows;
+  unsigned long long scale_base;
+  unsigned int dim;
+  unsigned int table_rank;
+};
+
+enum PushMode : unsigned int { kModeSafe = 0, kModeChecked = 1, kModeRejected = 2 };
+enum RejectBits : unsigned int {
+  kRejectNonFiniteInput = 1u,   // src/access/batch_access.cpp:97
+  kRejectLearningRate = 2u,     // src/update/lazy_adam.cpp:12
+  kRejectReduction = 4u,        // src/access/batch_access.cpp:122-123
+  kRejectOptimizer = 8u,        // src/update/lazy_adam.cpp:20-21
+};
+enum LookupErrorBits : unsigned int {
+  kLookupBadOffsets = 1u,       // src/access/batch_access.cpp:14-16
+  kLookupBadKey = 2u,           // key routed to another shard / outside the table
+  kLookupShortLength = 4u,      // src/access/batch_access.cpp:18-20
+};
+
+// Per-push control block (device).  Zeroed before each push.
+struct PushControl {
+  unsigned int nonfinite;
+  unsigned int maxabs_bits;
+  unsigned int mode;
+  unsigned int reject_bits;
+  unsigned int long_count;
+  unsigned int blocks_done;
+  unsigned int accepted;
+  unsigned int pad;
+};
+
+// A long coalesced segment (more than kLongRun occurrences): it is reduced in
+// per-tile pieces and combined in tile order by the long-segment kernel.
+struct LongRecord {
+  unsigned long long key;       // composite (table rank, slot)
+  unsigned int first_tile;      // tile in which the segment starts
+  unsigned int first_slot;      // 0: piece stored in part0[first_tile], 1: in part1
+};
+
+constexpr int kTile = 64;       // sorted occurrences per warp tile
+constexpr int kLongRun = 64;    // segments longer than this are "long"
+constexpr unsigned int kMaxFeatures = 1024;
+constexpr unsigned int kRowBits = 22;   // gradient row bits in the source code
+
+}  // namespace eps_b200

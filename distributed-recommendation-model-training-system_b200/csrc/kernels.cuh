@@ -1,0 +1,154 @@
+// kernels.cuh -- device helpers and kernel launch wrappers (sm_100a).
+//
+// Every floating-point operation on the parity path uses an explicitly rounded
+// intrinsic (__fadd_rn, __fmul_rn, __fdiv_rn, __fsqrt_rn): no FMA contraction
+// can occur, so each value rounds exactly as the reference's x86-64 build
+// (SSE2, no FMA) rounds it.  The library is also compiled with --fmad=false.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "device_types.h"
+
+namespace eps_b200 {
+
+template <int VEC> struct VecT;
+template <> struct VecT<1> { using type = float; };
+template <> struct VecT<2> { using type = float2; };
+template <> struct VecT<4> { using type = float4; };
+
+template <int VEC>
+__device__ __forceinline__ void load_vec(const float* p, float (&r)[VEC]) {
+  if constexpr (VEC == 4) {
+    const float4 x = *reinterpret_cast<const float4*>(p);
+    r[0] = x.x; r[1] = x.y; r[2] = x.z; r[3] = x.w;
+  } else if constexpr (VEC == 2) {
+    const float2 x = *reinterpret_cast<const float2*>(p);
+    r[0] = x.x; r[1] = x.y;
+  } else {
+    r[0] = *p;
+  }
+}
+
+template <int VEC>
+__device__ __forceinline__ void store_vec(float* p, const float (&r)[VEC]) {
+  if constexpr (VEC == 4) {
+    *reinterpret_cast<float4*>(p) = make_float4(r[0], r[1], r[2], r[3]);
+  } else if constexpr (VEC == 2) {
+    *reinterpret_cast<float2*>(p) = make_float2(r[0], r[1]);
+  } else {
+    *p = r[0];
+  }
+}
+
+// Streaming (evict-first) variants for data touched once per round.
+template <int VEC>
+__device__ __forceinline__ void load_vec_stream(const float* p, float (&r)[VEC]) {
+  if constexpr (VEC == 4) {
+    const float4 x = __ldcs(reinterpret_cast<const float4*>(p));
+    r[0] = x.x; r[1] = x.y; r[2] = x.z; r[3] = x.w;
+  } else if constexpr (VEC == 2) {
+    const float2 x = __ldcs(reinterpret_cast<const float2*>(p));
+    r[0] = x.x; r[1] = x.y;
+  } else {
+    r[0] = __ldcs(p);
+  }
+}
+
+__device__ __forceinline__ unsigned lane_id() { return threadIdx.x & 31u; }
+
+__device__ __forceinline__ bool finitef(float x) { return isfinite(x); }
+
+// Clamp with std::clamp semantics (src/common/optimizer_bounds.hpp:14-18).
+__device__ __forceinline__ float clamp_weight(float v, int has, float lo, float hi) {
+  if (!has) return v;
+  return v < lo ? lo : (hi < v ? hi : v);
+}
+
+__device__ __forceinline__ unsigned abs_bits(float x) { return __float_as_uint(fabsf(x)); }
+
+// ---------------------------------------------------------------- launchers
+struct LookupLaunch {
+  const LookupFeature* features;   // device array
+  unsigned int feature_count;
+  unsigned long long bag_total;
+  unsigned int shard_count, shard_id;
+  int client;                      // 1: merge + mean (DistributedClient), 0: shard partial
+  int emit;                        // 1: write occurrences for a later Push
+  unsigned int slot_bits;
+  int key64;                       // composite key width
+  void* occ_key;                   // KeyT[occurrences]
+  unsigned int* occ_src;           // [occurrences]
+  float* row_scale;                // [gradient rows]
+  unsigned int* error;             // LookupErrorBits
+  int vec, iters;
+};
+cudaError_t launch_lookup(const LookupLaunch& p, cudaStream_t stream);
+
+struct SortLaunch {
+  void* keys; void* keys_alt;      // KeyT
+  unsigned int* vals; unsigned int* vals_alt;
+  unsigned long long n;
+  unsigned int bits;
+  int key64;
+  unsigned int* tile_hist;         // scratch: 256 * tiles
+  unsigned int tiles;
+};
+// Stable LSD radix sort; returns in *swapped whether the result is in the alt
+// buffers.
+cudaError_t launch_sort(const SortLaunch& p, cudaStream_t stream, int* swapped);
+unsigned int sort_launch_count(const SortLaunch& p);
+unsigned int sort_tiles(unsigned long long n);
+
+struct PushLaunch {
+  const PushTable* tables;         // device, per table rank
+  unsigned int table_count;
+  const PushFeature* features;     // device, per feature index
+  unsigned int feature_count;
+  const float* row_scale;
+  const void* keys;                // sorted composite keys
+  const unsigned int* srcs;        // sorted sources
+  unsigned long long n;
+  unsigned int slot_bits;
+  int key64;
+  unsigned long long grad_values;  // total gradient values over features
+  const unsigned long long* grad_prefix;  // device: value prefix per feature
+  float* part0; float* part1;      // [tiles][dim_max] long-segment pieces
+  LongRecord* records;
+  unsigned int dim_max;
+  PushControl* control;
+  const unsigned int* lookup_error;
+  unsigned long long long_run;     // segments longer than this are reduced in pieces
+  int vec, iters;
+};
+// Push = prescan (+ device-side mode decision), apply (2 passes x {segments,
+// long segments}), finalize (beta powers / sequence iff accepted).
+cudaError_t launch_push_prescan(const PushLaunch& p, cudaStream_t stream);
+cudaError_t launch_push_apply(const PushLaunch& p, cudaStream_t stream);
+unsigned launch_push_apply_count(const PushLaunch& p);
+cudaError_t launch_push_finalize(const PushLaunch& p, cudaStream_t stream);
+
+struct InitLaunch {
+  float* state; unsigned long long* updates;
+  unsigned long long rows; unsigned int dim;
+  unsigned int shard_count, shard_id;
+  unsigned int table_id; unsigned long long seed;
+  float init_min, init_max;
+  int has_bounds; float bound_min, bound_max;
+};
+cudaError_t launch_init(const InitLaunch& p, cudaStream_t stream);
+
+// Row state gather/scatter for ReadState / Load (src/cuda/cache_backend.cu
+// ReadStateKernel / ScatterState contract, slots from keys).
+cudaError_t launch_read_rows(const float* state, const unsigned long long* updates,
+                             unsigned int dim, unsigned long long rows,
+                             unsigned int shard_count, const unsigned long long* keys,
+                             unsigned long long n, float* packed, unsigned long long* upd_out,
+                             unsigned int* error, cudaStream_t stream);
+cudaError_t launch_write_rows(float* state, unsigned long long* updates, unsigned int dim,
+                              unsigned long long rows, unsigned int shard_count,
+                              const unsigned long long* keys, unsigned long long n,
+                              const float* packed, const unsigned long long* upd_in,
+                              DeviceTable* dtable, cudaStream_t stream);
+
+}  // namespace eps_b200

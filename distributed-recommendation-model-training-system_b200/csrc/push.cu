@@ -1,0 +1,567 @@
+// push.cu -- gradient push: coalesced segment-sum fused with the row-wise sparse
+// LazyAdam update, with the reference's all-or-nothing rejection.
+//
+// Reference semantics followed:
+//   * src/access/batch_access.cpp:89-123 (ReduceGradients): every gradient value
+//     must be finite; per table, each unique row receives
+//     g += src_row * scale over its occurrences in (feature, bag, position) order,
+//     scale = 1.0f/valid_length for mean; a non-finite reduced value rejects.
+//   * src/update/lazy_adam.cpp:7-42 (ValidateLazyAdam / ApplyLazyAdam):
+//     lr_t = lr*sqrt(1-b2p)/(1-b1p) in float; m = b1*m + (1-b1)*g;
+//     v = b2*v + (1-b2)*g*g; w -= lr_t*m/(sqrt(v)+eps); clamp; ++updates; then
+//     ++optimizer_sequence, b1p *= b1, b2p *= b2 per table.
+//   * src/server/service.cpp:252-325: all tables are validated before any is
+//     written; a rejected Push leaves every byte of state unchanged.
+//
+// Launch sequence (all decisions are made on the device; no host sync):
+//   1. prescan   -- finiteness + max|g| of every gradient value; its last block
+//                   computes lr_t per table and picks the mode:
+//                   SAFE    when |g_reduced| <= 3*N*max|g| <= 1e17, the recorded
+//                           state bound <= 1e17 and lr_t/eps <= 1e20: then no
+//                           m, v or w can overflow (|lr_t*m/(sqrt(v)+eps)| <=
+//                           1e37) and the update is applied in ONE fused pass;
+//                   CHECKED otherwise: pass 0 validates exactly as the reference,
+//                           pass 1 applies only if nothing was rejected.
+//   2. segments pass 0, 3. long pass 0, 4. segments pass 1, 5. long pass 1,
+//   6. finalize  -- advances beta powers and the sequence iff accepted.
+//
+// Coalescing layout: the occurrences are sorted stably by composite key
+// (table rank, slot).  Warp w owns the tile [64w, 64w+64) of sorted occurrences
+// and fully processes every segment that STARTS in its tile and has at most 64
+// occurrences: the gradient sum runs serially in occurrence order (bit-exact
+// with the reference) and the Adam update of that row follows in the same pass
+// from state prefetched at the segment start.  Longer (Zipf-head) segments are
+// reduced per tile into part0/part1 and combined in tile order by a CTA of 16
+// warps in the long-segment kernel (deterministic; within 1e-6 relative of the
+// reference's serial order).
+#include "kernels.cuh"
+
+namespace eps_b200 {
+namespace {
+
+template <typename KeyT>
+__device__ __forceinline__ KeyT key_at(const void* keys, unsigned long long i) {
+  return __ldg(static_cast<const KeyT*>(keys) + i);
+}
+
+struct Role { bool run, apply, validate, partials; };
+
+__device__ __forceinline__ Role role(const PushControl* c, int pass) {
+  Role r{false, false, false, false};
+  const unsigned mode = *(volatile const unsigned*)&c->mode;
+  if (mode == kModeRejected) return r;
+  if (pass == 0) {
+    r.run = true; r.partials = true;
+    r.apply = mode == kModeSafe;
+    r.validate = mode == kModeChecked;
+  } else {
+    const unsigned bits = *(volatile const unsigned*)&c->reject_bits;
+    if (mode != kModeChecked || bits) return r;
+    r.run = true; r.apply = true;
+  }
+  return r;
+}
+
+// ------------------------------------------------------------------ prescan
+__global__ void __launch_bounds__(256) push_prescan(PushLaunch p, PushTable* tables_rw) {
+  __shared__ unsigned long long s_prefix[kMaxFeatures + 1];
+  __shared__ unsigned s_bad, s_max, s_last;
+  const unsigned fc = p.feature_count;
+  for (unsigned i = threadIdx.x; i <= fc; i += blockDim.x) s_prefix[i] = p.grad_prefix[i];
+  if (threadIdx.x == 0) { s_bad = 0; s_max = 0; }
+  __syncthreads();
+  const unsigned long long total = p.grad_values;
+  const unsigned long long per_block = (total + gridDim.x - 1) / gridDim.x;
+  const unsigned long long begin = min(total, per_block * blockIdx.x);
+  const unsigned long long end = min(total, begin + per_block);
+  unsigned bad = 0;
+  float mx = 0.0f;
+  unsigned f = 0;
+  {  // feature containing `begin`
+    unsigned lo = 0, hi = fc;
+    while (hi - lo > 1) { const unsigned mid = (lo + hi) >> 1; if (s_prefix[mid] <= begin) lo = mid; else hi = mid; }
+    f = lo;
+  }
+  for (unsigned long long i = begin + threadIdx.x; i < end; i += blockDim.x) {
+    while (f + 1 < fc && s_prefix[f + 1] <= i) ++f;
+    const float x = __ldg(p.features[f].grad + (i - s_prefix[f]));
+    bad |= !isfinite(x);
+    mx = fmaxf(mx, fabsf(x));
+  }
+  bad = __reduce_or_sync(0xffffffffu, bad);
+  unsigned mb = __reduce_max_sync(0xffffffffu, __float_as_uint(mx));
+  if ((threadIdx.x & 31) == 0) {
+    if (bad) atomicOr(&s_bad, 1u);
+    atomicMax(&s_max, mb);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (s_bad) atomicOr(&p.control->nonfinite, 1u);
+    atomicMax(&p.control->maxabs_bits, s_max);
+    __threadfence();
+    s_last = atomicAdd(&p.control->blocks_done, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last || threadIdx.x != 0) return;
+  __threadfence();
+  // ---- decision (single thread of the last block)
+  PushControl* c = p.control;
+  unsigned bits = 0;
+  const unsigned lookup_err = *(volatile const unsigned*)p.lookup_error;
+  if (lookup_err) { c->reject_bits = 16u; c->mode = kModeRejected; return; }
+  if (*(volatile unsigned*)&c->nonfinite) { c->reject_bits = kRejectNonFiniteInput; c->mode = kModeRejected; return; }
+  const float maxabs = __uint_as_float(*(volatile unsigned*)&c->maxabs_bits);
+  bool safe = true;
+  for (unsigned t = 0; t < p.table_count; ++t) {
+    PushTable& T = tables_rw[t];
+    const float b1p = T.dtable->beta1_power, b2p = T.dtable->beta2_power;
+    // src/update/lazy_adam.cpp:27 -- (lr * sqrt(1 - b2p)) / (1 - b1p)
+    const float lr_t = __fdiv_rn(__fmul_rn(T.learning_rate, __fsqrt_rn(__fsub_rn(1.0f, b2p))),
+                                 __fsub_rn(1.0f, b1p));
+    T.lr_t = lr_t;
+    if (!isfinite(lr_t)) bits |= kRejectLearningRate;
+    const double G = 3.0 * (double)T.occurrences * (double)maxabs;
+    const double A = (double)__uint_as_float(T.dtable->state_absmax_bits);
+    if (!(G <= 1e17 && A <= 1e17 && (double)lr_t <= 1e20 * (double)T.epsilon)) safe = false;
+  }
+  c->reject_bits = bits;
+  c->mode = (safe && !bits) ? kModeSafe : kModeChecked;
+  __threadfence();
+}
+
+// ------------------------------------------------------ reduction helpers
+// Sum of gradient references [s0, s1) (all with the same key), serially in order.
+template <int VEC, int ITERS>
+__device__ __forceinline__ void reduce_range(const PushLaunch& p, unsigned long long s0,
+                                             unsigned long long s1, unsigned D,
+                                             float (&acc)[VEC * ITERS]) {
+  constexpr int C = VEC * ITERS;
+  const unsigned lane = lane_id();
+#pragma unroll
+  for (int k = 0; k < C; ++k) acc[k] = 0.0f;
+  for (unsigned long long c0 = s0; c0 < s1; c0 += 32) {
+    const unsigned long long i = c0 + lane;
+    unsigned long long gp = 0;
+    float sc = 0.0f;
+    if (i < s1) {
+      const unsigned src = __ldg(p.srcs + i);
+      const unsigned f = src >> kRowBits;
+      const unsigned r = src & ((1u << kRowBits) - 1u);
+      const PushFeature* F = p.features + f;
+      const float* g = reinterpret_cast<const float*>(__ldg(reinterpret_cast<const unsigned long long*>(&F->grad)));
+      gp = reinterpret_cast<unsigned long long>(g + (unsigned long long)r * D);
+      sc = __ldg(p.row_scale + __ldg(&F->scale_base) + r);
+    }
+    const int cnt = (int)min(32ull, s1 - c0);
+    for (int j0 = 0; j0 < cnt; j0 += 4) {
+      float x[4][C];
+      float s[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const unsigned long long q = __shfl_sync(0xffffffffu, gp, (j0 + u) & 31);
+        s[u] = __shfl_sync(0xffffffffu, sc, (j0 + u) & 31);
+        const bool use = j0 + u < cnt;
+#pragma unroll
+        for (int it = 0; it < ITERS; ++it) {
+          const unsigned col = (it * 32 + lane) * VEC;
+          float t[VEC];
+          if (use && col < D) load_vec<VEC>(reinterpret_cast<const float*>(q) + col, t);
+          else {
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) t[v] = 0.0f;
+          }
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) x[u][it * VEC + v] = t[v];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (j0 + u >= cnt) break;
+        // batch_access.cpp:118: dest += src * scale
+#pragma unroll
+        for (int k = 0; k < C; ++k) acc[k] = __fadd_rn(acc[k], __fmul_rn(x[u][k], s[u]));
+      }
+    }
+  }
+}
+
+template <int VEC, int ITERS>
+__device__ __forceinline__ void load_state(const float* row, unsigned D, float (&w)[VEC * ITERS],
+                                           float (&m)[VEC * ITERS], float (&v)[VEC * ITERS]) {
+  const unsigned lane = lane_id();
+#pragma unroll
+  for (int it = 0; it < ITERS; ++it) {
+    const unsigned col = (it * 32 + lane) * VEC;
+    float a[VEC], b[VEC], c[VEC];
+    if (col < D) {
+      load_vec<VEC>(row + col, a);
+      load_vec<VEC>(row + D + col, b);
+      load_vec<VEC>(row + 2 * D + col, c);
+    } else {
+#pragma unroll
+      for (int x = 0; x < VEC; ++x) a[x] = b[x] = c[x] = 0.0f;
+    }
+#pragma unroll
+    for (int x = 0; x < VEC; ++x) { w[it * VEC + x] = a[x]; m[it * VEC + x] = b[x]; v[it * VEC + x] = c[x]; }
+  }
+}
+
+// LazyAdam on one row (src/update/lazy_adam.cpp:28-37).  Returns reject bits
+// (validate) and updates *absmax (apply).
+template <int VEC, int ITERS>
+__device__ __forceinline__ unsigned adam_row(const PushTable& T, float* row, unsigned D,
+                                             const float (&g)[VEC * ITERS], float (&w)[VEC * ITERS],
+                                             float (&m)[VEC * ITERS], float (&v)[VEC * ITERS],
+                                             bool apply, bool validate, unsigned* absmax) {
+  const unsigned lane = lane_id();
+  unsigned bits = 0;
+  unsigned mx = 0;
+#pragma unroll
+  for (int it = 0; it < ITERS; ++it) {
+    const unsigned col = (it * 32 + lane) * VEC;
+    if (col >= D) continue;
+    float nw[VEC], nm[VEC], nv[VEC];
+#pragma unroll
+    for (int x = 0; x < VEC; ++x) {
+      const int k = it * VEC + x;
+      const float gr = g[k];
+      const float mm = __fadd_rn(__fmul_rn(T.beta1, m[k]), __fmul_rn(T.one_minus_beta1, gr));
+      const float vv = __fadd_rn(__fmul_rn(T.beta2, v[k]),
+                                 __fmul_rn(__fmul_rn(T.one_minus_beta2, gr), gr));
+      const float ww = __fsub_rn(w[k], __fdiv_rn(__fmul_rn(T.lr_t, mm),
+                                                 __fadd_rn(__fsqrt_rn(vv), T.epsilon)));
+      if (validate) {
+        if (!isfinite(gr)) bits |= kRejectReduction;
+        if (!isfinite(mm) || !isfinite(vv) || !isfinite(ww)) bits |= kRejectOptimizer;
+      }
+      nm[x] = mm; nv[x] = vv;
+      nw[x] = clamp_weight(ww, T.has_bounds, T.bound_min, T.bound_max);
+      mx = max(mx, max(abs_bits(nw[x]), max(abs_bits(mm), abs_bits(vv))));
+    }
+    if (apply) {
+      store_vec<VEC>(row + col, nw);
+      store_vec<VEC>(row + D + col, nm);
+      store_vec<VEC>(row + 2 * D + col, nv);
+    }
+  }
+  if (apply) *absmax = max(*absmax, mx);
+  return bits;
+}
+
+// Run length of key K starting at q (keys sorted), capped at cap+1.
+template <typename KeyT>
+__device__ __forceinline__ unsigned long long run_forward(const void* keys, unsigned long long n,
+                                                          unsigned long long q, KeyT K,
+                                                          unsigned long long cap) {
+  const unsigned lane = lane_id();
+  unsigned long long len = 0;
+  while (len <= cap) {
+    const unsigned long long i = q + len + lane;
+    const bool same = i < n && key_at<KeyT>(keys, i) == K;
+    const unsigned ball = __ballot_sync(0xffffffffu, same);
+    if (ball != 0xffffffffu) return len + (unsigned long long)(__ffs(~ball) - 1);
+    len += 32;
+  }
+  return len;
+}
+
+// Number of keys equal to K immediately before position b, capped at cap+1.
+template <typename KeyT>
+__device__ __forceinline__ unsigned long long run_backward(const void* keys, unsigned long long b,
+                                                           KeyT K, unsigned long long cap) {
+  const unsigned lane = lane_id();
+  unsigned long long len = 0;
+  while (len <= cap) {
+    const bool in = b >= len + lane + 1;
+    const bool same = in && key_at<KeyT>(keys, b - len - lane - 1) == K;
+    const unsigned ball = __ballot_sync(0xffffffffu, same);
+    if (ball != 0xffffffffu) return len + (unsigned long long)(__ffs(~ball) - 1);
+    len += 32;
+  }
+  return len;
+}
+
+template <int VEC, int ITERS>
+__device__ __forceinline__ void store_piece(float* part, unsigned dim_max, unsigned long long tile,
+                                            unsigned D, const float (&acc)[VEC * ITERS]) {
+  const unsigned lane = lane_id();
+#pragma unroll
+  for (int it = 0; it < ITERS; ++it) {
+    const unsigned col = (it * 32 + lane) * VEC;
+    if (col >= D) continue;
+    float t[VEC];
+#pragma unroll
+    for (int x = 0; x < VEC; ++x) t[x] = acc[it * VEC + x];
+    store_vec<VEC>(part + tile * dim_max + col, t);
+  }
+}
+
+// Flush a warp's state-bound maximum for table tr (called by all 32 lanes).
+__device__ __forceinline__ void flush_absmax(const PushLaunch& p, int tr, unsigned mx) {
+  mx = __reduce_max_sync(0xffffffffu, mx);
+  if (lane_id() == 0 && tr >= 0 && mx) atomicMax(&p.tables[tr].dtable->state_absmax_bits, mx);
+}
+
+// ----------------------------------------------------------------- segments
+template <int VEC, int ITERS, typename KeyT>
+__global__ void __launch_bounds__(256) push_segments(PushLaunch p, int pass) {
+  const Role R = role(p.control, pass);
+  if (!R.run) return;
+  constexpr int C = VEC * ITERS;
+  const unsigned lane = lane_id();
+  const unsigned long long n = p.n;
+  const unsigned long long tiles = (n + kTile - 1) / kTile;
+  const unsigned long long warp = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) >> 5;
+  const unsigned long long nwarps = (gridDim.x * (unsigned long long)blockDim.x) >> 5;
+  const KeyT slot_mask = (p.slot_bits >= sizeof(KeyT) * 8) ? ~KeyT(0)
+                                                           : ((KeyT(1) << p.slot_bits) - 1);
+  unsigned bits = 0;
+  int cur_tr = -1;
+  unsigned cur_max = 0;
+
+  for (unsigned long long t = warp; t < tiles; t += nwarps) {
+    const unsigned long long b = t * kTile;
+    const unsigned long long e = min(n, b + kTile);
+    unsigned long long q = b;
+    const KeyT kb = key_at<KeyT>(p.keys, b);
+    if (b > 0 && key_at<KeyT>(p.keys, b - 1) == kb) {
+      // the segment holding b started in an earlier tile
+      const unsigned long long back = run_backward<KeyT>(p.keys, b, kb, p.long_run);
+      const unsigned long long fwd = run_forward<KeyT>(p.keys, n, b, kb, p.long_run);
+      const unsigned long long stop = min(b + fwd, e);
+      if (back + fwd > p.long_run) {
+        if (R.partials) {
+          const unsigned tr = (unsigned)(kb >> p.slot_bits);
+          const unsigned D = p.tables[tr].dim;
+          float acc[C];
+          reduce_range<VEC, ITERS>(p, b, stop, D, acc);
+          store_piece<VEC, ITERS>(p.part0, p.dim_max, t, D, acc);
+        }
+      }
+      q = stop;
+      if (back + fwd <= p.long_run) q = b + fwd;
+    }
+    while (q < e) {
+      const KeyT K = key_at<KeyT>(p.keys, q);
+      const unsigned long long len = run_forward<KeyT>(p.keys, n, q, K, p.long_run);
+      const unsigned tr = (unsigned)(K >> p.slot_bits);
+      const unsigned long long slot = (unsigned long long)(K & slot_mask);
+      if (tr >= p.table_count) { q += len; continue; }
+      const PushTable& T = p.tables[tr];
+      const unsigned D = T.dim;
+      if (len <= p.long_run) {
+        if (R.apply || R.validate) {
+          float* row = T.state + slot * 3ull * D;
+          float w[C], m[C], v[C], g[C];
+          load_state<VEC, ITERS>(row, D, w, m, v);   // issued before the reduction
+          reduce_range<VEC, ITERS>(p, q, q + len, D, g);
+          if ((int)tr != cur_tr) {
+            if (R.apply) flush_absmax(p, cur_tr, cur_max);
+            cur_tr = (int)tr; cur_max = 0;
+          }
+          bits |= adam_row<VEC, ITERS>(T, row, D, g, w, m, v, R.apply, R.validate, &cur_max);
+          if (R.apply && lane == 0) T.updates[slot] += 1ull;
+        }
+        q += len;
+      } else {
+        // long segment starting at q: it runs past e (len > long_run >= kTile >= e - q)
+        if (R.partials) {
+          float acc[C];
+          reduce_range<VEC, ITERS>(p, q, e, D, acc);
+          const unsigned which = q == b ? 0u : 1u;
+          store_piece<VEC, ITERS>(which ? p.part1 : p.part0, p.dim_max, t, D, acc);
+          if (lane == 0) {
+            const unsigned at = atomicAdd(&p.control->long_count, 1u);
+            p.records[at] = LongRecord{(unsigned long long)K, (unsigned)t, which};
+          }
+        }
+        q = e;
+      }
+    }
+  }
+  bits = __reduce_or_sync(0xffffffffu, bits);
+  if (lane == 0 && bits) atomicOr(&p.control->reject_bits, bits);
+  if (R.apply) flush_absmax(p, cur_tr, cur_max);
+}
+
+// ------------------------------------------------------------ long segments
+constexpr int kLongWarps = 16;
+
+template <int VEC, int ITERS, typename KeyT>
+__global__ void __launch_bounds__(kLongWarps * 32) push_long(PushLaunch p, int pass) {
+  const Role R = role(p.control, pass);
+  if (!R.run) return;
+  if (!R.apply && !R.validate) return;
+  extern __shared__ float s_acc[];   // [kLongWarps][dim_max]
+  constexpr int C = VEC * ITERS;
+  const unsigned lane = lane_id(), w = threadIdx.x >> 5;
+  const unsigned count = *(volatile const unsigned*)&p.control->long_count;
+  const unsigned long long n = p.n;
+  const unsigned long long tiles = (n + kTile - 1) / kTile;
+  const KeyT slot_mask = (p.slot_bits >= sizeof(KeyT) * 8) ? ~KeyT(0)
+                                                           : ((KeyT(1) << p.slot_bits) - 1);
+  unsigned bits = 0;
+  unsigned cur_max = 0;
+  int cur_tr = -1;
+  for (unsigned rec = blockIdx.x; rec < count; rec += gridDim.x) {
+    const LongRecord L = p.records[rec];
+    const KeyT K = (KeyT)L.key;
+    const unsigned tr = (unsigned)(K >> p.slot_bits);
+    const unsigned long long slot = (unsigned long long)(K & slot_mask);
+    if (tr >= p.table_count) continue;
+    const PushTable& T = p.tables[tr];
+    const unsigned D = T.dim;
+    // last tile whose first key is K (keys are sorted, so binary search)
+    unsigned long long lo = L.first_tile, hi = tiles;   // invariant: answer in [lo, hi)
+    while (hi - lo > 1) {
+      const unsigned long long mid = (lo + hi) >> 1;
+      if (key_at<KeyT>(p.keys, mid * kTile) == K) lo = mid; else hi = mid;
+    }
+    const unsigned long long pieces = lo - L.first_tile + 1;
+    // contiguous chunk of pieces for this warp
+    const unsigned long long per = (pieces + kLongWarps - 1) / kLongWarps;
+    const unsigned long long p0 = min(pieces, per * w), p1 = min(pieces, p0 + per);
+    float acc[C];
+#pragma unroll
+    for (int k = 0; k < C; ++k) acc[k] = 0.0f;
+    for (unsigned long long j0 = p0; j0 < p1; j0 += 4) {
+      float x[4][C];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const unsigned long long j = j0 + u;
+        const bool use = j < p1;
+        const float* src = (j == 0 && L.first_slot) ? p.part1 : p.part0;
+        const unsigned long long tile = L.first_tile + j;
+#pragma unroll
+        for (int it = 0; it < ITERS; ++it) {
+          const unsigned col = (it * 32 + lane) * VEC;
+          float t[VEC];
+          if (use && col < D) load_vec<VEC>(src + tile * p.dim_max + col, t);
+          else {
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) t[v] = 0.0f;
+          }
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) x[u][it * VEC + v] = t[v];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (j0 + u >= p1) break;
+#pragma unroll
+        for (int k = 0; k < C; ++k) acc[k] = __fadd_rn(acc[k], x[u][k]);
+      }
+    }
+#pragma unroll
+    for (int it = 0; it < ITERS; ++it) {
+      const unsigned col = (it * 32 + lane) * VEC;
+      if (col >= D) continue;
+#pragma unroll
+      for (int x = 0; x < VEC; ++x) s_acc[w * p.dim_max + col + x] = acc[it * VEC + x];
+    }
+    __syncthreads();
+    if (w == 0) {
+      float g[C], wv[C], mv[C], vv[C];
+      float* row = T.state + slot * 3ull * D;
+      load_state<VEC, ITERS>(row, D, wv, mv, vv);
+#pragma unroll
+      for (int k = 0; k < C; ++k) g[k] = 0.0f;
+      for (int x = 0; x < kLongWarps; ++x) {
+#pragma unroll
+        for (int it = 0; it < ITERS; ++it) {
+          const unsigned col = (it * 32 + lane) * VEC;
+          if (col >= D) continue;
+#pragma unroll
+          for (int y = 0; y < VEC; ++y)
+            g[it * VEC + y] = __fadd_rn(g[it * VEC + y], s_acc[x * p.dim_max + col + y]);
+        }
+      }
+      if ((int)tr != cur_tr) {
+        if (R.apply) flush_absmax(p, cur_tr, cur_max);
+        cur_tr = (int)tr; cur_max = 0;
+      }
+      bits |= adam_row<VEC, ITERS>(T, row, D, g, wv, mv, vv, R.apply, R.validate, &cur_max);
+      if (R.apply && lane == 0) T.updates[slot] += 1ull;
+    }
+    __syncthreads();
+  }
+  if (w == 0) {
+    bits = __reduce_or_sync(0xffffffffu, bits);
+    if (lane == 0 && bits) atomicOr(&p.control->reject_bits, bits);
+    if (R.apply) flush_absmax(p, cur_tr, cur_max);
+  }
+}
+
+// ----------------------------------------------------------------- finalize
+__global__ void push_finalize(PushLaunch p) {
+  PushControl* c = p.control;
+  const unsigned mode = *(volatile unsigned*)&c->mode;
+  const unsigned bits = *(volatile unsigned*)&c->reject_bits;
+  const bool accepted = mode != kModeRejected && bits == 0;
+  if (accepted) {
+    for (unsigned t = threadIdx.x; t < p.table_count; t += blockDim.x) {
+      const PushTable& T = p.tables[t];
+      DeviceTable* d = T.dtable;
+      // src/update/lazy_adam.cpp:39-41
+      d->optimizer_sequence += 1ull;
+      d->beta1_power = __fmul_rn(d->beta1_power, T.beta1);
+      d->beta2_power = __fmul_rn(d->beta2_power, T.beta2);
+    }
+  }
+  if (threadIdx.x == 0) c->accepted = accepted ? 1u : 0u;
+}
+
+template <int VEC, int ITERS, typename KeyT>
+cudaError_t run_apply(const PushLaunch& p, cudaStream_t s) {
+  const unsigned long long tiles = (p.n + kTile - 1) / kTile;
+  const unsigned long long want = (tiles + 7) / 8;
+  const unsigned grid = (unsigned)max(1ull, min(want, 148ull * 8));
+  const size_t long_smem = (size_t)kLongWarps * p.dim_max * sizeof(float);
+  const unsigned long_grid = 148 * 2;
+  for (int pass = 0; pass < 2; ++pass) {
+    if (p.n) push_segments<VEC, ITERS, KeyT><<<grid, 256, 0, s>>>(p, pass);
+    if (p.n) push_long<VEC, ITERS, KeyT><<<long_grid, kLongWarps * 32, long_smem, s>>>(p, pass);
+  }
+  return cudaGetLastError();
+}
+
+template <int VEC, int ITERS>
+cudaError_t run_key(const PushLaunch& p, cudaStream_t s) {
+  return p.key64 ? run_apply<VEC, ITERS, unsigned long long>(p, s)
+                 : run_apply<VEC, ITERS, unsigned int>(p, s);
+}
+template <int VEC>
+cudaError_t run_iters(const PushLaunch& p, cudaStream_t s) {
+  switch (p.iters) {
+    case 1: return run_key<VEC, 1>(p, s);
+    case 2: return run_key<VEC, 2>(p, s);
+    default: return run_key<VEC, 4>(p, s);
+  }
+}
+}  // namespace
+
+cudaError_t launch_push_prescan(const PushLaunch& p, cudaStream_t stream) {
+  // enough blocks to stream the gradients at full bandwidth
+  const unsigned long long per = 256ull * 16;
+  const unsigned long long want = (p.grad_values + per - 1) / per;
+  const unsigned grid = (unsigned)max(1ull, min(want, 148ull * 8));
+  push_prescan<<<grid, 256, 0, stream>>>(p, const_cast<PushTable*>(p.tables));
+  return cudaGetLastError();
+}
+
+unsigned launch_push_apply_count(const PushLaunch& p) { return p.n ? 4u : 0u; }
+
+cudaError_t launch_push_apply(const PushLaunch& p, cudaStream_t stream) {
+  switch (p.vec) {
+    case 4: return run_iters<4>(p, stream);
+    case 2: return run_iters<2>(p, stream);
+    default: return run_iters<1>(p, stream);
+  }
+}
+
+cudaError_t launch_push_finalize(const PushLaunch& p, cudaStream_t stream) {
+  push_finalize<<<1, 32, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace eps_b200

@@ -1,0 +1,1099 @@
+// runtime.cu -- host side of the B200 parameter store and its C ABI (eps_b200.h).
+//
+// Mirrors the shard contract of the reference (include/eps/parameter_service.hpp,
+// src/server/service.cpp Lookup/Push/Release) and its C-ABI error convention
+// (adapters/entropy/runtime_c.cpp:21-30): every call returns 0 or
+// eps::Error::Code + 1 with a message.  All device work of one store is ordered
+// on one stream at a time; switching streams inserts an event dependency.
+//
+// Lookup tickets (LookupReply::ticket, include/eps/types.hpp:151-156) own one
+// stream-ordered device slab holding the occurrence list emitted by the lookup
+// kernel and already sorted for the Push, the mean scales of every gradient row,
+// and the Push scratch.  A rejected Push keeps its ticket (retryable, as
+// tests/core_tests.cpp:98-105 of the reference requires); an accepted one retires
+// it into a bounded completed history so a repeated Push is acknowledged
+// without effect (src/server/service.cpp:241-245).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <deque>
+#include <map>
+#include <mutex>
+#include <new>
+#include <stdexcept>
+#include <string>
+#include <unordered_set>
+#include <vector>
+
+#include "eps_b200.h"
+#include "kernels.cuh"
+
+namespace eps_b200 {
+namespace {
+
+struct Failure : std::runtime_error {
+  int code;
+  Failure(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+void Require(bool ok, const char* message, int code = EPS_B200_INVALID_ARGUMENT) {
+  if (!ok) throw Failure(code, message);
+}
+// CUDA errors map as in the reference backend (src/cuda/cache_backend.cu:19-24).
+void Cuda(cudaError_t e) {
+  if (e != cudaSuccess)
+    throw Failure(e == cudaErrorMemoryAllocation ? EPS_B200_CAPACITY_EXCEEDED : EPS_B200_RUN_FAILED,
+                  cudaGetErrorString(e));
+}
+
+template <typename F>
+int Boundary(EpsB200Status* status, F fn) noexcept {
+  if (status) { status->code = 0; status->message[0] = 0; }
+  auto fail = [&](int code, const char* message) {
+    if (status) {
+      status->code = code;
+      std::strncpy(status->message, message, sizeof(status->message) - 1);
+      status->message[sizeof(status->message) - 1] = 0;
+    }
+    return code;
+  };
+  try { fn(); return 0; }
+  catch (const Failure& e) { return fail(e.code, e.what()); }
+  catch (const std::bad_alloc&) { return fail(EPS_B200_CAPACITY_EXCEEDED, "native runtime allocation failed"); }
+  catch (const std::exception& e) { return fail(EPS_B200_RUN_FAILED, e.what()); }
+  catch (...) { return fail(EPS_B200_RUN_FAILED, "unknown native runtime failure"); }
+}
+
+unsigned bits_for(unsigned long long max_value) {
+  unsigned b = 0;
+  while (b < 64 && (max_value >> b)) ++b;
+  return b;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct Table {
+  EpsB200Table def{};
+  float* state = nullptr;
+  unsigned long long* updates = nullptr;
+  DeviceTable* dtable = nullptr;
+  unsigned long long rows = 0;
+  unsigned long long bytes = 0;
+};
+
+struct HostStatus {
+  PushControl control;
+  unsigned lookup_error;
+  unsigned pad[7];
+};
+
+struct Ticket {
+  bool read_only = false;
+  void* slab = nullptr;
+  int slot = -1;
+  bool push_in_flight = false;
+  bool lookup_checked = false;
+  // layout
+  std::vector<unsigned> feature_ids, feature_tables, dims, ranks;
+  std::vector<unsigned long long> grad_rows, scale_base;
+  std::vector<unsigned> table_ids;
+  std::vector<unsigned long long> table_occ;
+  unsigned long long n = 0;
+  unsigned slot_bits = 0, dim_max = 0;
+  int key64 = 0;
+  void* keys = nullptr;
+  unsigned* srcs = nullptr;
+  float* row_scale = nullptr;
+  float* part0 = nullptr;
+  float* part1 = nullptr;
+  LongRecord* records = nullptr;
+  PushControl* control = nullptr;
+  unsigned* lookup_error = nullptr;
+  PushTable* push_tables = nullptr;
+  PushFeature* push_features = nullptr;
+  unsigned long long* grad_prefix = nullptr;
+};
+
+// Slab carve-out helper.
+struct Carver {
+  size_t offset = 0;
+  template <typename T> size_t take(size_t count) {
+    const size_t at = offset;
+    offset = align256(offset + count * sizeof(T));
+    return at;
+  }
+};
+
+void choose_vec(const std::vector<unsigned>& dims, bool align16, bool align8, int* vec, int* iters) {
+  unsigned dmax = 1;
+  bool all4 = true, all2 = true;
+  for (unsigned d : dims) { dmax = std::max(dmax, d); all4 &= d % 4 == 0; all2 &= d % 2 == 0; }
+  int v = 1;
+  if (all4 && align16 && dmax >= 128) v = 4;
+  else if (all2 && align8 && dmax >= 64) v = 2;
+  if (32u * v * 4u < dmax) {
+    if (all4 && align16) v = 4;
+    else if (all2 && align8) v = 2;
+  }
+  const unsigned need = (dmax + 32u * v - 1) / (32u * v);
+  Require(need <= 4, "embedding dimension/alignment not supported by this build",
+          EPS_B200_CAPACITY_EXCEEDED);
+  *vec = v;
+  *iters = need <= 1 ? 1 : (need <= 2 ? 2 : 4);
+}
+
+}  // namespace
+}  // namespace eps_b200
+
+using namespace eps_b200;
+
+struct EpsB200Store {
+  EpsB200Options opt{};
+  std::mutex mutex;
+  cudaStream_t own = nullptr;
+  cudaStream_t last = nullptr;
+  cudaEvent_t last_done = nullptr;
+  std::map<unsigned, Table> tables;
+  std::map<unsigned long long, Ticket> tickets;
+  std::deque<unsigned long long> completed_order;
+  std::unordered_set<unsigned long long> completed;
+  unsigned long long next_ticket = 1;
+  HostStatus* host_status = nullptr;
+  std::vector<int> free_slots;
+  unsigned* sticky_error = nullptr;     // device: errors of read-only device lookups
+  unsigned long long allocated_state = 0;
+  EpsB200Stats stats{};
+  // ---- per-phase device timing (CUDA events on the launching stream)
+  struct Pending { int phase; cudaEvent_t a, b; };
+  bool profiling = false;
+  std::vector<cudaEvent_t> event_pool;
+  std::vector<Pending> pending;
+  double phase_ms[EPS_B200_PHASES] = {};
+  unsigned long long phase_launches[EPS_B200_PHASES] = {}, phase_calls[EPS_B200_PHASES] = {};
+
+  cudaEvent_t Event() {
+    if (!event_pool.empty()) { cudaEvent_t e = event_pool.back(); event_pool.pop_back(); return e; }
+    cudaEvent_t e;
+    Cuda(cudaEventCreate(&e));
+    return e;
+  }
+  cudaEvent_t Begin(cudaStream_t stream) {
+    if (!profiling) return nullptr;
+    cudaEvent_t a = Event();
+    Cuda(cudaEventRecord(a, stream));
+    return a;
+  }
+  void End(int phase, cudaEvent_t a, cudaStream_t stream, unsigned launches) {
+    stats.kernel_launches += launches;
+    phase_launches[phase] += launches;
+    ++phase_calls[phase];
+    if (!a) return;
+    cudaEvent_t b = Event();
+    Cuda(cudaEventRecord(b, stream));
+    pending.push_back({phase, a, b});
+  }
+  void Collect() {
+    for (auto& x : pending) {
+      Cuda(cudaEventSynchronize(x.b));
+      float ms = 0;
+      Cuda(cudaEventElapsedTime(&ms, x.a, x.b));
+      phase_ms[x.phase] += ms;
+      event_pool.push_back(x.a);
+      event_pool.push_back(x.b);
+    }
+    pending.clear();
+  }
+
+  // ---- pinned staging ring for small host->device descriptor copies, so that
+  // enqueueing a lookup/push never waits for the device (pageable copies would).
+  static constexpr size_t kRing = 8u << 20;
+  char* ring = nullptr;
+  size_t ring_head = 0;
+  struct Fence { size_t begin, end; cudaEvent_t done; };
+  std::deque<Fence> fences;
+
+  // Copies `bytes` from host `src` to device `dst` on `stream` through the ring.
+  void Stage(void* dst, const void* src, size_t bytes, cudaStream_t stream) {
+    if (!bytes) return;
+    if (!ring || bytes > kRing / 4) {
+      Cuda(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, stream));
+      return;
+    }
+    const size_t need = (bytes + 255) & ~size_t(255);
+    if (ring_head + need > kRing) ring_head = 0;
+    const size_t a = ring_head, b = ring_head + need;
+    // wait for earlier copies that still read [a, b)
+    while (!fences.empty()) {
+      const Fence& f = fences.front();
+      const bool overlap = f.begin < b && a < f.end;
+      if (!overlap && cudaEventQuery(f.done) != cudaSuccess) break;
+      Cuda(cudaEventSynchronize(f.done));
+      event_pool.push_back(f.done);
+      fences.pop_front();
+    }
+    std::memcpy(ring + a, src, bytes);
+    Cuda(cudaMemcpyAsync(dst, ring + a, bytes, cudaMemcpyHostToDevice, stream));
+    cudaEvent_t e = Event();
+    Cuda(cudaEventRecord(e, stream));
+    fences.push_back({a, b, e});
+    ring_head = b;
+  }
+
+  void Activate() { Cuda(cudaSetDevice(opt.device)); }
+
+  cudaStream_t Use(void* s) {
+    cudaStream_t stream = s ? static_cast<cudaStream_t>(s) : own;
+    if (last && last != stream) Cuda(cudaStreamWaitEvent(stream, last_done, 0));
+    last = stream;
+    return stream;
+  }
+  void Done(cudaStream_t stream) { Cuda(cudaEventRecord(last_done, stream)); }
+  void Sync(cudaStream_t stream) { Cuda(cudaStreamSynchronize(stream)); }
+
+  Table& Get(unsigned id) {
+    auto it = tables.find(id);
+    Require(it != tables.end(), "unknown table");
+    return it->second;
+  }
+
+  void FreeTicket(std::map<unsigned long long, Ticket>::iterator it, cudaStream_t stream) {
+    if (it->second.slab) cudaFreeAsync(it->second.slab, stream);
+    if (it->second.slot >= 0) free_slots.push_back(it->second.slot);
+    tickets.erase(it);
+    stats.live_tickets = tickets.size();
+  }
+
+  void Complete(unsigned long long id) {
+    completed.insert(id);
+    completed_order.push_back(id);
+    while (completed_order.size() > 4096) {
+      completed.erase(completed_order.front());
+      completed_order.pop_front();
+    }
+  }
+
+  // Lookup-input errors recorded by the lookup kernel (LookupErrorBits).
+  static std::string LookupMessage(unsigned bits) {
+    if (bits & kLookupBadOffsets) return "invalid bag offsets";
+    if (bits & kLookupShortLength) return "original bag length is smaller than shard contribution";
+    return "key routed to wrong shard or outside the table";
+  }
+  // Push rejection reasons in the reference's order of checks.
+  static std::string PushMessage(unsigned bits, unsigned lookup) {
+    if (bits & 16u) return LookupMessage(lookup);
+    if (bits & kRejectNonFiniteInput) return "non-finite gradient";
+    if (bits & kRejectReduction) return "gradient reduction overflow";
+    if (bits & kRejectLearningRate) return "optimizer learning-rate overflow";
+    return "optimizer state would overflow";
+  }
+
+  // After the stream finished: settle an in-flight push of ticket `it`.
+  // Returns an empty string when the push was accepted.
+  std::string Resolve(std::map<unsigned long long, Ticket>::iterator it, cudaStream_t stream) {
+    Ticket& t = it->second;
+    const HostStatus& h = host_status[t.slot];
+    t.push_in_flight = false;
+    if (h.control.accepted) {
+      ++stats.updates;
+      Complete(it->first);
+      FreeTicket(it, stream);
+      return {};
+    }
+    ++stats.rejected_updates;
+    if (h.control.reject_bits & 16u) {
+      // the lookup itself was invalid: the reference never issued a ticket
+      const std::string m = LookupMessage(h.lookup_error);
+      FreeTicket(it, stream);
+      return m;
+    }
+    return PushMessage(h.control.reject_bits, h.lookup_error);
+  }
+};
+
+namespace {
+
+EpsB200Store* Checked(EpsB200Store* s) {
+  Require(s != nullptr, "null native store");
+  return s;
+}
+
+void ValidateTable(const EpsB200Store& s, const EpsB200Table& d) {
+  Require(d.dimension > 0 && d.dimension <= 65536, "invalid embedding dimension");
+  Require(d.dimension <= 128 || (d.dimension <= 512 && d.dimension % 4 == 0),
+          "embedding dimension not supported by this build", EPS_B200_CAPACITY_EXCEEDED);
+  Require(d.shard_count == s.opt.shard_count && d.partition_epoch == s.opt.partition_epoch,
+          "table partition does not match server");
+  if (d.has_weight_bounds)
+    Require(std::isfinite(d.weight_min) && std::isfinite(d.weight_max) &&
+                d.weight_min <= d.weight_max,
+            "invalid optimizer weight bounds");
+  Require(std::isfinite(d.learning_rate) && d.learning_rate > 0 && d.beta1 >= 0 && d.beta1 < 1 &&
+              d.beta2 >= 0 && d.beta2 < 1 && std::isfinite(d.epsilon) && d.epsilon > 0 &&
+              d.initial_beta1_power >= 0 && d.initial_beta1_power < 1 &&
+              d.initial_beta2_power >= 0 && d.initial_beta2_power < 1,
+          "invalid sparse LazyAdam configuration");
+  Require(std::isfinite(d.initialization_min) && std::isfinite(d.initialization_max) &&
+              d.initialization_min <= d.initialization_max,
+          "invalid initializer bounds");
+  Require(d.key_space > 0, "invalid key space");
+}
+
+bool SameTable(const EpsB200Table& a, const EpsB200Table& b) {
+  return a.id == b.id && a.dimension == b.dimension && a.shard_count == b.shard_count &&
+         a.partition_epoch == b.partition_epoch && a.learning_rate == b.learning_rate &&
+         a.beta1 == b.beta1 && a.beta2 == b.beta2 && a.epsilon == b.epsilon &&
+         a.initial_beta1_power == b.initial_beta1_power &&
+         a.initial_beta2_power == b.initial_beta2_power &&
+         a.has_weight_bounds == b.has_weight_bounds &&
+         (!a.has_weight_bounds || (a.weight_min == b.weight_min && a.weight_max == b.weight_max)) &&
+         a.initialization_min == b.initialization_min &&
+         a.initialization_max == b.initialization_max &&
+         a.initialization_seed == b.initialization_seed && a.key_space == b.key_space;
+}
+
+}  // namespace
+
+extern "C" {
+
+uint32_t eps_b200_abi_version(void) { return EPS_B200_ABI; }
+
+int eps_b200_create(const EpsB200Options* options, EpsB200Store** out, EpsB200Status* status) {
+  if (out) *out = nullptr;
+  return Boundary(status, [&] {
+    Require(options && out, "null store options/output");
+    Require(options->shard_count > 0 && options->shard_count <= 1024 &&
+                options->shard_id < options->shard_count,
+            "invalid shard topology");
+    int devices = 0;
+    Cuda(cudaGetDeviceCount(&devices));
+    Require(options->device >= 0 && options->device < devices, "invalid CUDA device",
+            EPS_B200_UNAVAILABLE);
+    auto s = new EpsB200Store();
+    try {
+      s->opt = *options;
+      if (!s->opt.max_live_tickets) s->opt.max_live_tickets = 1024;
+      s->Activate();
+      Cuda(cudaStreamCreateWithFlags(&s->own, cudaStreamNonBlocking));
+      Cuda(cudaEventCreateWithFlags(&s->last_done, cudaEventDisableTiming));
+      // one status slot per live ticket plus a scratch slot (index max_live_tickets)
+      Cuda(cudaMallocHost(&s->host_status, sizeof(HostStatus) * (s->opt.max_live_tickets + 1)));
+      std::memset(s->host_status, 0, sizeof(HostStatus) * (s->opt.max_live_tickets + 1));
+      for (int i = (int)s->opt.max_live_tickets - 1; i >= 0; --i) s->free_slots.push_back(i);
+      Cuda(cudaMallocHost(&s->ring, EpsB200Store::kRing));
+      Cuda(cudaMalloc(&s->sticky_error, sizeof(unsigned)));
+      Cuda(cudaMemset(s->sticky_error, 0, sizeof(unsigned)));
+      // keep freed ticket slabs in the stream-ordered pool for reuse
+      cudaMemPool_t pool;
+      Cuda(cudaDeviceGetDefaultMemPool(&pool, s->opt.device));
+      unsigned long long threshold = ~0ull;
+      Cuda(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &threshold));
+    } catch (...) {
+      eps_b200_destroy(s);
+      throw;
+    }
+    *out = s;
+  });
+}
+
+void eps_b200_destroy(EpsB200Store* s) {
+  if (!s) return;
+  try {
+    cudaSetDevice(s->opt.device);
+    if (s->last) cudaStreamSynchronize(s->last);
+    if (s->own) cudaStreamSynchronize(s->own);
+    for (auto& [id, t] : s->tickets) if (t.slab) cudaFree(t.slab);
+    for (auto& [id, t] : s->tables) {
+      cudaFree(t.state); cudaFree(t.updates); cudaFree(t.dtable);
+    }
+    for (auto& f : s->fences) cudaEventDestroy(f.done);
+    if (s->ring) cudaFreeHost(s->ring);
+    for (auto& x : s->pending) { cudaEventDestroy(x.a); cudaEventDestroy(x.b); }
+    for (auto e : s->event_pool) cudaEventDestroy(e);
+    if (s->sticky_error) cudaFree(s->sticky_error);
+    if (s->host_status) cudaFreeHost(s->host_status);
+    if (s->last_done) cudaEventDestroy(s->last_done);
+    if (s->own) cudaStreamDestroy(s->own);
+  } catch (...) {
+  }
+  delete s;
+}
+
+int eps_b200_create_table(EpsB200Store* store, const EpsB200Table* table, EpsB200Status* status) {
+  return Boundary(status, [&] {
+    auto& s = *Checked(store);
+    Require(table != nullptr, "null table definition");
+    std::lock_guard lock(s.mutex);
+    s.Activate();
+    const EpsB200Table d = *table;
+    ValidateTable(s, d);
+    if (auto it = s.tables.find(d.id); it != s.tables.end()) {
+      Require(SameTable(it->second.def, d), "table already exists with different configuration");
+      return;
+    }
+    Require(s.tables.size() < 1024, "table count exceeds limit", EPS_B200_CAPACITY_EXCEEDED);
+    const unsigned long long shard = s.opt.shard_id, n = s.opt.shard_count;
+    const unsigned long long rows = d.key_space > shard ? (d.key_space - 1 - shard) / n + 1 : 0;
+    Require(rows < (1ull << 40), "key space exceeds limit", EPS_B200_CAPACITY_EXCEEDED);
+    const unsigned long long bytes = rows * (12ull * d.dimension + 8);
+    Require(s.opt.state_bytes >= s.allocated_state && bytes <= s.opt.state_bytes - s.allocated_state,
+            "parameter-state budget exhausted", EPS_B200_CAPACITY_EXCEEDED);
+    Table t;
+    t.def = d;
+    t.rows = rows;
+    t.bytes = bytes;
+    try {
+      Cuda(cudaMalloc(&t.state, std::max<size_t>(rows * 12ull * d.dimension, 16)));
+      Cuda(cudaMalloc(&t.updates, std::max<size_t>(rows * 8ull, 16)));
+      Cuda(cudaMalloc(&t.dtable, sizeof(DeviceTable)));
+      DeviceTable dt{};
+      dt.beta1_power = d.initial_beta1_power;
+      dt.beta2_power = d.initial_beta2_power;
+      dt.optimizer_sequence = 0;
+      float bound = std::max(std::fabs(d.initialization_min), std::fabs(d.initialization_max));
+      if (d.has_weight_bounds)
+        bound = std::max(bound, std::max(std::fabs(d.weight_min), std::fabs(d.weight_max)));
+      std::memcpy(&dt.state_absmax_bits, &bound, sizeof(bound));
+      Cuda(cudaMemcpy(t.dtable, &dt, sizeof(dt), cudaMemcpyHostToDevice));
+      InitLaunch p{t.state, t.updates, rows, d.dimension, s.opt.shard_count, s.opt.shard_id,
+                   d.id, d.initialization_seed, d.initialization_min, d.initialization_max,
+                   d.has_weight_bounds, d.weight_min, d.weight_max};
+      Cuda(launch_init(p, s.own));
+      Cuda(cudaStreamSynchronize(s.own));
+    } catch (...) {
+      cudaFree(t.state); cudaFree(t.updates); cudaFree(t.dtable);
+      throw;
+    }
+    s.allocated_state += bytes;
+    s.stats.state_bytes = s.allocated_state;
+    s.stats.rows += rows;
+    s.stats.tables = s.tables.size() + 1;
+    s.tables.emplace(d.id, t);
+  });
+}
+
+int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_t count,
+                    int32_t input_on_device, int32_t read_only, int32_t shard_partial,
+                    EpsB200Buffer* outputs, void* stream_arg, uint64_t* ticket_out,
+                    EpsB200Status* status) {
+  return Boundary(status, [&] {
+    auto& s = *Checked(store);
+    Require(features && outputs && count > 0 && count <= kMaxFeatures,
+            "invalid native feature count");
+    Require(read_only || ticket_out, "null ticket output");
+    std::lock_guard lock(s.mutex);
+    s.Activate();
+    if (!read_only)
+      Require(s.tickets.size() < s.opt.max_live_tickets && !s.free_slots.empty(),
+              "live ticket limit reached", EPS_B200_CAPACITY_EXCEEDED);
+    Require(shard_partial || s.opt.shard_count == 1,
+            "a client-level lookup needs a single-shard store");
+
+    // ---- host-side validation of shapes (O(features)); keys/offsets are
+    // validated by the lookup kernel itself.
+    std::map<unsigned, unsigned> ranks;   // table id -> rank (ascending id)
+    std::unordered_set<unsigned> ids;
+    unsigned long long total_keys = 0, total_offsets = 0, total_lengths = 0, total_rows = 0,
+                       host_out_values = 0, bags = 0;
+    std::vector<unsigned> dims;
+    bool out16 = true, out8 = true, any_host_out = false;
+    for (uint64_t i = 0; i < count; ++i) {
+      const auto& f = features[i];
+      Require(ids.insert(f.feature).second, "duplicate feature ID");
+      const Table& t = s.Get(f.table);
+      Require(f.pooling <= 2, "unsupported pooling mode");
+      Require(f.offset_count >= 1 && f.offsets, "invalid bag offsets");
+      Require(!f.key_count || f.keys, "null feature keys");
+      const unsigned long long rows = f.pooling == 2 ? f.key_count : f.offset_count - 1;
+      Require(rows < (1ull << kRowBits) && f.key_count < (1ull << 31),
+              "feature exceeds the per-feature row limit", EPS_B200_CAPACITY_EXCEEDED);
+      const auto& o = outputs[i];
+      Require(o.feature == f.feature && o.rows == rows && o.columns == t.def.dimension,
+              "output buffer layout mismatch");
+      Require(!rows || o.data, "null output buffer");
+      Require(o.device < 0 || o.device == s.opt.device, "output device mismatch");
+      if (o.device < 0) { any_host_out = true; host_out_values += rows * t.def.dimension; }
+      else {
+        out16 &= (reinterpret_cast<uintptr_t>(o.data) & 15) == 0;
+        out8 &= (reinterpret_cast<uintptr_t>(o.data) & 7) == 0;
+      }
+      ranks.emplace(f.table, 0);
+      total_keys += f.key_count;
+      total_offsets += f.offset_count;
+      if (f.valid_lengths) total_lengths += f.offset_count - 1;
+      total_rows += rows;
+      bags += f.offset_count - 1;
+      dims.push_back(t.def.dimension);
+    }
+    Require(total_keys < (1ull << 32), "lookup exceeds the occurrence limit",
+            EPS_B200_CAPACITY_EXCEEDED);
+    {
+      unsigned r = 0;
+      for (auto& [id, rank] : ranks) rank = r++;
+    }
+    unsigned long long max_rows = 1;
+    unsigned dim_max = 1;
+    for (auto& [id, rank] : ranks) {
+      max_rows = std::max(max_rows, s.Get(id).rows);
+      dim_max = std::max(dim_max, s.Get(id).def.dimension);
+    }
+    const unsigned slot_bits = std::max(1u, bits_for(max_rows - 1));
+    const unsigned table_bits = bits_for(ranks.size() - 1);
+    const int key64 = slot_bits + table_bits > 32;
+    const size_t key_bytes = key64 ? 8 : 4;
+    int vec, iters;
+    choose_vec(dims, out16, out8, &vec, &iters);
+
+    // ---- slab layout
+    Carver c;
+    const size_t at_desc = c.take<LookupFeature>(count);
+    const size_t at_err = c.take<unsigned>(8);
+    size_t at_keys = 0, at_offsets = 0, at_lengths = 0, at_hostout = 0;
+    if (!input_on_device) {
+      at_keys = c.take<unsigned long long>(total_keys);
+      at_offsets = c.take<unsigned long long>(total_offsets);
+      at_lengths = c.take<unsigned long long>(total_lengths);
+    }
+    if (any_host_out) at_hostout = c.take<float>(host_out_values);
+    const unsigned stiles = sort_tiles(total_keys);
+    const unsigned long long ptiles = (total_keys + kTile - 1) / kTile;
+    size_t at_k0 = 0, at_k1 = 0, at_s0 = 0, at_s1 = 0, at_scale = 0, at_hist = 0, at_p0 = 0,
+           at_p1 = 0, at_rec = 0, at_ctl = 0, at_ptab = 0, at_pfeat = 0, at_gpre = 0;
+    if (!read_only) {
+      at_k0 = c.take<char>(total_keys * key_bytes);
+      at_k1 = c.take<char>(total_keys * key_bytes);
+      at_s0 = c.take<unsigned>(total_keys);
+      at_s1 = c.take<unsigned>(total_keys);
+      at_scale = c.take<float>(total_rows);
+      at_hist = c.take<unsigned>(256ull * std::max(1u, stiles));
+      at_p0 = c.take<float>(ptiles * dim_max);
+      at_p1 = c.take<float>(ptiles * dim_max);
+      at_rec = c.take<LongRecord>(std::max(1ull, ptiles));
+      at_ctl = c.take<PushControl>(1);
+      at_ptab = c.take<PushTable>(ranks.size());
+      at_pfeat = c.take<PushFeature>(count);
+      at_gpre = c.take<unsigned long long>(count + 1);
+    }
+    cudaStream_t stream = s.Use(stream_arg);
+    char* slab = nullptr;
+    Cuda(cudaMallocAsync(reinterpret_cast<void**>(&slab), std::max<size_t>(c.offset, 256), stream));
+    auto P = [&](size_t at) { return slab + at; };
+    try {
+      unsigned* err = reinterpret_cast<unsigned*>(P(at_err));
+      Cuda(cudaMemsetAsync(err, 0, 8 * sizeof(unsigned), stream));
+      // ---- descriptors (and staging of host inputs)
+      std::vector<LookupFeature> desc(count);
+      Ticket t;
+      t.read_only = read_only != 0;
+      unsigned long long bag_base = 0, occ_base = 0, scale_base = 0, koff = 0, ooff = 0, loff = 0,
+                         hoff = 0;
+      t.table_ids.resize(ranks.size());
+      t.table_occ.assign(ranks.size(), 0);
+      for (auto& [id, rank] : ranks) t.table_ids[rank] = id;
+      for (uint64_t i = 0; i < count; ++i) {
+        const auto& f = features[i];
+        const Table& tab = s.Get(f.table);
+        const unsigned D = tab.def.dimension;
+        LookupFeature& L = desc[i];
+        const unsigned long long rows = f.pooling == 2 ? f.key_count : f.offset_count - 1;
+        if (input_on_device) {
+          L.keys = reinterpret_cast<const unsigned long long*>(f.keys);
+          L.offsets = reinterpret_cast<const unsigned long long*>(f.offsets);
+          L.lengths = reinterpret_cast<const unsigned long long*>(f.valid_lengths);
+        } else {
+          auto* kd = reinterpret_cast<unsigned long long*>(P(at_keys)) + koff;
+          auto* od = reinterpret_cast<unsigned long long*>(P(at_offsets)) + ooff;
+          if (f.key_count) Cuda(cudaMemcpyAsync(kd, f.keys, f.key_count * 8, cudaMemcpyHostToDevice, stream));
+          Cuda(cudaMemcpyAsync(od, f.offsets, f.offset_count * 8, cudaMemcpyHostToDevice, stream));
+          L.keys = kd; L.offsets = od; L.lengths = nullptr;
+          if (f.valid_lengths) {
+            auto* ld = reinterpret_cast<unsigned long long*>(P(at_lengths)) + loff;
+            if (f.offset_count > 1)
+              Cuda(cudaMemcpyAsync(ld, f.valid_lengths, (f.offset_count - 1) * 8,
+                                   cudaMemcpyHostToDevice, stream));
+            L.lengths = ld;
+            loff += f.offset_count - 1;
+          }
+          koff += f.key_count;
+          ooff += f.offset_count;
+        }
+        if (outputs[i].device < 0) {
+          L.out = reinterpret_cast<float*>(P(at_hostout)) + hoff;
+          hoff += rows * D;
+        } else {
+          L.out = static_cast<float*>(outputs[i].data);
+        }
+        L.state = tab.state;
+        L.rows = tab.rows;
+        L.key_count = f.key_count;
+        L.bag_count = f.offset_count - 1;
+        L.bag_base = bag_base;
+        L.occ_base = occ_base;
+        L.scale_base = scale_base;
+        L.dim = D;
+        L.pooling = f.pooling;
+        L.table_rank = ranks.at(f.table);
+        L.feature_index = (unsigned)i;
+        bag_base += L.bag_count;
+        occ_base += f.key_count;
+        scale_base += rows;
+        t.feature_ids.push_back(f.feature);
+        t.feature_tables.push_back(f.table);
+        t.dims.push_back(D);
+        t.ranks.push_back(L.table_rank);
+        t.grad_rows.push_back(rows);
+        t.scale_base.push_back(L.scale_base);
+        t.table_occ[L.table_rank] += f.key_count;
+      }
+      s.Stage(P(at_desc), desc.data(), count * sizeof(LookupFeature), stream);
+      LookupLaunch lp{};
+      lp.features = reinterpret_cast<const LookupFeature*>(P(at_desc));
+      lp.feature_count = (unsigned)count;
+      lp.bag_total = bag_base;
+      lp.shard_count = s.opt.shard_count;
+      lp.shard_id = s.opt.shard_id;
+      lp.client = shard_partial ? 0 : 1;
+      lp.emit = read_only ? 0 : 1;
+      lp.slot_bits = slot_bits;
+      lp.key64 = key64;
+      lp.error = read_only && input_on_device && !any_host_out ? s.sticky_error : err;
+      lp.vec = vec;
+      lp.iters = iters;
+      if (!read_only) {
+        lp.occ_key = P(at_k0);
+        lp.occ_src = reinterpret_cast<unsigned*>(P(at_s0));
+        lp.row_scale = reinterpret_cast<float*>(P(at_scale));
+      }
+      cudaEvent_t ev = s.Begin(stream);
+      Cuda(launch_lookup(lp, stream));
+      s.End(EPS_B200_PHASE_LOOKUP, ev, stream, bag_base ? 1u : 0u);
+      if (!read_only) {
+        SortLaunch sp{P(at_k0), P(at_k1), reinterpret_cast<unsigned*>(P(at_s0)),
+                      reinterpret_cast<unsigned*>(P(at_s1)), total_keys, slot_bits + table_bits,
+                      key64, reinterpret_cast<unsigned*>(P(at_hist)), stiles};
+        int swapped = 0;
+        ev = s.Begin(stream);
+        Cuda(launch_sort(sp, stream, &swapped));
+        s.End(EPS_B200_PHASE_SORT, ev, stream, sort_launch_count(sp));
+        t.keys = swapped ? P(at_k1) : P(at_k0);
+        t.srcs = reinterpret_cast<unsigned*>(swapped ? P(at_s1) : P(at_s0));
+        t.n = total_keys;
+        t.slot_bits = slot_bits;
+        t.key64 = key64;
+        t.dim_max = dim_max;
+        t.row_scale = reinterpret_cast<float*>(P(at_scale));
+        t.part0 = reinterpret_cast<float*>(P(at_p0));
+        t.part1 = reinterpret_cast<float*>(P(at_p1));
+        t.records = reinterpret_cast<LongRecord*>(P(at_rec));
+        t.control = reinterpret_cast<PushControl*>(P(at_ctl));
+        t.lookup_error = err;
+        t.push_tables = reinterpret_cast<PushTable*>(P(at_ptab));
+        t.push_features = reinterpret_cast<PushFeature*>(P(at_pfeat));
+        t.grad_prefix = reinterpret_cast<unsigned long long*>(P(at_gpre));
+      }
+      // ---- host outputs
+      hoff = 0;
+      for (uint64_t i = 0; i < count; ++i) {
+        if (outputs[i].device >= 0) continue;
+        const unsigned long long n = outputs[i].rows * outputs[i].columns;
+        if (n)
+          Cuda(cudaMemcpyAsync(outputs[i].data, reinterpret_cast<float*>(P(at_hostout)) + hoff,
+                               n * 4, cudaMemcpyDeviceToHost, stream));
+        hoff += n;
+      }
+      const bool synchronous = !input_on_device || any_host_out;
+      int slot = -1;
+      if (!read_only) {
+        slot = s.free_slots.back();
+        s.free_slots.pop_back();
+        std::memset(&s.host_status[slot], 0, sizeof(HostStatus));
+        Cuda(cudaMemcpyAsync(&s.host_status[slot].lookup_error, err, sizeof(unsigned),
+                             cudaMemcpyDeviceToHost, stream));
+      }
+      unsigned sync_err = 0;
+      if (synchronous) {
+        HostStatus& scratch = s.host_status[s.opt.max_live_tickets];
+        if (read_only)
+          Cuda(cudaMemcpyAsync(&scratch.lookup_error, err, sizeof(unsigned),
+                               cudaMemcpyDeviceToHost, stream));
+        s.Sync(stream);
+        sync_err = read_only ? scratch.lookup_error : s.host_status[slot].lookup_error;
+      }
+      ++s.stats.lookups;
+      if (read_only || sync_err) {
+        if (slot >= 0) s.free_slots.push_back(slot);
+        cudaFreeAsync(slab, stream);
+        s.Done(stream);
+        Require(!sync_err, EpsB200Store::LookupMessage(sync_err).c_str());
+        return;
+      }
+      t.slab = slab;
+      t.slot = slot;
+      t.lookup_checked = synchronous;
+      const unsigned long long id = s.next_ticket++;
+      s.tickets.emplace(id, std::move(t));
+      s.stats.live_tickets = s.tickets.size();
+      *ticket_out = id;
+      s.Done(stream);
+    } catch (...) {
+      cudaStreamSynchronize(stream);
+      cudaFreeAsync(slab, stream);
+      throw;
+    }
+  });
+}
+
+int eps_b200_push(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gradients,
+                  uint64_t count, void* stream_arg, int32_t wait, EpsB200Status* status) {
+  return Boundary(status, [&] {
+    auto& s = *Checked(store);
+    std::lock_guard lock(s.mutex);
+    s.Activate();
+    cudaStream_t stream = s.Use(stream_arg);
+    auto it = s.tickets.find(ticket);
+    if (it == s.tickets.end()) {
+      // src/server/service.cpp:241-245: a completed Push is acknowledged again
+      Require(s.completed.count(ticket) != 0, "unknown lookup ticket");
+      ++s.stats.duplicate_requests;
+      return;
+    }
+    if (it->second.push_in_flight) {
+      s.Sync(stream);
+      const std::string m = s.Resolve(it, stream);
+      if (m.empty()) { ++s.stats.duplicate_requests; return; }
+      it = s.tickets.find(ticket);
+      Require(it != s.tickets.end(), m.c_str());
+    }
+    Ticket& t = it->second;
+    Require(!t.read_only, "ticket does not belong to update");
+    const size_t nf = t.feature_ids.size();
+    Require(gradients && count == nf, "gradient feature count mismatch");
+    // gradient index by feature id (src/access/batch_access.cpp:86-96)
+    std::map<unsigned, const EpsB200Buffer*> by_id;
+    for (uint64_t i = 0; i < count; ++i)
+      Require(by_id.emplace(gradients[i].feature, &gradients[i]).second, "duplicate gradient feature");
+    unsigned long long host_values = 0, total_values = 0;
+    bool g16 = true, g8 = true;
+    std::vector<const EpsB200Buffer*> ordered(nf);
+    for (size_t i = 0; i < nf; ++i) {
+      auto f = by_id.find(t.feature_ids[i]);
+      Require(f != by_id.end(), "missing feature gradient");
+      const EpsB200Buffer& g = *f->second;
+      Require(g.rows == t.grad_rows[i] && g.columns == t.dims[i], "gradient tensor layout mismatch");
+      const unsigned long long n = g.rows * g.columns;
+      Require(!n || g.data, "native gradient budget/pointer invalid");
+      Require(g.device < 0 || g.device == s.opt.device, "gradient device mismatch");
+      if (g.device < 0) host_values += n;
+      else {
+        g16 &= (reinterpret_cast<uintptr_t>(g.data) & 15) == 0;
+        g8 &= (reinterpret_cast<uintptr_t>(g.data) & 7) == 0;
+      }
+      total_values += n;
+      ordered[i] = &g;
+    }
+    int vec, iters;
+    choose_vec(t.dims, g16, g8, &vec, &iters);
+    float* stage = nullptr;
+    if (host_values)
+      Cuda(cudaMallocAsync(reinterpret_cast<void**>(&stage), host_values * 4, stream));
+    try {
+      std::vector<PushFeature> pf(nf);
+      std::vector<unsigned long long> prefix(nf + 1, 0);
+      unsigned long long hoff = 0;
+      for (size_t i = 0; i < nf; ++i) {
+        const EpsB200Buffer& g = *ordered[i];
+        const unsigned long long n = g.rows * g.columns;
+        const float* dev = static_cast<const float*>(g.data);
+        if (g.device < 0) {
+          if (n) Cuda(cudaMemcpyAsync(stage + hoff, g.data, n * 4, cudaMemcpyHostToDevice, stream));
+          dev = stage + hoff;
+          hoff += n;
+        }
+        pf[i] = PushFeature{dev, g.rows, t.scale_base[i], t.dims[i], t.ranks[i]};
+        prefix[i + 1] = prefix[i] + n;
+      }
+      std::vector<PushTable> pt(t.table_ids.size());
+      for (size_t r = 0; r < pt.size(); ++r) {
+        const Table& tab = s.Get(t.table_ids[r]);
+        const auto& d = tab.def;
+        PushTable& x = pt[r];
+        x.state = tab.state;
+        x.updates = tab.updates;
+        x.dtable = tab.dtable;
+        x.rows = tab.rows;
+        x.occurrences = t.table_occ[r];
+        x.learning_rate = d.learning_rate;
+        x.beta1 = d.beta1;
+        x.beta2 = d.beta2;
+        x.epsilon = d.epsilon;
+        x.one_minus_beta1 = 1.0f - d.beta1;   // exact (Sterbenz), as (1 - o.beta1) in the reference
+        x.one_minus_beta2 = 1.0f - d.beta2;
+        x.has_bounds = d.has_weight_bounds;
+        x.bound_min = d.weight_min;
+        x.bound_max = d.weight_max;
+        x.dim = d.dimension;
+        x.lr_t = 0.0f;
+      }
+      s.Stage(t.push_features, pf.data(), nf * sizeof(PushFeature), stream);
+      s.Stage(t.grad_prefix, prefix.data(), (nf + 1) * 8, stream);
+      s.Stage(t.push_tables, pt.data(), pt.size() * sizeof(PushTable), stream);
+      Cuda(cudaMemsetAsync(t.control, 0, sizeof(PushControl), stream));
+      PushLaunch pl{};
+      pl.tables = t.push_tables;
+      pl.table_count = (unsigned)pt.size();
+      pl.features = t.push_features;
+      pl.feature_count = (unsigned)nf;
+      pl.row_scale = t.row_scale;
+      pl.keys = t.keys;
+      pl.srcs = t.srcs;
+      pl.n = t.n;
+      pl.slot_bits = t.slot_bits;
+      pl.key64 = t.key64;
+      pl.grad_values = total_values;
+      pl.grad_prefix = t.grad_prefix;
+      pl.part0 = t.part0;
+      pl.part1 = t.part1;
+      pl.records = t.records;
+      pl.dim_max = t.dim_max;
+      pl.control = t.control;
+      pl.lookup_error = t.lookup_error;
+      pl.long_run = (s.opt.flags & EPS_B200_FLAG_REFERENCE_ORDER) ? ~0ull : (unsigned long long)kLongRun;
+      pl.vec = vec;
+      pl.iters = iters;
+      cudaEvent_t ev = s.Begin(stream);
+      Cuda(launch_push_prescan(pl, stream));
+      s.End(EPS_B200_PHASE_PRESCAN, ev, stream, 1);
+      ev = s.Begin(stream);
+      Cuda(launch_push_apply(pl, stream));
+      s.End(EPS_B200_PHASE_APPLY, ev, stream, launch_push_apply_count(pl));
+      ev = s.Begin(stream);
+      Cuda(launch_push_finalize(pl, stream));
+      s.End(EPS_B200_PHASE_FINALIZE, ev, stream, 1);
+      Cuda(cudaMemcpyAsync(&s.host_status[t.slot].control, t.control, sizeof(PushControl),
+                           cudaMemcpyDeviceToHost, stream));
+      Cuda(cudaMemcpyAsync(&s.host_status[t.slot].lookup_error, t.lookup_error, sizeof(unsigned),
+                           cudaMemcpyDeviceToHost, stream));
+      if (stage) { cudaFreeAsync(stage, stream); stage = nullptr; }
+      t.push_in_flight = true;
+      s.Done(stream);
+    } catch (...) {
+      cudaStreamSynchronize(stream);
+      if (stage) cudaFreeAsync(stage, stream);
+      throw;
+    }
+    if (wait || host_values) {
+      s.Sync(stream);
+      const std::string m = s.Resolve(it, stream);
+      Require(m.empty(), m.c_str());
+    }
+  });
+}
+
+int eps_b200_release(EpsB200Store* store, uint64_t ticket, EpsB200Status* status) {
+  return Boundary(status, [&] {
+    auto& s = *Checked(store);
+    std::lock_guard lock(s.mutex);
+    s.Activate();
+    cudaStream_t stream = s.Use(nullptr);
+    auto it = s.tickets.find(ticket);
+    if (it == s.tickets.end()) {
+      Require(s.completed.count(ticket) != 0, "unknown lookup ticket");
+      return;
+    }
+    if (it->second.push_in_flight) {
+      s.Sync(stream);
+      const std::string m = s.Resolve(it, stream);
+      it = s.tickets.find(ticket);
+      if (it == s.tickets.end()) { if (!m.empty()) Require(false, m.c_str()); return; }
+    }
+    s.FreeTicket(it, stream);
+    s.Done(stream);
+  });
+}
+
+int eps_b200_synchronize(EpsB200Store* store, EpsB200Status* status) {
+  return Boundary(status, [&] {
+    auto& s = *Checked(store);
+    std::lock_guard lock(s.mutex);
+    s.Activate();
+    cudaStream_t stream = s.Use(nullptr);
+    s.Sync(stream);
+    std::string first;
+    for (auto it = s.tickets.begin(); it != s.tickets.end();) {
+      auto next = std::next(it);
+      if (it->second.push_in_flight) {
+        const std::string m = s.Resolve(it, stream);
+        if (first.empty()) first = m;
+      } else if (!it->second.lookup_checked) {
+        const unsigned e = s.host_status[it->second.slot].lookup_error;
+        it->second.lookup_checked = true;
+        if (e) {
+          if (first.empty()) first = EpsB200Store::LookupMessage(e);
+          s.FreeTicket(it, stream);
+        }
+      }
+      it = next;
+    }
+    unsigned sticky = 0;
+    Cuda(cudaMemcpy(&sticky, s.sticky_error, sizeof(unsigned), cudaMemcpyDeviceToHost));
+    if (sticky) {
+      Cuda(cudaMemset(s.sticky_error, 0, sizeof(unsigned)));
+      if (first.empty()) first = EpsB200Store::LookupMessage(sticky);
+    }
+    s.Done(stream);
+    Require(first.empty(), first.c_str());
+  });
+}
+
+namespace {
+std::vector<unsigned long long> CheckedKeys(const EpsB200Store& s, const Table& t,
+                                            const uint64_t* keys, uint64_t count) {
+  Require(!count || keys, "null keys");
+  std::vector<unsigned long long> out(keys, keys + count);
+  std::unordered_set<unsigned long long> seen;
+  for (auto k : out) {
+    Require(k % s.opt.shard_count == s.opt.shard_id, "key belongs to another shard");
+    Require(k / s.opt.shard_count < t.rows, "unknown parameter row");
+    Require(seen.insert(k).second, "duplicate row");
+  }
+  return out;
+}
+}  // namespace
+
+int eps_b200_read_state(EpsB200Store* store, uint32_t table, const uint64_t* keys,
+                        uint64_t count, float* weights, float* first, float* second,
+                        uint64_t* row_updates, EpsB200Status* status) {
+  return Boundary(status, [&] {
+    auto& s = *Checked(store);
+    std::lock_guard lock(s.mutex);
+    s.Activate();
+    const Table& t = s.Get(table);
+    auto k = CheckedKeys(s, t, keys, count);
+    if (!count) return;
+    const unsigned D = t.def.dimension;
+    cudaStream_t stream = s.Use(nullptr);
+    char* buf = nullptr;
+    const size_t kb = align256(count * 8), pb = align256(count * 12ull * D);
+    Cuda(cudaMallocAsync(reinterpret_cast<void**>(&buf), kb + pb + align256(count * 8) + 256, stream));
+    std::vector<float> packed(count * 3ull * D);
+    std::vector<unsigned long long> upd(count);
+    unsigned* err = reinterpret_cast<unsigned*>(buf + kb + pb + align256(count * 8));
+    try {
+      Cuda(cudaMemsetAsync(err, 0, 4, stream));
+      Cuda(cudaMemcpyAsync(buf, k.data(), count * 8, cudaMemcpyHostToDevice, stream));
+      Cuda(launch_read_rows(t.state, t.updates, D, t.rows, s.opt.shard_count,
+                            reinterpret_cast<unsigned long long*>(buf), count,
+                            reinterpret_cast<float*>(buf + kb),
+                            reinterpret_cast<unsigned long long*>(buf + kb + pb), err, stream));
+      Cuda(cudaMemcpyAsync(packed.data(), buf + kb, count * 12ull * D, cudaMemcpyDeviceToHost, stream));
+      Cuda(cudaMemcpyAsync(upd.data(), buf + kb + pb, count * 8, cudaMemcpyDeviceToHost, stream));
+      cudaFreeAsync(buf, stream);
+      s.Sync(stream);
+    } catch (...) { cudaStreamSynchronize(stream); throw; }
+    s.Done(stream);
+    for (uint64_t r = 0; r < count; ++r) {
+      const float* row = packed.data() + r * 3ull * D;
+      if (weights) std::memcpy(weights + r * D, row, D * 4);
+      if (first) std::memcpy(first + r * D, row + D, D * 4);
+      if (second) std::memcpy(second + r * D, row + 2 * D, D * 4);
+      if (row_updates) row_updates[r] = upd[r];
+    }
+  });
+}
+
+int eps_b200_load_state(EpsB200Store* store, uint32_t table, const uint64_t* keys,
+                        uint64_t count, const float* weights, const float* first,
+                        const float* second, const uint64_t* row_updates,
+                        EpsB200Status* status) {
+  return Boundary(status, [&] {
+    auto& s = *Checked(store);
+    std::lock_guard lock(s.mutex);
+    s.Activate();
+    const Table& t = s.Get(table);
+    auto k = CheckedKeys(s, t, keys, count);
+    if (!count) return;
+    Require(weights && first && second, "null row state");
+    const unsigned D = t.def.dimension;
+    std::vector<float> packed(count * 3ull * D);
+    std::vector<unsigned long long> upd(count, 0);
+    for (uint64_t r = 0; r < count; ++r) {
+      float* row = packed.data() + r * 3ull * D;
+      std::memcpy(row, weights + r * D, D * 4);
+      std::memcpy(row + D, first + r * D, D * 4);
+      std::memcpy(row + 2 * D, second + r * D, D * 4);
+      for (unsigned d = 0; d < 3 * D; ++d) Require(std::isfinite(row[d]), "non-finite cache state");
+      for (unsigned d = 0; d < D; ++d) Require(row[2 * D + d] >= 0, "negative second moment");
+      if (row_updates) upd[r] = row_updates[r];
+    }
+    cudaStream_t stream = s.Use(nullptr);
+    char* buf = nullptr;
+    const size_t kb = align256(count * 8), pb = align256(count * 12ull * D);
+    Cuda(cudaMallocAsync(reinterpret_cast<void**>(&buf), kb + pb + align256(count * 8), stream));
+    try {
+      Cuda(cudaMemcpyAsync(buf, k.data(), count * 8, cudaMemcpyHostToDevice, stream));
+      Cuda(cudaMemcpyAsync(buf + kb, packed.data(), count * 12ull * D, cudaMemcpyHostToDevice, stream));
+      Cuda(cudaMemcpyAsync(buf + kb + pb, upd.data(), count * 8, cudaMemcpyHostToDevice, stream));
+      Cuda(launch_write_rows(t.state, t.updates, D, t.rows, s.opt.shard_count,
+                             reinterpret_cast<unsigned long long*>(buf), count,
+                             reinterpret_cast<float*>(buf + kb),
+                             reinterpret_cast<unsigned long long*>(buf + kb + pb), t.dtable, stream));
+      cudaFreeAsync(buf, stream);
+      s.Sync(stream);
+    } catch (...) { cudaStreamSynchronize(stream); throw; }
+    s.Done(stream);
+  });
+}
+
+int eps_b200_optimizer_state(EpsB200Store* store, uint32_t table, uint64_t* optimizer_sequence,
+                             float* beta1_power, float* beta2_power, EpsB200Status* status) {
+  return Boundary(status, [&] {
+    auto& s = *Checked(store);
+    std::lock_guard lock(s.mutex);
+    s.Activate();
+    const Table& t = s.Get(table);
+    cudaStream_t stream = s.Use(nullptr);
+    DeviceTable d{};
+    Cuda(cudaMemcpyAsync(&d, t.dtable, sizeof(d), cudaMemcpyDeviceToHost, stream));
+    s.Sync(stream);
+    s.Done(stream);
+    if (optimizer_sequence) *optimizer_sequence = d.optimizer_sequence;
+    if (beta1_power) *beta1_power = d.beta1_power;
+    if (beta2_power) *beta2_power = d.beta2_power;
+  });
+}
+
+int eps_b200_profile(EpsB200Store* store, int32_t mode, double* phase_ms,
+                     uint64_t* phase_launches, uint64_t* phase_calls, EpsB200Status* status) {
+  return Boundary(status, [&] {
+    auto& s = *Checked(store);
+    std::lock_guard lock(s.mutex);
+    s.Activate();
+    s.Collect();
+    for (int i = 0; i < EPS_B200_PHASES; ++i) {
+      if (phase_ms) phase_ms[i] = s.phase_ms[i];
+      if (phase_launches) phase_launches[i] = s.phase_launches[i];
+      if (phase_calls) phase_calls[i] = s.phase_calls[i];
+    }
+    if (mode == 1) {
+      for (int i = 0; i < EPS_B200_PHASES; ++i) {
+        s.phase_ms[i] = 0; s.phase_launches[i] = 0; s.phase_calls[i] = 0;
+      }
+      s.profiling = true;
+    } else if (mode == 0) {
+      s.profiling = false;
+    }
+  });
+}
+
+int eps_b200_stats(EpsB200Store* store, EpsB200Stats* out, EpsB200Status* status) {
+  return Boundary(status, [&] {
+    auto& s = *Checked(store);
+    Require(out != nullptr, "null stats output");
+    std::lock_guard lock(s.mutex);
+    s.stats.live_tickets = s.tickets.size();
+    s.stats.tables = s.tables.size();
+    *out = s.stats;
+  });
+}
+
+}  // extern "C"

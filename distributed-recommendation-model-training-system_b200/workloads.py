@@ -1,0 +1,212 @@
+"""Seeded synthetic inputs with the shapes of the reference's benchmark configs.
+
+No dataset is available offline, so every config is a seeded stand-in with the
+stated shapes and value distributions:
+
+* ids: Zipf(alpha) over R rows by exact inverse CDF on ranks 1..R, mapped to
+  ids by the seeded affine bijection id = (a*(rank-1) + b) mod R, gcd(a, R) = 1,
+  so hot rows are spread over the key space;
+* bag lengths: uniform in [1, 64] (config 2), fixed otherwise;
+* gradients: Normal(0, sigma=1e-2) from numpy's counter-based Philox generator;
+* tables: reference initializer U(-0.05, 0.05) with seed 42; LazyAdam
+  lr 1e-3, b1 0.9, b2 0.999, eps 1e-8, initial powers 0.9 / 0.999.
+
+Config numbering follows the reference benchmark list (1 = MovieLens-shaped
+two tables, 2 = 10M x 64 multi-hot, 3 = 26 tables x 128, 4 = push-heavy
+100M x 64, 5 = 1e9 x 32).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from math import gcd
+
+import numpy as np
+
+SUM, MEAN, SEQUENCE = 0, 1, 2
+
+
+@dataclass
+class TableSpec:
+    id: int
+    dimension: int
+    rows: int
+
+
+@dataclass
+class FeatureSpec:
+    table: int
+    feature: int
+    pooling: int
+    keys: np.ndarray          # uint64
+    offsets: np.ndarray       # uint64
+
+    @property
+    def output_rows(self):
+        return len(self.keys) if self.pooling == SEQUENCE else len(self.offsets) - 1
+
+
+@dataclass
+class Workload:
+    name: str
+    tables: list
+    features: list
+    gradients: list           # float32 [output_rows, dim] per feature
+    seed: int
+    meta: dict = field(default_factory=dict)
+
+    @property
+    def occurrences(self):
+        return int(sum(len(f.keys) for f in self.features))
+
+    @property
+    def bags(self):
+        return int(sum(f.output_rows for f in self.features))
+
+    def unique(self):
+        """Unique (table, key) count of the batch (coalesced rows U)."""
+        u = 0
+        for t in self.tables:
+            ks = [f.keys for f in self.features if f.table == t.id]
+            if ks:
+                u += len(np.unique(np.concatenate(ks)))
+        return u
+
+
+_CDF_CACHE: dict = {}
+
+
+def zipf_ranks(rng, rows: int, alpha: float, n: int) -> np.ndarray:
+    """Exact inverse-CDF Zipf ranks in [1, rows] (P(r) ~ r^-alpha)."""
+    key = (rows, alpha)
+    cdf = _CDF_CACHE.get(key)
+    if cdf is None:
+        r = np.arange(1, rows + 1, dtype=np.float64)
+        w = r ** (-alpha)
+        cdf = np.cumsum(w)
+        cdf /= cdf[-1]
+        if rows >= 10_000_000:
+            _CDF_CACHE.clear()
+        _CDF_CACHE[key] = cdf
+    u = rng.random(n)
+    return np.minimum(np.searchsorted(cdf, u, side="left"), rows - 1).astype(np.uint64) + 1
+
+
+def affine(rng, rows: int):
+    while True:
+        a = int(rng.integers(1, rows)) if rows > 1 else 1
+        if gcd(a, rows) == 1:
+            break
+    b = int(rng.integers(0, rows)) if rows > 1 else 0
+    return a, b
+
+
+def to_ids(ranks: np.ndarray, rows: int, a: int, b: int) -> np.ndarray:
+    r = ranks.astype(np.uint64) - np.uint64(1)
+    # (a*r + b) mod rows without overflow: rows < 2^40, use Python ints via object
+    # arithmetic only when needed
+    if rows * max(a, 1) < 2**63:
+        return ((r.astype(np.int64) * a + b) % rows).astype(np.uint64)
+    return np.array([(a * int(x) + b) % rows for x in r], dtype=np.uint64)
+
+
+def gradients_for(rng, features, dims, sigma=1e-2):
+    return [rng.normal(0.0, sigma, size=(f.output_rows, dims[f.table])).astype(np.float32)
+            for f in features]
+
+
+def config1(seed: int = 1) -> Workload:
+    """Two tables (943 x 32, 1682 x 32), batch 128, one uniform id per table, no pooling."""
+    rng = np.random.Generator(np.random.Philox(seed))
+    tables = [TableSpec(1, 32, 943), TableSpec(2, 32, 1682)]
+    feats = []
+    for i, t in enumerate(tables):
+        keys = rng.integers(0, t.rows, size=128).astype(np.uint64)
+        feats.append(FeatureSpec(t.id, i, SEQUENCE, keys, np.array([0, 128], np.uint64)))
+    grads = gradients_for(rng, feats, {t.id: t.dimension for t in tables})
+    return Workload("cfg1: 943x32 + 1682x32, batch 128, one id per table, sequence", tables,
+                    feats, grads, seed)
+
+
+def config2(seed: int = 2, batch: int = 4096, rows: int = 10_000_000, dim: int = 64,
+            features: int = 8, alpha: float = 1.05, max_bag: int = 64) -> Workload:
+    """One 10M x 64 table, 8 multi-hot features, bags U[1,64], Zipf(1.05),
+    features 0-3 sum and 4-7 mean."""
+    rng = np.random.Generator(np.random.Philox(seed))
+    a, b = affine(rng, rows)
+    feats = []
+    for fi in range(features):
+        lengths = rng.integers(1, max_bag + 1, size=batch).astype(np.uint64)
+        offsets = np.zeros(batch + 1, np.uint64)
+        np.cumsum(lengths, out=offsets[1:])
+        n = int(offsets[-1])
+        keys = to_ids(zipf_ranks(rng, rows, alpha, n), rows, a, b)
+        feats.append(FeatureSpec(1, fi, SUM if fi < features // 2 else MEAN, keys, offsets))
+    grads = gradients_for(rng, feats, {1: dim})
+    return Workload(f"cfg2: {rows}x{dim}, {features} features, batch {batch}, bags U[1,{max_bag}], "
+                    f"Zipf({alpha}), f0-3 sum / f4-7 mean", [TableSpec(1, dim, rows)], feats, grads,
+                    seed, {"a": a, "b": b, "alpha": alpha})
+
+
+def config4(seed: int = 4, rows: int = 100_000_000, dim: int = 64, n: int = 262_144,
+            alpha: float = 1.2) -> Workload:
+    """Push-heavy: one 100M x 64 table, 262,144 gradient rows, Zipf(1.2)
+    (one id per sequence position)."""
+    rng = np.random.Generator(np.random.Philox(seed))
+    a, b = affine(rng, rows)
+    keys = to_ids(zipf_ranks(rng, rows, alpha, n), rows, a, b)
+    feats = [FeatureSpec(1, 0, SEQUENCE, keys, np.array([0, n], np.uint64))]
+    grads = gradients_for(rng, feats, {1: dim})
+    return Workload(f"cfg4: {rows}x{dim}, {n} gradient rows, Zipf({alpha})",
+                    [TableSpec(1, dim, rows)], feats, grads, seed, {"a": a, "b": b})
+
+
+def config3(seed: int = 3, batch: int = 65536, tables: int = 26, dim: int = 128,
+            alpha: float = 1.1, row_scale: float = 1.0) -> Workload:
+    """26 tables x 128, rows log-uniform in [1e3, 4e7], one id per table, Zipf(1.1)."""
+    rng = np.random.Generator(np.random.Philox(seed))
+    specs, feats = [], []
+    for t in range(tables):
+        rows = int(np.exp(rng.uniform(np.log(1e3), np.log(4e7))) * row_scale)
+        rows = max(rows, 1)
+        specs.append(TableSpec(t + 1, dim, rows))
+        a, b = affine(rng, rows)
+        keys = to_ids(zipf_ranks(rng, rows, alpha, batch), rows, a, b)
+        feats.append(FeatureSpec(t + 1, t, SUM, keys, np.arange(batch + 1, dtype=np.uint64)))
+    grads = gradients_for(rng, feats, {s.id: s.dimension for s in specs})
+    return Workload(f"cfg3: {tables} tables x {dim}, batch {batch}, one id per table, Zipf({alpha})",
+                    specs, feats, grads, seed)
+
+
+def small(seed: int, dims=(2, 32, 64, 128), bags: int = 64, max_bag: int = 12,
+          rows: int = 300, alpha: float = 1.2, poolings=(SUM, MEAN, SEQUENCE)) -> Workload:
+    """Small multi-table case with duplicates, empty bags and all pooling modes."""
+    rng = np.random.Generator(np.random.Philox(seed))
+    tables = [TableSpec(i + 1, d, rows + 17 * i) for i, d in enumerate(dims)]
+    feats = []
+    fid = 0
+    for t in tables:
+        a, b = affine(rng, t.rows)
+        for pooling in poolings:
+            lengths = rng.integers(0, max_bag + 1, size=bags).astype(np.uint64)
+            offsets = np.zeros(bags + 1, np.uint64)
+            np.cumsum(lengths, out=offsets[1:])
+            keys = to_ids(zipf_ranks(rng, t.rows, alpha, int(offsets[-1])), t.rows, a, b)
+            feats.append(FeatureSpec(t.id, fid, pooling, keys, offsets))
+            fid += 1
+    grads = gradients_for(rng, feats, {t.id: t.dimension for t in tables})
+    return Workload("small", tables, feats, grads, seed)
+
+
+def hot(seed: int, dim: int = 64, rows: int = 1000, n: int = 20000) -> Workload:
+    """Very skewed single table: long coalesced segments (tile-spanning rows)."""
+    rng = np.random.Generator(np.random.Philox(seed))
+    keys = to_ids(zipf_ranks(rng, rows, 1.6, n), rows, *affine(rng, rows))
+    lengths = rng.integers(1, 40, size=n // 20).astype(np.uint64)
+    offsets = np.zeros(len(lengths) + 1, np.uint64)
+    np.cumsum(lengths, out=offsets[1:])
+    offsets = offsets[offsets <= n]
+    keys = keys[: int(offsets[-1])]
+    feats = [FeatureSpec(1, 0, MEAN, keys, offsets),
+             FeatureSpec(1, 1, SEQUENCE, keys.copy(), np.array([0, len(keys)], np.uint64))]
+    grads = gradients_for(rng, feats, {1: dim})
+    return Workload("hot", [TableSpec(1, dim, rows)], feats, grads, seed)

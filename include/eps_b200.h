@@ -1,0 +1,218 @@
+/*
+ * eps_b200.h -- C ABI of the B200 embedding parameter store (libeps_b200.so).
+ *
+ * The library keeps embedding tables and their sparse LazyAdam state resident in
+ * GPU memory and runs the reference parameter server's hot path on the GPU:
+ * batched pull (gather + sum/mean/sequence pooling), push (coalesce duplicate ids,
+ * segment-sum their gradients) and the row-wise LazyAdam update.
+ *
+ * Citations name the interface of the reference project
+ * (Zhang-Xin-Duke/distributed-recommendation-model-training-system) that each
+ * entry point replaces, as path:line inside that project.
+ *
+ * Conventions (mirroring include/eps/runtime_c.h and adapters/entropy/runtime_c.cpp):
+ *  - every entry point returns 0 on success, else eps::Error::Code + 1
+ *    (include/eps/types.hpp:17-25) and copies the message into status->message;
+ *  - plain pointers and sizes only; buffers flagged `device >= 0` / `*_on_device`
+ *    are device pointers on the store's GPU, otherwise host pointers;
+ *  - `stream` is a cudaStream_t (NULL = the store's own stream).  All work of one
+ *    store is serialised; calls on one store are thread-safe (one mutex, as the
+ *    reference runtime's per-runtime mutex, adapters/entropy/runtime_c.cpp:177).
+ *  - nothing here allocates on the caller's behalf except the returned store;
+ *    results are written into caller-provided buffers.
+ */
+#ifndef EPS_B200_H
+#define EPS_B200_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define EPS_B200_ABI 1
+
+#if defined(_WIN32)
+#define EPS_B200_EXPORT __declspec(dllexport)
+#else
+#define EPS_B200_EXPORT __attribute__((visibility("default")))
+#endif
+
+/* Same layout and codes as EpsStatus (include/eps/runtime_c.h:8). */
+typedef struct { int32_t code; char message[1024]; } EpsB200Status;
+
+enum {
+  EPS_B200_OK = 0,
+  EPS_B200_INVALID_ARGUMENT = 1,   /* Error::Code::invalid_argument + 1 */
+  EPS_B200_UNAVAILABLE = 2,
+  EPS_B200_STALE_GENERATION = 3,
+  EPS_B200_RETIRED_REQUEST = 4,
+  EPS_B200_CAPACITY_EXCEEDED = 5,
+  EPS_B200_RUN_FAILED = 6
+};
+
+/* eps::Pooling (include/eps/types.hpp:51) */
+enum { EPS_B200_SUM = 0, EPS_B200_MEAN = 1, EPS_B200_SEQUENCE = 2 };
+
+typedef struct EpsB200Store EpsB200Store;
+
+/* Subset of eps::RuntimeOptions (include/eps/runtime.hpp:15-39) plus the GPU. */
+typedef struct {
+  int32_t device;
+  uint32_t shard_id;
+  uint32_t shard_count;
+  uint32_t max_live_tickets;     /* RuntimeOptions::max_live_tickets (runtime.hpp:24) */
+  uint64_t partition_epoch;
+  uint64_t state_bytes;          /* HBM budget for table state (runtime.hpp:20) */
+  uint32_t flags;                /* EPS_B200_FLAG_* */
+  uint32_t reserved;
+} EpsB200Options;
+
+/* Sum every coalesced row's gradients serially in occurrence order, as the
+ * reference does (src/access/batch_access.cpp:109-119), also for rows with very
+ * many occurrences.  Without it such rows (> 64 occurrences) are reduced in
+ * parallel pieces combined in a fixed order: deterministic, and within 1e-6
+ * relative of the serial sum, but not bit-identical. */
+#define EPS_B200_FLAG_REFERENCE_ORDER 1u
+
+/* eps::TableDefinition + eps::OptimizerConfig (include/eps/types.hpp:76-97).
+ * key_space: keys of this table lie in [0, key_space); the shard holds the slots
+ * of keys k with k % shard_count == shard_id (src/store/shard_store.cpp:77),
+ * initialised up front with the reference initializer. */
+typedef struct {
+  uint32_t id;
+  uint32_t dimension;
+  uint32_t shard_count;
+  int32_t has_weight_bounds;
+  uint64_t partition_epoch;
+  float learning_rate, beta1, beta2, epsilon;
+  float initial_beta1_power, initial_beta2_power;
+  float weight_min, weight_max;
+  float initialization_min, initialization_max;
+  uint64_t initialization_seed;
+  uint64_t key_space;
+} EpsB200Table;
+
+/* eps::FeatureInput (include/eps/types.hpp:99-107).  valid_lengths may be NULL
+ * (then the offset differences are the bag lengths). */
+typedef struct {
+  uint32_t table, feature, pooling, reserved;
+  const uint64_t* keys; uint64_t key_count;
+  const uint64_t* offsets; uint64_t offset_count;
+  const uint64_t* valid_lengths;
+} EpsB200Feature;
+
+/* Feature tensor [rows, columns] f32: eps::EpsBuffer (include/eps/runtime_c.h:14-19)
+ * without the ownership callbacks, since the caller owns every buffer. */
+typedef struct {
+  uint32_t feature, reserved;
+  uint64_t rows, columns;
+  void* data;
+  int32_t device;                /* < 0: host memory */
+  int32_t reserved2;
+} EpsB200Buffer;
+
+/* Counters in the spirit of eps::RuntimeStats (include/eps/runtime.hpp:48-95). */
+typedef struct {
+  uint64_t lookups, updates, rejected_updates, duplicate_requests;
+  uint64_t live_tickets, state_bytes, rows, tables;
+  uint64_t kernel_launches;      /* device kernels this store has launched */
+} EpsB200Stats;
+
+/* Phases of a lookup + push round, for eps_b200_profile. */
+enum {
+  EPS_B200_PHASE_LOOKUP = 0,     /* gather + pooling (+ occurrence list) */
+  EPS_B200_PHASE_SORT = 1,       /* stable radix sort of the occurrences */
+  EPS_B200_PHASE_PRESCAN = 2,    /* gradient finiteness / bound scan + decision */
+  EPS_B200_PHASE_APPLY = 3,      /* coalesced segment-sum fused with LazyAdam */
+  EPS_B200_PHASE_FINALIZE = 4,   /* beta powers / optimizer sequence */
+  EPS_B200_PHASES = 5
+};
+
+EPS_B200_EXPORT uint32_t eps_b200_abi_version(void);
+
+/* Creates one shard store on `device`.  Replaces constructing
+ * eps::CpuParameterService (include/eps/runtime.hpp:104) /
+ * eps::CudaCacheBackend (include/eps/cuda_cache_backend.hpp:19). */
+EPS_B200_EXPORT int eps_b200_create(const EpsB200Options* options, EpsB200Store** out, EpsB200Status* status);
+EPS_B200_EXPORT void eps_b200_destroy(EpsB200Store* store);
+
+/* ParameterService::CreateTable (include/eps/parameter_service.hpp:16),
+ * CacheBackend::Define (include/eps/cache_backend.hpp:15); validation of
+ * ShardStore::Create (src/store/shard_store.cpp:33-60).  Idempotent for an
+ * identical definition. */
+EPS_B200_EXPORT int eps_b200_create_table(EpsB200Store* store, const EpsB200Table* table,
+                          EpsB200Status* status);
+
+/* Pull.  With shard_partial == 0: DistributedClient::Lookup
+ * (include/eps/distributed_client.hpp:36) over this store -- pooled outputs
+ * are merged and mean bags divided by the bag length
+ * (src/client/distributed_client.cpp:173-188,227-232).  With shard_partial == 1:
+ * ParameterService::Lookup (include/eps/parameter_service.hpp:17) -- the
+ * unnormalised shard contribution of src/access/batch_access.cpp:53-80 for keys
+ * owned by this shard, valid_lengths carrying the original bag lengths.
+ * outputs[i] receives feature i: [bags, dim] (sum/mean) or [keys, dim]
+ * (sequence).  Unless read_only, *ticket receives the lookup ticket to pass to
+ * eps_b200_push or eps_b200_release (LookupReply::ticket, types.hpp:151-156).
+ * Device inputs are validated on the GPU; such errors are reported by the next
+ * push / release / synchronize of the ticket.  Host outputs imply a synchronous
+ * call that reports them directly. */
+EPS_B200_EXPORT int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_t count,
+                    int32_t input_on_device, int32_t read_only, int32_t shard_partial,
+                    EpsB200Buffer* outputs, void* stream, uint64_t* ticket,
+                    EpsB200Status* status);
+
+/* Push gradients of a ticket's feature tensors: DistributedClient::Push /
+ * ParameterService::Push (include/eps/parameter_service.hpp:18), i.e.
+ * ReduceGradients (src/access/batch_access.cpp:82-125) + ValidateLazyAdam /
+ * ApplyLazyAdam (src/update/lazy_adam.cpp:7-42), all-or-nothing.  A rejected
+ * push leaves the state unchanged and the ticket live (retryable); a push of an
+ * already completed ticket is acknowledged without effect.  wait == 0 returns
+ * after enqueueing; its outcome is then reported by eps_b200_synchronize. */
+EPS_B200_EXPORT int eps_b200_push(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gradients,
+                  uint64_t count, void* stream, int32_t wait, EpsB200Status* status);
+
+/* ParameterService::Release (include/eps/parameter_service.hpp:20). */
+EPS_B200_EXPORT int eps_b200_release(EpsB200Store* store, uint64_t ticket, EpsB200Status* status);
+
+/* Waits for all queued work and reports the first deferred error
+ * (DeviceTensor::WaitOnStream contract, include/eps/cache_agent.hpp:7-14). */
+EPS_B200_EXPORT int eps_b200_synchronize(EpsB200Store* store, EpsB200Status* status);
+
+/* ParameterService::ReadState (include/eps/parameter_service.hpp:23-24) /
+ * CacheBackend::ReadBack (include/eps/cache_backend.hpp:27): host arrays,
+ * weights/first/second are [count, dim]. */
+EPS_B200_EXPORT int eps_b200_read_state(EpsB200Store* store, uint32_t table, const uint64_t* keys,
+                        uint64_t count, float* weights, float* first, float* second,
+                        uint64_t* row_updates, EpsB200Status* status);
+
+/* CacheBackend::Load (include/eps/cache_backend.hpp:17-18) /
+ * ShardStore::Import (src/store/shard_store.cpp:126-137): overwrite rows with
+ * finite state, v >= 0 (src/cache/host_backend.cpp:135-140). */
+EPS_B200_EXPORT int eps_b200_load_state(EpsB200Store* store, uint32_t table, const uint64_t* keys,
+                        uint64_t count, const float* weights, const float* first,
+                        const float* second, const uint64_t* row_updates,
+                        EpsB200Status* status);
+
+/* The table's optimizer bookkeeping (TableState, src/store/shard_store.hpp:11-16;
+ * the values an UpdateContext carries, include/eps/types.hpp:180-188). */
+EPS_B200_EXPORT int eps_b200_optimizer_state(EpsB200Store* store, uint32_t table, uint64_t* optimizer_sequence,
+                             float* beta1_power, float* beta2_power, EpsB200Status* status);
+
+/* Per-phase device time measured with CUDA events recorded on the launching
+ * stream around each phase (the reference's PhaseTimer counters,
+ * src/common/phase_timer.hpp:9-23, RuntimeStats *_nanoseconds fields).
+ * mode 1: reset and start recording, 0: stop, -1: leave as is.  Each output
+ * array (may be NULL) has EPS_B200_PHASES entries: accumulated milliseconds,
+ * kernel launches and calls per phase, collected after the recorded work ends. */
+EPS_B200_EXPORT int eps_b200_profile(EpsB200Store* store, int32_t mode, double* phase_ms,
+                                     uint64_t* phase_launches, uint64_t* phase_calls,
+                                     EpsB200Status* status);
+
+/* CpuParameterService::Stats (include/eps/runtime.hpp:134). */
+EPS_B200_EXPORT int eps_b200_stats(EpsB200Store* store, EpsB200Stats* stats, EpsB200Status* status);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

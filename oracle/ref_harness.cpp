@@ -1,0 +1,187 @@
+// ref_harness.cpp -- drives the UNMODIFIED reference CPU parameter server
+// (eps_core compiled from the reference sources by oracle/Makefile) through its
+// own public API: n in-process CpuParameterService shards behind a
+// DistributedClient (include/eps/distributed_client.hpp:32-70), exactly as the
+// reference's tests/weight_bounds_tests.cpp:23-33 does.
+//
+// TEST INFRASTRUCTURE ONLY: used by tests/golden/make_golden.py, the parity
+// tests and bench.py's CPU-baseline / --impl reference legs.  Never linked by
+// the product.
+//
+// Exposes a small C interface so Python (ctypes) can call it.
+#include <chrono>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "eps/distributed_client.hpp"
+#include "eps/prepared_lookup.hpp"
+#include "eps/runtime.hpp"
+
+using namespace eps;
+
+namespace {
+struct Harness {
+  std::vector<std::shared_ptr<CpuParameterService>> shards;
+  std::unique_ptr<DistributedClient> client;
+  std::map<std::uint64_t, DistributedBatch> batches;
+  std::uint64_t sequence = 0;
+  std::string run = "oracle";
+  std::uint32_t learner = 0;
+};
+
+void Message(char* err, const std::string& text) {
+  if (err) { std::strncpy(err, text.c_str(), 1023); err[1023] = 0; }
+}
+template <typename T> int Take(Result<T>&& r, T* out, char* err) {
+  if (auto e = std::get_if<Error>(&r)) { Message(err, e->message); return int(e->code) + 1; }
+  if (out) *out = std::get<T>(std::move(r));
+  return 0;
+}
+}  // namespace
+
+extern "C" {
+
+struct RhTable {
+  std::uint32_t id, dimension;
+  float learning_rate, beta1, beta2, epsilon, initial_beta1_power, initial_beta2_power;
+  std::int32_t has_bounds; float bound_min, bound_max;
+  float init_min, init_max; std::uint64_t init_seed;
+};
+
+struct RhFeature {
+  std::uint32_t table, feature, pooling;
+  const std::uint64_t* keys; std::uint64_t key_count;
+  const std::uint64_t* offsets; std::uint64_t offset_count;
+};
+
+void* rh_create(std::uint32_t shard_count, std::uint64_t state_bytes, char* err) {
+  try {
+    auto h = std::make_unique<Harness>();
+    for (std::uint32_t s = 0; s < shard_count; ++s) {
+      RuntimeOptions o;
+      o.run_id = h->run; o.shard_id = s; o.shard_count = shard_count;
+      // Raise the default request/ticket budgets (include/eps/runtime.hpp:20-23)
+      // so the benchmark batch sizes are admitted.
+      o.state_bytes = state_bytes;
+      o.max_request_bytes = 1ULL << 40;
+      o.ticket_payload_bytes = 1ULL << 40;
+      o.queue_payload_bytes = 1ULL << 40;
+      o.dependency_payload_bytes = 1ULL << 40;
+      h->shards.push_back(std::make_shared<CpuParameterService>(o));
+    }
+    std::vector<std::shared_ptr<ParameterService>> services(h->shards.begin(), h->shards.end());
+    h->client = std::make_unique<DistributedClient>(services);
+    return h.release();
+  } catch (const std::exception& e) { Message(err, e.what()); return nullptr; }
+}
+
+void rh_destroy(void* p) { delete static_cast<Harness*>(p); }
+
+int rh_create_table(void* p, const RhTable* t, char* err) {
+  auto& h = *static_cast<Harness*>(p);
+  TableDefinition d{t->id, t->dimension, std::uint32_t(h.shards.size()), 1,
+      {t->learning_rate, t->beta1, t->beta2, t->epsilon, t->initial_beta1_power,
+       t->initial_beta2_power}, t->init_min, t->init_max, t->init_seed};
+  if (t->has_bounds) d.optimizer.weight_bounds = WeightBounds{t->bound_min, t->bound_max};
+  Ack ack;
+  return Take(h.client->CreateTable(d), &ack, err);
+}
+
+// Lookup through PrepareLookupInputs with raised limits + LookupPrepared
+// (the default-limit Lookup would reject benchmark-sized batches,
+// src/client/distributed_client.cpp:39).  outputs[f] receive the merged,
+// mean-normalised feature tensors.
+int rh_lookup(void* p, std::uint32_t count, const RhFeature* features, std::int32_t read_only,
+              float** outputs, std::uint64_t* batch_out, char* err) {
+  auto& h = *static_cast<Harness*>(p);
+  std::vector<FeatureInput> input;
+  for (std::uint32_t i = 0; i < count; ++i) {
+    const auto& f = features[i];
+    FeatureInput x{f.table, f.feature, static_cast<Pooling>(f.pooling),
+                   std::vector<Key>(f.keys, f.keys + f.key_count),
+                   std::vector<std::uint64_t>(f.offsets, f.offsets + f.offset_count), {}};
+    for (std::uint64_t b = 0; b + 1 < f.offset_count; ++b)
+      x.valid_lengths.push_back(f.offsets[b + 1] - f.offsets[b]);
+    input.push_back(std::move(x));
+  }
+  PreparationLimits limits{1ULL << 40, 1ULL << 40, 1024};
+  auto prepared = PrepareLookupInputs(std::move(input), h.shards.size(), limits);
+  PreparedLookup lookup;
+  if (int rc = Take(std::move(prepared), &lookup, err)) return rc;
+  const auto seq = h.sequence++;
+  auto result = h.client->LookupPrepared({h.run, h.learner, seq, Phase::lookup}, 1,
+                                         read_only != 0, std::move(lookup));
+  DistributedBatch batch;
+  if (int rc = Take(std::move(result), &batch, err)) return rc;
+  for (std::uint32_t i = 0; i < count; ++i) {
+    const auto& values = batch.features()[i].values;
+    if (outputs && outputs[i]) std::memcpy(outputs[i], values.data(), values.size() * 4);
+  }
+  h.batches.emplace(seq, std::move(batch));
+  if (batch_out) *batch_out = seq;
+  return 0;
+}
+
+int rh_push(void* p, std::uint64_t batch, std::uint32_t count, const std::uint32_t* feature_ids,
+            const float* const* grads, const std::uint64_t* rows, const std::uint32_t* dims,
+            char* err) {
+  auto& h = *static_cast<Harness*>(p);
+  auto it = h.batches.find(batch);
+  if (it == h.batches.end()) { Message(err, "unknown batch"); return 1; }
+  std::vector<TensorBlock> gradients;
+  for (std::uint32_t i = 0; i < count; ++i)
+    gradients.push_back({feature_ids[i], {rows[i], dims[i]},
+                         std::vector<float>(grads[i], grads[i] + rows[i] * dims[i])});
+  Ack ack;
+  int rc = Take(h.client->Push(it->second, std::move(gradients)), &ack, err);
+  if (rc == 0) h.batches.erase(it);
+  return rc;
+}
+
+int rh_release(void* p, std::uint64_t batch, char* err) {
+  auto& h = *static_cast<Harness*>(p);
+  auto it = h.batches.find(batch);
+  if (it == h.batches.end()) { Message(err, "unknown batch"); return 1; }
+  Ack ack;
+  int rc = Take(h.client->Release(it->second), &ack, err);
+  h.batches.erase(it);
+  return rc;
+}
+
+// ParameterService::ReadState for one row on its home shard key % n.
+int rh_read(void* p, std::uint32_t table, std::uint64_t key, float* w, float* m, float* v,
+            std::uint64_t* updates, char* err) {
+  auto& h = *static_cast<Harness*>(p);
+  const auto home = ShardId(key % h.shards.size());
+  std::vector<RowState> rows;
+  int rc = Take(h.shards[home]->ReadState({{{table, key}, home, Placement::cpu, 0, 0, 0}}).get(),
+                &rows, err);
+  if (rc) return rc;
+  const auto& r = rows.at(0);
+  std::memcpy(w, r.weights.data(), r.weights.size() * 4);
+  std::memcpy(m, r.first_moment.data(), r.first_moment.size() * 4);
+  std::memcpy(v, r.second_moment.data(), r.second_moment.size() * 4);
+  *updates = r.row_updates;
+  return 0;
+}
+
+// Shard-level phase counters (include/eps/runtime.hpp:76-80) summed over shards.
+int rh_stats(void* p, std::uint64_t* out4, char* err) {
+  auto& h = *static_cast<Harness*>(p);
+  out4[0] = out4[1] = out4[2] = out4[3] = 0;
+  for (auto& s : h.shards) {
+    RuntimeStats st;
+    if (int rc = Take(s->Stats().get(), &st, err)) return rc;
+    out4[0] += st.lookup_prepare_nanoseconds;
+    out4[1] += st.gradient_prepare_nanoseconds;
+    out4[2] += st.cpu_optimizer_nanoseconds;
+    out4[3] += st.rows;
+  }
+  return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,304 @@
+"""GPU parity: the CUDA path (through the C ABI) against the reference's golden
+vectors and the CPU oracle, on the same seeded inputs.
+
+Bars (fp32):
+* lookup outputs (sum, mean, sequence; 1-shard client merge and 2-shard partials):
+  bit-exact;
+* coalescing + LazyAdam with the reference summation order flag: w, m, v and
+  row_updates bit-exact, beta powers and optimizer sequence exact;
+* default order: rows with at most 64 occurrences per push bit-exact; longer rows
+  (reduced in parallel pieces) within |a-b| <= 1e-6 * max(|b|, S) + 1e-12, where S
+  is the row's condition scale (propagated sum of |terms|, see below);
+* a rejected push leaves every row, counter and beta power unchanged.
+"""
+import numpy as np
+import pytest
+
+import golden_cases
+from oracle_lib import MEAN, SEQUENCE, SUM, Feature, Oracle, TableDef
+
+pytestmark = pytest.mark.gpu
+
+F32 = np.float32
+
+
+def bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+def make_store(eps, tables, reference_order=False, shard_count=1, shard_id=0):
+    s = eps.ParameterStore(device=0, reference_order=reference_order, shard_count=shard_count,
+                           shard_id=shard_id, state_bytes=8 << 30)
+    for t in tables:
+        s.create_table(eps.TableDefinition(
+            id=t.id, dimension=t.dimension, key_space=t.rows, learning_rate=t.learning_rate,
+            beta1=t.beta1, beta2=t.beta2, epsilon=t.epsilon,
+            initial_beta1_power=t.initial_beta1_power, initial_beta2_power=t.initial_beta2_power,
+            weight_bounds=t.bounds, initialization_min=t.init_min, initialization_max=t.init_max,
+            initialization_seed=t.init_seed, shard_count=shard_count))
+    return s
+
+
+def inputs(eps, feats):
+    return [eps.FeatureInput(f.table, f.feature, f.pooling, f.keys, f.offsets) for f in feats]
+
+
+def occurrence_counts(feats, table):
+    ks = [f.keys for f in feats if f.table == table]
+    if not ks:
+        return {}
+    u, c = np.unique(np.concatenate(ks), return_counts=True)
+    return dict(zip(u.tolist(), c.tolist()))
+
+
+# ----------------------------------------------------------------- golden
+@pytest.mark.parametrize("name", golden_cases.CASES)
+def test_lookup_bit_exact_vs_reference(eps, name):
+    case = golden_cases.load(name)
+    s = make_store(eps, case.tables)
+    _, outs = s.lookup(inputs(eps, case.features), read_only=True)
+    for got, want in zip(outs, case.lookup[1]):
+        assert got.shape == want.shape
+        assert np.array_equal(bits(got), bits(want)), name
+
+
+@pytest.mark.parametrize("reference_order", [True, False])
+@pytest.mark.parametrize("name", golden_cases.CASES)
+def test_push_vs_reference(eps, name, reference_order):
+    case = golden_cases.load(name)
+    s = make_store(eps, case.tables, reference_order=reference_order)
+    for step in range(case.steps):
+        ticket, outs = s.lookup(inputs(eps, case.features))
+        s.push(ticket, case.grads[step])
+    for t in case.tables:
+        keys, w, m, v, upd = case.state[t.id]
+        gw, gm, gv, gu = s.read_state(t.id, keys)
+        assert np.array_equal(gu, upd)
+        counts = occurrence_counts(case.features, t.id)
+        short = np.array([counts[int(k)] <= 64 for k in keys])
+        if reference_order:
+            short[:] = True
+        for got, want in ((gw, w), (gm, m), (gv, v)):
+            assert np.array_equal(bits(got[short]), bits(want[short])), name
+            if (~short).any():
+                err = np.abs(got[~short].astype(np.float64) - want[~short])
+                scale = np.maximum(np.abs(want[~short]), 1e-3)
+                assert (err <= 1e-5 * scale + 1e-9).all(), (name, err.max())
+        seq, b1p, b2p = s.optimizer_state(t.id)
+        assert seq == case.steps
+        e1, e2 = F32(0.9), F32(0.999)
+        for _ in range(case.steps):
+            e1, e2 = F32(e1 * F32(0.9)), F32(e2 * F32(0.999))
+        assert F32(b1p) == e1 and F32(b2p) == e2
+    s.close()
+
+
+def test_shard_partials_merge_bit_exact(eps):
+    """Two shard stores (key % 2) return the ParameterService::Lookup partials; merged
+    in shard order and divided once for mean they equal the reference's 2-shard
+    DistributedClient output bit for bit."""
+    case = golden_cases.load("small_multi_table")
+    stores = [make_store(eps, case.tables, shard_count=2, shard_id=i) for i in range(2)]
+    parts = []
+    for sid, st in enumerate(stores):
+        feats, positions = [], []
+        for f in case.features:
+            mask = (f.keys % 2) == sid
+            keys = f.keys[mask]
+            bag = np.repeat(np.arange(len(f.offsets) - 1), np.diff(f.offsets).astype(np.int64))
+            counts = np.bincount(bag[mask], minlength=len(f.offsets) - 1)
+            offs = np.zeros(len(f.offsets), np.uint64)
+            np.cumsum(counts, out=offs[1:])
+            lens = np.diff(f.offsets).astype(np.uint64)
+            feats.append(eps.FeatureInput(f.table, f.feature, f.pooling, keys, offs, lens))
+            positions.append(np.nonzero(mask)[0])
+        _, outs = st.lookup(feats, read_only=True, shard_partial=True)
+        parts.append((outs, positions))
+    for fi, f in enumerate(case.features):
+        d = outs[fi].shape[1]
+        out = np.zeros((f.output_rows, d), F32)
+        for outs_s, pos in parts:
+            if f.pooling == SEQUENCE:
+                out[pos[fi]] = outs_s[fi]
+            else:
+                out += outs_s[fi]
+        if f.pooling == MEAN:
+            lens = np.diff(f.offsets).astype(np.int64)
+            nz = lens > 0
+            out[nz] = out[nz] / lens[nz, None].astype(F32)
+        assert np.array_equal(bits(out), bits(case.lookup[2][fi]))
+    for st in stores:
+        st.close()
+
+
+# -------------------------------------------------------------- known answers
+def kat_tables():
+    return [TableDef(id=1, dimension=2, learning_rate=0.1, init_min=0.25, init_max=0.25, rows=8)]
+
+
+def test_pooling_and_update_kat(eps):
+    # tests/core_tests.cpp:68-85 of the reference
+    s = make_store(eps, kat_tables())
+    o = Oracle(kat_tables())
+    feats = [Feature(1, 0, SUM, [1, 1, 2], [0, 3, 3]), Feature(1, 1, MEAN, [1, 3], [0, 2])]
+    ticket, outs = s.lookup(inputs(eps, feats))
+    assert abs(outs[0][0, 0] - 0.75) < 1e-5 and outs[0][1, 0] == 0
+    assert abs(outs[1][0, 0] - 0.25) < 1e-5
+    grads = [np.array([[1, 2], [0, 0]], F32), np.array([[4, 6]], F32)]
+    s.push(ticket, grads)
+    assert o.push(feats, grads) == 0
+    w, m, v, u = s.read_state(1, [1, 2, 3])
+    st, upd = o.state(1)
+    assert np.array_equal(bits(w), bits(st[[1, 2, 3], 0])) and np.array_equal(bits(m), bits(st[[1, 2, 3], 1]))
+    assert np.array_equal(bits(v), bits(st[[1, 2, 3], 2])) and list(u) == [1, 1, 1]
+    assert abs(m[0, 0] - 0.4) < 1e-5 and abs(v[0, 1] - 0.049) < 1e-5 and abs(w[0, 0] - 0.15) < 1e-5
+    # a repeated Push of the same ticket is acknowledged without effect
+    s.push(ticket, grads)
+    assert s.read_state(1, [1])[3][0] == 1
+    assert s.stats()["duplicate_requests"] == 1
+
+
+def test_bounded_closed_form(eps):
+    # tests/weight_bounds_tests.cpp:28-43 of the reference, checked against the oracle
+    t = [TableDef(id=1, dimension=2, learning_rate=1.0, init_min=0.5, init_max=0.5,
+                  bounds=(-0.1, 0.2), rows=8)]
+    s, o = make_store(eps, t), Oracle(t)
+    f = [Feature(1, 0, SEQUENCE, [1], [0, 1])]
+    for seq in range(1, 7):
+        g = [np.full((1, 2), 10 if seq <= 2 else -10, F32)]
+        ticket, outs = s.lookup(inputs(eps, f))
+        assert np.array_equal(bits(outs[0]), bits(o.lookup(f)[0]))
+        s.push(ticket, g)
+        assert o.push(f, g) == 0
+        w, m, v, _ = s.read_state(1, [1])
+        st, _ = o.state(1)
+        assert np.array_equal(bits(w[0]), bits(st[1, 0])) and np.array_equal(bits(v[0]), bits(st[1, 2]))
+
+
+def test_rejected_push_leaves_state_unchanged_and_is_retryable(eps):
+    # tests/core_tests.cpp:98-105 and :214-222 of the reference
+    s = make_store(eps, kat_tables())
+    f = [Feature(1, 0, SEQUENCE, [1, 2], [0, 2])]
+    ticket, _ = s.lookup(inputs(eps, f))
+    before = s.read_state(1, [1, 2])
+    bad = np.array([[1, 1], [np.finfo(F32).max, 1]], F32)
+    with pytest.raises(eps.EpsError) as e:
+        s.push(ticket, [bad])
+    assert e.value.code == eps.INVALID_ARGUMENT and "overflow" in e.value.message
+    after = s.read_state(1, [1, 2])
+    for a, b in zip(before, after):
+        assert np.array_equal(np.asarray(a).view(np.uint32) if a.dtype == F32 else a,
+                              np.asarray(b).view(np.uint32) if b.dtype == F32 else b)
+    assert s.optimizer_state(1) == (0, F32(0.9), F32(0.999))
+    with pytest.raises(eps.EpsError) as e:
+        s.push(ticket, [np.array([[np.nan, 0], [0, 0]], F32)])
+    assert "non-finite" in e.value.message
+    with pytest.raises(eps.EpsError):
+        s.push(ticket, [np.zeros((3, 2), F32)])             # layout mismatch
+    good = np.array([[1, 2], [3, 4]], F32)
+    s.push(ticket, [good])                                    # same ticket, retried
+    o = Oracle(kat_tables())
+    assert o.push(f, [good]) == 0
+    w, m, v, u = s.read_state(1, [1, 2])
+    st, _ = o.state(1)
+    assert np.array_equal(bits(w), bits(st[[1, 2], 0])) and list(u) == [1, 1]
+
+
+def test_release_and_unknown_ticket(eps):
+    s = make_store(eps, kat_tables())
+    f = [Feature(1, 0, SUM, [1, 2], [0, 2])]
+    ticket, _ = s.lookup(inputs(eps, f))
+    assert s.stats()["live_tickets"] == 1
+    s.release(ticket)
+    assert s.stats()["live_tickets"] == 0
+    with pytest.raises(eps.EpsError):
+        s.push(ticket, [np.zeros((1, 2), F32)])
+
+
+def test_invalid_host_inputs_are_rejected(eps):
+    s = make_store(eps, kat_tables())
+    with pytest.raises(eps.EpsError):                        # key outside the table
+        s.lookup([eps.FeatureInput(1, 0, SUM, np.array([9], np.uint64), np.array([0, 1], np.uint64))])
+    with pytest.raises(eps.EpsError):                        # decreasing offsets
+        s.lookup([eps.FeatureInput(1, 0, SUM, np.array([1, 2], np.uint64),
+                                   np.array([0, 2, 1, 2], np.uint64))])
+    with pytest.raises(eps.EpsError):                        # offsets not ending at key count
+        s.lookup([eps.FeatureInput(1, 0, SUM, np.array([1, 2], np.uint64), np.array([0, 1], np.uint64))])
+    with pytest.raises(eps.EpsError):                        # unknown table
+        s.lookup([eps.FeatureInput(7, 0, SUM, np.array([1], np.uint64), np.array([0, 1], np.uint64))])
+    with pytest.raises(eps.EpsError):                        # duplicate feature id
+        f = eps.FeatureInput(1, 0, SUM, np.array([1], np.uint64), np.array([0, 1], np.uint64))
+        s.lookup([f, f])
+    assert s.stats()["live_tickets"] == 0
+
+
+def test_empty_and_ragged_features(eps):
+    t = [TableDef(id=1, dimension=64, learning_rate=0.01, rows=100)]
+    s, o = make_store(eps, t), Oracle(t)
+    feats = [Feature(1, 0, SUM, np.array([], np.uint64), [0]),            # no bags
+             Feature(1, 1, MEAN, np.array([], np.uint64), [0, 0, 0]),     # empty bags
+             Feature(1, 2, SEQUENCE, np.array([5], np.uint64), [0, 0, 1, 1]),
+             Feature(1, 3, SUM, np.array([5, 5, 7], np.uint64), [0, 0, 3])]
+    ticket, outs = s.lookup(inputs(eps, feats))
+    for a, b in zip(outs, o.lookup(feats)):
+        assert a.shape == b.shape and np.array_equal(bits(a), bits(b))
+    rng = np.random.default_rng(0)
+    grads = [rng.normal(0, 0.01, size=x.shape).astype(F32) for x in outs]
+    s.push(ticket, grads)
+    assert o.push(feats, grads) == 0
+    w, m, v, u = s.read_state(1, [5, 7])
+    st, upd = o.state(1)
+    assert np.array_equal(bits(w), bits(st[[5, 7], 0])) and np.array_equal(u, upd[[5, 7]])
+
+
+def test_device_inputs_async_push_matches_host_path(eps):
+    torch = pytest.importorskip("torch")
+    case = golden_cases.load("hot_segments")
+    host, dev = make_store(eps, case.tables), make_store(eps, case.tables)
+    for step in range(case.steps):
+        t1, o1 = host.lookup(inputs(eps, case.features))
+        dfeats = [eps.FeatureInput(f.table, f.feature, f.pooling,
+                                   torch.from_numpy(f.keys.astype(np.int64)).cuda(),
+                                   torch.from_numpy(f.offsets.astype(np.int64)).cuda())
+                  for f in case.features]
+        t2, o2 = dev.lookup(dfeats)
+        for a, b in zip(o1, o2):
+            assert np.array_equal(bits(a), bits(b.cpu().numpy()))
+        host.push(t1, case.grads[step])
+        dev.push(t2, [torch.from_numpy(g).cuda() for g in case.grads[step]], wait=False)
+    dev.synchronize()
+    keys = case.state[1][0]
+    for a, b in zip(host.read_state(1, keys), dev.read_state(1, keys)):
+        assert np.array_equal(a.view(np.uint32) if a.dtype == F32 else a,
+                              b.view(np.uint32) if b.dtype == F32 else b)
+
+
+def test_device_input_errors_are_deferred(eps):
+    torch = pytest.importorskip("torch")
+    s = make_store(eps, kat_tables())
+    before = s.read_state(1, [1])
+    f = [eps.FeatureInput(1, 0, SUM, torch.tensor([1, 99], device="cuda"),
+                          torch.tensor([0, 2], device="cuda"))]
+    ticket, _ = s.lookup(f)
+    with pytest.raises(eps.EpsError) as e:
+        s.push(ticket, [torch.zeros((1, 2), device="cuda")])
+    assert "wrong shard or outside" in e.value.message
+    after = s.read_state(1, [1])
+    assert np.array_equal(before[0], after[0]) and s.stats()["live_tickets"] == 0
+
+
+def test_two_live_tickets_any_order(eps):
+    case = golden_cases.load("small_bounded")
+    s = make_store(eps, case.tables)
+    o = Oracle(case.tables)
+    t1, _ = s.lookup(inputs(eps, case.features))
+    t2, _ = s.lookup(inputs(eps, case.features))
+    s.push(t2, case.grads[0])
+    s.push(t1, case.grads[1])
+    assert o.push(case.features, case.grads[0]) == 0
+    assert o.push(case.features, case.grads[1]) == 0
+    keys = case.state[1][0]
+    w, m, v, u = s.read_state(1, keys)
+    st, upd = o.state(1)
+    k = keys.astype(np.int64)
+    assert np.array_equal(bits(w), bits(st[k, 0])) and np.array_equal(u, upd[k])
