@@ -254,7 +254,8 @@ def run_b200(args):
     for t in w.tables:
         store.create_table(eps.TableDefinition(id=t.id, dimension=t.dimension, key_space=t.rows,
                                                learning_rate=1e-3))
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)          # flushes and events run on the store's stream
 
     # ---- device-resident inputs
     feats = [eps.FeatureInput(f.table, f.feature, f.pooling,

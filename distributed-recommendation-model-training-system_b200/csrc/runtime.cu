@@ -374,7 +374,9 @@ int eps_b200_create(const EpsB200Options* options, EpsB200Store** out, EpsB200St
       s->opt = *options;
       if (!s->opt.max_live_tickets) s->opt.max_live_tickets = 1024;
       s->Activate();
-      Cuda(cudaStreamCreateWithFlags(&s->own, cudaStreamNonBlocking));
+      // a blocking stream: work the caller queued on the legacy default stream
+      // (e.g. framework tensor copies) is ordered before the store's own work
+      Cuda(cudaStreamCreateWithFlags(&s->own, cudaStreamDefault));
       Cuda(cudaEventCreateWithFlags(&s->last_done, cudaEventDisableTiming));
       // one status slot per live ticket plus a scratch slot (index max_live_tickets)
       Cuda(cudaMallocHost(&s->host_status, sizeof(HostStatus) * (s->opt.max_live_tickets + 1)));

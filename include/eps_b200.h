@@ -15,7 +15,8 @@
  *    (include/eps/types.hpp:17-25) and copies the message into status->message;
  *  - plain pointers and sizes only; buffers flagged `device >= 0` / `*_on_device`
  *    are device pointers on the store's GPU, otherwise host pointers;
- *  - `stream` is a cudaStream_t (NULL = the store's own stream).  All work of one
+ *  - `stream` is a cudaStream_t (NULL = the store's own stream, a blocking stream
+ *    ordered with the legacy default stream).  All work of one
  *    store is serialised; calls on one store are thread-safe (one mutex, as the
  *    reference runtime's per-runtime mutex, adapters/entropy/runtime_c.cpp:177).
  *  - nothing here allocates on the caller's behalf except the returned store;
