@@ -71,6 +71,8 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 4])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="override the table rows of config 2 (smaller profiling captures)")
     return ap.parse_args()
 
 
@@ -79,11 +81,13 @@ def dist_env():
             int(os.environ.get("WORLD_SIZE", 1)))
 
 
-def workload_for(wl, config, rank):
+def workload_for(wl, config, rank, rows=0):
     if config == 1:
         return wl.config1(seed=1 + 1000 * rank)
     if config == 4:
         return wl.config4(seed=4 + 1000 * rank)
+    if rows:
+        return wl.config2(seed=2 + 1000 * rank, rows=rows)
     return wl.config2(seed=2 + 1000 * rank)
 
 
@@ -214,7 +218,7 @@ def run_reference(args):
     if rank != 0:
         return
     wl, _ = _import_package()
-    w = workload_for(wl, args.config, 0)
+    w = workload_for(wl, args.config, 0, args.rows)
     threads = host_threads()
     times = reference_rounds(w, args.steps, args.warmup, threads)
     if times is None:
@@ -247,7 +251,7 @@ def run_b200(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device(f"cuda:{local_rank}"))
     wl, eps = _import_package()
-    w = workload_for(wl, args.config, rank)
+    w = workload_for(wl, args.config, rank, args.rows)
     bm = byte_model(w)
     dev = torch.device(f"cuda:{local_rank}")
     store = eps.ParameterStore(device=local_rank, state_bytes=150 << 30)

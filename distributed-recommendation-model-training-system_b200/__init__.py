@@ -281,6 +281,8 @@ class ParameterStore:
         if outputs is None:
             outputs = []
             for f in feats:
+                if f.table not in self._tables:
+                    raise EpsError(INVALID_ARGUMENT, "unknown table")
                 shape = (f.output_rows, self._tables[f.table].dimension)
                 if host_outputs:
                     outputs.append(np.empty(shape, np.float32))
@@ -379,6 +381,8 @@ class ParameterStore:
 
     def read_state(self, table: int, keys):
         keys = _host_u64(keys)
+        if table not in self._tables:
+            raise EpsError(INVALID_ARGUMENT, "unknown table")
         d = self._tables[table].dimension
         w = np.empty((len(keys), d), np.float32)
         m = np.empty_like(w)

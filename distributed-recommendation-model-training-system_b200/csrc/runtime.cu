@@ -240,7 +240,10 @@ struct EpsB200Store {
     ring_head = b;
   }
 
-  void Activate() { Cuda(cudaSetDevice(opt.device)); }
+  void Activate() {
+    Cuda(cudaSetDevice(opt.device));
+    (void)cudaGetLastError();   // a launch check below must not see an older error
+  }
 
   cudaStream_t Use(void* s) {
     cudaStream_t stream = s ? static_cast<cudaStream_t>(s) : own;
@@ -724,7 +727,9 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       ++s.stats.lookups;
       if (read_only || sync_err) {
         if (slot >= 0) s.free_slots.push_back(slot);
-        cudaFreeAsync(slab, stream);
+        char* owned = slab;
+        slab = nullptr;                 // freed exactly once, here
+        Cuda(cudaFreeAsync(owned, stream));
         s.Done(stream);
         Require(!sync_err, EpsB200Store::LookupMessage(sync_err).c_str());
         return;
@@ -735,11 +740,12 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       const unsigned long long id = s.next_ticket++;
       s.tickets.emplace(id, std::move(t));
       s.stats.live_tickets = s.tickets.size();
+      slab = nullptr;                   // owned by the ticket now
       *ticket_out = id;
       s.Done(stream);
     } catch (...) {
       cudaStreamSynchronize(stream);
-      cudaFreeAsync(slab, stream);
+      if (slab) cudaFreeAsync(slab, stream);
       throw;
     }
   });
@@ -875,7 +881,7 @@ int eps_b200_push(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gra
                            cudaMemcpyDeviceToHost, stream));
       Cuda(cudaMemcpyAsync(&s.host_status[t.slot].lookup_error, t.lookup_error, sizeof(unsigned),
                            cudaMemcpyDeviceToHost, stream));
-      if (stage) { cudaFreeAsync(stage, stream); stage = nullptr; }
+      if (stage) { float* owned = stage; stage = nullptr; Cuda(cudaFreeAsync(owned, stream)); }
       t.push_in_flight = true;
       s.Done(stream);
     } catch (...) {
@@ -989,9 +995,15 @@ int eps_b200_read_state(EpsB200Store* store, uint32_t table, const uint64_t* key
                             reinterpret_cast<unsigned long long*>(buf + kb + pb), err, stream));
       Cuda(cudaMemcpyAsync(packed.data(), buf + kb, count * 12ull * D, cudaMemcpyDeviceToHost, stream));
       Cuda(cudaMemcpyAsync(upd.data(), buf + kb + pb, count * 8, cudaMemcpyDeviceToHost, stream));
-      cudaFreeAsync(buf, stream);
+      char* owned = buf;
+      buf = nullptr;
+      Cuda(cudaFreeAsync(owned, stream));
       s.Sync(stream);
-    } catch (...) { cudaStreamSynchronize(stream); throw; }
+    } catch (...) {
+      cudaStreamSynchronize(stream);
+      if (buf) cudaFreeAsync(buf, stream);
+      throw;
+    }
     s.Done(stream);
     for (uint64_t r = 0; r < count; ++r) {
       const float* row = packed.data() + r * 3ull * D;
@@ -1039,9 +1051,15 @@ int eps_b200_load_state(EpsB200Store* store, uint32_t table, const uint64_t* key
                              reinterpret_cast<unsigned long long*>(buf), count,
                              reinterpret_cast<float*>(buf + kb),
                              reinterpret_cast<unsigned long long*>(buf + kb + pb), t.dtable, stream));
-      cudaFreeAsync(buf, stream);
+      char* owned = buf;
+      buf = nullptr;
+      Cuda(cudaFreeAsync(owned, stream));
       s.Sync(stream);
-    } catch (...) { cudaStreamSynchronize(stream); throw; }
+    } catch (...) {
+      cudaStreamSynchronize(stream);
+      if (buf) cudaFreeAsync(buf, stream);
+      throw;
+    }
     s.Done(stream);
   });
 }
