@@ -97,7 +97,8 @@ PHASES = ("lookup", "sort", "prescan", "apply", "finalize")
 _lib = None
 
 ENTRY_POINTS = ("eps_b200_abi_version", "eps_b200_create", "eps_b200_destroy",
-                "eps_b200_create_table", "eps_b200_lookup", "eps_b200_push", "eps_b200_release",
+                "eps_b200_create_table", "eps_b200_lookup", "eps_b200_lookup_noalloc",
+                "eps_b200_push", "eps_b200_release",
                 "eps_b200_synchronize", "eps_b200_read_state", "eps_b200_load_state",
                 "eps_b200_optimizer_state", "eps_b200_profile", "eps_b200_stats")
 
@@ -120,6 +121,7 @@ def load_library() -> C.CDLL:
     lib.eps_b200_create_table.argtypes = [vp, P(Table), P(Status)]
     lib.eps_b200_lookup.argtypes = [vp, P(Feature), C.c_uint64, C.c_int32, C.c_int32, C.c_int32,
                                     P(Buffer), vp, P(C.c_uint64), P(Status)]
+    lib.eps_b200_lookup_noalloc.argtypes = [vp, P(Feature), C.c_uint64, P(Buffer), vp, P(Status)]
     lib.eps_b200_push.argtypes = [vp, C.c_uint64, P(Buffer), C.c_uint64, vp, C.c_int32, P(Status)]
     lib.eps_b200_release.argtypes = [vp, C.c_uint64, P(Status)]
     lib.eps_b200_synchronize.argtypes = [vp, P(Status)]
@@ -303,6 +305,25 @@ class ParameterStore:
         _check(rc, st)
         del keep
         return (None if read_only else ticket.value), outputs
+
+    def lookup_noalloc(self, feats: Sequence[FeatureInput], outputs, stream=None):
+        """Read-only pooled lookup through eps_b200_lookup_noalloc: writes the
+        given device output tensors and allocates no device memory (for callers
+        whose serving path may not allocate; at most 256 features per call).
+        Input errors surface at the next synchronize()."""
+        arr, on_device, keep = self._features(feats)
+        if not on_device:
+            raise EpsError(INVALID_ARGUMENT, "the allocation-free lookup needs device inputs")
+        bufs = (Buffer * len(feats))()
+        for i, (f, o) in enumerate(zip(feats, outputs)):
+            bufs[i] = Buffer(f.feature, 0, int(o.shape[0]), int(o.shape[1]), _ptr(o),
+                             self.device if _is_device(o) else -1, 0)
+        st = Status()
+        rc = self.lib.eps_b200_lookup_noalloc(self._h, arr, len(feats), bufs,
+                                              _stream_ptr(stream), C.byref(st))
+        _check(rc, st)
+        del keep
+        return outputs
 
     def prepare_lookup(self, feats: Sequence[FeatureInput], outputs, read_only=False,
                        shard_partial=False):

@@ -151,4 +151,12 @@ cudaError_t launch_write_rows(float* state, unsigned long long* updates, unsigne
                               const float* packed, const unsigned long long* upd_in,
                               DeviceTable* dtable, cudaStream_t stream);
 
+// Allocation-free lookup (eps_b200_lookup_noalloc): feature descriptors live in
+// a fixed file-scope device array in noalloc.cu instead of an allocated block.
+constexpr unsigned int kNoAllocFeatures = 256;
+constexpr int kNoAllocMaxDevices = 64;
+// Device address of this GPU's descriptor array; the first call on a GPU looks it
+// up (with that GPU current) and caches it.
+cudaError_t noalloc_feature_table(int device, LookupFeature** out);
+
 }  // namespace eps_b200

@@ -751,6 +751,97 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
   });
 }
 
+// Read-only pooled lookup that allocates nothing: see eps_b200.h.  Same kernel
+// and same results as eps_b200_lookup(read_only=1, shard_partial=0) with device
+// inputs and outputs; only the feature descriptors live elsewhere (noalloc.cu).
+int eps_b200_lookup_noalloc(EpsB200Store* store, const EpsB200Feature* features, uint64_t count,
+                            EpsB200Buffer* outputs, void* stream_arg, EpsB200Status* status) {
+  return Boundary(status, [&] {
+    auto& s = *Checked(store);
+    Require(features && outputs, "null features or outputs");
+    Require(count >= 1 && count <= kNoAllocFeatures,
+            "the allocation-free lookup takes 1 to 256 features per call",
+            EPS_B200_CAPACITY_EXCEEDED);
+    std::lock_guard lock(s.mutex);
+    s.Activate();
+    Require(s.opt.shard_count == 1, "a client-level lookup needs a single-shard store");
+    LookupFeature desc[kNoAllocFeatures];
+    unsigned long long bag_base = 0;
+    unsigned dmax = 1;
+    bool all4 = true, all2 = true, out16 = true, out8 = true;
+    for (uint64_t i = 0; i < count; ++i) {
+      const auto& f = features[i];
+      for (uint64_t j = 0; j < i; ++j) Require(features[j].feature != f.feature, "duplicate feature ID");
+      const Table& t = s.Get(f.table);
+      Require(f.pooling <= 2, "unsupported pooling mode");
+      Require(f.offset_count >= 1 && f.offsets, "invalid bag offsets");
+      Require(!f.key_count || f.keys, "null feature keys");
+      const unsigned long long rows = f.pooling == 2 ? f.key_count : f.offset_count - 1;
+      const unsigned D = t.def.dimension;
+      const auto& o = outputs[i];
+      Require(o.feature == f.feature && o.rows == rows && o.columns == D,
+              "output buffer layout mismatch");
+      Require(o.device == s.opt.device, "the allocation-free lookup writes device outputs only");
+      Require(!rows || o.data, "null output buffer");
+      dmax = std::max(dmax, D);
+      all4 &= D % 4 == 0;
+      all2 &= D % 2 == 0;
+      out16 &= (reinterpret_cast<uintptr_t>(o.data) & 15) == 0;
+      out8 &= (reinterpret_cast<uintptr_t>(o.data) & 7) == 0;
+      LookupFeature& L = desc[i];
+      L.keys = reinterpret_cast<const unsigned long long*>(f.keys);
+      L.offsets = reinterpret_cast<const unsigned long long*>(f.offsets);
+      L.lengths = reinterpret_cast<const unsigned long long*>(f.valid_lengths);
+      L.out = static_cast<float*>(o.data);
+      L.state = t.state;
+      L.rows = t.rows;
+      L.key_count = f.key_count;
+      L.bag_count = f.offset_count - 1;
+      L.bag_base = bag_base;
+      L.occ_base = 0;
+      L.scale_base = 0;
+      L.dim = D;
+      L.pooling = f.pooling;
+      L.table_rank = 0;
+      L.feature_index = (unsigned)i;
+      bag_base += L.bag_count;
+    }
+    // vector width as in the regular lookup (no heap use here)
+    int vec = 1;
+    if (all4 && out16 && dmax >= 128) vec = 4;
+    else if (all2 && out8 && dmax >= 64) vec = 2;
+    if (32u * vec * 4u < dmax) {
+      if (all4 && out16) vec = 4;
+      else if (all2 && out8) vec = 2;
+    }
+    const unsigned need = (dmax + 32u * vec - 1) / (32u * vec);
+    Require(need <= 4, "embedding dimension/alignment not supported by this build",
+            EPS_B200_CAPACITY_EXCEEDED);
+    LookupFeature* table = nullptr;
+    Cuda(noalloc_feature_table(s.opt.device, &table));
+    cudaStream_t stream = s.Use(stream_arg);
+    // desc is pageable: the copy has consumed it when cudaMemcpyAsync returns
+    Cuda(cudaMemcpyAsync(table, desc, count * sizeof(LookupFeature), cudaMemcpyHostToDevice, stream));
+    LookupLaunch lp{};
+    lp.features = table;
+    lp.feature_count = (unsigned)count;
+    lp.bag_total = bag_base;
+    lp.shard_count = 1;
+    lp.shard_id = 0;
+    lp.client = 1;
+    lp.emit = 0;
+    lp.slot_bits = 1;
+    lp.key64 = 0;
+    lp.error = s.sticky_error;      // reported by eps_b200_synchronize
+    lp.vec = vec;
+    lp.iters = need <= 1 ? 1 : (need <= 2 ? 2 : 4);
+    Cuda(launch_lookup(lp, stream));
+    ++s.stats.lookups;
+    if (bag_base) ++s.stats.kernel_launches;
+    s.Done(stream);
+  });
+}
+
 int eps_b200_push(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gradients,
                   uint64_t count, void* stream_arg, int32_t wait, EpsB200Status* status) {
   return Boundary(status, [&] {

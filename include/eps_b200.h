@@ -163,6 +163,26 @@ EPS_B200_EXPORT int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* f
                     EpsB200Buffer* outputs, void* stream, uint64_t* ticket,
                     EpsB200Status* status);
 
+/* Read-only pooled lookup that allocates no device memory.  It has no
+ * counterpart in the reference.  It gives the same outputs as eps_b200_lookup
+ * with read_only = 1 and shard_partial = 0 for device inputs and device
+ * outputs, for callers that must not allocate while serving a request (an
+ * inference engine or framework that owns all GPU memory through its own pool,
+ * or a latency-critical loop that must never wait on an allocator).
+ * Limits and sharing:
+ *  - 1 to 256 features per call (larger counts fail with CAPACITY_EXCEEDED);
+ *    inputs and outputs must be device buffers on the store's GPU;
+ *  - the feature descriptors go to one fixed ~26 KiB array per GPU, created when
+ *    the library is loaded on that GPU and kept until the process exits; every
+ *    call on that GPU reuses it, so calls that overlap on the GPU (two streams, or
+ *    two stores on one GPU) race; calls of one store on one stream are ordered;
+ *  - the first call on a GPU looks up that array's device address, so make the
+ *    first call before any CUDA stream capture starts;
+ *  - invalid keys or offsets are reported by the next eps_b200_synchronize. */
+EPS_B200_EXPORT int eps_b200_lookup_noalloc(EpsB200Store* store, const EpsB200Feature* features,
+                                            uint64_t count, EpsB200Buffer* outputs, void* stream,
+                                            EpsB200Status* status);
+
 /* Push gradients of a ticket's feature tensors: DistributedClient::Push /
  * ParameterService::Push (include/eps/parameter_service.hpp:18), i.e.
  * ReduceGradients (src/access/batch_access.cpp:82-125) + ValidateLazyAdam /
