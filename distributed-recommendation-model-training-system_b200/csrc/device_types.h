@@ -102,7 +102,7 @@ struct LongRecord {
   unsigned int first_slot;      // 0: piece stored in part0[first_tile], 1: in part1
 };
 
-constexpr int kTile = 64;       // sorted occurrences per warp tile
+constexpr int kTile = 32;       // sorted occurrences per group tile
 constexpr int kLongRun = 64;    // segments longer than this are "long"
 constexpr unsigned int kMaxFeatures = 1024;
 constexpr unsigned int kRowBits = 22;   // gradient row bits in the source code

@@ -67,6 +67,26 @@ __device__ __forceinline__ float clamp_weight(float v, int has, float lo, float 
 
 __device__ __forceinline__ unsigned abs_bits(float x) { return __float_as_uint(fabsf(x)); }
 
+// Launch shape of the row kernels: a group of `group` lanes owns one row, each
+// lane `vec` consecutive floats, `iters` times.  128-bit accesses (vec = 4) need
+// every dimension divisible by 4 and 16-byte aligned buffers; then
+// group = D/4 up to 32 lanes.  Otherwise one float per lane with 32 lanes.
+struct Shape { int vec, group, iters; };
+inline bool choose_shape(unsigned dmax, bool all4, bool align16, Shape* out) {
+  if (all4 && align16) {
+    if (dmax <= 32) { *out = {4, 8, 1}; return true; }
+    if (dmax <= 64) { *out = {4, 16, 1}; return true; }
+    if (dmax <= 128) { *out = {4, 32, 1}; return true; }
+    if (dmax <= 256) { *out = {4, 32, 2}; return true; }
+    if (dmax <= 512) { *out = {4, 32, 4}; return true; }
+    return false;
+  }
+  if (dmax <= 32) { *out = {1, 32, 1}; return true; }
+  if (dmax <= 64) { *out = {1, 32, 2}; return true; }
+  if (dmax <= 128) { *out = {1, 32, 4}; return true; }
+  return false;
+}
+
 // ---------------------------------------------------------------- launchers
 struct LookupLaunch {
   const LookupFeature* features;   // device array
@@ -81,7 +101,7 @@ struct LookupLaunch {
   unsigned int* occ_src;           // [occurrences]
   float* row_scale;                // [gradient rows]
   unsigned int* error;             // LookupErrorBits
-  int vec, iters;
+  int vec, group, iters;           // launch shape (see choose_shape)
 };
 cudaError_t launch_lookup(const LookupLaunch& p, cudaStream_t stream);
 
@@ -119,7 +139,7 @@ struct PushLaunch {
   PushControl* control;
   const unsigned int* lookup_error;
   unsigned long long long_run;     // segments longer than this are reduced in pieces
-  int vec, iters;
+  int vec, group, iters;           // launch shape (see choose_shape)
 };
 // Push = prescan (+ device-side mode decision), apply (2 passes x {segments,
 // long segments}), finalize (beta powers / sequence iff accepted).

@@ -26,15 +26,21 @@
 //   6. finalize  -- advances beta powers and the sequence iff accepted.
 //
 // Coalescing layout: the occurrences are sorted stably by composite key
-// (table rank, slot).  Warp w owns the tile [64w, 64w+64) of sorted occurrences
-// and fully processes every segment that STARTS in its tile and has at most 64
-// occurrences: the gradient sum runs serially in occurrence order (bit-exact
-// with the reference) and the Adam update of that row follows in the same pass
-// from state prefetched at the segment start.  Longer (Zipf-head) segments are
-// reduced per tile into part0/part1 and combined in tile order by a CTA of 16
-// warps in the long-segment kernel (deterministic; within 1e-6 relative of the
-// reference's serial order).
+// (table rank, slot).  A group of G lanes (G = D/4: one 128-bit access per lane
+// covers a row) owns the tile [32t, 32t+32) of sorted occurrences and fully
+// processes every segment that STARTS in its tile and has at most 64
+// occurrences: the row's state load is issued first, the gradient sum runs
+// serially in occurrence order (bit-exact with the reference) with up to 8
+// gradient rows in flight, and the Adam update of that row follows in the same
+// pass.  Longer (Zipf-head) segments are reduced per tile into part0/part1 and
+// combined in tile order by all groups of one CTA in the long-segment kernel
+// (deterministic; within 1e-6 * sum|terms| of the reference's serial sum).
+#include <cooperative_groups.h>
+#include <cooperative_groups/reduce.h>
+
 #include "kernels.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace eps_b200 {
 namespace {
@@ -130,17 +136,22 @@ __global__ void __launch_bounds__(256) push_prescan(PushLaunch p, PushTable* tab
 }
 
 // ------------------------------------------------------ reduction helpers
-// Sum of gradient references [s0, s1) (all with the same key), serially in order.
-template <int VEC, int ITERS>
-__device__ __forceinline__ void reduce_range(const PushLaunch& p, unsigned long long s0,
-                                             unsigned long long s1, unsigned D,
-                                             float (&acc)[VEC * ITERS]) {
+template <int G>
+__device__ __forceinline__ unsigned full_mask() { return G == 32 ? 0xffffffffu : ((1u << G) - 1u); }
+
+// Sum of gradient references [s0, s1) (all with the same key), serially in order,
+// by the G lanes of `grp` (each lane owns VEC*ITERS columns).
+template <int G, int VEC, int ITERS, typename Grp>
+__device__ __forceinline__ void reduce_range(const Grp& grp, const PushLaunch& p,
+                                             unsigned long long s0, unsigned long long s1,
+                                             unsigned D, float (&acc)[VEC * ITERS]) {
   constexpr int C = VEC * ITERS;
-  const unsigned lane = lane_id();
+  constexpr int DEPTH = C <= 4 ? 4 : 2;
+  const unsigned gl = grp.thread_rank();
 #pragma unroll
   for (int k = 0; k < C; ++k) acc[k] = 0.0f;
-  for (unsigned long long c0 = s0; c0 < s1; c0 += 32) {
-    const unsigned long long i = c0 + lane;
+  for (unsigned long long c0 = s0; c0 < s1; c0 += G) {
+    const unsigned long long i = c0 + gl;
     unsigned long long gp = 0;
     float sc = 0.0f;
     if (i < s1) {
@@ -152,18 +163,18 @@ __device__ __forceinline__ void reduce_range(const PushLaunch& p, unsigned long 
       gp = reinterpret_cast<unsigned long long>(g + (unsigned long long)r * D);
       sc = __ldg(p.row_scale + __ldg(&F->scale_base) + r);
     }
-    const int cnt = (int)min(32ull, s1 - c0);
-    for (int j0 = 0; j0 < cnt; j0 += 4) {
-      float x[4][C];
-      float s[4];
+    const int cnt = (int)min((unsigned long long)G, s1 - c0);
+    for (int j0 = 0; j0 < cnt; j0 += DEPTH) {
+      float x[DEPTH][C];
+      float s[DEPTH];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const unsigned long long q = __shfl_sync(0xffffffffu, gp, (j0 + u) & 31);
-        s[u] = __shfl_sync(0xffffffffu, sc, (j0 + u) & 31);
+      for (int u = 0; u < DEPTH; ++u) {
+        const unsigned long long q = grp.shfl(gp, (j0 + u) & (G - 1));
+        s[u] = grp.shfl(sc, (j0 + u) & (G - 1));
         const bool use = j0 + u < cnt;
 #pragma unroll
         for (int it = 0; it < ITERS; ++it) {
-          const unsigned col = (it * 32 + lane) * VEC;
+          const unsigned col = (it * G + gl) * VEC;
           float t[VEC];
           if (use && col < D) load_vec<VEC>(reinterpret_cast<const float*>(q) + col, t);
           else {
@@ -175,7 +186,7 @@ __device__ __forceinline__ void reduce_range(const PushLaunch& p, unsigned long 
         }
       }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < DEPTH; ++u) {
         if (j0 + u >= cnt) break;
         // batch_access.cpp:118: dest += src * scale
 #pragma unroll
@@ -185,13 +196,13 @@ __device__ __forceinline__ void reduce_range(const PushLaunch& p, unsigned long 
   }
 }
 
-template <int VEC, int ITERS>
-__device__ __forceinline__ void load_state(const float* row, unsigned D, float (&w)[VEC * ITERS],
-                                           float (&m)[VEC * ITERS], float (&v)[VEC * ITERS]) {
-  const unsigned lane = lane_id();
+template <int G, int VEC, int ITERS>
+__device__ __forceinline__ void load_state(unsigned gl, const float* row, unsigned D,
+                                           float (&w)[VEC * ITERS], float (&m)[VEC * ITERS],
+                                           float (&v)[VEC * ITERS]) {
 #pragma unroll
   for (int it = 0; it < ITERS; ++it) {
-    const unsigned col = (it * 32 + lane) * VEC;
+    const unsigned col = (it * G + gl) * VEC;
     float a[VEC], b[VEC], c[VEC];
     if (col < D) {
       load_vec<VEC>(row + col, a);
@@ -207,18 +218,17 @@ __device__ __forceinline__ void load_state(const float* row, unsigned D, float (
 }
 
 // LazyAdam on one row (src/update/lazy_adam.cpp:28-37).  Returns reject bits
-// (validate) and updates *absmax (apply).
-template <int VEC, int ITERS>
-__device__ __forceinline__ unsigned adam_row(const PushTable& T, float* row, unsigned D,
+// (validate) and raises *absmax (apply).
+template <int G, int VEC, int ITERS>
+__device__ __forceinline__ unsigned adam_row(unsigned gl, const PushTable& T, float* row, unsigned D,
                                              const float (&g)[VEC * ITERS], float (&w)[VEC * ITERS],
                                              float (&m)[VEC * ITERS], float (&v)[VEC * ITERS],
                                              bool apply, bool validate, unsigned* absmax) {
-  const unsigned lane = lane_id();
   unsigned bits = 0;
   unsigned mx = 0;
 #pragma unroll
   for (int it = 0; it < ITERS; ++it) {
-    const unsigned col = (it * 32 + lane) * VEC;
+    const unsigned col = (it * G + gl) * VEC;
     if (col >= D) continue;
     float nw[VEC], nm[VEC], nv[VEC];
 #pragma unroll
@@ -249,45 +259,46 @@ __device__ __forceinline__ unsigned adam_row(const PushTable& T, float* row, uns
 }
 
 // Run length of key K starting at q (keys sorted), capped at cap+1.
-template <typename KeyT>
-__device__ __forceinline__ unsigned long long run_forward(const void* keys, unsigned long long n,
-                                                          unsigned long long q, KeyT K,
-                                                          unsigned long long cap) {
-  const unsigned lane = lane_id();
+template <int G, typename KeyT, typename Grp>
+__device__ __forceinline__ unsigned long long run_forward(const Grp& grp, const void* keys,
+                                                          unsigned long long n, unsigned long long q,
+                                                          KeyT K, unsigned long long cap) {
+  const unsigned gl = grp.thread_rank();
   unsigned long long len = 0;
   while (len <= cap) {
-    const unsigned long long i = q + len + lane;
+    const unsigned long long i = q + len + gl;
     const bool same = i < n && key_at<KeyT>(keys, i) == K;
-    const unsigned ball = __ballot_sync(0xffffffffu, same);
-    if (ball != 0xffffffffu) return len + (unsigned long long)(__ffs(~ball) - 1);
-    len += 32;
+    const unsigned ball = grp.ballot(same);
+    if (ball != full_mask<G>()) return len + (unsigned long long)(__ffs(~ball) - 1);
+    len += G;
   }
   return len;
 }
 
 // Number of keys equal to K immediately before position b, capped at cap+1.
-template <typename KeyT>
-__device__ __forceinline__ unsigned long long run_backward(const void* keys, unsigned long long b,
-                                                           KeyT K, unsigned long long cap) {
-  const unsigned lane = lane_id();
+template <int G, typename KeyT, typename Grp>
+__device__ __forceinline__ unsigned long long run_backward(const Grp& grp, const void* keys,
+                                                           unsigned long long b, KeyT K,
+                                                           unsigned long long cap) {
+  const unsigned gl = grp.thread_rank();
   unsigned long long len = 0;
   while (len <= cap) {
-    const bool in = b >= len + lane + 1;
-    const bool same = in && key_at<KeyT>(keys, b - len - lane - 1) == K;
-    const unsigned ball = __ballot_sync(0xffffffffu, same);
-    if (ball != 0xffffffffu) return len + (unsigned long long)(__ffs(~ball) - 1);
-    len += 32;
+    const bool in = b >= len + gl + 1;
+    const bool same = in && key_at<KeyT>(keys, b - len - gl - 1) == K;
+    const unsigned ball = grp.ballot(same);
+    if (ball != full_mask<G>()) return len + (unsigned long long)(__ffs(~ball) - 1);
+    len += G;
   }
   return len;
 }
 
-template <int VEC, int ITERS>
-__device__ __forceinline__ void store_piece(float* part, unsigned dim_max, unsigned long long tile,
-                                            unsigned D, const float (&acc)[VEC * ITERS]) {
-  const unsigned lane = lane_id();
+template <int G, int VEC, int ITERS>
+__device__ __forceinline__ void store_piece(unsigned gl, float* part, unsigned dim_max,
+                                            unsigned long long tile, unsigned D,
+                                            const float (&acc)[VEC * ITERS]) {
 #pragma unroll
   for (int it = 0; it < ITERS; ++it) {
-    const unsigned col = (it * 32 + lane) * VEC;
+    const unsigned col = (it * G + gl) * VEC;
     if (col >= D) continue;
     float t[VEC];
 #pragma unroll
@@ -296,54 +307,59 @@ __device__ __forceinline__ void store_piece(float* part, unsigned dim_max, unsig
   }
 }
 
-// Flush a warp's state-bound maximum for table tr (called by all 32 lanes).
-__device__ __forceinline__ void flush_absmax(const PushLaunch& p, int tr, unsigned mx) {
-  mx = __reduce_max_sync(0xffffffffu, mx);
-  if (lane_id() == 0 && tr >= 0 && mx) atomicMax(&p.tables[tr].dtable->state_absmax_bits, mx);
+// Flush a group's state-bound maximum for table tr (called by all G lanes).
+template <typename Grp>
+__device__ __forceinline__ void flush_absmax(const Grp& grp, const PushLaunch& p, int tr, unsigned mx) {
+  mx = cg::reduce(grp, mx, cg::greater<unsigned>());
+  if (grp.thread_rank() == 0 && tr >= 0 && mx) atomicMax(&p.tables[tr].dtable->state_absmax_bits, mx);
 }
 
 // ----------------------------------------------------------------- segments
-template <int VEC, int ITERS, typename KeyT>
-__global__ void __launch_bounds__(256) push_segments(PushLaunch p, int pass) {
+template <int G, int VEC, int ITERS, typename KeyT>
+__global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? 3 : 2) push_segments(PushLaunch p, int pass) {
   const Role R = role(p.control, pass);
   if (!R.run) return;
   constexpr int C = VEC * ITERS;
-  const unsigned lane = lane_id();
+  const auto grp = cg::tiled_partition<G>(cg::this_thread_block());
+  const unsigned gl = grp.thread_rank();
   const unsigned long long n = p.n;
   const unsigned long long tiles = (n + kTile - 1) / kTile;
-  const unsigned long long warp = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) >> 5;
-  const unsigned long long nwarps = (gridDim.x * (unsigned long long)blockDim.x) >> 5;
+  const unsigned long long gid = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) / G;
+  const unsigned long long ngroups = (gridDim.x * (unsigned long long)blockDim.x) / G;
   const KeyT slot_mask = (p.slot_bits >= sizeof(KeyT) * 8) ? ~KeyT(0)
                                                            : ((KeyT(1) << p.slot_bits) - 1);
   unsigned bits = 0;
   int cur_tr = -1;
   unsigned cur_max = 0;
 
-  for (unsigned long long t = warp; t < tiles; t += nwarps) {
+  for (unsigned long long t = gid; t < tiles; t += ngroups) {
     const unsigned long long b = t * kTile;
     const unsigned long long e = min(n, b + kTile);
     unsigned long long q = b;
     const KeyT kb = key_at<KeyT>(p.keys, b);
     if (b > 0 && key_at<KeyT>(p.keys, b - 1) == kb) {
       // the segment holding b started in an earlier tile
-      const unsigned long long back = run_backward<KeyT>(p.keys, b, kb, p.long_run);
-      const unsigned long long fwd = run_forward<KeyT>(p.keys, n, b, kb, p.long_run);
+      const unsigned long long back = run_backward<G, KeyT>(grp, p.keys, b, kb, p.long_run);
+      const unsigned long long fwd = run_forward<G, KeyT>(grp, p.keys, n, b, kb, p.long_run);
       const unsigned long long stop = min(b + fwd, e);
       if (back + fwd > p.long_run) {
         if (R.partials) {
           const unsigned tr = (unsigned)(kb >> p.slot_bits);
-          const unsigned D = p.tables[tr].dim;
-          float acc[C];
-          reduce_range<VEC, ITERS>(p, b, stop, D, acc);
-          store_piece<VEC, ITERS>(p.part0, p.dim_max, t, D, acc);
+          if (tr < p.table_count) {
+            const unsigned D = p.tables[tr].dim;
+            float acc[C];
+            reduce_range<G, VEC, ITERS>(grp, p, b, stop, D, acc);
+            store_piece<G, VEC, ITERS>(gl, p.part0, p.dim_max, t, D, acc);
+          }
         }
+        q = stop;
+      } else {
+        q = b + fwd;   // a short segment, processed by the tile where it starts
       }
-      q = stop;
-      if (back + fwd <= p.long_run) q = b + fwd;
     }
     while (q < e) {
       const KeyT K = key_at<KeyT>(p.keys, q);
-      const unsigned long long len = run_forward<KeyT>(p.keys, n, q, K, p.long_run);
+      const unsigned long long len = run_forward<G, KeyT>(grp, p.keys, n, q, K, p.long_run);
       const unsigned tr = (unsigned)(K >> p.slot_bits);
       const unsigned long long slot = (unsigned long long)(K & slot_mask);
       if (tr >= p.table_count) { q += len; continue; }
@@ -353,24 +369,24 @@ __global__ void __launch_bounds__(256) push_segments(PushLaunch p, int pass) {
         if (R.apply || R.validate) {
           float* row = T.state + slot * 3ull * D;
           float w[C], m[C], v[C], g[C];
-          load_state<VEC, ITERS>(row, D, w, m, v);   // issued before the reduction
-          reduce_range<VEC, ITERS>(p, q, q + len, D, g);
+          load_state<G, VEC, ITERS>(gl, row, D, w, m, v);   // issued before the reduction
+          reduce_range<G, VEC, ITERS>(grp, p, q, q + len, D, g);
           if ((int)tr != cur_tr) {
-            if (R.apply) flush_absmax(p, cur_tr, cur_max);
+            if (R.apply) flush_absmax(grp, p, cur_tr, cur_max);
             cur_tr = (int)tr; cur_max = 0;
           }
-          bits |= adam_row<VEC, ITERS>(T, row, D, g, w, m, v, R.apply, R.validate, &cur_max);
-          if (R.apply && lane == 0) T.updates[slot] += 1ull;
+          bits |= adam_row<G, VEC, ITERS>(gl, T, row, D, g, w, m, v, R.apply, R.validate, &cur_max);
+          if (R.apply && gl == 0) T.updates[slot] += 1ull;
         }
         q += len;
       } else {
         // long segment starting at q: it runs past e (len > long_run >= kTile >= e - q)
         if (R.partials) {
           float acc[C];
-          reduce_range<VEC, ITERS>(p, q, e, D, acc);
+          reduce_range<G, VEC, ITERS>(grp, p, q, e, D, acc);
           const unsigned which = q == b ? 0u : 1u;
-          store_piece<VEC, ITERS>(which ? p.part1 : p.part0, p.dim_max, t, D, acc);
-          if (lane == 0) {
+          store_piece<G, VEC, ITERS>(gl, which ? p.part1 : p.part0, p.dim_max, t, D, acc);
+          if (gl == 0) {
             const unsigned at = atomicAdd(&p.control->long_count, 1u);
             p.records[at] = LongRecord{(unsigned long long)K, (unsigned)t, which};
           }
@@ -379,22 +395,24 @@ __global__ void __launch_bounds__(256) push_segments(PushLaunch p, int pass) {
       }
     }
   }
-  bits = __reduce_or_sync(0xffffffffu, bits);
-  if (lane == 0 && bits) atomicOr(&p.control->reject_bits, bits);
-  if (R.apply) flush_absmax(p, cur_tr, cur_max);
+  bits = cg::reduce(grp, bits, cg::bit_or<unsigned>());
+  if (gl == 0 && bits) atomicOr(&p.control->reject_bits, bits);
+  if (R.apply) flush_absmax(grp, p, cur_tr, cur_max);
 }
 
 // ------------------------------------------------------------ long segments
-constexpr int kLongWarps = 16;
+constexpr int kLongThreads = 512;
 
-template <int VEC, int ITERS, typename KeyT>
-__global__ void __launch_bounds__(kLongWarps * 32) push_long(PushLaunch p, int pass) {
+template <int G, int VEC, int ITERS, typename KeyT>
+__global__ void __launch_bounds__(kLongThreads) push_long(PushLaunch p, int pass) {
   const Role R = role(p.control, pass);
   if (!R.run) return;
   if (!R.apply && !R.validate) return;
-  extern __shared__ float s_acc[];   // [kLongWarps][dim_max]
+  extern __shared__ float s_acc[];   // [groups][dim_max]
   constexpr int C = VEC * ITERS;
-  const unsigned lane = lane_id(), w = threadIdx.x >> 5;
+  constexpr int NG = kLongThreads / G;
+  const auto grp = cg::tiled_partition<G>(cg::this_thread_block());
+  const unsigned gl = grp.thread_rank(), w = threadIdx.x / G;
   const unsigned count = *(volatile const unsigned*)&p.control->long_count;
   const unsigned long long n = p.n;
   const unsigned long long tiles = (n + kTile - 1) / kTile;
@@ -412,14 +430,14 @@ __global__ void __launch_bounds__(kLongWarps * 32) push_long(PushLaunch p, int p
     const PushTable& T = p.tables[tr];
     const unsigned D = T.dim;
     // last tile whose first key is K (keys are sorted, so binary search)
-    unsigned long long lo = L.first_tile, hi = tiles;   // invariant: answer in [lo, hi)
+    unsigned long long lo = L.first_tile, hi = tiles;   // answer in [lo, hi)
     while (hi - lo > 1) {
       const unsigned long long mid = (lo + hi) >> 1;
       if (key_at<KeyT>(p.keys, mid * kTile) == K) lo = mid; else hi = mid;
     }
     const unsigned long long pieces = lo - L.first_tile + 1;
-    // contiguous chunk of pieces for this warp
-    const unsigned long long per = (pieces + kLongWarps - 1) / kLongWarps;
+    // a contiguous chunk of pieces per group, combined afterwards in group order
+    const unsigned long long per = (pieces + NG - 1) / NG;
     const unsigned long long p0 = min(pieces, per * w), p1 = min(pieces, p0 + per);
     float acc[C];
 #pragma unroll
@@ -434,7 +452,7 @@ __global__ void __launch_bounds__(kLongWarps * 32) push_long(PushLaunch p, int p
         const unsigned long long tile = L.first_tile + j;
 #pragma unroll
         for (int it = 0; it < ITERS; ++it) {
-          const unsigned col = (it * 32 + lane) * VEC;
+          const unsigned col = (it * G + gl) * VEC;
           float t[VEC];
           if (use && col < D) load_vec<VEC>(src + tile * p.dim_max + col, t);
           else {
@@ -454,7 +472,7 @@ __global__ void __launch_bounds__(kLongWarps * 32) push_long(PushLaunch p, int p
     }
 #pragma unroll
     for (int it = 0; it < ITERS; ++it) {
-      const unsigned col = (it * 32 + lane) * VEC;
+      const unsigned col = (it * G + gl) * VEC;
       if (col >= D) continue;
 #pragma unroll
       for (int x = 0; x < VEC; ++x) s_acc[w * p.dim_max + col + x] = acc[it * VEC + x];
@@ -463,13 +481,13 @@ __global__ void __launch_bounds__(kLongWarps * 32) push_long(PushLaunch p, int p
     if (w == 0) {
       float g[C], wv[C], mv[C], vv[C];
       float* row = T.state + slot * 3ull * D;
-      load_state<VEC, ITERS>(row, D, wv, mv, vv);
+      load_state<G, VEC, ITERS>(gl, row, D, wv, mv, vv);
 #pragma unroll
       for (int k = 0; k < C; ++k) g[k] = 0.0f;
-      for (int x = 0; x < kLongWarps; ++x) {
+      for (int x = 0; x < NG; ++x) {
 #pragma unroll
         for (int it = 0; it < ITERS; ++it) {
-          const unsigned col = (it * 32 + lane) * VEC;
+          const unsigned col = (it * G + gl) * VEC;
           if (col >= D) continue;
 #pragma unroll
           for (int y = 0; y < VEC; ++y)
@@ -477,18 +495,18 @@ __global__ void __launch_bounds__(kLongWarps * 32) push_long(PushLaunch p, int p
         }
       }
       if ((int)tr != cur_tr) {
-        if (R.apply) flush_absmax(p, cur_tr, cur_max);
+        if (R.apply) flush_absmax(grp, p, cur_tr, cur_max);
         cur_tr = (int)tr; cur_max = 0;
       }
-      bits |= adam_row<VEC, ITERS>(T, row, D, g, wv, mv, vv, R.apply, R.validate, &cur_max);
-      if (R.apply && lane == 0) T.updates[slot] += 1ull;
+      bits |= adam_row<G, VEC, ITERS>(gl, T, row, D, g, wv, mv, vv, R.apply, R.validate, &cur_max);
+      if (R.apply && gl == 0) T.updates[slot] += 1ull;
     }
     __syncthreads();
   }
   if (w == 0) {
-    bits = __reduce_or_sync(0xffffffffu, bits);
-    if (lane == 0 && bits) atomicOr(&p.control->reject_bits, bits);
-    if (R.apply) flush_absmax(p, cur_tr, cur_max);
+    bits = cg::reduce(grp, bits, cg::bit_or<unsigned>());
+    if (gl == 0 && bits) atomicOr(&p.control->reject_bits, bits);
+    if (R.apply) flush_absmax(grp, p, cur_tr, cur_max);
   }
 }
 
@@ -511,32 +529,26 @@ __global__ void push_finalize(PushLaunch p) {
   if (threadIdx.x == 0) c->accepted = accepted ? 1u : 0u;
 }
 
-template <int VEC, int ITERS, typename KeyT>
+template <int G, int VEC, int ITERS, typename KeyT>
 cudaError_t run_apply(const PushLaunch& p, cudaStream_t s) {
   const unsigned long long tiles = (p.n + kTile - 1) / kTile;
-  const unsigned long long want = (tiles + 7) / 8;
-  const unsigned grid = (unsigned)max(1ull, min(want, 148ull * 8));
-  const size_t long_smem = (size_t)kLongWarps * p.dim_max * sizeof(float);
+  const unsigned long long groups_per_block = 256 / G;
+  const unsigned long long want = (tiles + groups_per_block - 1) / groups_per_block;
+  const unsigned long long cap = 148ull * ((VEC * ITERS <= 4) ? 3 : 2) * 8;
+  const unsigned grid = (unsigned)max(1ull, min(want, cap));
+  const size_t long_smem = (size_t)(kLongThreads / G) * p.dim_max * sizeof(float);
   const unsigned long_grid = 148 * 2;
   for (int pass = 0; pass < 2; ++pass) {
-    if (p.n) push_segments<VEC, ITERS, KeyT><<<grid, 256, 0, s>>>(p, pass);
-    if (p.n) push_long<VEC, ITERS, KeyT><<<long_grid, kLongWarps * 32, long_smem, s>>>(p, pass);
+    if (p.n) push_segments<G, VEC, ITERS, KeyT><<<grid, 256, 0, s>>>(p, pass);
+    if (p.n) push_long<G, VEC, ITERS, KeyT><<<long_grid, kLongThreads, long_smem, s>>>(p, pass);
   }
   return cudaGetLastError();
 }
 
-template <int VEC, int ITERS>
+template <int G, int VEC, int ITERS>
 cudaError_t run_key(const PushLaunch& p, cudaStream_t s) {
-  return p.key64 ? run_apply<VEC, ITERS, unsigned long long>(p, s)
-                 : run_apply<VEC, ITERS, unsigned int>(p, s);
-}
-template <int VEC>
-cudaError_t run_iters(const PushLaunch& p, cudaStream_t s) {
-  switch (p.iters) {
-    case 1: return run_key<VEC, 1>(p, s);
-    case 2: return run_key<VEC, 2>(p, s);
-    default: return run_key<VEC, 4>(p, s);
-  }
+  return p.key64 ? run_apply<G, VEC, ITERS, unsigned long long>(p, s)
+                 : run_apply<G, VEC, ITERS, unsigned int>(p, s);
 }
 }  // namespace
 
@@ -552,11 +564,19 @@ cudaError_t launch_push_prescan(const PushLaunch& p, cudaStream_t stream) {
 unsigned launch_push_apply_count(const PushLaunch& p) { return p.n ? 4u : 0u; }
 
 cudaError_t launch_push_apply(const PushLaunch& p, cudaStream_t stream) {
-  switch (p.vec) {
-    case 4: return run_iters<4>(p, stream);
-    case 2: return run_iters<2>(p, stream);
-    default: return run_iters<1>(p, stream);
+  if (p.vec == 4) {
+    switch (p.group) {
+      case 8: return run_key<8, 4, 1>(p, stream);
+      case 16: return run_key<16, 4, 1>(p, stream);
+      default:
+        if (p.iters == 1) return run_key<32, 4, 1>(p, stream);
+        if (p.iters == 2) return run_key<32, 4, 2>(p, stream);
+        return run_key<32, 4, 4>(p, stream);
+    }
   }
+  if (p.iters == 1) return run_key<32, 1, 1>(p, stream);
+  if (p.iters == 2) return run_key<32, 1, 2>(p, stream);
+  return run_key<32, 1, 4>(p, stream);
 }
 
 cudaError_t launch_push_finalize(const PushLaunch& p, cudaStream_t stream) {

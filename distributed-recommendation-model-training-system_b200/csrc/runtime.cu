@@ -94,6 +94,7 @@ struct Ticket {
   int slot = -1;
   bool push_in_flight = false;
   bool lookup_checked = false;
+  cudaEvent_t done = nullptr;       // recorded after an enqueued push's status copy
   // layout
   std::vector<unsigned> feature_ids, feature_tables, dims, ranks;
   std::vector<unsigned long long> grad_rows, scale_base;
@@ -125,22 +126,17 @@ struct Carver {
   }
 };
 
-void choose_vec(const std::vector<unsigned>& dims, bool align16, bool align8, int* vec, int* iters) {
+void choose_vec(const std::vector<unsigned>& dims, bool align16, bool /*align8*/, int* vec,
+                int* group, int* iters) {
   unsigned dmax = 1;
-  bool all4 = true, all2 = true;
-  for (unsigned d : dims) { dmax = std::max(dmax, d); all4 &= d % 4 == 0; all2 &= d % 2 == 0; }
-  int v = 1;
-  if (all4 && align16 && dmax >= 128) v = 4;
-  else if (all2 && align8 && dmax >= 64) v = 2;
-  if (32u * v * 4u < dmax) {
-    if (all4 && align16) v = 4;
-    else if (all2 && align8) v = 2;
-  }
-  const unsigned need = (dmax + 32u * v - 1) / (32u * v);
-  Require(need <= 4, "embedding dimension/alignment not supported by this build",
-          EPS_B200_CAPACITY_EXCEEDED);
-  *vec = v;
-  *iters = need <= 1 ? 1 : (need <= 2 ? 2 : 4);
+  bool all4 = true;
+  for (unsigned d : dims) { dmax = std::max(dmax, d); all4 &= d % 4 == 0; }
+  Shape sh;
+  Require(choose_shape(dmax, all4, align16, &sh),
+          "embedding dimension/alignment not supported by this build", EPS_B200_CAPACITY_EXCEEDED);
+  *vec = sh.vec;
+  *group = sh.group;
+  *iters = sh.iters;
 }
 
 }  // namespace
@@ -162,6 +158,9 @@ struct EpsB200Store {
   HostStatus* host_status = nullptr;
   std::vector<int> free_slots;
   unsigned* sticky_error = nullptr;     // device: errors of read-only device lookups
+  std::deque<unsigned long long> inflight;   // tickets whose push is enqueued, in order
+  std::string deferred;                     // first error of a push settled by Poll
+  std::vector<cudaEvent_t> sync_pool;       // timing-disabled events for completion checks
   unsigned long long allocated_state = 0;
   EpsB200Stats stats{};
   // ---- per-phase device timing (CUDA events on the launching stream)
@@ -176,6 +175,12 @@ struct EpsB200Store {
     if (!event_pool.empty()) { cudaEvent_t e = event_pool.back(); event_pool.pop_back(); return e; }
     cudaEvent_t e;
     Cuda(cudaEventCreate(&e));
+    return e;
+  }
+  cudaEvent_t SyncEvent() {
+    if (!sync_pool.empty()) { cudaEvent_t e = sync_pool.back(); sync_pool.pop_back(); return e; }
+    cudaEvent_t e;
+    Cuda(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     return e;
   }
   cudaEvent_t Begin(cudaStream_t stream) {
@@ -297,6 +302,7 @@ struct EpsB200Store {
     Ticket& t = it->second;
     const HostStatus& h = host_status[t.slot];
     t.push_in_flight = false;
+    if (t.done) { sync_pool.push_back(t.done); t.done = nullptr; }
     if (h.control.accepted) {
       ++stats.updates;
       Complete(it->first);
@@ -311,6 +317,20 @@ struct EpsB200Store {
       return m;
     }
     return PushMessage(h.control.reject_bits, h.lookup_error);
+  }
+  // Settles, without waiting, every enqueued push that the device has finished
+  // (in enqueue order), so tickets of asynchronous pushes release their device
+  // memory as soon as possible.  Rejections are reported by the next
+  // eps_b200_synchronize.
+  void Poll(cudaStream_t stream) {
+    while (!inflight.empty()) {
+      auto it = tickets.find(inflight.front());
+      if (it == tickets.end() || !it->second.push_in_flight) { inflight.pop_front(); continue; }
+      if (cudaEventQuery(it->second.done) != cudaSuccess) break;
+      inflight.pop_front();
+      const std::string m = Resolve(it, stream);
+      if (!m.empty() && deferred.empty()) deferred = m;
+    }
   }
 };
 
@@ -415,6 +435,8 @@ void eps_b200_destroy(EpsB200Store* s) {
     if (s->ring) cudaFreeHost(s->ring);
     for (auto& x : s->pending) { cudaEventDestroy(x.a); cudaEventDestroy(x.b); }
     for (auto e : s->event_pool) cudaEventDestroy(e);
+    for (auto e : s->sync_pool) cudaEventDestroy(e);
+    for (auto& [id, t] : s->tickets) if (t.done) cudaEventDestroy(t.done);
     if (s->sticky_error) cudaFree(s->sticky_error);
     if (s->host_status) cudaFreeHost(s->host_status);
     if (s->last_done) cudaEventDestroy(s->last_done);
@@ -439,7 +461,8 @@ int eps_b200_create_table(EpsB200Store* store, const EpsB200Table* table, EpsB20
     Require(s.tables.size() < 1024, "table count exceeds limit", EPS_B200_CAPACITY_EXCEEDED);
     const unsigned long long shard = s.opt.shard_id, n = s.opt.shard_count;
     const unsigned long long rows = d.key_space > shard ? (d.key_space - 1 - shard) / n + 1 : 0;
-    Require(rows < (1ull << 40), "key space exceeds limit", EPS_B200_CAPACITY_EXCEEDED);
+    Require(rows < 0xffffffffull, "key space exceeds the per-shard slot limit (2^32 - 1)",
+            EPS_B200_CAPACITY_EXCEEDED);
     const unsigned long long bytes = rows * (12ull * d.dimension + 8);
     Require(s.opt.state_bytes >= s.allocated_state && bytes <= s.opt.state_bytes - s.allocated_state,
             "parameter-state budget exhausted", EPS_B200_CAPACITY_EXCEEDED);
@@ -546,8 +569,8 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
     const unsigned table_bits = bits_for(ranks.size() - 1);
     const int key64 = slot_bits + table_bits > 32;
     const size_t key_bytes = key64 ? 8 : 4;
-    int vec, iters;
-    choose_vec(dims, out16, out8, &vec, &iters);
+    int vec, group, iters;
+    choose_vec(dims, out16, out8, &vec, &group, &iters);
 
     // ---- slab layout
     Carver c;
@@ -580,6 +603,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       at_gpre = c.take<unsigned long long>(count + 1);
     }
     cudaStream_t stream = s.Use(stream_arg);
+    s.Poll(stream);
     char* slab = nullptr;
     Cuda(cudaMallocAsync(reinterpret_cast<void**>(&slab), std::max<size_t>(c.offset, 256), stream));
     auto P = [&](size_t at) { return slab + at; };
@@ -663,6 +687,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       lp.key64 = key64;
       lp.error = read_only && input_on_device && !any_host_out ? s.sticky_error : err;
       lp.vec = vec;
+      lp.group = group;
       lp.iters = iters;
       if (!read_only) {
         lp.occ_key = P(at_k0);
@@ -806,17 +831,12 @@ int eps_b200_lookup_noalloc(EpsB200Store* store, const EpsB200Feature* features,
       L.feature_index = (unsigned)i;
       bag_base += L.bag_count;
     }
-    // vector width as in the regular lookup (no heap use here)
-    int vec = 1;
-    if (all4 && out16 && dmax >= 128) vec = 4;
-    else if (all2 && out8 && dmax >= 64) vec = 2;
-    if (32u * vec * 4u < dmax) {
-      if (all4 && out16) vec = 4;
-      else if (all2 && out8) vec = 2;
-    }
-    const unsigned need = (dmax + 32u * vec - 1) / (32u * vec);
-    Require(need <= 4, "embedding dimension/alignment not supported by this build",
-            EPS_B200_CAPACITY_EXCEEDED);
+    // launch shape as in the regular lookup (no heap use here)
+    Shape sh;
+    Require(choose_shape(dmax, all4, out16, &sh),
+            "embedding dimension/alignment not supported by this build", EPS_B200_CAPACITY_EXCEEDED);
+    (void)all2;
+    (void)out8;
     LookupFeature* table = nullptr;
     Cuda(noalloc_feature_table(s.opt.device, &table));
     cudaStream_t stream = s.Use(stream_arg);
@@ -833,8 +853,9 @@ int eps_b200_lookup_noalloc(EpsB200Store* store, const EpsB200Feature* features,
     lp.slot_bits = 1;
     lp.key64 = 0;
     lp.error = s.sticky_error;      // reported by eps_b200_synchronize
-    lp.vec = vec;
-    lp.iters = need <= 1 ? 1 : (need <= 2 ? 2 : 4);
+    lp.vec = sh.vec;
+    lp.group = sh.group;
+    lp.iters = sh.iters;
     Cuda(launch_lookup(lp, stream));
     ++s.stats.lookups;
     if (bag_base) ++s.stats.kernel_launches;
@@ -849,6 +870,7 @@ int eps_b200_push(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gra
     std::lock_guard lock(s.mutex);
     s.Activate();
     cudaStream_t stream = s.Use(stream_arg);
+    s.Poll(stream);
     auto it = s.tickets.find(ticket);
     if (it == s.tickets.end()) {
       // src/server/service.cpp:241-245: a completed Push is acknowledged again
@@ -890,8 +912,8 @@ int eps_b200_push(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gra
       total_values += n;
       ordered[i] = &g;
     }
-    int vec, iters;
-    choose_vec(t.dims, g16, g8, &vec, &iters);
+    int vec, group, iters;
+    choose_vec(t.dims, g16, g8, &vec, &group, &iters);
     float* stage = nullptr;
     if (host_values)
       Cuda(cudaMallocAsync(reinterpret_cast<void**>(&stage), host_values * 4, stream));
@@ -958,6 +980,7 @@ int eps_b200_push(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gra
       pl.lookup_error = t.lookup_error;
       pl.long_run = (s.opt.flags & EPS_B200_FLAG_REFERENCE_ORDER) ? ~0ull : (unsigned long long)kLongRun;
       pl.vec = vec;
+      pl.group = group;
       pl.iters = iters;
       cudaEvent_t ev = s.Begin(stream);
       Cuda(launch_push_prescan(pl, stream));
@@ -973,6 +996,9 @@ int eps_b200_push(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gra
       Cuda(cudaMemcpyAsync(&s.host_status[t.slot].lookup_error, t.lookup_error, sizeof(unsigned),
                            cudaMemcpyDeviceToHost, stream));
       if (stage) { float* owned = stage; stage = nullptr; Cuda(cudaFreeAsync(owned, stream)); }
+      t.done = s.SyncEvent();
+      Cuda(cudaEventRecord(t.done, stream));
+      s.inflight.push_back(ticket);
       t.push_in_flight = true;
       s.Done(stream);
     } catch (...) {
@@ -1017,7 +1043,9 @@ int eps_b200_synchronize(EpsB200Store* store, EpsB200Status* status) {
     s.Activate();
     cudaStream_t stream = s.Use(nullptr);
     s.Sync(stream);
-    std::string first;
+    std::string first = s.deferred;
+    s.deferred.clear();
+    s.inflight.clear();
     for (auto it = s.tickets.begin(); it != s.tickets.end();) {
       auto next = std::next(it);
       if (it->second.push_in_flight) {
