@@ -80,6 +80,7 @@ enum LookupErrorBits : unsigned int {
   kLookupBadOffsets = 1u,       // src/access/batch_access.cpp:14-16
   kLookupBadKey = 2u,           // key routed to another shard / outside the table
   kLookupShortLength = 4u,      // src/access/batch_access.cpp:18-20
+  kLookupSortFailed = 8u,       // a coalescing-sort wait ran out (never expected)
 };
 
 // Per-push control block (device).  Zeroed before each push.

@@ -67,6 +67,22 @@ __device__ __forceinline__ float clamp_weight(float v, int has, float lo, float 
 
 __device__ __forceinline__ unsigned abs_bits(float x) { return __float_as_uint(fabsf(x)); }
 
+// Asynchronous global -> shared copies (sm_80+ cp.async): VEC floats per lane.
+template <int VEC>
+__device__ __forceinline__ void cp_async_vec(float* smem, const float* gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  if constexpr (VEC == 4) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+  } else if constexpr (VEC == 2) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(s), "l"(gmem));
+  } else {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem));
+  }
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
 // Launch shape of the row kernels: a group of `group` lanes owns one row, each
 // lane `vec` consecutive floats, `iters` times.  128-bit accesses (vec = 4) need
 // every dimension divisible by 4 and 16-byte aligned buffers; then
@@ -111,14 +127,17 @@ struct SortLaunch {
   unsigned long long n;
   unsigned int bits;
   int key64;
-  unsigned int* tile_hist;         // scratch: 256 * tiles
-  unsigned int tiles;
+  unsigned int* scratch;           // sort_scratch_bytes(n, bits), 256-byte aligned
+  unsigned int tiles;              // sort_tiles(n)
+  unsigned int* error;             // set (kLookupSortFailed) if a look-back wait ran out
 };
 // Stable LSD radix sort; returns in *swapped whether the result is in the alt
 // buffers.
 cudaError_t launch_sort(const SortLaunch& p, cudaStream_t stream, int* swapped);
 unsigned int sort_launch_count(const SortLaunch& p);
 unsigned int sort_tiles(unsigned long long n);
+size_t sort_scratch_header(unsigned passes);
+size_t sort_scratch_bytes(unsigned long long n, unsigned bits);
 
 struct PushLaunch {
   const PushTable* tables;         // device, per table rank

@@ -142,14 +142,12 @@ __device__ __forceinline__ unsigned full_mask() { return G == 32 ? 0xffffffffu :
 // Sum of gradient references [s0, s1) (all with the same key), serially in order,
 // by the G lanes of `grp` (each lane owns VEC*ITERS columns).
 template <int G, int VEC, int ITERS, typename Grp>
-__device__ __forceinline__ void reduce_range(const Grp& grp, const PushLaunch& p,
-                                             unsigned long long s0, unsigned long long s1,
-                                             unsigned D, float (&acc)[VEC * ITERS]) {
+__device__ __forceinline__ void accumulate_global(const Grp& grp, const PushLaunch& p,
+                                                  unsigned long long s0, unsigned long long s1,
+                                                  unsigned D, float (&acc)[VEC * ITERS]) {
   constexpr int C = VEC * ITERS;
   constexpr int DEPTH = C <= 4 ? 4 : 2;
   const unsigned gl = grp.thread_rank();
-#pragma unroll
-  for (int k = 0; k < C; ++k) acc[k] = 0.0f;
   for (unsigned long long c0 = s0; c0 < s1; c0 += G) {
     const unsigned long long i = c0 + gl;
     unsigned long long gp = 0;
@@ -192,6 +190,65 @@ __device__ __forceinline__ void reduce_range(const Grp& grp, const PushLaunch& p
 #pragma unroll
         for (int k = 0; k < C; ++k) acc[k] = __fadd_rn(acc[k], __fmul_rn(x[u][k], s[u]));
       }
+    }
+  }
+}
+
+template <int G, int VEC, int ITERS, typename Grp>
+__device__ __forceinline__ void reduce_range(const Grp& grp, const PushLaunch& p,
+                                             unsigned long long s0, unsigned long long s1,
+                                             unsigned D, float (&acc)[VEC * ITERS]) {
+#pragma unroll
+  for (int k = 0; k < VEC * ITERS; ++k) acc[k] = 0.0f;
+  accumulate_global<G, VEC, ITERS>(grp, p, s0, s1, D, acc);
+}
+
+// Value held by lane (pos % G) in its register slot pos / G (pos uniform in the group).
+template <int PER, typename T, typename Grp>
+__device__ __forceinline__ T tile_value(const Grp& grp, const T (&arr)[PER], unsigned pos) {
+  constexpr unsigned G = Grp::num_threads();
+  const unsigned r = pos / G;
+  T v = arr[0];
+#pragma unroll
+  for (int i = 1; i < PER; ++i) if ((unsigned)i == r) v = arr[i];
+  return grp.shfl(v, pos % G);
+}
+
+// Accumulates the gradient rows of tile positions [lo, hi) in order, continuing acc.
+template <int G, int VEC, int ITERS, int PER, typename Grp>
+__device__ __forceinline__ void accumulate_tile(const Grp& grp, const unsigned long long (&gp)[PER],
+                                                const float (&sc)[PER], unsigned lo, unsigned hi,
+                                                unsigned D, float (&acc)[VEC * ITERS]) {
+  constexpr int C = VEC * ITERS;
+  constexpr int DEPTH = C <= 4 ? 4 : 2;
+  const unsigned gl = grp.thread_rank();
+  for (unsigned j0 = lo; j0 < hi; j0 += DEPTH) {
+    float x[DEPTH][C];
+    float s[DEPTH];
+#pragma unroll
+    for (int u = 0; u < DEPTH; ++u) {
+      const bool use = j0 + u < hi;
+      const unsigned pos = use ? j0 + u : lo;
+      const unsigned long long q = tile_value<PER>(grp, gp, pos);
+      s[u] = tile_value<PER>(grp, sc, pos);
+#pragma unroll
+      for (int it = 0; it < ITERS; ++it) {
+        const unsigned col = (it * G + gl) * VEC;
+        float t[VEC];
+        if (use && col < D) load_vec<VEC>(reinterpret_cast<const float*>(q) + col, t);
+        else {
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) t[v] = 0.0f;
+        }
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) x[u][it * VEC + v] = t[v];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < DEPTH; ++u) {
+      if (j0 + u >= hi) break;
+#pragma unroll
+      for (int k = 0; k < C; ++k) acc[k] = __fadd_rn(acc[k], __fmul_rn(x[u][k], s[u]));
     }
   }
 }
@@ -315,84 +372,194 @@ __device__ __forceinline__ void flush_absmax(const Grp& grp, const PushLaunch& p
 }
 
 // ----------------------------------------------------------------- segments
+// Shared-memory ring per group: RING slots of [w | m | v | first gradient row].
+template <int G, int VEC, int ITERS>
+struct SegShape {
+  static constexpr int C = VEC * ITERS;
+  static constexpr int DCOLS = G * VEC * ITERS;     // columns one group covers
+  static constexpr int RING = C <= 4 ? 4 : 2;
+  static constexpr int PER = kTile / G;             // tile positions per lane
+  static constexpr int GROUPS = 256 / G;
+  static constexpr size_t SMEM = (size_t)GROUPS * RING * 4 * DCOLS * sizeof(float);
+};
+
 template <int G, int VEC, int ITERS, typename KeyT>
-__global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? 3 : 2) push_segments(PushLaunch p, int pass) {
+__global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? 3 : 1) push_segments(PushLaunch p, int pass) {
   const Role R = role(p.control, pass);
   if (!R.run) return;
-  constexpr int C = VEC * ITERS;
+  using S = SegShape<G, VEC, ITERS>;
+  constexpr int C = S::C, DC = S::DCOLS, RING = S::RING, PER = S::PER;
+  extern __shared__ float s_ring[];
   const auto grp = cg::tiled_partition<G>(cg::this_thread_block());
   const unsigned gl = grp.thread_rank();
+  float* ring = s_ring + (threadIdx.x / G) * (RING * 4 * DC);
   const unsigned long long n = p.n;
   const unsigned long long tiles = (n + kTile - 1) / kTile;
   const unsigned long long gid = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) / G;
   const unsigned long long ngroups = (gridDim.x * (unsigned long long)blockDim.x) / G;
   const KeyT slot_mask = (p.slot_bits >= sizeof(KeyT) * 8) ? ~KeyT(0)
                                                            : ((KeyT(1) << p.slot_bits) - 1);
+  const bool work = R.apply || R.validate;
   unsigned bits = 0;
   int cur_tr = -1;
   unsigned cur_max = 0;
 
   for (unsigned long long t = gid; t < tiles; t += ngroups) {
     const unsigned long long b = t * kTile;
-    const unsigned long long e = min(n, b + kTile);
-    unsigned long long q = b;
-    const KeyT kb = key_at<KeyT>(p.keys, b);
-    if (b > 0 && key_at<KeyT>(p.keys, b - 1) == kb) {
-      // the segment holding b started in an earlier tile
+    const unsigned L = (unsigned)min((unsigned long long)kTile, n - b);   // valid positions
+    // ---- discovery: keys, segment heads, gradient sources of the whole tile
+    KeyT kp[PER];
+    unsigned heads = 0;
+    KeyT carry = (b > 0) ? key_at<KeyT>(p.keys, b - 1) : KeyT(0);
+#pragma unroll
+    for (int r = 0; r < PER; ++r) {
+      const unsigned j = r * G + gl;
+      const bool valid = j < L;
+      const KeyT k = valid ? key_at<KeyT>(p.keys, b + j) : KeyT(0);
+      KeyT prev = grp.shfl_up(k, 1);
+      if (gl == 0) prev = carry;
+      const bool head = valid && ((b + j == 0) || k != prev);
+      heads |= (unsigned)grp.ballot(head) << (r * G);
+      carry = grp.shfl(k, G - 1);
+      kp[r] = k;
+    }
+    unsigned long long gp[PER];
+    float sc[PER];
+#pragma unroll
+    for (int r = 0; r < PER; ++r) {
+      const unsigned j = r * G + gl;
+      gp[r] = 0;
+      sc[r] = 0.0f;
+      if (j < L) {
+        const unsigned src = __ldg(p.srcs + b + j);
+        const unsigned f = src >> kRowBits;
+        const unsigned row = src & ((1u << kRowBits) - 1u);
+        const PushFeature* F = p.features + f;
+        const unsigned Df = __ldg(&F->dim);
+        const float* g = reinterpret_cast<const float*>(__ldg(reinterpret_cast<const unsigned long long*>(&F->grad)));
+        gp[r] = reinterpret_cast<unsigned long long>(g + (unsigned long long)row * Df);
+        sc[r] = __ldg(p.row_scale + __ldg(&F->scale_base) + row);
+      }
+    }
+    const KeyT k_last = tile_value<PER>(grp, kp, L - 1);
+    const bool crosses = b + L < n && key_at<KeyT>(p.keys, b + L) == k_last;
+    const unsigned first_head = heads ? (unsigned)(__ffs(heads) - 1) : L;
+    // ---- a segment that started in an earlier tile
+    if (first_head > 0) {
+      const KeyT kb = tile_value<PER>(grp, kp, 0);
       const unsigned long long back = run_backward<G, KeyT>(grp, p.keys, b, kb, p.long_run);
-      const unsigned long long fwd = run_forward<G, KeyT>(grp, p.keys, n, b, kb, p.long_run);
-      const unsigned long long stop = min(b + fwd, e);
-      if (back + fwd > p.long_run) {
+      unsigned long long fwd = first_head;
+      if (first_head == L && crosses) fwd += run_forward<G, KeyT>(grp, p.keys, n, b + L, kb, p.long_run);
+      if (back + fwd > p.long_run && R.partials) {
+        const unsigned tr = (unsigned)(kb >> p.slot_bits);
+        if (tr < p.table_count) {
+          const unsigned D = p.tables[tr].dim;
+          float acc[C];
+#pragma unroll
+          for (int k = 0; k < C; ++k) acc[k] = 0.0f;
+          accumulate_tile<G, VEC, ITERS, PER>(grp, gp, sc, 0, first_head, D, acc);
+          store_piece<G, VEC, ITERS>(gl, p.part0, p.dim_max, t, D, acc);
+        }
+      }
+    }
+    // ---- the last segment starting in the tile may run on (and may be long)
+    unsigned short_mask = heads;
+    unsigned last_len = 0;
+    const int last_start = heads ? 31 - __clz(heads) : -1;
+    if (last_start >= 0) {
+      last_len = L - (unsigned)last_start;
+      unsigned long long tail = 0;
+      if (crosses) tail = run_forward<G, KeyT>(grp, p.keys, n, b + L, k_last, p.long_run);
+      if ((unsigned long long)last_len + tail > p.long_run) {
+        short_mask &= ~(1u << last_start);
         if (R.partials) {
-          const unsigned tr = (unsigned)(kb >> p.slot_bits);
+          const unsigned tr = (unsigned)(k_last >> p.slot_bits);
           if (tr < p.table_count) {
             const unsigned D = p.tables[tr].dim;
             float acc[C];
-            reduce_range<G, VEC, ITERS>(grp, p, b, stop, D, acc);
-            store_piece<G, VEC, ITERS>(gl, p.part0, p.dim_max, t, D, acc);
+#pragma unroll
+            for (int k = 0; k < C; ++k) acc[k] = 0.0f;
+            accumulate_tile<G, VEC, ITERS, PER>(grp, gp, sc, (unsigned)last_start, L, D, acc);
+            const unsigned which = last_start == 0 ? 0u : 1u;
+            store_piece<G, VEC, ITERS>(gl, which ? p.part1 : p.part0, p.dim_max, t, D, acc);
+            if (gl == 0) {
+              const unsigned at = atomicAdd(&p.control->long_count, 1u);
+              p.records[at] = LongRecord{(unsigned long long)k_last, (unsigned)t, which};
+            }
           }
         }
-        q = stop;
       } else {
-        q = b + fwd;   // a short segment, processed by the tile where it starts
+        last_len = (unsigned)(last_len + tail);
       }
     }
-    while (q < e) {
-      const KeyT K = key_at<KeyT>(p.keys, q);
-      const unsigned long long len = run_forward<G, KeyT>(grp, p.keys, n, q, K, p.long_run);
+    if (!work || !short_mask) continue;
+    // ---- short segments: row state + first gradient row prefetched RING deep
+    unsigned issue = short_mask, proc = short_mask;
+    const int nseg = __popc(short_mask);
+    for (int j = 0; j < nseg + RING - 1; ++j) {
+      if (issue) {
+        const unsigned s0 = (unsigned)(__ffs(issue) - 1);
+        issue &= issue - 1;
+        const KeyT K = tile_value<PER>(grp, kp, s0);
+        const unsigned tr = (unsigned)(K >> p.slot_bits);
+        if (tr < p.table_count) {
+          const unsigned D = p.tables[tr].dim;
+          const float* row = p.tables[tr].state + (unsigned long long)(K & slot_mask) * 3ull * D;
+          const float* g0 = reinterpret_cast<const float*>(tile_value<PER>(grp, gp, s0));
+          float* slot = ring + (j % RING) * (4 * DC);
+#pragma unroll
+          for (int it = 0; it < ITERS; ++it) {
+            const unsigned col = (it * G + gl) * VEC;
+            if (col < D) {
+              cp_async_vec<VEC>(slot + col, row + col);
+              cp_async_vec<VEC>(slot + DC + col, row + D + col);
+              cp_async_vec<VEC>(slot + 2 * DC + col, row + 2 * D + col);
+              cp_async_vec<VEC>(slot + 3 * DC + col, g0 + col);
+            }
+          }
+        }
+      }
+      cp_async_commit();
+      if (j < RING - 1) continue;
+      const int jj = j - (RING - 1);
+      const unsigned s1 = (unsigned)(__ffs(proc) - 1);
+      proc &= proc - 1;
+      cp_async_wait<RING - 1>();
+      const KeyT K = tile_value<PER>(grp, kp, s1);
       const unsigned tr = (unsigned)(K >> p.slot_bits);
-      const unsigned long long slot = (unsigned long long)(K & slot_mask);
-      if (tr >= p.table_count) { q += len; continue; }
+      if (tr >= p.table_count) continue;
       const PushTable& T = p.tables[tr];
       const unsigned D = T.dim;
-      if (len <= p.long_run) {
-        if (R.apply || R.validate) {
-          float* row = T.state + slot * 3ull * D;
-          float w[C], m[C], v[C], g[C];
-          load_state<G, VEC, ITERS>(gl, row, D, w, m, v);   // issued before the reduction
-          reduce_range<G, VEC, ITERS>(grp, p, q, q + len, D, g);
-          if ((int)tr != cur_tr) {
-            if (R.apply) flush_absmax(grp, p, cur_tr, cur_max);
-            cur_tr = (int)tr; cur_max = 0;
-          }
-          bits |= adam_row<G, VEC, ITERS>(gl, T, row, D, g, w, m, v, R.apply, R.validate, &cur_max);
-          if (R.apply && gl == 0) T.updates[slot] += 1ull;
+      // segment length: up to the next head, or last_len for the last one
+      const unsigned above = heads & ~((2u << s1) - 1u);
+      const unsigned len = above ? (unsigned)(__ffs(above) - 1) - s1 : last_len;
+      const unsigned in_tile = min(len, L - s1);
+      const float* slot = ring + (jj % RING) * (4 * DC);
+      float g[C], w[C], m[C], v[C];
+      const float s_first = tile_value<PER>(grp, sc, s1);
+#pragma unroll
+      for (int it = 0; it < ITERS; ++it) {
+        const unsigned col = (it * G + gl) * VEC;
+#pragma unroll
+        for (int x = 0; x < VEC; ++x) {
+          const int k = it * VEC + x;
+          const bool in = col + x < D;
+          w[k] = in ? slot[col + x] : 0.0f;
+          m[k] = in ? slot[DC + col + x] : 0.0f;
+          v[k] = in ? slot[2 * DC + col + x] : 0.0f;
+          // batch_access.cpp:118: 0 + first term
+          g[k] = __fadd_rn(0.0f, __fmul_rn(in ? slot[3 * DC + col + x] : 0.0f, s_first));
         }
-        q += len;
-      } else {
-        // long segment starting at q: it runs past e (len > long_run >= kTile >= e - q)
-        if (R.partials) {
-          float acc[C];
-          reduce_range<G, VEC, ITERS>(grp, p, q, e, D, acc);
-          const unsigned which = q == b ? 0u : 1u;
-          store_piece<G, VEC, ITERS>(gl, which ? p.part1 : p.part0, p.dim_max, t, D, acc);
-          if (gl == 0) {
-            const unsigned at = atomicAdd(&p.control->long_count, 1u);
-            p.records[at] = LongRecord{(unsigned long long)K, (unsigned)t, which};
-          }
-        }
-        q = e;
       }
+      if (in_tile > 1) accumulate_tile<G, VEC, ITERS, PER>(grp, gp, sc, s1 + 1, s1 + in_tile, D, g);
+      if (len > in_tile) accumulate_global<G, VEC, ITERS>(grp, p, b + L, b + s1 + len, D, g);
+      if ((int)tr != cur_tr) {
+        if (R.apply) flush_absmax(grp, p, cur_tr, cur_max);
+        cur_tr = (int)tr; cur_max = 0;
+      }
+      float* grow = T.state + (unsigned long long)(K & slot_mask) * 3ull * D;
+      bits |= adam_row<G, VEC, ITERS>(gl, T, grow, D, g, w, m, v, R.apply, R.validate, &cur_max);
+      if (R.apply && gl == 0) T.updates[(unsigned long long)(K & slot_mask)] += 1ull;
     }
   }
   bits = cg::reduce(grp, bits, cg::bit_or<unsigned>());
@@ -531,15 +698,27 @@ __global__ void push_finalize(PushLaunch p) {
 
 template <int G, int VEC, int ITERS, typename KeyT>
 cudaError_t run_apply(const PushLaunch& p, cudaStream_t s) {
+  using SS = SegShape<G, VEC, ITERS>;
+  // the shared-memory opt-in is a per-device attribute of the function
+  static bool configured[64] = {};
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return e;
+  if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
+  if (!configured[device]) {
+    e = cudaFuncSetAttribute(push_segments<G, VEC, ITERS, KeyT>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SS::SMEM);
+    if (e != cudaSuccess) return e;
+    configured[device] = true;
+  }
   const unsigned long long tiles = (p.n + kTile - 1) / kTile;
-  const unsigned long long groups_per_block = 256 / G;
-  const unsigned long long want = (tiles + groups_per_block - 1) / groups_per_block;
-  const unsigned long long cap = 148ull * ((VEC * ITERS <= 4) ? 3 : 2) * 8;
+  const unsigned long long want = (tiles + SS::GROUPS - 1) / SS::GROUPS;
+  const unsigned long long cap = 148ull * ((VEC * ITERS <= 4) ? 3 : 1);
   const unsigned grid = (unsigned)max(1ull, min(want, cap));
   const size_t long_smem = (size_t)(kLongThreads / G) * p.dim_max * sizeof(float);
   const unsigned long_grid = 148 * 2;
   for (int pass = 0; pass < 2; ++pass) {
-    if (p.n) push_segments<G, VEC, ITERS, KeyT><<<grid, 256, 0, s>>>(p, pass);
+    if (p.n) push_segments<G, VEC, ITERS, KeyT><<<grid, 256, SS::SMEM, s>>>(p, pass);
     if (p.n) push_long<G, VEC, ITERS, KeyT><<<long_grid, kLongThreads, long_smem, s>>>(p, pass);
   }
   return cudaGetLastError();

@@ -283,6 +283,7 @@ struct EpsB200Store {
 
   // Lookup-input errors recorded by the lookup kernel (LookupErrorBits).
   static std::string LookupMessage(unsigned bits) {
+    if (bits & kLookupSortFailed) return "coalescing sort did not complete";
     if (bits & kLookupBadOffsets) return "invalid bag offsets";
     if (bits & kLookupShortLength) return "original bag length is smaller than shard contribution";
     return "key routed to wrong shard or outside the table";
@@ -593,7 +594,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       at_s0 = c.take<unsigned>(total_keys);
       at_s1 = c.take<unsigned>(total_keys);
       at_scale = c.take<float>(total_rows);
-      at_hist = c.take<unsigned>(256ull * std::max(1u, stiles));
+      at_hist = c.take<char>(sort_scratch_bytes(total_keys, slot_bits + table_bits));
       at_p0 = c.take<float>(ptiles * dim_max);
       at_p1 = c.take<float>(ptiles * dim_max);
       at_rec = c.take<LongRecord>(std::max(1ull, ptiles));
@@ -700,7 +701,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       if (!read_only) {
         SortLaunch sp{P(at_k0), P(at_k1), reinterpret_cast<unsigned*>(P(at_s0)),
                       reinterpret_cast<unsigned*>(P(at_s1)), total_keys, slot_bits + table_bits,
-                      key64, reinterpret_cast<unsigned*>(P(at_hist)), stiles};
+                      key64, reinterpret_cast<unsigned*>(P(at_hist)), stiles, err};
         int swapped = 0;
         ev = s.Begin(stream);
         Cuda(launch_sort(sp, stream, &swapped));

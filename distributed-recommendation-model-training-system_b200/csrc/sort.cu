@@ -8,10 +8,18 @@
 // ordered list of (gradient row, scale) references as in the reference.  The
 // order of the unique rows themselves is not observable in the resulting state.
 //
-// Each 8-bit pass is reduce-then-scan: (1) per-tile digit histograms,
-// (2) one exclusive scan over the digit-major [digit][tile] table, (3) a stable
-// scatter in which every warp ranks its items with __match_any_sync, keeps
-// per-warp running digit counts in shared memory and combines warps in order.
+// Single-pass-per-digit ("onesweep") design, 8-bit digits:
+//   1. one histogram kernel computes the global digit counts of EVERY pass in a
+//      single read of the keys (digit counts do not depend on the order);
+//   2. per pass, one kernel: each CTA takes the next tile in launch order from an
+//      atomic counter, ranks its 4096 items stably (warp-private running counts
+//      with __match_any_sync), publishes its per-digit counts, obtains the
+//      exclusive prefix of all earlier tiles by decoupled look-back over their
+//      published (flag, count) words, and scatters.
+// A tile only waits for tiles taken earlier, whose CTAs are already running and
+// publish their counts before they wait themselves, so every wait ends; each
+// wait is nevertheless bounded, and a wait that runs out records an error that
+// rejects the dependent push instead of hanging.
 #include "kernels.cuh"
 
 namespace eps_b200 {
@@ -21,74 +29,55 @@ constexpr int kItems = 16;
 constexpr int kSortTile = kThreads * kItems;       // 4096 items per tile
 constexpr int kWarps = kThreads / 32;
 constexpr int kWarpSpan = kSortTile / kWarps;      // 512 items per warp
+constexpr unsigned long long kFlagAggregate = 1ull << 32;
+constexpr unsigned long long kFlagPrefix = 2ull << 32;
+constexpr unsigned kSpinLimit = 1u << 26;
 
+// Global digit histograms of all passes: hist[pass][256].
 template <typename KeyT>
-__global__ void __launch_bounds__(kThreads) upsweep(const KeyT* keys, unsigned long long n,
-                                                    unsigned shift, unsigned* hist,
-                                                    unsigned tiles) {
-  __shared__ unsigned s_hist[kWarps][256];
-  const unsigned w = threadIdx.x >> 5;
-  for (unsigned i = threadIdx.x; i < kWarps * 256; i += kThreads) (&s_hist[0][0])[i] = 0;
+__global__ void __launch_bounds__(kThreads) digit_histograms(const KeyT* keys, unsigned long long n,
+                                                             unsigned passes, unsigned* hist) {
+  __shared__ unsigned s_hist[8][256];
+  for (unsigned i = threadIdx.x; i < 8 * 256; i += kThreads) (&s_hist[0][0])[i] = 0;
   __syncthreads();
-  const unsigned long long base = (unsigned long long)blockIdx.x * kSortTile;
-#pragma unroll 4
-  for (int k = 0; k < kItems; ++k) {
-    const unsigned long long idx = base + (unsigned long long)k * kThreads + threadIdx.x;
-    if (idx < n) atomicAdd(&s_hist[w][(unsigned)(keys[idx] >> shift) & 255u], 1u);
-  }
-  __syncthreads();
-  for (unsigned d = threadIdx.x; d < 256; d += kThreads) {
-    unsigned sum = 0;
-#pragma unroll
-    for (int x = 0; x < kWarps; ++x) sum += s_hist[x][d];
-    hist[(unsigned long long)d * tiles + blockIdx.x] = sum;
-  }
-}
-
-// Exclusive scan of `total` counters in place, one block of 1024 threads.
-__global__ void __launch_bounds__(1024) scan_counts(unsigned* data, unsigned total) {
-  __shared__ unsigned s_warp[32];
-  const unsigned t = threadIdx.x, lane = t & 31, w = t >> 5;
-  const unsigned chunk = (total + 1023) / 1024;
-  const unsigned begin = min(total, t * chunk), end = min(total, begin + chunk);
-  unsigned sum = 0;
-  for (unsigned i = begin; i < end; ++i) sum += data[i];
-  // block exclusive scan of per-thread sums
-  unsigned x = sum;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const unsigned y = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= (unsigned)o) x += y;
-  }
-  if (lane == 31) s_warp[w] = x;
-  __syncthreads();
-  if (w == 0) {
-    unsigned z = s_warp[lane];
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const unsigned y = __shfl_up_sync(0xffffffffu, z, o);
-      if (lane >= (unsigned)o) z += y;
+  const unsigned lane = threadIdx.x & 31;
+  const unsigned lt = (1u << lane) - 1u;
+  for (unsigned long long base = blockIdx.x * (unsigned long long)kThreads; base < n;
+       base += (unsigned long long)gridDim.x * kThreads) {
+    const unsigned long long i = base + threadIdx.x;
+    const bool valid = i < n;
+    const KeyT k = valid ? keys[i] : KeyT(0);
+    for (unsigned p = 0; p < passes; ++p) {
+      const unsigned d = valid ? ((unsigned)(k >> (8 * p)) & 255u) : 256u;
+      const unsigned peers = __match_any_sync(0xffffffffu, d);   // warp-aggregated
+      if (valid && (peers & lt) == 0) atomicAdd(&s_hist[p][d], __popc(peers));
     }
-    s_warp[lane] = z;
   }
   __syncthreads();
-  unsigned run = x - sum + (w ? s_warp[w - 1] : 0u);
-  for (unsigned i = begin; i < end; ++i) { const unsigned c = data[i]; data[i] = run; run += c; }
+  for (unsigned i = threadIdx.x; i < passes * 256; i += kThreads) {
+    const unsigned c = (&s_hist[0][0])[i];
+    if (c) atomicAdd(hist + i, c);
+  }
 }
 
 template <typename KeyT>
-__global__ void __launch_bounds__(kThreads) downsweep(const KeyT* kin, const unsigned* vin,
-                                                      KeyT* kout, unsigned* vout,
-                                                      unsigned long long n, unsigned shift,
-                                                      const unsigned* hist, unsigned tiles) {
+__global__ void __launch_bounds__(kThreads) onesweep_pass(const KeyT* kin, const unsigned* vin,
+                                                          KeyT* kout, unsigned* vout,
+                                                          unsigned long long n, unsigned shift,
+                                                          const unsigned* hist,
+                                                          unsigned long long* status,
+                                                          unsigned* tile_counter,
+                                                          unsigned* error) {
   __shared__ unsigned s_cnt[kWarps][256];
-  __shared__ unsigned s_glob[256];
+  __shared__ unsigned s_base[256];       // global exclusive digit base + earlier tiles
+  __shared__ unsigned s_tile;
+  __shared__ unsigned s_warp_sum[kWarps];
   const unsigned w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (unsigned i = threadIdx.x; i < kWarps * 256; i += kThreads) (&s_cnt[0][0])[i] = 0;
-  for (unsigned d = threadIdx.x; d < 256; d += kThreads)
-    s_glob[d] = hist[(unsigned long long)d * tiles + blockIdx.x];
+  if (threadIdx.x == 0) s_tile = atomicAdd(tile_counter, 1u);
   __syncthreads();
-  const unsigned long long base = (unsigned long long)blockIdx.x * kSortTile + w * kWarpSpan;
+  const unsigned tile = s_tile;
+  const unsigned long long base = (unsigned long long)tile * kSortTile + w * kWarpSpan;
   const unsigned lt = (1u << lane) - 1u;
   KeyT k[kItems];
   unsigned v[kItems], rank[kItems];
@@ -99,6 +88,7 @@ __global__ void __launch_bounds__(kThreads) downsweep(const KeyT* kin, const uns
     k[r] = valid ? kin[idx] : KeyT(0);
     v[r] = valid ? vin[idx] : 0u;
   }
+  // stable rank of every item among the warp's items with the same digit
 #pragma unroll
   for (int r = 0; r < kItems; ++r) {
     const unsigned long long idx = base + r * 32 + lane;
@@ -110,23 +100,63 @@ __global__ void __launch_bounds__(kThreads) downsweep(const KeyT* kin, const uns
     __syncwarp();
     if (valid) {
       rank[r] = prior + __popc(peers & lt);
-      if (lane == (unsigned)(__ffs(peers) - 1)) s_cnt[w][d] = prior + __popc(peers);
+      if ((peers & lt) == 0) s_cnt[w][d] = prior + __popc(peers);
     }
     __syncwarp();
   }
   __syncthreads();
-  if (threadIdx.x < 256) {
-    unsigned run = 0;
+  // per-digit: exclusive prefix over warps, tile total, look-back over tiles
+  const unsigned d = threadIdx.x;          // kThreads == 256 digits
+  unsigned total = 0;
 #pragma unroll
-    for (int x = 0; x < kWarps; ++x) { const unsigned c = s_cnt[x][threadIdx.x]; s_cnt[x][threadIdx.x] = run; run += c; }
+  for (int x = 0; x < kWarps; ++x) { const unsigned c = s_cnt[x][d]; s_cnt[x][d] = total; total += c; }
+  unsigned long long* mine = status + (unsigned long long)tile * 256 + d;
+  if (tile == 0) {
+    __stcg(mine, kFlagPrefix | total);
+  } else {
+    __stcg(mine, kFlagAggregate | total);
   }
+  // exclusive digit base over all digits (global histogram of this pass)
+  const unsigned hcount = hist[d];
+  unsigned x = hcount;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= (unsigned)o) x += y;
+  }
+  if (lane == 31) s_warp_sum[w] = x;
+  __syncthreads();
+  unsigned before = 0;
+  for (unsigned q = 0; q < w; ++q) before += s_warp_sum[q];
+  unsigned digit_base = before + x - hcount;
+  unsigned prefix = 0;
+  if (tile > 0) {
+    // decoupled look-back over earlier tiles of this digit
+    long long t = (long long)tile - 1;
+    unsigned spins = 0;
+    bool failed = false;
+    while (t >= 0) {
+      const unsigned long long s = __ldcg(status + (unsigned long long)t * 256 + d);
+      if ((s >> 32) == 0) {
+        if (++spins > kSpinLimit) { failed = true; break; }
+        __nanosleep(64);
+        continue;
+      }
+      prefix += (unsigned)s;
+      if ((s >> 32) == 2) break;
+      --t;
+    }
+    if (failed) atomicOr(error, kLookupSortFailed);
+    __stcg(mine, kFlagPrefix | (prefix + total));
+  }
+  s_base[d] = digit_base + prefix;
   __syncthreads();
 #pragma unroll
   for (int r = 0; r < kItems; ++r) {
     const unsigned long long idx = base + r * 32 + lane;
     if (idx < n) {
-      const unsigned d = (unsigned)(k[r] >> shift) & 255u;
-      const unsigned long long pos = (unsigned long long)s_glob[d] + s_cnt[w][d] + rank[r];
+      const unsigned dd = (unsigned)(k[r] >> shift) & 255u;
+      const unsigned long long pos = (unsigned long long)s_base[dd] + s_cnt[w][dd] + rank[r];
       kout[pos] = k[r];
       vout[pos] = v[r];
     }
@@ -142,12 +172,19 @@ cudaError_t run_sort(const SortLaunch& p, cudaStream_t s, int* swapped) {
   *swapped = 0;
   if (p.n <= 1) return cudaSuccess;
   const unsigned passes = (p.bits + 7) / 8;
+  // scratch: hist[passes][256] | counters[passes] | status[passes][tiles][256]
+  unsigned* hist = p.scratch;
+  unsigned* counters = hist + passes * 256;
+  unsigned long long* status = reinterpret_cast<unsigned long long*>(
+      reinterpret_cast<char*>(p.scratch) + sort_scratch_header(passes));
+  cudaError_t e = cudaMemsetAsync(p.scratch, 0, sort_scratch_bytes(p.n, p.bits), s);
+  if (e != cudaSuccess) return e;
+  const unsigned long long hist_grid = min(148ull * 4, (p.n + kThreads - 1) / kThreads);
+  digit_histograms<KeyT><<<(unsigned)hist_grid, kThreads, 0, s>>>(k0, p.n, passes, hist);
   for (unsigned pass = 0; pass < passes; ++pass) {
-    const unsigned shift = pass * 8;
-    upsweep<KeyT><<<p.tiles, kThreads, 0, s>>>(k0, p.n, shift, p.tile_hist, p.tiles);
-    scan_counts<<<1, 1024, 0, s>>>(p.tile_hist, 256u * p.tiles);
-    downsweep<KeyT><<<p.tiles, kThreads, 0, s>>>(k0, v0, k1, v1, p.n, shift, p.tile_hist,
-                                                 p.tiles);
+    onesweep_pass<KeyT><<<p.tiles, kThreads, 0, s>>>(
+        k0, v0, k1, v1, p.n, pass * 8, hist + pass * 256,
+        status + (unsigned long long)pass * p.tiles * 256, counters + pass, p.error);
     KeyT* tk = k0; k0 = k1; k1 = tk;
     unsigned* tv = v0; v0 = v1; v1 = tv;
     *swapped ^= 1;
@@ -160,8 +197,18 @@ unsigned int sort_tiles(unsigned long long n) {
   return (unsigned)((n + kSortTile - 1) / kSortTile);
 }
 
+size_t sort_scratch_header(unsigned passes) {
+  return ((size_t)passes * 257 * sizeof(unsigned) + 255) & ~size_t(255);
+}
+
+size_t sort_scratch_bytes(unsigned long long n, unsigned bits) {
+  const unsigned passes = (bits + 7) / 8;
+  return sort_scratch_header(passes) +
+         (size_t)passes * sort_tiles(n) * 256 * sizeof(unsigned long long);
+}
+
 unsigned int sort_launch_count(const SortLaunch& p) {
-  return p.n <= 1 ? 0u : 3u * ((p.bits + 7) / 8);
+  return p.n <= 1 ? 0u : 1u + (p.bits + 7) / 8;
 }
 
 cudaError_t launch_sort(const SortLaunch& p, cudaStream_t stream, int* swapped) {
