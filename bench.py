@@ -153,7 +153,7 @@ class Clocks:
             os.close(fd)
             self.out = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", "-i", self.index, f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=self.out, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -181,7 +181,8 @@ class Clocks:
         reasons = sorted({n for r in rows for n, v in zip(names, r[4:8]) if v.lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(rows)}
+                "samples": len(rows),
+                "window": "warm-up start to the end of a 0.5 s untimed soak of the same rounds"}
 
 
 # --------------------------------------------------------------- reference arm
@@ -278,6 +279,8 @@ def run_b200(args):
         ticket = lookup(stream)
         push(ticket, stream, wait=False)
 
+    clocks = Clocks(local_rank)
+    clocks.start()
     for _ in range(args.warmup):
         flush.zero_()
         one_round()
@@ -285,8 +288,6 @@ def run_b200(args):
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
-    clocks = Clocks(local_rank)
-    clocks.start()
     store.profile(1)
     launches0 = store.stats()["kernel_launches"]
     events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -299,10 +300,17 @@ def run_b200(args):
         b.record(stream)
     torch.cuda.synchronize()
     store.synchronize()
+    prof = store.profile(0)
+    # the timed rounds last milliseconds, less than one nvidia-smi sample period:
+    # keep the same load running (untimed) for 0.5 s so the clock record covers it
+    t_soak = time.perf_counter()
+    while time.perf_counter() - t_soak < 0.5:
+        for _ in range(8):
+            one_round()
+        store.synchronize()
+    clk = clocks.stop()
     if dist:
         dist.barrier()
-    clk = clocks.stop()
-    prof = store.profile(0)
     launches = store.stats()["kernel_launches"] - launches0
     total_ms = sum(a.elapsed_time(b) for a, b in events)
     if dist:

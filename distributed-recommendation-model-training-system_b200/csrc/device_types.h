@@ -92,19 +92,20 @@ struct PushControl {
   unsigned int long_count;
   unsigned int blocks_done;
   unsigned int accepted;
-  unsigned int pad;
+  unsigned int piece_count;     // pieces reserved by long rows
 };
 
-// A long coalesced segment (more than kLongRun occurrences): it is reduced in
-// per-tile pieces and combined in tile order by the long-segment kernel.
+// A long coalesced row (more than kLongRun occurrences): its occurrences are
+// reduced in pieces of kPiece into part[piece_base ..] and combined in piece
+// order by the long-row kernel.
 struct LongRecord {
   unsigned long long key;       // composite (table rank, slot)
-  unsigned int first_tile;      // tile in which the segment starts
-  unsigned int first_slot;      // 0: piece stored in part0[first_tile], 1: in part1
+  unsigned int piece_base;
+  unsigned int npieces;
 };
 
-constexpr int kTile = 32;       // sorted occurrences per group tile
-constexpr int kLongRun = 64;    // segments longer than this are "long"
+constexpr int kLongRun = 64;    // rows with more occurrences than this are "long"
+constexpr int kPiece = 64;      // occurrences per piece of a long row
 constexpr unsigned int kMaxFeatures = 1024;
 constexpr unsigned int kRowBits = 22;   // gradient row bits in the source code
 

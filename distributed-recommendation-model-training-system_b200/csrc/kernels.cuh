@@ -139,6 +139,19 @@ unsigned int sort_tiles(unsigned long long n);
 size_t sort_scratch_header(unsigned passes);
 size_t sort_scratch_bytes(unsigned long long n, unsigned bits);
 
+// Segments (runs of equal keys) of the sorted occurrence keys.
+struct SegmentLaunch {
+  const void* keys;                // sorted KeyT[n]
+  unsigned long long n;
+  int key64;
+  unsigned int* seg_start;         // [n + 1]: run starts, then n
+  unsigned int* seg_total;         // number of runs U
+  unsigned int* scratch;           // segment_scratch_bytes(n)
+  unsigned int* error;
+};
+cudaError_t launch_segments(const SegmentLaunch& p, cudaStream_t stream);
+size_t segment_scratch_bytes(unsigned long long n);
+
 struct PushLaunch {
   const PushTable* tables;         // device, per table rank
   unsigned int table_count;
@@ -152,7 +165,11 @@ struct PushLaunch {
   int key64;
   unsigned long long grad_values;  // total gradient values over features
   const unsigned long long* grad_prefix;  // device: value prefix per feature
-  float* part0; float* part1;      // [tiles][dim_max] long-segment pieces
+  const unsigned int* seg_start;   // [U + 1] run starts of the sorted keys
+  const unsigned int* seg_total;   // U (device)
+  uint2* pieces;                   // [max_pieces] (start, count) of long-row pieces
+  unsigned int max_pieces;
+  float* part;                     // [max_pieces][dim_max] piece sums
   LongRecord* records;
   unsigned int dim_max;
   PushControl* control;

@@ -22,18 +22,19 @@
 //                           1e37) and the update is applied in ONE fused pass;
 //                   CHECKED otherwise: pass 0 validates exactly as the reference,
 //                           pass 1 applies only if nothing was rejected.
-//   2. segments pass 0, 3. long pass 0, 4. segments pass 1, 5. long pass 1,
-//   6. finalize  -- advances beta powers and the sequence iff accepted.
+//   2. rows pass 0, 3. pieces, 4. long pass 0, 5. rows pass 1, 6. long pass 1,
+//   7. finalize  -- advances beta powers and the sequence iff accepted.
 //
 // Coalescing layout: the occurrences are sorted stably by composite key
-// (table rank, slot).  A group of G lanes (G = D/4: one 128-bit access per lane
-// covers a row) owns the tile [32t, 32t+32) of sorted occurrences and fully
-// processes every segment that STARTS in its tile and has at most 64
-// occurrences: the row's state load is issued first, the gradient sum runs
-// serially in occurrence order (bit-exact with the reference) with up to 8
-// gradient rows in flight, and the Adam update of that row follows in the same
-// pass.  Longer (Zipf-head) segments are reduced per tile into part0/part1 and
-// combined in tile order by all groups of one CTA in the long-segment kernel
+// (table rank, slot) and the runs of equal keys are compacted into
+// seg_start[U + 1] at lookup time.  `push_rows` gives every coalesced row to a
+// group of G lanes (G = D/4: one 128-bit access per lane covers a row): for a
+// row with at most 64 occurrences the group issues the row's [w|m|v] loads,
+// sums the gradient references serially in occurrence order (bit-exact with the
+// reference) with up to 4 gradient rows in flight, and applies LazyAdam in the
+// same pass.  A longer (Zipf-head) row reserves ceil(len/64) contiguous piece
+// slots; `push_pieces` reduces the pieces in parallel and `push_long` combines
+// one row's pieces in piece order on one CTA and applies LazyAdam
 // (deterministic; within 1e-6 * sum|terms| of the reference's serial sum).
 #include <cooperative_groups.h>
 #include <cooperative_groups/reduce.h>
@@ -136,18 +137,17 @@ __global__ void __launch_bounds__(256) push_prescan(PushLaunch p, PushTable* tab
 }
 
 // ------------------------------------------------------ reduction helpers
-template <int G>
-__device__ __forceinline__ unsigned full_mask() { return G == 32 ? 0xffffffffu : ((1u << G) - 1u); }
-
-// Sum of gradient references [s0, s1) (all with the same key), serially in order,
-// by the G lanes of `grp` (each lane owns VEC*ITERS columns).
+// Sum of gradient references [s0, s1) (all with the same key), serially in
+// order, by the G lanes of `grp` (each lane owns VEC*ITERS columns).
 template <int G, int VEC, int ITERS, typename Grp>
-__device__ __forceinline__ void accumulate_global(const Grp& grp, const PushLaunch& p,
-                                                  unsigned long long s0, unsigned long long s1,
-                                                  unsigned D, float (&acc)[VEC * ITERS]) {
+__device__ __forceinline__ void reduce_range(const Grp& grp, const PushLaunch& p,
+                                             unsigned long long s0, unsigned long long s1,
+                                             unsigned D, float (&acc)[VEC * ITERS]) {
   constexpr int C = VEC * ITERS;
   constexpr int DEPTH = C <= 4 ? 4 : 2;
   const unsigned gl = grp.thread_rank();
+#pragma unroll
+  for (int k = 0; k < C; ++k) acc[k] = 0.0f;
   for (unsigned long long c0 = s0; c0 < s1; c0 += G) {
     const unsigned long long i = c0 + gl;
     unsigned long long gp = 0;
@@ -190,65 +190,6 @@ __device__ __forceinline__ void accumulate_global(const Grp& grp, const PushLaun
 #pragma unroll
         for (int k = 0; k < C; ++k) acc[k] = __fadd_rn(acc[k], __fmul_rn(x[u][k], s[u]));
       }
-    }
-  }
-}
-
-template <int G, int VEC, int ITERS, typename Grp>
-__device__ __forceinline__ void reduce_range(const Grp& grp, const PushLaunch& p,
-                                             unsigned long long s0, unsigned long long s1,
-                                             unsigned D, float (&acc)[VEC * ITERS]) {
-#pragma unroll
-  for (int k = 0; k < VEC * ITERS; ++k) acc[k] = 0.0f;
-  accumulate_global<G, VEC, ITERS>(grp, p, s0, s1, D, acc);
-}
-
-// Value held by lane (pos % G) in its register slot pos / G (pos uniform in the group).
-template <int PER, typename T, typename Grp>
-__device__ __forceinline__ T tile_value(const Grp& grp, const T (&arr)[PER], unsigned pos) {
-  constexpr unsigned G = Grp::num_threads();
-  const unsigned r = pos / G;
-  T v = arr[0];
-#pragma unroll
-  for (int i = 1; i < PER; ++i) if ((unsigned)i == r) v = arr[i];
-  return grp.shfl(v, pos % G);
-}
-
-// Accumulates the gradient rows of tile positions [lo, hi) in order, continuing acc.
-template <int G, int VEC, int ITERS, int PER, typename Grp>
-__device__ __forceinline__ void accumulate_tile(const Grp& grp, const unsigned long long (&gp)[PER],
-                                                const float (&sc)[PER], unsigned lo, unsigned hi,
-                                                unsigned D, float (&acc)[VEC * ITERS]) {
-  constexpr int C = VEC * ITERS;
-  constexpr int DEPTH = C <= 4 ? 4 : 2;
-  const unsigned gl = grp.thread_rank();
-  for (unsigned j0 = lo; j0 < hi; j0 += DEPTH) {
-    float x[DEPTH][C];
-    float s[DEPTH];
-#pragma unroll
-    for (int u = 0; u < DEPTH; ++u) {
-      const bool use = j0 + u < hi;
-      const unsigned pos = use ? j0 + u : lo;
-      const unsigned long long q = tile_value<PER>(grp, gp, pos);
-      s[u] = tile_value<PER>(grp, sc, pos);
-#pragma unroll
-      for (int it = 0; it < ITERS; ++it) {
-        const unsigned col = (it * G + gl) * VEC;
-        float t[VEC];
-        if (use && col < D) load_vec<VEC>(reinterpret_cast<const float*>(q) + col, t);
-        else {
-#pragma unroll
-          for (int v = 0; v < VEC; ++v) t[v] = 0.0f;
-        }
-#pragma unroll
-        for (int v = 0; v < VEC; ++v) x[u][it * VEC + v] = t[v];
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < DEPTH; ++u) {
-      if (j0 + u >= hi) break;
-#pragma unroll
-      for (int k = 0; k < C; ++k) acc[k] = __fadd_rn(acc[k], __fmul_rn(x[u][k], s[u]));
     }
   }
 }
@@ -315,55 +256,6 @@ __device__ __forceinline__ unsigned adam_row(unsigned gl, const PushTable& T, fl
   return bits;
 }
 
-// Run length of key K starting at q (keys sorted), capped at cap+1.
-template <int G, typename KeyT, typename Grp>
-__device__ __forceinline__ unsigned long long run_forward(const Grp& grp, const void* keys,
-                                                          unsigned long long n, unsigned long long q,
-                                                          KeyT K, unsigned long long cap) {
-  const unsigned gl = grp.thread_rank();
-  unsigned long long len = 0;
-  while (len <= cap) {
-    const unsigned long long i = q + len + gl;
-    const bool same = i < n && key_at<KeyT>(keys, i) == K;
-    const unsigned ball = grp.ballot(same);
-    if (ball != full_mask<G>()) return len + (unsigned long long)(__ffs(~ball) - 1);
-    len += G;
-  }
-  return len;
-}
-
-// Number of keys equal to K immediately before position b, capped at cap+1.
-template <int G, typename KeyT, typename Grp>
-__device__ __forceinline__ unsigned long long run_backward(const Grp& grp, const void* keys,
-                                                           unsigned long long b, KeyT K,
-                                                           unsigned long long cap) {
-  const unsigned gl = grp.thread_rank();
-  unsigned long long len = 0;
-  while (len <= cap) {
-    const bool in = b >= len + gl + 1;
-    const bool same = in && key_at<KeyT>(keys, b - len - gl - 1) == K;
-    const unsigned ball = grp.ballot(same);
-    if (ball != full_mask<G>()) return len + (unsigned long long)(__ffs(~ball) - 1);
-    len += G;
-  }
-  return len;
-}
-
-template <int G, int VEC, int ITERS>
-__device__ __forceinline__ void store_piece(unsigned gl, float* part, unsigned dim_max,
-                                            unsigned long long tile, unsigned D,
-                                            const float (&acc)[VEC * ITERS]) {
-#pragma unroll
-  for (int it = 0; it < ITERS; ++it) {
-    const unsigned col = (it * G + gl) * VEC;
-    if (col >= D) continue;
-    float t[VEC];
-#pragma unroll
-    for (int x = 0; x < VEC; ++x) t[x] = acc[it * VEC + x];
-    store_vec<VEC>(part + tile * dim_max + col, t);
-  }
-}
-
 // Flush a group's state-bound maximum for table tr (called by all G lanes).
 template <typename Grp>
 __device__ __forceinline__ void flush_absmax(const Grp& grp, const PushLaunch& p, int tr, unsigned mx) {
@@ -371,200 +263,96 @@ __device__ __forceinline__ void flush_absmax(const Grp& grp, const PushLaunch& p
   if (grp.thread_rank() == 0 && tr >= 0 && mx) atomicMax(&p.tables[tr].dtable->state_absmax_bits, mx);
 }
 
-// ----------------------------------------------------------------- segments
-// Shared-memory ring per group: RING slots of [w | m | v | first gradient row].
-template <int G, int VEC, int ITERS>
-struct SegShape {
-  static constexpr int C = VEC * ITERS;
-  static constexpr int DCOLS = G * VEC * ITERS;     // columns one group covers
-  static constexpr int RING = C <= 4 ? 4 : 2;
-  static constexpr int PER = kTile / G;             // tile positions per lane
-  static constexpr int GROUPS = 256 / G;
-  static constexpr size_t SMEM = (size_t)GROUPS * RING * 4 * DCOLS * sizeof(float);
-};
+template <typename KeyT>
+__device__ __forceinline__ KeyT slot_mask_of(unsigned slot_bits) {
+  return (slot_bits >= sizeof(KeyT) * 8) ? ~KeyT(0) : ((KeyT(1) << slot_bits) - 1);
+}
 
+// --------------------------------------------------------------------- rows
 template <int G, int VEC, int ITERS, typename KeyT>
-__global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? 3 : 1) push_segments(PushLaunch p, int pass) {
+__global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? 4 : 2) push_rows(PushLaunch p, int pass) {
   const Role R = role(p.control, pass);
   if (!R.run) return;
-  using S = SegShape<G, VEC, ITERS>;
-  constexpr int C = S::C, DC = S::DCOLS, RING = S::RING, PER = S::PER;
-  extern __shared__ float s_ring[];
+  constexpr int C = VEC * ITERS;
   const auto grp = cg::tiled_partition<G>(cg::this_thread_block());
   const unsigned gl = grp.thread_rank();
-  float* ring = s_ring + (threadIdx.x / G) * (RING * 4 * DC);
-  const unsigned long long n = p.n;
-  const unsigned long long tiles = (n + kTile - 1) / kTile;
+  const unsigned U = *(volatile const unsigned*)p.seg_total;
   const unsigned long long gid = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) / G;
   const unsigned long long ngroups = (gridDim.x * (unsigned long long)blockDim.x) / G;
-  const KeyT slot_mask = (p.slot_bits >= sizeof(KeyT) * 8) ? ~KeyT(0)
-                                                           : ((KeyT(1) << p.slot_bits) - 1);
+  const KeyT smask = slot_mask_of<KeyT>(p.slot_bits);
   const bool work = R.apply || R.validate;
   unsigned bits = 0;
   int cur_tr = -1;
   unsigned cur_max = 0;
-
-  for (unsigned long long t = gid; t < tiles; t += ngroups) {
-    const unsigned long long b = t * kTile;
-    const unsigned L = (unsigned)min((unsigned long long)kTile, n - b);   // valid positions
-    // ---- discovery: keys, segment heads, gradient sources of the whole tile
-    KeyT kp[PER];
-    unsigned heads = 0;
-    KeyT carry = (b > 0) ? key_at<KeyT>(p.keys, b - 1) : KeyT(0);
-#pragma unroll
-    for (int r = 0; r < PER; ++r) {
-      const unsigned j = r * G + gl;
-      const bool valid = j < L;
-      const KeyT k = valid ? key_at<KeyT>(p.keys, b + j) : KeyT(0);
-      KeyT prev = grp.shfl_up(k, 1);
-      if (gl == 0) prev = carry;
-      const bool head = valid && ((b + j == 0) || k != prev);
-      heads |= (unsigned)grp.ballot(head) << (r * G);
-      carry = grp.shfl(k, G - 1);
-      kp[r] = k;
-    }
-    unsigned long long gp[PER];
-    float sc[PER];
-#pragma unroll
-    for (int r = 0; r < PER; ++r) {
-      const unsigned j = r * G + gl;
-      gp[r] = 0;
-      sc[r] = 0.0f;
-      if (j < L) {
-        const unsigned src = __ldg(p.srcs + b + j);
-        const unsigned f = src >> kRowBits;
-        const unsigned row = src & ((1u << kRowBits) - 1u);
-        const PushFeature* F = p.features + f;
-        const unsigned Df = __ldg(&F->dim);
-        const float* g = reinterpret_cast<const float*>(__ldg(reinterpret_cast<const unsigned long long*>(&F->grad)));
-        gp[r] = reinterpret_cast<unsigned long long>(g + (unsigned long long)row * Df);
-        sc[r] = __ldg(p.row_scale + __ldg(&F->scale_base) + row);
-      }
-    }
-    const KeyT k_last = tile_value<PER>(grp, kp, L - 1);
-    const bool crosses = b + L < n && key_at<KeyT>(p.keys, b + L) == k_last;
-    const unsigned first_head = heads ? (unsigned)(__ffs(heads) - 1) : L;
-    // ---- a segment that started in an earlier tile
-    if (first_head > 0) {
-      const KeyT kb = tile_value<PER>(grp, kp, 0);
-      const unsigned long long back = run_backward<G, KeyT>(grp, p.keys, b, kb, p.long_run);
-      unsigned long long fwd = first_head;
-      if (first_head == L && crosses) fwd += run_forward<G, KeyT>(grp, p.keys, n, b + L, kb, p.long_run);
-      if (back + fwd > p.long_run && R.partials) {
-        const unsigned tr = (unsigned)(kb >> p.slot_bits);
-        if (tr < p.table_count) {
-          const unsigned D = p.tables[tr].dim;
-          float acc[C];
-#pragma unroll
-          for (int k = 0; k < C; ++k) acc[k] = 0.0f;
-          accumulate_tile<G, VEC, ITERS, PER>(grp, gp, sc, 0, first_head, D, acc);
-          store_piece<G, VEC, ITERS>(gl, p.part0, p.dim_max, t, D, acc);
-        }
-      }
-    }
-    // ---- the last segment starting in the tile may run on (and may be long)
-    unsigned short_mask = heads;
-    unsigned last_len = 0;
-    const int last_start = heads ? 31 - __clz(heads) : -1;
-    if (last_start >= 0) {
-      last_len = L - (unsigned)last_start;
-      unsigned long long tail = 0;
-      if (crosses) tail = run_forward<G, KeyT>(grp, p.keys, n, b + L, k_last, p.long_run);
-      if ((unsigned long long)last_len + tail > p.long_run) {
-        short_mask &= ~(1u << last_start);
-        if (R.partials) {
-          const unsigned tr = (unsigned)(k_last >> p.slot_bits);
-          if (tr < p.table_count) {
-            const unsigned D = p.tables[tr].dim;
-            float acc[C];
-#pragma unroll
-            for (int k = 0; k < C; ++k) acc[k] = 0.0f;
-            accumulate_tile<G, VEC, ITERS, PER>(grp, gp, sc, (unsigned)last_start, L, D, acc);
-            const unsigned which = last_start == 0 ? 0u : 1u;
-            store_piece<G, VEC, ITERS>(gl, which ? p.part1 : p.part0, p.dim_max, t, D, acc);
-            if (gl == 0) {
-              const unsigned at = atomicAdd(&p.control->long_count, 1u);
-              p.records[at] = LongRecord{(unsigned long long)k_last, (unsigned)t, which};
-            }
-          }
-        }
-      } else {
-        last_len = (unsigned)(last_len + tail);
-      }
-    }
-    if (!work || !short_mask) continue;
-    // ---- short segments: row state + first gradient row prefetched RING deep
-    unsigned issue = short_mask, proc = short_mask;
-    const int nseg = __popc(short_mask);
-    for (int j = 0; j < nseg + RING - 1; ++j) {
-      if (issue) {
-        const unsigned s0 = (unsigned)(__ffs(issue) - 1);
-        issue &= issue - 1;
-        const KeyT K = tile_value<PER>(grp, kp, s0);
-        const unsigned tr = (unsigned)(K >> p.slot_bits);
-        if (tr < p.table_count) {
-          const unsigned D = p.tables[tr].dim;
-          const float* row = p.tables[tr].state + (unsigned long long)(K & slot_mask) * 3ull * D;
-          const float* g0 = reinterpret_cast<const float*>(tile_value<PER>(grp, gp, s0));
-          float* slot = ring + (j % RING) * (4 * DC);
-#pragma unroll
-          for (int it = 0; it < ITERS; ++it) {
-            const unsigned col = (it * G + gl) * VEC;
-            if (col < D) {
-              cp_async_vec<VEC>(slot + col, row + col);
-              cp_async_vec<VEC>(slot + DC + col, row + D + col);
-              cp_async_vec<VEC>(slot + 2 * DC + col, row + 2 * D + col);
-              cp_async_vec<VEC>(slot + 3 * DC + col, g0 + col);
-            }
-          }
-        }
-      }
-      cp_async_commit();
-      if (j < RING - 1) continue;
-      const int jj = j - (RING - 1);
-      const unsigned s1 = (unsigned)(__ffs(proc) - 1);
-      proc &= proc - 1;
-      cp_async_wait<RING - 1>();
-      const KeyT K = tile_value<PER>(grp, kp, s1);
-      const unsigned tr = (unsigned)(K >> p.slot_bits);
-      if (tr >= p.table_count) continue;
-      const PushTable& T = p.tables[tr];
-      const unsigned D = T.dim;
-      // segment length: up to the next head, or last_len for the last one
-      const unsigned above = heads & ~((2u << s1) - 1u);
-      const unsigned len = above ? (unsigned)(__ffs(above) - 1) - s1 : last_len;
-      const unsigned in_tile = min(len, L - s1);
-      const float* slot = ring + (jj % RING) * (4 * DC);
-      float g[C], w[C], m[C], v[C];
-      const float s_first = tile_value<PER>(grp, sc, s1);
-#pragma unroll
-      for (int it = 0; it < ITERS; ++it) {
-        const unsigned col = (it * G + gl) * VEC;
-#pragma unroll
-        for (int x = 0; x < VEC; ++x) {
-          const int k = it * VEC + x;
-          const bool in = col + x < D;
-          w[k] = in ? slot[col + x] : 0.0f;
-          m[k] = in ? slot[DC + col + x] : 0.0f;
-          v[k] = in ? slot[2 * DC + col + x] : 0.0f;
-          // batch_access.cpp:118: 0 + first term
-          g[k] = __fadd_rn(0.0f, __fmul_rn(in ? slot[3 * DC + col + x] : 0.0f, s_first));
-        }
-      }
-      if (in_tile > 1) accumulate_tile<G, VEC, ITERS, PER>(grp, gp, sc, s1 + 1, s1 + in_tile, D, g);
-      if (len > in_tile) accumulate_global<G, VEC, ITERS>(grp, p, b + L, b + s1 + len, D, g);
+  for (unsigned long long u = gid; u < U; u += ngroups) {
+    const unsigned s0 = __ldg(p.seg_start + u), s1 = __ldg(p.seg_start + u + 1);
+    const unsigned len = s1 - s0;
+    const KeyT K = key_at<KeyT>(p.keys, s0);
+    const unsigned tr = (unsigned)(K >> p.slot_bits);
+    if (tr >= p.table_count) continue;
+    const PushTable& T = p.tables[tr];
+    const unsigned D = T.dim;
+    const unsigned long long slot = (unsigned long long)(K & smask);
+    if (len <= p.long_run) {
+      if (!work) continue;
+      float* row = T.state + slot * 3ull * D;
+      float w[C], m[C], v[C], g[C];
+      load_state<G, VEC, ITERS>(gl, row, D, w, m, v);   // issued before the reduction
+      reduce_range<G, VEC, ITERS>(grp, p, s0, s1, D, g);
       if ((int)tr != cur_tr) {
         if (R.apply) flush_absmax(grp, p, cur_tr, cur_max);
         cur_tr = (int)tr; cur_max = 0;
       }
-      float* grow = T.state + (unsigned long long)(K & slot_mask) * 3ull * D;
-      bits |= adam_row<G, VEC, ITERS>(gl, T, grow, D, g, w, m, v, R.apply, R.validate, &cur_max);
-      if (R.apply && gl == 0) T.updates[(unsigned long long)(K & slot_mask)] += 1ull;
+      bits |= adam_row<G, VEC, ITERS>(gl, T, row, D, g, w, m, v, R.apply, R.validate, &cur_max);
+      if (R.apply && gl == 0) T.updates[slot] += 1ull;
+    } else if (R.partials) {
+      // a long row: reserve contiguous piece slots, remember the row
+      const unsigned np = (len + kPiece - 1) / kPiece;
+      unsigned base = 0;
+      if (gl == 0) {
+        base = atomicAdd(&p.control->piece_count, np);
+        const unsigned rec = atomicAdd(&p.control->long_count, 1u);
+        p.records[rec] = LongRecord{(unsigned long long)K, base, np};
+      }
+      base = grp.shfl(base, 0);
+      for (unsigned k = gl; k < np; k += G)
+        p.pieces[base + k] = make_uint2(s0 + k * kPiece, min((unsigned)kPiece, len - k * kPiece));
     }
   }
   bits = cg::reduce(grp, bits, cg::bit_or<unsigned>());
   if (gl == 0 && bits) atomicOr(&p.control->reject_bits, bits);
   if (R.apply) flush_absmax(grp, p, cur_tr, cur_max);
+}
+
+// ------------------------------------------------------------------- pieces
+template <int G, int VEC, int ITERS, typename KeyT>
+__global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? 4 : 2) push_pieces(PushLaunch p, int pass) {
+  const Role R = role(p.control, pass);
+  if (!R.run || !R.partials) return;
+  constexpr int C = VEC * ITERS;
+  const auto grp = cg::tiled_partition<G>(cg::this_thread_block());
+  const unsigned gl = grp.thread_rank();
+  const unsigned count = *(volatile const unsigned*)&p.control->piece_count;
+  const unsigned long long gid = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) / G;
+  const unsigned long long ngroups = (gridDim.x * (unsigned long long)blockDim.x) / G;
+  for (unsigned long long item = gid; item < count; item += ngroups) {
+    const uint2 pc = p.pieces[item];
+    const KeyT K = key_at<KeyT>(p.keys, pc.x);
+    const unsigned tr = (unsigned)(K >> p.slot_bits);
+    if (tr >= p.table_count) continue;
+    const unsigned D = p.tables[tr].dim;
+    float acc[C];
+    reduce_range<G, VEC, ITERS>(grp, p, pc.x, (unsigned long long)pc.x + pc.y, D, acc);
+#pragma unroll
+    for (int it = 0; it < ITERS; ++it) {
+      const unsigned col = (it * G + gl) * VEC;
+      if (col >= D) continue;
+      float t[VEC];
+#pragma unroll
+      for (int x = 0; x < VEC; ++x) t[x] = acc[it * VEC + x];
+      store_vec<VEC>(p.part + item * p.dim_max + col, t);
+    }
+  }
 }
 
 // ------------------------------------------------------------ long segments
@@ -581,10 +369,7 @@ __global__ void __launch_bounds__(kLongThreads) push_long(PushLaunch p, int pass
   const auto grp = cg::tiled_partition<G>(cg::this_thread_block());
   const unsigned gl = grp.thread_rank(), w = threadIdx.x / G;
   const unsigned count = *(volatile const unsigned*)&p.control->long_count;
-  const unsigned long long n = p.n;
-  const unsigned long long tiles = (n + kTile - 1) / kTile;
-  const KeyT slot_mask = (p.slot_bits >= sizeof(KeyT) * 8) ? ~KeyT(0)
-                                                           : ((KeyT(1) << p.slot_bits) - 1);
+  const KeyT smask = slot_mask_of<KeyT>(p.slot_bits);
   unsigned bits = 0;
   unsigned cur_max = 0;
   int cur_tr = -1;
@@ -592,36 +377,27 @@ __global__ void __launch_bounds__(kLongThreads) push_long(PushLaunch p, int pass
     const LongRecord L = p.records[rec];
     const KeyT K = (KeyT)L.key;
     const unsigned tr = (unsigned)(K >> p.slot_bits);
-    const unsigned long long slot = (unsigned long long)(K & slot_mask);
     if (tr >= p.table_count) continue;
     const PushTable& T = p.tables[tr];
     const unsigned D = T.dim;
-    // last tile whose first key is K (keys are sorted, so binary search)
-    unsigned long long lo = L.first_tile, hi = tiles;   // answer in [lo, hi)
-    while (hi - lo > 1) {
-      const unsigned long long mid = (lo + hi) >> 1;
-      if (key_at<KeyT>(p.keys, mid * kTile) == K) lo = mid; else hi = mid;
-    }
-    const unsigned long long pieces = lo - L.first_tile + 1;
+    const unsigned long long slot = (unsigned long long)(K & smask);
     // a contiguous chunk of pieces per group, combined afterwards in group order
-    const unsigned long long per = (pieces + NG - 1) / NG;
-    const unsigned long long p0 = min(pieces, per * w), p1 = min(pieces, p0 + per);
+    const unsigned per = (L.npieces + NG - 1) / NG;
+    const unsigned p0 = min(L.npieces, per * w), p1 = min(L.npieces, p0 + per);
     float acc[C];
 #pragma unroll
     for (int k = 0; k < C; ++k) acc[k] = 0.0f;
-    for (unsigned long long j0 = p0; j0 < p1; j0 += 4) {
+    for (unsigned j0 = p0; j0 < p1; j0 += 4) {
       float x[4][C];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const unsigned long long j = j0 + u;
-        const bool use = j < p1;
-        const float* src = (j == 0 && L.first_slot) ? p.part1 : p.part0;
-        const unsigned long long tile = L.first_tile + j;
+        const bool use = j0 + u < p1;
+        const unsigned long long item = (unsigned long long)L.piece_base + j0 + u;
 #pragma unroll
         for (int it = 0; it < ITERS; ++it) {
           const unsigned col = (it * G + gl) * VEC;
           float t[VEC];
-          if (use && col < D) load_vec<VEC>(src + tile * p.dim_max + col, t);
+          if (use && col < D) load_vec<VEC>(p.part + item * p.dim_max + col, t);
           else {
 #pragma unroll
             for (int v = 0; v < VEC; ++v) t[v] = 0.0f;
@@ -698,29 +474,20 @@ __global__ void push_finalize(PushLaunch p) {
 
 template <int G, int VEC, int ITERS, typename KeyT>
 cudaError_t run_apply(const PushLaunch& p, cudaStream_t s) {
-  using SS = SegShape<G, VEC, ITERS>;
-  // the shared-memory opt-in is a per-device attribute of the function
-  static bool configured[64] = {};
-  int device = 0;
-  cudaError_t e = cudaGetDevice(&device);
-  if (e != cudaSuccess) return e;
-  if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
-  if (!configured[device]) {
-    e = cudaFuncSetAttribute(push_segments<G, VEC, ITERS, KeyT>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SS::SMEM);
-    if (e != cudaSuccess) return e;
-    configured[device] = true;
-  }
-  const unsigned long long tiles = (p.n + kTile - 1) / kTile;
-  const unsigned long long want = (tiles + SS::GROUPS - 1) / SS::GROUPS;
-  const unsigned long long cap = 148ull * ((VEC * ITERS <= 4) ? 3 : 1);
-  const unsigned grid = (unsigned)max(1ull, min(want, cap));
+  if (!p.n) return cudaSuccess;
+  constexpr unsigned blocks_per_sm = (VEC * ITERS <= 4) ? 4 : 2;
+  constexpr unsigned long long groups_per_block = 256 / G;
+  const unsigned long long cap = 148ull * blocks_per_sm;
+  const unsigned rows_grid = (unsigned)max(1ull, min((p.n + groups_per_block - 1) / groups_per_block, cap));
+  const unsigned piece_grid =
+      (unsigned)max(1ull, min(((unsigned long long)p.max_pieces + groups_per_block - 1) / groups_per_block, cap));
   const size_t long_smem = (size_t)(kLongThreads / G) * p.dim_max * sizeof(float);
   const unsigned long_grid = 148 * 2;
-  for (int pass = 0; pass < 2; ++pass) {
-    if (p.n) push_segments<G, VEC, ITERS, KeyT><<<grid, 256, SS::SMEM, s>>>(p, pass);
-    if (p.n) push_long<G, VEC, ITERS, KeyT><<<long_grid, kLongThreads, long_smem, s>>>(p, pass);
-  }
+  push_rows<G, VEC, ITERS, KeyT><<<rows_grid, 256, 0, s>>>(p, 0);
+  push_pieces<G, VEC, ITERS, KeyT><<<piece_grid, 256, 0, s>>>(p, 0);
+  push_long<G, VEC, ITERS, KeyT><<<long_grid, kLongThreads, long_smem, s>>>(p, 0);
+  push_rows<G, VEC, ITERS, KeyT><<<rows_grid, 256, 0, s>>>(p, 1);
+  push_long<G, VEC, ITERS, KeyT><<<long_grid, kLongThreads, long_smem, s>>>(p, 1);
   return cudaGetLastError();
 }
 
@@ -740,7 +507,7 @@ cudaError_t launch_push_prescan(const PushLaunch& p, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
-unsigned launch_push_apply_count(const PushLaunch& p) { return p.n ? 4u : 0u; }
+unsigned launch_push_apply_count(const PushLaunch& p) { return p.n ? 5u : 0u; }
 
 cudaError_t launch_push_apply(const PushLaunch& p, cudaStream_t stream) {
   if (p.vec == 4) {

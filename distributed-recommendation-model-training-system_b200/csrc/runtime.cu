@@ -106,8 +106,11 @@ struct Ticket {
   void* keys = nullptr;
   unsigned* srcs = nullptr;
   float* row_scale = nullptr;
-  float* part0 = nullptr;
-  float* part1 = nullptr;
+  unsigned* seg_start = nullptr;
+  unsigned* seg_total = nullptr;
+  uint2* pieces = nullptr;
+  unsigned max_pieces = 0;
+  float* part = nullptr;
   LongRecord* records = nullptr;
   PushControl* control = nullptr;
   unsigned* lookup_error = nullptr;
@@ -585,9 +588,12 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
     }
     if (any_host_out) at_hostout = c.take<float>(host_out_values);
     const unsigned stiles = sort_tiles(total_keys);
-    const unsigned long long ptiles = (total_keys + kTile - 1) / kTile;
-    size_t at_k0 = 0, at_k1 = 0, at_s0 = 0, at_s1 = 0, at_scale = 0, at_hist = 0, at_p0 = 0,
-           at_p1 = 0, at_rec = 0, at_ctl = 0, at_ptab = 0, at_pfeat = 0, at_gpre = 0;
+    // long rows (> kLongRun occurrences) split into pieces of kPiece
+    const unsigned long long max_long = total_keys / (kLongRun + 1) + 1;
+    const unsigned long long max_pieces = (total_keys + kPiece - 1) / kPiece + max_long;
+    size_t at_k0 = 0, at_k1 = 0, at_s0 = 0, at_s1 = 0, at_scale = 0, at_hist = 0, at_seg = 0,
+           at_segtot = 0, at_segscr = 0, at_pieces = 0, at_part = 0, at_rec = 0, at_ctl = 0,
+           at_ptab = 0, at_pfeat = 0, at_gpre = 0;
     if (!read_only) {
       at_k0 = c.take<char>(total_keys * key_bytes);
       at_k1 = c.take<char>(total_keys * key_bytes);
@@ -595,9 +601,12 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       at_s1 = c.take<unsigned>(total_keys);
       at_scale = c.take<float>(total_rows);
       at_hist = c.take<char>(sort_scratch_bytes(total_keys, slot_bits + table_bits));
-      at_p0 = c.take<float>(ptiles * dim_max);
-      at_p1 = c.take<float>(ptiles * dim_max);
-      at_rec = c.take<LongRecord>(std::max(1ull, ptiles));
+      at_seg = c.take<unsigned>(total_keys + 1);
+      at_segtot = c.take<unsigned>(1);
+      at_segscr = c.take<char>(segment_scratch_bytes(total_keys));
+      at_pieces = c.take<uint2>(max_pieces);
+      at_part = c.take<float>(max_pieces * dim_max);
+      at_rec = c.take<LongRecord>(max_long);
       at_ctl = c.take<PushControl>(1);
       at_ptab = c.take<PushTable>(ranks.size());
       at_pfeat = c.take<PushFeature>(count);
@@ -705,7 +714,12 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         int swapped = 0;
         ev = s.Begin(stream);
         Cuda(launch_sort(sp, stream, &swapped));
-        s.End(EPS_B200_PHASE_SORT, ev, stream, sort_launch_count(sp));
+        SegmentLaunch gl{swapped ? P(at_k1) : P(at_k0), total_keys, key64,
+                         reinterpret_cast<unsigned*>(P(at_seg)),
+                         reinterpret_cast<unsigned*>(P(at_segtot)),
+                         reinterpret_cast<unsigned*>(P(at_segscr)), err};
+        Cuda(launch_segments(gl, stream));
+        s.End(EPS_B200_PHASE_SORT, ev, stream, sort_launch_count(sp) + (total_keys ? 1u : 0u));
         t.keys = swapped ? P(at_k1) : P(at_k0);
         t.srcs = reinterpret_cast<unsigned*>(swapped ? P(at_s1) : P(at_s0));
         t.n = total_keys;
@@ -713,8 +727,11 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         t.key64 = key64;
         t.dim_max = dim_max;
         t.row_scale = reinterpret_cast<float*>(P(at_scale));
-        t.part0 = reinterpret_cast<float*>(P(at_p0));
-        t.part1 = reinterpret_cast<float*>(P(at_p1));
+        t.seg_start = reinterpret_cast<unsigned*>(P(at_seg));
+        t.seg_total = reinterpret_cast<unsigned*>(P(at_segtot));
+        t.pieces = reinterpret_cast<uint2*>(P(at_pieces));
+        t.max_pieces = (unsigned)max_pieces;
+        t.part = reinterpret_cast<float*>(P(at_part));
         t.records = reinterpret_cast<LongRecord*>(P(at_rec));
         t.control = reinterpret_cast<PushControl*>(P(at_ctl));
         t.lookup_error = err;
@@ -973,8 +990,11 @@ int eps_b200_push(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gra
       pl.key64 = t.key64;
       pl.grad_values = total_values;
       pl.grad_prefix = t.grad_prefix;
-      pl.part0 = t.part0;
-      pl.part1 = t.part1;
+      pl.seg_start = t.seg_start;
+      pl.seg_total = t.seg_total;
+      pl.pieces = t.pieces;
+      pl.max_pieces = t.max_pieces;
+      pl.part = t.part;
       pl.records = t.records;
       pl.dim_max = t.dim_max;
       pl.control = t.control;

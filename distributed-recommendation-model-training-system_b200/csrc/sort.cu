@@ -40,23 +40,103 @@ __global__ void __launch_bounds__(kThreads) digit_histograms(const KeyT* keys, u
   __shared__ unsigned s_hist[8][256];
   for (unsigned i = threadIdx.x; i < 8 * 256; i += kThreads) (&s_hist[0][0])[i] = 0;
   __syncthreads();
-  const unsigned lane = threadIdx.x & 31;
-  const unsigned lt = (1u << lane) - 1u;
-  for (unsigned long long base = blockIdx.x * (unsigned long long)kThreads; base < n;
-       base += (unsigned long long)gridDim.x * kThreads) {
-    const unsigned long long i = base + threadIdx.x;
-    const bool valid = i < n;
-    const KeyT k = valid ? keys[i] : KeyT(0);
-    for (unsigned p = 0; p < passes; ++p) {
-      const unsigned d = valid ? ((unsigned)(k >> (8 * p)) & 255u) : 256u;
-      const unsigned peers = __match_any_sync(0xffffffffu, d);   // warp-aggregated
-      if (valid && (peers & lt) == 0) atomicAdd(&s_hist[p][d], __popc(peers));
-    }
+  for (unsigned long long i = blockIdx.x * (unsigned long long)kThreads + threadIdx.x; i < n;
+       i += (unsigned long long)gridDim.x * kThreads) {
+    const KeyT k = keys[i];
+    for (unsigned p = 0; p < passes; ++p) atomicAdd(&s_hist[p][(unsigned)(k >> (8 * p)) & 255u], 1u);
   }
   __syncthreads();
   for (unsigned i = threadIdx.x; i < passes * 256; i += kThreads) {
     const unsigned c = (&s_hist[0][0])[i];
     if (c) atomicAdd(hist + i, c);
+  }
+}
+
+// Order-preserving compaction of segment heads of the sorted keys:
+// seg_start[u] = position of the u-th run of equal keys, seg_start[U] = n,
+// *seg_total = U.  Tiles of 4096 positions (16 consecutive per thread), taken
+// in launch order; a warp-wide look-back reads 32 predecessors per step.
+template <typename KeyT>
+__global__ void __launch_bounds__(kThreads) segment_heads(const KeyT* keys, unsigned long long n,
+                                                          unsigned* seg_start, unsigned* seg_total,
+                                                          unsigned long long* status,
+                                                          unsigned* tile_counter, unsigned* error) {
+  __shared__ unsigned s_tile, s_warp[kWarps], s_prefix;
+  const unsigned w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) s_tile = atomicAdd(tile_counter, 1u);
+  __syncthreads();
+  const unsigned tile = s_tile;
+  const unsigned long long base = (unsigned long long)tile * kSortTile + threadIdx.x * kItems;
+  unsigned flags = 0;
+  if (base < n) {
+    KeyT prev = base > 0 ? keys[base - 1] : KeyT(0);
+#pragma unroll
+    for (int j = 0; j < kItems; ++j) {
+      const unsigned long long i = base + j;
+      if (i < n) {
+        const KeyT k = keys[i];
+        if (i == 0 || k != prev) flags |= 1u << j;
+        prev = k;
+      }
+    }
+  }
+  const unsigned cnt = __popc(flags);
+  unsigned x = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= (unsigned)o) x += y;
+  }
+  if (lane == 31) s_warp[w] = x;
+  __syncthreads();
+  unsigned before = 0, total = 0;
+#pragma unroll
+  for (int q = 0; q < kWarps; ++q) { if ((unsigned)q < w) before += s_warp[q]; total += s_warp[q]; }
+  const unsigned excl = before + x - cnt;
+  unsigned long long* mine = status + tile;
+  if (w == 0) {
+    unsigned prefix = 0;
+    if (tile == 0) {
+      if (lane == 0) __stcg(mine, kFlagPrefix | total);
+    } else {
+      if (lane == 0) __stcg(mine, kFlagAggregate | total);
+      long long t = (long long)tile - 1;
+      unsigned spins = 0;
+      bool failed = false;
+      while (t >= 0) {
+        const long long tt = t - lane;
+        const unsigned long long s = tt >= 0 ? __ldcg(status + tt) : kFlagPrefix;
+        const unsigned flag = (unsigned)(s >> 32);
+        const unsigned pref = __ballot_sync(0xffffffffu, flag == 2);
+        const unsigned waiting = __ballot_sync(0xffffffffu, flag == 0);
+        const int pl = pref ? __ffs(pref) - 1 : 32;
+        const unsigned upto = pl >= 31 ? 0xffffffffu : ((2u << pl) - 1u);
+        if (waiting & upto) {
+          if (++spins > kSpinLimit) { failed = true; break; }
+          __nanosleep(64);
+          continue;
+        }
+        prefix += __reduce_add_sync(0xffffffffu, (unsigned)lane <= (unsigned)pl ? (unsigned)s : 0u);
+        if (pl < 32) break;
+        t -= 32;
+      }
+      if (failed && lane == 0) atomicOr(error, kLookupSortFailed);
+      if (lane == 0) __stcg(mine, kFlagPrefix | (prefix + total));
+    }
+    if (lane == 0) s_prefix = prefix;
+  }
+  __syncthreads();
+  unsigned r = s_prefix + excl;
+  while (flags) {
+    const int j = __ffs(flags) - 1;
+    flags &= flags - 1;
+    seg_start[r++] = (unsigned)(base + j);
+  }
+  const unsigned long long tiles = (n + kSortTile - 1) / kSortTile;
+  if (tile == tiles - 1 && threadIdx.x == 0) {
+    const unsigned U = s_prefix + total;
+    seg_start[U] = (unsigned)n;
+    *seg_total = U;
   }
 }
 
@@ -131,20 +211,34 @@ __global__ void __launch_bounds__(kThreads) onesweep_pass(const KeyT* kin, const
   unsigned digit_base = before + x - hcount;
   unsigned prefix = 0;
   if (tile > 0) {
-    // decoupled look-back over earlier tiles of this digit
+    // decoupled look-back over earlier tiles of this digit, 8 predecessors per
+    // step loaded together
+    constexpr int W = 8;
     long long t = (long long)tile - 1;
     unsigned spins = 0;
     bool failed = false;
     while (t >= 0) {
-      const unsigned long long s = __ldcg(status + (unsigned long long)t * 256 + d);
-      if ((s >> 32) == 0) {
+      unsigned long long sw[W];
+#pragma unroll
+      for (int j = 0; j < W; ++j)
+        sw[j] = (t - j >= 0) ? __ldcg(status + (unsigned long long)(t - j) * 256 + d) : (kFlagPrefix);
+      int used = 0;
+      bool done = false, not_ready = false;
+#pragma unroll
+      for (int j = 0; j < W; ++j) {
+        if (done || not_ready) continue;
+        const unsigned flag = (unsigned)(sw[j] >> 32);
+        if (flag == 0) { not_ready = true; continue; }
+        prefix += (unsigned)sw[j];
+        ++used;
+        if (flag == 2) done = true;
+      }
+      if (done) break;
+      t -= used;
+      if (not_ready) {
         if (++spins > kSpinLimit) { failed = true; break; }
         __nanosleep(64);
-        continue;
       }
-      prefix += (unsigned)s;
-      if ((s >> 32) == 2) break;
-      --t;
     }
     if (failed) atomicOr(error, kLookupSortFailed);
     __stcg(mine, kFlagPrefix | (prefix + total));
@@ -179,7 +273,7 @@ cudaError_t run_sort(const SortLaunch& p, cudaStream_t s, int* swapped) {
       reinterpret_cast<char*>(p.scratch) + sort_scratch_header(passes));
   cudaError_t e = cudaMemsetAsync(p.scratch, 0, sort_scratch_bytes(p.n, p.bits), s);
   if (e != cudaSuccess) return e;
-  const unsigned long long hist_grid = min(148ull * 4, (p.n + kThreads - 1) / kThreads);
+  const unsigned long long hist_grid = min(148ull * 8, (p.n + kThreads - 1) / kThreads);
   digit_histograms<KeyT><<<(unsigned)hist_grid, kThreads, 0, s>>>(k0, p.n, passes, hist);
   for (unsigned pass = 0; pass < passes; ++pass) {
     onesweep_pass<KeyT><<<p.tiles, kThreads, 0, s>>>(
@@ -191,7 +285,32 @@ cudaError_t run_sort(const SortLaunch& p, cudaStream_t s, int* swapped) {
   }
   return cudaGetLastError();
 }
+
+template <typename KeyT>
+cudaError_t run_heads(const SegmentLaunch& p, cudaStream_t s) {
+  if (p.n == 0) {
+    return cudaMemsetAsync(p.seg_total, 0, sizeof(unsigned), s);
+  }
+  const unsigned tiles = (unsigned)((p.n + kSortTile - 1) / kSortTile);
+  cudaError_t e = cudaMemsetAsync(p.scratch, 0, segment_scratch_bytes(p.n), s);
+  if (e != cudaSuccess) return e;
+  unsigned* counter = p.scratch;
+  unsigned long long* status = reinterpret_cast<unsigned long long*>(
+      reinterpret_cast<char*>(p.scratch) + 256);
+  segment_heads<KeyT><<<tiles, kThreads, 0, s>>>(static_cast<const KeyT*>(p.keys), p.n,
+                                                 p.seg_start, p.seg_total, status, counter,
+                                                 p.error);
+  return cudaGetLastError();
+}
 }  // namespace
+
+size_t segment_scratch_bytes(unsigned long long n) {
+  return 256 + (size_t)((n + kSortTile - 1) / kSortTile) * sizeof(unsigned long long);
+}
+
+cudaError_t launch_segments(const SegmentLaunch& p, cudaStream_t stream) {
+  return p.key64 ? run_heads<unsigned long long>(p, stream) : run_heads<unsigned int>(p, stream);
+}
 
 unsigned int sort_tiles(unsigned long long n) {
   return (unsigned)((n + kSortTile - 1) / kSortTile);
