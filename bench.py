@@ -301,6 +301,7 @@ def run_b200(args):
     torch.cuda.synchronize()
     store.synchronize()
     prof = store.profile(0)
+    launches = store.stats()["kernel_launches"] - launches0
     # the timed rounds last milliseconds, less than one nvidia-smi sample period:
     # keep the same load running (untimed) for 0.5 s so the clock record covers it
     t_soak = time.perf_counter()
@@ -311,7 +312,6 @@ def run_b200(args):
     clk = clocks.stop()
     if dist:
         dist.barrier()
-    launches = store.stats()["kernel_launches"] - launches0
     total_ms = sum(a.elapsed_time(b) for a, b in events)
     if dist:
         t = torch.tensor([total_ms], dtype=torch.float64, device=dev)

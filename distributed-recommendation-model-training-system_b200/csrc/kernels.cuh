@@ -127,7 +127,7 @@ struct SortLaunch {
   unsigned long long n;
   unsigned int bits;
   int key64;
-  unsigned int* scratch;           // sort_scratch_bytes(n, bits), 256-byte aligned
+  unsigned int* scratch;           // sort_scratch_bytes(n, bits), 256-byte aligned, zeroed
   unsigned int tiles;              // sort_tiles(n)
   unsigned int* error;             // set (kLookupSortFailed) if a look-back wait ran out
 };
@@ -146,7 +146,7 @@ struct SegmentLaunch {
   int key64;
   unsigned int* seg_start;         // [n + 1]: run starts, then n
   unsigned int* seg_total;         // number of runs U
-  unsigned int* scratch;           // segment_scratch_bytes(n)
+  unsigned int* scratch;           // segment_scratch_bytes(n), zeroed
   unsigned int* error;
 };
 cudaError_t launch_segments(const SegmentLaunch& p, cudaStream_t stream);
@@ -164,6 +164,8 @@ struct PushLaunch {
   unsigned int slot_bits;
   int key64;
   unsigned long long grad_values;  // total gradient values over features
+  unsigned long long grad_max_values;  // largest feature's gradient values
+  int grad_vec4;                   // every gradient buffer 16-byte aligned, size % 4 == 0
   const unsigned long long* grad_prefix;  // device: value prefix per feature
   const unsigned int* seg_start;   // [U + 1] run starts of the sorted keys
   const unsigned int* seg_total;   // U (device)

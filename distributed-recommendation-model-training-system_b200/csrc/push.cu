@@ -70,30 +70,31 @@ __device__ __forceinline__ Role role(const PushControl* c, int pass) {
 }
 
 // ------------------------------------------------------------------ prescan
+// Grid (x, features): blocks of row y scan feature y's gradient values.
 __global__ void __launch_bounds__(256) push_prescan(PushLaunch p, PushTable* tables_rw) {
-  __shared__ unsigned long long s_prefix[kMaxFeatures + 1];
   __shared__ unsigned s_bad, s_max, s_last;
-  const unsigned fc = p.feature_count;
-  for (unsigned i = threadIdx.x; i <= fc; i += blockDim.x) s_prefix[i] = p.grad_prefix[i];
   if (threadIdx.x == 0) { s_bad = 0; s_max = 0; }
   __syncthreads();
-  const unsigned long long total = p.grad_values;
-  const unsigned long long per_block = (total + gridDim.x - 1) / gridDim.x;
-  const unsigned long long begin = min(total, per_block * blockIdx.x);
-  const unsigned long long end = min(total, begin + per_block);
+  const PushFeature& F = p.features[blockIdx.y];
+  const unsigned long long nvals = F.rows * (unsigned long long)F.dim;
+  const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
   unsigned bad = 0;
   float mx = 0.0f;
-  unsigned f = 0;
-  {  // feature containing `begin`
-    unsigned lo = 0, hi = fc;
-    while (hi - lo > 1) { const unsigned mid = (lo + hi) >> 1; if (s_prefix[mid] <= begin) lo = mid; else hi = mid; }
-    f = lo;
-  }
-  for (unsigned long long i = begin + threadIdx.x; i < end; i += blockDim.x) {
-    while (f + 1 < fc && s_prefix[f + 1] <= i) ++f;
-    const float x = __ldg(p.features[f].grad + (i - s_prefix[f]));
-    bad |= !isfinite(x);
-    mx = fmaxf(mx, fabsf(x));
+  if (p.grad_vec4) {
+    const float4* g4 = reinterpret_cast<const float4*>(F.grad);
+    const unsigned long long n4 = nvals / 4;
+#pragma unroll 4
+    for (unsigned long long i = blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x; i < n4; i += stride) {
+      const float4 x = __ldg(g4 + i);
+      bad |= !isfinite(x.x) | !isfinite(x.y) | !isfinite(x.z) | !isfinite(x.w);
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+    }
+  } else {
+    for (unsigned long long i = blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x; i < nvals; i += stride) {
+      const float x = __ldg(F.grad + i);
+      bad |= !isfinite(x);
+      mx = fmaxf(mx, fabsf(x));
+    }
   }
   bad = __reduce_or_sync(0xffffffffu, bad);
   unsigned mb = __reduce_max_sync(0xffffffffu, __float_as_uint(mx));
@@ -106,7 +107,7 @@ __global__ void __launch_bounds__(256) push_prescan(PushLaunch p, PushTable* tab
     if (s_bad) atomicOr(&p.control->nonfinite, 1u);
     atomicMax(&p.control->maxabs_bits, s_max);
     __threadfence();
-    s_last = atomicAdd(&p.control->blocks_done, 1u) == gridDim.x - 1;
+    s_last = atomicAdd(&p.control->blocks_done, 1u) == gridDim.x * gridDim.y - 1;
   }
   __syncthreads();
   if (!s_last || threadIdx.x != 0) return;
@@ -499,10 +500,11 @@ cudaError_t run_key(const PushLaunch& p, cudaStream_t s) {
 }  // namespace
 
 cudaError_t launch_push_prescan(const PushLaunch& p, cudaStream_t stream) {
-  // enough blocks to stream the gradients at full bandwidth
-  const unsigned long long per = 256ull * 16;
-  const unsigned long long want = (p.grad_values + per - 1) / per;
-  const unsigned grid = (unsigned)max(1ull, min(want, 148ull * 8));
+  // one grid row per feature; enough columns to stream the largest feature
+  const unsigned long long per = 256ull * (p.grad_vec4 ? 16 : 4);
+  const unsigned long long want = (p.grad_max_values + per - 1) / per;
+  const unsigned gx = (unsigned)max(1ull, min(want, 148ull * 4));
+  const dim3 grid(gx, max(1u, p.feature_count));
   push_prescan<<<grid, 256, 0, stream>>>(p, const_cast<PushTable*>(p.tables));
   return cudaGetLastError();
 }

@@ -82,11 +82,15 @@ struct Table {
   unsigned long long bytes = 0;
 };
 
-struct HostStatus {
-  PushControl control;
+// Per-ticket status block, laid out identically in the device slab and in the
+// pinned host mirror so that one copy transfers it: the lookup-error word (set
+// by the lookup / sort kernels) and the push control block.
+struct StatusBlock {
   unsigned lookup_error;
-  unsigned pad[7];
+  unsigned pad[63];
+  PushControl control;
 };
+using HostStatus = StatusBlock;
 
 struct Ticket {
   bool read_only = false;
@@ -114,9 +118,11 @@ struct Ticket {
   LongRecord* records = nullptr;
   PushControl* control = nullptr;
   unsigned* lookup_error = nullptr;
+  StatusBlock* status = nullptr;
   PushTable* push_tables = nullptr;
   PushFeature* push_features = nullptr;
   unsigned long long* grad_prefix = nullptr;
+  char* stage_end = nullptr;        // end of the span staged by a push
 };
 
 // Slab carve-out helper.
@@ -579,7 +585,6 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
     // ---- slab layout
     Carver c;
     const size_t at_desc = c.take<LookupFeature>(count);
-    const size_t at_err = c.take<unsigned>(8);
     size_t at_keys = 0, at_offsets = 0, at_lengths = 0, at_hostout = 0;
     if (!input_on_device) {
       at_keys = c.take<unsigned long long>(total_keys);
@@ -592,25 +597,33 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
     const unsigned long long max_long = total_keys / (kLongRun + 1) + 1;
     const unsigned long long max_pieces = (total_keys + kPiece - 1) / kPiece + max_long;
     size_t at_k0 = 0, at_k1 = 0, at_s0 = 0, at_s1 = 0, at_scale = 0, at_hist = 0, at_seg = 0,
-           at_segtot = 0, at_segscr = 0, at_pieces = 0, at_part = 0, at_rec = 0, at_ctl = 0,
-           at_ptab = 0, at_pfeat = 0, at_gpre = 0;
+           at_segtot = 0, at_segscr = 0, at_pieces = 0, at_part = 0, at_rec = 0,
+           at_ptab = 0, at_pfeat = 0, at_gpre = 0, at_end = 0;
+    size_t at_zero = 0;   // start of the region zeroed by the lookup's single memset
     if (!read_only) {
       at_k0 = c.take<char>(total_keys * key_bytes);
       at_k1 = c.take<char>(total_keys * key_bytes);
       at_s0 = c.take<unsigned>(total_keys);
       at_s1 = c.take<unsigned>(total_keys);
       at_scale = c.take<float>(total_rows);
-      at_hist = c.take<char>(sort_scratch_bytes(total_keys, slot_bits + table_bits));
       at_seg = c.take<unsigned>(total_keys + 1);
       at_segtot = c.take<unsigned>(1);
-      at_segscr = c.take<char>(segment_scratch_bytes(total_keys));
       at_pieces = c.take<uint2>(max_pieces);
       at_part = c.take<float>(max_pieces * dim_max);
       at_rec = c.take<LongRecord>(max_long);
-      at_ctl = c.take<PushControl>(1);
+      // [sort scratch | segment scratch | status] zeroed together
+      at_zero = at_hist = c.take<char>(sort_scratch_bytes(total_keys, slot_bits + table_bits));
+      at_segscr = c.take<char>(segment_scratch_bytes(total_keys));
+    }
+    const size_t at_status = c.take<StatusBlock>(1);
+    if (read_only) at_zero = at_status;
+    const size_t zero_bytes = c.offset - at_zero;
+    if (!read_only) {
+      // [status.control | push tables | push features | gradient prefix] staged by one copy
       at_ptab = c.take<PushTable>(ranks.size());
       at_pfeat = c.take<PushFeature>(count);
       at_gpre = c.take<unsigned long long>(count + 1);
+      at_end = c.offset;
     }
     cudaStream_t stream = s.Use(stream_arg);
     s.Poll(stream);
@@ -618,8 +631,9 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
     Cuda(cudaMallocAsync(reinterpret_cast<void**>(&slab), std::max<size_t>(c.offset, 256), stream));
     auto P = [&](size_t at) { return slab + at; };
     try {
-      unsigned* err = reinterpret_cast<unsigned*>(P(at_err));
-      Cuda(cudaMemsetAsync(err, 0, 8 * sizeof(unsigned), stream));
+      StatusBlock* status_block = reinterpret_cast<StatusBlock*>(P(at_status));
+      unsigned* err = &status_block->lookup_error;
+      Cuda(cudaMemsetAsync(P(at_zero), 0, zero_bytes, stream));
       // ---- descriptors (and staging of host inputs)
       std::vector<LookupFeature> desc(count);
       Ticket t;
@@ -733,11 +747,13 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         t.max_pieces = (unsigned)max_pieces;
         t.part = reinterpret_cast<float*>(P(at_part));
         t.records = reinterpret_cast<LongRecord*>(P(at_rec));
-        t.control = reinterpret_cast<PushControl*>(P(at_ctl));
+        t.status = status_block;
+        t.control = &status_block->control;
         t.lookup_error = err;
         t.push_tables = reinterpret_cast<PushTable*>(P(at_ptab));
         t.push_features = reinterpret_cast<PushFeature*>(P(at_pfeat));
         t.grad_prefix = reinterpret_cast<unsigned long long*>(P(at_gpre));
+        t.stage_end = P(at_end);
       }
       // ---- host outputs
       hoff = 0;
@@ -755,8 +771,9 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         slot = s.free_slots.back();
         s.free_slots.pop_back();
         std::memset(&s.host_status[slot], 0, sizeof(HostStatus));
-        Cuda(cudaMemcpyAsync(&s.host_status[slot].lookup_error, err, sizeof(unsigned),
-                             cudaMemcpyDeviceToHost, stream));
+        if (synchronous)
+          Cuda(cudaMemcpyAsync(&s.host_status[slot].lookup_error, err, sizeof(unsigned),
+                               cudaMemcpyDeviceToHost, stream));
       }
       unsigned sync_err = 0;
       if (synchronous) {
@@ -973,10 +990,19 @@ int eps_b200_push(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gra
         x.dim = d.dimension;
         x.lr_t = 0.0f;
       }
-      s.Stage(t.push_features, pf.data(), nf * sizeof(PushFeature), stream);
-      s.Stage(t.grad_prefix, prefix.data(), (nf + 1) * 8, stream);
-      s.Stage(t.push_tables, pt.data(), pt.size() * sizeof(PushTable), stream);
-      Cuda(cudaMemsetAsync(t.control, 0, sizeof(PushControl), stream));
+      {
+        // one host image of [control (zeroed) | tables | features | prefix]
+        char* first = reinterpret_cast<char*>(t.control);
+        const size_t span = t.stage_end - first;
+        std::vector<char> image(span, 0);
+        std::memcpy(image.data() + (reinterpret_cast<char*>(t.push_tables) - first), pt.data(),
+                    pt.size() * sizeof(PushTable));
+        std::memcpy(image.data() + (reinterpret_cast<char*>(t.push_features) - first), pf.data(),
+                    nf * sizeof(PushFeature));
+        std::memcpy(image.data() + (reinterpret_cast<char*>(t.grad_prefix) - first), prefix.data(),
+                    (nf + 1) * 8);
+        s.Stage(first, image.data(), span, stream);
+      }
       PushLaunch pl{};
       pl.tables = t.push_tables;
       pl.table_count = (unsigned)pt.size();
@@ -989,6 +1015,17 @@ int eps_b200_push(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gra
       pl.slot_bits = t.slot_bits;
       pl.key64 = t.key64;
       pl.grad_values = total_values;
+      {
+        unsigned long long mx = 0;
+        bool v4 = true;
+        for (size_t i = 0; i < nf; ++i) {
+          const unsigned long long nv = pf[i].rows * (unsigned long long)pf[i].dim;
+          mx = std::max(mx, nv);
+          v4 &= nv % 4 == 0 && (reinterpret_cast<uintptr_t>(pf[i].grad) & 15) == 0;
+        }
+        pl.grad_max_values = mx;
+        pl.grad_vec4 = v4 ? 1 : 0;
+      }
       pl.grad_prefix = t.grad_prefix;
       pl.seg_start = t.seg_start;
       pl.seg_total = t.seg_total;
@@ -1012,9 +1049,7 @@ int eps_b200_push(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gra
       ev = s.Begin(stream);
       Cuda(launch_push_finalize(pl, stream));
       s.End(EPS_B200_PHASE_FINALIZE, ev, stream, 1);
-      Cuda(cudaMemcpyAsync(&s.host_status[t.slot].control, t.control, sizeof(PushControl),
-                           cudaMemcpyDeviceToHost, stream));
-      Cuda(cudaMemcpyAsync(&s.host_status[t.slot].lookup_error, t.lookup_error, sizeof(unsigned),
+      Cuda(cudaMemcpyAsync(&s.host_status[t.slot], t.status, sizeof(StatusBlock),
                            cudaMemcpyDeviceToHost, stream));
       if (stage) { float* owned = stage; stage = nullptr; Cuda(cudaFreeAsync(owned, stream)); }
       t.done = s.SyncEvent();
@@ -1073,7 +1108,8 @@ int eps_b200_synchronize(EpsB200Store* store, EpsB200Status* status) {
         const std::string m = s.Resolve(it, stream);
         if (first.empty()) first = m;
       } else if (!it->second.lookup_checked) {
-        const unsigned e = s.host_status[it->second.slot].lookup_error;
+        unsigned e = 0;
+        Cuda(cudaMemcpy(&e, it->second.lookup_error, sizeof(unsigned), cudaMemcpyDeviceToHost));
         it->second.lookup_checked = true;
         if (e) {
           if (first.empty()) first = EpsB200Store::LookupMessage(e);

@@ -174,7 +174,13 @@ __global__ void __launch_bounds__(kThreads) onesweep_pass(const KeyT* kin, const
     const unsigned long long idx = base + r * 32 + lane;
     const bool valid = idx < n;
     const unsigned d = valid ? ((unsigned)(k[r] >> shift) & 255u) : 256u;
-    const unsigned peers = __match_any_sync(0xffffffffu, d);
+    // lanes with the same digit: intersect the 8 per-bit ballots
+    unsigned peers = __ballot_sync(0xffffffffu, valid);
+#pragma unroll
+    for (int bit = 0; bit < 8; ++bit) {
+      const unsigned on = __ballot_sync(0xffffffffu, (d >> bit) & 1u);
+      peers &= ((d >> bit) & 1u) ? on : ~on;
+    }
     unsigned prior = 0;
     if (valid) prior = s_cnt[w][d];
     __syncwarp();
@@ -271,8 +277,7 @@ cudaError_t run_sort(const SortLaunch& p, cudaStream_t s, int* swapped) {
   unsigned* counters = hist + passes * 256;
   unsigned long long* status = reinterpret_cast<unsigned long long*>(
       reinterpret_cast<char*>(p.scratch) + sort_scratch_header(passes));
-  cudaError_t e = cudaMemsetAsync(p.scratch, 0, sort_scratch_bytes(p.n, p.bits), s);
-  if (e != cudaSuccess) return e;
+  // the caller hands over zeroed scratch (sort_scratch_bytes)
   const unsigned long long hist_grid = min(148ull * 8, (p.n + kThreads - 1) / kThreads);
   digit_histograms<KeyT><<<(unsigned)hist_grid, kThreads, 0, s>>>(k0, p.n, passes, hist);
   for (unsigned pass = 0; pass < passes; ++pass) {
@@ -292,8 +297,7 @@ cudaError_t run_heads(const SegmentLaunch& p, cudaStream_t s) {
     return cudaMemsetAsync(p.seg_total, 0, sizeof(unsigned), s);
   }
   const unsigned tiles = (unsigned)((p.n + kSortTile - 1) / kSortTile);
-  cudaError_t e = cudaMemsetAsync(p.scratch, 0, segment_scratch_bytes(p.n), s);
-  if (e != cudaSuccess) return e;
+  // the caller hands over zeroed scratch (segment_scratch_bytes)
   unsigned* counter = p.scratch;
   unsigned long long* status = reinterpret_cast<unsigned long long*>(
       reinterpret_cast<char*>(p.scratch) + 256);
