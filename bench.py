@@ -288,7 +288,6 @@ def run_b200(args):
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
-    store.profile(1)
     launches0 = store.stats()["kernel_launches"]
     events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in range(args.steps)]
@@ -300,8 +299,16 @@ def run_b200(args):
         b.record(stream)
     torch.cuda.synchronize()
     store.synchronize()
-    prof = store.profile(0)
     launches = store.stats()["kernel_launches"] - launches0
+    # per-phase device time: the same rounds again with the library's phase events
+    # (kept out of the timed rounds above, whose stream they would otherwise join)
+    store.profile(1)
+    for _ in range(args.steps):
+        flush.zero_()
+        one_round()
+    torch.cuda.synchronize()
+    store.synchronize()
+    prof = store.profile(0)
     # the timed rounds last milliseconds, less than one nvidia-smi sample period:
     # keep the same load running (untimed) for 0.5 s so the clock record covers it
     t_soak = time.perf_counter()
