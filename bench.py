@@ -292,10 +292,13 @@ def run_b200(args):
     events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in range(args.steps)]
     torch.cuda.synchronize()
+    host_s = []
     for a, b in events:
         flush.zero_()
         a.record(stream)
+        h0 = time.perf_counter()
         one_round()
+        host_s.append(time.perf_counter() - h0)
         b.record(stream)
     torch.cuda.synchronize()
     store.synchronize()
@@ -413,6 +416,8 @@ def run_b200(args):
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,
+        "host_us_per_round": {"median": 1e6 * float(np.median(host_s)),
+                              "max": 1e6 * max(host_s)},
         "clocks": clk,
     }
     print(json.dumps(line))

@@ -66,8 +66,9 @@ __global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? 3 : 2) lookup_kernel
       bad |= gl == nb && b0 + nb == bag_count && ob != key_count;  // must end at N
       if (grp.any(bad)) {
         err |= kLookupBadOffsets;
-        ob = (gl <= nb) ? grp.shfl(ob, 0) : 0;                   // treat every bag as empty
-        ob = min(ob, key_count);
+        // treat every bag as empty (the shuffle runs on every lane of the group)
+        const unsigned long long first = grp.shfl(ob, 0);
+        ob = (gl <= nb) ? min(first, key_count) : 0;
       }
     }
     const float* state = F->state;

@@ -31,7 +31,7 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kWarpSpan = kSortTile / kWarps;      // 512 items per warp
 constexpr unsigned long long kFlagAggregate = 1ull << 32;
 constexpr unsigned long long kFlagPrefix = 2ull << 32;
-constexpr unsigned kSpinLimit = 1u << 26;
+constexpr unsigned kSpinLimit = 1u << 22;
 
 // Global digit histograms of all passes: hist[pass][256].
 template <typename KeyT>
