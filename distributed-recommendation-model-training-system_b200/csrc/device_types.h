@@ -52,7 +52,6 @@ struct LookupFeature {
   unsigned long long key_count;
   unsigned long long bag_count;
   unsigned long long bag_base;         // prefix of bags over features
-  unsigned long long item_base;        // prefix of work items (bag ranges) over features
   unsigned long long occ_base;         // first occurrence index in the ticket
   unsigned long long scale_base;       // first gradient-row index in row_scale
   unsigned int dim;

@@ -108,8 +108,6 @@ struct LookupLaunch {
   const LookupFeature* features;   // device array
   unsigned int feature_count;
   unsigned long long bag_total;
-  unsigned long long item_total;   // work items: ranges of bags_per_item consecutive bags
-  unsigned int bags_per_item;      // 1 .. group - 1
   unsigned int shard_count, shard_id;
   int client;                      // 1: merge + mean (DistributedClient), 0: shard partial
   int emit;                        // 1: write occurrences for a later Push

@@ -13,8 +13,11 @@
 //
 // Work decomposition: a group of G lanes (G = D/4 for D = 32/64/128, so a row
 // is read with one 128-bit load per lane) owns one bag at a time; a warp holds
-// 32/G bags.  The group fetches G keys with one coalesced load, broadcasts them
-// by shuffle and keeps up to 8 row loads in flight ahead of the dependent adds.
+// 32/G bags.  The group fetches G keys with one coalesced load (the next chunk's
+// keys are requested before the current chunk's rows), broadcasts the slots by
+// shuffle and issues up to DEPTH = min(G, 64/C) row loads back to back before the
+// dependent adds.  Rows past the end of a chunk are added as -0.0f, the additive
+// identity of round-to-nearest addition, so the add loop carries no predicates.
 // When the lookup will be pushed (non-read-only), the same pass writes the
 // occurrence list consumed by the coalescing sort: composite key (table rank,
 // slot) and gradient source (feature, row), plus the mean scale 1.0f/len of
@@ -29,12 +32,19 @@ namespace cg = cooperative_groups;
 namespace eps_b200 {
 namespace {
 
+#ifndef EPS_LOOKUP_DEPTH_REGS
+#define EPS_LOOKUP_DEPTH_REGS 64     // registers per lane for rows in flight
+#endif
+#ifndef EPS_LOOKUP_MIN_BLOCKS
+#define EPS_LOOKUP_MIN_BLOCKS 2
+#endif
+
 template <int G, int VEC, int ITERS, typename KeyT>
-__global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? 3 : 2) lookup_kernel(LookupLaunch p) {
-  __shared__ unsigned long long s_item_base[kMaxFeatures + 1];
+__global__ void __launch_bounds__(256, EPS_LOOKUP_MIN_BLOCKS) lookup_kernel(LookupLaunch p) {
+  __shared__ unsigned long long s_bag_base[kMaxFeatures + 1];
   const unsigned fc = p.feature_count;
-  for (unsigned i = threadIdx.x; i < fc; i += blockDim.x) s_item_base[i] = p.features[i].item_base;
-  if (threadIdx.x == 0) s_item_base[fc] = p.item_total;
+  for (unsigned i = threadIdx.x; i < fc; i += blockDim.x) s_bag_base[i] = p.features[i].bag_base;
+  if (threadIdx.x == 0) s_bag_base[fc] = p.bag_total;
   __syncthreads();
 
   const auto grp = cg::tiled_partition<G>(cg::this_thread_block());
@@ -42,167 +52,132 @@ __global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? 3 : 2) lookup_kernel
   const unsigned long long gid = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) / G;
   const unsigned long long ngroups = (gridDim.x * (unsigned long long)blockDim.x) / G;
   constexpr int C = VEC * ITERS;
-  constexpr int DEPTH = C <= 4 ? 8 : (C <= 8 ? 4 : 2);
+  constexpr int DEPTH = G < EPS_LOOKUP_DEPTH_REGS / C ? G : EPS_LOOKUP_DEPTH_REGS / C;
   unsigned int err = 0;
 
-  for (unsigned long long item = gid; item < p.item_total; item += ngroups) {
-    // feature owning the item: largest f with item_base[f] <= item
+  for (unsigned long long g = gid; g < p.bag_total; g += ngroups) {
+    // feature owning bag g: largest f with bag_base[f] <= g
     unsigned lo = 0, hi = fc;
-    while (hi - lo > 1) { const unsigned mid = (lo + hi) >> 1; if (s_item_base[mid] <= item) lo = mid; else hi = mid; }
+    while (hi - lo > 1) { const unsigned mid = (lo + hi) >> 1; if (s_bag_base[mid] <= g) lo = mid; else hi = mid; }
     const LookupFeature* F = p.features + lo;
-    const unsigned long long bag_count = F->bag_count;
-    const unsigned long long b0 = (item - s_item_base[lo]) * p.bags_per_item;
-    const unsigned nb = (unsigned)min((unsigned long long)p.bags_per_item, bag_count - b0);
+    const unsigned long long b = g - s_bag_base[lo];
     const unsigned long long key_count = F->key_count;
-    // offsets of bags b0 .. b0+nb in one load: lane j holds offsets[b0 + j]
-    unsigned long long ob = 0, lb = 0;
-    if (gl <= nb) ob = F->offsets[b0 + gl];
-    if (F->lengths && gl < nb) lb = F->lengths[b0 + gl];
-    {
-      const unsigned long long nxt = grp.shfl_down(ob, 1);
-      bool bad = gl < nb && nxt < ob;                              // decreasing
-      bad |= gl == nb && ob > key_count;                           // beyond the keys
-      bad |= gl == 0 && b0 == 0 && ob != 0;                        // must start at 0
-      bad |= gl == nb && b0 + nb == bag_count && ob != key_count;  // must end at N
-      if (grp.any(bad)) {
-        err |= kLookupBadOffsets;
-        // treat every bag as empty (the shuffle runs on every lane of the group)
-        const unsigned long long first = grp.shfl(ob, 0);
-        ob = (gl <= nb) ? min(first, key_count) : 0;
-      }
-    }
-    const float* state = F->state;
+    // offsets[b] and offsets[b + 1] by lanes 0 and 1
+    unsigned long long o = 0;
+    if (gl < 2) o = F->offsets[b + gl];
+    unsigned long long s = grp.shfl(o, 0), e = grp.shfl(o, 1);
+    if (b == 0 && s != 0) err |= kLookupBadOffsets;
+    if (b + 1 == F->bag_count && e != key_count) err |= kLookupBadOffsets;
+    if (s > e || e > key_count) { err |= kLookupBadOffsets; s = e = 0; }
+    const unsigned long long* const keys = F->keys;
+    const float* const state = F->state;
+    float* const out = F->out;
     const unsigned D = F->dim;
+    const unsigned long long rows = F->rows;
     const unsigned long long row_stride = 3ull * D;
     const bool sequence = F->pooling == 2;
-    const bool mean = F->pooling == 1;
-    float* const out = F->out;
-    const unsigned long long k_begin = grp.shfl(ob, 0);
-    const unsigned long long k_end = grp.shfl(ob, nb);
 
     float acc[C];
 #pragma unroll
     for (int k = 0; k < C; ++k) acc[k] = 0.0f;
-    unsigned j = 0;                                    // bag being accumulated (relative)
-    unsigned long long bag_end = grp.shfl(ob, 1);
 
-    // writes the pooled row of relative bag j (sum or mean) and its scale
-    auto finish_bag = [&](unsigned jb) {
-      const unsigned long long b = b0 + jb;
-      const unsigned long long s = grp.shfl(ob, jb), e = grp.shfl(ob, jb + 1);
-      unsigned long long len = e - s;
-      if (F->lengths) {
-        const unsigned long long given = grp.shfl(lb, jb);
-        if (given < len) err |= kLookupShortLength;
-        len = given;
-      }
-      if (!sequence) {
-        const float denom = (float)len;   // u64 -> float, round to nearest
-#pragma unroll
-        for (int it = 0; it < ITERS; ++it) {
-          const unsigned col = (it * G + gl) * VEC;
-          if (col >= D) continue;
-          float t[VEC];
-#pragma unroll
-          for (int v = 0; v < VEC; ++v) {
-            float x = acc[it * VEC + v];
-            if (p.client) {
-              x = __fadd_rn(0.0f, x);
-              if (mean && len) x = __fdiv_rn(x, denom);
-            }
-            t[v] = x;
-          }
-          store_vec<VEC>(out + b * D + col, t);
-        }
-        if (p.emit && gl == 0)
-          p.row_scale[F->scale_base + b] = (mean && len) ? __fdiv_rn(1.0f, denom) : 1.0f;
-      }
-#pragma unroll
-      for (int k = 0; k < C; ++k) acc[k] = 0.0f;
-    };
-    // bags that end before the first key (empty bags)
-    while (j < nb && bag_end <= k_begin) { finish_bag(j); ++j; bag_end = grp.shfl(ob, min(j + 1, nb)); }
-
-    for (unsigned long long c0 = k_begin; c0 < k_end; c0 += G) {
+    unsigned long long key = (s + gl < e) ? keys[s + gl] : 0ull;
+    for (unsigned long long c0 = s; c0 < e; c0 += G) {
       const unsigned long long i = c0 + gl;
-      unsigned slot = ~0u;                     // slots fit 32 bits: rows < 2^32 per shard
-      // bag of key i among this item's bags: largest q with offsets[b0 + q] <= i
-      // (fixed-step binary search, executed by every lane of the group)
-      unsigned long long bag = b0;
-      if (p.emit && !sequence) {
-        unsigned qlo = 0, qhi = nb;
-#pragma unroll
-        for (int step = 0; step < 5; ++step) {
-          const unsigned mid = (qlo + qhi + 1) >> 1;
-          const unsigned long long om = grp.shfl(ob, min(mid, nb));
-          if (qhi > qlo && om <= i) qlo = mid; else if (qhi > qlo) qhi = mid - 1;
-        }
-        bag = b0 + qlo;
-      }
-      if (i < k_end) {
-        const unsigned long long key = F->keys[i];
+      unsigned slot = ~0u;              // slots fit 32 bits: rows < 2^32 per shard
+      if (i < e) {
         unsigned long long sl, sh;
         if (p.shard_count == 1) { sl = key; sh = 0; }
         else { sl = key / p.shard_count; sh = key - sl * p.shard_count; }
-        if (sh == p.shard_id && sl < F->rows) slot = (unsigned)sl;
+        if (sh == p.shard_id && sl < rows) slot = (unsigned)sl;
         else err |= kLookupBadKey;
         if (p.emit) {
-          const unsigned long long o = F->occ_base + i;
+          const unsigned long long o2 = F->occ_base + i;
           const KeyT ck = (slot == ~0u) ? KeyT(0)
               : (KeyT(F->table_rank) << p.slot_bits) | KeyT(slot);
-          static_cast<KeyT*>(p.occ_key)[o] = ck;
-          p.occ_src[o] = (F->feature_index << kRowBits) | (unsigned)(sequence ? i : bag);
+          static_cast<KeyT*>(p.occ_key)[o2] = ck;
+          p.occ_src[o2] = (F->feature_index << kRowBits) | (unsigned)(sequence ? i : b);
           if (sequence) p.row_scale[F->scale_base + i] = 1.0f;
         }
       }
-      const int cnt = (int)min((unsigned long long)G, k_end - c0);
+      // next chunk's keys in flight while this chunk's rows load
+      if (i + G < e) key = keys[i + G];
+      const int cnt = (int)min((unsigned long long)G, e - c0);
+#pragma unroll 1
       for (int j0 = 0; j0 < cnt; j0 += DEPTH) {
         float r[DEPTH][C];
-        unsigned sl[DEPTH];
+        bool use[DEPTH];
 #pragma unroll
         for (int u = 0; u < DEPTH; ++u) {
-          sl[u] = grp.shfl(slot, (j0 + u) & (G - 1));
-          const bool use = (j0 + u < cnt) && sl[u] != ~0u;
+          const unsigned su = grp.shfl(slot, (j0 + u) & (G - 1));
+          use[u] = (j0 + u < cnt) && su != ~0u;
+          const float* row = state + (unsigned long long)su * row_stride;
 #pragma unroll
           for (int it = 0; it < ITERS; ++it) {
             const unsigned col = (it * G + gl) * VEC;
             float t[VEC];
-            if (use && col < D) load_vec<VEC>(state + (unsigned long long)sl[u] * row_stride + col, t);
+            if (use[u] && col < D) load_vec<VEC>(row + col, t);
             else {
 #pragma unroll
-              for (int v = 0; v < VEC; ++v) t[v] = 0.0f;
+              for (int v = 0; v < VEC; ++v) t[v] = -0.0f;
             }
 #pragma unroll
             for (int v = 0; v < VEC; ++v) r[u][it * VEC + v] = t[v];
           }
         }
+        if (sequence) {
+          // one output row per position: 0 + w (batch_access.cpp:74-76)
 #pragma unroll
-        for (int u = 0; u < DEPTH; ++u) {
-          if (j0 + u >= cnt) break;
-          const unsigned long long ki = c0 + j0 + u;
-          if (sl[u] != ~0u) {
-            if (sequence) {
-              // one output row per position: 0 + w (batch_access.cpp:74-76)
+          for (int u = 0; u < DEPTH; ++u) {
+            if (!use[u]) continue;
+            const unsigned long long pos = c0 + j0 + u;
 #pragma unroll
-              for (int it = 0; it < ITERS; ++it) {
-                const unsigned col = (it * G + gl) * VEC;
-                if (col >= D) continue;
-                float t[VEC];
+            for (int it = 0; it < ITERS; ++it) {
+              const unsigned col = (it * G + gl) * VEC;
+              if (col >= D) continue;
+              float t[VEC];
 #pragma unroll
-                for (int v = 0; v < VEC; ++v) t[v] = __fadd_rn(0.0f, r[u][it * VEC + v]);
-                store_vec<VEC>(out + ki * D + col, t);
-              }
-            } else {
-#pragma unroll
-              for (int k = 0; k < C; ++k) acc[k] = __fadd_rn(acc[k], r[u][k]);
+              for (int v = 0; v < VEC; ++v) t[v] = __fadd_rn(0.0f, r[u][it * VEC + v]);
+              store_vec<VEC>(out + pos * D + col, t);
             }
           }
-          // bags ending at this key (and empty bags right after it)
-          while (j < nb && bag_end <= ki + 1) { finish_bag(j); ++j; bag_end = grp.shfl(ob, min(j + 1, nb)); }
+        } else {
+          // position order; -0.0f padding leaves acc unchanged
+#pragma unroll
+          for (int u = 0; u < DEPTH; ++u)
+#pragma unroll
+            for (int k = 0; k < C; ++k) acc[k] = __fadd_rn(acc[k], r[u][k]);
         }
       }
     }
-    while (j < nb) { finish_bag(j); ++j; }
+    if (!sequence) {
+      unsigned long long len = e - s;
+      if (F->lengths) {
+        const unsigned long long given = F->lengths[b];
+        if (given < len) err |= kLookupShortLength;
+        len = given;
+      }
+      const bool mean = F->pooling == 1;
+      const float denom = (float)len;   // u64 -> float, round to nearest
+#pragma unroll
+      for (int it = 0; it < ITERS; ++it) {
+        const unsigned col = (it * G + gl) * VEC;
+        if (col >= D) continue;
+        float t[VEC];
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) {
+          float x = acc[it * VEC + v];
+          if (p.client) {
+            x = __fadd_rn(0.0f, x);
+            if (mean && len) x = __fdiv_rn(x, denom);
+          }
+          t[v] = x;
+        }
+        store_vec<VEC>(out + b * D + col, t);
+      }
+      if (p.emit && gl == 0)
+        p.row_scale[F->scale_base + b] = (mean && len) ? __fdiv_rn(1.0f, denom) : 1.0f;
+    }
   }
   err = cg::reduce(grp, err, cg::bit_or<unsigned>());
   if (err && gl == 0) atomicOr(p.error, err);
@@ -211,8 +186,8 @@ __global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? 3 : 2) lookup_kernel
 template <int G, int VEC, int ITERS>
 cudaError_t launch_key(const LookupLaunch& p, cudaStream_t s) {
   const unsigned long long groups_per_block = 256 / G;
-  const unsigned long long want = (p.item_total + groups_per_block - 1) / groups_per_block;
-  const unsigned long long cap = 148ull * ((VEC * ITERS <= 4) ? 3 : 2) * 8;
+  const unsigned long long want = (p.bag_total + groups_per_block - 1) / groups_per_block;
+  const unsigned long long cap = 148ull * EPS_LOOKUP_MIN_BLOCKS * 4;   // 4 waves
   const unsigned grid = (unsigned)(want < cap ? want : cap);
   if (p.key64) lookup_kernel<G, VEC, ITERS, unsigned long long><<<grid, 256, 0, s>>>(p);
   else lookup_kernel<G, VEC, ITERS, unsigned int><<<grid, 256, 0, s>>>(p);
@@ -221,7 +196,7 @@ cudaError_t launch_key(const LookupLaunch& p, cudaStream_t s) {
 }  // namespace
 
 cudaError_t launch_lookup(const LookupLaunch& p, cudaStream_t stream) {
-  if (p.item_total == 0) return cudaSuccess;
+  if (p.bag_total == 0) return cudaSuccess;
   if (p.vec == 4) {
     switch (p.group) {
       case 8: return launch_key<8, 4, 1>(p, stream);

@@ -582,10 +582,6 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
     const size_t key_bytes = key64 ? 8 : 4;
     int vec, group, iters;
     choose_vec(dims, out16, out8, &vec, &group, &iters);
-    // work items: ranges of consecutive bags holding ~128 keys, at most group-1 bags
-    const unsigned long long avg_len = bags ? std::max(1ull, total_keys / bags) : 1ull;
-    const unsigned bags_per_item =
-        (unsigned)std::max(1ull, std::min((unsigned long long)(group - 1), 128ull / avg_len));
 
     // ---- slab layout
     Carver c;
@@ -643,7 +639,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       std::vector<LookupFeature> desc(count);
       Ticket t;
       t.read_only = read_only != 0;
-      unsigned long long bag_base = 0, item_base = 0, occ_base = 0, scale_base = 0, koff = 0,
+      unsigned long long bag_base = 0, occ_base = 0, scale_base = 0, koff = 0,
                          ooff = 0, loff = 0, hoff = 0;
       t.table_ids.resize(ranks.size());
       t.table_occ.assign(ranks.size(), 0);
@@ -686,7 +682,6 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         L.key_count = f.key_count;
         L.bag_count = f.offset_count - 1;
         L.bag_base = bag_base;
-        L.item_base = item_base;
         L.occ_base = occ_base;
         L.scale_base = scale_base;
         L.dim = D;
@@ -694,7 +689,6 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         L.table_rank = ranks.at(f.table);
         L.feature_index = (unsigned)i;
         bag_base += L.bag_count;
-        item_base += (L.bag_count + bags_per_item - 1) / bags_per_item;
         occ_base += f.key_count;
         scale_base += rows;
         t.feature_ids.push_back(f.feature);
@@ -710,8 +704,6 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       lp.features = reinterpret_cast<const LookupFeature*>(P(at_desc));
       lp.feature_count = (unsigned)count;
       lp.bag_total = bag_base;
-      lp.item_total = item_base;
-      lp.bags_per_item = bags_per_item;
       lp.shard_count = s.opt.shard_count;
       lp.shard_id = s.opt.shard_id;
       lp.client = shard_partial ? 0 : 1;
@@ -868,8 +860,7 @@ int eps_b200_lookup_noalloc(EpsB200Store* store, const EpsB200Feature* features,
       L.key_count = f.key_count;
       L.bag_count = f.offset_count - 1;
       L.bag_base = bag_base;
-      L.item_base = bag_base;          // one bag per work item
-      L.occ_base = 0;
+        L.occ_base = 0;
       L.scale_base = 0;
       L.dim = D;
       L.pooling = f.pooling;
@@ -892,8 +883,6 @@ int eps_b200_lookup_noalloc(EpsB200Store* store, const EpsB200Feature* features,
     lp.features = table;
     lp.feature_count = (unsigned)count;
     lp.bag_total = bag_base;
-    lp.item_total = bag_base;
-    lp.bags_per_item = 1;
     lp.shard_count = 1;
     lp.shard_id = 0;
     lp.client = 1;
