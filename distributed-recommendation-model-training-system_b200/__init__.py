@@ -100,7 +100,9 @@ ENTRY_POINTS = ("eps_b200_abi_version", "eps_b200_create", "eps_b200_destroy",
                 "eps_b200_create_table", "eps_b200_lookup", "eps_b200_lookup_noalloc",
                 "eps_b200_push", "eps_b200_release",
                 "eps_b200_synchronize", "eps_b200_read_state", "eps_b200_load_state",
-                "eps_b200_optimizer_state", "eps_b200_profile", "eps_b200_stats")
+                "eps_b200_optimizer_state", "eps_b200_profile", "eps_b200_stats",
+                "eps_b200_route", "eps_b200_route_scatter", "eps_b200_route_merge",
+                "eps_b200_route_gather", "eps_b200_route_release")
 
 
 def load_library() -> C.CDLL:
@@ -132,6 +134,12 @@ def load_library() -> C.CDLL:
     lib.eps_b200_stats.argtypes = [vp, P(Stats), P(Status)]
     lib.eps_b200_profile.argtypes = [vp, C.c_int32, P(C.c_double), P(C.c_uint64), P(C.c_uint64),
                                      P(Status)]
+    lib.eps_b200_route.argtypes = [vp, P(Feature), C.c_uint64, C.c_uint32, vp, P(C.c_uint64), vp,
+                                   P(Status)]
+    lib.eps_b200_route_scatter.argtypes = [vp, C.c_uint64, vp, vp, P(Status)]
+    lib.eps_b200_route_merge.argtypes = [vp, C.c_uint64, vp, P(Buffer), vp, P(Status)]
+    lib.eps_b200_route_gather.argtypes = [vp, C.c_uint64, P(Buffer), vp, vp, vp, P(Status)]
+    lib.eps_b200_route_release.argtypes = [vp, C.c_uint64, P(Status)]
     for name in ENTRY_POINTS[1:]:
         if name != "eps_b200_destroy":
             getattr(lib, name).restype = C.c_int
@@ -443,6 +451,54 @@ class ParameterStore:
         st = Status()
         _check(self.lib.eps_b200_profile(self._h, mode, ms, la, ca, C.byref(st)), st)
         return {p: {"ms": ms[i], "launches": la[i], "calls": ca[i]} for i, p in enumerate(PHASES)}
+
+    # ---- client side of a multi-GPU round (see distributed.ShardedClient)
+    def dimension(self, table: int) -> int:
+        if table not in self._tables:
+            raise EpsError(INVALID_ARGUMENT, "unknown table")
+        return self._tables[table].dimension
+
+    def route(self, feats: Sequence[FeatureInput], shard_count: int, stream=None):
+        """Partitions device features by key % shard_count (eps_b200_route).
+        Returns (route id, counts[shard, feature, (keys, kept bags)])."""
+        arr, on_device, keep = self._features(feats)
+        if not on_device:
+            raise EpsError(INVALID_ARGUMENT, "a route needs device inputs")
+        counts = np.zeros((shard_count, len(feats), 2), np.uint64)
+        rid = C.c_uint64(0)
+        st = Status()
+        _check(self.lib.eps_b200_route(self._h, arr, len(feats), shard_count, _stream_ptr(stream),
+                                       C.byref(rid), _ptr(counts), C.byref(st)), st)
+        self._route_keep = getattr(self, "_route_keep", {})
+        self._route_keep[rid.value] = keep
+        return rid.value, counts
+
+    def route_scatter(self, route: int, payload, stream=None):
+        st = Status()
+        _check(self.lib.eps_b200_route_scatter(self._h, route, _ptr(payload), _stream_ptr(stream),
+                                               C.byref(st)), st)
+
+    def _buffers(self, tensors, rows_cols=None):
+        bufs = (Buffer * len(tensors))()
+        for i, t in enumerate(tensors):
+            bufs[i] = Buffer(i, 0, int(t.shape[0]), int(t.shape[1]), _ptr(t),
+                             self.device if _is_device(t) else -1, 0)
+        return bufs
+
+    def route_merge(self, route: int, partials, outputs, stream=None):
+        st = Status()
+        _check(self.lib.eps_b200_route_merge(self._h, route, _ptr(partials), self._buffers(outputs),
+                                             _stream_ptr(stream), C.byref(st)), st)
+
+    def route_gather(self, route: int, gradients, send, nonfinite=None, stream=None):
+        st = Status()
+        _check(self.lib.eps_b200_route_gather(self._h, route, self._buffers(gradients), _ptr(send),
+                                              _ptr(nonfinite), _stream_ptr(stream), C.byref(st)), st)
+
+    def route_release(self, route: int):
+        st = Status()
+        _check(self.lib.eps_b200_route_release(self._h, route, C.byref(st)), st)
+        getattr(self, "_route_keep", {}).pop(route, None)
 
     def stats(self) -> dict:
         s = Stats()

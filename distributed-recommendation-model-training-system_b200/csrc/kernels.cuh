@@ -121,6 +121,43 @@ struct LookupLaunch {
 };
 cudaError_t launch_lookup(const LookupLaunch& p, cudaStream_t stream);
 
+// Shard partition of a lookup (multi-GPU round) and the client-side merge.
+struct RouteLaunch {
+  const LookupFeature* features;   // requester features; `rows` holds the table's key space
+  unsigned int feature_count;
+  unsigned int shard_count;        // 1 .. 32
+  unsigned long long bag_total;    // B
+  unsigned long long key_total;    // N
+  unsigned long long cells;        // shard_count * B
+  unsigned int tiles;              // route_tiles(cells)
+  unsigned int* cnt;               // [cells] keys of bag g on shard o at o * B + g
+  unsigned int* pk;                // [cells + 1] exclusive prefix of cnt
+  unsigned int* pb;                // [cells + 1] exclusive prefix of (cnt > 0)
+  unsigned int* tile_k;            // [tiles]
+  unsigned int* tile_b;            // [tiles]
+  unsigned int* bounds;            // [shard_count][feature_count + 1][2]
+  unsigned int* error;             // LookupErrorBits
+  unsigned long long* payload;     // scatter output (u64 words, shard-major)
+  unsigned int* bag_map;           // [cells] kept bag -> bag index in its feature
+  unsigned int* pos_map;           // [N] shard-ordered key -> position in its feature
+  const float* partials;           // merge input, shard-major then feature-major
+  const unsigned long long* part_off;   // [shard_count * feature_count] float offsets
+  float* const* outs;              // [feature_count] merge outputs
+  const float* const* grads;       // [feature_count] gradient inputs of the gather
+  float* send;                     // gather output (same layout as partials)
+  unsigned int* nonfinite;         // gather: set to 1 if any gradient value is not finite
+  const unsigned long long* row_pre;    // [shard_count * feature_count] row prefix
+  unsigned long long row_total;
+  int has_sequence;
+  int vec, group, iters;           // launch shape (see choose_shape)
+};
+unsigned route_tiles(unsigned long long cells);
+cudaError_t launch_route_count(const RouteLaunch& p, cudaStream_t stream);
+unsigned route_count_launches(const RouteLaunch& p);
+cudaError_t launch_route_scatter(const RouteLaunch& p, cudaStream_t stream);
+cudaError_t launch_route_merge(const RouteLaunch& p, cudaStream_t stream);
+cudaError_t launch_route_gather(const RouteLaunch& p, cudaStream_t stream);
+
 struct SortLaunch {
   void* keys; void* keys_alt;      // KeyT
   unsigned int* vals; unsigned int* vals_alt;

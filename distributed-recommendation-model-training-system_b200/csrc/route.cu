@@ -1,0 +1,499 @@
+// route.cu -- the shard-partition step of a multi-GPU round and the client-side
+// merge, on the device.
+//
+// Reference semantics followed:
+//   * PrepareLookupInputs, src/access/prepared_lookup.cpp:47-83: every key goes to
+//     shard key % n in (bag, position) order; every shard receives every bag of
+//     every feature (offsets per shard) and the GLOBAL valid lengths, which must
+//     equal the offset differences (:24-25).
+//   * DistributedClient merge, src/client/distributed_client.cpp:173-188: the
+//     zeroed output receives the shard partials in shard order; sequence rows are
+//     scattered by position; mean bags are divided once by (float)valid_length
+//     after the merge (:227-232).
+//   * Push split, src/client/distributed_client.cpp:252-265: each shard receives
+//     the full bag gradients of pooled features and the position rows of its
+//     keys for sequence features.
+//
+// Bags without a key on a shard contribute an all-zero partial (0 + nothing) and
+// no gradient term, so they are dropped from that shard's part: a merge that
+// skips them adds +0.0f fewer times, which leaves every value unchanged (a
+// partial is never -0.0f: 0 + w rounds an exact cancellation to +0.0f).
+//
+// Index spaces (n shards, B = bags of all features, N = keys of all features):
+//   cell (o, g) = o * B + g, g = feature bag base + bag: count of bag g's keys on
+//   shard o.  pk / pb = exclusive prefix over cells of the key counts / of
+//   (count > 0), so shard o's keys are [pk[o*B], pk[(o+1)*B]) in (feature, bag,
+//   position) order and its kept bags [pb[o*B], pb[(o+1)*B]).
+//   Payload sent to shard o (u64): [keys | offsets (kept + 1 per feature) |
+//   valid lengths (kept)], feature-major inside each region.
+#include "kernels.cuh"
+
+namespace eps_b200 {
+namespace {
+
+constexpr int kScanThreads = 256;
+constexpr int kScanItems = 8;
+constexpr int kScanTile = kScanThreads * kScanItems;
+
+__device__ __forceinline__ unsigned feature_of(const unsigned long long* s_base, unsigned fc,
+                                               unsigned long long g) {
+  unsigned lo = 0, hi = fc;
+  while (hi - lo > 1) { const unsigned mid = (lo + hi) >> 1; if (s_base[mid] <= g) lo = mid; else hi = mid; }
+  return lo;
+}
+
+// ------------------------------------------------------------------ count
+// One warp per bag: validates the bag and counts its keys per shard (lane o
+// holds shard o's count; n <= 32).
+__global__ void __launch_bounds__(256) route_count(RouteLaunch p) {
+  __shared__ unsigned long long s_base[kMaxFeatures + 1];
+  const unsigned fc = p.feature_count;
+  for (unsigned i = threadIdx.x; i < fc; i += blockDim.x) s_base[i] = p.features[i].bag_base;
+  if (threadIdx.x == 0) s_base[fc] = p.bag_total;
+  __syncthreads();
+  const unsigned lane = threadIdx.x & 31;
+  const unsigned long long warp = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) >> 5;
+  const unsigned long long nwarps = (gridDim.x * (unsigned long long)blockDim.x) >> 5;
+  const unsigned n = p.shard_count;
+  unsigned err = 0;
+  for (unsigned long long g = warp; g < p.bag_total; g += nwarps) {
+    const LookupFeature* F = p.features + feature_of(s_base, fc, g);
+    const unsigned long long b = g - F->bag_base;
+    const unsigned long long key_count = F->key_count;
+    unsigned long long o2 = 0;
+    if (lane < 2) o2 = F->offsets[b + lane];
+    unsigned long long s = __shfl_sync(~0u, o2, 0), e = __shfl_sync(~0u, o2, 1);
+    if (b == 0 && s != 0) err |= kLookupBadOffsets;
+    if (b + 1 == F->bag_count && e != key_count) err |= kLookupBadOffsets;
+    if (s > e || e > key_count) { err |= kLookupBadOffsets; s = e = 0; }
+    if (F->lengths && F->lengths[b] != e - s) err |= kLookupShortLength;
+    const unsigned long long key_space = F->rows;
+    unsigned count = 0;
+    for (unsigned long long c0 = s; c0 < e; c0 += 32) {
+      const unsigned long long i = c0 + lane;
+      unsigned owner = ~0u;
+      if (i < e) {
+        const unsigned long long key = F->keys[i];
+        if (key < key_space) owner = (unsigned)(key % n);
+        else err |= kLookupBadKey;
+      }
+      for (unsigned o = 0; o < n; ++o) {
+        const unsigned m = __ballot_sync(~0u, owner == o);
+        if (lane == o) count += __popc(m);
+      }
+    }
+    if (lane < n) p.cnt[lane * p.bag_total + g] = count;
+  }
+  err = __reduce_or_sync(~0u, err);
+  if (err && lane == 0) atomicOr(p.error, err);
+}
+
+// --------------------------------------------------------- three-phase scan
+__device__ __forceinline__ void load_cells(const RouteLaunch& p, unsigned long long tile, unsigned (&k)[kScanItems],
+                                           unsigned (&b)[kScanItems]) {
+  const unsigned long long base = tile * kScanTile + threadIdx.x * (unsigned long long)kScanItems;
+#pragma unroll
+  for (int j = 0; j < kScanItems; ++j) {
+    const unsigned long long idx = base + j;
+    const unsigned c = idx < p.cells ? p.cnt[idx] : 0u;
+    k[j] = c;
+    b[j] = c ? 1u : 0u;
+  }
+}
+
+// Block-wide exclusive scan of one value per thread; returns the block total.
+__device__ __forceinline__ unsigned block_exclusive(unsigned x, unsigned* s_warp, unsigned& total) {
+  const unsigned lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  unsigned inc = x;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const unsigned y = __shfl_up_sync(~0u, inc, d);
+    if (lane >= d) inc += y;
+  }
+  if (lane == 31) s_warp[w] = inc;
+  __syncthreads();
+  if (w == 0) {
+    unsigned v = lane < blockDim.x / 32 ? s_warp[lane] : 0u;
+    unsigned vi = v;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const unsigned y = __shfl_up_sync(~0u, vi, d);
+      if (lane >= d) vi += y;
+    }
+    if (lane < blockDim.x / 32) s_warp[lane] = vi - v;
+    if (lane == 31) s_warp[32] = vi;
+  }
+  __syncthreads();
+  const unsigned r = s_warp[w] + inc - x;
+  total = s_warp[32];
+  __syncthreads();
+  return r;
+}
+
+__global__ void __launch_bounds__(kScanThreads) route_tile_sums(RouteLaunch p) {
+  __shared__ unsigned s_warp[33];
+  unsigned k[kScanItems], b[kScanItems];
+  load_cells(p, blockIdx.x, k, b);
+  unsigned sk = 0, sb = 0;
+#pragma unroll
+  for (int j = 0; j < kScanItems; ++j) { sk += k[j]; sb += b[j]; }
+  unsigned tk, tb;
+  block_exclusive(sk, s_warp, tk);
+  block_exclusive(sb, s_warp, tb);
+  if (threadIdx.x == 0) { p.tile_k[blockIdx.x] = tk; p.tile_b[blockIdx.x] = tb; }
+}
+
+// One block: exclusive prefixes of the tile sums (in place) and the totals.
+__global__ void __launch_bounds__(1024) route_tile_scan(RouteLaunch p) {
+  __shared__ unsigned s_warp[33];
+  unsigned carry_k = 0, carry_b = 0;
+  for (unsigned base = 0; base < p.tiles; base += blockDim.x) {
+    const unsigned t = base + threadIdx.x;
+    const unsigned xk = t < p.tiles ? p.tile_k[t] : 0u, xb = t < p.tiles ? p.tile_b[t] : 0u;
+    unsigned tk, tb;
+    const unsigned ek = block_exclusive(xk, s_warp, tk);
+    const unsigned eb = block_exclusive(xb, s_warp, tb);
+    if (t < p.tiles) { p.tile_k[t] = carry_k + ek; p.tile_b[t] = carry_b + eb; }
+    carry_k += tk;
+    carry_b += tb;
+  }
+  if (threadIdx.x == 0) { p.pk[p.cells] = carry_k; p.pb[p.cells] = carry_b; }
+}
+
+__global__ void __launch_bounds__(kScanThreads) route_tile_apply(RouteLaunch p) {
+  __shared__ unsigned s_warp[33];
+  unsigned k[kScanItems], b[kScanItems];
+  load_cells(p, blockIdx.x, k, b);
+  unsigned sk = 0, sb = 0;
+#pragma unroll
+  for (int j = 0; j < kScanItems; ++j) { sk += k[j]; sb += b[j]; }
+  unsigned tk, tb;
+  unsigned ek = block_exclusive(sk, s_warp, tk) + p.tile_k[blockIdx.x];
+  unsigned eb = block_exclusive(sb, s_warp, tb) + p.tile_b[blockIdx.x];
+  const unsigned long long base = blockIdx.x * (unsigned long long)kScanTile + threadIdx.x * (unsigned long long)kScanItems;
+#pragma unroll
+  for (int j = 0; j < kScanItems; ++j) {
+    const unsigned long long idx = base + j;
+    if (idx < p.cells) { p.pk[idx] = ek; p.pb[idx] = eb; }
+    ek += k[j];
+    eb += b[j];
+  }
+}
+
+// bounds[(o * (F + 1) + f) * 2 + {0,1}] = pk, pb at the first cell of (o, f);
+// f = F gives the first cell of shard o + 1.
+__global__ void route_bounds(RouteLaunch p) {
+  const unsigned F = p.feature_count;
+  const unsigned t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= p.shard_count * (F + 1)) return;
+  const unsigned o = t / (F + 1), f = t % (F + 1);
+  const unsigned long long idx = f < F ? o * p.bag_total + p.features[f].bag_base : (o + 1ull) * p.bag_total;
+  p.bounds[2 * t] = p.pk[idx];
+  p.bounds[2 * t + 1] = p.pb[idx];
+}
+
+// ---------------------------------------------------------------- scatter
+__device__ __forceinline__ unsigned long long extra_of(const RouteLaunch& p, unsigned o) {
+  // u64 words before shard o's keys that are not keys: the offsets and lengths
+  // regions of shards 0 .. o-1 (2 per kept bag + 1 per feature)
+  return 2ull * p.pb[o * p.bag_total] + (unsigned long long)o * p.feature_count;
+}
+
+__global__ void __launch_bounds__(256) route_scatter(RouteLaunch p) {
+  __shared__ unsigned long long s_base[kMaxFeatures + 1];
+  const unsigned fc = p.feature_count;
+  for (unsigned i = threadIdx.x; i < fc; i += blockDim.x) s_base[i] = p.features[i].bag_base;
+  if (threadIdx.x == 0) s_base[fc] = p.bag_total;
+  __syncthreads();
+  const unsigned n = p.shard_count;
+  const unsigned long long B = p.bag_total;
+  // leading zero of every (shard, feature) offsets region
+  {
+    const unsigned long long t = blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x;
+    if (t < (unsigned long long)n * fc) {
+      const unsigned o = (unsigned)(t / fc), f = (unsigned)(t % fc);
+      const unsigned long long keys_end = p.pk[(o + 1ull) * B] + extra_of(p, o);
+      const unsigned long long at = keys_end + (p.pb[o * B + s_base[f]] - p.pb[o * B]) + f;
+      p.payload[at] = 0ull;
+    }
+  }
+  const unsigned lane = threadIdx.x & 31;
+  const unsigned long long warp = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) >> 5;
+  const unsigned long long nwarps = (gridDim.x * (unsigned long long)blockDim.x) >> 5;
+  const unsigned lt = (1u << lane) - 1u;
+  // per-lane constants of shard `lane`
+  unsigned long long my_extra = 0, my_keys_end = 0, my_lens_at = 0;
+  if (lane < n) {
+    my_extra = extra_of(p, lane);
+    my_keys_end = p.pk[(lane + 1ull) * B] + my_extra;
+    my_lens_at = my_keys_end + (p.pb[(lane + 1ull) * B] - p.pb[lane * B]) + fc;
+  }
+  for (unsigned long long g = warp; g < B; g += nwarps) {
+    const unsigned f = feature_of(s_base, fc, g);
+    const LookupFeature* F = p.features + f;
+    const unsigned long long b = g - s_base[f];
+    unsigned long long o2 = 0;
+    if (lane < 2) o2 = F->offsets[b + lane];
+    const unsigned long long s = __shfl_sync(~0u, o2, 0), e = __shfl_sync(~0u, o2, 1);
+    // (validated by route_count: s <= e <= key_count)
+    unsigned c = 0, kept = 0, k_at = 0;
+    if (lane < n) {
+      c = p.cnt[lane * B + g];
+      k_at = p.pk[lane * B + g];
+      kept = p.pb[lane * B + g];
+      if (c) {
+        const unsigned long long fk = p.pk[lane * B + s_base[f]];
+        const unsigned long long fb = p.pb[lane * B + s_base[f]];
+        const unsigned long long j = kept - fb;                 // kept index inside (shard, feature)
+        const unsigned long long rel = fb - p.pb[lane * B];     // kept bags of earlier features
+        p.payload[my_keys_end + rel + f + j + 1] = (unsigned long long)k_at + c - fk;
+        p.payload[my_lens_at + rel + j] = e - s;
+        p.bag_map[kept] = (unsigned)b;
+      }
+    }
+    unsigned run = k_at;                 // lane o: next key index of shard o in this bag
+    for (unsigned long long c0 = s; c0 < e; c0 += 32) {
+      const unsigned long long i = c0 + lane;
+      unsigned long long key = 0;
+      unsigned owner = ~0u, rank = 0;
+      if (i < e) { key = F->keys[i]; owner = (unsigned)(key % n); }
+      const unsigned before = run;
+      for (unsigned o = 0; o < n; ++o) {
+        const unsigned m = __ballot_sync(~0u, owner == o);
+        if (owner == o) rank = __popc(m & lt);
+        if (lane == o) run += __popc(m);
+      }
+      const unsigned o_safe = owner < n ? owner : 0u;
+      const unsigned base = __shfl_sync(~0u, before, o_safe);
+      const unsigned long long ex = __shfl_sync(~0u, my_extra, o_safe);
+      if (owner < n) {
+        const unsigned q = base + rank;    // shard-ordered key index
+        p.payload[q + ex] = key;
+        p.pos_map[q] = (unsigned)i;
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ merge
+// Group of G lanes per pooled bag: out = ((0 + p_0) + p_1) + ... over the shards
+// that hold keys of the bag, then mean.  Sequence rows are copied to their
+// positions by the second loop.
+template <int G, int VEC, int ITERS>
+__global__ void __launch_bounds__(256) route_merge(RouteLaunch p) {
+  __shared__ unsigned long long s_base[kMaxFeatures + 1];
+  const unsigned fc = p.feature_count;
+  for (unsigned i = threadIdx.x; i < fc; i += blockDim.x) s_base[i] = p.features[i].bag_base;
+  if (threadIdx.x == 0) s_base[fc] = p.bag_total;
+  __syncthreads();
+  constexpr int C = VEC * ITERS;
+  const unsigned gl = threadIdx.x % G;
+  const unsigned long long gid = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) / G;
+  const unsigned long long ngroups = (gridDim.x * (unsigned long long)blockDim.x) / G;
+  const unsigned n = p.shard_count;
+  const unsigned long long B = p.bag_total;
+  for (unsigned long long g = gid; g < B; g += ngroups) {
+    const unsigned f = feature_of(s_base, fc, g);
+    const LookupFeature* F = p.features + f;
+    if (F->pooling == 2) continue;
+    const unsigned long long b = g - s_base[f];
+    const unsigned D = F->dim;
+    float acc[C];
+#pragma unroll
+    for (int k = 0; k < C; ++k) acc[k] = 0.0f;
+    for (unsigned o = 0; o < n; ++o) {
+      if (!p.cnt[o * B + g]) continue;
+      const unsigned long long j = p.pb[o * B + g] - p.pb[o * B + s_base[f]];
+      const float* row = p.partials + p.part_off[o * fc + f] + j * D;
+#pragma unroll
+      for (int it = 0; it < ITERS; ++it) {
+        const unsigned col = (it * G + gl) * VEC;
+        if (col >= D) continue;
+        float t[VEC];
+        load_vec<VEC>(row + col, t);
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) acc[it * VEC + v] = __fadd_rn(acc[it * VEC + v], t[v]);
+      }
+    }
+    const bool mean = F->pooling == 1;
+    const unsigned long long len = F->offsets[b + 1] - F->offsets[b];
+    const float denom = (float)len;
+    float* out = p.outs[f] + b * D;
+#pragma unroll
+    for (int it = 0; it < ITERS; ++it) {
+      const unsigned col = (it * G + gl) * VEC;
+      if (col >= D) continue;
+      float t[VEC];
+#pragma unroll
+      for (int v = 0; v < VEC; ++v)
+        t[v] = (mean && len) ? __fdiv_rn(acc[it * VEC + v], denom) : acc[it * VEC + v];
+      store_vec<VEC>(out + col, t);
+    }
+  }
+  if (!p.has_sequence) return;
+  // sequence features: shard-ordered key q -> position pos_map[q]
+  for (unsigned long long q = gid; q < p.key_total; q += ngroups) {
+    // shard: largest o with pk[o * B] <= q; then feature inside the shard
+    unsigned o = 0;
+    {
+      unsigned lo = 0, hi = n;
+      while (hi - lo > 1) { const unsigned mid = (lo + hi) >> 1; if (p.bounds[2 * mid * (fc + 1)] <= q) lo = mid; else hi = mid; }
+      o = lo;
+    }
+    const unsigned* ob = p.bounds + 2ull * o * (fc + 1);
+    unsigned lo = 0, hi = fc;
+    while (hi - lo > 1) { const unsigned mid = (lo + hi) >> 1; if (ob[2 * mid] <= q) lo = mid; else hi = mid; }
+    // skip empty features that share the start index
+    while (lo + 1 < fc && ob[2 * (lo + 1)] <= q) ++lo;
+    const unsigned f = lo;
+    const LookupFeature* F = p.features + f;
+    if (F->pooling != 2) continue;
+    const unsigned D = F->dim;
+    const float* row = p.partials + p.part_off[o * fc + f] + (q - ob[2 * f]) * (unsigned long long)D;
+    float* out = p.outs[f] + (unsigned long long)p.pos_map[q] * D;
+#pragma unroll
+    for (int it = 0; it < ITERS; ++it) {
+      const unsigned col = (it * G + gl) * VEC;
+      if (col >= D) continue;
+      float t[VEC];
+      load_vec<VEC>(row + col, t);
+      store_vec<VEC>(out + col, t);
+    }
+  }
+}
+
+// ----------------------------------------------------------------- gather
+// Gradient rows sent to each shard, shard-major then feature-major: pooled
+// features send the kept bags' rows, sequence features the rows of the keys.
+template <int G, int VEC, int ITERS>
+__global__ void __launch_bounds__(256) route_gather(RouteLaunch p) {
+  const unsigned fc = p.feature_count;
+  const unsigned blocks = p.shard_count * fc;        // (shard, feature) row blocks
+  const unsigned gl = threadIdx.x % G;
+  const unsigned long long gid = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) / G;
+  const unsigned long long ngroups = (gridDim.x * (unsigned long long)blockDim.x) / G;
+  const unsigned long long B = p.bag_total;
+  for (unsigned long long r = gid; r < p.row_total; r += ngroups) {
+    unsigned lo = 0, hi = blocks;
+    while (hi - lo > 1) { const unsigned mid = (lo + hi) >> 1; if (p.row_pre[mid] <= r) lo = mid; else hi = mid; }
+    while (lo + 1 < blocks && p.row_pre[lo + 1] <= r) ++lo;
+    const unsigned o = lo / fc, f = lo % fc;
+    const LookupFeature* F = p.features + f;
+    const unsigned D = F->dim;
+    const unsigned long long j = r - p.row_pre[lo];
+    unsigned long long src;
+    if (F->pooling == 2) src = p.pos_map[p.pk[o * B + F->bag_base] + j];
+    else src = p.bag_map[p.pb[o * B + F->bag_base] + j];
+    const float* row = p.grads[f] + src * D;
+    float* dst = p.send + p.part_off[lo] + j * D;
+#pragma unroll
+    for (int it = 0; it < ITERS; ++it) {
+      const unsigned col = (it * G + gl) * VEC;
+      if (col >= D) continue;
+      float t[VEC];
+      load_vec<VEC>(row + col, t);
+      store_vec<VEC>(dst + col, t);
+    }
+  }
+  if (!p.nonfinite) return;
+  // every gradient value must be finite, sent or not (distributed_client.cpp:249)
+  const unsigned long long tid = blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x;
+  const unsigned long long nthreads = gridDim.x * (unsigned long long)blockDim.x;
+  unsigned bad = 0;
+  for (unsigned f = 0; f < fc; ++f) {
+    const LookupFeature* F = p.features + f;
+    const unsigned long long rows = F->pooling == 2 ? F->key_count : F->bag_count;
+    const unsigned long long total = rows * F->dim;
+    const float* g = p.grads[f];
+    for (unsigned long long i = tid; i < total; i += nthreads) bad |= !isfinite(g[i]);
+  }
+  bad = __reduce_or_sync(~0u, bad);
+  if (bad && (threadIdx.x & 31) == 0) atomicOr(p.nonfinite, 1u);
+}
+
+unsigned grid_for(unsigned long long groups, unsigned per_block) {
+  const unsigned long long want = (groups + per_block - 1) / per_block;
+  const unsigned long long cap = 148ull * 8 * 4;
+  return (unsigned)std::max(1ull, std::min(want, cap));
+}
+
+template <int G, int VEC, int ITERS>
+cudaError_t launch_merge_shape(const RouteLaunch& p, cudaStream_t s) {
+  const unsigned long long items = std::max(p.bag_total, p.has_sequence ? p.key_total : 0ull);
+  route_merge<G, VEC, ITERS><<<grid_for(items, 256 / G), 256, 0, s>>>(p);
+  return cudaGetLastError();
+}
+template <int G, int VEC, int ITERS>
+cudaError_t launch_gather_shape(const RouteLaunch& p, cudaStream_t s) {
+  route_gather<G, VEC, ITERS><<<grid_for(std::max(p.row_total, 1ull), 256 / G), 256, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+#define EPS_ROUTE_SHAPES(FN)                                         \
+  if (p.vec == 4) {                                                  \
+    switch (p.group) {                                               \
+      case 8: return FN<8, 4, 1>(p, stream);                         \
+      case 16: return FN<16, 4, 1>(p, stream);                       \
+      default:                                                       \
+        if (p.iters == 1) return FN<32, 4, 1>(p, stream);            \
+        if (p.iters == 2) return FN<32, 4, 2>(p, stream);            \
+        return FN<32, 4, 4>(p, stream);                              \
+    }                                                                \
+  }                                                                  \
+  if (p.iters == 1) return FN<32, 1, 1>(p, stream);                  \
+  if (p.iters == 2) return FN<32, 1, 2>(p, stream);                  \
+  return FN<32, 1, 4>(p, stream);
+
+}  // namespace
+
+unsigned route_tiles(unsigned long long cells) {
+  return (unsigned)((cells + kScanTile - 1) / kScanTile);
+}
+
+cudaError_t launch_route_count(const RouteLaunch& p, cudaStream_t stream) {
+  if (p.bag_total) {
+    route_count<<<grid_for(p.bag_total, 8), 256, 0, stream>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  const unsigned tiles = route_tiles(p.cells);
+  if (tiles) {
+    route_tile_sums<<<tiles, kScanThreads, 0, stream>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  route_tile_scan<<<1, 1024, 0, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  if (tiles) {
+    route_tile_apply<<<tiles, kScanThreads, 0, stream>>>(p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  const unsigned nb = p.shard_count * (p.feature_count + 1);
+  route_bounds<<<(nb + 255) / 256, 256, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+unsigned route_count_launches(const RouteLaunch& p) {
+  const unsigned tiles = route_tiles(p.cells);
+  return (p.bag_total ? 1u : 0u) + (tiles ? 2u : 0u) + 2u;
+}
+
+cudaError_t launch_route_scatter(const RouteLaunch& p, cudaStream_t stream) {
+  const unsigned long long zeros_blocks = ((unsigned long long)p.shard_count * p.feature_count + 255) / 256;
+  const unsigned grid = std::max<unsigned>(grid_for(p.bag_total, 8), (unsigned)zeros_blocks);
+  route_scatter<<<grid, 256, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_route_merge(const RouteLaunch& p, cudaStream_t stream) {
+  EPS_ROUTE_SHAPES(launch_merge_shape)
+}
+
+cudaError_t launch_route_gather(const RouteLaunch& p, cudaStream_t stream) {
+  if (!p.row_total && !p.nonfinite) return cudaSuccess;
+  EPS_ROUTE_SHAPES(launch_gather_shape)
+}
+
+}  // namespace eps_b200

@@ -230,6 +230,50 @@ EPS_B200_EXPORT int eps_b200_profile(EpsB200Store* store, int32_t mode, double* 
                                      uint64_t* phase_launches, uint64_t* phase_calls,
                                      EpsB200Status* status);
 
+/* ---- Multi-GPU round: the client side of a sharded lookup / push.
+ * A route splits device-resident features over `shard_count` shards (one per
+ * GPU; 1 .. 32) by key % shard_count:
+ *   PrepareLookupInputs (src/access/prepared_lookup.cpp:47-83) on the device.
+ * Shard o's part of feature f keeps the bags that have keys on o, with the
+ * original (global) bag lengths as valid lengths, so the shard's
+ * eps_b200_lookup(shard_partial = 1) returns the reference's shard contribution
+ * for exactly those bags (bags without keys there contribute zeros).
+ * counts (host, [shard_count][count][2]) receives per (shard, feature) the
+ * number of keys and of kept bags.  The inputs must stay valid until
+ * eps_b200_route_release.  Keys must be < the table's key_space.  The call
+ * waits for its stream (the counts are needed to size the exchange). */
+EPS_B200_EXPORT int eps_b200_route(EpsB200Store* store, const EpsB200Feature* features, uint64_t count,
+                                   uint32_t shard_count, void* stream, uint64_t* route,
+                                   uint64_t* counts, EpsB200Status* status);
+/* Writes the u64 words sent to every shard, shard after shard (what the
+ * reference's DistributedClient sends in each shard's LookupRequest,
+ * src/client/distributed_client.cpp:96-104): for shard o, the keys of every
+ * feature, then every feature's kept-bag offsets (kept + 1 words), then every
+ * feature's kept-bag valid lengths.  Shard o's part has
+ * sum_f (keys + 2 * kept + 1) words. */
+EPS_B200_EXPORT int eps_b200_route_scatter(EpsB200Store* store, uint64_t route, uint64_t* payload,
+                                           void* stream, EpsB200Status* status);
+/* Client merge (src/client/distributed_client.cpp:173-188,227-232): partials holds the
+ * shard contributions received from every shard, shard after shard, each
+ * feature after feature as [kept bags, dim] (sum/mean) or [keys, dim]
+ * (sequence); outputs[i] ([bags, dim] or [keys, dim], device) receives the
+ * zero-initialised shard-ordered sum, mean bags divided by (float)length, and
+ * sequence rows at their positions. */
+EPS_B200_EXPORT int eps_b200_route_merge(EpsB200Store* store, uint64_t route, const float* partials,
+                                         const EpsB200Buffer* outputs, void* stream,
+                                         EpsB200Status* status);
+/* Push split (src/client/distributed_client.cpp:252-265): gathers into `send`
+ * (device, the layout of route_merge's partials) the gradient rows each shard
+ * needs: the kept bags' rows of pooled features, the keys' rows of sequence
+ * features.  If `nonfinite` (device u32, may be NULL) is given, 1 is stored
+ * there when any value of any gradient tensor is not finite (the client check
+ * of src/client/distributed_client.cpp:249); the caller zeroes it. */
+EPS_B200_EXPORT int eps_b200_route_gather(EpsB200Store* store, uint64_t route,
+                                          const EpsB200Buffer* gradients, float* send,
+                                          uint32_t* nonfinite, void* stream, EpsB200Status* status);
+/* Frees a route (after the work that uses it has been enqueued). */
+EPS_B200_EXPORT int eps_b200_route_release(EpsB200Store* store, uint64_t route, EpsB200Status* status);
+
 /* CpuParameterService::Stats (include/eps/runtime.hpp:134). */
 EPS_B200_EXPORT int eps_b200_stats(EpsB200Store* store, EpsB200Stats* stats, EpsB200Status* status);
 
