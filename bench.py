@@ -220,6 +220,16 @@ def run_reference(args):
         return
     wl, _ = _import_package()
     w = workload_for(wl, args.config, 0, args.rows)
+    if world > 1:
+        # the same job as the GPU arm at this N: every rank's batch, served as one
+        # combined request (features rank-major, ids r * F + f) by the CPU shards
+        parts = [workload_for(wl, args.config, r, args.rows) for r in range(world)]
+        F = len(w.features)
+        feats = [type(f)(f.table, r * F + f.feature, f.pooling, f.keys, f.offsets)
+                 for r, p in enumerate(parts) for f in p.features]
+        grads = [g for p in parts for g in p.gradients]
+        w = type(w)(f"{w.name}, {world} batches (one per GPU of the sharded run)", w.tables,
+                    feats, grads, w.seed, dict(w.meta))
     threads = host_threads()
     times = reference_rounds(w, args.steps, args.warmup, threads)
     if times is None:
@@ -255,10 +265,12 @@ def run_b200(args):
     w = workload_for(wl, args.config, rank, args.rows)
     bm = byte_model(w)
     dev = torch.device(f"cuda:{local_rank}")
-    store = eps.ParameterStore(device=local_rank, state_bytes=150 << 30)
+    # one shard per rank: keys k with k % world == rank (the table's rows are split)
+    store = eps.ParameterStore(device=local_rank, shard_id=rank, shard_count=world,
+                               state_bytes=150 << 30)
     for t in w.tables:
         store.create_table(eps.TableDefinition(id=t.id, dimension=t.dimension, key_space=t.rows,
-                                               learning_rate=1e-3))
+                                               learning_rate=1e-3, shard_count=world))
     stream = torch.cuda.Stream(device=dev)
     torch.cuda.set_stream(stream)          # flushes and events run on the store's stream
 
@@ -271,13 +283,23 @@ def run_b200(args):
     outs = [torch.empty((f.output_rows, dims[f.table]), dtype=torch.float32, device=dev)
             for f in w.features]
     grads = [torch.from_numpy(g).to(dev) for g in w.gradients]
-    lookup = store.prepare_lookup(feats, outs)
-    push = store.prepare_push(grads)
     flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)   # 256 MiB > 126 MB L2
+    if dist:
+        # every rank's batch is routed to the owners over NCCL all-to-all
+        import importlib
+        client = importlib.import_module("eps_b200.distributed").ShardedClient(store)
+        ids_stream = torch.cuda.Stream(device=dev)   # partition + key exchange overlap the push
 
-    def one_round():
-        ticket = lookup(stream)
-        push(ticket, stream, wait=False)
+        def one_round():
+            handle, _ = client.lookup(feats, outputs=outs, input_stream=ids_stream)
+            client.push(handle, grads)
+    else:
+        lookup = store.prepare_lookup(feats, outs)
+        push = store.prepare_push(grads)
+
+        def one_round():
+            ticket = lookup(stream)
+            push(ticket, stream, wait=False)
 
     clocks = Clocks(local_rank)
     clocks.start()
@@ -314,20 +336,30 @@ def run_b200(args):
     prof = store.profile(0)
     # the timed rounds last milliseconds, less than one nvidia-smi sample period:
     # keep the same load running (untimed) for 0.5 s so the clock record covers it
-    t_soak = time.perf_counter()
-    while time.perf_counter() - t_soak < 0.5:
-        for _ in range(8):
-            one_round()
-        store.synchronize()
+    # (a fixed round count, the same on every rank, so that collectives match)
+    step_ms = sum(a.elapsed_time(b) for a, b in events) / args.steps
+    if dist:
+        t = torch.tensor([step_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        step_ms = float(t.item())
+    for i in range(max(8, int(500.0 / max(step_ms, 1e-3)))):
+        one_round()
+        if i % 8 == 7:
+            store.synchronize()
+    store.synchronize()
     clk = clocks.stop()
     if dist:
         dist.barrier()
     total_ms = sum(a.elapsed_time(b) for a, b in events)
+    job_N, job_U = bm["N"], bm["U"]          # occurrences / unique rows of the whole job
     if dist:
         t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms = float(t.item())
-    value = bm["N"] * args.steps * world / (total_ms / 1e3)
+        t = torch.tensor([bm["N"], bm["U"]], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        job_N, job_U = int(t[0].item()), int(t[1].item())
+    value = job_N * args.steps / (total_ms / 1e3)
 
     # ---- roofline of the dominant phase
     peak, peak_kind = load_peaks()
@@ -353,11 +385,33 @@ def run_b200(args):
               for f in w.features]
     houts = [pinned(np.zeros((f.output_rows, dims[f.table]), np.float32)) for f in w.features]
     hgrads = [pinned(g) for g in w.gradients]
-    hlookup = store.prepare_lookup(hfeats, houts)
-    hpush = store.prepare_push(hgrads)
+    if dist:
+        # host buffers: pinned copies in, the round through ShardedClient, outputs out
+        tk = [torch.from_numpy(f.keys.view(np.int64)) for f in hfeats]
+        to = [torch.from_numpy(f.offsets.view(np.int64)) for f in hfeats]
+        th = [torch.from_numpy(o) for o in houts]
+        tg = [torch.from_numpy(g) for g in hgrads]
+
+        def e2e_round():
+            with torch.cuda.stream(ids_stream):
+                dfeats = [eps.FeatureInput(f.table, f.feature, f.pooling,
+                                           k.to(dev, non_blocking=True),
+                                           o.to(dev, non_blocking=True))
+                          for f, k, o in zip(w.features, tk, to)]
+            handle, _ = client.lookup(dfeats, outputs=outs, input_stream=ids_stream)
+            for h, o in zip(th, outs):
+                h.copy_(o, non_blocking=True)
+            client.push(handle, [g.to(dev, non_blocking=True) for g in tg])
+            torch.cuda.current_stream(dev).synchronize()
+    else:
+        hlookup = store.prepare_lookup(hfeats, houts)
+        hpush = store.prepare_push(hgrads)
+
+        def e2e_round():
+            hpush(hlookup(stream), stream, wait=True)
     e2e_steps = max(3, args.steps // 2)
     for _ in range(2):
-        hpush(hlookup(stream), stream, wait=True)
+        e2e_round()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(e2e_steps)]
     torch.cuda.synchronize()
@@ -366,7 +420,7 @@ def run_b200(args):
     for a, b in ev:
         flush.zero_()
         a.record(stream)
-        hpush(hlookup(stream), stream, wait=True)
+        e2e_round()
         b.record(stream)
     torch.cuda.synchronize()
     e2e_ms = sum(a.elapsed_time(b) for a, b in ev)
@@ -374,7 +428,7 @@ def run_b200(args):
         t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
-    e2e_value = bm["N"] * e2e_steps * world / (e2e_ms / 1e3)
+    e2e_value = job_N * e2e_steps / (e2e_ms / 1e3)
     h2d = sum(f.keys.nbytes + f.offsets.nbytes for f in w.features) + \
         sum(g.nbytes for g in w.gradients)
     d2h = sum(o.nbytes for o in houts) + 36      # pooled outputs + push status
@@ -401,12 +455,14 @@ def run_b200(args):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": w.name, "occurrences_per_round": bm["N"],
+        "config": {"workload": w.name, "occurrences_per_round": job_N,
                    "unique_rows_per_round": bm["U"], "output_rows_per_round": bm["B"],
                    "compulsory_bytes_per_round": bm["pull"] + bm["push"],
                    "l2": "flushed (256 MiB write) before every timed round",
-                   "parallelism": "single GPU" if world == 1 else f"{world} replicas"},
-        "unique_rows_per_s": bm["U"] * args.steps * world / (total_ms / 1e3),
+                   "parallelism": "single GPU" if world == 1 else
+                   f"{world} shards (rows by key % {world}), NCCL all-to-all of keys, "
+                   f"partials and gradients; one batch per GPU"},
+        "unique_rows_per_s": job_U * args.steps / (total_ms / 1e3),
         "round_hbm_frac": ((bm["pull"] + bm["push"]) * args.steps / (total_ms / 1e3) / 1e9) / peak,
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,

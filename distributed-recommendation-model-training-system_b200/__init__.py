@@ -102,7 +102,8 @@ ENTRY_POINTS = ("eps_b200_abi_version", "eps_b200_create", "eps_b200_destroy",
                 "eps_b200_synchronize", "eps_b200_read_state", "eps_b200_load_state",
                 "eps_b200_optimizer_state", "eps_b200_profile", "eps_b200_stats",
                 "eps_b200_route", "eps_b200_route_scatter", "eps_b200_route_merge",
-                "eps_b200_route_gather", "eps_b200_route_release")
+                "eps_b200_route_gather", "eps_b200_route_release", "eps_b200_serve",
+                "eps_b200_serve_push")
 
 
 def load_library() -> C.CDLL:
@@ -140,6 +141,10 @@ def load_library() -> C.CDLL:
     lib.eps_b200_route_merge.argtypes = [vp, C.c_uint64, vp, P(Buffer), vp, P(Status)]
     lib.eps_b200_route_gather.argtypes = [vp, C.c_uint64, P(Buffer), vp, vp, vp, P(Status)]
     lib.eps_b200_route_release.argtypes = [vp, C.c_uint64, P(Status)]
+    lib.eps_b200_serve.argtypes = [vp, vp, vp, vp, vp, C.c_uint32, C.c_uint32, C.c_int32, vp, vp,
+                                   P(C.c_uint64), P(Status)]
+    lib.eps_b200_serve_push.argtypes = [vp, C.c_uint64, vp, vp, vp, vp, C.c_uint32, C.c_uint32, vp,
+                                        vp, C.c_int32, P(Status)]
     for name in ENTRY_POINTS[1:]:
         if name != "eps_b200_destroy":
             getattr(lib, name).restype = C.c_int
@@ -494,6 +499,33 @@ class ParameterStore:
         st = Status()
         _check(self.lib.eps_b200_route_gather(self._h, route, self._buffers(gradients), _ptr(send),
                                               _ptr(nonfinite), _stream_ptr(stream), C.byref(st)), st)
+
+    @staticmethod
+    def _schema(peer_counts, tables, poolings):
+        pc = np.ascontiguousarray(peer_counts, dtype=np.uint64)
+        tb = np.ascontiguousarray(tables, dtype=np.uint32)
+        po = np.ascontiguousarray(poolings, dtype=np.uint32)
+        return pc, tb, po, int(pc.shape[0]), int(tb.shape[0])
+
+    def serve(self, payload, peer_counts, tables, poolings, partials, read_only=False,
+              stream=None):
+        """Owner side of a sharded round (eps_b200_serve); returns the ticket."""
+        pc, tb, po, n, F = self._schema(peer_counts, tables, poolings)
+        ticket = C.c_uint64(0)
+        st = Status()
+        _check(self.lib.eps_b200_serve(self._h, _ptr(payload), _ptr(pc), _ptr(tb), _ptr(po), n, F,
+                                       int(read_only), _ptr(partials), _stream_ptr(stream),
+                                       C.byref(ticket), C.byref(st)), st)
+        return None if read_only else ticket.value
+
+    def serve_push(self, ticket, gradients, peer_counts, tables, poolings, reject=None,
+                   stream=None, wait=False):
+        """Owner side of a sharded push (eps_b200_serve_push)."""
+        pc, tb, po, n, F = self._schema(peer_counts, tables, poolings)
+        st = Status()
+        _check(self.lib.eps_b200_serve_push(self._h, ticket, _ptr(gradients), _ptr(pc), _ptr(tb),
+                                            _ptr(po), n, F, _ptr(reject), _stream_ptr(stream),
+                                            int(wait), C.byref(st)), st)
 
     def route_release(self, route: int):
         st = Status()

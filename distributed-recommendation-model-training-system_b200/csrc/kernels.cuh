@@ -213,6 +213,7 @@ struct PushLaunch {
   unsigned int dim_max;
   PushControl* control;
   const unsigned int* lookup_error;
+  const unsigned int* external_reject;  // optional device word: nonzero rejects (non-finite input)
   unsigned long long long_run;     // segments longer than this are reduced in pieces
   int vec, group, iters;           // launch shape (see choose_shape)
 };

@@ -117,7 +117,10 @@ __global__ void __launch_bounds__(256) push_prescan(PushLaunch p, PushTable* tab
   unsigned bits = 0;
   const unsigned lookup_err = *(volatile const unsigned*)p.lookup_error;
   if (lookup_err) { c->reject_bits = 16u; c->mode = kModeRejected; return; }
-  if (*(volatile unsigned*)&c->nonfinite) { c->reject_bits = kRejectNonFiniteInput; c->mode = kModeRejected; return; }
+  if (*(volatile unsigned*)&c->nonfinite ||
+      (p.external_reject && *(volatile const unsigned*)p.external_reject)) {
+    c->reject_bits = kRejectNonFiniteInput; c->mode = kModeRejected; return;
+  }
   const float maxabs = __uint_as_float(*(volatile unsigned*)&c->maxabs_bits);
   bool safe = true;
   for (unsigned t = 0; t < p.table_count; ++t) {

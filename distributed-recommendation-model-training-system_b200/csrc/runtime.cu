@@ -925,8 +925,13 @@ int eps_b200_lookup_noalloc(EpsB200Store* store, const EpsB200Feature* features,
   });
 }
 
-int eps_b200_push(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gradients,
-                  uint64_t count, void* stream_arg, int32_t wait, EpsB200Status* status) {
+}  // extern "C"
+
+namespace {
+// eps_b200_push with an optional device reject word (sharded rounds).
+int PushEntry(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gradients,
+              uint64_t count, void* stream_arg, int32_t wait, const unsigned* external_reject,
+              EpsB200Status* status) {
   return Boundary(status, [&] {
     auto& s = *Checked(store);
     std::lock_guard lock(s.mutex);
@@ -1063,6 +1068,7 @@ int eps_b200_push(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gra
       pl.dim_max = t.dim_max;
       pl.control = t.control;
       pl.lookup_error = t.lookup_error;
+      pl.external_reject = external_reject;
       pl.long_run = (s.opt.flags & EPS_B200_FLAG_REFERENCE_ORDER) ? ~0ull : (unsigned long long)kLongRun;
       pl.vec = vec;
       pl.group = group;
@@ -1095,6 +1101,14 @@ int eps_b200_push(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gra
       Require(m.empty(), m.c_str());
     }
   });
+}
+}  // namespace
+
+extern "C" {
+
+int eps_b200_push(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gradients,
+                  uint64_t count, void* stream_arg, int32_t wait, EpsB200Status* status) {
+  return PushEntry(store, ticket, gradients, count, stream_arg, wait, nullptr, status);
 }
 
 int eps_b200_release(EpsB200Store* store, uint64_t ticket, EpsB200Status* status) {
@@ -1571,6 +1585,98 @@ int eps_b200_route_release(EpsB200Store* store, uint64_t route, EpsB200Status* s
     char* slab = it->second.slab;
     s.routes.erase(it);
     Cuda(cudaFreeAsync(slab, s.last ? s.last : s.own));
+  });
+}
+
+namespace {
+// Owner-side layout of a sharded round: requester r's payload region and the
+// (requester, feature) row blocks of the partial / gradient buffers.
+struct ServeLayout {
+  std::vector<EpsB200Feature> feats;
+  std::vector<EpsB200Buffer> blocks;     // rows x dim views (data = byte offset until bound)
+};
+ServeLayout MakeServeLayout(EpsB200Store& s, const uint64_t* payload, const uint64_t* peer_counts,
+                            const uint32_t* tables, const uint32_t* poolings, uint32_t n,
+                            uint32_t F, const float* rows_base) {
+  Require(peer_counts && tables && poolings && n >= 1 && n <= 32 && F >= 1 &&
+          (uint64_t)n * F <= kMaxFeatures, "invalid sharded round layout");
+  std::vector<unsigned> dims(F);
+  {
+    std::lock_guard lock(s.mutex);
+    for (uint32_t f = 0; f < F; ++f) {
+      Require(poolings[f] <= 2, "unsupported pooling mode");
+      dims[f] = s.Get(tables[f]).def.dimension;
+    }
+  }
+  ServeLayout L;
+  L.feats.resize((size_t)n * F);
+  L.blocks.resize((size_t)n * F);
+  unsigned long long base = 0, floats = 0;
+  for (uint32_t r = 0; r < n; ++r) {
+    const uint64_t* c = peer_counts + (size_t)r * F * 2;
+    unsigned long long NK = 0, KB = 0;
+    for (uint32_t f = 0; f < F; ++f) { NK += c[2 * f]; KB += c[2 * f + 1]; }
+    unsigned long long ko = 0, oo = 0, lo = 0;
+    for (uint32_t f = 0; f < F; ++f) {
+      const unsigned long long nk = c[2 * f], kb = c[2 * f + 1];
+      EpsB200Feature& x = L.feats[(size_t)r * F + f];
+      x.table = tables[f];
+      x.feature = r * F + f;
+      x.pooling = poolings[f];
+      x.reserved = 0;
+      x.keys = payload + base + ko;
+      x.key_count = nk;
+      x.offsets = payload + base + NK + oo;
+      x.offset_count = kb + 1;
+      x.valid_lengths = payload + base + NK + KB + F + lo;
+      ko += nk; oo += kb + 1; lo += kb;
+      const unsigned long long rows = poolings[f] == 2 ? nk : kb;
+      EpsB200Buffer& b = L.blocks[(size_t)r * F + f];
+      b.feature = r * F + f;
+      b.reserved = 0;
+      b.rows = rows;
+      b.columns = dims[f];
+      b.data = const_cast<float*>(rows_base) + floats;
+      b.device = s.opt.device;
+      b.reserved2 = 0;
+      floats += rows * dims[f];
+    }
+    base += NK + 2 * KB + F;
+  }
+  return L;
+}
+}  // namespace
+
+int eps_b200_serve(EpsB200Store* store, const uint64_t* payload, const uint64_t* peer_counts,
+                   const uint32_t* tables, const uint32_t* poolings, uint32_t requesters,
+                   uint32_t feature_count, int32_t read_only, float* partials, void* stream,
+                   uint64_t* ticket, EpsB200Status* status) {
+  return Boundary(status, [&] {
+    auto& s = *Checked(store);
+    Require(payload != nullptr && partials != nullptr, "null sharded round buffer");
+    ServeLayout L = MakeServeLayout(s, payload, peer_counts, tables, poolings, requesters,
+                                    feature_count, partials);
+    EpsB200Status inner;
+    const int rc = eps_b200_lookup(store, L.feats.data(), L.feats.size(), 1, read_only, 1,
+                                   L.blocks.data(), stream, ticket, &inner);
+    if (rc) throw Failure(rc, inner.message);
+  });
+}
+
+int eps_b200_serve_push(EpsB200Store* store, uint64_t ticket, const float* gradients,
+                        const uint64_t* peer_counts, const uint32_t* tables,
+                        const uint32_t* poolings, uint32_t requesters, uint32_t feature_count,
+                        const uint32_t* reject, void* stream, int32_t wait, EpsB200Status* status) {
+  return Boundary(status, [&] {
+    auto& s = *Checked(store);
+    Require(gradients != nullptr, "null sharded round buffer");
+    static const uint64_t kNoPayload = 0;
+    ServeLayout L = MakeServeLayout(s, &kNoPayload, peer_counts, tables, poolings, requesters,
+                                    feature_count, gradients);
+    EpsB200Status inner;
+    const int rc = PushEntry(store, ticket, L.blocks.data(), L.blocks.size(), stream, wait,
+                             reject, &inner);
+    if (rc) throw Failure(rc, inner.message);
   });
 }
 

@@ -39,7 +39,7 @@ from typing import Sequence
 
 import numpy as np
 
-from . import EpsError, FeatureInput, INVALID_ARGUMENT, SEQUENCE
+from . import EpsError, FeatureInput, INVALID_ARGUMENT, SEQUENCE  # noqa: F401
 
 
 @dataclass
@@ -52,6 +52,7 @@ class RoundHandle:
     dims: list
     poolings: list
     read_only: bool
+    tables: list
 
 
 def _rows(counts: np.ndarray, poolings) -> np.ndarray:
@@ -103,125 +104,124 @@ class ShardedClient:
             return self.torch.cuda.current_stream(self.device)
         return None
 
+    def _on(self, stream):
+        if stream is None:
+            import contextlib
+            return contextlib.nullcontext()
+        return self.torch.cuda.stream(stream)
+
     def _a2a(self, out, inp, out_splits=None, in_splits=None):
         self.dist.all_to_all_single(out, inp, output_split_sizes=out_splits,
                                     input_split_sizes=in_splits, group=self.group)
 
     # ------------------------------------------------------------- lookup
-    def lookup(self, feats: Sequence[FeatureInput], outputs=None, read_only: bool = False):
-        """Sharded pull of this rank's features.  Returns (handle, outputs)."""
+    def lookup(self, feats: Sequence[FeatureInput], outputs=None, read_only: bool = False,
+               input_stream=None):
+        """Sharded pull of this rank's features.  Returns (handle, outputs).
+
+        The partition and the key exchange run on `input_stream` (a stream on
+        which the inputs are ready; default: the current stream), so that they
+        can overlap the previous round's push; the shard lookup and the merge run
+        on the current stream.  The call waits for the partition counts (they
+        size the exchange)."""
         torch, n, F = self.torch, self.n, len(feats)
-        stream = self._stream()
+        main = self._stream()
+        side = input_stream if (input_stream is not None and main is not None) else main
         dims = [self.store.dimension(f.table) for f in feats]
         pools = [int(f.pooling) for f in feats]
-        err, route = None, None
-        counts = np.zeros((n, F, 2), np.uint64)
-        try:
-            route, counts = self.store.route(feats, n, stream)
-        except EpsError as e:
-            err = e
-        # ---- 2. counts + schema + error flag, one row per peer
-        width = 4 * F + 1
-        send = np.zeros((n, width), np.int64)
-        send[:, :2 * F] = counts.reshape(n, 2 * F).astype(np.int64)
-        send[:, 2 * F:3 * F] = [f.table for f in feats]
-        send[:, 3 * F:4 * F] = pools
-        send[:, 4 * F] = 1 if err else 0
-        send_t = torch.from_numpy(send).to(self.device)
-        recv_t = torch.empty_like(send_t)
-        self._a2a(recv_t, send_t)
-        recv = recv_t.cpu().numpy()
-        bad_schema = (recv[:, 2 * F:4 * F] != send[0, 2 * F:4 * F][None, :]).any()
-        if err is not None or recv[:, 4 * F].any() or bad_schema:
-            if route is not None:
-                self.store.route_release(route)
-            if err is not None:
-                raise err
-            raise EpsError(INVALID_ARGUMENT, "a peer rank rejected its lookup inputs"
-                           if not bad_schema else "ranks disagree on the feature schema")
-        peer = recv[:, :2 * F].reshape(n, F, 2).astype(np.uint64)   # [requester, f, (k, b)]
-
-        # ---- 3. payload: keys / offsets / valid lengths per owner
-        send_words = [payload_layout(counts[o])[3] for o in range(n)]
-        recv_lay = [payload_layout(peer[r]) for r in range(n)]
-        recv_words = [lay[3] for lay in recv_lay]
-        payload = torch.empty(sum(send_words), dtype=torch.int64, device=self.device)
-        self.store.route_scatter(route, payload, stream)
-        rpay = torch.empty(sum(recv_words), dtype=torch.int64, device=self.device)
-        self._a2a(rpay, payload, recv_words, send_words)
-
-        # ---- 4. this shard's lookup over every requester's part
+        tables = [int(f.table) for f in feats]
+        with self._on(side):
+            err, route = None, None
+            counts = np.zeros((n, F, 2), np.uint64)
+            try:
+                route, counts = self.store.route(feats, n, side)
+            except EpsError as e:
+                err = e
+            # ---- 2. counts + schema + error flag, one row per peer
+            width = 4 * F + 1
+            send = np.zeros((n, width), np.int64)
+            send[:, :2 * F] = counts.reshape(n, 2 * F).astype(np.int64)
+            send[:, 2 * F:3 * F] = tables
+            send[:, 3 * F:4 * F] = pools
+            send[:, 4 * F] = 1 if err else 0
+            send_t = torch.from_numpy(send).to(self.device)
+            recv_t = torch.empty_like(send_t)
+            self._a2a(recv_t, send_t)
+            recv = recv_t.cpu().numpy()
+            bad_schema = (recv[:, 2 * F:4 * F] != send[0, 2 * F:4 * F][None, :]).any()
+            if err is not None or recv[:, 4 * F].any() or bad_schema:
+                if route is not None:
+                    self.store.route_release(route)
+                if err is not None:
+                    raise err
+                raise EpsError(INVALID_ARGUMENT, "a peer rank rejected its lookup inputs"
+                               if not bad_schema else "ranks disagree on the feature schema")
+            peer = recv[:, :2 * F].reshape(n, F, 2).astype(np.uint64)   # [requester, f, (k, b)]
+            # ---- 3. payload: keys / offsets / valid lengths per owner
+            send_words = [payload_layout(counts[o])[3] for o in range(n)]
+            recv_words = [payload_layout(peer[r])[3] for r in range(n)]
+            payload = torch.empty(sum(send_words), dtype=torch.int64, device=self.device)
+            self.store.route_scatter(route, payload, side)
+            rpay = torch.empty(sum(recv_words), dtype=torch.int64, device=self.device)
+            self._a2a(rpay, payload, recv_words, send_words)
+        if side is not main:
+            main.wait_stream(side)
+            rpay.record_stream(main)
+        # ---- 4. this shard's lookup over every requester's part (C++ layout)
+        dim_arr = np.array(dims)
         prow = _rows(peer, pools)                 # [requester, f]
-        own_feats, part_views = [], []
-        part_send = torch.empty(int((prow * np.array(dims)[None, :]).sum()),
+        part_send = torch.empty(max(1, int((prow * dim_arr[None, :]).sum())),
                                 dtype=torch.float32, device=self.device)
-        base, fo = 0, 0
-        for r in range(n):
-            keys_at, off_at, len_at, words = recv_lay[r]
-            for f in range(F):
-                nk, kb = int(peer[r, f, 0]), int(peer[r, f, 1])
-                k0, o0, l0 = base + int(keys_at[f]), base + int(off_at[f]), base + int(len_at[f])
-                own_feats.append(FeatureInput(feats[f].table, r * F + f, pools[f],
-                                              rpay[k0:k0 + nk], rpay[o0:o0 + kb + 1],
-                                              rpay[l0:l0 + kb]))
-                rows = int(prow[r, f])
-                part_views.append(part_send[fo:fo + rows * dims[f]].view(rows, dims[f]))
-                fo += rows * dims[f]
-            base += words
-        ticket, _ = self.store.lookup(own_feats, read_only=read_only, shard_partial=True,
-                                      outputs=part_views, stream=stream)
-
+        ticket = self.store.serve(rpay, peer, tables, pools, part_send, read_only=read_only,
+                                  stream=main)
         # ---- 5. partials back to their requesters, merged in shard order
         mrow = _rows(counts, pools)               # [owner, f]
-        send_f = [int((prow[r] * np.array(dims)).sum()) for r in range(n)]
-        recv_f = [int((mrow[o] * np.array(dims)).sum()) for o in range(n)]
-        part_recv = torch.empty(sum(recv_f), dtype=torch.float32, device=self.device)
-        self._a2a(part_recv, part_send, recv_f, send_f)
+        send_f = [int((prow[r] * dim_arr).sum()) for r in range(n)]
+        recv_f = [int((mrow[o] * dim_arr).sum()) for o in range(n)]
+        part_recv = torch.empty(max(1, sum(recv_f)), dtype=torch.float32, device=self.device)
+        self._a2a(part_recv[:sum(recv_f)], part_send[:sum(send_f)], recv_f, send_f)
         if outputs is None:
             outputs = [torch.empty((f.output_rows, d), dtype=torch.float32, device=self.device)
                        for f, d in zip(feats, dims)]
-        self.store.route_merge(route, part_recv, outputs, stream)
-        handle = RoundHandle(route, ticket, counts, peer, dims, pools, read_only)
+        self.store.route_merge(route, part_recv, outputs, main)
+        handle = RoundHandle(route, ticket, counts, peer, dims, pools, read_only, tables)
         if read_only:
             self.store.route_release(route)
+            handle.route = None
         return handle, outputs
 
     # --------------------------------------------------------------- push
     def push(self, handle: RoundHandle, gradients, wait: bool = False):
         """Sharded push of this rank's feature gradients (one tensor per feature,
-        shaped like the lookup outputs).  Every rank must call it."""
+        shaped like the lookup outputs).  Every rank must call it.
+
+        The client-side finiteness check (distributed_client.cpp:249) is agreed
+        by every rank on the device (all-reduce of a flag) and consumed by every
+        owner's push on the device, so a non-finite value anywhere rejects the
+        push on every shard (state unchanged, round pushable again or
+        releasable) without a host round trip; with wait=False the rejection is
+        reported by the store's synchronize()."""
         if handle.read_only:
             raise EpsError(INVALID_ARGUMENT, "read-only lookups cannot be pushed")
         torch, n = self.torch, self.n
-        F = len(handle.dims)
-        stream = self._stream()
+        main = self._stream()
         dims = np.array(handle.dims)
         mrow = _rows(handle.counts, handle.poolings)
         prow = _rows(handle.peer_counts, handle.poolings)
         send_f = [int((mrow[o] * dims).sum()) for o in range(n)]
         recv_f = [int((prow[r] * dims).sum()) for r in range(n)]
-        send = torch.empty(sum(send_f), dtype=torch.float32, device=self.device)
+        send = torch.empty(max(1, sum(send_f)), dtype=torch.float32, device=self.device)
         flag = torch.zeros(1, dtype=torch.int32, device=self.device)
-        self.store.route_gather(handle.route, gradients, send, flag, stream)
-        # the client-side finiteness check (distributed_client.cpp:249), agreed by
-        # every rank before any shard applies anything: a rejected push leaves the
-        # round pushable (retry) or releasable, as in the reference
+        self.store.route_gather(handle.route, gradients, send, flag, main)
         self.dist.all_reduce(flag, op=self.dist.ReduceOp.MAX, group=self.group)
-        if int(flag.item()):
-            raise EpsError(INVALID_ARGUMENT, "non-finite gradient")
+        recv = torch.empty(max(1, sum(recv_f)), dtype=torch.float32, device=self.device)
+        self._a2a(recv[:sum(recv_f)], send[:sum(send_f)], recv_f, send_f)
+        # a rejected push with wait=True raises here and keeps the route and the
+        # ticket (push again, or release); an enqueued push releases the route
+        self.store.serve_push(handle.ticket, recv, handle.peer_counts, handle.tables,
+                              handle.poolings, reject=flag, stream=main, wait=wait)
         self.store.route_release(handle.route)
         handle.route = None
-        recv = torch.empty(sum(recv_f), dtype=torch.float32, device=self.device)
-        self._a2a(recv, send, recv_f, send_f)
-        views, ids, fo = [], [], 0
-        for r in range(n):
-            for f in range(F):
-                rows = int(prow[r, f])
-                views.append(recv[fo:fo + rows * int(dims[f])].view(rows, int(dims[f])))
-                ids.append(r * F + f)
-                fo += rows * int(dims[f])
-        self.store.push(handle.ticket, views, features=ids, wait=wait, stream=stream)
-        handle.ticket = None
 
     def release(self, handle: RoundHandle):
         """Abandons a round: frees its route and this shard's ticket (Release)."""

@@ -271,6 +271,32 @@ EPS_B200_EXPORT int eps_b200_route_merge(EpsB200Store* store, uint64_t route, co
 EPS_B200_EXPORT int eps_b200_route_gather(EpsB200Store* store, uint64_t route,
                                           const EpsB200Buffer* gradients, float* send,
                                           uint32_t* nonfinite, void* stream, EpsB200Status* status);
+/* Owner side of a sharded round: ParameterService::Lookup of the combined
+ * request of `requesters` clients (include/eps/parameter_service.hpp:17).
+ * payload (device) holds the words every requester's route_scatter sent to this
+ * shard, requester after requester; peer_counts (host, [requesters][F][2]) the
+ * (keys, kept bags) of each part; tables / poolings (host, [F]) the feature
+ * schema shared by all requesters.  Runs eps_b200_lookup(shard_partial = 1) on
+ * the requesters' features (ids r * F + f), writing the contributions into
+ * `partials` (device), requester after requester, feature after feature, as
+ * [kept bags, dim] (sum/mean) or [keys, dim] (sequence).  *ticket as for
+ * eps_b200_lookup. */
+EPS_B200_EXPORT int eps_b200_serve(EpsB200Store* store, const uint64_t* payload,
+                                   const uint64_t* peer_counts, const uint32_t* tables,
+                                   const uint32_t* poolings, uint32_t requesters,
+                                   uint32_t feature_count, int32_t read_only, float* partials,
+                                   void* stream, uint64_t* ticket, EpsB200Status* status);
+/* Owner side of the push of a served round (ParameterService::Push,
+ * include/eps/parameter_service.hpp:18): gradients (device) hold the rows every
+ * requester's route_gather sent, in the layout of eps_b200_serve's partials.
+ * If `reject` (device u32, may be NULL) is nonzero when the push runs, the push
+ * is rejected on the device as a non-finite input (state unchanged, ticket
+ * live); with wait == 0 that outcome is reported by eps_b200_synchronize. */
+EPS_B200_EXPORT int eps_b200_serve_push(EpsB200Store* store, uint64_t ticket, const float* gradients,
+                                        const uint64_t* peer_counts, const uint32_t* tables,
+                                        const uint32_t* poolings, uint32_t requesters,
+                                        uint32_t feature_count, const uint32_t* reject,
+                                        void* stream, int32_t wait, EpsB200Status* status);
 /* Frees a route (after the work that uses it has been enqueued). */
 EPS_B200_EXPORT int eps_b200_route_release(EpsB200Store* store, uint64_t route, EpsB200Status* status);
 

@@ -224,6 +224,54 @@ class FakeShardStore:
         gs = [by_id[fid].numpy().copy() for *_, fid in rec]
         self.pushed.append((feats, gs))
 
+    def serve(self, payload, peer_counts, tables, poolings, partials, read_only=False,
+              stream=None):
+        """Owner side: parse every requester's payload region and run the shard
+        lookup (ids r * F + f) into `partials`, requester-major."""
+        import torch
+        pay = payload.numpy()
+        n, F = peer_counts.shape[0], len(tables)
+        feats, outs, base, at = [], [], 0, 0
+        for r in range(n):
+            nk = [int(peer_counts[r, f, 0]) for f in range(F)]
+            kb = [int(peer_counts[r, f, 1]) for f in range(F)]
+            k0, o0, l0 = base, base + sum(nk), base + sum(nk) + sum(kb) + F
+            for f in range(F):
+                keys = pay[k0:k0 + nk[f]]
+                offs = pay[o0:o0 + kb[f] + 1]
+                lens = pay[l0:l0 + kb[f]]
+                k0 += nk[f]; o0 += kb[f] + 1; l0 += kb[f]
+                feats.append(type("F", (), dict(table=tables[f], pooling=poolings[f],
+                                                feature=r * F + f,
+                                                keys=torch.from_numpy(keys.copy()),
+                                                offsets=torch.from_numpy(offs.copy()),
+                                                valid_lengths=torch.from_numpy(lens.copy()))))
+                rows = nk[f] if poolings[f] == SEQUENCE else kb[f]
+                D = self.dimension(tables[f])
+                outs.append(partials[at:at + rows * D].view(rows, D))
+                at += rows * D
+            base += sum(nk) + 2 * sum(kb) + F
+        ticket, _ = self.lookup(feats, read_only=read_only, shard_partial=True, outputs=outs)
+        return ticket
+
+    def serve_push(self, ticket, gradients, peer_counts, tables, poolings, reject=None,
+                   stream=None, wait=False):
+        from eps_b200 import EpsError
+        n, F = peer_counts.shape[0], len(tables)
+        if reject is not None and int(reject[0]):
+            if wait:
+                raise EpsError(1, "non-finite gradient")
+            return
+        views, ids, at = [], [], 0
+        for r in range(n):
+            for f in range(F):
+                rows = int(peer_counts[r, f, 0] if poolings[f] == SEQUENCE else peer_counts[r, f, 1])
+                D = self.dimension(tables[f])
+                views.append(gradients[at:at + rows * D].view(rows, D))
+                ids.append(r * F + f)
+                at += rows * D
+        self.push(ticket, views, features=ids)
+
     def release(self, ticket):
         self.tickets.pop(ticket, None)
 

@@ -105,7 +105,7 @@ def _gloo_worker(rank, n, port, steps):
         if rank == 0:
             grads[1][0, 0] = np.inf
         with pytest.raises(eps.EpsError):
-            client.push(handle, [torch.from_numpy(g) for g in grads])
+            client.push(handle, [torch.from_numpy(g) for g in grads], wait=True)
         client.release(handle)
         assert not store.routes and not store.tickets
     finally:
