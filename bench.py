@@ -287,11 +287,22 @@ def run_b200(args):
     if dist:
         # every rank's batch is routed to the owners over NCCL all-to-all
         import importlib
-        client = importlib.import_module("eps_b200.distributed").ShardedClient(store)
-        ids_stream = torch.cuda.Stream(device=dev)   # partition + key exchange overlap the push
+        D = importlib.import_module("eps_b200.distributed")
+        comm = D.NcclComm.from_process_group(local_rank)    # NCCL group calls on our streams
+        comm_in = D.NcclComm.from_process_group(local_rank)  # the prepare phase's exchanges
+        client = D.NativeClient(store, comm, comm_in)        # the round's host side in C++
+        # the next batch's partition + key exchange (prepare) is issued before this
+        # round's push, on a high-priority input stream, as a training loop whose
+        # loader holds the next batch would; every timed step contains exactly one
+        # prepare, one lookup and one push
+        ids_stream = torch.cuda.Stream(device=dev, priority=-1)
+        nxt = [None]
 
         def one_round():
-            handle, _ = client.lookup(feats, outputs=outs, input_stream=ids_stream)
+            if nxt[0] is None:
+                nxt[0] = client.prepare(feats, input_stream=ids_stream)
+            handle, _ = client.lookup_prepared(nxt[0], outputs=outs)
+            nxt[0] = client.prepare(feats, input_stream=ids_stream)
             client.push(handle, grads)
     else:
         lookup = store.prepare_lookup(feats, outs)
@@ -432,6 +443,13 @@ def run_b200(args):
     h2d = sum(f.keys.nbytes + f.offsets.nbytes for f in w.features) + \
         sum(g.nbytes for g in w.gradients)
     d2h = sum(o.nbytes for o in houts) + 36      # pooled outputs + push status
+    if dist:
+        if nxt[0] is not None:
+            client.discard(nxt[0])
+        torch.cuda.synchronize()
+        client.close()
+        comm.close()
+        comm_in.close()
     store.close()
 
     # ---- CPU baseline (rank 0, N = 1): reference CPU path, bounded sample

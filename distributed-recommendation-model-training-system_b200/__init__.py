@@ -103,7 +103,10 @@ ENTRY_POINTS = ("eps_b200_abi_version", "eps_b200_create", "eps_b200_destroy",
                 "eps_b200_optimizer_state", "eps_b200_profile", "eps_b200_stats",
                 "eps_b200_route", "eps_b200_route_scatter", "eps_b200_route_merge",
                 "eps_b200_route_gather", "eps_b200_route_release", "eps_b200_serve",
-                "eps_b200_serve_push")
+                "eps_b200_serve_push", "eps_b200_comm_unique_id", "eps_b200_comm_create",
+                "eps_b200_comm_destroy", "eps_b200_comm_alltoallv", "eps_b200_comm_allreduce_max",
+                "eps_b200_client_create", "eps_b200_client_destroy", "eps_b200_client_prepare",
+                "eps_b200_client_lookup", "eps_b200_client_push", "eps_b200_client_release")
 
 
 def load_library() -> C.CDLL:
@@ -145,8 +148,22 @@ def load_library() -> C.CDLL:
                                    P(C.c_uint64), P(Status)]
     lib.eps_b200_serve_push.argtypes = [vp, C.c_uint64, vp, vp, vp, vp, C.c_uint32, C.c_uint32, vp,
                                         vp, C.c_int32, P(Status)]
+    lib.eps_b200_comm_unique_id.argtypes = [vp, P(Status)]
+    lib.eps_b200_comm_create.argtypes = [C.c_int32, C.c_uint32, C.c_uint32, vp, P(vp), P(Status)]
+    lib.eps_b200_comm_destroy.argtypes = [vp]
+    lib.eps_b200_comm_destroy.restype = None
+    lib.eps_b200_comm_alltoallv.argtypes = [vp, vp, vp, vp, vp, C.c_uint32, vp, P(Status)]
+    lib.eps_b200_comm_allreduce_max.argtypes = [vp, vp, C.c_uint64, vp, P(Status)]
+    lib.eps_b200_client_create.argtypes = [vp, vp, vp, P(vp), P(Status)]
+    lib.eps_b200_client_destroy.argtypes = [vp]
+    lib.eps_b200_client_destroy.restype = None
+    lib.eps_b200_client_prepare.argtypes = [vp, P(Feature), C.c_uint64, vp, P(C.c_uint64), P(Status)]
+    lib.eps_b200_client_lookup.argtypes = [vp, C.c_uint64, P(Buffer), C.c_int32, vp,
+                                           P(C.c_uint64), P(Status)]
+    lib.eps_b200_client_push.argtypes = [vp, C.c_uint64, P(Buffer), vp, C.c_int32, P(Status)]
+    lib.eps_b200_client_release.argtypes = [vp, C.c_uint64, P(Status)]
     for name in ENTRY_POINTS[1:]:
-        if name != "eps_b200_destroy":
+        if name not in ("eps_b200_destroy", "eps_b200_comm_destroy", "eps_b200_client_destroy"):
             getattr(lib, name).restype = C.c_int
     if lib.eps_b200_abi_version() != 1:
         raise ImportError("libeps_b200.so ABI version mismatch")
@@ -463,20 +480,21 @@ class ParameterStore:
             raise EpsError(INVALID_ARGUMENT, "unknown table")
         return self._tables[table].dimension
 
-    def route(self, feats: Sequence[FeatureInput], shard_count: int, stream=None):
-        """Partitions device features by key % shard_count (eps_b200_route).
-        Returns (route id, counts[shard, feature, (keys, kept bags)])."""
+    def route(self, feats: Sequence[FeatureInput], shard_count: int, counts, stream=None):
+        """Partitions device features by key % shard_count (eps_b200_route,
+        asynchronous).  `counts` is a device int64 tensor [shard_count,
+        4 * len(feats) + 1] that receives the per-shard count rows.  Returns the
+        route id."""
         arr, on_device, keep = self._features(feats)
         if not on_device:
             raise EpsError(INVALID_ARGUMENT, "a route needs device inputs")
-        counts = np.zeros((shard_count, len(feats), 2), np.uint64)
         rid = C.c_uint64(0)
         st = Status()
         _check(self.lib.eps_b200_route(self._h, arr, len(feats), shard_count, _stream_ptr(stream),
                                        C.byref(rid), _ptr(counts), C.byref(st)), st)
         self._route_keep = getattr(self, "_route_keep", {})
         self._route_keep[rid.value] = keep
-        return rid.value, counts
+        return rid.value
 
     def route_scatter(self, route: int, payload, stream=None):
         st = Status()

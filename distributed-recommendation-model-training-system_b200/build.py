@@ -21,7 +21,8 @@ INCLUDE = os.path.join(ROOT, "include")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libeps_b200.so")
 
-SOURCES = ["store.cu", "lookup.cu", "sort.cu", "push.cu", "route.cu", "noalloc.cu", "runtime.cu"]
+SOURCES = ["store.cu", "lookup.cu", "sort.cu", "push.cu", "route.cu", "noalloc.cu", "runtime.cu",
+           "comm.cu", "client.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "--fmad=false", "-Xcompiler", "-fPIC",
          "-Xcompiler", "-fvisibility=hidden", "-I", CSRC, "-I", INCLUDE]
@@ -68,7 +69,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
         raise RuntimeError(f"nvcc failed for {failed}")
     if force or _stale(LIB, objs):
         # static cudart: the library needs only the driver (libcuda) at run time
-        cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", LIB, *objs]
+        cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", LIB, *objs, "-ldl"]
         subprocess.check_call(cmd)
     return LIB
 

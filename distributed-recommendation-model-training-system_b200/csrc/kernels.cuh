@@ -141,13 +141,14 @@ struct RouteLaunch {
   unsigned int* bag_map;           // [cells] kept bag -> bag index in its feature
   unsigned int* pos_map;           // [N] shard-ordered key -> position in its feature
   const float* partials;           // merge input, shard-major then feature-major
-  const unsigned long long* part_off;   // [shard_count * feature_count] float offsets
+  unsigned long long* part_off;         // [shard_count * feature_count] float offsets
   float* const* outs;              // [feature_count] merge outputs
   const float* const* grads;       // [feature_count] gradient inputs of the gather
   float* send;                     // gather output (same layout as partials)
   unsigned int* nonfinite;         // gather: set to 1 if any gradient value is not finite
-  const unsigned long long* row_pre;    // [shard_count * feature_count] row prefix
-  unsigned long long row_total;
+  unsigned long long* row_pre;          // [shard_count * feature_count] row prefix
+  unsigned long long* row_total_dev;    // rows of all blocks (device)
+  long long* counts_out;                // [shard_count][4F + 1] count rows (route_layout)
   int has_sequence;
   int vec, group, iters;           // launch shape (see choose_shape)
 };

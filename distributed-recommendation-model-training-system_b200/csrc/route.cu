@@ -192,6 +192,48 @@ __global__ void route_bounds(RouteLaunch p) {
   p.bounds[2 * t + 1] = p.pb[idx];
 }
 
+// One block: the (shard, feature) row blocks of the partial / gradient exchange
+// (part_off: float offsets, row_pre: row prefix, shard-major) and the count rows
+// sent to every shard before the payload: [keys(F) kept(F) interleaved as
+// (keys, kept) per feature | table ids (F) | poolings (F) | error], int64.
+__global__ void __launch_bounds__(1024) route_layout(RouteLaunch p) {
+  __shared__ unsigned s_warp[33];
+  __shared__ unsigned long long s_carry[2];
+  const unsigned F = p.feature_count, cells = p.shard_count * F;
+  if (threadIdx.x == 0) { s_carry[0] = 0; s_carry[1] = 0; }
+  __syncthreads();
+  const unsigned err = *(volatile const unsigned*)p.error;
+  for (unsigned base = 0; base < cells; base += blockDim.x) {
+    const unsigned c = base + threadIdx.x;
+    unsigned rows = 0, floats = 0;
+    if (c < cells) {
+      const unsigned o = c / F, f = c % F;
+      const unsigned* a = p.bounds + 2 * (o * (F + 1) + f);
+      const unsigned keys = a[2] - a[0], kept = a[3] - a[1];
+      const LookupFeature* X = p.features + f;
+      rows = X->pooling == 2 ? keys : kept;
+      floats = rows * X->dim;
+      long long* row = p.counts_out + (unsigned long long)o * (4 * F + 1);
+      row[2 * f] = keys;
+      row[2 * f + 1] = kept;
+      row[2 * F + f] = X->table_rank;        // the table id, in a route's descriptors
+      row[3 * F + f] = X->pooling;
+      if (f == 0) row[4 * F] = err;
+    }
+    unsigned tr, tf;
+    const unsigned er = block_exclusive(rows, s_warp, tr);
+    const unsigned ef = block_exclusive(floats, s_warp, tf);
+    if (c < cells) {
+      p.row_pre[c] = s_carry[0] + er;
+      p.part_off[c] = s_carry[1] + ef;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) { s_carry[0] += tr; s_carry[1] += tf; }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *p.row_total_dev = s_carry[0];
+}
+
 // ---------------------------------------------------------------- scatter
 __device__ __forceinline__ unsigned long long extra_of(const RouteLaunch& p, unsigned o) {
   // u64 words before shard o's keys that are not keys: the offsets and lengths
@@ -373,7 +415,8 @@ __global__ void __launch_bounds__(256) route_gather(RouteLaunch p) {
   const unsigned long long gid = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) / G;
   const unsigned long long ngroups = (gridDim.x * (unsigned long long)blockDim.x) / G;
   const unsigned long long B = p.bag_total;
-  for (unsigned long long r = gid; r < p.row_total; r += ngroups) {
+  const unsigned long long row_total = *p.row_total_dev;
+  for (unsigned long long r = gid; r < row_total; r += ngroups) {
     unsigned lo = 0, hi = blocks;
     while (hi - lo > 1) { const unsigned mid = (lo + hi) >> 1; if (p.row_pre[mid] <= r) lo = mid; else hi = mid; }
     while (lo + 1 < blocks && p.row_pre[lo + 1] <= r) ++lo;
@@ -425,7 +468,8 @@ cudaError_t launch_merge_shape(const RouteLaunch& p, cudaStream_t s) {
 }
 template <int G, int VEC, int ITERS>
 cudaError_t launch_gather_shape(const RouteLaunch& p, cudaStream_t s) {
-  route_gather<G, VEC, ITERS><<<grid_for(std::max(p.row_total, 1ull), 256 / G), 256, 0, s>>>(p);
+  // rows are at most keys + bags (the exact count is read on the device)
+  route_gather<G, VEC, ITERS><<<grid_for(std::max(p.key_total + p.bag_total, 1ull), 256 / G), 256, 0, s>>>(p);
   return cudaGetLastError();
 }
 
@@ -472,12 +516,15 @@ cudaError_t launch_route_count(const RouteLaunch& p, cudaStream_t stream) {
   }
   const unsigned nb = p.shard_count * (p.feature_count + 1);
   route_bounds<<<(nb + 255) / 256, 256, 0, stream>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  route_layout<<<1, 1024, 0, stream>>>(p);
   return cudaGetLastError();
 }
 
 unsigned route_count_launches(const RouteLaunch& p) {
   const unsigned tiles = route_tiles(p.cells);
-  return (p.bag_total ? 1u : 0u) + (tiles ? 2u : 0u) + 2u;
+  return (p.bag_total ? 1u : 0u) + (tiles ? 2u : 0u) + 3u;
 }
 
 cudaError_t launch_route_scatter(const RouteLaunch& p, cudaStream_t stream) {
@@ -492,7 +539,6 @@ cudaError_t launch_route_merge(const RouteLaunch& p, cudaStream_t stream) {
 }
 
 cudaError_t launch_route_gather(const RouteLaunch& p, cudaStream_t stream) {
-  if (!p.row_total && !p.nonfinite) return cudaSuccess;
   EPS_ROUTE_SHAPES(launch_gather_shape)
 }
 

@@ -128,13 +128,13 @@ struct Ticket {
 // A shard partition of one lookup (multi-GPU round), see eps_b200_route.
 struct Route {
   char* slab = nullptr;
+  cudaStream_t last = nullptr;          // stream of the latest call that used the route
   unsigned n = 0, F = 0;
   unsigned long long B = 0, N = 0, cells = 0;
   unsigned tiles = 0;
   std::vector<unsigned> dims, pooling;
   std::vector<unsigned long long> rows;           // [F] output rows (bags or keys)
-  std::vector<unsigned long long> counts;         // [n][F][2] keys, kept bags
-  unsigned long long row_total = 0;
+  unsigned long long* row_total = nullptr;   // device: rows of all (shard, feature) blocks
   int has_sequence = 0;
   LookupFeature* desc = nullptr;
   unsigned *cnt = nullptr, *pk = nullptr, *pb = nullptr, *tile_k = nullptr, *tile_b = nullptr,
@@ -182,8 +182,6 @@ struct EpsB200Store {
   std::map<unsigned long long, Ticket> tickets;
   std::map<unsigned long long, Route> routes;
   unsigned long long next_route = 1;
-  unsigned* route_host = nullptr;           // pinned: bounds + error word of eps_b200_route
-  size_t route_host_words = 0;
   std::deque<unsigned long long> completed_order;
   std::unordered_set<unsigned long long> completed;
   unsigned long long next_ticket = 1;
@@ -289,6 +287,10 @@ struct EpsB200Store {
     return stream;
   }
   void Done(cudaStream_t stream) { Cuda(cudaEventRecord(last_done, stream)); }
+  // Route calls touch no table state, only their inputs and their own slab, so
+  // they run on the caller's stream without joining the store's stream order
+  // (the partition of the next round can then overlap this round's push).
+  cudaStream_t RouteStream(void* s) { return s ? static_cast<cudaStream_t>(s) : own; }
   void Sync(cudaStream_t stream) { Cuda(cudaStreamSynchronize(stream)); }
 
   Table& Get(unsigned id) {
@@ -462,7 +464,6 @@ void eps_b200_destroy(EpsB200Store* s) {
     if (s->own) cudaStreamSynchronize(s->own);
     for (auto& [id, t] : s->tickets) if (t.slab) cudaFree(t.slab);
     for (auto& [id, r] : s->routes) if (r.slab) cudaFree(r.slab);
-    if (s->route_host) cudaFreeHost(s->route_host);
     for (auto& [id, t] : s->tables) {
       cudaFree(t.state); cudaFree(t.updates); cudaFree(t.dtable);
     }
@@ -1322,145 +1323,6 @@ int eps_b200_profile(EpsB200Store* store, int32_t mode, double* phase_ms,
   });
 }
 
-int eps_b200_route(EpsB200Store* store, const EpsB200Feature* features, uint64_t count,
-                   uint32_t shard_count, void* stream_arg, uint64_t* route_out, uint64_t* counts,
-                   EpsB200Status* status) {
-  return Boundary(status, [&] {
-    auto& s = *Checked(store);
-    Require(features && route_out && counts && count > 0 && count <= kMaxFeatures,
-            "invalid native feature count");
-    Require(shard_count >= 1 && shard_count <= 32, "route shard count must be 1 .. 32");
-    std::lock_guard lock(s.mutex);
-    s.Activate();
-    Route r;
-    r.n = shard_count;
-    r.F = (unsigned)count;
-    std::vector<LookupFeature> desc(count);
-    std::unordered_set<unsigned> ids;
-    for (uint64_t i = 0; i < count; ++i) {
-      const auto& f = features[i];
-      Require(ids.insert(f.feature).second, "duplicate feature ID");
-      const Table& t = s.Get(f.table);
-      Require(f.pooling <= 2, "unsupported pooling mode");
-      Require(f.offset_count >= 1 && f.offsets, "invalid bag offsets");
-      Require(f.offset_count > 1 || f.key_count == 0, "invalid bag offsets");
-      Require(!f.key_count || f.keys, "null feature keys");
-      const unsigned long long rows = f.pooling == 2 ? f.key_count : f.offset_count - 1;
-      Require(rows < (1ull << kRowBits) && f.key_count < (1ull << 31),
-              "feature exceeds the per-feature row limit", EPS_B200_CAPACITY_EXCEEDED);
-      LookupFeature& L = desc[i];
-      L.keys = reinterpret_cast<const unsigned long long*>(f.keys);
-      L.offsets = reinterpret_cast<const unsigned long long*>(f.offsets);
-      L.lengths = reinterpret_cast<const unsigned long long*>(f.valid_lengths);
-      L.rows = t.def.key_space;
-      L.key_count = f.key_count;
-      L.bag_count = f.offset_count - 1;
-      L.bag_base = r.B;
-      L.dim = t.def.dimension;
-      L.pooling = f.pooling;
-      L.feature_index = (unsigned)i;
-      r.B += L.bag_count;
-      r.N += f.key_count;
-      r.dims.push_back(t.def.dimension);
-      r.pooling.push_back(f.pooling);
-      r.rows.push_back(rows);
-      r.has_sequence |= f.pooling == 2;
-    }
-    r.cells = (unsigned long long)r.n * r.B;
-    Require(r.N < (1ull << 32) && r.cells < (1ull << 32), "route exceeds the occurrence limit",
-            EPS_B200_CAPACITY_EXCEEDED);
-    r.tiles = route_tiles(r.cells);
-    const size_t nb = (size_t)r.n * (r.F + 1) * 2;
-    Carver c;
-    const size_t at_desc = c.take<LookupFeature>(count);
-    const size_t at_cnt = c.take<unsigned>(r.cells);
-    const size_t at_pk = c.take<unsigned>(r.cells + 1);
-    const size_t at_pb = c.take<unsigned>(r.cells + 1);
-    const size_t at_tk = c.take<unsigned>(r.tiles);
-    const size_t at_tb = c.take<unsigned>(r.tiles);
-    const size_t at_bounds = c.take<unsigned>(nb + 1);   // + error word
-    const size_t at_bag = c.take<unsigned>(r.cells);
-    const size_t at_pos = c.take<unsigned>(r.N);
-    const size_t at_poff = c.take<unsigned long long>((size_t)r.n * r.F);
-    const size_t at_rpre = c.take<unsigned long long>((size_t)r.n * r.F);
-    const size_t at_outs = c.take<float*>(count);
-    const size_t at_grads = c.take<float*>(count);
-    if (s.route_host_words < nb + 1) {
-      if (s.route_host) Cuda(cudaFreeHost(s.route_host));
-      s.route_host = nullptr;
-      s.route_host_words = 0;
-      Cuda(cudaMallocHost(reinterpret_cast<void**>(&s.route_host), (nb + 1) * sizeof(unsigned)));
-      s.route_host_words = nb + 1;
-    }
-    cudaStream_t stream = s.Use(stream_arg);
-    Cuda(cudaMallocAsync(reinterpret_cast<void**>(&r.slab), std::max<size_t>(c.offset, 256), stream));
-    try {
-      auto P = [&](size_t at) { return r.slab + at; };
-      r.desc = reinterpret_cast<LookupFeature*>(P(at_desc));
-      r.cnt = reinterpret_cast<unsigned*>(P(at_cnt));
-      r.pk = reinterpret_cast<unsigned*>(P(at_pk));
-      r.pb = reinterpret_cast<unsigned*>(P(at_pb));
-      r.tile_k = reinterpret_cast<unsigned*>(P(at_tk));
-      r.tile_b = reinterpret_cast<unsigned*>(P(at_tb));
-      r.bounds = reinterpret_cast<unsigned*>(P(at_bounds));
-      r.error = r.bounds + nb;
-      r.bag_map = reinterpret_cast<unsigned*>(P(at_bag));
-      r.pos_map = reinterpret_cast<unsigned*>(P(at_pos));
-      r.part_off = reinterpret_cast<unsigned long long*>(P(at_poff));
-      r.row_pre = reinterpret_cast<unsigned long long*>(P(at_rpre));
-      r.outs = reinterpret_cast<float**>(P(at_outs));
-      r.grads = reinterpret_cast<const float**>(P(at_grads));
-      Cuda(cudaMemsetAsync(r.error, 0, sizeof(unsigned), stream));
-      s.Stage(r.desc, desc.data(), count * sizeof(LookupFeature), stream);
-      RouteLaunch lp{};
-      lp.features = r.desc;
-      lp.feature_count = r.F;
-      lp.shard_count = r.n;
-      lp.bag_total = r.B;
-      lp.key_total = r.N;
-      lp.cells = r.cells;
-      lp.tiles = r.tiles;
-      lp.cnt = r.cnt; lp.pk = r.pk; lp.pb = r.pb; lp.tile_k = r.tile_k; lp.tile_b = r.tile_b;
-      lp.bounds = r.bounds;
-      lp.error = r.error;
-      Cuda(launch_route_count(lp, stream));
-      s.stats.kernel_launches += route_count_launches(lp);
-      Cuda(cudaMemcpyAsync(s.route_host, r.bounds, (nb + 1) * sizeof(unsigned),
-                           cudaMemcpyDeviceToHost, stream));
-      s.Done(stream);
-      s.Sync(stream);
-      const unsigned err = s.route_host[nb];
-      Require(!err, EpsB200Store::LookupMessage(err).c_str());
-      // counts, and the (shard, feature) row blocks of the partial / gradient exchange
-      r.counts.assign((size_t)r.n * r.F * 2, 0);
-      std::vector<unsigned long long> part_off((size_t)r.n * r.F), row_pre((size_t)r.n * r.F);
-      unsigned long long floats = 0;
-      for (unsigned o = 0; o < r.n; ++o)
-        for (unsigned f = 0; f < r.F; ++f) {
-          const unsigned* a = s.route_host + 2 * ((size_t)o * (r.F + 1) + f);
-          const unsigned long long keys = a[2] - a[0], kept = a[3] - a[1];
-          r.counts[2 * ((size_t)o * r.F + f)] = keys;
-          r.counts[2 * ((size_t)o * r.F + f) + 1] = kept;
-          const unsigned long long rows = r.pooling[f] == 2 ? keys : kept;
-          part_off[(size_t)o * r.F + f] = floats;
-          row_pre[(size_t)o * r.F + f] = r.row_total;
-          floats += rows * r.dims[f];
-          r.row_total += rows;
-        }
-      s.Stage(r.part_off, part_off.data(), part_off.size() * 8, stream);
-      s.Stage(r.row_pre, row_pre.data(), row_pre.size() * 8, stream);
-      s.Done(stream);
-      std::memcpy(counts, r.counts.data(), r.counts.size() * 8);
-    } catch (...) {
-      cudaFreeAsync(r.slab, stream);
-      throw;
-    }
-    const unsigned long long id = s.next_route++;
-    s.routes.emplace(id, std::move(r));
-    *route_out = id;
-  });
-}
-
 namespace {
 Route& GetRoute(EpsB200Store& s, uint64_t id) {
   auto it = s.routes.find(id);
@@ -1483,12 +1345,119 @@ RouteLaunch RouteParams(const Route& r) {
   lp.pos_map = r.pos_map;
   lp.part_off = r.part_off;
   lp.row_pre = r.row_pre;
-  lp.row_total = r.row_total;
+  lp.row_total_dev = r.row_total;
   lp.has_sequence = r.has_sequence;
   return lp;
 }
 bool Aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 }  // namespace
+
+int eps_b200_route(EpsB200Store* store, const EpsB200Feature* features, uint64_t count,
+                   uint32_t shard_count, void* stream_arg, uint64_t* route_out, int64_t* counts,
+                   EpsB200Status* status) {
+  return Boundary(status, [&] {
+    auto& s = *Checked(store);
+    Require(features && route_out && counts && count > 0 && count <= kMaxFeatures,
+            "invalid native feature count");
+    Require(shard_count >= 1 && shard_count <= 32 && shard_count * count <= kMaxFeatures,
+            "route shard count must be 1 .. 32, with shards x features <= 1024");
+    std::lock_guard lock(s.mutex);
+    s.Activate();
+    Route r;
+    r.n = shard_count;
+    r.F = (unsigned)count;
+    std::vector<LookupFeature> desc(count);
+    std::unordered_set<unsigned> ids;
+    unsigned dim_max = 1;
+    for (uint64_t i = 0; i < count; ++i) {
+      const auto& f = features[i];
+      Require(ids.insert(f.feature).second, "duplicate feature ID");
+      const Table& t = s.Get(f.table);
+      Require(f.pooling <= 2, "unsupported pooling mode");
+      Require(f.offset_count >= 1 && f.offsets, "invalid bag offsets");
+      Require(f.offset_count > 1 || f.key_count == 0, "invalid bag offsets");
+      Require(!f.key_count || f.keys, "null feature keys");
+      const unsigned long long rows = f.pooling == 2 ? f.key_count : f.offset_count - 1;
+      Require(rows < (1ull << kRowBits) && f.key_count < (1ull << 31),
+              "feature exceeds the per-feature row limit", EPS_B200_CAPACITY_EXCEEDED);
+      LookupFeature& L = desc[i];
+      L.keys = reinterpret_cast<const unsigned long long*>(f.keys);
+      L.offsets = reinterpret_cast<const unsigned long long*>(f.offsets);
+      L.lengths = reinterpret_cast<const unsigned long long*>(f.valid_lengths);
+      L.rows = t.def.key_space;
+      L.key_count = f.key_count;
+      L.bag_count = f.offset_count - 1;
+      L.bag_base = r.B;
+      L.dim = t.def.dimension;
+      L.pooling = f.pooling;
+      L.table_rank = f.table;            // a route's descriptors carry the table id
+      L.feature_index = (unsigned)i;
+      r.B += L.bag_count;
+      r.N += f.key_count;
+      r.dims.push_back(t.def.dimension);
+      r.pooling.push_back(f.pooling);
+      r.rows.push_back(rows);
+      r.has_sequence |= f.pooling == 2;
+      dim_max = std::max(dim_max, t.def.dimension);
+    }
+    r.cells = (unsigned long long)r.n * r.B;
+    Require(r.N < (1ull << 32) && r.cells < (1ull << 32) &&
+            (r.N + r.B) * (unsigned long long)dim_max < (1ull << 32),
+            "route exceeds the occurrence limit", EPS_B200_CAPACITY_EXCEEDED);
+    r.tiles = route_tiles(r.cells);
+    const size_t nb = (size_t)r.n * (r.F + 1) * 2;
+    Carver c;
+    const size_t at_desc = c.take<LookupFeature>(count);
+    const size_t at_cnt = c.take<unsigned>(r.cells);
+    const size_t at_pk = c.take<unsigned>(r.cells + 1);
+    const size_t at_pb = c.take<unsigned>(r.cells + 1);
+    const size_t at_tk = c.take<unsigned>(r.tiles);
+    const size_t at_tb = c.take<unsigned>(r.tiles);
+    const size_t at_bounds = c.take<unsigned>(nb + 1);   // + error word
+    const size_t at_bag = c.take<unsigned>(r.cells);
+    const size_t at_pos = c.take<unsigned>(r.N);
+    const size_t at_poff = c.take<unsigned long long>((size_t)r.n * r.F);
+    const size_t at_rpre = c.take<unsigned long long>((size_t)r.n * r.F + 1);   // + row total
+    const size_t at_outs = c.take<float*>(count);
+    const size_t at_grads = c.take<float*>(count);
+    cudaStream_t stream = s.RouteStream(stream_arg);
+    Cuda(cudaMallocAsync(reinterpret_cast<void**>(&r.slab), std::max<size_t>(c.offset, 256), stream));
+    try {
+      auto P = [&](size_t at) { return r.slab + at; };
+      r.desc = reinterpret_cast<LookupFeature*>(P(at_desc));
+      r.cnt = reinterpret_cast<unsigned*>(P(at_cnt));
+      r.pk = reinterpret_cast<unsigned*>(P(at_pk));
+      r.pb = reinterpret_cast<unsigned*>(P(at_pb));
+      r.tile_k = reinterpret_cast<unsigned*>(P(at_tk));
+      r.tile_b = reinterpret_cast<unsigned*>(P(at_tb));
+      r.bounds = reinterpret_cast<unsigned*>(P(at_bounds));
+      r.error = r.bounds + nb;
+      r.bag_map = reinterpret_cast<unsigned*>(P(at_bag));
+      r.pos_map = reinterpret_cast<unsigned*>(P(at_pos));
+      r.part_off = reinterpret_cast<unsigned long long*>(P(at_poff));
+      r.row_pre = reinterpret_cast<unsigned long long*>(P(at_rpre));
+      r.row_total = r.row_pre + (size_t)r.n * r.F;
+      r.outs = reinterpret_cast<float**>(P(at_outs));
+      r.grads = reinterpret_cast<const float**>(P(at_grads));
+      Cuda(cudaMemsetAsync(r.error, 0, sizeof(unsigned), stream));
+      s.Stage(r.desc, desc.data(), count * sizeof(LookupFeature), stream);
+      RouteLaunch lp = RouteParams(r);
+      lp.tile_k = r.tile_k;
+      lp.tile_b = r.tile_b;
+      lp.counts_out = reinterpret_cast<long long*>(counts);
+      Cuda(launch_route_count(lp, stream));
+      s.stats.kernel_launches += route_count_launches(lp);
+    } catch (...) {
+      cudaFreeAsync(r.slab, stream);
+      throw;
+    }
+    r.last = stream;
+    const unsigned long long id = s.next_route++;
+    s.routes.emplace(id, std::move(r));
+    *route_out = id;
+  });
+}
+
 
 int eps_b200_route_scatter(EpsB200Store* store, uint64_t route, uint64_t* payload, void* stream_arg,
                            EpsB200Status* status) {
@@ -1499,12 +1468,12 @@ int eps_b200_route_scatter(EpsB200Store* store, uint64_t route, uint64_t* payloa
     Route& r = GetRoute(s, route);
     Require(payload != nullptr, "null route payload");
     Require((reinterpret_cast<uintptr_t>(payload) & 7) == 0, "misaligned route payload");
-    cudaStream_t stream = s.Use(stream_arg);
+    cudaStream_t stream = s.RouteStream(stream_arg);
     RouteLaunch lp = RouteParams(r);
     lp.payload = reinterpret_cast<unsigned long long*>(payload);
     Cuda(launch_route_scatter(lp, stream));
     s.stats.kernel_launches += 1;
-    s.Done(stream);
+    r.last = stream;
   });
 }
 
@@ -1516,7 +1485,7 @@ int eps_b200_route_merge(EpsB200Store* store, uint64_t route, const float* parti
     s.Activate();
     Route& r = GetRoute(s, route);
     Require(outputs != nullptr, "null route outputs");
-    Require(partials || r.row_total == 0, "null route partials");
+    Require(partials != nullptr, "null route partials");
     std::vector<float*> outs(r.F);
     bool a16 = Aligned16(partials);
     for (unsigned f = 0; f < r.F; ++f) {
@@ -1527,7 +1496,7 @@ int eps_b200_route_merge(EpsB200Store* store, uint64_t route, const float* parti
       outs[f] = static_cast<float*>(o.data);
       a16 &= Aligned16(o.data);
     }
-    cudaStream_t stream = s.Use(stream_arg);
+    cudaStream_t stream = s.RouteStream(stream_arg);
     s.Stage(r.outs, outs.data(), r.F * sizeof(float*), stream);
     RouteLaunch lp = RouteParams(r);
     lp.partials = partials;
@@ -1537,7 +1506,7 @@ int eps_b200_route_merge(EpsB200Store* store, uint64_t route, const float* parti
       Cuda(launch_route_merge(lp, stream));
       s.stats.kernel_launches += 1;
     }
-    s.Done(stream);
+    r.last = stream;
   });
 }
 
@@ -1549,7 +1518,7 @@ int eps_b200_route_gather(EpsB200Store* store, uint64_t route, const EpsB200Buff
     s.Activate();
     Route& r = GetRoute(s, route);
     Require(gradients != nullptr, "null route gradients");
-    Require(send || r.row_total == 0, "null route send buffer");
+    Require(send != nullptr, "null route send buffer");
     std::vector<const float*> grads(r.F);
     bool a16 = Aligned16(send);
     for (unsigned f = 0; f < r.F; ++f) {
@@ -1560,18 +1529,18 @@ int eps_b200_route_gather(EpsB200Store* store, uint64_t route, const EpsB200Buff
       grads[f] = static_cast<const float*>(g.data);
       a16 &= Aligned16(g.data);
     }
-    cudaStream_t stream = s.Use(stream_arg);
+    cudaStream_t stream = s.RouteStream(stream_arg);
     s.Stage(r.grads, grads.data(), r.F * sizeof(float*), stream);
     RouteLaunch lp = RouteParams(r);
     lp.grads = r.grads;
     lp.send = send;
     lp.nonfinite = nonfinite;
     choose_vec(r.dims, a16, false, &lp.vec, &lp.group, &lp.iters);
-    if (r.row_total || nonfinite) {
+    {
       Cuda(launch_route_gather(lp, stream));
       s.stats.kernel_launches += 1;
     }
-    s.Done(stream);
+    r.last = stream;
   });
 }
 
@@ -1583,8 +1552,9 @@ int eps_b200_route_release(EpsB200Store* store, uint64_t route, EpsB200Status* s
     auto it = s.routes.find(route);
     Require(it != s.routes.end(), "unknown route");
     char* slab = it->second.slab;
+    cudaStream_t last = it->second.last;
     s.routes.erase(it);
-    Cuda(cudaFreeAsync(slab, s.last ? s.last : s.own));
+    Cuda(cudaFreeAsync(slab, last ? last : s.own));
   });
 }
 
@@ -1679,6 +1649,27 @@ int eps_b200_serve_push(EpsB200Store* store, uint64_t ticket, const float* gradi
     if (rc) throw Failure(rc, inner.message);
   });
 }
+
+}  // extern "C"
+
+namespace eps_b200 {
+// Internal queries for the sharded client (client.cu).
+bool store_table_dimension(EpsB200Store* s, unsigned table, unsigned* dim) {
+  if (!s) return false;
+  std::lock_guard lock(s->mutex);
+  auto it = s->tables.find(table);
+  if (it == s->tables.end()) return false;
+  *dim = it->second.def.dimension;
+  return true;
+}
+int store_device(EpsB200Store* s) { return s ? s->opt.device : -1; }
+unsigned store_shard(EpsB200Store* s, unsigned* count) {
+  *count = s->opt.shard_count;
+  return s->opt.shard_id;
+}
+}  // namespace eps_b200
+
+extern "C" {
 
 int eps_b200_stats(EpsB200Store* store, EpsB200Stats* out, EpsB200Status* status) {
   return Boundary(status, [&] {

@@ -232,19 +232,21 @@ EPS_B200_EXPORT int eps_b200_profile(EpsB200Store* store, int32_t mode, double* 
 
 /* ---- Multi-GPU round: the client side of a sharded lookup / push.
  * A route splits device-resident features over `shard_count` shards (one per
- * GPU; 1 .. 32) by key % shard_count:
+ * GPU; 1 .. 32, shards x features <= 1024) by key % shard_count:
  *   PrepareLookupInputs (src/access/prepared_lookup.cpp:47-83) on the device.
  * Shard o's part of feature f keeps the bags that have keys on o, with the
  * original (global) bag lengths as valid lengths, so the shard's
  * eps_b200_lookup(shard_partial = 1) returns the reference's shard contribution
  * for exactly those bags (bags without keys there contribute zeros).
- * counts (host, [shard_count][count][2]) receives per (shard, feature) the
- * number of keys and of kept bags.  The inputs must stay valid until
- * eps_b200_route_release.  Keys must be < the table's key_space.  The call
- * waits for its stream (the counts are needed to size the exchange). */
+ * Asynchronous: `counts` (device, int64 [shard_count][4 * count + 1]) receives,
+ * for every shard o, the row sent to o before the payload: (keys, kept bags)
+ * of every feature, then the features' table ids, then their poolings, then the
+ * input-error bits (nonzero: offsets not monotone from 0 to key_count, a valid
+ * length that differs from the offset difference, or a key >= the table's
+ * key_space).  The inputs must stay valid until eps_b200_route_release. */
 EPS_B200_EXPORT int eps_b200_route(EpsB200Store* store, const EpsB200Feature* features, uint64_t count,
                                    uint32_t shard_count, void* stream, uint64_t* route,
-                                   uint64_t* counts, EpsB200Status* status);
+                                   int64_t* counts, EpsB200Status* status);
 /* Writes the u64 words sent to every shard, shard after shard (what the
  * reference's DistributedClient sends in each shard's LookupRequest,
  * src/client/distributed_client.cpp:96-104): for shard o, the keys of every
@@ -299,6 +301,66 @@ EPS_B200_EXPORT int eps_b200_serve_push(EpsB200Store* store, uint64_t ticket, co
                                         void* stream, int32_t wait, EpsB200Status* status);
 /* Frees a route (after the work that uses it has been enqueued). */
 EPS_B200_EXPORT int eps_b200_route_release(EpsB200Store* store, uint64_t route, EpsB200Status* status);
+
+/* ---- Exchange of a multi-GPU round (no counterpart in the reference, whose
+ * shards talk over BRPC): an NCCL communicator over the round's ranks, one per
+ * GPU, whose calls enqueue NCCL group send/receive straight onto the caller's
+ * stream.  NCCL is loaded at run time (libnccl.so.2); without it these calls
+ * fail with EPS_B200_UNAVAILABLE.  The 128-byte unique id is made by one rank
+ * and handed to all ranks (e.g. over torch.distributed). */
+typedef struct EpsB200Comm EpsB200Comm;
+EPS_B200_EXPORT int eps_b200_comm_unique_id(uint8_t* id, EpsB200Status* status);
+EPS_B200_EXPORT int eps_b200_comm_create(int32_t device, uint32_t rank, uint32_t world,
+                                         const uint8_t* id, EpsB200Comm** out,
+                                         EpsB200Status* status);
+EPS_B200_EXPORT void eps_b200_comm_destroy(EpsB200Comm* comm);
+/* All-to-all with per-peer element counts (send_counts / recv_counts: host,
+ * [world]); peer p's block starts after the blocks of peers 0 .. p-1. */
+EPS_B200_EXPORT int eps_b200_comm_alltoallv(EpsB200Comm* comm, const void* send,
+                                            const uint64_t* send_counts, void* recv,
+                                            const uint64_t* recv_counts, uint32_t elem_bytes,
+                                            void* stream, EpsB200Status* status);
+/* In-place element-wise maximum of `count` u32 over all ranks. */
+EPS_B200_EXPORT int eps_b200_comm_allreduce_max(EpsB200Comm* comm, uint32_t* buf, uint64_t count,
+                                                void* stream, EpsB200Status* status);
+
+/* ---- The client side of a multi-GPU round in one call per phase:
+ * DistributedClient (include/eps/distributed_client.hpp:32-70) over one shard
+ * per GPU, each rank also serving the keys k with k % n == rank from `store`
+ * (created with shard_id = rank, shard_count = n; every table on every rank).
+ * `comm` carries the lookup/push exchanges, `input_comm` (may be NULL: comm)
+ * the prepare exchanges, so that a batch can be prepared while the previous
+ * round's push runs.  One round of n ranks is what a reference shard serves
+ * for one combined request of every rank's features, rank-major.  Every rank
+ * must make the same calls in the same order with the same feature schema;
+ * input errors are reported on every rank before any data moves. */
+typedef struct EpsB200Client EpsB200Client;
+EPS_B200_EXPORT int eps_b200_client_create(EpsB200Store* store, EpsB200Comm* comm,
+                                           EpsB200Comm* input_comm, EpsB200Client** out,
+                                           EpsB200Status* status);
+EPS_B200_EXPORT void eps_b200_client_destroy(EpsB200Client* client);
+/* PrepareLookupInputs + the key exchange (DistributedClient::LookupPrepared's
+ * input), on input_stream; device inputs that stay valid until the lookup.
+ * Waits once, for the partition counts. */
+EPS_B200_EXPORT int eps_b200_client_prepare(EpsB200Client* client, const EpsB200Feature* features,
+                                            uint64_t count, void* input_stream, uint64_t* prepared,
+                                            EpsB200Status* status);
+/* Shard lookup + partial exchange + shard-ordered merge of a prepared batch
+ * into outputs (device, as eps_b200_lookup's), on `stream`.  Unless read_only,
+ * *round receives the handle for eps_b200_client_push. */
+EPS_B200_EXPORT int eps_b200_client_lookup(EpsB200Client* client, uint64_t prepared,
+                                           EpsB200Buffer* outputs, int32_t read_only, void* stream,
+                                           uint64_t* round, EpsB200Status* status);
+/* Gradient exchange + one push per shard (DistributedClient::Push).  A
+ * non-finite value on any rank rejects the push on every shard; with
+ * wait != 0 the rejection is returned here and the round stays pushable or
+ * releasable, with wait == 0 it is reported by eps_b200_synchronize. */
+EPS_B200_EXPORT int eps_b200_client_push(EpsB200Client* client, uint64_t round,
+                                         const EpsB200Buffer* gradients, void* stream, int32_t wait,
+                                         EpsB200Status* status);
+/* Drops a prepared batch or an unpushed round (DistributedClient::Release). */
+EPS_B200_EXPORT int eps_b200_client_release(EpsB200Client* client, uint64_t handle,
+                                            EpsB200Status* status);
 
 /* CpuParameterService::Stats (include/eps/runtime.hpp:134). */
 EPS_B200_EXPORT int eps_b200_stats(EpsB200Store* store, EpsB200Stats* stats, EpsB200Status* status);

@@ -89,38 +89,45 @@ class FakeShardStore:
         return self.weights[table].shape[1]
 
     # ---- route: PrepareLookupInputs with the bags that have keys on each shard
-    def route(self, feats, n, stream=None):
-        from eps_b200 import EpsError
+    def route(self, feats, n, counts, stream=None):
+        """Writes the count rows [n][4F + 1] into `counts` (tables, poolings,
+        input-error bits last) and keeps the partition."""
         F = len(feats)
-        counts = np.zeros((n, F, 2), np.uint64)
-        parts = []                                   # [f][o] -> dict
+        rows = np.zeros((n, 4 * F + 1), np.int64)
+        rows[:, 2 * F:3 * F] = [f.table for f in feats]
+        rows[:, 3 * F:4 * F] = [f.pooling for f in feats]
+        parts, bits = [], 0
         for fi, f in enumerate(feats):
             keys = f.keys.numpy().astype(np.uint64)
             offs = f.offsets.numpy().astype(np.uint64)
             space = self.weights[f.table].shape[0]
             if offs[0] != 0 or offs[-1] != len(keys) or np.any(np.diff(offs.astype(np.int64)) < 0):
-                raise EpsError(1, "invalid bag offsets")
+                bits |= 1
             if np.any(keys >= space):
-                raise EpsError(1, "key outside the table")
+                bits |= 2
             per = [dict(keys=[], pos=[], kept=[], kept_len=[], kept_end=[]) for _ in range(n)]
-            for b in range(len(offs) - 1):
-                for i in range(int(offs[b]), int(offs[b + 1])):
-                    o = int(keys[i] % n)
-                    per[o]["keys"].append(int(keys[i]))
-                    per[o]["pos"].append(i)
-                for o in range(n):
-                    got = len(per[o]["keys"]) - (per[o]["kept_end"][-1] if per[o]["kept_end"] else 0)
-                    if got:
-                        per[o]["kept"].append(b)
-                        per[o]["kept_len"].append(int(offs[b + 1] - offs[b]))
-                        per[o]["kept_end"].append(len(per[o]["keys"]))
+            if not bits:
+                for b in range(len(offs) - 1):
+                    for i in range(int(offs[b]), int(offs[b + 1])):
+                        o = int(keys[i] % n)
+                        per[o]["keys"].append(int(keys[i]))
+                        per[o]["pos"].append(i)
+                    for o in range(n):
+                        got = len(per[o]["keys"]) - (per[o]["kept_end"][-1] if per[o]["kept_end"] else 0)
+                        if got:
+                            per[o]["kept"].append(b)
+                            per[o]["kept_len"].append(int(offs[b + 1] - offs[b]))
+                            per[o]["kept_end"].append(len(per[o]["keys"]))
             for o in range(n):
-                counts[o, fi] = (len(per[o]["keys"]), len(per[o]["kept"]))
+                rows[o, 2 * fi] = len(per[o]["keys"])
+                rows[o, 2 * fi + 1] = len(per[o]["kept"])
             parts.append(per)
+        rows[:, 4 * F] = bits
+        counts.copy_(__import__("torch").from_numpy(rows))
         rid = self._next
         self._next += 1
         self.routes[rid] = dict(feats=feats, parts=parts, n=n)
-        return rid, counts
+        return rid
 
     def route_scatter(self, rid, payload, stream=None):
         r = self.routes[rid]

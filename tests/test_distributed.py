@@ -198,7 +198,7 @@ def test_sharded_round_three_ranks_one_gpu():
 
 
 # ------------------------------------------------------------ GPU, NCCL ranks
-def _nccl_worker(rank, n, port, steps):
+def _nccl_worker(rank, n, port, steps, kind):
     import datetime
     import torch
     import torch.distributed as dist
@@ -217,11 +217,37 @@ def _nccl_worker(rank, n, port, steps):
             outputs[step] = oracle.lookup(cf, shards=n)
             assert oracle.push(cf, cg) == 0
         store = _make_store(eps, rank, n, device=rank)
-        client = D.ShardedClient(store)
+        comm = D.NcclComm.from_process_group(rank)
+        comm_in = D.NcclComm.from_process_group(rank)
+        if kind == "native":
+            client = D.NativeClient(store, comm, comm_in)
+        else:
+            client = D.ShardedClient(store, comm=comm, input_comm=comm_in)
         _rank_body(eps, D, store, client, rank, n, steps, f"cuda:{rank}", outputs,
                    threading.Lock())
         store.synchronize()
         _check_state(store, oracle, rank, n)
+        # an invalid key on one rank is rejected on every rank before any exchange
+        feats, grads = H.make_batch(rank, 99)
+        if rank == 1:
+            feats[0].keys[0] = 10 ** 6
+        with pytest.raises(eps.EpsError):
+            client.lookup(_inputs(eps, feats, f"cuda:{rank}"))
+        # a non-finite gradient on one rank rejects the push on every shard
+        feats, grads = H.make_batch(rank, 100)
+        handle, outs = client.lookup(_inputs(eps, feats, f"cuda:{rank}"))
+        if rank == 0:
+            grads[1][0, 0] = np.nan
+        with pytest.raises(eps.EpsError):
+            client.push(handle, [torch.from_numpy(g).cuda(rank) for g in grads], wait=True)
+        client.release(handle)
+        store.synchronize()
+        _check_state(store, oracle, rank, n)            # nothing was applied
+        assert store.stats()["live_tickets"] == 0
+        if kind == "native":
+            client.close()
+        comm.close()
+        comm_in.close()
         store.close()
         dist.barrier()
     finally:
@@ -230,11 +256,14 @@ def _nccl_worker(rank, n, port, steps):
 
 @pytest.mark.gpu
 @pytest.mark.skipif(not gpu_available(), reason="needs a GPU")
-def test_sharded_round_nccl_all_gpus():
+@pytest.mark.parametrize("kind", ["native", "python"])
+def test_sharded_round_nccl_all_gpus(kind):
+    """One process per GPU over NCCL: the C++ client (NativeClient, the measured
+    path) and the Python ShardedClient over the library's NCCL communicator."""
     import torch
     import torch.multiprocessing as mp
     n = torch.cuda.device_count()
     if n < 2:
         pytest.skip("needs at least two GPUs")
     n = min(n, 8)
-    mp.spawn(_nccl_worker, args=(n, _port(), 3), nprocs=n, join=True)
+    mp.spawn(_nccl_worker, args=(n, _port(), 3, kind), nprocs=n, join=True)
