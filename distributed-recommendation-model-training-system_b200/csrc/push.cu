@@ -43,6 +43,13 @@
 
 namespace cg = cooperative_groups;
 
+#ifndef EPS_PUSH_DEPTH_REGS
+#define EPS_PUSH_DEPTH_REGS 16        // registers per lane for gradient rows in flight
+#endif
+#ifndef EPS_PUSH_MIN_BLOCKS
+#define EPS_PUSH_MIN_BLOCKS 4         // resident 256-thread blocks per SM (C <= 4)
+#endif
+
 namespace eps_b200 {
 namespace {
 
@@ -141,61 +148,75 @@ __global__ void __launch_bounds__(256) push_prescan(PushLaunch p, PushTable* tab
 }
 
 // ------------------------------------------------------ reduction helpers
-// Sum of gradient references [s0, s1) (all with the same key), serially in
-// order, by the G lanes of `grp` (each lane owns VEC*ITERS columns).
+// Sum of the gradient references [s0, s1) of one coalesced row (all with the
+// same key), serially in occurrence order, by the G lanes of `grp` (each lane
+// owns VEC*ITERS columns), bit-exact with the reference's serial loop.
+// The gradient sources of the features are staged in shared memory (row
+// pointer and scale index without dependent descriptor loads); up to
+// EPS_PUSH_DEPTH_REGS / C gradient rows are in flight; rows past the end add
+// -0.0f (the identity).
 template <int G, int VEC, int ITERS, typename Grp>
-__device__ __forceinline__ void reduce_range(const Grp& grp, const PushLaunch& p,
-                                             unsigned long long s0, unsigned long long s1,
-                                             unsigned D, float (&acc)[VEC * ITERS]) {
+__device__ __forceinline__ void reduce_staged(const Grp& grp, const PushLaunch& p,
+                                              const float* const* s_grad,
+                                              const unsigned long long* s_sbase,
+                                              unsigned long long s0, unsigned long long s1,
+                                              unsigned D, float (&acc)[VEC * ITERS]) {
   constexpr int C = VEC * ITERS;
-  constexpr int DEPTH = C <= 4 ? 4 : 2;
+  constexpr int DEPTH = G < EPS_PUSH_DEPTH_REGS / C ? G : (EPS_PUSH_DEPTH_REGS / C > 0 ? EPS_PUSH_DEPTH_REGS / C : 1);
   const unsigned gl = grp.thread_rank();
 #pragma unroll
   for (int k = 0; k < C; ++k) acc[k] = 0.0f;
   for (unsigned long long c0 = s0; c0 < s1; c0 += G) {
     const unsigned long long i = c0 + gl;
-    unsigned long long gp = 0;
-    float sc = 0.0f;
+    const float* rowp = nullptr;
+    float sc = 1.0f;
     if (i < s1) {
       const unsigned src = __ldg(p.srcs + i);
       const unsigned f = src >> kRowBits;
       const unsigned r = src & ((1u << kRowBits) - 1u);
-      const PushFeature* F = p.features + f;
-      const float* g = reinterpret_cast<const float*>(__ldg(reinterpret_cast<const unsigned long long*>(&F->grad)));
-      gp = reinterpret_cast<unsigned long long>(g + (unsigned long long)r * D);
-      sc = __ldg(p.row_scale + __ldg(&F->scale_base) + r);
+      rowp = s_grad[f] + (unsigned long long)r * D;
+      sc = __ldg(p.row_scale + s_sbase[f] + r);
     }
     const int cnt = (int)min((unsigned long long)G, s1 - c0);
+#pragma unroll 1
     for (int j0 = 0; j0 < cnt; j0 += DEPTH) {
       float x[DEPTH][C];
-      float s[DEPTH];
+      float sv[DEPTH];
 #pragma unroll
       for (int u = 0; u < DEPTH; ++u) {
-        const unsigned long long q = grp.shfl(gp, (j0 + u) & (G - 1));
-        s[u] = grp.shfl(sc, (j0 + u) & (G - 1));
+        const float* q = grp.shfl(rowp, (j0 + u) & (G - 1));
+        sv[u] = grp.shfl(sc, (j0 + u) & (G - 1));
         const bool use = j0 + u < cnt;
 #pragma unroll
         for (int it = 0; it < ITERS; ++it) {
           const unsigned col = (it * G + gl) * VEC;
           float t[VEC];
-          if (use && col < D) load_vec<VEC>(reinterpret_cast<const float*>(q) + col, t);
+          if (use && col < D) load_vec<VEC>(q + col, t);
           else {
 #pragma unroll
-            for (int v = 0; v < VEC; ++v) t[v] = 0.0f;
+            for (int v = 0; v < VEC; ++v) t[v] = -0.0f;
           }
 #pragma unroll
           for (int v = 0; v < VEC; ++v) x[u][it * VEC + v] = t[v];
         }
       }
+      // batch_access.cpp:118: dest += src * scale, in occurrence order
 #pragma unroll
-      for (int u = 0; u < DEPTH; ++u) {
-        if (j0 + u >= cnt) break;
-        // batch_access.cpp:118: dest += src * scale
+      for (int u = 0; u < DEPTH; ++u)
 #pragma unroll
-        for (int k = 0; k < C; ++k) acc[k] = __fadd_rn(acc[k], __fmul_rn(x[u][k], s[u]));
-      }
+        for (int k = 0; k < C; ++k) acc[k] = __fadd_rn(acc[k], __fmul_rn(x[u][k], sv[u]));
     }
   }
+}
+
+// Stages every feature's gradient pointer and row-scale base in shared memory.
+__device__ __forceinline__ void stage_features(const PushLaunch& p, const float** s_grad,
+                                               unsigned long long* s_sbase) {
+  for (unsigned f = threadIdx.x; f < p.feature_count; f += blockDim.x) {
+    s_grad[f] = p.features[f].grad;
+    s_sbase[f] = p.features[f].scale_base;
+  }
+  __syncthreads();
 }
 
 template <int G, int VEC, int ITERS>
@@ -273,55 +294,83 @@ __device__ __forceinline__ KeyT slot_mask_of(unsigned slot_bits) {
 }
 
 // --------------------------------------------------------------------- rows
+// A warp takes 32 consecutive coalesced rows at a time: their bounds and keys
+// are fetched with one load per lane into shared memory, then its groups of G
+// lanes handle the rows round-robin.  A row with at most long_run occurrences
+// is reduced and updated in place (its [w|m|v] and counter loads issued before
+// the reduction); a longer row reserves its pieces for push_pieces/push_long.
 template <int G, int VEC, int ITERS, typename KeyT>
-__global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? 4 : 2) push_rows(PushLaunch p, int pass) {
+__global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? EPS_PUSH_MIN_BLOCKS : 2) push_rows(PushLaunch p, int pass) {
+  __shared__ const float* s_grad[kMaxFeatures];
+  __shared__ unsigned long long s_sbase[kMaxFeatures];
+  __shared__ unsigned s_seg[8][33];
+  __shared__ KeyT s_key[8][32];
   const Role R = role(p.control, pass);
   if (!R.run) return;
   constexpr int C = VEC * ITERS;
+  constexpr unsigned GPW = 32 / G;            // groups per warp
+  stage_features(p, s_grad, s_sbase);
   const auto grp = cg::tiled_partition<G>(cg::this_thread_block());
   const unsigned gl = grp.thread_rank();
+  const unsigned lane = threadIdx.x & 31, wib = threadIdx.x >> 5, gw = lane / G;
   const unsigned U = *(volatile const unsigned*)p.seg_total;
-  const unsigned long long gid = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) / G;
-  const unsigned long long ngroups = (gridDim.x * (unsigned long long)blockDim.x) / G;
+  const unsigned long long warp = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) >> 5;
+  const unsigned long long nwarps = (gridDim.x * (unsigned long long)blockDim.x) >> 5;
   const KeyT smask = slot_mask_of<KeyT>(p.slot_bits);
   const bool work = R.apply || R.validate;
   unsigned bits = 0;
   int cur_tr = -1;
   unsigned cur_max = 0;
-  for (unsigned long long u = gid; u < U; u += ngroups) {
-    const unsigned s0 = __ldg(p.seg_start + u), s1 = __ldg(p.seg_start + u + 1);
-    const unsigned len = s1 - s0;
-    const KeyT K = key_at<KeyT>(p.keys, s0);
-    const unsigned tr = (unsigned)(K >> p.slot_bits);
-    if (tr >= p.table_count) continue;
-    const PushTable& T = p.tables[tr];
-    const unsigned D = T.dim;
-    const unsigned long long slot = (unsigned long long)(K & smask);
-    if (len <= p.long_run) {
-      if (!work) continue;
-      float* row = T.state + slot * 3ull * D;
-      float w[C], m[C], v[C], g[C];
-      load_state<G, VEC, ITERS>(gl, row, D, w, m, v);   // issued before the reduction
-      reduce_range<G, VEC, ITERS>(grp, p, s0, s1, D, g);
-      if ((int)tr != cur_tr) {
-        if (R.apply) flush_absmax(grp, p, cur_tr, cur_max);
-        cur_tr = (int)tr; cur_max = 0;
+  for (unsigned long long base = warp * 32; base < U; base += nwarps * 32) {
+    const unsigned nseg = (unsigned)min(32ull, U - base);
+    {
+      const unsigned long long idx = base + lane;
+      if (lane < nseg) {
+        const unsigned st = __ldg(p.seg_start + idx);
+        s_seg[wib][lane] = st;
+        s_key[wib][lane] = key_at<KeyT>(p.keys, st);
       }
-      bits |= adam_row<G, VEC, ITERS>(gl, T, row, D, g, w, m, v, R.apply, R.validate, &cur_max);
-      if (R.apply && gl == 0) T.updates[slot] += 1ull;
-    } else if (R.partials) {
-      // a long row: reserve contiguous piece slots, remember the row
-      const unsigned np = (len + kPiece - 1) / kPiece;
-      unsigned base = 0;
-      if (gl == 0) {
-        base = atomicAdd(&p.control->piece_count, np);
-        const unsigned rec = atomicAdd(&p.control->long_count, 1u);
-        p.records[rec] = LongRecord{(unsigned long long)K, base, np};
-      }
-      base = grp.shfl(base, 0);
-      for (unsigned k = gl; k < np; k += G)
-        p.pieces[base + k] = make_uint2(s0 + k * kPiece, min((unsigned)kPiece, len - k * kPiece));
+      if (lane == nseg - 1) s_seg[wib][nseg] = __ldg(p.seg_start + idx + 1);
     }
+    __syncwarp();
+    for (unsigned j = gw; j < nseg; j += GPW) {
+      const unsigned s0 = s_seg[wib][j], s1 = s_seg[wib][j + 1];
+      const unsigned len = s1 - s0;
+      const KeyT K = s_key[wib][j];
+      const unsigned tr = (unsigned)(K >> p.slot_bits);
+      if (tr >= p.table_count) continue;
+      const PushTable& T = p.tables[tr];
+      const unsigned D = T.dim;
+      const unsigned long long slot = (unsigned long long)(K & smask);
+      if (len <= p.long_run) {
+        if (!work) continue;
+        float* row = T.state + slot * 3ull * D;
+        float w[C], m[C], v[C], g[C];
+        unsigned long long upd = 0;
+        if (R.apply && gl == 0) upd = T.updates[slot];
+        load_state<G, VEC, ITERS>(gl, row, D, w, m, v);   // issued before the reduction
+        reduce_staged<G, VEC, ITERS>(grp, p, s_grad, s_sbase, s0, s1, D, g);
+        if ((int)tr != cur_tr) {
+          if (R.apply) flush_absmax(grp, p, cur_tr, cur_max);
+          cur_tr = (int)tr; cur_max = 0;
+        }
+        bits |= adam_row<G, VEC, ITERS>(gl, T, row, D, g, w, m, v, R.apply, R.validate, &cur_max);
+        if (R.apply && gl == 0) T.updates[slot] = upd + 1ull;
+      } else if (R.partials) {
+        // a long row: reserve contiguous piece slots, remember the row
+        const unsigned np = (len + kPiece - 1) / kPiece;
+        unsigned pbase = 0;
+        if (gl == 0) {
+          pbase = atomicAdd(&p.control->piece_count, np);
+          const unsigned rec = atomicAdd(&p.control->long_count, 1u);
+          p.records[rec] = LongRecord{(unsigned long long)K, pbase, np};
+        }
+        pbase = grp.shfl(pbase, 0);
+        for (unsigned k = gl; k < np; k += G)
+          p.pieces[pbase + k] = make_uint2(s0 + k * kPiece, min((unsigned)kPiece, len - k * kPiece));
+      }
+    }
+    __syncwarp();
   }
   bits = cg::reduce(grp, bits, cg::bit_or<unsigned>());
   if (gl == 0 && bits) atomicOr(&p.control->reject_bits, bits);
@@ -330,10 +379,13 @@ __global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? 4 : 2) push_rows(Pus
 
 // ------------------------------------------------------------------- pieces
 template <int G, int VEC, int ITERS, typename KeyT>
-__global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? 4 : 2) push_pieces(PushLaunch p, int pass) {
+__global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? EPS_PUSH_MIN_BLOCKS : 2) push_pieces(PushLaunch p, int pass) {
+  __shared__ const float* s_grad[kMaxFeatures];
+  __shared__ unsigned long long s_sbase[kMaxFeatures];
   const Role R = role(p.control, pass);
   if (!R.run || !R.partials) return;
   constexpr int C = VEC * ITERS;
+  stage_features(p, s_grad, s_sbase);
   const auto grp = cg::tiled_partition<G>(cg::this_thread_block());
   const unsigned gl = grp.thread_rank();
   const unsigned count = *(volatile const unsigned*)&p.control->piece_count;
@@ -346,7 +398,7 @@ __global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? 4 : 2) push_pieces(P
     if (tr >= p.table_count) continue;
     const unsigned D = p.tables[tr].dim;
     float acc[C];
-    reduce_range<G, VEC, ITERS>(grp, p, pc.x, (unsigned long long)pc.x + pc.y, D, acc);
+    reduce_staged<G, VEC, ITERS>(grp, p, s_grad, s_sbase, pc.x, (unsigned long long)pc.x + pc.y, D, acc);
 #pragma unroll
     for (int it = 0; it < ITERS; ++it) {
       const unsigned col = (it * G + gl) * VEC;
@@ -479,7 +531,7 @@ __global__ void push_finalize(PushLaunch p) {
 template <int G, int VEC, int ITERS, typename KeyT>
 cudaError_t run_apply(const PushLaunch& p, cudaStream_t s) {
   if (!p.n) return cudaSuccess;
-  constexpr unsigned blocks_per_sm = (VEC * ITERS <= 4) ? 4 : 2;
+  constexpr unsigned blocks_per_sm = (VEC * ITERS <= 4) ? EPS_PUSH_MIN_BLOCKS : 2;
   constexpr unsigned long long groups_per_block = 256 / G;
   const unsigned long long cap = 148ull * blocks_per_sm;
   const unsigned rows_grid = (unsigned)max(1ull, min((p.n + groups_per_block - 1) / groups_per_block, cap));
