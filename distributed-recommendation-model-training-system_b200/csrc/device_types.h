@@ -105,7 +105,10 @@ struct LongRecord {
 };
 
 constexpr int kLongRun = 64;    // rows with more occurrences than this are "long"
-constexpr int kPiece = 64;      // occurrences per piece of a long row
+#ifndef EPS_PIECE
+#define EPS_PIECE 32
+#endif
+constexpr int kPiece = EPS_PIECE;   // occurrences per piece of a long row
 constexpr unsigned int kMaxFeatures = 1024;
 constexpr unsigned int kRowBits = 22;   // gradient row bits in the source code
 

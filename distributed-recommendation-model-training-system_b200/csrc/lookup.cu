@@ -33,10 +33,10 @@ namespace eps_b200 {
 namespace {
 
 #ifndef EPS_LOOKUP_DEPTH_REGS
-#define EPS_LOOKUP_DEPTH_REGS 64     // registers per lane for rows in flight
+#define EPS_LOOKUP_DEPTH_REGS 32     // registers per lane for rows in flight
 #endif
 #ifndef EPS_LOOKUP_MIN_BLOCKS
-#define EPS_LOOKUP_MIN_BLOCKS 2
+#define EPS_LOOKUP_MIN_BLOCKS 3
 #endif
 
 template <int G, int VEC, int ITERS, typename KeyT>

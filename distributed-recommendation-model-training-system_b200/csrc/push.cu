@@ -49,6 +49,12 @@ namespace cg = cooperative_groups;
 #ifndef EPS_PUSH_MIN_BLOCKS
 #define EPS_PUSH_MIN_BLOCKS 4         // resident 256-thread blocks per SM (C <= 4)
 #endif
+#ifndef EPS_PIECE_DEPTH_REGS
+#define EPS_PIECE_DEPTH_REGS 32       // the same for the long rows' pieces
+#endif
+#ifndef EPS_PIECE_MIN_BLOCKS
+#define EPS_PIECE_MIN_BLOCKS 3
+#endif
 
 namespace eps_b200 {
 namespace {
@@ -155,15 +161,36 @@ __global__ void __launch_bounds__(256) push_prescan(PushLaunch p, PushTable* tab
 // pointer and scale index without dependent descriptor loads); up to
 // EPS_PUSH_DEPTH_REGS / C gradient rows are in flight; rows past the end add
 // -0.0f (the identity).
-template <int G, int VEC, int ITERS, typename Grp>
+template <int G, int VEC, int ITERS, int DEPTH_REGS, typename Grp>
 __device__ __forceinline__ void reduce_staged(const Grp& grp, const PushLaunch& p,
                                               const float* const* s_grad,
                                               const unsigned long long* s_sbase,
                                               unsigned long long s0, unsigned long long s1,
                                               unsigned D, float (&acc)[VEC * ITERS]) {
   constexpr int C = VEC * ITERS;
-  constexpr int DEPTH = G < EPS_PUSH_DEPTH_REGS / C ? G : (EPS_PUSH_DEPTH_REGS / C > 0 ? EPS_PUSH_DEPTH_REGS / C : 1);
+  constexpr int DEPTH = G < DEPTH_REGS / C ? G : (DEPTH_REGS / C > 0 ? DEPTH_REGS / C : 1);
   const unsigned gl = grp.thread_rank();
+  if (s1 - s0 == 1) {
+    // a single term (most rows): 0 + src * scale, every lane reading the source
+    const unsigned src = __ldg(p.srcs + s0);
+    const unsigned f = src >> kRowBits;
+    const unsigned r = src & ((1u << kRowBits) - 1u);
+    const float* q = s_grad[f] + (unsigned long long)r * D;
+    const float sc = __ldg(p.row_scale + s_sbase[f] + r);
+#pragma unroll
+    for (int it = 0; it < ITERS; ++it) {
+      const unsigned col = (it * G + gl) * VEC;
+      float t[VEC];
+      if (col < D) load_vec<VEC>(q + col, t);
+      else {
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) t[v] = 0.0f;
+      }
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) acc[it * VEC + v] = __fadd_rn(0.0f, __fmul_rn(t[v], sc));
+    }
+    return;
+  }
 #pragma unroll
   for (int k = 0; k < C; ++k) acc[k] = 0.0f;
   for (unsigned long long c0 = s0; c0 < s1; c0 += G) {
@@ -349,7 +376,7 @@ __global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? EPS_PUSH_MIN_BLOCKS 
         unsigned long long upd = 0;
         if (R.apply && gl == 0) upd = T.updates[slot];
         load_state<G, VEC, ITERS>(gl, row, D, w, m, v);   // issued before the reduction
-        reduce_staged<G, VEC, ITERS>(grp, p, s_grad, s_sbase, s0, s1, D, g);
+        reduce_staged<G, VEC, ITERS, EPS_PUSH_DEPTH_REGS>(grp, p, s_grad, s_sbase, s0, s1, D, g);
         if ((int)tr != cur_tr) {
           if (R.apply) flush_absmax(grp, p, cur_tr, cur_max);
           cur_tr = (int)tr; cur_max = 0;
@@ -379,7 +406,7 @@ __global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? EPS_PUSH_MIN_BLOCKS 
 
 // ------------------------------------------------------------------- pieces
 template <int G, int VEC, int ITERS, typename KeyT>
-__global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? EPS_PUSH_MIN_BLOCKS : 2) push_pieces(PushLaunch p, int pass) {
+__global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? EPS_PIECE_MIN_BLOCKS : 2) push_pieces(PushLaunch p, int pass) {
   __shared__ const float* s_grad[kMaxFeatures];
   __shared__ unsigned long long s_sbase[kMaxFeatures];
   const Role R = role(p.control, pass);
@@ -398,7 +425,8 @@ __global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? EPS_PUSH_MIN_BLOCKS 
     if (tr >= p.table_count) continue;
     const unsigned D = p.tables[tr].dim;
     float acc[C];
-    reduce_staged<G, VEC, ITERS>(grp, p, s_grad, s_sbase, pc.x, (unsigned long long)pc.x + pc.y, D, acc);
+    reduce_staged<G, VEC, ITERS, EPS_PIECE_DEPTH_REGS>(grp, p, s_grad, s_sbase, pc.x,
+                                                       (unsigned long long)pc.x + pc.y, D, acc);
 #pragma unroll
     for (int it = 0; it < ITERS; ++it) {
       const unsigned col = (it * G + gl) * VEC;
@@ -535,8 +563,10 @@ cudaError_t run_apply(const PushLaunch& p, cudaStream_t s) {
   constexpr unsigned long long groups_per_block = 256 / G;
   const unsigned long long cap = 148ull * blocks_per_sm;
   const unsigned rows_grid = (unsigned)max(1ull, min((p.n + groups_per_block - 1) / groups_per_block, cap));
+  constexpr unsigned piece_blocks = (VEC * ITERS <= 4) ? EPS_PIECE_MIN_BLOCKS : 2;
   const unsigned piece_grid =
-      (unsigned)max(1ull, min(((unsigned long long)p.max_pieces + groups_per_block - 1) / groups_per_block, cap));
+      (unsigned)max(1ull, min(((unsigned long long)p.max_pieces + groups_per_block - 1) / groups_per_block,
+                              148ull * piece_blocks));
   const size_t long_smem = (size_t)(kLongThreads / G) * p.dim_max * sizeof(float);
   const unsigned long_grid = 148 * 2;
   push_rows<G, VEC, ITERS, KeyT><<<rows_grid, 256, 0, s>>>(p, 0);
