@@ -120,6 +120,8 @@ struct LookupLaunch {
   int vec, group, iters;           // launch shape (see choose_shape)
 };
 cudaError_t launch_lookup(const LookupLaunch& p, cudaStream_t stream);
+// Occurrence list of a non-read-only lookup (one launch, before the gather).
+cudaError_t launch_emit(const LookupLaunch& p, cudaStream_t stream);
 
 // Shard partition of a lookup (multi-GPU round) and the client-side merge.
 struct RouteLaunch {

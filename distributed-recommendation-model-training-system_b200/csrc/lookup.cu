@@ -183,6 +183,66 @@ __global__ void __launch_bounds__(256, EPS_LOOKUP_MIN_BLOCKS) lookup_kernel(Look
   if (err && gl == 0) atomicOr(p.error, err);
 }
 
+// Occurrence list of a lookup that will be pushed, ahead of (and independent
+// of) the gather, so that the coalescing sort can run concurrently with the
+// gather: one warp per bag writes every occurrence's composite key (table
+// rank, slot) and gradient source (feature, bag or position) and the gradient
+// row scales (1.0f / valid length for mean, src/access/batch_access.cpp:107-108).
+// Validation matches the gather kernel's.
+template <typename KeyT>
+__global__ void __launch_bounds__(256) emit_kernel(LookupLaunch p) {
+  __shared__ unsigned long long s_bag_base[kMaxFeatures + 1];
+  const unsigned fc = p.feature_count;
+  for (unsigned i = threadIdx.x; i < fc; i += blockDim.x) s_bag_base[i] = p.features[i].bag_base;
+  if (threadIdx.x == 0) s_bag_base[fc] = p.bag_total;
+  __syncthreads();
+  const unsigned lane = threadIdx.x & 31;
+  const unsigned long long warp = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) >> 5;
+  const unsigned long long nwarps = (gridDim.x * (unsigned long long)blockDim.x) >> 5;
+  unsigned err = 0;
+  for (unsigned long long g = warp; g < p.bag_total; g += nwarps) {
+    unsigned lo = 0, hi = fc;
+    while (hi - lo > 1) { const unsigned mid = (lo + hi) >> 1; if (s_bag_base[mid] <= g) lo = mid; else hi = mid; }
+    const LookupFeature* F = p.features + lo;
+    const unsigned long long b = g - s_bag_base[lo];
+    const unsigned long long key_count = F->key_count;
+    unsigned long long o = 0;
+    if (lane < 2) o = F->offsets[b + lane];
+    unsigned long long s = __shfl_sync(~0u, o, 0), e = __shfl_sync(~0u, o, 1);
+    if (b == 0 && s != 0) err |= kLookupBadOffsets;
+    if (b + 1 == F->bag_count && e != key_count) err |= kLookupBadOffsets;
+    if (s > e || e > key_count) { err |= kLookupBadOffsets; s = e = 0; }
+    const bool sequence = F->pooling == 2;
+    if (!sequence && lane == 0) {
+      unsigned long long len = e - s;
+      if (F->lengths) {
+        const unsigned long long given = F->lengths[b];
+        if (given < len) err |= kLookupShortLength;
+        len = given;
+      }
+      const bool mean = F->pooling == 1;
+      p.row_scale[F->scale_base + b] = (mean && len) ? __fdiv_rn(1.0f, (float)len) : 1.0f;
+    }
+    const unsigned long long rows = F->rows, occ_base = F->occ_base;
+    const unsigned src_hi = F->feature_index << kRowBits;
+    const KeyT rank_bits = KeyT(F->table_rank) << p.slot_bits;
+    for (unsigned long long i = s + lane; i < e; i += 32) {
+      const unsigned long long key = F->keys[i];
+      unsigned long long sl, sh;
+      if (p.shard_count == 1) { sl = key; sh = 0; }
+      else { sl = key / p.shard_count; sh = key - sl * p.shard_count; }
+      KeyT ck = KeyT(0);
+      if (sh == p.shard_id && sl < rows) ck = rank_bits | KeyT(sl);
+      else err |= kLookupBadKey;
+      static_cast<KeyT*>(p.occ_key)[occ_base + i] = ck;
+      p.occ_src[occ_base + i] = src_hi | (unsigned)(sequence ? i : b);
+      if (sequence) p.row_scale[F->scale_base + i] = 1.0f;
+    }
+  }
+  err = __reduce_or_sync(~0u, err);
+  if (err && lane == 0) atomicOr(p.error, err);
+}
+
 template <int G, int VEC, int ITERS>
 cudaError_t launch_key(const LookupLaunch& p, cudaStream_t s) {
   const unsigned long long groups_per_block = 256 / G;
@@ -194,6 +254,15 @@ cudaError_t launch_key(const LookupLaunch& p, cudaStream_t s) {
   return cudaGetLastError();
 }
 }  // namespace
+
+cudaError_t launch_emit(const LookupLaunch& p, cudaStream_t stream) {
+  if (p.bag_total == 0) return cudaSuccess;
+  const unsigned long long want = (p.bag_total + 7) / 8;
+  const unsigned grid = (unsigned)(want < 148ull * 8 * 2 ? want : 148ull * 8 * 2);
+  if (p.key64) emit_kernel<unsigned long long><<<grid, 256, 0, stream>>>(p);
+  else emit_kernel<unsigned int><<<grid, 256, 0, stream>>>(p);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_lookup(const LookupLaunch& p, cudaStream_t stream) {
   if (p.bag_total == 0) return cudaSuccess;

@@ -176,6 +176,11 @@ struct EpsB200Store {
   EpsB200Options opt{};
   std::mutex mutex;
   cudaStream_t own = nullptr;
+  // the coalescing sort of a lookup runs on `side`, concurrently with the
+  // gather on the caller's stream: fork after the occurrence list, join before
+  // anything that follows the lookup on the caller's stream
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
   cudaStream_t last = nullptr;
   cudaEvent_t last_done = nullptr;
   std::map<unsigned, Table> tables;
@@ -436,6 +441,14 @@ int eps_b200_create(const EpsB200Options* options, EpsB200Store** out, EpsB200St
       // (e.g. framework tensor copies) is ordered before the store's own work
       Cuda(cudaStreamCreateWithFlags(&s->own, cudaStreamDefault));
       Cuda(cudaEventCreateWithFlags(&s->last_done, cudaEventDisableTiming));
+      {
+        // highest priority: the sort's blocks are scheduled ahead of the gather's
+        int lowest = 0, greatest = 0;
+        Cuda(cudaDeviceGetStreamPriorityRange(&lowest, &greatest));
+        Cuda(cudaStreamCreateWithPriority(&s->side, cudaStreamNonBlocking, greatest));
+      }
+      Cuda(cudaEventCreateWithFlags(&s->fork, cudaEventDisableTiming));
+      Cuda(cudaEventCreateWithFlags(&s->join, cudaEventDisableTiming));
       // one status slot per live ticket plus a scratch slot (index max_live_tickets)
       Cuda(cudaMallocHost(&s->host_status, sizeof(HostStatus) * (s->opt.max_live_tickets + 1)));
       std::memset(s->host_status, 0, sizeof(HostStatus) * (s->opt.max_live_tickets + 1));
@@ -476,6 +489,9 @@ void eps_b200_destroy(EpsB200Store* s) {
     if (s->sticky_error) cudaFree(s->sticky_error);
     if (s->host_status) cudaFreeHost(s->host_status);
     if (s->last_done) cudaEventDestroy(s->last_done);
+    if (s->side) { cudaStreamSynchronize(s->side); cudaStreamDestroy(s->side); }
+    if (s->fork) cudaEventDestroy(s->fork);
+    if (s->join) cudaEventDestroy(s->join);
     if (s->own) cudaStreamDestroy(s->own);
   } catch (...) {
   }
@@ -746,21 +762,33 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         lp.row_scale = reinterpret_cast<float*>(P(at_scale));
       }
       cudaEvent_t ev = s.Begin(stream);
-      Cuda(launch_lookup(lp, stream));
-      s.End(EPS_B200_PHASE_LOOKUP, ev, stream, bag_base ? 1u : 0u);
       if (!read_only) {
+        // the occurrence list first; the gather below does not emit, and the
+        // sort (histograms, digit passes, segment compaction) runs on the side
+        // stream concurrently with the gather
+        lp.emit = 0;
+        Cuda(launch_emit(lp, stream));
+        Cuda(cudaEventRecord(s.fork, stream));
+      }
+      Cuda(launch_lookup(lp, stream));
+      s.End(EPS_B200_PHASE_LOOKUP, ev, stream, (bag_base ? 1u : 0u) + (!read_only && bag_base ? 1u : 0u));
+      if (!read_only) {
+        cudaStream_t sort_stream = s.side;
+        Cuda(cudaStreamWaitEvent(s.side, s.fork, 0));
         SortLaunch sp{P(at_k0), P(at_k1), reinterpret_cast<unsigned*>(P(at_s0)),
                       reinterpret_cast<unsigned*>(P(at_s1)), total_keys, slot_bits + table_bits,
                       key64, reinterpret_cast<unsigned*>(P(at_hist)), stiles, err};
         int swapped = 0;
-        ev = s.Begin(stream);
-        Cuda(launch_sort(sp, stream, &swapped));
+        ev = s.Begin(sort_stream);
+        Cuda(launch_sort(sp, sort_stream, &swapped));
         SegmentLaunch gl{swapped ? P(at_k1) : P(at_k0), total_keys, key64,
                          reinterpret_cast<unsigned*>(P(at_seg)),
                          reinterpret_cast<unsigned*>(P(at_segtot)),
                          reinterpret_cast<unsigned*>(P(at_segscr)), err};
-        Cuda(launch_segments(gl, stream));
-        s.End(EPS_B200_PHASE_SORT, ev, stream, sort_launch_count(sp) + (total_keys ? 1u : 0u));
+        Cuda(launch_segments(gl, sort_stream));
+        s.End(EPS_B200_PHASE_SORT, ev, sort_stream, sort_launch_count(sp) + (total_keys ? 1u : 0u));
+        Cuda(cudaEventRecord(s.join, s.side));
+        Cuda(cudaStreamWaitEvent(stream, s.join, 0));
         t.keys = swapped ? P(at_k1) : P(at_k0);
         t.srcs = reinterpret_cast<unsigned*>(swapped ? P(at_s1) : P(at_s0));
         t.n = total_keys;
