@@ -74,9 +74,9 @@ class Table(C.Structure):
 
 class Feature(C.Structure):
     _fields_ = [("table", C.c_uint32), ("feature", C.c_uint32), ("pooling", C.c_uint32),
-                ("reserved", C.c_uint32), ("keys", C.c_void_p), ("key_count", C.c_uint64),
+                ("has_padding", C.c_uint32), ("keys", C.c_void_p), ("key_count", C.c_uint64),
                 ("offsets", C.c_void_p), ("offset_count", C.c_uint64),
-                ("valid_lengths", C.c_void_p)]
+                ("valid_lengths", C.c_void_p), ("padding_key", C.c_uint64)]
 
 
 class Buffer(C.Structure):
@@ -201,6 +201,8 @@ class FeatureInput:
 
     keys/offsets/valid_lengths are uint64 numpy arrays (host) or int64/uint64
     torch CUDA tensors (device).  valid_lengths=None means offset differences.
+    padding_key: keys equal to it are dropped as in PrepareAdapterInput
+    (src/access/prepare_queue.cpp:58-85); sequence positions holding it read 0.
     """
     table: int
     feature: int
@@ -208,6 +210,7 @@ class FeatureInput:
     keys: object
     offsets: object
     valid_lengths: object = None
+    padding_key: int | None = None     # keys equal to it are dropped (adapter padding)
 
     @property
     def output_rows(self) -> int:
@@ -299,8 +302,10 @@ class ParameterStore:
                 keys, offs = _host_u64(keys), _host_u64(offs)
                 lens = None if lens is None else _host_u64(lens)
             keep += [keys, offs, lens]
-            arr[i] = Feature(f.table, f.feature, f.pooling, 0, _ptr(keys), _length(keys),
-                             _ptr(offs), _length(offs), _ptr(lens))
+            pad = getattr(f, "padding_key", None)
+            arr[i] = Feature(f.table, f.feature, f.pooling, 0 if pad is None else 1, _ptr(keys),
+                             _length(keys), _ptr(offs), _length(offs), _ptr(lens),
+                             0 if pad is None else int(pad))
         return arr, bool(on_device), keep
 
     def lookup(self, feats: Sequence[FeatureInput], read_only: bool = False,

@@ -58,7 +58,11 @@ struct LookupFeature {
   unsigned int pooling;                // 0 sum, 1 mean, 2 sequence
   unsigned int table_rank;             // rank of the table inside this lookup
   unsigned int feature_index;          // index inside the lookup (gradient slot)
+  unsigned int has_padding;            // keys equal to padding_key are dropped
+  unsigned int pad_reserved;
+  unsigned long long padding_key;
 };
+constexpr unsigned int kPadSlot = 0xFFFFFFFEu;   // slot marker of a padding key
 
 // Gradient source of one feature for a Push.
 struct PushFeature {

@@ -110,9 +110,9 @@ struct LookupLaunch {
   unsigned long long bag_total;
   unsigned int shard_count, shard_id;
   int client;                      // 1: merge + mean (DistributedClient), 0: shard partial
-  int emit;                        // 1: write occurrences for a later Push
   unsigned int slot_bits;
   int key64;                       // composite key width
+  unsigned long long pad_key;      // composite key of padding occurrences (table rank = table count)
   void* occ_key;                   // KeyT[occurrences]
   unsigned int* occ_src;           // [occurrences]
   float* row_scale;                // [gradient rows]

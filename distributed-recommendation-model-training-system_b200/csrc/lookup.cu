@@ -15,13 +15,13 @@
 // is read with one 128-bit load per lane) owns one bag at a time; a warp holds
 // 32/G bags.  The group fetches G keys with one coalesced load (the next chunk's
 // keys are requested before the current chunk's rows), broadcasts the slots by
-// shuffle and issues up to DEPTH = min(G, 64/C) row loads back to back before the
-// dependent adds.  Rows past the end of a chunk are added as -0.0f, the additive
-// identity of round-to-nearest addition, so the add loop carries no predicates.
-// When the lookup will be pushed (non-read-only), the same pass writes the
-// occurrence list consumed by the coalescing sort: composite key (table rank,
-// slot) and gradient source (feature, row), plus the mean scale 1.0f/len of
-// every gradient row (src/access/batch_access.cpp:107-108).
+// shuffle and issues up to DEPTH row loads back to back before the dependent
+// adds.  Rows past the end of a chunk are added as -0.0f, the additive identity
+// of round-to-nearest addition, so the add loop carries no predicates.
+// When the lookup will be pushed (non-read-only), `emit_kernel` writes the
+// occurrence list consumed by the coalescing sort before the gather runs:
+// composite key (table rank, slot) and gradient source (feature, row), plus the
+// mean scale 1.0f/len of every gradient row (src/access/batch_access.cpp:107-108).
 #include <cooperative_groups.h>
 #include <cooperative_groups/reduce.h>
 
@@ -81,36 +81,38 @@ __global__ void __launch_bounds__(256, EPS_LOOKUP_MIN_BLOCKS) lookup_kernel(Look
 #pragma unroll
     for (int k = 0; k < C; ++k) acc[k] = 0.0f;
 
+    // padding keys (PrepareAdapterInput, src/access/prepare_queue.cpp:69-77) are
+    // dropped: no row, no gradient; mean bags divide by the kept count and
+    // sequence positions holding padding read as zeros
+    const bool has_pad = F->has_padding != 0;
+    const unsigned long long pad_key = F->padding_key;
+    unsigned long long kept = 0;
     unsigned long long key = (s + gl < e) ? keys[s + gl] : 0ull;
     for (unsigned long long c0 = s; c0 < e; c0 += G) {
       const unsigned long long i = c0 + gl;
-      unsigned slot = ~0u;              // slots fit 32 bits: rows < 2^32 per shard
-      if (i < e) {
+      unsigned slot = ~0u;              // slots fit 32 bits: rows < 2^32 - 2 per shard
+      if (i < e && has_pad && key == pad_key) {
+        slot = kPadSlot;
+      } else if (i < e) {
         unsigned long long sl, sh;
         if (p.shard_count == 1) { sl = key; sh = 0; }
         else { sl = key / p.shard_count; sh = key - sl * p.shard_count; }
         if (sh == p.shard_id && sl < rows) slot = (unsigned)sl;
         else err |= kLookupBadKey;
-        if (p.emit) {
-          const unsigned long long o2 = F->occ_base + i;
-          const KeyT ck = (slot == ~0u) ? KeyT(0)
-              : (KeyT(F->table_rank) << p.slot_bits) | KeyT(slot);
-          static_cast<KeyT*>(p.occ_key)[o2] = ck;
-          p.occ_src[o2] = (F->feature_index << kRowBits) | (unsigned)(sequence ? i : b);
-          if (sequence) p.row_scale[F->scale_base + i] = 1.0f;
-        }
       }
       // next chunk's keys in flight while this chunk's rows load
       if (i + G < e) key = keys[i + G];
       const int cnt = (int)min((unsigned long long)G, e - c0);
+      if (has_pad) kept += __popc(grp.ballot(i < e && slot != kPadSlot));
 #pragma unroll 1
       for (int j0 = 0; j0 < cnt; j0 += DEPTH) {
         float r[DEPTH][C];
-        bool use[DEPTH];
+        bool use[DEPTH], padrow[DEPTH];
 #pragma unroll
         for (int u = 0; u < DEPTH; ++u) {
           const unsigned su = grp.shfl(slot, (j0 + u) & (G - 1));
-          use[u] = (j0 + u < cnt) && su != ~0u;
+          padrow[u] = (j0 + u < cnt) && su == kPadSlot;
+          use[u] = (j0 + u < cnt) && su < kPadSlot;
           const float* row = state + (unsigned long long)su * row_stride;
 #pragma unroll
           for (int it = 0; it < ITERS; ++it) {
@@ -129,7 +131,7 @@ __global__ void __launch_bounds__(256, EPS_LOOKUP_MIN_BLOCKS) lookup_kernel(Look
           // one output row per position: 0 + w (batch_access.cpp:74-76)
 #pragma unroll
           for (int u = 0; u < DEPTH; ++u) {
-            if (!use[u]) continue;
+            if (!use[u] && !padrow[u]) continue;
             const unsigned long long pos = c0 + j0 + u;
 #pragma unroll
             for (int it = 0; it < ITERS; ++it) {
@@ -137,7 +139,7 @@ __global__ void __launch_bounds__(256, EPS_LOOKUP_MIN_BLOCKS) lookup_kernel(Look
               if (col >= D) continue;
               float t[VEC];
 #pragma unroll
-              for (int v = 0; v < VEC; ++v) t[v] = __fadd_rn(0.0f, r[u][it * VEC + v]);
+              for (int v = 0; v < VEC; ++v) t[v] = padrow[u] ? 0.0f : __fadd_rn(0.0f, r[u][it * VEC + v]);
               store_vec<VEC>(out + pos * D + col, t);
             }
           }
@@ -151,7 +153,7 @@ __global__ void __launch_bounds__(256, EPS_LOOKUP_MIN_BLOCKS) lookup_kernel(Look
       }
     }
     if (!sequence) {
-      unsigned long long len = e - s;
+      unsigned long long len = has_pad ? kept : e - s;
       if (F->lengths) {
         const unsigned long long given = F->lengths[b];
         if (given < len) err |= kLookupShortLength;
@@ -175,8 +177,6 @@ __global__ void __launch_bounds__(256, EPS_LOOKUP_MIN_BLOCKS) lookup_kernel(Look
         }
         store_vec<VEC>(out + b * D + col, t);
       }
-      if (p.emit && gl == 0)
-        p.row_scale[F->scale_base + b] = (mean && len) ? __fdiv_rn(1.0f, denom) : 1.0f;
     }
   }
   err = cg::reduce(grp, err, cg::bit_or<unsigned>());
@@ -213,8 +213,36 @@ __global__ void __launch_bounds__(256) emit_kernel(LookupLaunch p) {
     if (b + 1 == F->bag_count && e != key_count) err |= kLookupBadOffsets;
     if (s > e || e > key_count) { err |= kLookupBadOffsets; s = e = 0; }
     const bool sequence = F->pooling == 2;
+    const bool has_pad = F->has_padding != 0;
+    const unsigned long long pad_key = F->padding_key;
+    const unsigned long long rows = F->rows, occ_base = F->occ_base;
+    const unsigned src_hi = F->feature_index << kRowBits;
+    const KeyT rank_bits = KeyT(F->table_rank) << p.slot_bits;
+    unsigned long long kept = 0;
+    for (unsigned long long c0 = s; c0 < e; c0 += 32) {
+      const unsigned long long i = c0 + lane;
+      bool pad = false;
+      if (i < e) {
+        const unsigned long long key = F->keys[i];
+        KeyT ck = KeyT(0);
+        if (has_pad && key == pad_key) {
+          pad = true;
+          ck = KeyT(p.pad_key);        // sorts after every row key; the push skips it
+        } else {
+          unsigned long long sl, sh;
+          if (p.shard_count == 1) { sl = key; sh = 0; }
+          else { sl = key / p.shard_count; sh = key - sl * p.shard_count; }
+          if (sh == p.shard_id && sl < rows) ck = rank_bits | KeyT(sl);
+          else err |= kLookupBadKey;
+        }
+        static_cast<KeyT*>(p.occ_key)[occ_base + i] = ck;
+        p.occ_src[occ_base + i] = src_hi | (unsigned)(sequence ? i : b);
+        if (sequence) p.row_scale[F->scale_base + i] = 1.0f;
+      }
+      kept += __popc(__ballot_sync(~0u, i < e && !pad));
+    }
     if (!sequence && lane == 0) {
-      unsigned long long len = e - s;
+      unsigned long long len = has_pad ? kept : e - s;
       if (F->lengths) {
         const unsigned long long given = F->lengths[b];
         if (given < len) err |= kLookupShortLength;
@@ -222,21 +250,6 @@ __global__ void __launch_bounds__(256) emit_kernel(LookupLaunch p) {
       }
       const bool mean = F->pooling == 1;
       p.row_scale[F->scale_base + b] = (mean && len) ? __fdiv_rn(1.0f, (float)len) : 1.0f;
-    }
-    const unsigned long long rows = F->rows, occ_base = F->occ_base;
-    const unsigned src_hi = F->feature_index << kRowBits;
-    const KeyT rank_bits = KeyT(F->table_rank) << p.slot_bits;
-    for (unsigned long long i = s + lane; i < e; i += 32) {
-      const unsigned long long key = F->keys[i];
-      unsigned long long sl, sh;
-      if (p.shard_count == 1) { sl = key; sh = 0; }
-      else { sl = key / p.shard_count; sh = key - sl * p.shard_count; }
-      KeyT ck = KeyT(0);
-      if (sh == p.shard_id && sl < rows) ck = rank_bits | KeyT(sl);
-      else err |= kLookupBadKey;
-      static_cast<KeyT*>(p.occ_key)[occ_base + i] = ck;
-      p.occ_src[occ_base + i] = src_hi | (unsigned)(sequence ? i : b);
-      if (sequence) p.row_scale[F->scale_base + i] = 1.0f;
     }
   }
   err = __reduce_or_sync(~0u, err);

@@ -576,7 +576,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
     unsigned long long total_keys = 0, total_offsets = 0, total_lengths = 0, total_rows = 0,
                        host_out_values = 0, bags = 0;
     std::vector<unsigned> dims;
-    bool out16 = true, out8 = true, any_host_out = false;
+    bool out16 = true, out8 = true, any_host_out = false, any_padding = false;
     for (uint64_t i = 0; i < count; ++i) {
       const auto& f = features[i];
       Require(ids.insert(f.feature).second, "duplicate feature ID");
@@ -585,6 +585,9 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       Require(f.offset_count >= 1 && f.offsets, "invalid bag offsets");
       Require(f.offset_count > 1 || f.key_count == 0, "invalid bag offsets");
       Require(!f.key_count || f.keys, "null feature keys");
+      Require(!f.has_padding || !f.valid_lengths,
+              "valid lengths are derived from the padding key; pass one or the other");
+      any_padding |= f.has_padding != 0;
       const unsigned long long rows = f.pooling == 2 ? f.key_count : f.offset_count - 1;
       Require(rows < (1ull << kRowBits) && f.key_count < (1ull << 31),
               "feature exceeds the per-feature row limit", EPS_B200_CAPACITY_EXCEEDED);
@@ -620,7 +623,10 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
     }
     const unsigned slot_bits = std::max(1u, bits_for(max_rows - 1));
     const unsigned table_bits = bits_for(ranks.size() - 1);
-    const int key64 = slot_bits + table_bits > 32;
+    // padding occurrences get the composite key (table rank = 2^table_bits, slot 0):
+    // one more bit, sorted after every row key, skipped by the push
+    const unsigned key_bits = slot_bits + table_bits + (any_padding ? 1u : 0u);
+    const int key64 = key_bits > 32;
     const size_t key_bytes = key64 ? 8 : 4;
     int vec, group, iters;
     choose_vec(dims, out16, out8, &vec, &group, &iters);
@@ -655,7 +661,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       at_part = c.take<float>(max_pieces * dim_max);
       at_rec = c.take<LongRecord>(max_long);
       // [sort scratch | segment scratch | status] zeroed together
-      at_zero = at_hist = c.take<char>(sort_scratch_bytes(total_keys, slot_bits + table_bits));
+      at_zero = at_hist = c.take<char>(sort_scratch_bytes(total_keys, key_bits));
       at_segscr = c.take<char>(segment_scratch_bytes(total_keys));
     }
     const size_t at_status = c.take<StatusBlock>(1);
@@ -730,6 +736,8 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         L.pooling = f.pooling;
         L.table_rank = ranks.at(f.table);
         L.feature_index = (unsigned)i;
+        L.has_padding = f.has_padding ? 1u : 0u;
+        L.padding_key = f.padding_key;
         bag_base += L.bag_count;
         occ_base += f.key_count;
         scale_base += rows;
@@ -749,9 +757,9 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       lp.shard_count = s.opt.shard_count;
       lp.shard_id = s.opt.shard_id;
       lp.client = shard_partial ? 0 : 1;
-      lp.emit = read_only ? 0 : 1;
       lp.slot_bits = slot_bits;
       lp.key64 = key64;
+      lp.pad_key = 1ull << (slot_bits + table_bits);
       lp.error = read_only && input_on_device && !any_host_out ? s.sticky_error : err;
       lp.vec = vec;
       lp.group = group;
@@ -766,7 +774,6 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         // the occurrence list first; the gather below does not emit, and the
         // sort (histograms, digit passes, segment compaction) runs on the side
         // stream concurrently with the gather
-        lp.emit = 0;
         Cuda(launch_emit(lp, stream));
         Cuda(cudaEventRecord(s.fork, stream));
       }
@@ -776,7 +783,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         cudaStream_t sort_stream = s.side;
         Cuda(cudaStreamWaitEvent(s.side, s.fork, 0));
         SortLaunch sp{P(at_k0), P(at_k1), reinterpret_cast<unsigned*>(P(at_s0)),
-                      reinterpret_cast<unsigned*>(P(at_s1)), total_keys, slot_bits + table_bits,
+                      reinterpret_cast<unsigned*>(P(at_s1)), total_keys, key_bits,
                       key64, reinterpret_cast<unsigned*>(P(at_hist)), stiles, err};
         int swapped = 0;
         ev = s.Begin(sort_stream);
@@ -920,6 +927,8 @@ int eps_b200_lookup_noalloc(EpsB200Store* store, const EpsB200Feature* features,
       L.pooling = f.pooling;
       L.table_rank = 0;
       L.feature_index = (unsigned)i;
+      L.has_padding = f.has_padding ? 1u : 0u;
+      L.padding_key = f.padding_key;
       bag_base += L.bag_count;
     }
     // launch shape as in the regular lookup (no heap use here)
@@ -940,7 +949,6 @@ int eps_b200_lookup_noalloc(EpsB200Store* store, const EpsB200Feature* features,
     lp.shard_count = 1;
     lp.shard_id = 0;
     lp.client = 1;
-    lp.emit = 0;
     lp.slot_bits = 1;
     lp.key64 = 0;
     lp.error = s.sticky_error;      // reported by eps_b200_synchronize
@@ -1405,6 +1413,7 @@ int eps_b200_route(EpsB200Store* store, const EpsB200Feature* features, uint64_t
       Require(f.offset_count >= 1 && f.offsets, "invalid bag offsets");
       Require(f.offset_count > 1 || f.key_count == 0, "invalid bag offsets");
       Require(!f.key_count || f.keys, "null feature keys");
+      Require(!f.has_padding, "padding keys are not supported by the multi-GPU round");
       const unsigned long long rows = f.pooling == 2 ? f.key_count : f.offset_count - 1;
       Require(rows < (1ull << kRowBits) && f.key_count < (1ull << 31),
               "feature exceeds the per-feature row limit", EPS_B200_CAPACITY_EXCEEDED);
@@ -1621,7 +1630,8 @@ ServeLayout MakeServeLayout(EpsB200Store& s, const uint64_t* payload, const uint
       x.table = tables[f];
       x.feature = r * F + f;
       x.pooling = poolings[f];
-      x.reserved = 0;
+      x.has_padding = 0;
+      x.padding_key = 0;
       x.keys = payload + base + ko;
       x.key_count = nk;
       x.offsets = payload + base + NK + oo;

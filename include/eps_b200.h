@@ -95,12 +95,20 @@ typedef struct {
 } EpsB200Table;
 
 /* eps::FeatureInput (include/eps/types.hpp:99-107).  valid_lengths may be NULL
- * (then the offset differences are the bag lengths). */
+ * (then the offset differences are the bag lengths).  has_padding / padding_key
+ * as eps::entropy::Feature::padding_key (include/eps/entropy_adapter.hpp:13,
+ * EpsFeature in include/eps/runtime_c.h:10-15): keys equal to padding_key are
+ * dropped as in PrepareAdapterInput (src/access/prepare_queue.cpp:58-85) --
+ * pooled bags sum the other keys and mean divides by their count; sequence
+ * outputs keep every position, padding positions read 0 and take no gradient.
+ * With has_padding, valid_lengths must be NULL (the kept counts are the
+ * lengths).  The multi-GPU round does not take padding keys. */
 typedef struct {
-  uint32_t table, feature, pooling, reserved;
+  uint32_t table, feature, pooling, has_padding;
   const uint64_t* keys; uint64_t key_count;
   const uint64_t* offsets; uint64_t offset_count;
   const uint64_t* valid_lengths;
+  uint64_t padding_key;
 } EpsB200Feature;
 
 /* Feature tensor [rows, columns] f32: eps::EpsBuffer (include/eps/runtime_c.h:14-19)

@@ -268,6 +268,63 @@ def test_invalid_host_inputs_are_rejected(eps):
     assert s.stats()["live_tickets"] == 0
 
 
+def _drop_padding(f, pad):
+    """Host restatement of PrepareAdapterInput (src/access/prepare_queue.cpp:69-77):
+    the compacted feature and, for sequence, the kept positions."""
+    keys, offs = [], [0]
+    positions = []
+    for b in range(len(f.offsets) - 1):
+        for i in range(int(f.offsets[b]), int(f.offsets[b + 1])):
+            if int(f.keys[i]) != pad:
+                keys.append(int(f.keys[i]))
+                positions.append(i)
+        offs.append(len(keys))
+    return Feature(f.table, f.feature, f.pooling, np.array(keys, np.uint64), offs), positions
+
+
+def test_padding_keys_are_dropped(eps):
+    """Adapter padding (EpsFeature::has_padding): padding keys contribute no row and
+    no gradient, mean divides by the kept count, sequence positions read 0."""
+    t = [TableDef(id=1, dimension=32, learning_rate=0.01, init_min=-0.05, init_max=0.05, rows=200)]
+    pad = 197                                   # a key inside the table: must be skipped
+    rng = np.random.default_rng(11)
+    feats = []
+    for fi, pool in enumerate([SUM, MEAN, SEQUENCE, MEAN]):
+        lens = rng.integers(0, 7, size=40)
+        offs = np.concatenate([[0], np.cumsum(lens)]).astype(np.uint64)
+        keys = rng.integers(0, 200, size=int(offs[-1])).astype(np.uint64)
+        keys[rng.random(len(keys)) < 0.3] = pad
+        if len(lens) > 3 and lens[3]:
+            keys[int(offs[3]):int(offs[4])] = pad      # a bag of padding only
+        feats.append(Feature(1, fi, pool, keys, offs))
+    s, o = make_store(eps, t), Oracle(t)
+    ins = [eps.FeatureInput(f.table, f.feature, f.pooling, f.keys, f.offsets, padding_key=pad)
+           for f in feats]
+    ticket, outs = s.lookup(ins)
+    compact = [_drop_padding(f, pad) for f in feats]
+    ref = o.lookup([c for c, _ in compact])
+    for f, (c, pos), a, r in zip(feats, compact, outs, ref):
+        if f.pooling == SEQUENCE:
+            want = np.zeros_like(a)
+            want[pos] = r
+        else:
+            want = r
+        assert np.array_equal(bits(a), bits(want)), f.feature
+    grads = [rng.normal(0, 0.01, size=a.shape).astype(F32) for a in outs]
+    s.push(ticket, grads)
+    cgrads = [g[pos] if f.pooling == SEQUENCE else g for f, (c, pos), g in zip(feats, compact, grads)]
+    assert o.push([c for c, _ in compact], cgrads) == 0
+    keys = np.arange(200, dtype=np.uint64)
+    w, m, v, u = s.read_state(1, keys)
+    st, upd = o.state(1)
+    assert np.array_equal(bits(w), bits(st[:, 0])) and np.array_equal(bits(m), bits(st[:, 1]))
+    assert np.array_equal(bits(v), bits(st[:, 2])) and np.array_equal(u, upd)
+    assert u[pad] == 0                           # the padding key's row was never touched
+    with pytest.raises(eps.EpsError):           # padding derives the lengths itself
+        s.lookup([eps.FeatureInput(1, 0, SUM, feats[0].keys, feats[0].offsets,
+                                   valid_lengths=np.diff(feats[0].offsets), padding_key=pad)])
+
+
 def test_empty_and_ragged_features(eps):
     t = [TableDef(id=1, dimension=64, learning_rate=0.01, rows=100)]
     s, o = make_store(eps, t), Oracle(t)
