@@ -85,6 +85,14 @@ class Buffer(C.Structure):
                 ("reserved2", C.c_int32)]
 
 
+class WorkerGradients(C.Structure):
+    _fields_ = [("keys", C.c_void_p), ("values", C.c_void_p), ("rows", C.c_uint64),
+                ("sample_count", C.c_uint64)]
+
+
+REDUCE_SUM, REDUCE_WORKER_MEAN, REDUCE_SAMPLE_MEAN = 0, 1, 2
+
+
 class Stats(C.Structure):
     _fields_ = [(n, C.c_uint64) for n in ("lookups", "updates", "rejected_updates",
                                           "duplicate_requests", "live_tickets", "state_bytes",
@@ -106,7 +114,8 @@ ENTRY_POINTS = ("eps_b200_abi_version", "eps_b200_create", "eps_b200_destroy",
                 "eps_b200_serve_push", "eps_b200_comm_unique_id", "eps_b200_comm_create",
                 "eps_b200_comm_destroy", "eps_b200_comm_alltoallv", "eps_b200_comm_allreduce_max",
                 "eps_b200_client_create", "eps_b200_client_destroy", "eps_b200_client_prepare",
-                "eps_b200_client_lookup", "eps_b200_client_push", "eps_b200_client_release")
+                "eps_b200_client_lookup", "eps_b200_client_push", "eps_b200_client_release",
+                "eps_b200_sync_reduce")
 
 
 def load_library() -> C.CDLL:
@@ -162,6 +171,8 @@ def load_library() -> C.CDLL:
                                            P(C.c_uint64), P(Status)]
     lib.eps_b200_client_push.argtypes = [vp, C.c_uint64, P(Buffer), vp, C.c_int32, P(Status)]
     lib.eps_b200_client_release.argtypes = [vp, C.c_uint64, P(Status)]
+    lib.eps_b200_sync_reduce.argtypes = [vp, C.c_uint32, vp, C.c_uint32, C.c_int32, vp, vp,
+                                         C.c_uint64, P(C.c_uint64), vp, P(Status)]
     for name in ENTRY_POINTS[1:]:
         if name not in ("eps_b200_destroy", "eps_b200_comm_destroy", "eps_b200_client_destroy"):
             getattr(lib, name).restype = C.c_int
@@ -554,6 +565,42 @@ class ParameterStore:
         st = Status()
         _check(self.lib.eps_b200_route_release(self._h, route, C.byref(st)), st)
         getattr(self, "_route_keep", {}).pop(route, None)
+
+    # ---- synchronous multi-worker round (SynchronousGradientCollector)
+    def sync_reduce(self, table: int, workers, reduction: int = REDUCE_SAMPLE_MEAN, stream=None):
+        """Reduces one round of worker gradients for `table` on the device
+        (eps_b200_sync_reduce).  workers: [(keys, values, sample_count)] with
+        device tensors (keys int64 sorted unique, values float32 [rows, dim]).
+        Returns (keys, values) device tensors of the ascending key union."""
+        import torch
+        arr = (WorkerGradients * len(workers))()
+        total = 0
+        for i, (k, v, c) in enumerate(workers):
+            arr[i] = WorkerGradients(_ptr(k) if len(k) else None, _ptr(v) if len(k) else None,
+                                     int(k.shape[0]), int(c))
+            total += int(k.shape[0])
+        dim = self.dimension(table)
+        dev = f"cuda:{self.device}"
+        keys = torch.empty(max(1, total), dtype=torch.int64, device=dev)
+        values = torch.empty((max(1, total), dim), dtype=torch.float32, device=dev)
+        rows = C.c_uint64(0)
+        st = Status()
+        _check(self.lib.eps_b200_sync_reduce(self._h, table, arr, len(workers), reduction,
+                                             _ptr(keys), _ptr(values), max(1, total),
+                                             C.byref(rows), _stream_ptr(stream), C.byref(st)), st)
+        return keys[:rows.value], values[:rows.value]
+
+    def apply_rows(self, table: int, keys, values, feature: int = 0, stream=None):
+        """Applies reduced row gradients as the reference's synchronous applier does
+        (src/transport/brpc_synchronous_server.cpp:62-78): one sequence feature of
+        the keys, looked up and pushed (one LazyAdam step of the table)."""
+        import torch
+        n = int(keys.shape[0])
+        offs = torch.tensor([0, n], dtype=torch.int64, device=keys.device)
+        f = FeatureInput(table, feature, SEQUENCE, keys, offs)
+        out = torch.empty((n, self.dimension(table)), dtype=torch.float32, device=keys.device)
+        ticket, _ = self.lookup([f], outputs=[out], stream=stream)
+        self.push(ticket, [values], features=[feature], wait=True, stream=stream)
 
     def stats(self) -> dict:
         s = Stats()

@@ -192,6 +192,36 @@ struct SegmentLaunch {
 cudaError_t launch_segments(const SegmentLaunch& p, cudaStream_t stream);
 size_t segment_scratch_bytes(unsigned long long n);
 
+// Synchronous multi-worker round reduce (sync.cu).
+struct SyncWorker {                  // layout of EpsB200WorkerGradients
+  const unsigned long long* keys;
+  const float* values;
+  unsigned long long rows;
+  unsigned long long sample_count;
+};
+struct SyncLaunch {
+  const SyncWorker* workers;
+  unsigned int worker_count;
+  const unsigned long long* row_base;   // [workers + 1] prefix of rows
+  const double* scale;                  // [workers]
+  unsigned long long total_rows;
+  unsigned int dim;
+  unsigned long long key_space;
+  unsigned int shard_count, shard_id;
+  unsigned long long* keys;             // pack output: concatenated keys
+  unsigned int* rows;                   // pack output: global row index
+  const unsigned long long* sorted_keys;
+  const unsigned int* sorted_rows;
+  const unsigned int* seg_start;
+  const unsigned int* seg_total;
+  unsigned long long* keys_out;
+  float* values_out;
+  unsigned int* error;                  // 1 unsorted, 2 not owned, 4 non-finite, 16 overflow
+                                        // (8: a sort wait ran out)
+};
+cudaError_t launch_sync_pack(const SyncLaunch& p, cudaStream_t stream);
+cudaError_t launch_sync_accumulate(const SyncLaunch& p, cudaStream_t stream);
+
 struct PushLaunch {
   const PushTable* tables;         // device, per table rank
   unsigned int table_count;

@@ -1688,6 +1688,113 @@ int eps_b200_serve_push(EpsB200Store* store, uint64_t ticket, const float* gradi
   });
 }
 
+int eps_b200_sync_reduce(EpsB200Store* store, uint32_t table, const EpsB200WorkerGradients* workers,
+                         uint32_t worker_count, int32_t reduction, uint64_t* keys_out,
+                         float* values_out, uint64_t capacity, uint64_t* rows_out, void* stream_arg,
+                         EpsB200Status* status) {
+  return Boundary(status, [&] {
+    auto& s = *Checked(store);
+    Require(workers && rows_out && worker_count >= 1 && worker_count <= 1023,
+            "invalid synchronous gradient workers");
+    Require(reduction >= EPS_B200_REDUCE_SUM && reduction <= EPS_B200_REDUCE_SAMPLE_MEAN,
+            "invalid gradient reduction");
+    std::lock_guard lock(s.mutex);
+    s.Activate();
+    const Table& t = s.Get(table);
+    const unsigned D = t.def.dimension;
+    // synchronous_gradients.cpp:92-97,104: the denominator and per-worker scale
+    double denominator = 1;
+    if (reduction == EPS_B200_REDUCE_WORKER_MEAN) denominator = worker_count;
+    else if (reduction == EPS_B200_REDUCE_SAMPLE_MEAN) {
+      denominator = 0;
+      for (uint32_t w = 0; w < worker_count; ++w) denominator += double(workers[w].sample_count);
+    }
+    std::vector<double> scale(worker_count);
+    std::vector<unsigned long long> row_base(worker_count + 1, 0);
+    for (uint32_t w = 0; w < worker_count; ++w) {
+      const auto& W = workers[w];
+      Require(W.sample_count && W.sample_count <= (1ull << 40), "invalid sample count");
+      Require(!W.rows || (W.keys && W.values), "null worker gradient buffer");
+      scale[w] = (reduction == EPS_B200_REDUCE_SAMPLE_MEAN ? double(W.sample_count) : 1.) / denominator;
+      row_base[w + 1] = row_base[w] + W.rows;
+    }
+    const unsigned long long n = row_base[worker_count];
+    Require(n < (1ull << 31), "gradient rows exceed budget", EPS_B200_CAPACITY_EXCEEDED);
+    Require(capacity >= n && (!n || (keys_out && values_out)), "reduce output capacity too small");
+    cudaStream_t stream = s.Use(stream_arg);
+    if (n == 0) { *rows_out = 0; return; }
+    const unsigned bits = std::max(1u, bits_for(t.def.key_space - 1));
+    Carver c;
+    const size_t at_w = c.take<SyncWorker>(worker_count);
+    const size_t at_base = c.take<unsigned long long>(worker_count + 1);
+    const size_t at_scale = c.take<double>(worker_count);
+    const size_t at_k0 = c.take<unsigned long long>(n), at_k1 = c.take<unsigned long long>(n);
+    const size_t at_r0 = c.take<unsigned>(n), at_r1 = c.take<unsigned>(n);
+    const size_t at_seg = c.take<unsigned>(n + 1);
+    const size_t at_zero = c.take<char>(sort_scratch_bytes(n, bits));
+    const size_t at_segscr = c.take<char>(segment_scratch_bytes(n));
+    const size_t at_tot = c.take<unsigned>(2);       // seg_total, error
+    const size_t zero_bytes = c.offset - at_zero;
+    char* slab = nullptr;
+    Cuda(cudaMallocAsync(reinterpret_cast<void**>(&slab), c.offset, stream));
+    try {
+      auto P = [&](size_t at) { return slab + at; };
+      Cuda(cudaMemsetAsync(P(at_zero), 0, zero_bytes, stream));
+      s.Stage(P(at_w), workers, worker_count * sizeof(SyncWorker), stream);
+      s.Stage(P(at_base), row_base.data(), row_base.size() * 8, stream);
+      s.Stage(P(at_scale), scale.data(), scale.size() * 8, stream);
+      unsigned* tot = reinterpret_cast<unsigned*>(P(at_tot));
+      SyncLaunch lp{};
+      lp.workers = reinterpret_cast<const SyncWorker*>(P(at_w));
+      lp.worker_count = worker_count;
+      lp.row_base = reinterpret_cast<const unsigned long long*>(P(at_base));
+      lp.scale = reinterpret_cast<const double*>(P(at_scale));
+      lp.total_rows = n;
+      lp.dim = D;
+      lp.key_space = t.def.key_space;
+      lp.shard_count = s.opt.shard_count;
+      lp.shard_id = s.opt.shard_id;
+      lp.keys = reinterpret_cast<unsigned long long*>(P(at_k0));
+      lp.rows = reinterpret_cast<unsigned*>(P(at_r0));
+      lp.error = tot + 1;
+      Cuda(launch_sync_pack(lp, stream));
+      SortLaunch sp{P(at_k0), P(at_k1), reinterpret_cast<unsigned*>(P(at_r0)),
+                    reinterpret_cast<unsigned*>(P(at_r1)), n, bits, 1,
+                    reinterpret_cast<unsigned*>(P(at_zero)), sort_tiles(n), tot + 1};
+      int swapped = 0;
+      Cuda(launch_sort(sp, stream, &swapped));
+      SegmentLaunch gl{swapped ? P(at_k1) : P(at_k0), n, 1, reinterpret_cast<unsigned*>(P(at_seg)),
+                       tot, reinterpret_cast<unsigned*>(P(at_segscr)), tot + 1};
+      Cuda(launch_segments(gl, stream));
+      lp.sorted_keys = reinterpret_cast<const unsigned long long*>(swapped ? P(at_k1) : P(at_k0));
+      lp.sorted_rows = reinterpret_cast<const unsigned*>(swapped ? P(at_r1) : P(at_r0));
+      lp.seg_start = reinterpret_cast<const unsigned*>(P(at_seg));
+      lp.seg_total = tot;
+      lp.keys_out = reinterpret_cast<unsigned long long*>(keys_out);
+      lp.values_out = values_out;
+      Cuda(launch_sync_accumulate(lp, stream));
+      s.stats.kernel_launches += 3 + sort_launch_count(sp);
+      unsigned host[2];
+      Cuda(cudaMemcpyAsync(host, tot, sizeof(host), cudaMemcpyDeviceToHost, stream));
+      s.Sync(stream);
+      char* owned = slab;
+      slab = nullptr;
+      Cuda(cudaFreeAsync(owned, stream));
+      s.Done(stream);
+      const unsigned err = host[1];
+      // synchronous_gradients.cpp:75-77 (validation) and :120 (overflow)
+      Require(!(err & 3u), "gradient keys must be unique, sorted and owned by this shard");
+      Require(!(err & 4u), "non-finite gradient");
+      Require(!(err & 16u), "gradient reduction overflow", EPS_B200_RUN_FAILED);
+      Require(!(err & kLookupSortFailed), "coalescing sort wait ran out", EPS_B200_RUN_FAILED);
+      *rows_out = host[0];
+    } catch (...) {
+      if (slab) cudaFreeAsync(slab, stream);
+      throw;
+    }
+  });
+}
+
 }  // extern "C"
 
 namespace eps_b200 {

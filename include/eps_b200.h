@@ -370,6 +370,34 @@ EPS_B200_EXPORT int eps_b200_client_push(EpsB200Client* client, uint64_t round,
 EPS_B200_EXPORT int eps_b200_client_release(EpsB200Client* client, uint64_t handle,
                                             EpsB200Status* status);
 
+/* ---- Synchronous multi-worker round reduce:
+ * SynchronousGradientCollector::Reduce (src/training/synchronous_gradients.cpp:91-126)
+ * on the device, for one table of this shard.  Each worker contributes sorted
+ * unique keys owned by this shard and float rows [rows][dimension] (device),
+ * plus its sample count.  keys_out / values_out (device, capacity >= the sum of
+ * the workers' rows) receive the union of the keys in ascending order and
+ * float(sum over workers, in worker order, of double(value) * scale) with
+ * scale = 1 / denominator: 1 (SUM), the worker count (WORKER_MEAN) or the
+ * round's total samples with each worker weighted by its sample count
+ * (SAMPLE_MEAN).  *rows receives the number of keys.  The reduced rows are
+ * applied like the reference's synchronous applier
+ * (src/transport/brpc_synchronous_server.cpp:62-78): one sequence feature of
+ * those keys through eps_b200_lookup + eps_b200_push.  Waits for the stream. */
+#define EPS_B200_REDUCE_SUM 0
+#define EPS_B200_REDUCE_WORKER_MEAN 1
+#define EPS_B200_REDUCE_SAMPLE_MEAN 2
+typedef struct {
+  const uint64_t* keys;     /* device, strictly increasing */
+  const float* values;      /* device, [rows][dimension] */
+  uint64_t rows;
+  uint64_t sample_count;    /* 1 .. 2^40 */
+} EpsB200WorkerGradients;
+EPS_B200_EXPORT int eps_b200_sync_reduce(EpsB200Store* store, uint32_t table,
+                                         const EpsB200WorkerGradients* workers, uint32_t worker_count,
+                                         int32_t reduction, uint64_t* keys_out, float* values_out,
+                                         uint64_t capacity, uint64_t* rows, void* stream,
+                                         EpsB200Status* status);
+
 /* CpuParameterService::Stats (include/eps/runtime.hpp:134). */
 EPS_B200_EXPORT int eps_b200_stats(EpsB200Store* store, EpsB200Stats* stats, EpsB200Status* status);
 

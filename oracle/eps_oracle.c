@@ -366,3 +366,54 @@ uint64_t eo_drop_padding(const uint64_t* keys, const uint64_t* offsets, uint64_t
   }
   return n;
 }
+
+static int eo_cmp_u64(const void* a, const void* b) {
+  const uint64_t x = *(const uint64_t*)a, y = *(const uint64_t*)b;
+  return x < y ? -1 : x > y;
+}
+
+/* src/training/synchronous_gradients.cpp:91-126: denominator (:92-97), per-worker
+ * scale (:104), accumulation in worker order in double (:105-110), ascending keys
+ * of the std::map and the float conversion with its overflow check (:113-121). */
+uint64_t eo_sync_reduce(uint32_t dim, uint32_t workers, const uint64_t* const* keys,
+                        const float* const* values, const uint64_t* rows,
+                        const uint64_t* sample_counts, int reduction, uint64_t* keys_out,
+                        float* values_out) {
+  double denominator = 1;
+  if (reduction == 1) denominator = workers;
+  else if (reduction == 2) {
+    denominator = 0;
+    for (uint32_t w = 0; w < workers; ++w) denominator += (double)sample_counts[w];
+  }
+  uint64_t total = 0;
+  for (uint32_t w = 0; w < workers; ++w) total += rows[w];
+  uint64_t* all = (uint64_t*)malloc((total ? total : 1) * sizeof(uint64_t));
+  uint64_t n = 0;
+  for (uint32_t w = 0; w < workers; ++w)
+    for (uint64_t r = 0; r < rows[w]; ++r) all[n++] = keys[w][r];
+  qsort(all, n, sizeof(uint64_t), eo_cmp_u64);
+  uint64_t u = 0;
+  for (uint64_t i = 0; i < n; ++i)
+    if (i == 0 || all[i] != all[i - 1]) all[u++] = all[i];
+  double* acc = (double*)malloc((dim ? dim : 1) * sizeof(double));
+  int overflow = 0;
+  for (uint64_t k = 0; k < u; ++k) {
+    for (uint32_t d = 0; d < dim; ++d) acc[d] = 0.0;
+    for (uint32_t w = 0; w < workers; ++w) {
+      const double scale = (reduction == 2 ? (double)sample_counts[w] : 1.) / denominator;
+      uint64_t lo = 0, hi = rows[w];
+      while (lo < hi) { const uint64_t mid = (lo + hi) / 2; if (keys[w][mid] < all[k]) lo = mid + 1; else hi = mid; }
+      if (lo < rows[w] && keys[w][lo] == all[k])
+        for (uint32_t d = 0; d < dim; ++d) acc[d] += (double)values[w][lo * dim + d] * scale;
+    }
+    keys_out[k] = all[k];
+    for (uint32_t d = 0; d < dim; ++d) {
+      const float f = (float)acc[d];
+      if (!isfinite(f)) overflow = 1;
+      values_out[k * dim + d] = f;
+    }
+  }
+  free(acc);
+  free(all);
+  return overflow ? UINT64_MAX : u;
+}

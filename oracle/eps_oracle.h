@@ -106,6 +106,16 @@ uint64_t eo_drop_padding(const uint64_t* keys, const uint64_t* offsets, uint64_t
                          uint64_t padding_key, uint64_t* keys_out, uint64_t* offsets_out,
                          uint64_t* positions_out);
 
+/* SynchronousGradientCollector::Reduce (src/training/synchronous_gradients.cpp:91-126)
+ * for one table: workers' sorted unique keys + float rows, reduction 0 sum,
+ * 1 worker_mean, 2 sample_mean.  Writes the ascending union of keys and the
+ * float of the worker-ordered double sums; returns the key count, or
+ * UINT64_MAX if a reduced value is not finite. */
+uint64_t eo_sync_reduce(uint32_t dim, uint32_t workers, const uint64_t* const* keys,
+                        const float* const* values, const uint64_t* rows,
+                        const uint64_t* sample_counts, int reduction, uint64_t* keys_out,
+                        float* values_out);
+
 #ifdef __cplusplus
 }
 #endif

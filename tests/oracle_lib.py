@@ -193,6 +193,26 @@ class Oracle:
                                           C.byref(u))
         return rc, rows[:u.value], vals[:u.value]
 
+    def sync_reduce(self, dim, workers, reduction):
+        """eo_sync_reduce: workers = [(keys u64[k], values f32[k, dim], sample_count)]."""
+        W = len(workers)
+        keys = [_u64(k) for k, _, _ in workers]
+        vals = [_f32(v).reshape(-1) for _, v, _ in workers]
+        kp = (u64p * W)(*[_ptr(k, u64p) for k in keys])
+        vp = (f32p * W)(*[_ptr(v, f32p) for v in vals])
+        rows = _u64([len(k) for k in keys])
+        samples = _u64([c for _, _, c in workers])
+        total = max(1, int(rows.sum()))
+        ko = np.zeros(total, np.uint64)
+        vo = np.zeros((total, dim), np.float32)
+        self.lib.eo_sync_reduce.restype = C.c_uint64
+        u = self.lib.eo_sync_reduce(C.c_uint32(dim), C.c_uint32(W), kp, vp, _ptr(rows, u64p),
+                                    _ptr(samples, u64p), C.c_int(reduction), _ptr(ko, u64p),
+                                    _ptr(vo, f32p))
+        if u == (1 << 64) - 1:
+            raise ValueError("gradient reduction overflow")
+        return ko[:u], vo[:u]
+
     def powers(self, tid):
         t = self.table(tid)
         return t.beta1_power, t.beta2_power, t.optimizer_sequence

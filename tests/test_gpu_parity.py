@@ -396,3 +396,55 @@ def test_two_live_tickets_any_order(eps):
     st, upd = o.state(1)
     k = keys.astype(np.int64)
     assert np.array_equal(bits(w), bits(st[k, 0])) and np.array_equal(u, upd[k])
+
+
+def test_sync_reduce_known_answers_and_oracle(eps):
+    """SynchronousGradientCollector::Reduce on the device: the reference's known
+    answers (tests/synchronous_gradients_tests.cpp:37-50), bit-exact agreement
+    with the oracle on a larger round, input rejection, and the reduced rows
+    applied like the reference's synchronous applier."""
+    import torch
+    dev = "cuda:0"
+    t2 = [TableDef(id=1, dimension=2, rows=8)]
+    s = make_store(eps, t2)
+    W = [(torch.tensor([1, 4], device=dev), torch.tensor([[3., 6.], [9., 12.]], device=dev), 1),
+         (torch.tensor([1, 2], device=dev), torch.tensor([[6., 9.], [12., 15.]], device=dev), 3),
+         (torch.empty(0, dtype=torch.int64, device=dev), torch.empty((0, 2), device=dev), 2)]
+    expected = {0: [9, 15, 12, 15, 9, 12], 1: [3, 5, 4, 5, 3, 4], 2: [3.5, 5.5, 6, 7.5, 1.5, 2]}
+    for reduction, want in expected.items():
+        keys, values = s.sync_reduce(1, W, reduction)
+        assert keys.cpu().tolist() == [1, 2, 4]
+        assert values.cpu().reshape(-1).tolist() == want
+    # a larger round against the oracle (sample_mean, 7 workers, overlapping keys)
+    t = [TableDef(id=1, dimension=48, learning_rate=0.01, init_min=-0.05, init_max=0.05, rows=5000)]
+    s, o = make_store(eps, t), Oracle(t)
+    rng = np.random.default_rng(5)
+    workers = []
+    for w in range(7):
+        k = np.unique(rng.integers(0, 5000, size=int(rng.integers(0, 900)))).astype(np.uint64)
+        v = rng.normal(0, 0.01, size=(len(k), 48)).astype(F32)
+        workers.append((k, v, int(rng.integers(1, 50))))
+    for reduction in (0, 1, 2):
+        ok, ov = o.sync_reduce(48, workers, reduction)
+        dk, dv = s.sync_reduce(1, [(torch.from_numpy(k.astype(np.int64)).to(dev),
+                                    torch.from_numpy(v).to(dev), c) for k, v, c in workers],
+                               reduction)
+        assert np.array_equal(dk.cpu().numpy().astype(np.uint64), ok)
+        assert np.array_equal(bits(dv.cpu().numpy()), bits(ov))
+    # the reduced rows applied as one sequence lookup + push, as the reference applier does
+    s.apply_rows(1, dk, dv)
+    feat = Feature(1, 0, SEQUENCE, ok, [0, len(ok)])
+    o.lookup([feat])
+    assert o.push([feat], [ov]) == 0
+    w_, m_, v_, u_ = s.read_state(1, np.arange(5000, dtype=np.uint64))
+    st, upd = o.state(1)
+    assert np.array_equal(bits(w_), bits(st[:, 0])) and np.array_equal(bits(v_), bits(st[:, 2]))
+    assert np.array_equal(u_, upd)
+    # rejected inputs: unsorted keys, non-finite values
+    bad = [(torch.tensor([3, 1], device=dev), torch.zeros((2, 48), device=dev), 1)]
+    with pytest.raises(eps.EpsError):
+        s.sync_reduce(1, bad, 0)
+    nan = torch.zeros((1, 48), device=dev)
+    nan[0, 5] = float("nan")
+    with pytest.raises(eps.EpsError):
+        s.sync_reduce(1, [(torch.tensor([7], device=dev), nan, 1)], 0)
