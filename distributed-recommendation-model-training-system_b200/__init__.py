@@ -93,6 +93,18 @@ class WorkerGradients(C.Structure):
 REDUCE_SUM, REDUCE_WORKER_MEAN, REDUCE_SAMPLE_MEAN = 0, 1, 2
 
 
+class UpdateContext(C.Structure):
+    _fields_ = [("table", C.c_uint32), ("learning_rate", C.c_float), ("beta1_power", C.c_float),
+                ("beta2_power", C.c_float), ("optimizer_sequence", C.c_uint64)]
+
+
+class CompactGradients(C.Structure):
+    _fields_ = [("keys", C.c_void_p), ("rows", C.c_uint64), ("dimension", C.c_uint32),
+                ("source_values", C.c_void_p), ("sources", C.c_uint64),
+                ("row_offsets", C.c_void_p), ("source_rows", C.c_void_p), ("scales", C.c_void_p),
+                ("refs", C.c_uint64)]
+
+
 class Stats(C.Structure):
     _fields_ = [(n, C.c_uint64) for n in ("lookups", "updates", "rejected_updates",
                                           "duplicate_requests", "live_tickets", "state_bytes",
@@ -115,7 +127,7 @@ ENTRY_POINTS = ("eps_b200_abi_version", "eps_b200_create", "eps_b200_destroy",
                 "eps_b200_comm_destroy", "eps_b200_comm_alltoallv", "eps_b200_comm_allreduce_max",
                 "eps_b200_client_create", "eps_b200_client_destroy", "eps_b200_client_prepare",
                 "eps_b200_client_lookup", "eps_b200_client_push", "eps_b200_client_release",
-                "eps_b200_sync_reduce")
+                "eps_b200_sync_reduce", "eps_b200_apply_rows", "eps_b200_apply_compact")
 
 
 def load_library() -> C.CDLL:
@@ -173,6 +185,9 @@ def load_library() -> C.CDLL:
     lib.eps_b200_client_release.argtypes = [vp, C.c_uint64, P(Status)]
     lib.eps_b200_sync_reduce.argtypes = [vp, C.c_uint32, vp, C.c_uint32, C.c_int32, vp, vp,
                                          C.c_uint64, P(C.c_uint64), vp, P(Status)]
+    lib.eps_b200_apply_rows.argtypes = [vp, P(UpdateContext), vp, C.c_uint64, vp, C.c_int32, vp,
+                                        P(Status)]
+    lib.eps_b200_apply_compact.argtypes = [vp, P(UpdateContext), P(CompactGradients), vp, P(Status)]
     for name in ENTRY_POINTS[1:]:
         if name not in ("eps_b200_destroy", "eps_b200_comm_destroy", "eps_b200_client_destroy"):
             getattr(lib, name).restype = C.c_int
@@ -566,6 +581,38 @@ class ParameterStore:
         _check(self.lib.eps_b200_route_release(self._h, route, C.byref(st)), st)
         getattr(self, "_route_keep", {}).pop(route, None)
 
+    # ---- agent-style updates (CacheBackend::ApplyHost / ApplyCompact)
+    def apply_rows(self, table: int, keys, values, learning_rate: float, beta1_power: float,
+                   beta2_power: float, optimizer_sequence: int = 0, stream=None):
+        """LazyAdam on unique rows with an external optimizer context
+        (eps_b200_apply_rows); values: numpy [rows, dim] or a device tensor."""
+        keys = _host_u64(keys)
+        dev = _is_device(values)
+        if not dev:
+            values = np.ascontiguousarray(values, dtype=np.float32)
+        ctx = UpdateContext(table, learning_rate, beta1_power, beta2_power, optimizer_sequence)
+        st = Status()
+        _check(self.lib.eps_b200_apply_rows(self._h, C.byref(ctx), _ptr(keys), len(keys),
+                                            _ptr(values), int(dev), _stream_ptr(stream),
+                                            C.byref(st)), st)
+
+    def apply_compact(self, table: int, keys, source_values, row_offsets, source_rows, scales,
+                      learning_rate: float, beta1_power: float, beta2_power: float,
+                      optimizer_sequence: int = 0, stream=None):
+        """CompactGradients (CSR) expanded on the device and applied with an external
+        context (eps_b200_apply_compact); host numpy arrays."""
+        keys = _host_u64(keys)
+        sv = np.ascontiguousarray(source_values, dtype=np.float32)
+        ro, sr = _host_u64(row_offsets), _host_u64(source_rows)
+        sc = np.ascontiguousarray(scales, dtype=np.float32)
+        dim = self.dimension(table)
+        cg = CompactGradients(_ptr(keys), len(keys), dim, _ptr(sv), sv.size // dim, _ptr(ro),
+                              _ptr(sr), _ptr(sc), len(sr))
+        ctx = UpdateContext(table, learning_rate, beta1_power, beta2_power, optimizer_sequence)
+        st = Status()
+        _check(self.lib.eps_b200_apply_compact(self._h, C.byref(ctx), C.byref(cg),
+                                               _stream_ptr(stream), C.byref(st)), st)
+
     # ---- synchronous multi-worker round (SynchronousGradientCollector)
     def sync_reduce(self, table: int, workers, reduction: int = REDUCE_SAMPLE_MEAN, stream=None):
         """Reduces one round of worker gradients for `table` on the device
@@ -590,7 +637,7 @@ class ParameterStore:
                                              C.byref(rows), _stream_ptr(stream), C.byref(st)), st)
         return keys[:rows.value], values[:rows.value]
 
-    def apply_rows(self, table: int, keys, values, feature: int = 0, stream=None):
+    def apply_reduced(self, table: int, keys, values, feature: int = 0, stream=None):
         """Applies reduced row gradients as the reference's synchronous applier does
         (src/transport/brpc_synchronous_server.cpp:62-78): one sequence feature of
         the keys, looked up and pushed (one LazyAdam step of the table)."""

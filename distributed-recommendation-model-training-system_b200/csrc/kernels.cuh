@@ -192,6 +192,23 @@ struct SegmentLaunch {
 cudaError_t launch_segments(const SegmentLaunch& p, cudaStream_t stream);
 size_t segment_scratch_bytes(unsigned long long n);
 
+// Agent-style update with an external optimizer context (push.cu):
+// CacheBackend::ApplyHost / ApplyCompact.
+struct ApplyLaunch {
+  PushTable table;                       // lr_t from the UpdateContext
+  const unsigned long long* slots;       // [rows]
+  unsigned long long rows;
+  const float* values;                   // direct rows [rows][dim], or
+  const float* source_values;            // compact: [sources][dim]
+  const unsigned long long* row_offsets; // compact: [rows + 1]
+  const unsigned long long* source_rows; // compact: [refs]
+  const float* scales;                   // compact: [refs]
+  int compact;
+  unsigned int* reject;                  // RejectBits, zeroed by the caller
+  int vec, group, iters;
+};
+cudaError_t launch_apply_rows(const ApplyLaunch& p, cudaStream_t stream);   // two launches
+
 // Synchronous multi-worker round reduce (sync.cu).
 struct SyncWorker {                  // layout of EpsB200WorkerGradients
   const unsigned long long* keys;

@@ -537,6 +537,69 @@ __global__ void __launch_bounds__(kLongThreads) push_long(PushLaunch p, int pass
   }
 }
 
+// --------------------------------------------------- agent-style updates
+// CacheBackend::ApplyHost (src/cache/host_backend.cpp:119-146): LazyAdam with the
+// caller's optimizer context on unique rows, all-or-nothing, no power advance.
+// With `compact`, each row's gradient is first expanded from the CSR references
+// in order (ExpandCompactGradients, src/access/compact_gradients.cpp:27-39:
+// sum = 0; sum += source * scale).  Pass 0 validates, pass 1 applies iff pass 0
+// rejected nothing.
+template <int G, int VEC, int ITERS>
+__global__ void __launch_bounds__(256) apply_rows_kernel(ApplyLaunch p, int pass) {
+  if (pass == 1 && *(volatile const unsigned*)p.reject) return;
+  constexpr int C = VEC * ITERS;
+  const auto grp = cg::tiled_partition<G>(cg::this_thread_block());
+  const unsigned gl = grp.thread_rank();
+  const PushTable& T = p.table;
+  const unsigned D = T.dim;
+  const unsigned long long gid = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) / G;
+  const unsigned long long ngroups = (gridDim.x * (unsigned long long)blockDim.x) / G;
+  unsigned bits = 0, mx = 0;
+  for (unsigned long long u = gid; u < p.rows; u += ngroups) {
+    const unsigned long long slot = p.slots[u];
+    float* row = T.state + slot * 3ull * D;
+    float w[C], m[C], v[C], g[C];
+    load_state<G, VEC, ITERS>(gl, row, D, w, m, v);
+#pragma unroll
+    for (int it = 0; it < ITERS; ++it) {
+      const unsigned col = (it * G + gl) * VEC;
+#pragma unroll
+      for (int x = 0; x < VEC; ++x) {
+        const unsigned d = col + x;
+        float gv = 0.0f;
+        if (d < D) {
+          if (p.compact) {
+            for (unsigned long long j = p.row_offsets[u]; j < p.row_offsets[u + 1]; ++j)
+              gv = __fadd_rn(gv, __fmul_rn(p.source_values[p.source_rows[j] * D + d], p.scales[j]));
+            if (!isfinite(gv)) bits |= kRejectReduction;
+          } else {
+            gv = p.values[u * D + d];
+          }
+        }
+        g[it * VEC + x] = gv;
+      }
+    }
+    bits |= adam_row<G, VEC, ITERS>(gl, T, row, D, g, w, m, v, pass == 1, pass == 0, &mx);
+    if (pass == 1 && gl == 0) T.updates[slot] += 1ull;
+  }
+  bits = cg::reduce(grp, bits, cg::bit_or<unsigned>());
+  if (pass == 0 && gl == 0 && bits) atomicOr(p.reject, bits);
+  if (pass == 1) {
+    mx = cg::reduce(grp, mx, cg::greater<unsigned>());
+    if (gl == 0 && mx) atomicMax(&T.dtable->state_absmax_bits, mx);
+  }
+}
+
+template <int G, int VEC, int ITERS>
+cudaError_t run_apply_rows(const ApplyLaunch& p, cudaStream_t s) {
+  const unsigned long long groups_per_block = 256 / G;
+  const unsigned long long want = (p.rows + groups_per_block - 1) / groups_per_block;
+  const unsigned grid = (unsigned)max(1ull, min(want, 148ull * 8));
+  apply_rows_kernel<G, VEC, ITERS><<<grid, 256, 0, s>>>(p, 0);
+  apply_rows_kernel<G, VEC, ITERS><<<grid, 256, 0, s>>>(p, 1);
+  return cudaGetLastError();
+}
+
 // ----------------------------------------------------------------- finalize
 __global__ void push_finalize(PushLaunch p) {
   PushControl* c = p.control;
@@ -610,6 +673,23 @@ cudaError_t launch_push_apply(const PushLaunch& p, cudaStream_t stream) {
   if (p.iters == 1) return run_key<32, 1, 1>(p, stream);
   if (p.iters == 2) return run_key<32, 1, 2>(p, stream);
   return run_key<32, 1, 4>(p, stream);
+}
+
+cudaError_t launch_apply_rows(const ApplyLaunch& p, cudaStream_t stream) {
+  if (!p.rows) return cudaSuccess;
+  if (p.vec == 4) {
+    switch (p.group) {
+      case 8: return run_apply_rows<8, 4, 1>(p, stream);
+      case 16: return run_apply_rows<16, 4, 1>(p, stream);
+      default:
+        if (p.iters == 1) return run_apply_rows<32, 4, 1>(p, stream);
+        if (p.iters == 2) return run_apply_rows<32, 4, 2>(p, stream);
+        return run_apply_rows<32, 4, 4>(p, stream);
+    }
+  }
+  if (p.iters == 1) return run_apply_rows<32, 1, 1>(p, stream);
+  if (p.iters == 2) return run_apply_rows<32, 1, 2>(p, stream);
+  return run_apply_rows<32, 1, 4>(p, stream);
 }
 
 cudaError_t launch_push_finalize(const PushLaunch& p, cudaStream_t stream) {

@@ -1688,6 +1688,156 @@ int eps_b200_serve_push(EpsB200Store* store, uint64_t ticket, const float* gradi
   });
 }
 
+namespace {
+// Shared body of eps_b200_apply_rows / eps_b200_apply_compact.
+void ApplyWithContext(EpsB200Store& s, const EpsB200UpdateContext& c, const uint64_t* keys,
+                      uint64_t rows, const float* values, bool values_on_device,
+                      const EpsB200CompactGradients* compact, void* stream_arg) {
+  // src/cache/host_backend.cpp:122-125: a usable optimizer context
+  Require(c.beta1_power >= 0 && c.beta1_power < 1 && c.beta2_power >= 0 && c.beta2_power < 1 &&
+          std::isfinite(c.learning_rate) && c.learning_rate > 0, "invalid cache optimizer context");
+  std::lock_guard lock(s.mutex);
+  s.Activate();
+  const Table& t = s.Get(c.table);
+  const auto& d = t.def;
+  const unsigned D = d.dimension;
+  Require(rows == 0 || keys, "null gradient rows");
+  std::vector<unsigned long long> slots(rows);
+  {
+    std::unordered_set<uint64_t> unique;
+    unique.reserve(rows * 2);
+    for (uint64_t i = 0; i < rows; ++i) {
+      Require(unique.insert(keys[i]).second, "duplicate cached gradient row");
+      Require(keys[i] < d.key_space && keys[i] % s.opt.shard_count == s.opt.shard_id,
+              "cached gradient routed to wrong owner");
+      slots[i] = keys[i] / s.opt.shard_count;
+    }
+  }
+  unsigned long long sources = 0, refs = 0;
+  if (compact) {
+    // src/access/compact_gradients.cpp:10-22 (ValidateCompactGradients)
+    const auto& p = *compact;
+    Require(p.dimension == D, "compact CUDA table dimension mismatch");
+    Require(p.row_offsets && p.row_offsets[0] == 0, "invalid compact gradient offsets");
+    for (uint64_t i = 0; i < rows; ++i)
+      Require(p.row_offsets[i] <= p.row_offsets[i + 1], "invalid compact gradient offsets");
+    refs = p.row_offsets[rows];
+    Require(refs == p.refs && (!refs || (p.source_rows && p.scales)), "invalid compact gradient offsets");
+    sources = p.sources;
+    Require(!sources || p.source_values, "null compact gradient values");
+    for (uint64_t j = 0; j < refs; ++j) {
+      Require(p.source_rows[j] < sources, "compact gradient source out of range");
+      Require(std::isfinite(p.scales[j]) && p.scales[j] >= 0, "invalid compact gradient scale");
+    }
+    for (uint64_t j = 0; j < sources * D; ++j)
+      Require(std::isfinite(p.source_values[j]), "non-finite compact gradient value");
+  }
+  cudaStream_t stream = s.Use(stream_arg);
+  if (rows == 0) return;
+  Carver cv;
+  const size_t at_slots = cv.take<unsigned long long>(rows);
+  const size_t at_vals = cv.take<float>(compact ? sources * D : (values_on_device ? 0 : rows * D));
+  const size_t at_off = cv.take<unsigned long long>(compact ? rows + 1 : 0);
+  const size_t at_src = cv.take<unsigned long long>(refs);
+  const size_t at_sc = cv.take<float>(refs);
+  const size_t at_rej = cv.take<unsigned>(1);
+  char* slab = nullptr;
+  Cuda(cudaMallocAsync(reinterpret_cast<void**>(&slab), cv.offset, stream));
+  try {
+    auto P = [&](size_t at) { return slab + at; };
+    auto H2D = [&](size_t at, const void* src, size_t bytes) {
+      if (bytes) Cuda(cudaMemcpyAsync(P(at), src, bytes, cudaMemcpyHostToDevice, stream));
+    };
+    H2D(at_slots, slots.data(), rows * 8);
+    ApplyLaunch lp{};
+    if (compact) {
+      H2D(at_vals, compact->source_values, sources * D * 4);
+      H2D(at_off, compact->row_offsets, (rows + 1) * 8);
+      H2D(at_src, compact->source_rows, refs * 8);
+      H2D(at_sc, compact->scales, refs * 4);
+      lp.source_values = reinterpret_cast<const float*>(P(at_vals));
+      lp.row_offsets = reinterpret_cast<const unsigned long long*>(P(at_off));
+      lp.source_rows = reinterpret_cast<const unsigned long long*>(P(at_src));
+      lp.scales = reinterpret_cast<const float*>(P(at_sc));
+      lp.compact = 1;
+    } else if (values_on_device) {
+      lp.values = values;
+    } else {
+      H2D(at_vals, values, rows * D * 4);
+      lp.values = reinterpret_cast<const float*>(P(at_vals));
+    }
+    Cuda(cudaMemsetAsync(P(at_rej), 0, sizeof(unsigned), stream));
+    PushTable& x = lp.table;
+    x.state = t.state;
+    x.updates = t.updates;
+    x.dtable = t.dtable;
+    x.rows = t.rows;
+    x.learning_rate = d.learning_rate;
+    x.beta1 = d.beta1;
+    x.beta2 = d.beta2;
+    x.epsilon = d.epsilon;
+    x.one_minus_beta1 = 1.0f - d.beta1;
+    x.one_minus_beta2 = 1.0f - d.beta2;
+    x.has_bounds = d.has_weight_bounds;
+    x.bound_min = d.weight_min;
+    x.bound_max = d.weight_max;
+    x.dim = D;
+    // src/cache/host_backend.cpp:127 -- (lr * sqrt(1 - b2p)) / (1 - b1p) in float
+    volatile float one_b2 = 1.0f - c.beta2_power, one_b1 = 1.0f - c.beta1_power;
+    volatile float num = c.learning_rate * std::sqrt((float)one_b2);
+    x.lr_t = num / one_b1;
+    lp.slots = reinterpret_cast<const unsigned long long*>(P(at_slots));
+    lp.rows = rows;
+    lp.reject = reinterpret_cast<unsigned*>(P(at_rej));
+    std::vector<unsigned> dims{D};
+    const bool a16 = !lp.values || (reinterpret_cast<uintptr_t>(lp.values) & 15) == 0;
+    choose_vec(dims, a16, false, &lp.vec, &lp.group, &lp.iters);
+    Cuda(launch_apply_rows(lp, stream));
+    s.stats.kernel_launches += 2;
+    unsigned rej = 0;
+    Cuda(cudaMemcpyAsync(&s.host_status[s.opt.max_live_tickets].lookup_error, P(at_rej),
+                         sizeof(unsigned), cudaMemcpyDeviceToHost, stream));
+    s.Sync(stream);
+    rej = s.host_status[s.opt.max_live_tickets].lookup_error;
+    char* owned = slab;
+    slab = nullptr;
+    Cuda(cudaFreeAsync(owned, stream));
+    s.Done(stream);
+    if (rej) {
+      ++s.stats.rejected_updates;
+      Require(!(compact && (rej & kRejectReduction)), "compact gradient reduction overflow");
+      Require(false, "cached optimizer overflow");
+    }
+    ++s.stats.updates;
+  } catch (...) {
+    if (slab) cudaFreeAsync(slab, stream);
+    throw;
+  }
+}
+}  // namespace
+
+int eps_b200_apply_rows(EpsB200Store* store, const EpsB200UpdateContext* context,
+                        const uint64_t* keys, uint64_t rows, const float* values,
+                        int32_t values_on_device, void* stream, EpsB200Status* status) {
+  return Boundary(status, [&] {
+    auto& s = *Checked(store);
+    Require(context != nullptr, "null optimizer context");
+    Require(rows == 0 || values, "null gradient values");
+    ApplyWithContext(s, *context, keys, rows, values, values_on_device != 0, nullptr, stream);
+  });
+}
+
+int eps_b200_apply_compact(EpsB200Store* store, const EpsB200UpdateContext* context,
+                           const EpsB200CompactGradients* gradients, void* stream,
+                           EpsB200Status* status) {
+  return Boundary(status, [&] {
+    auto& s = *Checked(store);
+    Require(context && gradients, "null compact gradient arguments");
+    ApplyWithContext(s, *context, gradients->keys, gradients->rows, nullptr, false, gradients,
+                     stream);
+  });
+}
+
 int eps_b200_sync_reduce(EpsB200Store* store, uint32_t table, const EpsB200WorkerGradients* workers,
                          uint32_t worker_count, int32_t reduction, uint64_t* keys_out,
                          float* values_out, uint64_t capacity, uint64_t* rows_out, void* stream_arg,

@@ -370,6 +370,41 @@ EPS_B200_EXPORT int eps_b200_client_push(EpsB200Client* client, uint64_t round,
 EPS_B200_EXPORT int eps_b200_client_release(EpsB200Client* client, uint64_t handle,
                                             EpsB200Status* status);
 
+/* ---- Agent-style updates with an external optimizer context: the device
+ * contract of a GpuCacheAgent (include/eps/cache_backend.hpp:12-29).
+ * eps::UpdateContext (include/eps/types.hpp:181-189). */
+typedef struct {
+  uint32_t table;
+  float learning_rate, beta1_power, beta2_power;
+  uint64_t optimizer_sequence;
+} EpsB200UpdateContext;
+/* CacheBackend::ApplyHost (src/cache/host_backend.cpp:119-146): LazyAdam on
+ * unique rows of this shard with the context's powers (the table's own powers
+ * are not advanced), ++row_updates, all-or-nothing ("cached optimizer
+ * overflow").  keys: host; values: [rows][dim] on the host or, with
+ * values_on_device, on the store's device.  Waits for the stream. */
+EPS_B200_EXPORT int eps_b200_apply_rows(EpsB200Store* store, const EpsB200UpdateContext* context,
+                                        const uint64_t* keys, uint64_t rows, const float* values,
+                                        int32_t values_on_device, void* stream,
+                                        EpsB200Status* status);
+/* eps::CompactGradients (include/eps/types.hpp:199-206), host arrays: per target
+ * row (keys[rows]) the ordered references row_offsets[rows + 1] into
+ * source_rows[refs] / scales[refs] over source_values[sources][dimension]. */
+typedef struct {
+  const uint64_t* keys; uint64_t rows;
+  uint32_t dimension;
+  const float* source_values; uint64_t sources;
+  const uint64_t* row_offsets;
+  const uint64_t* source_rows; const float* scales; uint64_t refs;
+} EpsB200CompactGradients;
+/* CacheBackend::ApplyCompact (src/cuda/cache_backend.cu:514-539): validation of
+ * src/access/compact_gradients.cpp:10-22, the rows expanded on the device in
+ * reference order (ExpandCompactGradients, :27-39) and applied as
+ * eps_b200_apply_rows. */
+EPS_B200_EXPORT int eps_b200_apply_compact(EpsB200Store* store, const EpsB200UpdateContext* context,
+                                           const EpsB200CompactGradients* gradients, void* stream,
+                                           EpsB200Status* status);
+
 /* ---- Synchronous multi-worker round reduce:
  * SynchronousGradientCollector::Reduce (src/training/synchronous_gradients.cpp:91-126)
  * on the device, for one table of this shard.  Each worker contributes sorted

@@ -193,6 +193,25 @@ class Oracle:
                                           C.byref(u))
         return rc, rows[:u.value], vals[:u.value]
 
+    def apply_host(self, tid, lr, b1p, b2p, keys, values):
+        """eo_apply_host: LazyAdam with an external context; returns 0 or 1 (rejected)."""
+        t = self.table(tid)
+        keys = _u64(keys)
+        values = _f32(values).reshape(-1)
+        self.lib.eo_apply_host.argtypes = [C.POINTER(_EoTable), C.c_float, C.c_float, C.c_float,
+                                           u64p, f32p, C.c_uint64]
+        return self.lib.eo_apply_host(C.byref(t), lr, b1p, b2p, _ptr(keys, u64p), _ptr(values, f32p),
+                                      len(keys))
+
+    def expand_compact(self, dim, rows, source_values, row_offsets, source_rows, scales):
+        sv = _f32(source_values).reshape(-1)
+        ro, sr, sc = _u64(row_offsets), _u64(source_rows), _f32(scales)
+        out = np.zeros((rows, dim), np.float32)
+        rc = self.lib.eo_expand_compact(C.c_uint32(dim), C.c_uint64(rows), _ptr(sv, f32p),
+                                        C.c_uint64(len(sv) // max(1, dim)), _ptr(ro, u64p),
+                                        _ptr(sr, u64p), _ptr(sc, f32p), _ptr(out, f32p))
+        return rc, out
+
     def sync_reduce(self, dim, workers, reduction):
         """eo_sync_reduce: workers = [(keys u64[k], values f32[k, dim], sample_count)]."""
         W = len(workers)

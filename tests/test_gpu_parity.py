@@ -432,7 +432,7 @@ def test_sync_reduce_known_answers_and_oracle(eps):
         assert np.array_equal(dk.cpu().numpy().astype(np.uint64), ok)
         assert np.array_equal(bits(dv.cpu().numpy()), bits(ov))
     # the reduced rows applied as one sequence lookup + push, as the reference applier does
-    s.apply_rows(1, dk, dv)
+    s.apply_reduced(1, dk, dv)
     feat = Feature(1, 0, SEQUENCE, ok, [0, len(ok)])
     o.lookup([feat])
     assert o.push([feat], [ov]) == 0
@@ -448,3 +448,50 @@ def test_sync_reduce_known_answers_and_oracle(eps):
     nan[0, 5] = float("nan")
     with pytest.raises(eps.EpsError):
         s.sync_reduce(1, [(torch.tensor([7], device=dev), nan, 1)], 0)
+
+
+def test_agent_apply_rows_and_compact(eps):
+    """The GpuCacheAgent device contract: ApplyHost with an external optimizer
+    context and ApplyCompact (CSR expanded in reference order), against the oracle;
+    the table's own powers do not advance; rejections leave the state unchanged."""
+    import torch
+    t = [TableDef(id=1, dimension=40, learning_rate=0.02, init_min=-0.05, init_max=0.05, rows=600,
+                  bounds=(-0.06, 0.06))]
+    s, o = make_store(eps, t), Oracle(t)
+    rng = np.random.default_rng(9)
+    before = s.optimizer_state(1)
+    ctx = (0.03, 0.5, 0.7)                       # lr, beta1_power, beta2_power of the caller
+    keys = rng.choice(600, size=250, replace=False).astype(np.uint64)
+    vals = rng.normal(0, 0.5, size=(250, 40)).astype(F32)
+    s.apply_rows(1, keys, vals, *ctx)
+    assert o.apply_host(1, *ctx, keys, vals) == 0
+    # device values, another context
+    keys2 = rng.choice(600, size=100, replace=False).astype(np.uint64)
+    vals2 = rng.normal(0, 0.5, size=(100, 40)).astype(F32)
+    s.apply_rows(1, keys2, torch.from_numpy(vals2).cuda(), 0.01, 0.81, 0.998)
+    assert o.apply_host(1, 0.01, 0.81, 0.998, keys2, vals2) == 0
+    # compact: 80 target rows referencing 30 source rows with scales
+    tk = rng.choice(600, size=80, replace=False).astype(np.uint64)
+    src = rng.normal(0, 0.3, size=(30, 40)).astype(F32)
+    counts = rng.integers(0, 6, size=80)
+    offs = np.concatenate([[0], np.cumsum(counts)]).astype(np.uint64)
+    srows = rng.integers(0, 30, size=int(offs[-1])).astype(np.uint64)
+    scales = rng.choice([1.0, 0.5, 1.0 / 3.0, 0.125], size=int(offs[-1])).astype(F32)
+    s.apply_compact(1, tk, src, offs, srows, scales, *ctx)
+    rc, expanded = o.expand_compact(40, 80, src, offs, srows, scales)
+    assert rc == 0 and o.apply_host(1, *ctx, tk, expanded) == 0
+    allk = np.arange(600, dtype=np.uint64)
+    w, m, v, u = s.read_state(1, allk)
+    st, upd = o.state(1)
+    assert np.array_equal(bits(w), bits(st[:, 0])) and np.array_equal(bits(m), bits(st[:, 1]))
+    assert np.array_equal(bits(v), bits(st[:, 2])) and np.array_equal(u, upd)
+    assert s.optimizer_state(1) == before             # agents do not advance the powers
+    # rejections: non-finite value, duplicate row, bad context; nothing changes
+    bad = vals.copy()
+    bad[3, 7] = np.inf
+    for args in [(keys, bad, *ctx), (np.array([5, 5], np.uint64), vals[:2], *ctx),
+                 (keys, vals, 0.03, 1.0, 0.7)]:
+        with pytest.raises(eps.EpsError):
+            s.apply_rows(1, *args)
+    w2, m2, v2, u2 = s.read_state(1, allk)
+    assert np.array_equal(bits(w2), bits(w)) and np.array_equal(u2, u)
