@@ -105,6 +105,12 @@ class CompactGradients(C.Structure):
                 ("refs", C.c_uint64)]
 
 
+class SnapshotInfo(C.Structure):
+    _fields_ = [("format", C.c_uint32), ("run", C.c_char * 1025), ("shard", C.c_uint64),
+                ("shard_count", C.c_uint64), ("partition_epoch", C.c_uint64),
+                ("checksum", C.c_uint64), ("tables", C.c_uint64)]
+
+
 class Stats(C.Structure):
     _fields_ = [(n, C.c_uint64) for n in ("lookups", "updates", "rejected_updates",
                                           "duplicate_requests", "live_tickets", "state_bytes",
@@ -115,6 +121,11 @@ PHASES = ("lookup", "sort", "prescan", "apply", "finalize")
 
 
 _lib = None
+
+class SnapshotTable(C.Structure):
+    _fields_ = [("definition", Table), ("optimizer_sequence", C.c_uint64),
+                ("beta1_power", C.c_float), ("beta2_power", C.c_float), ("rows", C.c_uint64)]
+
 
 ENTRY_POINTS = ("eps_b200_abi_version", "eps_b200_create", "eps_b200_destroy",
                 "eps_b200_create_table", "eps_b200_lookup", "eps_b200_lookup_noalloc",
@@ -127,7 +138,9 @@ ENTRY_POINTS = ("eps_b200_abi_version", "eps_b200_create", "eps_b200_destroy",
                 "eps_b200_comm_destroy", "eps_b200_comm_alltoallv", "eps_b200_comm_allreduce_max",
                 "eps_b200_client_create", "eps_b200_client_destroy", "eps_b200_client_prepare",
                 "eps_b200_client_lookup", "eps_b200_client_push", "eps_b200_client_release",
-                "eps_b200_sync_reduce", "eps_b200_apply_rows", "eps_b200_apply_compact")
+                "eps_b200_sync_reduce", "eps_b200_apply_rows", "eps_b200_apply_compact",
+                "eps_b200_snapshot_write", "eps_b200_snapshot_read", "eps_b200_snapshot_inspect",
+                "eps_b200_snapshot_rows")
 
 
 def load_library() -> C.CDLL:
@@ -188,6 +201,10 @@ def load_library() -> C.CDLL:
     lib.eps_b200_apply_rows.argtypes = [vp, P(UpdateContext), vp, C.c_uint64, vp, C.c_int32, vp,
                                         P(Status)]
     lib.eps_b200_apply_compact.argtypes = [vp, P(UpdateContext), P(CompactGradients), vp, P(Status)]
+    lib.eps_b200_snapshot_write.argtypes = [vp, C.c_char_p, C.c_char_p, C.c_int32, P(Status)]
+    lib.eps_b200_snapshot_read.argtypes = [vp, C.c_char_p, C.c_char_p, P(Status)]
+    lib.eps_b200_snapshot_inspect.argtypes = [C.c_char_p, P(SnapshotInfo), vp, C.c_uint64, P(Status)]
+    lib.eps_b200_snapshot_rows.argtypes = [C.c_char_p, C.c_uint64, vp, vp, vp, C.c_uint64, P(Status)]
     for name in ENTRY_POINTS[1:]:
         if name not in ("eps_b200_destroy", "eps_b200_comm_destroy", "eps_b200_client_destroy"):
             getattr(lib, name).restype = C.c_int
@@ -581,6 +598,17 @@ class ParameterStore:
         _check(self.lib.eps_b200_route_release(self._h, route, C.byref(st)), st)
         getattr(self, "_route_keep", {}).pop(route, None)
 
+    # ---- snapshots (DrainAndFlush / Restore, src/store/snapshot.cpp format)
+    def snapshot_write(self, path: str, run: str, all_rows: bool = False):
+        st = Status()
+        _check(self.lib.eps_b200_snapshot_write(self._h, str(path).encode(), run.encode(),
+                                                int(all_rows), C.byref(st)), st)
+
+    def snapshot_read(self, path: str, new_run: str):
+        st = Status()
+        _check(self.lib.eps_b200_snapshot_read(self._h, str(path).encode(), new_run.encode(),
+                                               C.byref(st)), st)
+
     # ---- agent-style updates (CacheBackend::ApplyHost / ApplyCompact)
     def apply_rows(self, table: int, keys, values, learning_rate: float, beta1_power: float,
                    beta2_power: float, optimizer_sequence: int = 0, stream=None):
@@ -662,3 +690,39 @@ def _stream_ptr(stream):
     if hasattr(stream, "cuda_stream"):
         return stream.cuda_stream
     return int(stream)
+
+
+def snapshot_inspect(path: str):
+    """Reads a snapshot file on the host (no GPU): (info dict, [table dicts])."""
+    lib = load_library()
+    info = SnapshotInfo()
+    tabs = (SnapshotTable * 1024)()
+    st = Status()
+    _check(lib.eps_b200_snapshot_inspect(str(path).encode(), C.byref(info), tabs, 1024,
+                                         C.byref(st)), st)
+    meta = {"format": info.format, "run": info.run.decode(), "shard": info.shard,
+            "shard_count": info.shard_count, "partition_epoch": info.partition_epoch,
+            "checksum": info.checksum}
+    out = []
+    for i in range(info.tables):
+        t = tabs[i]
+        d = t.definition
+        out.append({"id": d.id, "dimension": d.dimension, "learning_rate": d.learning_rate,
+                    "has_weight_bounds": d.has_weight_bounds, "initialization_min": d.initialization_min,
+                    "initialization_seed": d.initialization_seed,
+                    "optimizer_sequence": t.optimizer_sequence, "beta1_power": t.beta1_power,
+                    "beta2_power": t.beta2_power, "rows": t.rows})
+    return meta, out
+
+
+def snapshot_rows(path: str, table_index: int, rows: int, dim: int):
+    """One table's rows of a snapshot file: (keys, row_updates, w, m, v)."""
+    lib = load_library()
+    keys = np.zeros(max(1, rows), np.uint64)
+    upd = np.zeros(max(1, rows), np.uint64)
+    state = np.zeros((max(1, rows), 3, dim), np.float32)
+    st = Status()
+    _check(lib.eps_b200_snapshot_rows(str(path).encode(), table_index, keys.ctypes.data,
+                                      upd.ctypes.data, state.ctypes.data, max(1, rows),
+                                      C.byref(st)), st)
+    return keys[:rows], upd[:rows], state[:rows, 0], state[:rows, 1], state[:rows, 2]

@@ -17,6 +17,8 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
+#include <unistd.h>
 #include <cstring>
 #include <deque>
 #include <map>
@@ -1942,6 +1944,389 @@ int eps_b200_sync_reduce(EpsB200Store* store, uint32_t table, const EpsB200Worke
       if (slab) cudaFreeAsync(slab, stream);
       throw;
     }
+  });
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ snapshots
+// The reference's checksummed shard snapshot (src/store/snapshot.cpp): little-
+// endian u64 / f32 fields, FNV-1a 64 over every byte before the trailing
+// checksum.  Layout (format 2; format 1 lacks the weight-bounds field):
+//   magic | run (u64 length + bytes) | shard | shard count | partition epoch |
+//   tables | per table (ascending id): id, dim, shard count, epoch, lr, b1, b2,
+//   eps, initial powers, bounds flag [+ min, max], init min/max, seed,
+//   optimizer sequence, beta1/beta2 powers, rows, per row: key, row_updates,
+//   w[D] m[D] v[D] | checksum.
+namespace {
+constexpr uint64_t kSnapMagicV1 = 0x3153504541524853ULL;
+constexpr uint64_t kSnapMagicV2 = 0x3253504541524853ULL;
+constexpr uint64_t kFnvOffset = 14695981039346656037ULL;
+constexpr uint64_t kFnvPrime = 1099511628211ULL;
+
+struct SnapWriter {
+  FILE* f;
+  uint64_t hash = kFnvOffset;
+  std::vector<unsigned char> buf;
+  void Bytes(const void* p, size_t n, bool hashed = true) {
+    const auto* c = static_cast<const unsigned char*>(p);
+    if (hashed) for (size_t i = 0; i < n; ++i) hash = (hash ^ c[i]) * kFnvPrime;
+    buf.insert(buf.end(), c, c + n);
+    if (buf.size() >= (1u << 20)) Flush();
+  }
+  void U64(uint64_t v, bool hashed = true) {
+    unsigned char b[8];
+    for (int i = 0; i < 8; ++i) b[i] = (v >> (8 * i)) & 255;
+    Bytes(b, 8, hashed);
+  }
+  void F32(float x) {
+    uint32_t u;
+    std::memcpy(&u, &x, 4);
+    unsigned char b[4];
+    for (int i = 0; i < 4; ++i) b[i] = (u >> (8 * i)) & 255;
+    Bytes(b, 4);
+  }
+  void Flush() {
+    if (!buf.empty())
+      Require(std::fwrite(buf.data(), 1, buf.size(), f) == buf.size(), "snapshot write failed",
+              EPS_B200_UNAVAILABLE);
+    buf.clear();
+  }
+};
+
+struct SnapReader {
+  const std::vector<unsigned char>& d;
+  size_t pos = 0;
+  uint64_t hash = kFnvOffset;
+  void Bytes(void* p, size_t n, bool hashed = true) {
+    Require(pos + n <= d.size(), "snapshot truncated", EPS_B200_UNAVAILABLE);
+    std::memcpy(p, d.data() + pos, n);
+    if (hashed) for (size_t i = 0; i < n; ++i) hash = (hash ^ d[pos + i]) * kFnvPrime;
+    pos += n;
+  }
+  uint64_t U64(bool hashed = true) {
+    unsigned char b[8];
+    Bytes(b, 8, hashed);
+    uint64_t v = 0;
+    for (int i = 0; i < 8; ++i) v |= uint64_t(b[i]) << (8 * i);
+    return v;
+  }
+  float F32() {
+    unsigned char b[4];
+    Bytes(b, 4);
+    uint32_t u = 0;
+    for (int i = 0; i < 4; ++i) u |= uint32_t(b[i]) << (8 * i);
+    float x;
+    std::memcpy(&x, &u, 4);
+    Require(std::isfinite(x), "snapshot contains non-finite state");
+    return x;
+  }
+};
+
+struct SnapTable {
+  EpsB200Table def{};
+  uint64_t sequence = 0;
+  float beta1_power = 0, beta2_power = 0;
+  std::vector<uint64_t> keys, updates;
+  std::vector<float> state;                 // [rows][3D] (w | m | v)
+};
+
+std::vector<SnapTable> ParseSnapshot(const std::vector<unsigned char>& bytes, std::string* run,
+                                     uint64_t* shard, uint64_t* count, uint64_t* epoch) {
+  SnapReader r{bytes};
+  const uint64_t magic = r.U64();
+  Require(magic == kSnapMagicV1 || magic == kSnapMagicV2, "unsupported snapshot format");
+  const uint64_t n = r.U64();
+  Require(n <= 1024, "snapshot string too long");
+  run->resize(n);
+  r.Bytes(run->data(), n);
+  *shard = r.U64();
+  *count = r.U64();
+  *epoch = r.U64();
+  const uint64_t tables = r.U64();
+  Require(tables <= 1024, "snapshot table count exceeds limit");
+  std::vector<SnapTable> out(tables);
+  for (auto& t : out) {
+    auto& d = t.def;
+    const uint64_t id = r.U64(), dim = r.U64(), sc = r.U64();
+    Require(id <= UINT32_MAX && dim && dim <= 65536 && sc <= UINT32_MAX,
+            "invalid snapshot table definition");
+    d.id = (uint32_t)id;
+    d.dimension = (uint32_t)dim;
+    d.shard_count = (uint32_t)sc;
+    d.partition_epoch = r.U64();
+    d.learning_rate = r.F32(); d.beta1 = r.F32(); d.beta2 = r.F32(); d.epsilon = r.F32();
+    d.initial_beta1_power = r.F32(); d.initial_beta2_power = r.F32();
+    if (magic == kSnapMagicV2) {
+      const uint64_t enabled = r.U64();
+      Require(enabled <= 1, "invalid snapshot weight-bounds flag");
+      d.has_weight_bounds = (int32_t)enabled;
+      if (enabled) { d.weight_min = r.F32(); d.weight_max = r.F32(); }
+    }
+    d.initialization_min = r.F32();
+    d.initialization_max = r.F32();
+    d.initialization_seed = r.U64();
+    t.sequence = r.U64();
+    t.beta1_power = r.F32();
+    t.beta2_power = r.F32();
+    Require(t.beta1_power >= 0 && t.beta1_power < 1 && t.beta2_power >= 0 && t.beta2_power < 1,
+            "invalid snapshot optimizer state");
+    const uint64_t rows = r.U64();
+    const uint64_t row_bytes = 16 + 12 * dim;
+    Require(rows <= (bytes.size() - r.pos) / row_bytes, "snapshot truncated", EPS_B200_UNAVAILABLE);
+    t.keys.resize(rows);
+    t.updates.resize(rows);
+    t.state.resize(rows * 3 * dim);
+    for (uint64_t j = 0; j < rows; ++j) {
+      t.keys[j] = r.U64();
+      t.updates[j] = r.U64();
+      float* row = t.state.data() + j * 3 * dim;
+      for (uint64_t i = 0; i < 3 * dim; ++i) row[i] = r.F32();
+      for (uint64_t i = 2 * dim; i < 3 * dim; ++i)
+        Require(row[i] >= 0, "negative second moment in snapshot");
+    }
+  }
+  const uint64_t actual = r.hash;
+  const uint64_t expected = r.U64(false);
+  Require(actual == expected, "snapshot checksum mismatch");
+  Require(r.pos == bytes.size(), "snapshot contains trailing data");
+  return out;
+}
+
+bool SameOptimizer(const EpsB200Table& a, const EpsB200Table& b) {
+  return a.dimension == b.dimension && a.learning_rate == b.learning_rate && a.beta1 == b.beta1 &&
+         a.beta2 == b.beta2 && a.epsilon == b.epsilon &&
+         a.initial_beta1_power == b.initial_beta1_power &&
+         a.initial_beta2_power == b.initial_beta2_power &&
+         a.has_weight_bounds == b.has_weight_bounds &&
+         (!a.has_weight_bounds || (a.weight_min == b.weight_min && a.weight_max == b.weight_max)) &&
+         a.initialization_min == b.initialization_min &&
+         a.initialization_max == b.initialization_max &&
+         a.initialization_seed == b.initialization_seed;
+}
+}  // namespace
+
+extern "C" {
+
+namespace {
+std::vector<unsigned char> ReadFile(const char* path) {
+  std::vector<unsigned char> bytes;
+  FILE* f = std::fopen(path, "rb");
+  Require(f != nullptr, "cannot open snapshot", EPS_B200_UNAVAILABLE);
+  unsigned char chunk[1 << 16];
+  size_t n;
+  while ((n = std::fread(chunk, 1, sizeof(chunk), f)) > 0) bytes.insert(bytes.end(), chunk, chunk + n);
+  std::fclose(f);
+  return bytes;
+}
+}  // namespace
+
+int eps_b200_snapshot_inspect(const char* path, EpsB200SnapshotInfo* info,
+                              EpsB200SnapshotTable* tables, uint64_t capacity,
+                              EpsB200Status* status) {
+  return Boundary(status, [&] {
+    Require(path && info, "invalid snapshot arguments");
+    auto bytes = ReadFile(path);
+    std::string run;
+    uint64_t shard = 0, count = 0, epoch = 0;
+    auto parsed = ParseSnapshot(bytes, &run, &shard, &count, &epoch);
+    std::memset(info, 0, sizeof(*info));
+    uint64_t magic = 0;
+    for (int i = 0; i < 8; ++i) magic |= uint64_t(bytes[i]) << (8 * i);
+    info->format = magic == kSnapMagicV2 ? 2 : 1;
+    std::strncpy(info->run, run.c_str(), sizeof(info->run) - 1);
+    info->shard = shard;
+    info->shard_count = count;
+    info->partition_epoch = epoch;
+    for (int i = 0; i < 8; ++i) info->checksum |= uint64_t(bytes[bytes.size() - 8 + i]) << (8 * i);
+    info->tables = parsed.size();
+    for (uint64_t i = 0; i < parsed.size() && tables && i < capacity; ++i) {
+      auto& t = parsed[i];
+      tables[i] = EpsB200SnapshotTable{t.def, t.sequence, t.beta1_power, t.beta2_power, t.keys.size()};
+    }
+  });
+}
+
+int eps_b200_snapshot_rows(const char* path, uint64_t table_index, uint64_t* keys,
+                           uint64_t* row_updates, float* state, uint64_t capacity,
+                           EpsB200Status* status) {
+  return Boundary(status, [&] {
+    Require(path != nullptr, "invalid snapshot arguments");
+    auto bytes = ReadFile(path);
+    std::string run;
+    uint64_t shard = 0, count = 0, epoch = 0;
+    auto parsed = ParseSnapshot(bytes, &run, &shard, &count, &epoch);
+    Require(table_index < parsed.size(), "snapshot table index out of range");
+    auto& t = parsed[table_index];
+    Require(capacity >= t.keys.size(), "snapshot row capacity too small");
+    if (keys) std::memcpy(keys, t.keys.data(), t.keys.size() * 8);
+    if (row_updates) std::memcpy(row_updates, t.updates.data(), t.updates.size() * 8);
+    if (state) std::memcpy(state, t.state.data(), t.state.size() * 4);
+  });
+}
+
+int eps_b200_snapshot_write(EpsB200Store* store, const char* path, const char* run,
+                            int32_t all_rows, EpsB200Status* status) {
+  return Boundary(status, [&] {
+    auto& s = *Checked(store);
+    Require(path && run && std::strlen(run) > 0 && std::strlen(run) <= 1024, "invalid snapshot arguments");
+    std::lock_guard lock(s.mutex);
+    s.Activate();
+    Require(s.tickets.empty(), "snapshot needs a drained store (live lookup tickets)",
+            EPS_B200_UNAVAILABLE);
+    cudaStream_t stream = s.Use(nullptr);
+    s.Sync(stream);
+    const std::string pending = std::string(path) + ".pending";
+    FILE* f = std::fopen(pending.c_str(), "wbx");
+    Require(f != nullptr, "cannot create snapshot staging file", EPS_B200_UNAVAILABLE);
+    try {
+      SnapWriter w{f};
+      w.U64(kSnapMagicV2);
+      const uint64_t n = std::strlen(run);
+      w.U64(n);
+      w.Bytes(run, n);
+      w.U64(s.opt.shard_id);
+      w.U64(s.opt.shard_count);
+      w.U64(s.opt.partition_epoch);
+      w.U64(s.tables.size());
+      for (auto& [id, t] : s.tables) {             // ascending id, as the reference's map
+        const auto& d = t.def;
+        const unsigned D = d.dimension;
+        w.U64(d.id); w.U64(D); w.U64(s.opt.shard_count); w.U64(d.partition_epoch);
+        w.F32(d.learning_rate); w.F32(d.beta1); w.F32(d.beta2); w.F32(d.epsilon);
+        w.F32(d.initial_beta1_power); w.F32(d.initial_beta2_power);
+        w.U64(d.has_weight_bounds ? 1 : 0);
+        if (d.has_weight_bounds) { w.F32(d.weight_min); w.F32(d.weight_max); }
+        w.F32(d.initialization_min); w.F32(d.initialization_max); w.U64(d.initialization_seed);
+        DeviceTable dt{};
+        Cuda(cudaMemcpy(&dt, t.dtable, sizeof(dt), cudaMemcpyDeviceToHost));
+        w.U64(dt.optimizer_sequence); w.F32(dt.beta1_power); w.F32(dt.beta2_power);
+        // rows: every updated row (rows never updated hold their initial value,
+        // which a restore reproduces), or every row with all_rows
+        std::vector<unsigned long long> upd(t.rows);
+        if (t.rows) Cuda(cudaMemcpy(upd.data(), t.updates, t.rows * 8, cudaMemcpyDeviceToHost));
+        uint64_t rows = 0;
+        for (auto u : upd) rows += (all_rows || u) ? 1 : 0;
+        w.U64(rows);
+        const uint64_t chunk = std::max<uint64_t>(1, (64ull << 20) / (12ull * D));
+        std::vector<float> st;
+        for (uint64_t b = 0; b < t.rows; b += chunk) {
+          const uint64_t e = std::min<uint64_t>(t.rows, b + chunk);
+          bool any = all_rows != 0;
+          for (uint64_t i = b; i < e && !any; ++i) any = upd[i] != 0;
+          if (!any) continue;
+          st.resize((e - b) * 3ull * D);
+          Cuda(cudaMemcpy(st.data(), t.state + b * 3ull * D, st.size() * 4, cudaMemcpyDeviceToHost));
+          for (uint64_t i = b; i < e; ++i) {
+            if (!all_rows && !upd[i]) continue;
+            w.U64(i * s.opt.shard_count + s.opt.shard_id);     // key of slot i
+            w.U64(upd[i]);
+            const float* row = st.data() + (i - b) * 3ull * D;
+            for (unsigned k = 0; k < 3 * D; ++k) w.F32(row[k]);
+          }
+        }
+      }
+      w.U64(w.hash, false);
+      w.Flush();
+      Require(std::fflush(f) == 0 && ::fsync(fileno(f)) == 0, "snapshot fsync failed",
+              EPS_B200_UNAVAILABLE);
+      std::fclose(f);
+      f = nullptr;
+      // link: an atomic publication that never overwrites an existing snapshot
+      Require(::link(pending.c_str(), path) == 0, "snapshot already exists or cannot be published",
+              EPS_B200_UNAVAILABLE);
+      ::unlink(pending.c_str());
+    } catch (...) {
+      if (f) std::fclose(f);
+      ::unlink(pending.c_str());
+      throw;
+    }
+    s.Done(stream);
+  });
+}
+
+int eps_b200_snapshot_read(EpsB200Store* store, const char* path, const char* new_run,
+                           EpsB200Status* status) {
+  return Boundary(status, [&] {
+    auto& s = *Checked(store);
+    Require(path && new_run, "invalid snapshot arguments");
+    std::vector<unsigned char> bytes;
+    {
+      FILE* f = std::fopen(path, "rb");
+      Require(f != nullptr, "cannot open snapshot", EPS_B200_UNAVAILABLE);
+      unsigned char chunk[1 << 16];
+      size_t n;
+      while ((n = std::fread(chunk, 1, sizeof(chunk), f)) > 0) bytes.insert(bytes.end(), chunk, chunk + n);
+      std::fclose(f);
+    }
+    std::string old_run;
+    uint64_t shard = 0, count = 0, epoch = 0;
+    auto tables = ParseSnapshot(bytes, &old_run, &shard, &count, &epoch);
+    // src/store/snapshot.cpp:226-231: a restore starts a new run on the same partition
+    Require(old_run != new_run, "restore requires a new run ID");
+    std::lock_guard lock(s.mutex);
+    s.Activate();
+    Require(shard == s.opt.shard_id && count == s.opt.shard_count && epoch == s.opt.partition_epoch,
+            "snapshot partition does not match server");
+    Require(s.tickets.empty(), "restore needs a drained store (live lookup tickets)",
+            EPS_B200_UNAVAILABLE);
+    Require(tables.size() == s.tables.size(), "snapshot table set does not match the store");
+    for (auto& t : tables) {
+      auto it = s.tables.find(t.def.id);
+      Require(it != s.tables.end(), "snapshot table is not defined in the store");
+      Require(SameOptimizer(t.def, it->second.def) && t.def.shard_count == count &&
+              t.def.partition_epoch == epoch, "snapshot table definition differs from the store's");
+      for (auto k : t.keys)
+        Require(k % count == shard && k < it->second.def.key_space,
+                "snapshot row outside this shard's key space");
+    }
+    // every check passed: re-initialise, then write the snapshot's rows and powers
+    cudaStream_t stream = s.Use(nullptr);
+    for (auto& t : tables) {
+      Table& tab = s.tables.at(t.def.id);
+      const unsigned D = tab.def.dimension;
+      const auto& d = tab.def;
+      InitLaunch ip{tab.state, tab.updates, tab.rows, D, s.opt.shard_count, s.opt.shard_id,
+                    d.id, d.initialization_seed, d.initialization_min, d.initialization_max,
+                    d.has_weight_bounds, d.weight_min, d.weight_max};
+      Cuda(launch_init(ip, stream));
+      DeviceTable dt{};
+      dt.beta1_power = t.beta1_power;
+      dt.beta2_power = t.beta2_power;
+      dt.optimizer_sequence = t.sequence;
+      float bound = std::max(std::fabs(d.initialization_min), std::fabs(d.initialization_max));
+      if (d.has_weight_bounds)
+        bound = std::max(bound, std::max(std::fabs(d.weight_min), std::fabs(d.weight_max)));
+      std::memcpy(&dt.state_absmax_bits, &bound, 4);
+      Cuda(cudaMemcpyAsync(tab.dtable, &dt, sizeof(dt), cudaMemcpyHostToDevice, stream));
+      s.Sync(stream);
+      const uint64_t rows = t.keys.size();
+      if (!rows) continue;
+      std::vector<unsigned long long> slots(rows);
+      for (uint64_t j = 0; j < rows; ++j) slots[j] = t.keys[j];
+      char* buf = nullptr;
+      const size_t kb = align256(rows * 8), pb = align256(rows * 12ull * D);
+      Cuda(cudaMallocAsync(reinterpret_cast<void**>(&buf), kb + pb + align256(rows * 8), stream));
+      try {
+        Cuda(cudaMemcpyAsync(buf, slots.data(), rows * 8, cudaMemcpyHostToDevice, stream));
+        Cuda(cudaMemcpyAsync(buf + kb, t.state.data(), rows * 12ull * D, cudaMemcpyHostToDevice, stream));
+        Cuda(cudaMemcpyAsync(buf + kb + pb, t.updates.data(), rows * 8, cudaMemcpyHostToDevice, stream));
+        Cuda(launch_write_rows(tab.state, tab.updates, D, tab.rows, s.opt.shard_count,
+                               reinterpret_cast<unsigned long long*>(buf), rows,
+                               reinterpret_cast<float*>(buf + kb),
+                               reinterpret_cast<unsigned long long*>(buf + kb + pb), tab.dtable,
+                               stream));
+        char* owned = buf;
+        buf = nullptr;
+        Cuda(cudaFreeAsync(owned, stream));
+        s.Sync(stream);
+      } catch (...) {
+        cudaStreamSynchronize(stream);
+        if (buf) cudaFreeAsync(buf, stream);
+        throw;
+      }
+    }
+    s.Done(stream);
   });
 }
 

@@ -433,6 +433,45 @@ EPS_B200_EXPORT int eps_b200_sync_reduce(EpsB200Store* store, uint32_t table,
                                          uint64_t capacity, uint64_t* rows, void* stream,
                                          EpsB200Status* status);
 
+/* ---- Snapshots in the reference's checksummed shard format (src/store/snapshot.cpp):
+ * little-endian, FNV-1a 64 checksum, format 2 (with weight bounds; format 1
+ * files are read too).  Write = DrainAndFlush's state file
+ * (include/eps/runtime.hpp:116-117): needs no live tickets; holds every row
+ * that has been updated (all_rows = 0; a row never updated holds its initial
+ * value, which a restore reproduces) or every row of the shard (all_rows = 1);
+ * published atomically, never over an existing file.  Read = Restore
+ * (include/eps/runtime.hpp:121): new_run must differ from the file's run, the
+ * partition (shard, shard count, epoch) and table definitions must match the
+ * store's (tables are created first, with their key space); all checks pass
+ * before any state changes; then the tables are re-initialised and the file's
+ * rows, counters, powers and sequences loaded. */
+/* Host-only reading of a snapshot file (no GPU needed; the reference's
+ * InspectSnapshot, src/store/snapshot.cpp:190-214, plus the rows): the header,
+ * per table its definition, optimizer sequence, powers and row count, and one
+ * table's rows (keys, row_updates, [rows][3][dim] = w | m | v).  The checksum
+ * and every field are validated as by Restore. */
+typedef struct {
+  uint32_t format;                 /* 1 or 2 */
+  char run[1025];
+  uint64_t shard, shard_count, partition_epoch, checksum, tables;
+} EpsB200SnapshotInfo;
+typedef struct {
+  EpsB200Table definition;         /* key_space = 0 (not part of the format) */
+  uint64_t optimizer_sequence;
+  float beta1_power, beta2_power;
+  uint64_t rows;
+} EpsB200SnapshotTable;
+EPS_B200_EXPORT int eps_b200_snapshot_inspect(const char* path, EpsB200SnapshotInfo* info,
+                                              EpsB200SnapshotTable* tables, uint64_t capacity,
+                                              EpsB200Status* status);
+EPS_B200_EXPORT int eps_b200_snapshot_rows(const char* path, uint64_t table_index, uint64_t* keys,
+                                           uint64_t* row_updates, float* state, uint64_t capacity,
+                                           EpsB200Status* status);
+EPS_B200_EXPORT int eps_b200_snapshot_write(EpsB200Store* store, const char* path, const char* run,
+                                            int32_t all_rows, EpsB200Status* status);
+EPS_B200_EXPORT int eps_b200_snapshot_read(EpsB200Store* store, const char* path,
+                                           const char* new_run, EpsB200Status* status);
+
 /* CpuParameterService::Stats (include/eps/runtime.hpp:134). */
 EPS_B200_EXPORT int eps_b200_stats(EpsB200Store* store, EpsB200Stats* stats, EpsB200Status* status);
 

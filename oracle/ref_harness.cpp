@@ -58,12 +58,15 @@ struct RhFeature {
   const std::uint64_t* offsets; std::uint64_t offset_count;
 };
 
-void* rh_create(std::uint32_t shard_count, std::uint64_t state_bytes, char* err) {
+void* rh_create_run(std::uint32_t shard_count, std::uint64_t state_bytes, const char* run,
+                    const char* snapshot_dir, char* err) {
   try {
     auto h = std::make_unique<Harness>();
+    if (run) h->run = run;
     for (std::uint32_t s = 0; s < shard_count; ++s) {
       RuntimeOptions o;
       o.run_id = h->run; o.shard_id = s; o.shard_count = shard_count;
+      if (snapshot_dir) o.snapshot_directory = snapshot_dir;
       // Raise the default request/ticket budgets (include/eps/runtime.hpp:20-23)
       // so the benchmark batch sizes are admitted.
       o.state_bytes = state_bytes;
@@ -79,7 +82,33 @@ void* rh_create(std::uint32_t shard_count, std::uint64_t state_bytes, char* err)
   } catch (const std::exception& e) { Message(err, e.what()); return nullptr; }
 }
 
+void* rh_create(std::uint32_t shard_count, std::uint64_t state_bytes, char* err) {
+  return rh_create_run(shard_count, state_bytes, nullptr, nullptr, err);
+}
+
 void rh_destroy(void* p) { delete static_cast<Harness*>(p); }
+
+// CpuParameterService::DrainAndFlush (include/eps/runtime.hpp:116-117) on one
+// shard: writes its snapshot state file; the path goes to path_out.
+int rh_snapshot(void* p, std::uint32_t shard, const char* id, char* path_out, char* err) {
+  auto& h = *static_cast<Harness*>(p);
+  try {
+    SnapshotMetadata meta;
+    const int rc = Take(h.shards.at(shard)->DrainAndFlush(id).get(), &meta, err);
+    if (rc) return rc;
+    Message(path_out, meta.state_files.at(0));
+    return 0;
+  } catch (const std::exception& e) { Message(err, e.what()); return 6; }
+}
+
+// CpuParameterService::Restore (include/eps/runtime.hpp:121) of one shard.
+int rh_restore(void* p, std::uint32_t shard, const char* path, char* err) {
+  auto& h = *static_cast<Harness*>(p);
+  try {
+    Ack ack;
+    return Take(h.shards.at(shard)->Restore(path).get(), &ack, err);
+  } catch (const std::exception& e) { Message(err, e.what()); return 6; }
+}
 
 int rh_create_table(void* p, const RhTable* t, char* err) {
   auto& h = *static_cast<Harness*>(p);

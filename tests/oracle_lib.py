@@ -260,20 +260,30 @@ def reference_available():
 class Reference:
     """The reference's own CPU path (CpuParameterService x n + DistributedClient)."""
 
-    def __init__(self, tables: list[TableDef], shards: int = 1, state_bytes: int = 8 << 30):
+    def __init__(self, tables: list[TableDef], shards: int = 1, state_bytes: int = 8 << 30,
+                 run: str | None = None, snapshot_dir: str | None = None, define: bool = True):
         self.lib = _load(REF_SO)
-        self.lib.rh_create.restype = C.c_void_p
-        self.lib.rh_create.argtypes = [C.c_uint32, C.c_uint64, C.c_char_p]
+        self.lib.rh_create_run.restype = C.c_void_p
+        self.lib.rh_create_run.argtypes = [C.c_uint32, C.c_uint64, C.c_char_p, C.c_char_p,
+                                           C.c_char_p]
         for name in ("rh_create_table", "rh_lookup", "rh_push", "rh_release", "rh_read",
-                     "rh_stats"):
+                     "rh_stats", "rh_snapshot", "rh_restore"):
             getattr(self.lib, name).restype = C.c_int
         self.lib.rh_destroy.argtypes = [C.c_void_p]
         self.err = C.create_string_buffer(1024)
-        self.h = self.lib.rh_create(shards, state_bytes, self.err)
+        self.h = self.lib.rh_create_run(shards, state_bytes,
+                                        run.encode() if run else None,
+                                        snapshot_dir.encode() if snapshot_dir else None, self.err)
         if not self.h:
             raise RuntimeError(self.err.value.decode())
         self._defs = {t.id: t for t in tables}
-        for t in tables:
+        if define:                             # a service to Restore into stays empty
+            self.define()
+
+    def define(self):
+        """CreateTable through the client (idempotent on shards that already
+        hold the table, e.g. after Restore)."""
+        for t in self._defs.values():
             rt = _RhTable(t.id, t.dimension, t.learning_rate, t.beta1, t.beta2, t.epsilon,
                           t.initial_beta1_power, t.initial_beta2_power,
                           1 if t.bounds else 0, *(t.bounds if t.bounds else (0.0, 0.0)),
@@ -326,6 +336,16 @@ class Reference:
         self._check(self.lib.rh_read(C.c_void_p(self.h), tid, key, _ptr(w, f32p),
                                      _ptr(m, f32p), _ptr(v, f32p), C.byref(upd), self.err))
         return w, m, v, upd.value
+
+    def snapshot(self, snapshot_id: str, shard: int = 0) -> str:
+        """DrainAndFlush of one shard; returns the state file path."""
+        out = C.create_string_buffer(1024)
+        self._check(self.lib.rh_snapshot(C.c_void_p(self.h), shard, snapshot_id.encode(), out,
+                                         self.err))
+        return out.value.decode()
+
+    def restore(self, path: str, shard: int = 0):
+        self._check(self.lib.rh_restore(C.c_void_p(self.h), shard, path.encode(), self.err))
 
     def stats(self):
         out = (C.c_uint64 * 4)()
