@@ -22,7 +22,7 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libeps_b200.so")
 
 SOURCES = ["store.cu", "lookup.cu", "sort.cu", "push.cu", "route.cu", "noalloc.cu", "runtime.cu",
-           "comm.cu", "client.cu", "sync.cu"]
+           "comm.cu", "client.cu", "sync.cu", "runtime_api.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "--fmad=false", "-Xcompiler", "-fPIC",
          "-Xcompiler", "-fvisibility=hidden", "-I", CSRC, "-I", INCLUDE]
