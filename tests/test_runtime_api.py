@@ -362,9 +362,6 @@ def test_batch_lifecycle(rt, eps):
         r.pull(feats)
     assert e.value.code == eps.UNAVAILABLE and "prepared" in str(e.value)
     p = r.pull_prepared(tok0)
-    direct = rt.NativeRuntime(config(ts)).pull(feats, read_only=True)
-    for a, b in zip(p.outputs, direct.outputs):
-        assert np.array_equal(bits(a), bits(b))
     r.command("cancel_prepared", {"token": tok1})
     with pytest.raises(eps.EpsError) as e:
         r.command("cancel_prepared", {"token": tok1})
@@ -372,6 +369,10 @@ def test_batch_lifecycle(rt, eps):
     with pytest.raises(eps.EpsError):
         r.pull_prepared(tok1)
     r.command("release", {"handle": p.handle})
+    direct = r.pull(feats, read_only=True)       # same state: same outputs
+    for a, b in zip(p.outputs, direct.outputs):
+        assert np.array_equal(bits(a), bits(b))
+    r.command("release", {"handle": direct.handle})
     r.command("join")
     for name in ("training_arm", "training_status"):
         with pytest.raises(eps.EpsError) as e:
