@@ -108,6 +108,26 @@ struct LongRecord {
   unsigned int npieces;
 };
 
+// One coalesced row of a lookup ticket (rows[u] for run u of the sorted keys),
+// prepared on the side stream after the coalescing sort so that the push reads
+// everything it needs about a row in one 16-byte load:
+//   b < 2^31  -- a single-occurrence row: a = its gradient source, b = the
+//                float bits of its row scale (positive);
+//   b = 2^31 | len, len in 2..long_run -- a = the piece that reduces all of
+//                its occurrences in order (its gradient is part[a]);
+//   b = kRowSkip -- a padding row or a long row (handled by pieces).
+struct alignas(16) RowRec {
+  unsigned long long key;       // composite (table rank, slot)
+  unsigned int a, b;
+};
+constexpr unsigned int kRowMulti = 0x80000000u;
+constexpr unsigned int kRowSkip = 0xFFFFFFFFu;
+// Counts of the row plan: `piece_count` pieces (one per row with 2..long_run
+// occurrences, ceil(len / kPiece) per long row) and `long_count` LongRecords.
+struct RowPlan {
+  unsigned int long_count, piece_count, reserved0, reserved1;
+};
+
 constexpr int kLongRun = 64;    // rows with more occurrences than this are "long"
 #ifndef EPS_PIECE
 #define EPS_PIECE 32

@@ -192,6 +192,25 @@ struct SegmentLaunch {
 cudaError_t launch_segments(const SegmentLaunch& p, cudaStream_t stream);
 size_t segment_scratch_bytes(unsigned long long n);
 
+// The push's row plan (RowRec / RowPlan), built from the segments at lookup time.
+struct PlanLaunch {
+  const void* keys;                // sorted KeyT[n]
+  const unsigned int* srcs;        // sorted sources
+  const unsigned int* seg_start;   // [U + 1]
+  const unsigned int* seg_total;   // U (device)
+  const LookupFeature* features;   // scale_base per feature
+  const float* row_scale;
+  unsigned long long n;
+  int key64;
+  unsigned int slot_bits, table_count;
+  unsigned long long long_run;
+  RowRec* rows;                    // [n]
+  RowPlan* plan;                   // zeroed
+  uint2* pieces;
+  LongRecord* longs;
+};
+cudaError_t launch_row_plan(const PlanLaunch& p, cudaStream_t stream);
+
 // Agent-style update with an external optimizer context (push.cu):
 // CacheBackend::ApplyHost / ApplyCompact.
 struct ApplyLaunch {
@@ -256,6 +275,8 @@ struct PushLaunch {
   const unsigned long long* grad_prefix;  // device: value prefix per feature
   const unsigned int* seg_start;   // [U + 1] run starts of the sorted keys
   const unsigned int* seg_total;   // U (device)
+  const RowRec* rows;              // the row plan: rows[u] for u < U
+  const RowPlan* plan;
   uint2* pieces;                   // [max_pieces] (start, count) of long-row pieces
   unsigned int max_pieces;
   float* part;                     // [max_pieces][dim_max] piece sums

@@ -321,83 +321,91 @@ __device__ __forceinline__ KeyT slot_mask_of(unsigned slot_bits) {
 }
 
 // --------------------------------------------------------------------- rows
-// A warp takes 32 consecutive coalesced rows at a time: their bounds and keys
-// are fetched with one load per lane into shared memory, then its groups of G
-// lanes handle the rows round-robin.  A row with at most long_run occurrences
-// is reduced and updated in place (its [w|m|v] and counter loads issued before
-// the reduction); a longer row reserves its pieces for push_pieces/push_long.
+// Coalesced rows come from the lookup's row plan (rows[u], one 16-byte record
+// per run of the sorted keys), taken in key order.  A warp takes 32
+// consecutive records per step (one load per lane, the next step's records
+// loaded one step ahead); its groups of G lanes take the rows round-robin,
+// reading the record fields from the owning lane with shuffles.  Every row's
+// gradient is one row away: the single occurrence's gradient row times its
+// scale (0 + src * scale, batch_access.cpp:118), or, for a row with
+// 2..long_run occurrences, its piece sum reduced in occurrence order by
+// push_pieces.  The gradient-row, [w|m|v] and counter loads are issued
+// together, then LazyAdam.  Padding rows and long rows (push_long) are
+// skipped.
 template <int G, int VEC, int ITERS, typename KeyT>
 __global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? EPS_PUSH_MIN_BLOCKS : 2) push_rows(PushLaunch p, int pass) {
   __shared__ const float* s_grad[kMaxFeatures];
-  __shared__ unsigned long long s_sbase[kMaxFeatures];
-  __shared__ unsigned s_seg[8][33];
-  __shared__ KeyT s_key[8][32];
   const Role R = role(p.control, pass);
-  if (!R.run) return;
+  if (!R.run || !(R.apply || R.validate)) return;
+  for (unsigned f = threadIdx.x; f < p.feature_count; f += blockDim.x) s_grad[f] = p.features[f].grad;
+  __syncthreads();
   constexpr int C = VEC * ITERS;
   constexpr unsigned GPW = 32 / G;            // groups per warp
-  stage_features(p, s_grad, s_sbase);
   const auto grp = cg::tiled_partition<G>(cg::this_thread_block());
   const unsigned gl = grp.thread_rank();
-  const unsigned lane = threadIdx.x & 31, wib = threadIdx.x >> 5, gw = lane / G;
+  const unsigned lane = threadIdx.x & 31, gw = lane / G;
   const unsigned U = *(volatile const unsigned*)p.seg_total;
   const unsigned long long warp = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) >> 5;
-  const unsigned long long nwarps = (gridDim.x * (unsigned long long)blockDim.x) >> 5;
+  const unsigned long long step = ((gridDim.x * (unsigned long long)blockDim.x) >> 5) * 32ull;
   const KeyT smask = slot_mask_of<KeyT>(p.slot_bits);
-  const bool work = R.apply || R.validate;
   unsigned bits = 0;
   int cur_tr = -1;
   unsigned cur_max = 0;
-  for (unsigned long long base = warp * 32; base < U; base += nwarps * 32) {
-    const unsigned nseg = (unsigned)min(32ull, U - base);
-    {
-      const unsigned long long idx = base + lane;
-      if (lane < nseg) {
-        const unsigned st = __ldg(p.seg_start + idx);
-        s_seg[wib][lane] = st;
-        s_key[wib][lane] = key_at<KeyT>(p.keys, st);
-      }
-      if (lane == nseg - 1) s_seg[wib][nseg] = __ldg(p.seg_start + idx + 1);
-    }
-    __syncwarp();
-    for (unsigned j = gw; j < nseg; j += GPW) {
-      const unsigned s0 = s_seg[wib][j], s1 = s_seg[wib][j + 1];
-      const unsigned len = s1 - s0;
-      const KeyT K = s_key[wib][j];
+  unsigned long long base = warp * 32ull;
+  RowRec nxt{0ull, 0u, kRowSkip};
+  if (base + lane < U) nxt = p.rows[base + lane];
+  for (; base < U; base += step) {
+    const RowRec cur = nxt;
+    if (base + step + lane < U) nxt = p.rows[base + step + lane];   // one step ahead
+    const unsigned nrow = (unsigned)min(32ull, U - base);
+    const unsigned iters = (nrow + GPW - 1) / GPW;
+    for (unsigned i = 0; i < iters; ++i) {
+      const unsigned j = i * GPW + gw;
+      const unsigned jj = j < nrow ? j : 0u;
+      const unsigned long long key = __shfl_sync(0xffffffffu, cur.key, jj);
+      const unsigned a = __shfl_sync(0xffffffffu, cur.a, jj);
+      const unsigned b = __shfl_sync(0xffffffffu, cur.b, jj);
+      if (j >= nrow || b == kRowSkip) continue;
+      const KeyT K = (KeyT)key;
       const unsigned tr = (unsigned)(K >> p.slot_bits);
-      if (tr >= p.table_count) continue;
       const PushTable& T = p.tables[tr];
       const unsigned D = T.dim;
       const unsigned long long slot = (unsigned long long)(K & smask);
-      if (len <= p.long_run) {
-        if (!work) continue;
-        float* row = T.state + slot * 3ull * D;
-        float w[C], m[C], v[C], g[C];
-        unsigned long long upd = 0;
-        if (R.apply && gl == 0) upd = T.updates[slot];
-        load_state<G, VEC, ITERS>(gl, row, D, w, m, v);   // issued before the reduction
-        reduce_staged<G, VEC, ITERS, EPS_PUSH_DEPTH_REGS>(grp, p, s_grad, s_sbase, s0, s1, D, g);
-        if ((int)tr != cur_tr) {
-          if (R.apply) flush_absmax(grp, p, cur_tr, cur_max);
-          cur_tr = (int)tr; cur_max = 0;
+      float* row = T.state + slot * 3ull * D;
+      const bool multi = (b & kRowMulti) != 0;
+      const float* q = multi ? p.part + (unsigned long long)a * p.dim_max
+                             : s_grad[a >> kRowBits] + (unsigned long long)(a & ((1u << kRowBits) - 1u)) * D;
+      float t[C], w[C], m[C], v[C], g[C];
+#pragma unroll
+      for (int it = 0; it < ITERS; ++it) {
+        const unsigned col = (it * G + gl) * VEC;
+        float x[VEC];
+        if (col < D) load_vec<VEC>(q + col, x);
+        else {
+#pragma unroll
+          for (int y = 0; y < VEC; ++y) x[y] = 0.0f;
         }
-        bits |= adam_row<G, VEC, ITERS>(gl, T, row, D, g, w, m, v, R.apply, R.validate, &cur_max);
-        if (R.apply && gl == 0) T.updates[slot] = upd + 1ull;
-      } else if (R.partials) {
-        // a long row: reserve contiguous piece slots, remember the row
-        const unsigned np = (len + kPiece - 1) / kPiece;
-        unsigned pbase = 0;
-        if (gl == 0) {
-          pbase = atomicAdd(&p.control->piece_count, np);
-          const unsigned rec = atomicAdd(&p.control->long_count, 1u);
-          p.records[rec] = LongRecord{(unsigned long long)K, pbase, np};
-        }
-        pbase = grp.shfl(pbase, 0);
-        for (unsigned k = gl; k < np; k += G)
-          p.pieces[pbase + k] = make_uint2(s0 + k * kPiece, min((unsigned)kPiece, len - k * kPiece));
+#pragma unroll
+        for (int y = 0; y < VEC; ++y) t[it * VEC + y] = x[y];
       }
+      load_state<G, VEC, ITERS>(gl, row, D, w, m, v);
+      unsigned long long upd = 0;
+      if (R.apply && gl == 0) upd = T.updates[slot];
+      if (multi) {
+#pragma unroll
+        for (int k = 0; k < C; ++k) g[k] = t[k];
+      } else {
+        const float scale = __uint_as_float(b);
+#pragma unroll
+        for (int k = 0; k < C; ++k) g[k] = __fadd_rn(0.0f, __fmul_rn(t[k], scale));
+      }
+      if ((int)tr != cur_tr) {
+        if (R.apply) flush_absmax(grp, p, cur_tr, cur_max);
+        cur_tr = (int)tr; cur_max = 0;
+      }
+      bits |= adam_row<G, VEC, ITERS>(gl, T, row, D, g, w, m, v, R.apply, R.validate, &cur_max);
+      if (R.apply && gl == 0) T.updates[slot] = upd + 1ull;
     }
-    __syncwarp();
   }
   bits = cg::reduce(grp, bits, cg::bit_or<unsigned>());
   if (gl == 0 && bits) atomicOr(&p.control->reject_bits, bits);
@@ -415,7 +423,7 @@ __global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? EPS_PIECE_MIN_BLOCKS
   stage_features(p, s_grad, s_sbase);
   const auto grp = cg::tiled_partition<G>(cg::this_thread_block());
   const unsigned gl = grp.thread_rank();
-  const unsigned count = *(volatile const unsigned*)&p.control->piece_count;
+  const unsigned count = *(volatile const unsigned*)&p.plan->piece_count;
   const unsigned long long gid = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) / G;
   const unsigned long long ngroups = (gridDim.x * (unsigned long long)blockDim.x) / G;
   for (unsigned long long item = gid; item < count; item += ngroups) {
@@ -452,7 +460,7 @@ __global__ void __launch_bounds__(kLongThreads) push_long(PushLaunch p, int pass
   constexpr int NG = kLongThreads / G;
   const auto grp = cg::tiled_partition<G>(cg::this_thread_block());
   const unsigned gl = grp.thread_rank(), w = threadIdx.x / G;
-  const unsigned count = *(volatile const unsigned*)&p.control->long_count;
+  const unsigned count = *(volatile const unsigned*)&p.plan->long_count;
   const KeyT smask = slot_mask_of<KeyT>(p.slot_bits);
   unsigned bits = 0;
   unsigned cur_max = 0;
@@ -622,18 +630,18 @@ __global__ void push_finalize(PushLaunch p) {
 template <int G, int VEC, int ITERS, typename KeyT>
 cudaError_t run_apply(const PushLaunch& p, cudaStream_t s) {
   if (!p.n) return cudaSuccess;
-  constexpr unsigned blocks_per_sm = (VEC * ITERS <= 4) ? EPS_PUSH_MIN_BLOCKS : 2;
+  constexpr unsigned rows_blocks = (VEC * ITERS <= 4) ? EPS_PUSH_MIN_BLOCKS : 2;
   constexpr unsigned long long groups_per_block = 256 / G;
-  const unsigned long long cap = 148ull * blocks_per_sm;
-  const unsigned rows_grid = (unsigned)max(1ull, min((p.n + groups_per_block - 1) / groups_per_block, cap));
+  const unsigned long long want = (p.n + groups_per_block - 1) / groups_per_block;
+  const unsigned rows_grid = (unsigned)max(1ull, min(want, 148ull * rows_blocks));
   constexpr unsigned piece_blocks = (VEC * ITERS <= 4) ? EPS_PIECE_MIN_BLOCKS : 2;
   const unsigned piece_grid =
       (unsigned)max(1ull, min(((unsigned long long)p.max_pieces + groups_per_block - 1) / groups_per_block,
                               148ull * piece_blocks));
   const size_t long_smem = (size_t)(kLongThreads / G) * p.dim_max * sizeof(float);
   const unsigned long_grid = 148 * 2;
-  push_rows<G, VEC, ITERS, KeyT><<<rows_grid, 256, 0, s>>>(p, 0);
   push_pieces<G, VEC, ITERS, KeyT><<<piece_grid, 256, 0, s>>>(p, 0);
+  push_rows<G, VEC, ITERS, KeyT><<<rows_grid, 256, 0, s>>>(p, 0);
   push_long<G, VEC, ITERS, KeyT><<<long_grid, kLongThreads, long_smem, s>>>(p, 0);
   push_rows<G, VEC, ITERS, KeyT><<<rows_grid, 256, 0, s>>>(p, 1);
   push_long<G, VEC, ITERS, KeyT><<<long_grid, kLongThreads, long_smem, s>>>(p, 1);

@@ -112,6 +112,8 @@ struct Ticket {
   void* keys = nullptr;
   unsigned* srcs = nullptr;
   float* row_scale = nullptr;
+  RowRec* rows = nullptr;          // the push's row plan (built after the sort)
+  RowPlan* plan = nullptr;
   unsigned* seg_start = nullptr;
   unsigned* seg_total = nullptr;
   uint2* pieces = nullptr;
@@ -644,11 +646,13 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
     }
     if (any_host_out) at_hostout = c.take<float>(host_out_values);
     const unsigned stiles = sort_tiles(total_keys);
-    // long rows (> kLongRun occurrences) split into pieces of kPiece
+    // pieces: one per row with 2..kLongRun occurrences (at most total_keys / 2
+    // rows) and ceil(len / kPiece) per longer row
     const unsigned long long max_long = total_keys / (kLongRun + 1) + 1;
-    const unsigned long long max_pieces = (total_keys + kPiece - 1) / kPiece + max_long;
+    const unsigned long long max_pieces = (total_keys + kPiece - 1) / kPiece + max_long + total_keys / 2;
     size_t at_k0 = 0, at_k1 = 0, at_s0 = 0, at_s1 = 0, at_scale = 0, at_hist = 0, at_seg = 0,
-           at_segtot = 0, at_segscr = 0, at_pieces = 0, at_part = 0, at_rec = 0,
+           at_segtot = 0, at_segscr = 0, at_pieces = 0, at_part = 0, at_rec = 0, at_rows = 0,
+           at_plan = 0,
            at_ptab = 0, at_pfeat = 0, at_gpre = 0, at_end = 0;
     size_t at_zero = 0;   // start of the region zeroed by the lookup's single memset
     if (!read_only) {
@@ -662,9 +666,11 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       at_pieces = c.take<uint2>(max_pieces);
       at_part = c.take<float>(max_pieces * dim_max);
       at_rec = c.take<LongRecord>(max_long);
-      // [sort scratch | segment scratch | status] zeroed together
+      at_rows = c.take<RowRec>(total_keys);
+      // [sort scratch | segment scratch | row plan counts | status] zeroed together
       at_zero = at_hist = c.take<char>(sort_scratch_bytes(total_keys, key_bits));
       at_segscr = c.take<char>(segment_scratch_bytes(total_keys));
+      at_plan = c.take<RowPlan>(1);
     }
     const size_t at_status = c.take<StatusBlock>(1);
     if (read_only) at_zero = at_status;
@@ -795,7 +801,24 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
                          reinterpret_cast<unsigned*>(P(at_segtot)),
                          reinterpret_cast<unsigned*>(P(at_segscr)), err};
         Cuda(launch_segments(gl, sort_stream));
-        s.End(EPS_B200_PHASE_SORT, ev, sort_stream, sort_launch_count(sp) + (total_keys ? 1u : 0u));
+        PlanLaunch pp{};
+        pp.keys = swapped ? P(at_k1) : P(at_k0);
+        pp.srcs = reinterpret_cast<const unsigned*>(swapped ? P(at_s1) : P(at_s0));
+        pp.seg_start = reinterpret_cast<const unsigned*>(P(at_seg));
+        pp.seg_total = reinterpret_cast<const unsigned*>(P(at_segtot));
+        pp.features = lp.features;
+        pp.row_scale = reinterpret_cast<const float*>(P(at_scale));
+        pp.n = total_keys;
+        pp.key64 = key64;
+        pp.slot_bits = slot_bits;
+        pp.table_count = (unsigned)ranks.size();
+        pp.long_run = (s.opt.flags & EPS_B200_FLAG_REFERENCE_ORDER) ? ~0ull : (unsigned long long)kLongRun;
+        pp.rows = reinterpret_cast<RowRec*>(P(at_rows));
+        pp.plan = reinterpret_cast<RowPlan*>(P(at_plan));
+        pp.pieces = reinterpret_cast<uint2*>(P(at_pieces));
+        pp.longs = reinterpret_cast<LongRecord*>(P(at_rec));
+        Cuda(launch_row_plan(pp, sort_stream));
+        s.End(EPS_B200_PHASE_SORT, ev, sort_stream, sort_launch_count(sp) + (total_keys ? 2u : 0u));
         Cuda(cudaEventRecord(s.join, s.side));
         Cuda(cudaStreamWaitEvent(stream, s.join, 0));
         t.keys = swapped ? P(at_k1) : P(at_k0);
@@ -811,6 +834,8 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         t.max_pieces = (unsigned)max_pieces;
         t.part = reinterpret_cast<float*>(P(at_part));
         t.records = reinterpret_cast<LongRecord*>(P(at_rec));
+        t.rows = reinterpret_cast<RowRec*>(P(at_rows));
+        t.plan = reinterpret_cast<RowPlan*>(P(at_plan));
         t.status = status_block;
         t.control = &status_block->control;
         t.lookup_error = err;
@@ -1100,6 +1125,8 @@ int PushEntry(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gradien
       pl.grad_prefix = t.grad_prefix;
       pl.seg_start = t.seg_start;
       pl.seg_total = t.seg_total;
+      pl.rows = t.rows;
+      pl.plan = t.plan;
       pl.pieces = t.pieces;
       pl.max_pieces = t.max_pieces;
       pl.part = t.part;

@@ -308,12 +308,103 @@ cudaError_t run_heads(const SegmentLaunch& p, cudaStream_t s) {
 }
 }  // namespace
 
+// ------------------------------------------------------------------ row plan
+// One thread per coalesced row u (a block takes 256 consecutive rows): rows[u]
+// gets the row's key and, for a row with one occurrence, its gradient source
+// and row scale.  A row with 2..long_run occurrences gets one piece covering
+// all of them (reserved with one atomic per block), reduced in order by the
+// piece kernel; a longer row reserves ceil(len / kPiece) contiguous pieces
+// (its warp writes them) and a LongRecord.  Padding rows (table rank >=
+// table_count) are skipped.
+template <typename KeyT>
+__global__ void __launch_bounds__(256) row_plan(PlanLaunch p) {
+  __shared__ unsigned s_cnt[8];
+  __shared__ unsigned s_base;
+  const unsigned U = *(volatile const unsigned*)p.seg_total;
+  const unsigned lane = threadIdx.x & 31u, w = threadIdx.x >> 5;
+  const unsigned below = (1u << lane) - 1u;
+  const KeyT* keys = static_cast<const KeyT*>(p.keys);
+  for (unsigned long long base = blockIdx.x * 256ull; base < U; base += gridDim.x * 256ull) {
+    const unsigned long long u = base + threadIdx.x;
+    unsigned kind = 0;                    // 1 single, 2 multi, 3 long
+    unsigned s0 = 0, len = 0;
+    unsigned long long key = 0;
+    RowRec r{0ull, 0u, kRowSkip};
+    if (u < U) {
+      s0 = p.seg_start[u];
+      len = p.seg_start[u + 1] - s0;
+      const KeyT K = keys[s0];
+      const unsigned src = p.srcs[s0];
+      key = (unsigned long long)K;
+      r.key = key;
+      if ((unsigned)(K >> p.slot_bits) < p.table_count) {
+        if (len > p.long_run) {
+          kind = 3;
+        } else if (len == 1) {
+          kind = 1;
+          const unsigned f = src >> kRowBits;
+          r.a = src;
+          r.b = __float_as_uint(p.row_scale[p.features[f].scale_base + (src & ((1u << kRowBits) - 1u))]);
+        } else {
+          kind = 2;
+          r.b = kRowMulti | len;
+        }
+      }
+    }
+    const unsigned mm = __ballot_sync(0xffffffffu, kind == 2);
+    if (lane == 0) s_cnt[w] = __popc(mm);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      unsigned tot = 0;
+      for (int q = 0; q < 8; ++q) tot += s_cnt[q];
+      s_base = tot ? atomicAdd(&p.plan->piece_count, tot) : 0u;
+    }
+    __syncthreads();
+    if (kind == 2) {
+      unsigned piece = s_base + __popc(mm & below);
+      for (unsigned q = 0; q < w; ++q) piece += s_cnt[q];
+      r.a = piece;
+      p.pieces[piece] = make_uint2(s0, len);
+    }
+    if (u < U) p.rows[u] = r;
+    for (unsigned todo = __ballot_sync(0xffffffffu, kind == 3); todo; todo &= todo - 1u) {
+      const int L = __ffs(todo) - 1;
+      const unsigned ls0 = __shfl_sync(0xffffffffu, s0, L);
+      const unsigned llen = __shfl_sync(0xffffffffu, len, L);
+      const unsigned long long lkey = __shfl_sync(0xffffffffu, key, L);
+      const unsigned np = (llen + kPiece - 1) / kPiece;
+      unsigned pbase = 0;
+      if (lane == 0) {
+        pbase = atomicAdd(&p.plan->piece_count, np);
+        const unsigned rec = atomicAdd(&p.plan->long_count, 1u);
+        p.longs[rec] = LongRecord{lkey, pbase, np};
+      }
+      pbase = __shfl_sync(0xffffffffu, pbase, 0);
+      for (unsigned q = lane; q < np; q += 32)
+        p.pieces[pbase + q] = make_uint2(ls0 + q * kPiece, min((unsigned)kPiece, llen - q * kPiece));
+    }
+    __syncthreads();                      // s_cnt / s_base are reused
+  }
+}
+
+template <typename KeyT>
+cudaError_t run_plan(const PlanLaunch& p, cudaStream_t s) {
+  const unsigned long long want = (p.n + 255) / 256;
+  row_plan<KeyT><<<(unsigned)max(1ull, min(want, 148ull * 8)), 256, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
 size_t segment_scratch_bytes(unsigned long long n) {
   return 256 + (size_t)((n + kSortTile - 1) / kSortTile) * sizeof(unsigned long long);
 }
 
 cudaError_t launch_segments(const SegmentLaunch& p, cudaStream_t stream) {
   return p.key64 ? run_heads<unsigned long long>(p, stream) : run_heads<unsigned int>(p, stream);
+}
+
+cudaError_t launch_row_plan(const PlanLaunch& p, cudaStream_t stream) {
+  if (!p.n) return cudaSuccess;
+  return p.key64 ? run_plan<unsigned long long>(p, stream) : run_plan<unsigned int>(p, stream);
 }
 
 unsigned int sort_tiles(unsigned long long n) {
