@@ -59,6 +59,7 @@ class Options(C.Structure):
 
 
 FLAG_REFERENCE_ORDER = 1
+FLAG_REGISTER_ROWS = 2
 
 
 class Table(C.Structure):
@@ -290,13 +291,15 @@ class ParameterStore:
 
     def __init__(self, device: int = 0, shard_id: int = 0, shard_count: int = 1,
                  state_bytes: int = 64 << 30, max_live_tickets: int = 1024,
-                 partition_epoch: int = 1, reference_order: bool = False):
+                 partition_epoch: int = 1, reference_order: bool = False,
+                 register_rows: bool = False):
         self.lib = load_library()
         self.device = device
         self.shard_count = shard_count
         self._tables: dict[int, TableDefinition] = {}
         opt = Options(device, shard_id, shard_count, max_live_tickets, partition_epoch, state_bytes,
-                      FLAG_REFERENCE_ORDER if reference_order else 0, 0)
+                      (FLAG_REFERENCE_ORDER if reference_order else 0) |
+                      (FLAG_REGISTER_ROWS if register_rows else 0), 0)
         st = Status()
         h = C.c_void_p()
         _check(self.lib.eps_b200_create(C.byref(opt), C.byref(h), C.byref(st)), st)

@@ -64,13 +64,20 @@ struct LookupFeature {
 };
 constexpr unsigned int kPadSlot = 0xFFFFFFFEu;   // slot marker of a padding key
 
-// Gradient source of one feature for a Push.
+// Gradient source of one feature for a Push.  The coalescing kernels read
+// `scaled`: for a mean feature the prescan writes there every gradient value
+// times its row scale 1.0f/len (the product the reference forms per occurrence,
+// src/access/batch_access.cpp:118), so the reductions add without a scale load;
+// for sum and sequence features (scale 1) it is `grad` itself.
 struct PushFeature {
   const float* grad;                   // [rows][dim]
+  float* scaled;                       // [rows][dim]: grad * row scale (mean), or grad
   unsigned long long rows;
   unsigned long long scale_base;
   unsigned int dim;
   unsigned int table_rank;
+  unsigned int mean;                   // 1: pooling mean (scaled is written by the prescan)
+  unsigned int pad;
 };
 
 enum PushMode : unsigned int { kModeSafe = 0, kModeChecked = 1, kModeRejected = 2 };
@@ -97,6 +104,12 @@ struct PushControl {
   unsigned int blocks_done;
   unsigned int accepted;
   unsigned int piece_count;     // pieces reserved by long rows
+  unsigned int blocks_done_b;   // blocks of push stage B that finished
+  unsigned int blocks_done_c;   // blocks of push stage C that finished
+  unsigned int work_a;          // chunks claimed in push stage A
+  unsigned int work_b;          // row chunks claimed in push stage B
+  unsigned int work_long;       // long rows claimed in push stage B
+  unsigned int work_ring;       // row chunks claimed by the async-ring row kernel
 };
 
 // A long coalesced row (more than kLongRun occurrences): its occurrences are
@@ -130,7 +143,7 @@ struct RowPlan {
 
 constexpr int kLongRun = 64;    // rows with more occurrences than this are "long"
 #ifndef EPS_PIECE
-#define EPS_PIECE 32
+#define EPS_PIECE 64
 #endif
 constexpr int kPiece = EPS_PIECE;   // occurrences per piece of a long row
 constexpr unsigned int kMaxFeatures = 1024;

@@ -55,6 +55,17 @@ __device__ __forceinline__ void load_vec_stream(const float* p, float (&r)[VEC])
   }
 }
 
+template <int VEC>
+__device__ __forceinline__ void store_vec_stream(float* p, const float (&r)[VEC]) {
+  if constexpr (VEC == 4) {
+    __stcs(reinterpret_cast<float4*>(p), make_float4(r[0], r[1], r[2], r[3]));
+  } else if constexpr (VEC == 2) {
+    __stcs(reinterpret_cast<float2*>(p), make_float2(r[0], r[1]));
+  } else {
+    __stcs(p, r[0]);
+  }
+}
+
 __device__ __forceinline__ unsigned lane_id() { return threadIdx.x & 31u; }
 
 __device__ __forceinline__ bool finitef(float x) { return isfinite(x); }
@@ -287,12 +298,18 @@ struct PushLaunch {
   const unsigned int* external_reject;  // optional device word: nonzero rejects (non-finite input)
   unsigned long long long_run;     // segments longer than this are reduced in pieces
   int vec, group, iters;           // launch shape (see choose_shape)
+  int ring_dim;                    // 32 / 64 / 128: rows updated through the async ring
+                                   // (every table has this dimension, 16-byte aligned
+                                   // gradients); 0: register path only
 };
-// Push = prescan (+ device-side mode decision), apply (2 passes x {segments,
-// long segments}), finalize (beta powers / sequence iff accepted).
+// Push = prescan (+ device-side mode decision), apply (stage A: piece sums and
+// single-occurrence rows; stage B: long rows and rows with a piece sum, then the
+// beta powers / sequence iff accepted; stage C: the apply pass of a CHECKED
+// push); finalize launches a kernel only for a push without occurrences.
 cudaError_t launch_push_prescan(const PushLaunch& p, cudaStream_t stream);
 cudaError_t launch_push_apply(const PushLaunch& p, cudaStream_t stream);
 unsigned launch_push_apply_count(const PushLaunch& p);
+unsigned launch_push_finalize_count(const PushLaunch& p);
 cudaError_t launch_push_finalize(const PushLaunch& p, cudaStream_t stream);
 
 struct InitLaunch {

@@ -47,7 +47,7 @@ namespace cg = cooperative_groups;
 #define EPS_PUSH_DEPTH_REGS 16        // registers per lane for gradient rows in flight
 #endif
 #ifndef EPS_PUSH_MIN_BLOCKS
-#define EPS_PUSH_MIN_BLOCKS 4         // resident 256-thread blocks per SM (C <= 4)
+#define EPS_PUSH_MIN_BLOCKS 2         // resident 256-thread blocks per SM (C <= 4)
 #endif
 #ifndef EPS_PIECE_DEPTH_REGS
 #define EPS_PIECE_DEPTH_REGS 32       // the same for the long rows' pieces
@@ -64,24 +64,6 @@ __device__ __forceinline__ KeyT key_at(const void* keys, unsigned long long i) {
   return __ldg(static_cast<const KeyT*>(keys) + i);
 }
 
-struct Role { bool run, apply, validate, partials; };
-
-__device__ __forceinline__ Role role(const PushControl* c, int pass) {
-  Role r{false, false, false, false};
-  const unsigned mode = *(volatile const unsigned*)&c->mode;
-  if (mode == kModeRejected) return r;
-  if (pass == 0) {
-    r.run = true; r.partials = true;
-    r.apply = mode == kModeSafe;
-    r.validate = mode == kModeChecked;
-  } else {
-    const unsigned bits = *(volatile const unsigned*)&c->reject_bits;
-    if (mode != kModeChecked || bits) return r;
-    r.run = true; r.apply = true;
-  }
-  return r;
-}
-
 // ------------------------------------------------------------------ prescan
 // Grid (x, features): blocks of row y scan feature y's gradient values.
 __global__ void __launch_bounds__(256) push_prescan(PushLaunch p, PushTable* tables_rw) {
@@ -93,6 +75,11 @@ __global__ void __launch_bounds__(256) push_prescan(PushLaunch p, PushTable* tab
   const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
   unsigned bad = 0;
   float mx = 0.0f;
+  // mean features: scaled[e] = grad[e] * row_scale[row of e] (rows < 2^22,
+  // dim <= 512: element indices fit 32 bits)
+  const float* scale = p.row_scale + F.scale_base;
+  float* const out = F.mean ? F.scaled : nullptr;
+  const unsigned D = F.dim;
   if (p.grad_vec4) {
     const float4* g4 = reinterpret_cast<const float4*>(F.grad);
     const unsigned long long n4 = nvals / 4;
@@ -101,12 +88,25 @@ __global__ void __launch_bounds__(256) push_prescan(PushLaunch p, PushTable* tab
       const float4 x = __ldg(g4 + i);
       bad |= !isfinite(x.x) | !isfinite(x.y) | !isfinite(x.z) | !isfinite(x.w);
       mx = fmaxf(mx, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+      if (out) {
+        const unsigned e = (unsigned)i * 4u;
+        float4 y;
+        if (D % 4u == 0) {
+          const float sc = __ldg(scale + e / D);
+          y = make_float4(__fmul_rn(x.x, sc), __fmul_rn(x.y, sc), __fmul_rn(x.z, sc), __fmul_rn(x.w, sc));
+        } else {
+          y = make_float4(__fmul_rn(x.x, __ldg(scale + e / D)), __fmul_rn(x.y, __ldg(scale + (e + 1) / D)),
+                          __fmul_rn(x.z, __ldg(scale + (e + 2) / D)), __fmul_rn(x.w, __ldg(scale + (e + 3) / D)));
+        }
+        reinterpret_cast<float4*>(out)[i] = y;
+      }
     }
   } else {
     for (unsigned long long i = blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x; i < nvals; i += stride) {
       const float x = __ldg(F.grad + i);
       bad |= !isfinite(x);
       mx = fmaxf(mx, fabsf(x));
+      if (out) out[i] = __fmul_rn(x, __ldg(scale + (unsigned)i / D));
     }
   }
   bad = __reduce_or_sync(0xffffffffu, bad);
@@ -156,63 +156,34 @@ __global__ void __launch_bounds__(256) push_prescan(PushLaunch p, PushTable* tab
 // ------------------------------------------------------ reduction helpers
 // Sum of the gradient references [s0, s1) of one coalesced row (all with the
 // same key), serially in occurrence order, by the G lanes of `grp` (each lane
-// owns VEC*ITERS columns), bit-exact with the reference's serial loop.
-// The gradient sources of the features are staged in shared memory (row
-// pointer and scale index without dependent descriptor loads); up to
-// EPS_PUSH_DEPTH_REGS / C gradient rows are in flight; rows past the end add
-// -0.0f (the identity).
+// owns VEC*ITERS columns), bit-exact with the reference's serial loop
+// g = 0; g += src * scale (src/access/batch_access.cpp:118): the products are
+// the pre-scaled rows (PushFeature::scaled), whose pointers are staged in
+// shared memory.  The next chunk's sources are requested before the current
+// chunk's rows; up to DEPTH_REGS / C gradient rows are in flight; rows past the
+// end add -0.0f (the identity).
 template <int G, int VEC, int ITERS, int DEPTH_REGS, typename Grp>
 __device__ __forceinline__ void reduce_staged(const Grp& grp, const PushLaunch& p,
                                               const float* const* s_grad,
-                                              const unsigned long long* s_sbase,
                                               unsigned long long s0, unsigned long long s1,
                                               unsigned D, float (&acc)[VEC * ITERS]) {
   constexpr int C = VEC * ITERS;
   constexpr int DEPTH = G < DEPTH_REGS / C ? G : (DEPTH_REGS / C > 0 ? DEPTH_REGS / C : 1);
   const unsigned gl = grp.thread_rank();
-  if (s1 - s0 == 1) {
-    // a single term (most rows): 0 + src * scale, every lane reading the source
-    const unsigned src = __ldg(p.srcs + s0);
-    const unsigned f = src >> kRowBits;
-    const unsigned r = src & ((1u << kRowBits) - 1u);
-    const float* q = s_grad[f] + (unsigned long long)r * D;
-    const float sc = __ldg(p.row_scale + s_sbase[f] + r);
-#pragma unroll
-    for (int it = 0; it < ITERS; ++it) {
-      const unsigned col = (it * G + gl) * VEC;
-      float t[VEC];
-      if (col < D) load_vec<VEC>(q + col, t);
-      else {
-#pragma unroll
-        for (int v = 0; v < VEC; ++v) t[v] = 0.0f;
-      }
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) acc[it * VEC + v] = __fadd_rn(0.0f, __fmul_rn(t[v], sc));
-    }
-    return;
-  }
 #pragma unroll
   for (int k = 0; k < C; ++k) acc[k] = 0.0f;
+  unsigned src = (s0 + gl < s1) ? __ldg(p.srcs + s0 + gl) : 0u;
   for (unsigned long long c0 = s0; c0 < s1; c0 += G) {
     const unsigned long long i = c0 + gl;
-    const float* rowp = nullptr;
-    float sc = 1.0f;
-    if (i < s1) {
-      const unsigned src = __ldg(p.srcs + i);
-      const unsigned f = src >> kRowBits;
-      const unsigned r = src & ((1u << kRowBits) - 1u);
-      rowp = s_grad[f] + (unsigned long long)r * D;
-      sc = __ldg(p.row_scale + s_sbase[f] + r);
-    }
+    const float* rowp = s_grad[src >> kRowBits] + (unsigned long long)(src & ((1u << kRowBits) - 1u)) * D;
+    if (i + G < s1) src = __ldg(p.srcs + i + G);
     const int cnt = (int)min((unsigned long long)G, s1 - c0);
 #pragma unroll 1
     for (int j0 = 0; j0 < cnt; j0 += DEPTH) {
       float x[DEPTH][C];
-      float sv[DEPTH];
 #pragma unroll
       for (int u = 0; u < DEPTH; ++u) {
         const float* q = grp.shfl(rowp, (j0 + u) & (G - 1));
-        sv[u] = grp.shfl(sc, (j0 + u) & (G - 1));
         const bool use = j0 + u < cnt;
 #pragma unroll
         for (int it = 0; it < ITERS; ++it) {
@@ -227,22 +198,17 @@ __device__ __forceinline__ void reduce_staged(const Grp& grp, const PushLaunch& 
           for (int v = 0; v < VEC; ++v) x[u][it * VEC + v] = t[v];
         }
       }
-      // batch_access.cpp:118: dest += src * scale, in occurrence order
 #pragma unroll
       for (int u = 0; u < DEPTH; ++u)
 #pragma unroll
-        for (int k = 0; k < C; ++k) acc[k] = __fadd_rn(acc[k], __fmul_rn(x[u][k], sv[u]));
+        for (int k = 0; k < C; ++k) acc[k] = __fadd_rn(acc[k], x[u][k]);
     }
   }
 }
 
-// Stages every feature's gradient pointer and row-scale base in shared memory.
-__device__ __forceinline__ void stage_features(const PushLaunch& p, const float** s_grad,
-                                               unsigned long long* s_sbase) {
-  for (unsigned f = threadIdx.x; f < p.feature_count; f += blockDim.x) {
-    s_grad[f] = p.features[f].grad;
-    s_sbase[f] = p.features[f].scale_base;
-  }
+// Stages every feature's pre-scaled gradient pointer in shared memory.
+__device__ __forceinline__ void stage_features(const PushLaunch& p, const float** s_grad) {
+  for (unsigned f = threadIdx.x; f < p.feature_count; f += blockDim.x) s_grad[f] = p.features[f].scaled;
   __syncthreads();
 }
 
@@ -299,9 +265,9 @@ __device__ __forceinline__ unsigned adam_row(unsigned gl, const PushTable& T, fl
       mx = max(mx, max(abs_bits(nw[x]), max(abs_bits(mm), abs_bits(vv))));
     }
     if (apply) {
-      store_vec<VEC>(row + col, nw);
-      store_vec<VEC>(row + D + col, nm);
-      store_vec<VEC>(row + 2 * D + col, nv);
+      store_vec_stream<VEC>(row + col, nw);
+      store_vec_stream<VEC>(row + D + col, nm);
+      store_vec_stream<VEC>(row + 2 * D + col, nv);
     }
   }
   if (apply) *absmax = max(*absmax, mx);
@@ -320,231 +286,652 @@ __device__ __forceinline__ KeyT slot_mask_of(unsigned slot_bits) {
   return (slot_bits >= sizeof(KeyT) * 8) ? ~KeyT(0) : ((KeyT(1) << slot_bits) - 1);
 }
 
-// --------------------------------------------------------------------- rows
-// Coalesced rows come from the lookup's row plan (rows[u], one 16-byte record
-// per run of the sorted keys), taken in key order.  A warp takes 32
-// consecutive records per step (one load per lane, the next step's records
-// loaded one step ahead); its groups of G lanes take the rows round-robin,
-// reading the record fields from the owning lane with shuffles.  Every row's
-// gradient is one row away: the single occurrence's gradient row times its
-// scale (0 + src * scale, batch_access.cpp:118), or, for a row with
-// 2..long_run occurrences, its piece sum reduced in occurrence order by
-// push_pieces.  The gradient-row, [w|m|v] and counter loads are issued
-// together, then LazyAdam.  Padding rows and long rows (push_long) are
-// skipped.
+// ------------------------------------------------------------- row updates
+// One coalesced row of the lookup's row plan (rows[u], one 16-byte record per
+// run of the sorted keys), updated by a group of G lanes in two steps so that a
+// group keeps two rows' loads in flight: `load` issues the gradient-row, [w|m|v]
+// and counter loads; `finish` applies LazyAdam and stores.  The gradient is one
+// row away: the single occurrence's pre-scaled gradient row, 0 + src * scale
+// (batch_access.cpp:118), or, for a row with 2..long_run occurrences, its piece
+// sum reduced in occurrence order in stage A.  The row state is read and
+// written with streaming hints (touched once per push).
+template <int C>
+struct RowRegs {
+  float* row;
+  const PushTable* T;
+  unsigned long long slot, upd;
+  unsigned tr;
+  bool multi;
+  float t[C], w[C], m[C], v[C];
+};
+
 template <int G, int VEC, int ITERS, typename KeyT>
-__global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? EPS_PUSH_MIN_BLOCKS : 2) push_rows(PushLaunch p, int pass) {
-  __shared__ const float* s_grad[kMaxFeatures];
-  const Role R = role(p.control, pass);
-  if (!R.run || !(R.apply || R.validate)) return;
-  for (unsigned f = threadIdx.x; f < p.feature_count; f += blockDim.x) s_grad[f] = p.features[f].grad;
-  __syncthreads();
+__device__ __forceinline__ void load_row(unsigned gl, const PushLaunch& p, const float* const* s_grad,
+                                         unsigned long long key, unsigned a, unsigned b, bool apply,
+                                         RowRegs<VEC * ITERS>& r) {
+  const KeyT K = (KeyT)key;
+  r.tr = (unsigned)(K >> p.slot_bits);
+  r.T = p.tables + r.tr;
+  const unsigned D = r.T->dim;
+  r.slot = (unsigned long long)(K & slot_mask_of<KeyT>(p.slot_bits));
+  r.row = r.T->state + r.slot * 3ull * D;
+  r.multi = (b & kRowMulti) != 0;
+  const float* q = r.multi ? p.part + (unsigned long long)a * p.dim_max
+                           : s_grad[a >> kRowBits] + (unsigned long long)(a & ((1u << kRowBits) - 1u)) * D;
+#pragma unroll
+  for (int it = 0; it < ITERS; ++it) {
+    const unsigned col = (it * G + gl) * VEC;
+    float x[VEC], y[VEC], z[VEC], u[VEC];
+    if (col < D) {
+      load_vec<VEC>(q + col, x);
+      load_vec_stream<VEC>(r.row + col, y);
+      load_vec_stream<VEC>(r.row + D + col, z);
+      load_vec_stream<VEC>(r.row + 2 * D + col, u);
+    } else {
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) x[k] = y[k] = z[k] = u[k] = 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) {
+      r.t[it * VEC + k] = x[k]; r.w[it * VEC + k] = y[k];
+      r.m[it * VEC + k] = z[k]; r.v[it * VEC + k] = u[k];
+    }
+  }
+  r.upd = (apply && gl == 0) ? __ldcs(r.T->updates + r.slot) : 0ull;
+}
+
+template <int G, int VEC, int ITERS, typename Grp>
+__device__ __forceinline__ void finish_row(const Grp& grp, const PushLaunch& p, RowRegs<VEC * ITERS>& r,
+                                           bool apply, bool validate, unsigned& bits, int& cur_tr,
+                                           unsigned& cur_max) {
   constexpr int C = VEC * ITERS;
-  constexpr unsigned GPW = 32 / G;            // groups per warp
-  const auto grp = cg::tiled_partition<G>(cg::this_thread_block());
   const unsigned gl = grp.thread_rank();
-  const unsigned lane = threadIdx.x & 31, gw = lane / G;
-  const unsigned U = *(volatile const unsigned*)p.seg_total;
-  const unsigned long long warp = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) >> 5;
-  const unsigned long long step = ((gridDim.x * (unsigned long long)blockDim.x) >> 5) * 32ull;
-  const KeyT smask = slot_mask_of<KeyT>(p.slot_bits);
-  unsigned bits = 0;
-  int cur_tr = -1;
-  unsigned cur_max = 0;
-  unsigned long long base = warp * 32ull;
-  RowRec nxt{0ull, 0u, kRowSkip};
-  if (base + lane < U) nxt = p.rows[base + lane];
-  for (; base < U; base += step) {
-    const RowRec cur = nxt;
-    if (base + step + lane < U) nxt = p.rows[base + step + lane];   // one step ahead
-    const unsigned nrow = (unsigned)min(32ull, U - base);
-    const unsigned iters = (nrow + GPW - 1) / GPW;
-    for (unsigned i = 0; i < iters; ++i) {
-      const unsigned j = i * GPW + gw;
-      const unsigned jj = j < nrow ? j : 0u;
-      const unsigned long long key = __shfl_sync(0xffffffffu, cur.key, jj);
-      const unsigned a = __shfl_sync(0xffffffffu, cur.a, jj);
-      const unsigned b = __shfl_sync(0xffffffffu, cur.b, jj);
-      if (j >= nrow || b == kRowSkip) continue;
-      const KeyT K = (KeyT)key;
-      const unsigned tr = (unsigned)(K >> p.slot_bits);
-      const PushTable& T = p.tables[tr];
-      const unsigned D = T.dim;
-      const unsigned long long slot = (unsigned long long)(K & smask);
-      float* row = T.state + slot * 3ull * D;
-      const bool multi = (b & kRowMulti) != 0;
-      const float* q = multi ? p.part + (unsigned long long)a * p.dim_max
-                             : s_grad[a >> kRowBits] + (unsigned long long)(a & ((1u << kRowBits) - 1u)) * D;
-      float t[C], w[C], m[C], v[C], g[C];
+  float g[C];
+  if (r.multi) {
+#pragma unroll
+    for (int k = 0; k < C; ++k) g[k] = r.t[k];
+  } else {
+#pragma unroll
+    for (int k = 0; k < C; ++k) g[k] = __fadd_rn(0.0f, r.t[k]);
+  }
+  if ((int)r.tr != cur_tr) {
+    if (apply) flush_absmax(grp, p, cur_tr, cur_max);
+    cur_tr = (int)r.tr; cur_max = 0;
+  }
+  bits |= adam_row<G, VEC, ITERS>(gl, *r.T, r.row, r.T->dim, g, r.w, r.m, r.v, apply, validate, &cur_max);
+  if (apply && gl == 0) __stcs(r.T->updates + r.slot, r.upd + 1ull);
+}
+
+// Rows [base, base + 32) of the row plan by one warp: one record per lane; the
+// warp's groups take the rows round-robin, reading the record fields from the
+// owning lane by shuffle.  Software-pipelined: a group issues the loads of its
+// next row before it runs LazyAdam on the current one (two register sets,
+// ping-pong).  `kinds`: 1 single-occurrence rows, 2 rows with a piece sum,
+// 3 both.  Padding and long rows are skipped.
+template <int G, int VEC, int ITERS, typename KeyT, typename Grp>
+__device__ __forceinline__ void update_chunk(const Grp& grp, const PushLaunch& p,
+                                             const float* const* s_grad, unsigned long long base,
+                                             unsigned U, unsigned kinds, bool apply, bool validate,
+                                             unsigned& bits, int& cur_tr, unsigned& cur_max) {
+  constexpr unsigned GPW = 32 / G;
+  const unsigned lane = threadIdx.x & 31u, gw = lane / G, gl = grp.thread_rank();
+  RowRec rec{0ull, 0u, kRowSkip};
+  if (base + lane < U) rec = p.rows[base + lane];
+  const unsigned nrow = (unsigned)min(32ull, (unsigned long long)U - base);
+  // this group's rows: j = i * GPW + gw for i < iters; a row is used iff its
+  // record is of a requested kind (the mask is warp-uniform after the ballots)
+  const unsigned kind = rec.b == kRowSkip ? 0u : ((rec.b & kRowMulti) ? 2u : 1u);
+  const unsigned mine = __ballot_sync(0xffffffffu, (kind & kinds) != 0 && lane < nrow);
+  // lanes j of this group's rows: bit i of `todo` <=> row i * GPW + gw is used
+  unsigned todo = 0;
+#pragma unroll
+  for (unsigned i = 0; i < 32 / GPW; ++i)
+    if ((mine >> (i * GPW + gw)) & 1u) todo |= 1u << i;
+  RowRegs<VEC * ITERS> r[2];
+  // The record fields come from lane jj of the warp; shuffles need every lane
+  // of the warp, so all lanes run the same number of steps.
+  unsigned cur = todo;
+  bool have = false;
+  // prime: first used row of this group
+  {
+    const unsigned i0 = cur ? (unsigned)__ffs(cur) - 1u : 0u;
+    const unsigned jj = i0 * GPW + gw;
+    const unsigned long long key = __shfl_sync(0xffffffffu, rec.key, jj);
+    const unsigned a = __shfl_sync(0xffffffffu, rec.a, jj);
+    const unsigned b = __shfl_sync(0xffffffffu, rec.b, jj);
+    if (cur) { load_row<G, VEC, ITERS, KeyT>(gl, p, s_grad, key, a, b, apply, r[0]); have = true; cur &= cur - 1u; }
+  }
+  // every lane runs the same number of steps (shuffles are warp-wide)
+  const unsigned steps = __reduce_max_sync(0xffffffffu, (unsigned)__popc(todo));
+#pragma unroll 1
+  for (unsigned st = 0; st < steps; st += 2) {
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      // issue the next row's loads into r[1 - hh], then finish r[hh]
+      const unsigned i1 = cur ? (unsigned)__ffs(cur) - 1u : 0u;
+      const unsigned jj = i1 * GPW + gw;
+      const unsigned long long key = __shfl_sync(0xffffffffu, rec.key, jj);
+      const unsigned a = __shfl_sync(0xffffffffu, rec.a, jj);
+      const unsigned b = __shfl_sync(0xffffffffu, rec.b, jj);
+      const bool next = cur != 0;
+      if (next) { load_row<G, VEC, ITERS, KeyT>(gl, p, s_grad, key, a, b, apply, r[1 - hh]); cur &= cur - 1u; }
+      if (have) finish_row<G, VEC, ITERS>(grp, p, r[hh], apply, validate, bits, cur_tr, cur_max);
+      have = next;
+    }
+  }
+}
+
+// Gradient of a long row: its pieces [piece_base, piece_base + npieces) summed
+// in a fixed tree order -- group x of the block sums the contiguous pieces
+// [x * per, (x + 1) * per) in order, then group 0 sums the group partials in
+// group order (deterministic; within 1e-6 * sum|terms| of the reference's
+// serial sum).  Called by every thread of the block; the result is valid in
+// group 0.  s_acc holds (blockDim.x / G) * dim_max floats.
+constexpr int kCombineDepth = 8;
+template <int G, int VEC, int ITERS, typename Grp>
+__device__ __forceinline__ void combine_long(const Grp& grp, const PushLaunch& p, const LongRecord& L,
+                                             unsigned D, float* s_acc, float (&g)[VEC * ITERS]) {
+  constexpr int C = VEC * ITERS;
+  constexpr unsigned NG = 256 / G;
+  const unsigned gl = grp.thread_rank(), x = threadIdx.x / G;
+  const unsigned per = (L.npieces + NG - 1) / NG;
+  const unsigned p0 = min(L.npieces, per * x), p1 = min(L.npieces, p0 + per);
+  float acc[C];
+#pragma unroll
+  for (int k = 0; k < C; ++k) acc[k] = 0.0f;
+  for (unsigned j0 = p0; j0 < p1; j0 += kCombineDepth) {
+    float r[kCombineDepth][C];
+#pragma unroll
+    for (int u = 0; u < kCombineDepth; ++u) {
+      const bool use = j0 + u < p1;
+      const float* q = p.part + ((unsigned long long)L.piece_base + j0 + u) * p.dim_max;
 #pragma unroll
       for (int it = 0; it < ITERS; ++it) {
         const unsigned col = (it * G + gl) * VEC;
-        float x[VEC];
-        if (col < D) load_vec<VEC>(q + col, x);
+        float t[VEC];
+        if (use && col < D) load_vec<VEC>(q + col, t);
         else {
 #pragma unroll
-          for (int y = 0; y < VEC; ++y) x[y] = 0.0f;
+          for (int y = 0; y < VEC; ++y) t[y] = -0.0f;
         }
 #pragma unroll
-        for (int y = 0; y < VEC; ++y) t[it * VEC + y] = x[y];
+        for (int y = 0; y < VEC; ++y) r[u][it * VEC + y] = t[y];
       }
-      load_state<G, VEC, ITERS>(gl, row, D, w, m, v);
-      unsigned long long upd = 0;
-      if (R.apply && gl == 0) upd = T.updates[slot];
-      if (multi) {
+    }
 #pragma unroll
-        for (int k = 0; k < C; ++k) g[k] = t[k];
-      } else {
-        const float scale = __uint_as_float(b);
+    for (int u = 0; u < kCombineDepth; ++u)
 #pragma unroll
-        for (int k = 0; k < C; ++k) g[k] = __fadd_rn(0.0f, __fmul_rn(t[k], scale));
+      for (int k = 0; k < C; ++k) acc[k] = __fadd_rn(acc[k], r[u][k]);
+  }
+#pragma unroll
+  for (int it = 0; it < ITERS; ++it) {
+    const unsigned col = (it * G + gl) * VEC;
+    if (col >= D) continue;
+#pragma unroll
+    for (int y = 0; y < VEC; ++y) s_acc[x * p.dim_max + col + y] = acc[it * VEC + y];
+  }
+  __syncthreads();
+  if (x == 0) {
+#pragma unroll
+    for (int k = 0; k < C; ++k) g[k] = 0.0f;
+    for (unsigned z = 0; z < NG; ++z) {
+#pragma unroll
+      for (int it = 0; it < ITERS; ++it) {
+        const unsigned col = (it * G + gl) * VEC;
+        if (col >= D) continue;
+#pragma unroll
+        for (int y = 0; y < VEC; ++y)
+          g[it * VEC + y] = __fadd_rn(g[it * VEC + y], s_acc[z * p.dim_max + col + y]);
       }
-      if ((int)tr != cur_tr) {
-        if (R.apply) flush_absmax(grp, p, cur_tr, cur_max);
-        cur_tr = (int)tr; cur_max = 0;
-      }
-      bits |= adam_row<G, VEC, ITERS>(gl, T, row, D, g, w, m, v, R.apply, R.validate, &cur_max);
-      if (R.apply && gl == 0) T.updates[slot] = upd + 1ull;
     }
   }
-  bits = cg::reduce(grp, bits, cg::bit_or<unsigned>());
-  if (gl == 0 && bits) atomicOr(&p.control->reject_bits, bits);
-  if (R.apply) flush_absmax(grp, p, cur_tr, cur_max);
 }
 
-// ------------------------------------------------------------------- pieces
-template <int G, int VEC, int ITERS, typename KeyT>
-__global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? EPS_PIECE_MIN_BLOCKS : 2) push_pieces(PushLaunch p, int pass) {
-  __shared__ const float* s_grad[kMaxFeatures];
-  __shared__ unsigned long long s_sbase[kMaxFeatures];
-  const Role R = role(p.control, pass);
-  if (!R.run || !R.partials) return;
+// Long rows of the plan (one per block at a time): combine, then LazyAdam by
+// group 0.  Called by every thread of the block.
+template <int G, int VEC, int ITERS, typename KeyT, typename Grp>
+__device__ __forceinline__ void update_long_rows(const Grp& grp, const PushLaunch& p, float* s_acc,
+                                                 unsigned* counter, bool apply, bool validate,
+                                                 unsigned& bits, int& cur_tr, unsigned& cur_max) {
   constexpr int C = VEC * ITERS;
-  stage_features(p, s_grad, s_sbase);
-  const auto grp = cg::tiled_partition<G>(cg::this_thread_block());
+  __shared__ unsigned s_rec;
   const unsigned gl = grp.thread_rank();
-  const unsigned count = *(volatile const unsigned*)&p.plan->piece_count;
-  const unsigned long long gid = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) / G;
-  const unsigned long long ngroups = (gridDim.x * (unsigned long long)blockDim.x) / G;
-  for (unsigned long long item = gid; item < count; item += ngroups) {
-    const uint2 pc = p.pieces[item];
-    const KeyT K = key_at<KeyT>(p.keys, pc.x);
-    const unsigned tr = (unsigned)(K >> p.slot_bits);
-    if (tr >= p.table_count) continue;
-    const unsigned D = p.tables[tr].dim;
-    float acc[C];
-    reduce_staged<G, VEC, ITERS, EPS_PIECE_DEPTH_REGS>(grp, p, s_grad, s_sbase, pc.x,
-                                                       (unsigned long long)pc.x + pc.y, D, acc);
-#pragma unroll
-    for (int it = 0; it < ITERS; ++it) {
-      const unsigned col = (it * G + gl) * VEC;
-      if (col >= D) continue;
-      float t[VEC];
-#pragma unroll
-      for (int x = 0; x < VEC; ++x) t[x] = acc[it * VEC + x];
-      store_vec<VEC>(p.part + item * p.dim_max + col, t);
-    }
-  }
-}
-
-// ------------------------------------------------------------ long segments
-constexpr int kLongThreads = 512;
-
-template <int G, int VEC, int ITERS, typename KeyT>
-__global__ void __launch_bounds__(kLongThreads) push_long(PushLaunch p, int pass) {
-  const Role R = role(p.control, pass);
-  if (!R.run) return;
-  if (!R.apply && !R.validate) return;
-  extern __shared__ float s_acc[];   // [groups][dim_max]
-  constexpr int C = VEC * ITERS;
-  constexpr int NG = kLongThreads / G;
-  const auto grp = cg::tiled_partition<G>(cg::this_thread_block());
-  const unsigned gl = grp.thread_rank(), w = threadIdx.x / G;
   const unsigned count = *(volatile const unsigned*)&p.plan->long_count;
   const KeyT smask = slot_mask_of<KeyT>(p.slot_bits);
-  unsigned bits = 0;
-  unsigned cur_max = 0;
-  int cur_tr = -1;
-  for (unsigned rec = blockIdx.x; rec < count; rec += gridDim.x) {
+  // records are claimed per block from `counter` (or taken grid-stride without one)
+  auto next = [&](unsigned prev) -> unsigned {
+    if (!counter) return prev + gridDim.x;
+    __syncthreads();                       // every thread has read s_rec
+    if (threadIdx.x == 0) s_rec = atomicAdd(counter, 1u);
+    __syncthreads();
+    return s_rec;
+  };
+  for (unsigned rec = counter ? next(0) : blockIdx.x; rec < count; rec = next(rec)) {
     const LongRecord L = p.records[rec];
     const KeyT K = (KeyT)L.key;
     const unsigned tr = (unsigned)(K >> p.slot_bits);
-    if (tr >= p.table_count) continue;
     const PushTable& T = p.tables[tr];
     const unsigned D = T.dim;
-    const unsigned long long slot = (unsigned long long)(K & smask);
-    // a contiguous chunk of pieces per group, combined afterwards in group order
-    const unsigned per = (L.npieces + NG - 1) / NG;
-    const unsigned p0 = min(L.npieces, per * w), p1 = min(L.npieces, p0 + per);
-    float acc[C];
-#pragma unroll
-    for (int k = 0; k < C; ++k) acc[k] = 0.0f;
-    for (unsigned j0 = p0; j0 < p1; j0 += 4) {
-      float x[4][C];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const bool use = j0 + u < p1;
-        const unsigned long long item = (unsigned long long)L.piece_base + j0 + u;
-#pragma unroll
-        for (int it = 0; it < ITERS; ++it) {
-          const unsigned col = (it * G + gl) * VEC;
-          float t[VEC];
-          if (use && col < D) load_vec<VEC>(p.part + item * p.dim_max + col, t);
-          else {
-#pragma unroll
-            for (int v = 0; v < VEC; ++v) t[v] = 0.0f;
-          }
-#pragma unroll
-          for (int v = 0; v < VEC; ++v) x[u][it * VEC + v] = t[v];
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (j0 + u >= p1) break;
-#pragma unroll
-        for (int k = 0; k < C; ++k) acc[k] = __fadd_rn(acc[k], x[u][k]);
-      }
-    }
-#pragma unroll
-    for (int it = 0; it < ITERS; ++it) {
-      const unsigned col = (it * G + gl) * VEC;
-      if (col >= D) continue;
-#pragma unroll
-      for (int x = 0; x < VEC; ++x) s_acc[w * p.dim_max + col + x] = acc[it * VEC + x];
-    }
-    __syncthreads();
-    if (w == 0) {
-      float g[C], wv[C], mv[C], vv[C];
+    float g[C];
+    combine_long<G, VEC, ITERS>(grp, p, L, D, s_acc, g);
+    if (threadIdx.x < G) {
+      const unsigned long long slot = (unsigned long long)(K & smask);
       float* row = T.state + slot * 3ull * D;
-      load_state<G, VEC, ITERS>(gl, row, D, wv, mv, vv);
-#pragma unroll
-      for (int k = 0; k < C; ++k) g[k] = 0.0f;
-      for (int x = 0; x < NG; ++x) {
+      float w[C], m[C], v[C];
+      load_state<G, VEC, ITERS>(gl, row, D, w, m, v);
+      if ((int)tr != cur_tr) {
+        if (apply) flush_absmax(grp, p, cur_tr, cur_max);
+        cur_tr = (int)tr; cur_max = 0;
+      }
+      bits |= adam_row<G, VEC, ITERS>(gl, T, row, D, g, w, m, v, apply, validate, &cur_max);
+      if (apply && gl == 0) T.updates[slot] += 1ull;
+    }
+    __syncthreads();                       // s_acc is reused
+  }
+}
+
+// Flush a block's reject bits and state bound; then the last block of the
+// launch (counted in *done) runs `last` once every other block's writes are
+// visible.  Called by every thread of the block.
+template <typename Grp>
+__device__ __forceinline__ bool flush_and_count(const Grp& grp, const PushLaunch& p, unsigned bits,
+                                                bool apply, int cur_tr, unsigned cur_max,
+                                                unsigned* done) {
+  __shared__ unsigned s_last;
+  bits = cg::reduce(grp, bits, cg::bit_or<unsigned>());
+  if (grp.thread_rank() == 0 && bits) atomicOr(&p.control->reject_bits, bits);
+  if (apply) flush_absmax(grp, p, cur_tr, cur_max);
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(done, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (s_last) __threadfence();
+  return s_last;
+}
+
+// src/update/lazy_adam.cpp:39-41: once per table iff the push is accepted.
+__device__ __forceinline__ void finalize_tables(const PushLaunch& p) {
+  PushControl* c = p.control;
+  const unsigned mode = *(volatile unsigned*)&c->mode;
+  const unsigned bits = *(volatile unsigned*)&c->reject_bits;
+  const bool accepted = mode != kModeRejected && bits == 0;
+  if (accepted) {
+    for (unsigned t = threadIdx.x; t < p.table_count; t += blockDim.x) {
+      const PushTable& T = p.tables[t];
+      DeviceTable* d = T.dtable;
+      d->optimizer_sequence += 1ull;
+      d->beta1_power = __fmul_rn(d->beta1_power, T.beta1);
+      d->beta2_power = __fmul_rn(d->beta2_power, T.beta2);
+    }
+  }
+  if (threadIdx.x == 0) c->accepted = accepted ? 1u : 0u;
+}
+
+// ----------------------------------------------------------------- stage A
+// Piece sums and single-occurrence rows in one launch, interleaved so that the
+// L2-bound piece reductions (gradient rows re-read per occurrence) overlap the
+// HBM-bound read-modify-write of single rows: the launch's chunk sequence
+// holds R row chunks (32 plan records) and Q piece chunks (kChunkPieces pieces
+// per group), chunk c being a piece chunk iff floor((c+1)Q/T) > floor(cQ/T)
+// (T = R + Q); warps take chunks grid-stride.  SAFE mode applies single rows
+// here; CHECKED mode only validates them (stage C applies).
+constexpr unsigned kChunkPieces = 1;
+template <int G, int VEC, int ITERS, typename KeyT>
+__global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? EPS_PUSH_MIN_BLOCKS : 2) push_stage_a(PushLaunch p) {
+  __shared__ const float* s_grad[kMaxFeatures];
+  const unsigned mode = *(volatile const unsigned*)&p.control->mode;
+  if (mode == kModeRejected) return;
+  const bool apply = mode == kModeSafe, validate = mode == kModeChecked;
+  stage_features(p, s_grad);
+  constexpr int C = VEC * ITERS;
+  constexpr unsigned GPW = 32 / G;
+  const auto grp = cg::tiled_partition<G>(cg::this_thread_block());
+  const unsigned gl = grp.thread_rank();
+  const unsigned lane = threadIdx.x & 31u, gw = lane / G;
+  const unsigned U = *(volatile const unsigned*)p.seg_total;
+  const unsigned P = *(volatile const unsigned*)&p.plan->piece_count;
+  // with the ring path (push_rows_ring) this launch reduces only the pieces
+  const unsigned long long R = p.ring_dim ? 0ull : (U + 31ull) / 32ull;
+  const unsigned long long Q = (P + kChunkPieces * GPW - 1ull) / (kChunkPieces * GPW);
+  const unsigned long long T = R + Q;
+  unsigned bits = 0;
+  int cur_tr = -1;
+  unsigned cur_max = 0;
+  // chunks are claimed dynamically (one counter per launch); the next claim is
+  // issued before the current chunk is processed
+  unsigned claim = 0;
+  if (lane == 0) claim = atomicAdd(&p.control->work_a, 1u);
+  unsigned long long c = __shfl_sync(0xffffffffu, claim, 0);
+  while (c < T) {
+    if (lane == 0) claim = atomicAdd(&p.control->work_a, 1u);
+    const unsigned long long qb = c * Q / T, qa = (c + 1) * Q / T;
+    if (qa > qb) {
+      for (unsigned k = 0; k < kChunkPieces; ++k) {
+        const unsigned long long item = (qb * GPW + gw) * kChunkPieces + k;
+        if (item >= P) break;
+        const uint2 pc = p.pieces[item];
+        const KeyT K = key_at<KeyT>(p.keys, pc.x);
+        const unsigned D = p.tables[(unsigned)(K >> p.slot_bits)].dim;
+        float acc[C];
+        reduce_staged<G, VEC, ITERS, EPS_PIECE_DEPTH_REGS>(grp, p, s_grad, pc.x,
+                                                           (unsigned long long)pc.x + pc.y, D, acc);
 #pragma unroll
         for (int it = 0; it < ITERS; ++it) {
           const unsigned col = (it * G + gl) * VEC;
           if (col >= D) continue;
+          float t[VEC];
 #pragma unroll
-          for (int y = 0; y < VEC; ++y)
-            g[it * VEC + y] = __fadd_rn(g[it * VEC + y], s_acc[x * p.dim_max + col + y]);
+          for (int x = 0; x < VEC; ++x) t[x] = acc[it * VEC + x];
+          store_vec<VEC>(p.part + item * p.dim_max + col, t);
         }
       }
-      if ((int)tr != cur_tr) {
-        if (R.apply) flush_absmax(grp, p, cur_tr, cur_max);
-        cur_tr = (int)tr; cur_max = 0;
-      }
-      bits |= adam_row<G, VEC, ITERS>(gl, T, row, D, g, wv, mv, vv, R.apply, R.validate, &cur_max);
-      if (R.apply && gl == 0) T.updates[slot] += 1ull;
+    } else {
+      update_chunk<G, VEC, ITERS, KeyT>(grp, p, s_grad, (c - qb) * 32ull, U, 1u, apply, validate,
+                                        bits, cur_tr, cur_max);
     }
-    __syncthreads();
+    c = __shfl_sync(0xffffffffu, claim, 0);
   }
-  if (w == 0) {
-    bits = cg::reduce(grp, bits, cg::bit_or<unsigned>());
-    if (gl == 0 && bits) atomicOr(&p.control->reject_bits, bits);
-    if (R.apply) flush_absmax(grp, p, cur_tr, cur_max);
-  }
+  bits = cg::reduce(grp, bits, cg::bit_or<unsigned>());
+  if (gl == 0 && bits) atomicOr(&p.control->reject_bits, bits);
+  if (apply) flush_absmax(grp, p, cur_tr, cur_max);
 }
 
+// --------------------------------------------------- rows through an async ring
+// The row updates for the common shape (every table of the push has the same
+// dimension D in {32, 64, 128}; 16-byte aligned gradients).  A warp works in
+// steps of 32 / G rows, one per group of G = D / 4 lanes (one float4 of each of
+// w, m, v and g per lane), and keeps the rows of the next kRingSlots / (32 / G)
+// - 1 steps in flight through a ring of shared-memory slots filled by cp.async
+// (16-byte per-lane asynchronous copies, one commit group per step): the
+// [w|m|v] row, the row's gradient (the single occurrence's pre-scaled row or,
+// for 2..long_run occurrences, its in-order piece sum) and the 16-byte block
+// holding its counter.  Rows in flight hold no registers, so an SM keeps
+// warps x kRingSlots rows in flight.  Rows come from chunks of 32 plan records
+// claimed dynamically; the next chunk's records load while the current chunk is
+// issued.  Long rows and padding rows are skipped (stage B).
+constexpr int kRingSlots = 8;
+constexpr unsigned long long kEmptySlot = ~0ull;
+template <int D> struct RingShape {
+  static constexpr int kGroup = D / 4;                    // lanes per row
+  static constexpr int kRows = 32 / kGroup;               // rows per step
+  static constexpr int kSteps = kRingSlots / kRows;       // steps in the ring
+  static constexpr int kSlot = 4 * D + 8;                 // floats: w, m, v, g, counter block, key
+  static constexpr int kWarps = D >= 128 ? 4 : 8;          // warps per block
+  static constexpr size_t kBytes = (size_t)kWarps * kRingSlots * kSlot * sizeof(float);
+};  // D = 64: 67.6 KB ring + 3.6 KB descriptors per block, three blocks per SM
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_group() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+
+// LazyAdam parameters of one table, held in registers while a warp's rows
+// stay in that table.
+struct AdamRegs {
+  float b1, o1, b2, o2, lr, eps, lo, hi;
+  int bounded;
+  float* state;
+  unsigned long long* updates;
+};
+__device__ __forceinline__ AdamRegs adam_regs(const PushTable& T) {
+  return AdamRegs{T.beta1, T.one_minus_beta1, T.beta2, T.one_minus_beta2, T.lr_t, T.epsilon,
+                  T.bound_min, T.bound_max, T.has_bounds, T.state, T.updates};
+}
+
+// LazyAdam on N consecutive elements of one row (src/update/lazy_adam.cpp:28-37),
+// in place; VALIDATE returns the reject bits, APPLY raises *mx to the largest
+// |w|, |m|, v written.
+template <int N, bool APPLY, bool VALIDATE>
+__device__ __forceinline__ unsigned adam_elems(const AdamRegs& P, const float (&g)[N], float (&w)[N],
+                                               float (&m)[N], float (&v)[N], float& mx) {
+  unsigned bits = 0;
+#pragma unroll
+  for (int x = 0; x < N; ++x) {
+    const float mm = __fadd_rn(__fmul_rn(P.b1, m[x]), __fmul_rn(P.o1, g[x]));
+    const float vv = __fadd_rn(__fmul_rn(P.b2, v[x]), __fmul_rn(__fmul_rn(P.o2, g[x]), g[x]));
+    const float ww = __fsub_rn(w[x], __fdiv_rn(__fmul_rn(P.lr, mm), __fadd_rn(__fsqrt_rn(vv), P.eps)));
+    if (VALIDATE) {
+      if (!isfinite(g[x])) bits |= kRejectReduction;
+      if (!isfinite(mm) || !isfinite(vv) || !isfinite(ww)) bits |= kRejectOptimizer;
+    }
+    m[x] = mm; v[x] = vv; w[x] = ww;
+  }
+  if (P.bounded) {
+#pragma unroll
+    for (int x = 0; x < N; ++x) w[x] = w[x] < P.lo ? P.lo : (P.hi < w[x] ? P.hi : w[x]);
+  }
+  if (APPLY) {
+#pragma unroll
+    for (int x = 0; x < N; ++x) mx = fmaxf(mx, fmaxf(fabsf(w[x]), fmaxf(fabsf(m[x]), fabsf(v[x]))));
+  }
+  return bits;
+}
+
+template <int D, typename KeyT, bool APPLY, bool VALIDATE>
+__device__ __forceinline__ void ring_rows(const PushLaunch& p, const PushTable* s_tab, bool tabs_shared,
+                                          const float* const* s_feat, bool feats_shared) {
+  using S = RingShape<D>;
+  constexpr int G = S::kGroup, RP = S::kRows, NS = S::kSteps;
+  extern __shared__ float4 ring_smem[];
+  const auto grp = cg::tiled_partition<G>(cg::this_thread_block());
+  const unsigned lane = threadIdx.x & 31u, gw = lane / G, gl = grp.thread_rank();
+  float* const ring = reinterpret_cast<float*>(ring_smem) + (threadIdx.x >> 5) * (kRingSlots * S::kSlot);
+  const unsigned U = *(volatile const unsigned*)p.seg_total;
+  const unsigned long long R = (U + 31ull) / 32ull;
+  const unsigned slot_bits = p.slot_bits;
+  const KeyT smask = slot_mask_of<KeyT>(slot_bits);
+  auto table = [&](unsigned tr) -> const PushTable& { return tabs_shared ? s_tab[tr] : p.tables[tr]; };
+
+  // ---- producer: the chunk being issued (records one per lane, mask of the
+  // rows still to issue) and the next chunk (records loaded ahead)
+  auto claim_chunk = [&]() -> unsigned long long {
+    unsigned c = 0;
+    if (lane == 0) c = atomicAdd(&p.control->work_ring, 1u);
+    return __shfl_sync(0xffffffffu, c, 0);
+  };
+  auto load_chunk = [&](unsigned long long c, RowRec& rec) {
+    rec = RowRec{0ull, 0u, kRowSkip};
+    if (c < R && c * 32ull + lane < U) rec = p.rows[c * 32ull + lane];
+  };
+  unsigned long long c_cur = claim_chunk();
+  RowRec r_cur, r_nxt;
+  load_chunk(c_cur, r_cur);
+  unsigned long long c_nxt = c_cur < R ? claim_chunk() : R;
+  load_chunk(c_nxt, r_nxt);
+  bool more = c_cur < R;
+  unsigned m_cur = __ballot_sync(0xffffffffu, r_cur.b != kRowSkip);
+  int p_tr = -1;                          // producer's cached table
+  const float* p_state = nullptr;
+  const unsigned long long* p_upd = nullptr;
+
+  // issues the next step's rows into the step's slots, all groups at once:
+  // group h takes the h-th remaining row of the current chunk (a step never
+  // spans two chunks; groups without a row write an empty marker); one commit
+  // group per call; returns whether any row was issued
+  auto produce = [&](int step) -> bool {
+    while (more && m_cur == 0) {
+      c_cur = c_nxt; r_cur = r_nxt;
+      more = c_cur < R;
+      if (!more) break;
+      m_cur = __ballot_sync(0xffffffffu, r_cur.b != kRowSkip);
+      c_nxt = claim_chunk();
+      load_chunk(c_nxt, r_nxt);
+    }
+    unsigned mine = more ? m_cur : 0u;
+#pragma unroll
+    for (int h = 0; h < RP - 1; ++h)
+      if ((unsigned)h < gw) mine &= mine - 1u;
+    const bool has = mine != 0;
+    const int j = has ? __ffs(mine) - 1 : 0;
+#pragma unroll
+    for (int h = 0; h < RP; ++h) m_cur &= m_cur - 1u;
+    const unsigned long long key = __shfl_sync(0xffffffffu, r_cur.key, j);
+    const unsigned a = __shfl_sync(0xffffffffu, r_cur.a, j);
+    const unsigned b = __shfl_sync(0xffffffffu, r_cur.b, j);
+    float* slot = ring + (step * RP + gw) * S::kSlot;
+    if (has) {
+      const KeyT K = (KeyT)key;
+      const int tr = (int)(K >> slot_bits);
+      if (tr != p_tr) { const PushTable& T = table((unsigned)tr); p_state = T.state; p_upd = T.updates; p_tr = tr; }
+      const unsigned long long sl = (unsigned long long)(K & smask);
+      const float* st = p_state + sl * (3ull * D);
+      const unsigned f = a >> kRowBits;
+      const float* gr = (b & kRowMulti) ? p.part + (unsigned long long)a * D
+                                        : (feats_shared ? s_feat[f] : p.features[f].scaled) +
+                                              (unsigned long long)(a & ((1u << kRowBits) - 1u)) * D;
+      // [w|m|v]: 3G 16-byte pieces, three per lane; gradient: one per lane
+#pragma unroll
+      for (int q = 0; q < 3; ++q) cp_async16(slot + 4 * (q * G + gl), st + 4 * (q * G + gl));
+      cp_async16(slot + 3 * D + 4 * gl, gr + 4 * gl);
+      if (gl == 0) cp_async16(slot + 4 * D, p_upd + (sl & ~1ull));
+    }
+    if (gl == 0) *reinterpret_cast<unsigned long long*>(slot + 4 * D + 4) = has ? key : kEmptySlot;
+    cp_async_commit_group();
+    return __any_sync(0xffffffffu, has);
+  };
+
+  unsigned bits = 0;
+  int cur_tr = -1;
+  float cur_max = 0.0f;
+  AdamRegs P{};
+  int live = 0;                          // steps in the ring holding rows
+#pragma unroll
+  for (int k = 0; k < NS - 1; ++k) live += produce(k) ? 1 : 0;
+  // step t: issue into ring step (t - 1) % NS (consumed at t - 1), then consume
+  // ring step t % NS; unrolled over the ring so that slot offsets are constants
+  bool done = live == 0 && !more;
+  while (!done) {
+#pragma unroll
+    for (int k = 0; k < NS; ++k) {
+      live += produce((k + NS - 1) % NS) ? 1 : 0;
+      asm volatile("cp.async.wait_group %0;\n" ::"n"(NS - 1) : "memory");
+      __syncwarp();
+      const float* s = ring + (k * RP + gw) * S::kSlot;
+      const unsigned long long key = *reinterpret_cast<const unsigned long long*>(s + 4 * D + 4);
+      const bool step_used = __any_sync(0xffffffffu, key != kEmptySlot);
+      if (key != kEmptySlot) {
+        const KeyT K = (KeyT)key;
+        const int tr = (int)(K >> slot_bits);
+        if (tr != cur_tr) {
+          if (APPLY) flush_absmax(grp, p, cur_tr, __float_as_uint(cur_max));
+          P = adam_regs(table((unsigned)tr));
+          cur_tr = tr; cur_max = 0.0f;
+        }
+        const unsigned long long sl = (unsigned long long)(K & smask);
+        float w[4], m[4], v[4], g[4];
+        load_vec<4>(s + 4 * gl, w);
+        load_vec<4>(s + D + 4 * gl, m);
+        load_vec<4>(s + 2 * D + 4 * gl, v);
+        load_vec<4>(s + 3 * D + 4 * gl, g);
+        // 0 + src * scale for a single row (batch_access.cpp:118); a piece sum
+        // starts from +0 and is never -0, so 0 + sum leaves it unchanged
+#pragma unroll
+        for (int x = 0; x < 4; ++x) g[x] = __fadd_rn(0.0f, g[x]);
+        bits |= adam_elems<4, APPLY, VALIDATE>(P, g, w, m, v, cur_max);
+        if (APPLY) {
+          float* row = P.state + sl * (3ull * D) + 4 * gl;
+          store_vec_stream<4>(row, w);
+          store_vec_stream<4>(row + D, m);
+          store_vec_stream<4>(row + 2 * D, v);
+          if (gl == 0) {
+            const unsigned long long upd = *reinterpret_cast<const unsigned long long*>(s + 4 * D + 2 * (sl & 1ull));
+            __stcs(P.updates + sl, upd + 1ull);
+          }
+        }
+      }
+      live -= step_used ? 1 : 0;
+      __syncwarp();
+      if (live == 0 && !more) { done = true; break; }
+    }
+  }
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+  bits = cg::reduce(grp, bits, cg::bit_or<unsigned>());
+  if (gl == 0 && bits) atomicOr(&p.control->reject_bits, bits);
+  if (APPLY) flush_absmax(grp, p, cur_tr, __float_as_uint(cur_max));
+}
+
+template <int D, typename KeyT>
+__global__ void __launch_bounds__(RingShape<D>::kWarps * 32) push_rows_ring(PushLaunch p) {
+  // table and feature descriptors of small pushes live in shared memory: the
+  // large ring leaves little L1, and a descriptor miss would stall the warp
+  constexpr unsigned kTabs = 32, kFeats = 128;
+  __shared__ PushTable s_tab[kTabs];
+  __shared__ const float* s_feat[kFeats];
+  const unsigned mode = *(volatile const unsigned*)&p.control->mode;
+  if (mode == kModeRejected) return;
+  for (unsigned i = threadIdx.x; i < min(p.table_count, kTabs); i += blockDim.x) s_tab[i] = p.tables[i];
+  for (unsigned i = threadIdx.x; i < min(p.feature_count, kFeats); i += blockDim.x) s_feat[i] = p.features[i].scaled;
+  __syncthreads();
+  const bool tabs_shared = p.table_count <= kTabs, feats_shared = p.feature_count <= kFeats;
+  if (mode == kModeSafe) ring_rows<D, KeyT, true, false>(p, s_tab, tabs_shared, s_feat, feats_shared);
+  else ring_rows<D, KeyT, false, true>(p, s_tab, tabs_shared, s_feat, feats_shared);
+}
+
+// ----------------------------------------------------------------- stage B
+// Long rows (block-level combine of their pieces) and rows with a piece sum;
+// SAFE mode applies, CHECKED mode validates.  Unless the push is CHECKED, the
+// launch's last block then advances the beta powers iff it was accepted.
+template <int G, int VEC, int ITERS, typename KeyT>
+__global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? EPS_PUSH_MIN_BLOCKS : 2) push_stage_b(PushLaunch p) {
+  __shared__ const float* s_grad[kMaxFeatures];
+  extern __shared__ float s_acc[];
+  const unsigned mode = *(volatile const unsigned*)&p.control->mode;
+  const auto grp = cg::tiled_partition<G>(cg::this_thread_block());
+  if (mode == kModeRejected) {
+    if (blockIdx.x == 0) finalize_tables(p);
+    return;
+  }
+  const bool apply = mode == kModeSafe, validate = mode == kModeChecked;
+  stage_features(p, s_grad);
+  unsigned bits = 0;
+  int cur_tr = -1;
+  unsigned cur_max = 0;
+  update_long_rows<G, VEC, ITERS, KeyT>(grp, p, s_acc, &p.control->work_long, apply, validate, bits,
+                                        cur_tr, cur_max);
+  const unsigned U = *(volatile const unsigned*)p.seg_total;
+  const unsigned lane = threadIdx.x & 31u;
+  unsigned claim = 0;
+  if (lane == 0) claim = atomicAdd(&p.control->work_b, 1u);
+  unsigned long long c = __shfl_sync(0xffffffffu, claim, 0);
+  while (!p.ring_dim && c * 32ull < U) {
+    if (lane == 0) claim = atomicAdd(&p.control->work_b, 1u);
+    update_chunk<G, VEC, ITERS, KeyT>(grp, p, s_grad, c * 32ull, U, 2u, apply, validate, bits,
+                                      cur_tr, cur_max);
+    c = __shfl_sync(0xffffffffu, claim, 0);
+  }
+  if (flush_and_count(grp, p, bits, apply, cur_tr, cur_max, &p.control->blocks_done_b) &&
+      mode != kModeChecked)
+    finalize_tables(p);
+}
+
+// ----------------------------------------------------------------- stage C
+// CHECKED mode only: when stages A and B rejected nothing, apply every row
+// (recomputing the same gradients), then the last block finalizes.
+template <int G, int VEC, int ITERS, typename KeyT>
+__global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? EPS_PUSH_MIN_BLOCKS : 2) push_stage_c(PushLaunch p) {
+  __shared__ const float* s_grad[kMaxFeatures];
+  extern __shared__ float s_acc[];
+  const unsigned mode = *(volatile const unsigned*)&p.control->mode;
+  if (mode != kModeChecked) return;
+  const auto grp = cg::tiled_partition<G>(cg::this_thread_block());
+  const bool apply = *(volatile const unsigned*)&p.control->reject_bits == 0;
+  unsigned bits = 0;
+  int cur_tr = -1;
+  unsigned cur_max = 0;
+  if (apply) {
+    stage_features(p, s_grad);
+    update_long_rows<G, VEC, ITERS, KeyT>(grp, p, s_acc, nullptr, true, false, bits, cur_tr, cur_max);
+    const unsigned U = *(volatile const unsigned*)p.seg_total;
+    const unsigned long long warp = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) >> 5;
+    const unsigned long long nwarps = (gridDim.x * (unsigned long long)blockDim.x) >> 5;
+    for (unsigned long long c = warp; c * 32ull < U; c += nwarps)
+      update_chunk<G, VEC, ITERS, KeyT>(grp, p, s_grad, c * 32ull, U, 3u, true, false, bits,
+                                        cur_tr, cur_max);
+  }
+  if (flush_and_count(grp, p, 0u, apply, cur_tr, cur_max, &p.control->blocks_done_c))
+    finalize_tables(p);
+}
 // --------------------------------------------------- agent-style updates
 // CacheBackend::ApplyHost (src/cache/host_backend.cpp:119-146): LazyAdam with the
 // caller's optimizer context on unique rows, all-or-nothing, no power advance.
@@ -609,42 +996,56 @@ cudaError_t run_apply_rows(const ApplyLaunch& p, cudaStream_t s) {
 }
 
 // ----------------------------------------------------------------- finalize
-__global__ void push_finalize(PushLaunch p) {
-  PushControl* c = p.control;
-  const unsigned mode = *(volatile unsigned*)&c->mode;
-  const unsigned bits = *(volatile unsigned*)&c->reject_bits;
-  const bool accepted = mode != kModeRejected && bits == 0;
-  if (accepted) {
-    for (unsigned t = threadIdx.x; t < p.table_count; t += blockDim.x) {
-      const PushTable& T = p.tables[t];
-      DeviceTable* d = T.dtable;
-      // src/update/lazy_adam.cpp:39-41
-      d->optimizer_sequence += 1ull;
-      d->beta1_power = __fmul_rn(d->beta1_power, T.beta1);
-      d->beta2_power = __fmul_rn(d->beta2_power, T.beta2);
-    }
+// Only a push without occurrences launches this kernel; otherwise stage B or C
+// finalizes.
+__global__ void push_finalize(PushLaunch p) { finalize_tables(p); }
+
+// Persistent grid of the ring kernel: as many blocks as fit on the SMs.
+template <int D, typename KeyT>
+cudaError_t run_ring(const PushLaunch& p, cudaStream_t s) {
+  using S = RingShape<D>;
+  static int blocks_per_sm[64] = {};          // per device, set on first use
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  int& bps = blocks_per_sm[dev & 63];
+  if (!bps) {
+    e = cudaFuncSetAttribute(push_rows_ring<D, KeyT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)S::kBytes);
+    if (e != cudaSuccess) return e;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, push_rows_ring<D, KeyT>, S::kWarps * 32,
+                                                      S::kBytes);
+    if (e != cudaSuccess) return e;
+    if (bps < 1) bps = 1;
   }
-  if (threadIdx.x == 0) c->accepted = accepted ? 1u : 0u;
+  int sms = 0;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long want = (p.n + 31) / 32;
+  const unsigned grid = (unsigned)max(1ull, min(want, (unsigned long long)sms * bps));
+  push_rows_ring<D, KeyT><<<grid, S::kWarps * 32, S::kBytes, s>>>(p);
+  return cudaGetLastError();
 }
 
 template <int G, int VEC, int ITERS, typename KeyT>
 cudaError_t run_apply(const PushLaunch& p, cudaStream_t s) {
   if (!p.n) return cudaSuccess;
-  constexpr unsigned rows_blocks = (VEC * ITERS <= 4) ? EPS_PUSH_MIN_BLOCKS : 2;
-  constexpr unsigned long long groups_per_block = 256 / G;
-  const unsigned long long want = (p.n + groups_per_block - 1) / groups_per_block;
-  const unsigned rows_grid = (unsigned)max(1ull, min(want, 148ull * rows_blocks));
-  constexpr unsigned piece_blocks = (VEC * ITERS <= 4) ? EPS_PIECE_MIN_BLOCKS : 2;
-  const unsigned piece_grid =
-      (unsigned)max(1ull, min(((unsigned long long)p.max_pieces + groups_per_block - 1) / groups_per_block,
-                              148ull * piece_blocks));
-  const size_t long_smem = (size_t)(kLongThreads / G) * p.dim_max * sizeof(float);
-  const unsigned long_grid = 148 * 2;
-  push_pieces<G, VEC, ITERS, KeyT><<<piece_grid, 256, 0, s>>>(p, 0);
-  push_rows<G, VEC, ITERS, KeyT><<<rows_grid, 256, 0, s>>>(p, 0);
-  push_long<G, VEC, ITERS, KeyT><<<long_grid, kLongThreads, long_smem, s>>>(p, 0);
-  push_rows<G, VEC, ITERS, KeyT><<<rows_grid, 256, 0, s>>>(p, 1);
-  push_long<G, VEC, ITERS, KeyT><<<long_grid, kLongThreads, long_smem, s>>>(p, 1);
+  constexpr unsigned blocks = (VEC * ITERS <= 4) ? EPS_PUSH_MIN_BLOCKS : 2;
+  const unsigned long long want = (p.n + 255) / 256;
+  const unsigned grid = (unsigned)max(1ull, min(want, 148ull * blocks));
+  const size_t smem = (size_t)(256 / G) * p.dim_max * sizeof(float);
+  push_stage_a<G, VEC, ITERS, KeyT><<<grid, 256, 0, s>>>(p);
+  if (p.ring_dim) {
+    cudaError_t e = cudaSuccess;
+    switch (p.ring_dim) {
+      case 32: e = run_ring<32, KeyT>(p, s); break;
+      case 64: e = run_ring<64, KeyT>(p, s); break;
+      default: e = run_ring<128, KeyT>(p, s); break;
+    }
+    if (e != cudaSuccess) return e;
+  }
+  push_stage_b<G, VEC, ITERS, KeyT><<<grid, 256, smem, s>>>(p);
+  push_stage_c<G, VEC, ITERS, KeyT><<<min(grid, 148u), 256, smem, s>>>(p);
   return cudaGetLastError();
 }
 
@@ -665,7 +1066,8 @@ cudaError_t launch_push_prescan(const PushLaunch& p, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
-unsigned launch_push_apply_count(const PushLaunch& p) { return p.n ? 5u : 0u; }
+unsigned launch_push_apply_count(const PushLaunch& p) { return p.n ? (p.ring_dim ? 4u : 3u) : 0u; }
+unsigned launch_push_finalize_count(const PushLaunch& p) { return p.n ? 0u : 1u; }
 
 cudaError_t launch_push_apply(const PushLaunch& p, cudaStream_t stream) {
   if (p.vec == 4) {
@@ -701,6 +1103,7 @@ cudaError_t launch_apply_rows(const ApplyLaunch& p, cudaStream_t stream) {
 }
 
 cudaError_t launch_push_finalize(const PushLaunch& p, cudaStream_t stream) {
+  if (p.n) return cudaSuccess;          // finalized by the apply stages
   push_finalize<<<1, 32, 0, stream>>>(p);
   return cudaGetLastError();
 }

@@ -104,6 +104,9 @@ struct Ticket {
   // layout
   std::vector<unsigned> feature_ids, feature_tables, dims, ranks;
   std::vector<unsigned long long> grad_rows, scale_base;
+  std::vector<unsigned> pooling;
+  std::vector<unsigned long long> scaled_off;   // value offset of a mean feature in `scaled`
+  float* scaled = nullptr;          // pre-scaled gradients of the mean features
   std::vector<unsigned> table_ids;
   std::vector<unsigned long long> table_occ;
   unsigned long long n = 0;
@@ -118,7 +121,6 @@ struct Ticket {
   unsigned* seg_total = nullptr;
   uint2* pieces = nullptr;
   unsigned max_pieces = 0;
-  float* part = nullptr;
   LongRecord* records = nullptr;
   PushControl* control = nullptr;
   unsigned* lookup_error = nullptr;
@@ -362,6 +364,20 @@ struct EpsB200Store {
     }
     return PushMessage(h.control.reject_bits, h.lookup_error);
   }
+  // Back-pressure for callers that enqueue rounds faster than the device runs
+  // them: with kMaxInflight asynchronous pushes still enqueued, the host waits
+  // for the oldest before the next lookup allocates its ticket, so that the
+  // ticket memory of a steady stream of rounds stays bounded (and the
+  // stream-ordered pool stops growing after the first rounds).
+  static constexpr size_t kMaxInflight = 3;
+  void Throttle(cudaStream_t stream) {
+    while (inflight.size() >= kMaxInflight) {
+      auto it = tickets.find(inflight.front());
+      if (it == tickets.end() || !it->second.push_in_flight) { inflight.pop_front(); continue; }
+      Cuda(cudaEventSynchronize(it->second.done));
+      Poll(stream);
+    }
+  }
   // Settles, without waiting, every enqueued push that the device has finished
   // (in enqueue order), so tickets of asynchronous pushes release their device
   // memory as soon as possible.  Rejections are reported by the next
@@ -528,7 +544,8 @@ int eps_b200_create_table(EpsB200Store* store, const EpsB200Table* table, EpsB20
     t.bytes = bytes;
     try {
       Cuda(cudaMalloc(&t.state, std::max<size_t>(rows * 12ull * d.dimension, 16)));
-      Cuda(cudaMalloc(&t.updates, std::max<size_t>(rows * 8ull, 16)));
+      // an even number of counters: the ring push reads the 16-byte block of two
+      Cuda(cudaMalloc(&t.updates, std::max<size_t>(((rows + 1ull) & ~1ull) * 8ull, 16)));
       Cuda(cudaMalloc(&t.dtable, sizeof(DeviceTable)));
       DeviceTable dt{};
       dt.beta1_power = d.initial_beta1_power;
@@ -578,7 +595,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
     std::map<unsigned, unsigned> ranks;   // table id -> rank (ascending id)
     std::unordered_set<unsigned> ids;
     unsigned long long total_keys = 0, total_offsets = 0, total_lengths = 0, total_rows = 0,
-                       host_out_values = 0, bags = 0;
+                       host_out_values = 0, bags = 0, mean_values = 0;
     std::vector<unsigned> dims;
     bool out16 = true, out8 = true, any_host_out = false, any_padding = false;
     for (uint64_t i = 0; i < count; ++i) {
@@ -610,6 +627,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       total_offsets += f.offset_count;
       if (f.valid_lengths) total_lengths += f.offset_count - 1;
       total_rows += rows;
+      if (f.pooling == 1) mean_values += rows * t.def.dimension;
       bags += f.offset_count - 1;
       dims.push_back(t.def.dimension);
     }
@@ -651,8 +669,8 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
     const unsigned long long max_long = total_keys / (kLongRun + 1) + 1;
     const unsigned long long max_pieces = (total_keys + kPiece - 1) / kPiece + max_long + total_keys / 2;
     size_t at_k0 = 0, at_k1 = 0, at_s0 = 0, at_s1 = 0, at_scale = 0, at_hist = 0, at_seg = 0,
-           at_segtot = 0, at_segscr = 0, at_pieces = 0, at_part = 0, at_rec = 0, at_rows = 0,
-           at_plan = 0,
+           at_segtot = 0, at_segscr = 0, at_pieces = 0, at_rec = 0, at_rows = 0,
+           at_plan = 0, at_scaled = 0,
            at_ptab = 0, at_pfeat = 0, at_gpre = 0, at_end = 0;
     size_t at_zero = 0;   // start of the region zeroed by the lookup's single memset
     if (!read_only) {
@@ -664,9 +682,9 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       at_seg = c.take<unsigned>(total_keys + 1);
       at_segtot = c.take<unsigned>(1);
       at_pieces = c.take<uint2>(max_pieces);
-      at_part = c.take<float>(max_pieces * dim_max);
       at_rec = c.take<LongRecord>(max_long);
       at_rows = c.take<RowRec>(total_keys);
+      at_scaled = c.take<float>(mean_values);
       // [sort scratch | segment scratch | row plan counts | status] zeroed together
       at_zero = at_hist = c.take<char>(sort_scratch_bytes(total_keys, key_bits));
       at_segscr = c.take<char>(segment_scratch_bytes(total_keys));
@@ -684,6 +702,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
     }
     cudaStream_t stream = s.Use(stream_arg);
     s.Poll(stream);
+    s.Throttle(stream);
     char* slab = nullptr;
     Cuda(cudaMallocAsync(reinterpret_cast<void**>(&slab), std::max<size_t>(c.offset, 256), stream));
     auto P = [&](size_t at) { return slab + at; };
@@ -696,7 +715,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       Ticket t;
       t.read_only = read_only != 0;
       unsigned long long bag_base = 0, occ_base = 0, scale_base = 0, koff = 0,
-                         ooff = 0, loff = 0, hoff = 0;
+                         ooff = 0, loff = 0, hoff = 0, soff = 0;
       t.table_ids.resize(ranks.size());
       t.table_occ.assign(ranks.size(), 0);
       for (auto& [id, rank] : ranks) t.table_ids[rank] = id;
@@ -755,6 +774,9 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         t.ranks.push_back(L.table_rank);
         t.grad_rows.push_back(rows);
         t.scale_base.push_back(L.scale_base);
+        t.pooling.push_back(f.pooling);
+        t.scaled_off.push_back(soff);
+        if (f.pooling == 1) soff += rows * D;
         t.table_occ[L.table_rank] += f.key_count;
       }
       s.Stage(P(at_desc), desc.data(), count * sizeof(LookupFeature), stream);
@@ -832,9 +854,9 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         t.seg_total = reinterpret_cast<unsigned*>(P(at_segtot));
         t.pieces = reinterpret_cast<uint2*>(P(at_pieces));
         t.max_pieces = (unsigned)max_pieces;
-        t.part = reinterpret_cast<float*>(P(at_part));
         t.records = reinterpret_cast<LongRecord*>(P(at_rec));
         t.rows = reinterpret_cast<RowRec*>(P(at_rows));
+        t.scaled = reinterpret_cast<float*>(P(at_scaled));
         t.plan = reinterpret_cast<RowPlan*>(P(at_plan));
         t.status = status_block;
         t.control = &status_block->control;
@@ -1048,6 +1070,16 @@ int PushEntry(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gradien
     float* stage = nullptr;
     if (host_values)
       Cuda(cudaMallocAsync(reinterpret_cast<void**>(&stage), host_values * 4, stream));
+    // the piece sums live only for the push's kernels: one stream-ordered block
+    // per push, released right after them, so consecutive pushes reuse it
+    float* part = nullptr;
+    try {
+      Cuda(cudaMallocAsync(reinterpret_cast<void**>(&part),
+                           std::max<size_t>((size_t)t.max_pieces * t.dim_max * 4, 256), stream));
+    } catch (...) {
+      if (stage) cudaFreeAsync(stage, stream);
+      throw;
+    }
     try {
       std::vector<PushFeature> pf(nf);
       std::vector<unsigned long long> prefix(nf + 1, 0);
@@ -1061,7 +1093,9 @@ int PushEntry(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gradien
           dev = stage + hoff;
           hoff += n;
         }
-        pf[i] = PushFeature{dev, g.rows, t.scale_base[i], t.dims[i], t.ranks[i]};
+        const bool mean = t.pooling[i] == 1;
+        pf[i] = PushFeature{dev, mean ? t.scaled + t.scaled_off[i] : const_cast<float*>(dev), g.rows,
+                            t.scale_base[i], t.dims[i], t.ranks[i], mean ? 1u : 0u, 0u};
         prefix[i + 1] = prefix[i] + n;
       }
       std::vector<PushTable> pt(t.table_ids.size());
@@ -1129,7 +1163,7 @@ int PushEntry(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gradien
       pl.plan = t.plan;
       pl.pieces = t.pieces;
       pl.max_pieces = t.max_pieces;
-      pl.part = t.part;
+      pl.part = part;
       pl.records = t.records;
       pl.dim_max = t.dim_max;
       pl.control = t.control;
@@ -1139,6 +1173,14 @@ int PushEntry(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gradien
       pl.vec = vec;
       pl.group = group;
       pl.iters = iters;
+      {
+        // the async ring row path: one dimension in {32, 64, 128}, aligned gradients
+        const unsigned d0 = t.dims.empty() ? 0u : t.dims[0];
+        bool same = d0 == 32 || d0 == 64 || d0 == 128;
+        for (unsigned d : t.dims) same &= d == d0;
+        pl.ring_dim = (same && pl.grad_vec4 && t.dim_max == d0 && !(s.opt.flags & EPS_B200_FLAG_REGISTER_ROWS))
+                          ? (int)d0 : 0;
+      }
       cudaEvent_t ev = s.Begin(stream);
       Cuda(launch_push_prescan(pl, stream));
       s.End(EPS_B200_PHASE_PRESCAN, ev, stream, 1);
@@ -1147,9 +1189,10 @@ int PushEntry(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gradien
       s.End(EPS_B200_PHASE_APPLY, ev, stream, launch_push_apply_count(pl));
       ev = s.Begin(stream);
       Cuda(launch_push_finalize(pl, stream));
-      s.End(EPS_B200_PHASE_FINALIZE, ev, stream, 1);
+      s.End(EPS_B200_PHASE_FINALIZE, ev, stream, launch_push_finalize_count(pl));
       Cuda(cudaMemcpyAsync(&s.host_status[t.slot], t.status, sizeof(StatusBlock),
                            cudaMemcpyDeviceToHost, stream));
+      { float* owned = part; part = nullptr; Cuda(cudaFreeAsync(owned, stream)); }
       if (stage) { float* owned = stage; stage = nullptr; Cuda(cudaFreeAsync(owned, stream)); }
       t.done = s.SyncEvent();
       Cuda(cudaEventRecord(t.done, stream));
@@ -1158,6 +1201,7 @@ int PushEntry(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gradien
       s.Done(stream);
     } catch (...) {
       cudaStreamSynchronize(stream);
+      if (part) cudaFreeAsync(part, stream);
       if (stage) cudaFreeAsync(stage, stream);
       throw;
     }

@@ -76,6 +76,13 @@ typedef struct {
  * relative of the serial sum, but not bit-identical. */
 #define EPS_B200_FLAG_REFERENCE_ORDER 1u
 
+/* Update coalesced rows with the register-resident kernels only.  By default a
+ * push whose tables all have one dimension in {32, 64, 128} (16-byte aligned
+ * gradients) streams its rows through a shared-memory ring of asynchronous
+ * copies; other pushes always take the register path.  Both give identical
+ * results; the flag exists so that tests can run the second path on any shape. */
+#define EPS_B200_FLAG_REGISTER_ROWS 2u
+
 /* eps::TableDefinition + eps::OptimizerConfig (include/eps/types.hpp:76-97).
  * key_space: keys of this table lie in [0, key_space); the shard holds the slots
  * of keys k with k % shard_count == shard_id (src/store/shard_store.cpp:77),

@@ -26,9 +26,9 @@ def bits(a):
     return np.ascontiguousarray(a, np.float32).view(np.uint32)
 
 
-def make_store(eps, tables, reference_order=False, shard_count=1, shard_id=0):
+def make_store(eps, tables, reference_order=False, shard_count=1, shard_id=0, register_rows=False):
     s = eps.ParameterStore(device=0, reference_order=reference_order, shard_count=shard_count,
-                           shard_id=shard_id, state_bytes=8 << 30)
+                           shard_id=shard_id, state_bytes=8 << 30, register_rows=register_rows)
     for t in tables:
         s.create_table(eps.TableDefinition(
             id=t.id, dimension=t.dimension, key_space=t.rows, learning_rate=t.learning_rate,
@@ -62,11 +62,12 @@ def test_lookup_bit_exact_vs_reference(eps, name):
         assert np.array_equal(bits(got), bits(want)), name
 
 
+@pytest.mark.parametrize("register_rows", [False, True])
 @pytest.mark.parametrize("reference_order", [True, False])
 @pytest.mark.parametrize("name", golden_cases.CASES)
-def test_push_vs_reference(eps, name, reference_order):
+def test_push_vs_reference(eps, name, reference_order, register_rows):
     case = golden_cases.load(name)
-    s = make_store(eps, case.tables, reference_order=reference_order)
+    s = make_store(eps, case.tables, reference_order=reference_order, register_rows=register_rows)
     for step in range(case.steps):
         ticket, outs = s.lookup(inputs(eps, case.features))
         s.push(ticket, case.grads[step])
@@ -127,6 +128,38 @@ def test_long_rows_condition_aware(eps, workloads, reference_order):
         worst = max(worst, float((err / (a64[k] + 1e-30)).max()))
         assert (err <= bound).all(), (k, counts[k], err.max())
     print(f"long rows: {len(long_keys)}, max normalised error {worst:.3e}")
+
+
+@pytest.mark.parametrize("register_rows", [False, True])
+@pytest.mark.parametrize("reference_order", [False, True])
+def test_checked_mode_applies_large_finite_gradients(eps, workloads, reference_order, register_rows):
+    """Gradients too large for the single-pass overflow proof (3 * N * max|g| >
+    1e17) take the validate-then-apply path (stages A and B validate, stage C
+    applies); every finite update must still equal the oracle's: rows with at
+    most 64 occurrences bit-exact (every row in reference order), counters and
+    beta powers advanced once."""
+    w = workloads.hot(37, dim=64, rows=700, n=20000)
+    t = [TableDef(id=1, dimension=64, learning_rate=1e-3, rows=700)]
+    s = make_store(eps, t, reference_order=reference_order, register_rows=register_rows)
+    o = Oracle(t)
+    feats = [Feature(f.table, f.feature, f.pooling, f.keys, f.offsets) for f in w.features]
+    grads = [np.ascontiguousarray(g * F32(1e15), F32) for g in w.gradients]
+    assert 3 * sum(len(f.keys) for f in feats) * max(float(np.abs(g).max()) for g in grads) > 1e17
+    ticket, _ = s.lookup(inputs(eps, feats))
+    s.push(ticket, grads)
+    assert o.push(feats, grads) == 0
+    counts = occurrence_counts(feats, 1)
+    keys = np.array(sorted(k for k, c in counts.items() if reference_order or c <= 64), np.uint64)
+    assert len(keys) > 100
+    gw, gm, gv, gu = s.read_state(1, keys)
+    st, upd = o.state(1)
+    k = keys.astype(np.int64)
+    assert np.isfinite(gv).all() and float(gv.max()) > 1e20
+    for got, want in ((gw, st[k, 0]), (gm, st[k, 1]), (gv, st[k, 2])):
+        assert np.array_equal(bits(got), bits(want))
+    assert np.array_equal(gu, upd[k])
+    assert s.optimizer_state(1) == (1, F32(F32(0.9) * F32(0.9)), F32(F32(0.999) * F32(0.999)))
+    s.close()
 
 
 def test_shard_partials_merge_bit_exact(eps):
