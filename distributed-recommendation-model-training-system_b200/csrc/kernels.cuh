@@ -210,6 +210,7 @@ struct PlanLaunch {
   const unsigned int* seg_start;   // [U + 1]
   const unsigned int* seg_total;   // U (device)
   const LookupFeature* features;   // scale_base per feature
+  unsigned int feature_count;
   const float* row_scale;
   unsigned long long n;
   int key64;

@@ -32,11 +32,14 @@ namespace cg = cooperative_groups;
 namespace eps_b200 {
 namespace {
 
+// The gather is bound by each bag's chain of dependent loads (offsets, keys,
+// rows), so more bags in flight (4 blocks of 256 per SM) pays more than more
+// rows in flight per bag (4 per group): cfg2 109 -> 90 us.
 #ifndef EPS_LOOKUP_DEPTH_REGS
-#define EPS_LOOKUP_DEPTH_REGS 32     // registers per lane for rows in flight
+#define EPS_LOOKUP_DEPTH_REGS 16     // registers per lane for rows in flight
 #endif
 #ifndef EPS_LOOKUP_MIN_BLOCKS
-#define EPS_LOOKUP_MIN_BLOCKS 3
+#define EPS_LOOKUP_MIN_BLOCKS 4
 #endif
 
 template <int G, int VEC, int ITERS, typename KeyT>

@@ -829,6 +829,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         pp.seg_start = reinterpret_cast<const unsigned*>(P(at_seg));
         pp.seg_total = reinterpret_cast<const unsigned*>(P(at_segtot));
         pp.features = lp.features;
+        pp.feature_count = (unsigned)count;
         pp.row_scale = reinterpret_cast<const float*>(P(at_scale));
         pp.n = total_keys;
         pp.key64 = key64;

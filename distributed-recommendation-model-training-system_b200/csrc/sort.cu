@@ -141,6 +141,25 @@ __global__ void __launch_bounds__(kThreads) segment_heads(const KeyT* keys, unsi
 }
 
 template <typename KeyT>
+struct OnesweepSmem {
+  unsigned cnt[kWarps][256];     // warp-private digit counts, then warp offsets
+  unsigned dig_off[256];         // tile-local exclusive prefix of the digit counts
+  unsigned gbase[256];           // global position of tile position 0 of each digit
+  unsigned warp_sum[kWarps];
+  unsigned tile;
+  KeyT keys[kSortTile];          // the tile in tile-sorted order
+  unsigned vals[kSortTile];
+};
+
+// One digit pass: each CTA takes the next tile in launch order from an atomic
+// counter, ranks its items stably (per warp: __match_any_sync groups the lanes
+// with the same digit, a warp-private running count per digit orders the warp's
+// rounds), publishes its per-digit counts, scatters the tile into shared memory
+// in tile-sorted order while the exclusive prefix of the earlier tiles is
+// obtained by decoupled look-back over their published (flag, count) words, and
+// finally writes the tile out in tile-sorted order, so that consecutive threads
+// write consecutive positions of each digit's run.
+template <typename KeyT>
 __global__ void __launch_bounds__(kThreads) onesweep_pass(const KeyT* kin, const unsigned* vin,
                                                           KeyT* kout, unsigned* vout,
                                                           unsigned long long n, unsigned shift,
@@ -148,16 +167,16 @@ __global__ void __launch_bounds__(kThreads) onesweep_pass(const KeyT* kin, const
                                                           unsigned long long* status,
                                                           unsigned* tile_counter,
                                                           unsigned* error) {
-  __shared__ unsigned s_cnt[kWarps][256];
-  __shared__ unsigned s_base[256];       // global exclusive digit base + earlier tiles
-  __shared__ unsigned s_tile;
-  __shared__ unsigned s_warp_sum[kWarps];
+  extern __shared__ __align__(16) unsigned char os_raw[];
+  OnesweepSmem<KeyT>& S = *reinterpret_cast<OnesweepSmem<KeyT>*>(os_raw);
   const unsigned w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (unsigned i = threadIdx.x; i < kWarps * 256; i += kThreads) (&s_cnt[0][0])[i] = 0;
-  if (threadIdx.x == 0) s_tile = atomicAdd(tile_counter, 1u);
+  for (unsigned i = threadIdx.x; i < kWarps * 256; i += kThreads) (&S.cnt[0][0])[i] = 0;
+  if (threadIdx.x == 0) S.tile = atomicAdd(tile_counter, 1u);
   __syncthreads();
-  const unsigned tile = s_tile;
-  const unsigned long long base = (unsigned long long)tile * kSortTile + w * kWarpSpan;
+  const unsigned tile = S.tile;
+  const unsigned long long tbase = (unsigned long long)tile * kSortTile;
+  const unsigned tcount = (unsigned)min((unsigned long long)kSortTile, n - tbase);
+  const unsigned long long base = tbase + w * kWarpSpan;
   const unsigned lt = (1u << lane) - 1u;
   KeyT k[kItems];
   unsigned v[kItems], rank[kItems];
@@ -168,57 +187,61 @@ __global__ void __launch_bounds__(kThreads) onesweep_pass(const KeyT* kin, const
     k[r] = valid ? kin[idx] : KeyT(0);
     v[r] = valid ? vin[idx] : 0u;
   }
-  // stable rank of every item among the warp's items with the same digit
+  // stable rank of every item among the warp's earlier items with its digit
 #pragma unroll
   for (int r = 0; r < kItems; ++r) {
-    const unsigned long long idx = base + r * 32 + lane;
-    const bool valid = idx < n;
-    const unsigned d = valid ? ((unsigned)(k[r] >> shift) & 255u) : 256u;
-    // lanes with the same digit: intersect the 8 per-bit ballots
-    unsigned peers = __ballot_sync(0xffffffffu, valid);
-#pragma unroll
-    for (int bit = 0; bit < 8; ++bit) {
-      const unsigned on = __ballot_sync(0xffffffffu, (d >> bit) & 1u);
-      peers &= ((d >> bit) & 1u) ? on : ~on;
-    }
+    const bool valid = base + r * 32 + lane < n;
+    const unsigned d = valid ? ((unsigned)(k[r] >> shift) & 255u) : 256u + lane;
+    const unsigned peers = __match_any_sync(0xffffffffu, d);
     unsigned prior = 0;
-    if (valid) prior = s_cnt[w][d];
+    if (valid) prior = S.cnt[w][d];
     __syncwarp();
     if (valid) {
       rank[r] = prior + __popc(peers & lt);
-      if ((peers & lt) == 0) s_cnt[w][d] = prior + __popc(peers);
+      if ((peers & lt) == 0) S.cnt[w][d] = prior + __popc(peers);
     }
     __syncwarp();
   }
   __syncthreads();
-  // per-digit: exclusive prefix over warps, tile total, look-back over tiles
+  // per digit (thread d): warp offsets, tile total, published aggregate
   const unsigned d = threadIdx.x;          // kThreads == 256 digits
   unsigned total = 0;
 #pragma unroll
-  for (int x = 0; x < kWarps; ++x) { const unsigned c = s_cnt[x][d]; s_cnt[x][d] = total; total += c; }
+  for (int x = 0; x < kWarps; ++x) { const unsigned c = S.cnt[x][d]; S.cnt[x][d] = total; total += c; }
   unsigned long long* mine = status + (unsigned long long)tile * 256 + d;
-  if (tile == 0) {
-    __stcg(mine, kFlagPrefix | total);
-  } else {
-    __stcg(mine, kFlagAggregate | total);
-  }
-  // exclusive digit base over all digits (global histogram of this pass)
+  __stcg(mine, (tile == 0 ? kFlagPrefix : kFlagAggregate) | total);
+  // tile-local and global exclusive digit prefixes (block scans over 256 digits)
   const unsigned hcount = hist[d];
-  unsigned x = hcount;
+  unsigned xt = total, xh = hcount;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const unsigned y = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= (unsigned)o) x += y;
+    const unsigned yt = __shfl_up_sync(0xffffffffu, xt, o);
+    const unsigned yh = __shfl_up_sync(0xffffffffu, xh, o);
+    if (lane >= (unsigned)o) { xt += yt; xh += yh; }
   }
-  if (lane == 31) s_warp_sum[w] = x;
+  __shared__ unsigned s_wh[kWarps];
+  if (lane == 31) { S.warp_sum[w] = xt; s_wh[w] = xh; }
   __syncthreads();
-  unsigned before = 0;
-  for (unsigned q = 0; q < w; ++q) before += s_warp_sum[q];
-  unsigned digit_base = before + x - hcount;
+  unsigned bt = 0, bh = 0;
+  for (unsigned q = 0; q < w; ++q) { bt += S.warp_sum[q]; bh += s_wh[q]; }
+  const unsigned dig_off = bt + xt - total;
+  const unsigned digit_base = bh + xh - hcount;
+  S.dig_off[d] = dig_off;
+  __syncthreads();
+  // scatter the tile into shared memory in tile-sorted order
+#pragma unroll
+  for (int r = 0; r < kItems; ++r) {
+    if (base + r * 32 + lane < n) {
+      const unsigned dd = (unsigned)(k[r] >> shift) & 255u;
+      const unsigned pos = S.dig_off[dd] + S.cnt[w][dd] + rank[r];
+      S.keys[pos] = k[r];
+      S.vals[pos] = v[r];
+    }
+  }
+  // decoupled look-back over earlier tiles of this digit (8 predecessors per
+  // step loaded together; every wait bounded)
   unsigned prefix = 0;
   if (tile > 0) {
-    // decoupled look-back over earlier tiles of this digit, 8 predecessors per
-    // step loaded together
     constexpr int W = 8;
     long long t = (long long)tile - 1;
     unsigned spins = 0;
@@ -249,16 +272,16 @@ __global__ void __launch_bounds__(kThreads) onesweep_pass(const KeyT* kin, const
     if (failed) atomicOr(error, kLookupSortFailed);
     __stcg(mine, kFlagPrefix | (prefix + total));
   }
-  s_base[d] = digit_base + prefix;
+  S.gbase[d] = digit_base + prefix - dig_off;
   __syncthreads();
-#pragma unroll
-  for (int r = 0; r < kItems; ++r) {
-    const unsigned long long idx = base + r * 32 + lane;
-    if (idx < n) {
-      const unsigned dd = (unsigned)(k[r] >> shift) & 255u;
-      const unsigned long long pos = (unsigned long long)s_base[dd] + s_cnt[w][dd] + rank[r];
-      kout[pos] = k[r];
-      vout[pos] = v[r];
+  // write out in tile-sorted order: runs of one digit land on consecutive
+  // positions (the bound is a guard only: counts and ranks always agree)
+  for (unsigned i = threadIdx.x; i < tcount; i += kThreads) {
+    const KeyT kk = S.keys[i];
+    const unsigned pos = S.gbase[(unsigned)(kk >> shift) & 255u] + i;
+    if (pos < n) {
+      kout[pos] = kk;
+      vout[pos] = S.vals[i];
     }
   }
 }
@@ -280,8 +303,18 @@ cudaError_t run_sort(const SortLaunch& p, cudaStream_t s, int* swapped) {
   // the caller hands over zeroed scratch (sort_scratch_bytes)
   const unsigned long long hist_grid = min(148ull * 8, (p.n + kThreads - 1) / kThreads);
   digit_histograms<KeyT><<<(unsigned)hist_grid, kThreads, 0, s>>>(k0, p.n, passes, hist);
+  const size_t smem = sizeof(OnesweepSmem<KeyT>);
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (!attr_set[dev & 63]) {
+    e = cudaFuncSetAttribute(onesweep_pass<KeyT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attr_set[dev & 63] = true;
+  }
   for (unsigned pass = 0; pass < passes; ++pass) {
-    onesweep_pass<KeyT><<<p.tiles, kThreads, 0, s>>>(
+    onesweep_pass<KeyT><<<p.tiles, kThreads, smem, s>>>(
         k0, v0, k1, v1, p.n, pass * 8, hist + pass * 256,
         status + (unsigned long long)pass * p.tiles * 256, counters + pass, p.error);
     KeyT* tk = k0; k0 = k1; k1 = tk;
@@ -337,14 +370,21 @@ __global__ void __launch_bounds__(256) row_plan(PlanLaunch p) {
       const unsigned src = p.srcs[s0];
       key = (unsigned long long)K;
       r.key = key;
-      if ((unsigned)(K >> p.slot_bits) < p.table_count) {
+      // a source outside the lookup's features or rows can only come from an
+      // invalid lookup (whose push is rejected): such rows are skipped
+      const unsigned f = src >> kRowBits, gr = src & ((1u << kRowBits) - 1u);
+      bool src_ok = f < p.feature_count;
+      if (src_ok) {
+        const LookupFeature& F = p.features[f];
+        src_ok = gr < (F.pooling == 2 ? F.key_count : F.bag_count);
+      }
+      if ((unsigned)(K >> p.slot_bits) < p.table_count && src_ok) {
         if (len > p.long_run) {
           kind = 3;
         } else if (len == 1) {
           kind = 1;
-          const unsigned f = src >> kRowBits;
           r.a = src;
-          r.b = __float_as_uint(p.row_scale[p.features[f].scale_base + (src & ((1u << kRowBits) - 1u))]);
+          r.b = __float_as_uint(p.row_scale[p.features[f].scale_base + gr]);
         } else {
           kind = 2;
           r.b = kRowMulti | len;
