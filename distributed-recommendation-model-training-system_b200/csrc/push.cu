@@ -427,7 +427,10 @@ __device__ __forceinline__ void update_chunk(const Grp& grp, const PushLaunch& p
 // group order (deterministic; within 1e-6 * sum|terms| of the reference's
 // serial sum).  Called by every thread of the block; the result is valid in
 // group 0.  s_acc holds (blockDim.x / G) * dim_max floats.
-constexpr int kCombineDepth = 8;
+#ifndef EPS_COMBINE_DEPTH
+#define EPS_COMBINE_DEPTH 16          // piece sums in flight per group when combining a long row
+#endif
+constexpr int kCombineDepth = EPS_COMBINE_DEPTH;
 template <int G, int VEC, int ITERS, typename Grp>
 __device__ __forceinline__ void combine_long(const Grp& grp, const PushLaunch& p, const LongRecord& L,
                                              unsigned D, float* s_acc, float (&g)[VEC * ITERS]) {
@@ -634,6 +637,104 @@ __global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? EPS_PUSH_MIN_BLOCKS 
   bits = cg::reduce(grp, bits, cg::bit_or<unsigned>());
   if (gl == 0 && bits) atomicOr(&p.control->reject_bits, bits);
   if (apply) flush_absmax(grp, p, cur_tr, cur_max);
+}
+
+// ----------------------------------------------- pieces for the uniform shape
+// The piece sums of stage A for the common shape (every table has dimension D
+// in {32, 64, 128}): a group of G = D / 4 lanes reduces one piece at a time,
+// serially in occurrence order (reduce_staged's arithmetic), with the latency
+// of the index loads taken off the chain: pieces are claimed one at a time
+// (the descriptor of the next claim loaded a claim ahead; claiming several
+// contiguous long-row pieces at once left a tail: cfg2 68 -> 45 us), and the
+// first sources of the next piece are loaded while the current piece is summed.
+#ifndef EPS_PIECES_DEPTH
+#define EPS_PIECES_DEPTH 8            // gradient rows in flight per group
+#endif
+#ifndef EPS_PIECES_MIN_BLOCKS
+#define EPS_PIECES_MIN_BLOCKS 3
+#endif
+#ifndef EPS_PIECES_PER_CLAIM
+#define EPS_PIECES_PER_CLAIM 1        // long-row pieces are contiguous: claim them singly
+#endif
+constexpr unsigned kPiecesPerClaim = EPS_PIECES_PER_CLAIM;
+template <int D>
+__global__ void __launch_bounds__(256, EPS_PIECES_MIN_BLOCKS) push_pieces_uniform(PushLaunch p) {
+  constexpr int G = D / 4;
+  constexpr int DEPTH = EPS_PIECES_DEPTH;
+  __shared__ const float* s_grad[kMaxFeatures];
+  const unsigned mode = *(volatile const unsigned*)&p.control->mode;
+  if (mode == kModeRejected) return;
+  stage_features(p, s_grad);
+  const auto grp = cg::tiled_partition<G>(cg::this_thread_block());
+  const unsigned gl = grp.thread_rank();
+  const unsigned P = *(volatile const unsigned*)&p.plan->piece_count;
+  auto claim = [&]() -> unsigned {
+    unsigned c = 0;
+    if (gl == 0) c = atomicAdd(&p.control->work_a, kPiecesPerClaim);
+    return grp.shfl(c, 0);
+  };
+  auto descs = [&](unsigned b) -> uint2 {
+    return (gl < kPiecesPerClaim && b + gl < P) ? p.pieces[b + gl] : make_uint2(0u, 0u);
+  };
+  auto first_src = [&](uint2 pc) -> unsigned { return gl < pc.y ? __ldg(p.srcs + pc.x + gl) : 0u; };
+  unsigned base = claim();
+  uint2 pcs = descs(base);
+  unsigned nbase = claim();
+  uint2 npcs = descs(nbase);
+  unsigned src = first_src(make_uint2(grp.shfl(pcs.x, 0), grp.shfl(pcs.y, 0)));
+  while (base < P) {
+#pragma unroll 1
+    for (unsigned k = 0; k < kPiecesPerClaim && base + k < P; ++k) {
+      const uint2 pc = make_uint2(grp.shfl(pcs.x, k), grp.shfl(pcs.y, k));
+      // the next piece's first sources, in flight during this piece
+      const bool last_here = k + 1 == kPiecesPerClaim || base + k + 1 >= P;
+      const uint2 pn = last_here ? make_uint2(grp.shfl(npcs.x, 0), grp.shfl(npcs.y, 0))
+                                 : make_uint2(grp.shfl(pcs.x, k + 1), grp.shfl(pcs.y, k + 1));
+      const bool has_next = last_here ? nbase < P : true;
+      const unsigned nsrc = has_next ? first_src(pn) : 0u;
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      for (unsigned c0 = 0; c0 < pc.y; c0 += G) {
+        const float* rowp = s_grad[src >> kRowBits] + (unsigned long long)(src & ((1u << kRowBits) - 1u)) * D;
+        if (c0 + G + gl < pc.y) src = __ldg(p.srcs + pc.x + c0 + G + gl);
+        const int cnt = (int)min((unsigned)G, pc.y - c0);
+#pragma unroll 1
+        for (int j0 = 0; j0 < cnt; j0 += DEPTH) {
+          float x[DEPTH][4];
+#pragma unroll
+          for (int u = 0; u < DEPTH; ++u) {
+            const float* q = grp.shfl(rowp, (j0 + u) & (G - 1));
+            if (j0 + u < cnt) {
+              const float4 t = *reinterpret_cast<const float4*>(q + 4 * gl);
+              x[u][0] = t.x; x[u][1] = t.y; x[u][2] = t.z; x[u][3] = t.w;
+            } else {
+              x[u][0] = x[u][1] = x[u][2] = x[u][3] = -0.0f;
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < DEPTH; ++u)
+#pragma unroll
+            for (int v = 0; v < 4; ++v) acc[v] = __fadd_rn(acc[v], x[u][v]);
+        }
+      }
+      *reinterpret_cast<float4*>(p.part + (unsigned long long)(base + k) * D + 4 * gl) =
+          make_float4(acc[0], acc[1], acc[2], acc[3]);
+      src = nsrc;
+    }
+    base = nbase;
+    pcs = npcs;
+    if (base < P) {
+      nbase = claim();
+      npcs = descs(nbase);
+    }
+  }
+}
+
+template <int D>
+cudaError_t run_pieces_uniform(const PushLaunch& p, cudaStream_t s) {
+  const unsigned long long want = (p.n / 2 + 255) / 256;
+  const unsigned grid = (unsigned)max(1ull, min(want, 148ull * EPS_PIECES_MIN_BLOCKS));
+  push_pieces_uniform<D><<<grid, 256, 0, s>>>(p);
+  return cudaGetLastError();
 }
 
 // --------------------------------------------------- rows through an async ring
@@ -1034,15 +1135,22 @@ cudaError_t run_apply(const PushLaunch& p, cudaStream_t s) {
   const unsigned long long want = (p.n + 255) / 256;
   const unsigned grid = (unsigned)max(1ull, min(want, 148ull * blocks));
   const size_t smem = (size_t)(256 / G) * p.dim_max * sizeof(float);
-  push_stage_a<G, VEC, ITERS, KeyT><<<grid, 256, 0, s>>>(p);
   if (p.ring_dim) {
     cudaError_t e = cudaSuccess;
+    switch (p.ring_dim) {
+      case 32: e = run_pieces_uniform<32>(p, s); break;
+      case 64: e = run_pieces_uniform<64>(p, s); break;
+      default: e = run_pieces_uniform<128>(p, s); break;
+    }
+    if (e != cudaSuccess) return e;
     switch (p.ring_dim) {
       case 32: e = run_ring<32, KeyT>(p, s); break;
       case 64: e = run_ring<64, KeyT>(p, s); break;
       default: e = run_ring<128, KeyT>(p, s); break;
     }
     if (e != cudaSuccess) return e;
+  } else {
+    push_stage_a<G, VEC, ITERS, KeyT><<<grid, 256, 0, s>>>(p);
   }
   push_stage_b<G, VEC, ITERS, KeyT><<<grid, 256, smem, s>>>(p);
   push_stage_c<G, VEC, ITERS, KeyT><<<min(grid, 148u), 256, smem, s>>>(p);
