@@ -118,7 +118,7 @@ class Stats(C.Structure):
                                           "rows", "tables", "kernel_launches")]
 
 
-PHASES = ("lookup", "sort", "prescan", "apply", "finalize")
+PHASES = ("lookup", "sort", "prescan", "apply", "finalize", "emit", "pieces", "long")
 
 
 _lib = None
@@ -209,7 +209,7 @@ def load_library() -> C.CDLL:
     for name in ENTRY_POINTS[1:]:
         if name not in ("eps_b200_destroy", "eps_b200_comm_destroy", "eps_b200_client_destroy"):
             getattr(lib, name).restype = C.c_int
-    if lib.eps_b200_abi_version() != 1:
+    if lib.eps_b200_abi_version() != 2:
         raise ImportError("libeps_b200.so ABI version mismatch")
     _lib = lib
     return lib

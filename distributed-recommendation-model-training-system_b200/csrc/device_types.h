@@ -64,20 +64,13 @@ struct LookupFeature {
 };
 constexpr unsigned int kPadSlot = 0xFFFFFFFEu;   // slot marker of a padding key
 
-// Gradient source of one feature for a Push.  The coalescing kernels read
-// `scaled`: for a mean feature the prescan writes there every gradient value
-// times its row scale 1.0f/len (the product the reference forms per occurrence,
-// src/access/batch_access.cpp:118), so the reductions add without a scale load;
-// for sum and sequence features (scale 1) it is `grad` itself.
+// Gradient source of one feature for a Push.
 struct PushFeature {
   const float* grad;                   // [rows][dim]
-  float* scaled;                       // [rows][dim]: grad * row scale (mean), or grad
   unsigned long long rows;
   unsigned long long scale_base;
   unsigned int dim;
   unsigned int table_rank;
-  unsigned int mean;                   // 1: pooling mean (scaled is written by the prescan)
-  unsigned int pad;
 };
 
 enum PushMode : unsigned int { kModeSafe = 0, kModeChecked = 1, kModeRejected = 2 };

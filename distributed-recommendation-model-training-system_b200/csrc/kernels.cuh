@@ -308,8 +308,10 @@ struct PushLaunch {
 // beta powers / sequence iff accepted; stage C: the apply pass of a CHECKED
 // push); finalize launches a kernel only for a push without occurrences.
 cudaError_t launch_push_prescan(const PushLaunch& p, cudaStream_t stream);
-cudaError_t launch_push_apply(const PushLaunch& p, cudaStream_t stream);
-unsigned launch_push_apply_count(const PushLaunch& p);
+// part 0: piece sums (uniform shape only), 1: row updates, 2: long rows and
+// the checked apply
+cudaError_t launch_push_apply(const PushLaunch& p, cudaStream_t stream, int part);
+unsigned launch_push_apply_count(const PushLaunch& p, int part);
 unsigned launch_push_finalize_count(const PushLaunch& p);
 cudaError_t launch_push_finalize(const PushLaunch& p, cudaStream_t stream);
 

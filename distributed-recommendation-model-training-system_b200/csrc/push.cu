@@ -75,11 +75,6 @@ __global__ void __launch_bounds__(256) push_prescan(PushLaunch p, PushTable* tab
   const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
   unsigned bad = 0;
   float mx = 0.0f;
-  // mean features: scaled[e] = grad[e] * row_scale[row of e] (rows < 2^22,
-  // dim <= 512: element indices fit 32 bits)
-  const float* scale = p.row_scale + F.scale_base;
-  float* const out = F.mean ? F.scaled : nullptr;
-  const unsigned D = F.dim;
   if (p.grad_vec4) {
     const float4* g4 = reinterpret_cast<const float4*>(F.grad);
     const unsigned long long n4 = nvals / 4;
@@ -88,25 +83,12 @@ __global__ void __launch_bounds__(256) push_prescan(PushLaunch p, PushTable* tab
       const float4 x = __ldg(g4 + i);
       bad |= !isfinite(x.x) | !isfinite(x.y) | !isfinite(x.z) | !isfinite(x.w);
       mx = fmaxf(mx, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
-      if (out) {
-        const unsigned e = (unsigned)i * 4u;
-        float4 y;
-        if (D % 4u == 0) {
-          const float sc = __ldg(scale + e / D);
-          y = make_float4(__fmul_rn(x.x, sc), __fmul_rn(x.y, sc), __fmul_rn(x.z, sc), __fmul_rn(x.w, sc));
-        } else {
-          y = make_float4(__fmul_rn(x.x, __ldg(scale + e / D)), __fmul_rn(x.y, __ldg(scale + (e + 1) / D)),
-                          __fmul_rn(x.z, __ldg(scale + (e + 2) / D)), __fmul_rn(x.w, __ldg(scale + (e + 3) / D)));
-        }
-        reinterpret_cast<float4*>(out)[i] = y;
-      }
     }
   } else {
     for (unsigned long long i = blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x; i < nvals; i += stride) {
       const float x = __ldg(F.grad + i);
       bad |= !isfinite(x);
       mx = fmaxf(mx, fabsf(x));
-      if (out) out[i] = __fmul_rn(x, __ldg(scale + (unsigned)i / D));
     }
   }
   bad = __reduce_or_sync(0xffffffffu, bad);
@@ -157,14 +139,15 @@ __global__ void __launch_bounds__(256) push_prescan(PushLaunch p, PushTable* tab
 // Sum of the gradient references [s0, s1) of one coalesced row (all with the
 // same key), serially in occurrence order, by the G lanes of `grp` (each lane
 // owns VEC*ITERS columns), bit-exact with the reference's serial loop
-// g = 0; g += src * scale (src/access/batch_access.cpp:118): the products are
-// the pre-scaled rows (PushFeature::scaled), whose pointers are staged in
-// shared memory.  The next chunk's sources are requested before the current
-// chunk's rows; up to DEPTH_REGS / C gradient rows are in flight; rows past the
-// end add -0.0f (the identity).
+// g = 0; g += src * scale (src/access/batch_access.cpp:118).  The gradient
+// pointers and row-scale bases of the features are staged in shared memory;
+// each lane loads its occurrence's row scale together with the rows, the next
+// chunk's sources are requested before the current chunk's rows, up to
+// DEPTH_REGS / C gradient rows are in flight, and rows past the end add -0.0f
+// (the identity).
 template <int G, int VEC, int ITERS, int DEPTH_REGS, typename Grp>
 __device__ __forceinline__ void reduce_staged(const Grp& grp, const PushLaunch& p,
-                                              const float* const* s_grad,
+                                              const float* const* s_grad, const unsigned* s_sbase,
                                               unsigned long long s0, unsigned long long s1,
                                               unsigned D, float (&acc)[VEC * ITERS]) {
   constexpr int C = VEC * ITERS;
@@ -175,15 +158,19 @@ __device__ __forceinline__ void reduce_staged(const Grp& grp, const PushLaunch& 
   unsigned src = (s0 + gl < s1) ? __ldg(p.srcs + s0 + gl) : 0u;
   for (unsigned long long c0 = s0; c0 < s1; c0 += G) {
     const unsigned long long i = c0 + gl;
-    const float* rowp = s_grad[src >> kRowBits] + (unsigned long long)(src & ((1u << kRowBits) - 1u)) * D;
+    const unsigned f = src >> kRowBits, r = src & ((1u << kRowBits) - 1u);
+    const float* rowp = s_grad[f] + (unsigned long long)r * D;
+    const float sc = i < s1 ? __ldg(p.row_scale + s_sbase[f] + r) : 0.0f;
     if (i + G < s1) src = __ldg(p.srcs + i + G);
     const int cnt = (int)min((unsigned long long)G, s1 - c0);
 #pragma unroll 1
     for (int j0 = 0; j0 < cnt; j0 += DEPTH) {
       float x[DEPTH][C];
+      float sv[DEPTH];
 #pragma unroll
       for (int u = 0; u < DEPTH; ++u) {
         const float* q = grp.shfl(rowp, (j0 + u) & (G - 1));
+        sv[u] = grp.shfl(sc, (j0 + u) & (G - 1));
         const bool use = j0 + u < cnt;
 #pragma unroll
         for (int it = 0; it < ITERS; ++it) {
@@ -198,17 +185,23 @@ __device__ __forceinline__ void reduce_staged(const Grp& grp, const PushLaunch& 
           for (int v = 0; v < VEC; ++v) x[u][it * VEC + v] = t[v];
         }
       }
+      // batch_access.cpp:118: dest += src * scale, in occurrence order; the
+      // padding rows add (-0) * scale = -0 (scale > 0), the identity
 #pragma unroll
       for (int u = 0; u < DEPTH; ++u)
 #pragma unroll
-        for (int k = 0; k < C; ++k) acc[k] = __fadd_rn(acc[k], x[u][k]);
+        for (int k = 0; k < C; ++k) acc[k] = __fadd_rn(acc[k], __fmul_rn(x[u][k], sv[u]));
     }
   }
 }
 
-// Stages every feature's pre-scaled gradient pointer in shared memory.
-__device__ __forceinline__ void stage_features(const PushLaunch& p, const float** s_grad) {
-  for (unsigned f = threadIdx.x; f < p.feature_count; f += blockDim.x) s_grad[f] = p.features[f].scaled;
+// Stages every feature's gradient pointer and row-scale base in shared memory.
+__device__ __forceinline__ void stage_features(const PushLaunch& p, const float** s_grad,
+                                               unsigned* s_sbase) {
+  for (unsigned f = threadIdx.x; f < p.feature_count; f += blockDim.x) {
+    s_grad[f] = p.features[f].grad;
+    s_sbase[f] = (unsigned)p.features[f].scale_base;
+  }
   __syncthreads();
 }
 
@@ -291,7 +284,7 @@ __device__ __forceinline__ KeyT slot_mask_of(unsigned slot_bits) {
 // run of the sorted keys), updated by a group of G lanes in two steps so that a
 // group keeps two rows' loads in flight: `load` issues the gradient-row, [w|m|v]
 // and counter loads; `finish` applies LazyAdam and stores.  The gradient is one
-// row away: the single occurrence's pre-scaled gradient row, 0 + src * scale
+// row away: the single occurrence's gradient row times its scale, 0 + src * scale
 // (batch_access.cpp:118), or, for a row with 2..long_run occurrences, its piece
 // sum reduced in occurrence order in stage A.  The row state is read and
 // written with streaming hints (touched once per push).
@@ -302,6 +295,7 @@ struct RowRegs {
   unsigned long long slot, upd;
   unsigned tr;
   bool multi;
+  float scale;
   float t[C], w[C], m[C], v[C];
 };
 
@@ -316,6 +310,7 @@ __device__ __forceinline__ void load_row(unsigned gl, const PushLaunch& p, const
   r.slot = (unsigned long long)(K & slot_mask_of<KeyT>(p.slot_bits));
   r.row = r.T->state + r.slot * 3ull * D;
   r.multi = (b & kRowMulti) != 0;
+  r.scale = r.multi ? 1.0f : __uint_as_float(b);
   const float* q = r.multi ? p.part + (unsigned long long)a * p.dim_max
                            : s_grad[a >> kRowBits] + (unsigned long long)(a & ((1u << kRowBits) - 1u)) * D;
 #pragma unroll
@@ -351,8 +346,9 @@ __device__ __forceinline__ void finish_row(const Grp& grp, const PushLaunch& p, 
 #pragma unroll
     for (int k = 0; k < C; ++k) g[k] = r.t[k];
   } else {
+    // 0 + src * scale (batch_access.cpp:118)
 #pragma unroll
-    for (int k = 0; k < C; ++k) g[k] = __fadd_rn(0.0f, r.t[k]);
+    for (int k = 0; k < C; ++k) g[k] = __fadd_rn(0.0f, __fmul_rn(r.t[k], r.scale));
   }
   if ((int)r.tr != cur_tr) {
     if (apply) flush_absmax(grp, p, cur_tr, cur_max);
@@ -582,10 +578,11 @@ constexpr unsigned kChunkPieces = 1;
 template <int G, int VEC, int ITERS, typename KeyT>
 __global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? EPS_PUSH_MIN_BLOCKS : 2) push_stage_a(PushLaunch p) {
   __shared__ const float* s_grad[kMaxFeatures];
+  __shared__ unsigned s_sbase[kMaxFeatures];
   const unsigned mode = *(volatile const unsigned*)&p.control->mode;
   if (mode == kModeRejected) return;
   const bool apply = mode == kModeSafe, validate = mode == kModeChecked;
-  stage_features(p, s_grad);
+  stage_features(p, s_grad, s_sbase);
   constexpr int C = VEC * ITERS;
   constexpr unsigned GPW = 32 / G;
   const auto grp = cg::tiled_partition<G>(cg::this_thread_block());
@@ -616,7 +613,7 @@ __global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? EPS_PUSH_MIN_BLOCKS 
         const KeyT K = key_at<KeyT>(p.keys, pc.x);
         const unsigned D = p.tables[(unsigned)(K >> p.slot_bits)].dim;
         float acc[C];
-        reduce_staged<G, VEC, ITERS, EPS_PIECE_DEPTH_REGS>(grp, p, s_grad, pc.x,
+        reduce_staged<G, VEC, ITERS, EPS_PIECE_DEPTH_REGS>(grp, p, s_grad, s_sbase, pc.x,
                                                            (unsigned long long)pc.x + pc.y, D, acc);
 #pragma unroll
         for (int it = 0; it < ITERS; ++it) {
@@ -662,9 +659,12 @@ __global__ void __launch_bounds__(256, EPS_PIECES_MIN_BLOCKS) push_pieces_unifor
   constexpr int G = D / 4;
   constexpr int DEPTH = EPS_PIECES_DEPTH;
   __shared__ const float* s_grad[kMaxFeatures];
-  const unsigned mode = *(volatile const unsigned*)&p.control->mode;
-  if (mode == kModeRejected) return;
-  stage_features(p, s_grad);
+  __shared__ unsigned s_sbase[kMaxFeatures];
+  // runs concurrently with the prescan (it writes no state, so the push's
+  // accept/reject decision is not needed); an invalid lookup's plan may hold
+  // sources its occurrence list never wrote, so nothing is summed then
+  if (*(volatile const unsigned*)p.lookup_error) return;
+  stage_features(p, s_grad, s_sbase);
   const auto grp = cg::tiled_partition<G>(cg::this_thread_block());
   const unsigned gl = grp.thread_rank();
   const unsigned P = *(volatile const unsigned*)&p.plan->piece_count;
@@ -694,15 +694,19 @@ __global__ void __launch_bounds__(256, EPS_PIECES_MIN_BLOCKS) push_pieces_unifor
       const unsigned nsrc = has_next ? first_src(pn) : 0u;
       float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
       for (unsigned c0 = 0; c0 < pc.y; c0 += G) {
-        const float* rowp = s_grad[src >> kRowBits] + (unsigned long long)(src & ((1u << kRowBits) - 1u)) * D;
+        const unsigned f = src >> kRowBits, r = src & ((1u << kRowBits) - 1u);
+        const float* rowp = s_grad[f] + (unsigned long long)r * D;
+        const float sc = c0 + gl < pc.y ? __ldg(p.row_scale + s_sbase[f] + r) : 0.0f;
         if (c0 + G + gl < pc.y) src = __ldg(p.srcs + pc.x + c0 + G + gl);
         const int cnt = (int)min((unsigned)G, pc.y - c0);
 #pragma unroll 1
         for (int j0 = 0; j0 < cnt; j0 += DEPTH) {
           float x[DEPTH][4];
+          float sv[DEPTH];
 #pragma unroll
           for (int u = 0; u < DEPTH; ++u) {
             const float* q = grp.shfl(rowp, (j0 + u) & (G - 1));
+            sv[u] = grp.shfl(sc, (j0 + u) & (G - 1));
             if (j0 + u < cnt) {
               const float4 t = *reinterpret_cast<const float4*>(q + 4 * gl);
               x[u][0] = t.x; x[u][1] = t.y; x[u][2] = t.z; x[u][3] = t.w;
@@ -710,10 +714,11 @@ __global__ void __launch_bounds__(256, EPS_PIECES_MIN_BLOCKS) push_pieces_unifor
               x[u][0] = x[u][1] = x[u][2] = x[u][3] = -0.0f;
             }
           }
+          // dest += src * scale in occurrence order (batch_access.cpp:118)
 #pragma unroll
           for (int u = 0; u < DEPTH; ++u)
 #pragma unroll
-            for (int v = 0; v < 4; ++v) acc[v] = __fadd_rn(acc[v], x[u][v]);
+            for (int v = 0; v < 4; ++v) acc[v] = __fadd_rn(acc[v], __fmul_rn(x[u][v], sv[u]));
         }
       }
       *reinterpret_cast<float4*>(p.part + (unsigned long long)(base + k) * D + 4 * gl) =
@@ -744,7 +749,7 @@ cudaError_t run_pieces_uniform(const PushLaunch& p, cudaStream_t s) {
 // w, m, v and g per lane), and keeps the rows of the next kRingSlots / (32 / G)
 // - 1 steps in flight through a ring of shared-memory slots filled by cp.async
 // (16-byte per-lane asynchronous copies, one commit group per step): the
-// [w|m|v] row, the row's gradient (the single occurrence's pre-scaled row or,
+// [w|m|v] row, the row's gradient (the single occurrence's gradient row or,
 // for 2..long_run occurrences, its in-order piece sum) and the 16-byte block
 // holding its counter.  Rows in flight hold no registers, so an SM keeps
 // warps x kRingSlots rows in flight.  Rows come from chunks of 32 plan records
@@ -879,7 +884,7 @@ __device__ __forceinline__ void ring_rows(const PushLaunch& p, const PushTable* 
       const float* st = p_state + sl * (3ull * D);
       const unsigned f = a >> kRowBits;
       const float* gr = (b & kRowMulti) ? p.part + (unsigned long long)a * D
-                                        : (feats_shared ? s_feat[f] : p.features[f].scaled) +
+                                        : (feats_shared ? s_feat[f] : p.features[f].grad) +
                                               (unsigned long long)(a & ((1u << kRowBits) - 1u)) * D;
       // [w|m|v]: 3G 16-byte pieces, three per lane; gradient: one per lane
 #pragma unroll
@@ -887,7 +892,12 @@ __device__ __forceinline__ void ring_rows(const PushLaunch& p, const PushTable* 
       cp_async16(slot + 3 * D + 4 * gl, gr + 4 * gl);
       if (gl == 0) cp_async16(slot + 4 * D, p_upd + (sl & ~1ull));
     }
-    if (gl == 0) *reinterpret_cast<unsigned long long*>(slot + 4 * D + 4) = has ? key : kEmptySlot;
+    if (gl == 0) {
+      *reinterpret_cast<unsigned long long*>(slot + 4 * D + 4) = has ? key : kEmptySlot;
+      // a single row's gradient is its occurrence's row times the row scale;
+      // a piece sum is used as summed (times 1, exact)
+      slot[4 * D + 6] = (b & kRowMulti) ? 1.0f : __uint_as_float(b);
+    }
     cp_async_commit_group();
     return __any_sync(0xffffffffu, has);
   };
@@ -926,9 +936,10 @@ __device__ __forceinline__ void ring_rows(const PushLaunch& p, const PushTable* 
         load_vec<4>(s + 2 * D + 4 * gl, v);
         load_vec<4>(s + 3 * D + 4 * gl, g);
         // 0 + src * scale for a single row (batch_access.cpp:118); a piece sum
-        // starts from +0 and is never -0, so 0 + sum leaves it unchanged
+        // (scale 1) starts from +0 and is never -0, so 0 + sum * 1 leaves it unchanged
+        const float scale = s[4 * D + 6];
 #pragma unroll
-        for (int x = 0; x < 4; ++x) g[x] = __fadd_rn(0.0f, g[x]);
+        for (int x = 0; x < 4; ++x) g[x] = __fadd_rn(0.0f, __fmul_rn(g[x], scale));
         bits |= adam_elems<4, APPLY, VALIDATE>(P, g, w, m, v, cur_max);
         if (APPLY) {
           float* row = P.state + sl * (3ull * D) + 4 * gl;
@@ -962,7 +973,7 @@ __global__ void __launch_bounds__(RingShape<D>::kWarps * 32) push_rows_ring(Push
   const unsigned mode = *(volatile const unsigned*)&p.control->mode;
   if (mode == kModeRejected) return;
   for (unsigned i = threadIdx.x; i < min(p.table_count, kTabs); i += blockDim.x) s_tab[i] = p.tables[i];
-  for (unsigned i = threadIdx.x; i < min(p.feature_count, kFeats); i += blockDim.x) s_feat[i] = p.features[i].scaled;
+  for (unsigned i = threadIdx.x; i < min(p.feature_count, kFeats); i += blockDim.x) s_feat[i] = p.features[i].grad;
   __syncthreads();
   const bool tabs_shared = p.table_count <= kTabs, feats_shared = p.feature_count <= kFeats;
   if (mode == kModeSafe) ring_rows<D, KeyT, true, false>(p, s_tab, tabs_shared, s_feat, feats_shared);
@@ -976,6 +987,7 @@ __global__ void __launch_bounds__(RingShape<D>::kWarps * 32) push_rows_ring(Push
 template <int G, int VEC, int ITERS, typename KeyT>
 __global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? EPS_PUSH_MIN_BLOCKS : 2) push_stage_b(PushLaunch p) {
   __shared__ const float* s_grad[kMaxFeatures];
+  __shared__ unsigned s_sbase[kMaxFeatures];
   extern __shared__ float s_acc[];
   const unsigned mode = *(volatile const unsigned*)&p.control->mode;
   const auto grp = cg::tiled_partition<G>(cg::this_thread_block());
@@ -984,7 +996,7 @@ __global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? EPS_PUSH_MIN_BLOCKS 
     return;
   }
   const bool apply = mode == kModeSafe, validate = mode == kModeChecked;
-  stage_features(p, s_grad);
+  stage_features(p, s_grad, s_sbase);
   unsigned bits = 0;
   int cur_tr = -1;
   unsigned cur_max = 0;
@@ -1012,6 +1024,7 @@ __global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? EPS_PUSH_MIN_BLOCKS 
 template <int G, int VEC, int ITERS, typename KeyT>
 __global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? EPS_PUSH_MIN_BLOCKS : 2) push_stage_c(PushLaunch p) {
   __shared__ const float* s_grad[kMaxFeatures];
+  __shared__ unsigned s_sbase[kMaxFeatures];
   extern __shared__ float s_acc[];
   const unsigned mode = *(volatile const unsigned*)&p.control->mode;
   if (mode != kModeChecked) return;
@@ -1021,7 +1034,7 @@ __global__ void __launch_bounds__(256, (VEC * ITERS <= 4) ? EPS_PUSH_MIN_BLOCKS 
   int cur_tr = -1;
   unsigned cur_max = 0;
   if (apply) {
-    stage_features(p, s_grad);
+    stage_features(p, s_grad, s_sbase);
     update_long_rows<G, VEC, ITERS, KeyT>(grp, p, s_acc, nullptr, true, false, bits, cur_tr, cur_max);
     const unsigned U = *(volatile const unsigned*)p.seg_total;
     const unsigned long long warp = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) >> 5;
@@ -1129,28 +1142,30 @@ cudaError_t run_ring(const PushLaunch& p, cudaStream_t s) {
 }
 
 template <int G, int VEC, int ITERS, typename KeyT>
-cudaError_t run_apply(const PushLaunch& p, cudaStream_t s) {
+cudaError_t run_apply(const PushLaunch& p, cudaStream_t s, int part) {
   if (!p.n) return cudaSuccess;
   constexpr unsigned blocks = (VEC * ITERS <= 4) ? EPS_PUSH_MIN_BLOCKS : 2;
   const unsigned long long want = (p.n + 255) / 256;
   const unsigned grid = (unsigned)max(1ull, min(want, 148ull * blocks));
   const size_t smem = (size_t)(256 / G) * p.dim_max * sizeof(float);
-  if (p.ring_dim) {
-    cudaError_t e = cudaSuccess;
+  if (part == 0) {
+    if (!p.ring_dim) return cudaSuccess;            // stage A sums the pieces itself
     switch (p.ring_dim) {
-      case 32: e = run_pieces_uniform<32>(p, s); break;
-      case 64: e = run_pieces_uniform<64>(p, s); break;
-      default: e = run_pieces_uniform<128>(p, s); break;
+      case 32: return run_pieces_uniform<32>(p, s);
+      case 64: return run_pieces_uniform<64>(p, s);
+      default: return run_pieces_uniform<128>(p, s);
     }
-    if (e != cudaSuccess) return e;
+  }
+  if (part == 1) {
+    if (!p.ring_dim) {
+      push_stage_a<G, VEC, ITERS, KeyT><<<grid, 256, 0, s>>>(p);
+      return cudaGetLastError();
+    }
     switch (p.ring_dim) {
-      case 32: e = run_ring<32, KeyT>(p, s); break;
-      case 64: e = run_ring<64, KeyT>(p, s); break;
-      default: e = run_ring<128, KeyT>(p, s); break;
+      case 32: return run_ring<32, KeyT>(p, s);
+      case 64: return run_ring<64, KeyT>(p, s);
+      default: return run_ring<128, KeyT>(p, s);
     }
-    if (e != cudaSuccess) return e;
-  } else {
-    push_stage_a<G, VEC, ITERS, KeyT><<<grid, 256, 0, s>>>(p);
   }
   push_stage_b<G, VEC, ITERS, KeyT><<<grid, 256, smem, s>>>(p);
   push_stage_c<G, VEC, ITERS, KeyT><<<min(grid, 148u), 256, smem, s>>>(p);
@@ -1158,9 +1173,9 @@ cudaError_t run_apply(const PushLaunch& p, cudaStream_t s) {
 }
 
 template <int G, int VEC, int ITERS>
-cudaError_t run_key(const PushLaunch& p, cudaStream_t s) {
-  return p.key64 ? run_apply<G, VEC, ITERS, unsigned long long>(p, s)
-                 : run_apply<G, VEC, ITERS, unsigned int>(p, s);
+cudaError_t run_key(const PushLaunch& p, cudaStream_t s, int part) {
+  return p.key64 ? run_apply<G, VEC, ITERS, unsigned long long>(p, s, part)
+                 : run_apply<G, VEC, ITERS, unsigned int>(p, s, part);
 }
 }  // namespace
 
@@ -1174,23 +1189,27 @@ cudaError_t launch_push_prescan(const PushLaunch& p, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
-unsigned launch_push_apply_count(const PushLaunch& p) { return p.n ? (p.ring_dim ? 4u : 3u) : 0u; }
+unsigned launch_push_apply_count(const PushLaunch& p, int part) {
+  if (!p.n) return 0u;
+  if (part == 0) return p.ring_dim ? 1u : 0u;
+  return part == 1 ? 1u : 2u;
+}
 unsigned launch_push_finalize_count(const PushLaunch& p) { return p.n ? 0u : 1u; }
 
-cudaError_t launch_push_apply(const PushLaunch& p, cudaStream_t stream) {
+cudaError_t launch_push_apply(const PushLaunch& p, cudaStream_t stream, int part) {
   if (p.vec == 4) {
     switch (p.group) {
-      case 8: return run_key<8, 4, 1>(p, stream);
-      case 16: return run_key<16, 4, 1>(p, stream);
+      case 8: return run_key<8, 4, 1>(p, stream, part);
+      case 16: return run_key<16, 4, 1>(p, stream, part);
       default:
-        if (p.iters == 1) return run_key<32, 4, 1>(p, stream);
-        if (p.iters == 2) return run_key<32, 4, 2>(p, stream);
-        return run_key<32, 4, 4>(p, stream);
+        if (p.iters == 1) return run_key<32, 4, 1>(p, stream, part);
+        if (p.iters == 2) return run_key<32, 4, 2>(p, stream, part);
+        return run_key<32, 4, 4>(p, stream, part);
     }
   }
-  if (p.iters == 1) return run_key<32, 1, 1>(p, stream);
-  if (p.iters == 2) return run_key<32, 1, 2>(p, stream);
-  return run_key<32, 1, 4>(p, stream);
+  if (p.iters == 1) return run_key<32, 1, 1>(p, stream, part);
+  if (p.iters == 2) return run_key<32, 1, 2>(p, stream, part);
+  return run_key<32, 1, 4>(p, stream, part);
 }
 
 cudaError_t launch_apply_rows(const ApplyLaunch& p, cudaStream_t stream) {

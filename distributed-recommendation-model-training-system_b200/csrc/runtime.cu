@@ -104,9 +104,6 @@ struct Ticket {
   // layout
   std::vector<unsigned> feature_ids, feature_tables, dims, ranks;
   std::vector<unsigned long long> grad_rows, scale_base;
-  std::vector<unsigned> pooling;
-  std::vector<unsigned long long> scaled_off;   // value offset of a mean feature in `scaled`
-  float* scaled = nullptr;          // pre-scaled gradients of the mean features
   std::vector<unsigned> table_ids;
   std::vector<unsigned long long> table_occ;
   unsigned long long n = 0;
@@ -187,6 +184,8 @@ struct EpsB200Store {
   // anything that follows the lookup on the caller's stream
   cudaStream_t side = nullptr;
   cudaEvent_t fork = nullptr, join = nullptr;
+  // a push's piece sums run on `side` concurrently with its prescan
+  cudaEvent_t push_fork = nullptr, push_join = nullptr;
   cudaStream_t last = nullptr;
   cudaEvent_t last_done = nullptr;
   std::map<unsigned, Table> tables;
@@ -369,7 +368,7 @@ struct EpsB200Store {
   // for the oldest before the next lookup allocates its ticket, so that the
   // ticket memory of a steady stream of rounds stays bounded (and the
   // stream-ordered pool stops growing after the first rounds).
-  static constexpr size_t kMaxInflight = 3;
+  static constexpr size_t kMaxInflight = 6;
   void Throttle(cudaStream_t stream) {
     while (inflight.size() >= kMaxInflight) {
       auto it = tickets.find(inflight.front());
@@ -469,6 +468,8 @@ int eps_b200_create(const EpsB200Options* options, EpsB200Store** out, EpsB200St
       }
       Cuda(cudaEventCreateWithFlags(&s->fork, cudaEventDisableTiming));
       Cuda(cudaEventCreateWithFlags(&s->join, cudaEventDisableTiming));
+      Cuda(cudaEventCreateWithFlags(&s->push_fork, cudaEventDisableTiming));
+      Cuda(cudaEventCreateWithFlags(&s->push_join, cudaEventDisableTiming));
       // one status slot per live ticket plus a scratch slot (index max_live_tickets)
       Cuda(cudaMallocHost(&s->host_status, sizeof(HostStatus) * (s->opt.max_live_tickets + 1)));
       std::memset(s->host_status, 0, sizeof(HostStatus) * (s->opt.max_live_tickets + 1));
@@ -512,6 +513,8 @@ void eps_b200_destroy(EpsB200Store* s) {
     if (s->side) { cudaStreamSynchronize(s->side); cudaStreamDestroy(s->side); }
     if (s->fork) cudaEventDestroy(s->fork);
     if (s->join) cudaEventDestroy(s->join);
+    if (s->push_fork) cudaEventDestroy(s->push_fork);
+    if (s->push_join) cudaEventDestroy(s->push_join);
     if (s->own) cudaStreamDestroy(s->own);
   } catch (...) {
   }
@@ -595,7 +598,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
     std::map<unsigned, unsigned> ranks;   // table id -> rank (ascending id)
     std::unordered_set<unsigned> ids;
     unsigned long long total_keys = 0, total_offsets = 0, total_lengths = 0, total_rows = 0,
-                       host_out_values = 0, bags = 0, mean_values = 0;
+                       host_out_values = 0, bags = 0;
     std::vector<unsigned> dims;
     bool out16 = true, out8 = true, any_host_out = false, any_padding = false;
     for (uint64_t i = 0; i < count; ++i) {
@@ -627,7 +630,6 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       total_offsets += f.offset_count;
       if (f.valid_lengths) total_lengths += f.offset_count - 1;
       total_rows += rows;
-      if (f.pooling == 1) mean_values += rows * t.def.dimension;
       bags += f.offset_count - 1;
       dims.push_back(t.def.dimension);
     }
@@ -670,7 +672,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
     const unsigned long long max_pieces = (total_keys + kPiece - 1) / kPiece + max_long + total_keys / 2;
     size_t at_k0 = 0, at_k1 = 0, at_s0 = 0, at_s1 = 0, at_scale = 0, at_hist = 0, at_seg = 0,
            at_segtot = 0, at_segscr = 0, at_pieces = 0, at_rec = 0, at_rows = 0,
-           at_plan = 0, at_scaled = 0,
+           at_plan = 0,
            at_ptab = 0, at_pfeat = 0, at_gpre = 0, at_end = 0;
     size_t at_zero = 0;   // start of the region zeroed by the lookup's single memset
     if (!read_only) {
@@ -684,7 +686,6 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       at_pieces = c.take<uint2>(max_pieces);
       at_rec = c.take<LongRecord>(max_long);
       at_rows = c.take<RowRec>(total_keys);
-      at_scaled = c.take<float>(mean_values);
       // [sort scratch | segment scratch | row plan counts | status] zeroed together
       at_zero = at_hist = c.take<char>(sort_scratch_bytes(total_keys, key_bits));
       at_segscr = c.take<char>(segment_scratch_bytes(total_keys));
@@ -715,7 +716,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       Ticket t;
       t.read_only = read_only != 0;
       unsigned long long bag_base = 0, occ_base = 0, scale_base = 0, koff = 0,
-                         ooff = 0, loff = 0, hoff = 0, soff = 0;
+                         ooff = 0, loff = 0, hoff = 0;
       t.table_ids.resize(ranks.size());
       t.table_occ.assign(ranks.size(), 0);
       for (auto& [id, rank] : ranks) t.table_ids[rank] = id;
@@ -774,9 +775,6 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         t.ranks.push_back(L.table_rank);
         t.grad_rows.push_back(rows);
         t.scale_base.push_back(L.scale_base);
-        t.pooling.push_back(f.pooling);
-        t.scaled_off.push_back(soff);
-        if (f.pooling == 1) soff += rows * D;
         t.table_occ[L.table_rank] += f.key_count;
       }
       s.Stage(P(at_desc), desc.data(), count * sizeof(LookupFeature), stream);
@@ -799,16 +797,19 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         lp.occ_src = reinterpret_cast<unsigned*>(P(at_s0));
         lp.row_scale = reinterpret_cast<float*>(P(at_scale));
       }
-      cudaEvent_t ev = s.Begin(stream);
+      cudaEvent_t ev = nullptr;
       if (!read_only) {
         // the occurrence list first; the gather below does not emit, and the
         // sort (histograms, digit passes, segment compaction) runs on the side
         // stream concurrently with the gather
+        ev = s.Begin(stream);
         Cuda(launch_emit(lp, stream));
+        s.End(EPS_B200_PHASE_EMIT, ev, stream, bag_base ? 1u : 0u);
         Cuda(cudaEventRecord(s.fork, stream));
       }
+      ev = s.Begin(stream);
       Cuda(launch_lookup(lp, stream));
-      s.End(EPS_B200_PHASE_LOOKUP, ev, stream, (bag_base ? 1u : 0u) + (!read_only && bag_base ? 1u : 0u));
+      s.End(EPS_B200_PHASE_LOOKUP, ev, stream, bag_base ? 1u : 0u);
       if (!read_only) {
         cudaStream_t sort_stream = s.side;
         Cuda(cudaStreamWaitEvent(s.side, s.fork, 0));
@@ -857,7 +858,6 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         t.max_pieces = (unsigned)max_pieces;
         t.records = reinterpret_cast<LongRecord*>(P(at_rec));
         t.rows = reinterpret_cast<RowRec*>(P(at_rows));
-        t.scaled = reinterpret_cast<float*>(P(at_scaled));
         t.plan = reinterpret_cast<RowPlan*>(P(at_plan));
         t.status = status_block;
         t.control = &status_block->control;
@@ -1094,9 +1094,7 @@ int PushEntry(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gradien
           dev = stage + hoff;
           hoff += n;
         }
-        const bool mean = t.pooling[i] == 1;
-        pf[i] = PushFeature{dev, mean ? t.scaled + t.scaled_off[i] : const_cast<float*>(dev), g.rows,
-                            t.scale_base[i], t.dims[i], t.ranks[i], mean ? 1u : 0u, 0u};
+        pf[i] = PushFeature{dev, g.rows, t.scale_base[i], t.dims[i], t.ranks[i]};
         prefix[i + 1] = prefix[i] + n;
       }
       std::vector<PushTable> pt(t.table_ids.size());
@@ -1182,12 +1180,28 @@ int PushEntry(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gradien
         pl.ring_dim = (same && pl.grad_vec4 && t.dim_max == d0 && !(s.opt.flags & EPS_B200_FLAG_REGISTER_ROWS))
                           ? (int)d0 : 0;
       }
+      // the piece sums (uniform shape) write only the push's scratch, so they
+      // run on the side stream concurrently with the prescan; the row updates
+      // wait for both
+      const unsigned piece_launches = launch_push_apply_count(pl, 0);
+      if (piece_launches) {
+        Cuda(cudaEventRecord(s.push_fork, stream));
+        Cuda(cudaStreamWaitEvent(s.side, s.push_fork, 0));
+        cudaEvent_t evp = s.Begin(s.side);
+        Cuda(launch_push_apply(pl, s.side, 0));
+        s.End(EPS_B200_PHASE_PIECES, evp, s.side, piece_launches);
+        Cuda(cudaEventRecord(s.push_join, s.side));
+      }
       cudaEvent_t ev = s.Begin(stream);
       Cuda(launch_push_prescan(pl, stream));
       s.End(EPS_B200_PHASE_PRESCAN, ev, stream, 1);
+      if (piece_launches) Cuda(cudaStreamWaitEvent(stream, s.push_join, 0));
       ev = s.Begin(stream);
-      Cuda(launch_push_apply(pl, stream));
-      s.End(EPS_B200_PHASE_APPLY, ev, stream, launch_push_apply_count(pl));
+      Cuda(launch_push_apply(pl, stream, 1));
+      s.End(EPS_B200_PHASE_APPLY, ev, stream, launch_push_apply_count(pl, 1));
+      ev = s.Begin(stream);
+      Cuda(launch_push_apply(pl, stream, 2));
+      s.End(EPS_B200_PHASE_LONG, ev, stream, launch_push_apply_count(pl, 2));
       ev = s.Begin(stream);
       Cuda(launch_push_finalize(pl, stream));
       s.End(EPS_B200_PHASE_FINALIZE, ev, stream, launch_push_finalize_count(pl));

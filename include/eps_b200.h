@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define EPS_B200_ABI 1
+#define EPS_B200_ABI 2
 
 #if defined(_WIN32)
 #define EPS_B200_EXPORT __declspec(dllexport)
@@ -137,12 +137,16 @@ typedef struct {
 
 /* Phases of a lookup + push round, for eps_b200_profile. */
 enum {
-  EPS_B200_PHASE_LOOKUP = 0,     /* gather + pooling (+ occurrence list) */
-  EPS_B200_PHASE_SORT = 1,       /* stable radix sort of the occurrences */
+  EPS_B200_PHASE_LOOKUP = 0,     /* gather + pooling */
+  EPS_B200_PHASE_SORT = 1,       /* stable radix sort, segments and row plan */
   EPS_B200_PHASE_PRESCAN = 2,    /* gradient finiteness / bound scan + decision */
-  EPS_B200_PHASE_APPLY = 3,      /* coalesced segment-sum fused with LazyAdam */
-  EPS_B200_PHASE_FINALIZE = 4,   /* beta powers / optimizer sequence */
-  EPS_B200_PHASES = 5
+  EPS_B200_PHASE_APPLY = 3,      /* LazyAdam row updates (single rows and piece sums) */
+  EPS_B200_PHASE_FINALIZE = 4,   /* beta powers / optimizer sequence (own launch only
+                                    for a push without occurrences) */
+  EPS_B200_PHASE_EMIT = 5,       /* occurrence list of a lookup that will be pushed */
+  EPS_B200_PHASE_PIECES = 6,     /* in-order piece sums of rows with several occurrences */
+  EPS_B200_PHASE_LONG = 7,       /* long rows (piece combine + LazyAdam), checked apply */
+  EPS_B200_PHASES = 8
 };
 
 EPS_B200_EXPORT uint32_t eps_b200_abi_version(void);
