@@ -14,28 +14,30 @@
 //     written; a rejected Push leaves every byte of state unchanged.
 //
 // Launch sequence (all decisions are made on the device; no host sync):
-//   1. prescan   -- finiteness + max|g| of every gradient value; its last block
-//                   computes lr_t per table and picks the mode:
-//                   SAFE    when |g_reduced| <= 3*N*max|g| <= 1e17, the recorded
-//                           state bound <= 1e17 and lr_t/eps <= 1e20: then no
-//                           m, v or w can overflow (|lr_t*m/(sqrt(v)+eps)| <=
-//                           1e37) and the update is applied in ONE fused pass;
-//                   CHECKED otherwise: pass 0 validates exactly as the reference,
-//                           pass 1 applies only if nothing was rejected.
-//   2. rows pass 0, 3. pieces, 4. long pass 0, 5. rows pass 1, 6. long pass 1,
-//   7. finalize  -- advances beta powers and the sequence iff accepted.
+//   prescan    -- finiteness + max|g| of every gradient value (read-only); its
+//                 last block computes lr_t per table and picks the mode:
+//                 SAFE    when |g_reduced| <= 3*N*max|g| <= 1e17, the recorded
+//                         state bound <= 1e17 and lr_t/eps <= 1e20: then no
+//                         m, v or w can overflow (|lr_t*m/(sqrt(v)+eps)| <=
+//                         1e37) and every row is updated in ONE pass;
+//                 CHECKED otherwise: the row kernels validate exactly as the
+//                         reference and stage C applies only if nothing was
+//                         rejected;
+//   pieces     -- push_pieces_uniform (side stream, beside the prescan) for the
+//                 uniform shape; stage A sums them itself otherwise;
+//   rows       -- push_rows_ring (uniform shape) or push_stage_a;
+//   long rows  -- push_stage_b, whose last block advances the beta powers and
+//                 the sequence iff the push is accepted (SAFE / REJECTED);
+//   stage C    -- the apply pass of a CHECKED push (and its finalize).
 //
 // Coalescing layout: the occurrences are sorted stably by composite key
-// (table rank, slot) and the runs of equal keys are compacted into
-// seg_start[U + 1] at lookup time.  `push_rows` gives every coalesced row to a
-// group of G lanes (G = D/4: one 128-bit access per lane covers a row): for a
-// row with at most 64 occurrences the group issues the row's [w|m|v] loads,
-// sums the gradient references serially in occurrence order (bit-exact with the
-// reference) with up to 4 gradient rows in flight, and applies LazyAdam in the
-// same pass.  A longer (Zipf-head) row reserves ceil(len/64) contiguous piece
-// slots; `push_pieces` reduces the pieces in parallel and `push_long` combines
-// one row's pieces in piece order on one CTA and applies LazyAdam
-// (deterministic; within 1e-6 * sum|terms| of the reference's serial sum).
+// (table rank, slot), the runs of equal keys are compacted into seg_start[U + 1]
+// and a row plan (one RowRec per run) is built at lookup time.  A row with one
+// occurrence takes 0 + src * scale; a row with 2..64 occurrences gets one piece,
+// summed serially in occurrence order (bit-exact with the reference); a longer
+// (Zipf-head) row gets ceil(len / 64) pieces, summed in parallel and combined
+// in a fixed group tree by one CTA (deterministic; within 1e-6 * sum|terms| of
+// the reference's serial sum).
 #include <cooperative_groups.h>
 #include <cooperative_groups/reduce.h>
 
