@@ -162,6 +162,51 @@ def test_checked_mode_applies_large_finite_gradients(eps, workloads, reference_o
     s.close()
 
 
+@pytest.mark.parametrize("register_rows", [False, True])
+@pytest.mark.parametrize("dim,tables", [(32, 45), (128, 3)])
+def test_many_tables_one_dimension(eps, workloads, dim, tables, register_rows):
+    """Pushes whose tables share one dimension in {32, 64, 128} take the ring row
+    updates and the uniform piece sums (register_rows=False); with more than 32
+    tables and 128 features those kernels read the table and feature
+    descriptors from global memory instead of shared memory.  Two rounds must
+    equal the oracle bit for bit for every row with at most 64 occurrences per
+    push (and the first round's pooled outputs), counters and beta powers
+    exactly."""
+    w = workloads.small(11 + dim, dims=(dim,) * tables, bags=24, max_bag=10, rows=40)
+    defs = [TableDef(id=x.id, dimension=x.dimension, learning_rate=1e-2, rows=x.rows) for x in w.tables]
+    s = make_store(eps, defs, register_rows=register_rows)
+    o = Oracle(defs)
+    feats = [Feature(f.table, f.feature, f.pooling, f.keys, f.offsets) for f in w.features]
+    assert len(feats) > 128 or tables <= 32
+    for step in range(2):
+        ticket, outs = s.lookup(inputs(eps, feats))
+        want = o.lookup(feats)
+        if step == 0:
+            # pooled outputs are bit-exact until a row with > 64 occurrences has
+            # been updated (its piece tree differs from the serial sum in the
+            # last bits); the second round's bags may read such rows
+            for got, ref in zip(outs, want):
+                assert np.array_equal(bits(got), bits(ref))
+        s.push(ticket, w.gradients)
+        assert o.push(feats, w.gradients) == 0
+    long_seen = 0
+    for x in w.tables:
+        counts = occurrence_counts(feats, x.id)
+        keys = np.array(sorted(counts), np.uint64)
+        gw, gm, gv, gu = s.read_state(x.id, keys)
+        st, upd = o.state(x.id)
+        k = keys.astype(np.int64)
+        short = np.array([counts[int(q)] <= 64 for q in keys])
+        long_seen += int((~short).sum())
+        for got, want in ((gw, st[k, 0]), (gm, st[k, 1]), (gv, st[k, 2])):
+            assert np.array_equal(bits(got[short]), bits(want[short])), x.id
+        assert np.array_equal(gu, upd[k])
+        assert s.optimizer_state(x.id)[0] == 2
+    if dim == 128:
+        assert long_seen > 0           # the long-row path ran too
+    s.close()
+
+
 def test_shard_partials_merge_bit_exact(eps):
     """Two shard stores (key % 2) return the ParameterService::Lookup partials; merged
     in shard order and divided once for mean they equal the reference's 2-shard
