@@ -201,6 +201,7 @@ struct SegmentLaunch {
   unsigned int* error;
 };
 cudaError_t launch_segments(const SegmentLaunch& p, cudaStream_t stream);
+unsigned segment_launch_count(unsigned long long n);
 size_t segment_scratch_bytes(unsigned long long n);
 
 // The push's row plan (RowRec / RowPlan), built from the segments at lookup time.

@@ -842,7 +842,8 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         pp.pieces = reinterpret_cast<uint2*>(P(at_pieces));
         pp.longs = reinterpret_cast<LongRecord*>(P(at_rec));
         Cuda(launch_row_plan(pp, sort_stream));
-        s.End(EPS_B200_PHASE_SORT, ev, sort_stream, sort_launch_count(sp) + (total_keys ? 2u : 0u));
+        s.End(EPS_B200_PHASE_SORT, ev, sort_stream,
+              sort_launch_count(sp) + segment_launch_count(total_keys) + (total_keys ? 1u : 0u));
         Cuda(cudaEventRecord(s.join, s.side));
         Cuda(cudaStreamWaitEvent(stream, s.join, 0));
         t.keys = swapped ? P(at_k1) : P(at_k0);
@@ -2011,7 +2012,7 @@ int eps_b200_sync_reduce(EpsB200Store* store, uint32_t table, const EpsB200Worke
       lp.keys_out = reinterpret_cast<unsigned long long*>(keys_out);
       lp.values_out = values_out;
       Cuda(launch_sync_accumulate(lp, stream));
-      s.stats.kernel_launches += 3 + sort_launch_count(sp);
+      s.stats.kernel_launches += 2 + segment_launch_count(n) + sort_launch_count(sp);
       unsigned host[2];
       Cuda(cudaMemcpyAsync(host, tot, sizeof(host), cudaMemcpyDeviceToHost, stream));
       s.Sync(stream);

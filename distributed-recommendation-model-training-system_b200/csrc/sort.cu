@@ -61,6 +61,93 @@ __global__ void __launch_bounds__(kThreads) digit_histograms(const KeyT* keys, u
 // seg_start[u] = position of the u-th run of equal keys, seg_start[U] = n,
 // *seg_total = U.  Tiles of 4096 positions (16 consecutive per thread), taken
 // in launch order; a warp-wide look-back reads 32 predecessors per step.
+// Segment heads without a look-back chain, for up to kDirectTiles tiles: the
+// first launch counts each tile's run heads, the second gives every tile the
+// sum of its predecessors' counts (read directly, at most kDirectTiles values)
+// and writes its heads' positions.  The look-back kernel below serves larger
+// inputs: with every tile of a one-wave grid running at once, its prefix
+// frontier crosses the tiles only a few at a time.
+constexpr unsigned kDirectTiles = 4096;
+
+template <typename KeyT>
+__device__ __forceinline__ unsigned tile_head_flags(const KeyT* keys, unsigned long long n,
+                                                    unsigned long long base) {
+  unsigned flags = 0;
+  if (base < n) {
+    KeyT prev = base > 0 ? keys[base - 1] : KeyT(0);
+#pragma unroll
+    for (int j = 0; j < kItems; ++j) {
+      const unsigned long long i = base + j;
+      if (i < n) {
+        const KeyT k = keys[i];
+        if (i == 0 || k != prev) flags |= 1u << j;
+        prev = k;
+      }
+    }
+  }
+  return flags;
+}
+
+template <typename KeyT>
+__global__ void __launch_bounds__(kThreads) segment_counts(const KeyT* keys, unsigned long long n,
+                                                           unsigned* tile_cnt) {
+  __shared__ unsigned s_warp[kWarps];
+  const unsigned w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const unsigned long long base = (unsigned long long)blockIdx.x * kSortTile + threadIdx.x * kItems;
+  const unsigned c = __reduce_add_sync(0xffffffffu, (unsigned)__popc(tile_head_flags(keys, n, base)));
+  if (lane == 0) s_warp[w] = c;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned t = 0;
+#pragma unroll
+    for (int q = 0; q < kWarps; ++q) t += s_warp[q];
+    tile_cnt[blockIdx.x] = t;
+  }
+}
+
+template <typename KeyT>
+__global__ void __launch_bounds__(kThreads) segment_write(const KeyT* keys, unsigned long long n,
+                                                          const unsigned* tile_cnt,
+                                                          unsigned* seg_start, unsigned* seg_total) {
+  __shared__ unsigned s_warp[kWarps], s_pre[kWarps];
+  const unsigned w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const unsigned tile = blockIdx.x;
+  // heads of the earlier tiles
+  unsigned part = 0;
+  for (unsigned t = threadIdx.x; t < tile; t += kThreads) part += tile_cnt[t];
+  part = __reduce_add_sync(0xffffffffu, part);
+  const unsigned long long base = (unsigned long long)tile * kSortTile + threadIdx.x * kItems;
+  unsigned flags = tile_head_flags(keys, n, base);
+  const unsigned cnt = __popc(flags);
+  unsigned x = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= (unsigned)o) x += y;
+  }
+  if (lane == 31) s_warp[w] = x;
+  if (lane == 0) s_pre[w] = part;
+  __syncthreads();
+  unsigned before = 0, total = 0, prefix = 0;
+#pragma unroll
+  for (int q = 0; q < kWarps; ++q) {
+    if ((unsigned)q < w) before += s_warp[q];
+    total += s_warp[q];
+    prefix += s_pre[q];
+  }
+  unsigned r = prefix + before + x - cnt;
+  while (flags) {
+    const int j = __ffs(flags) - 1;
+    flags &= flags - 1;
+    seg_start[r++] = (unsigned)(base + j);
+  }
+  const unsigned long long tiles = (n + kSortTile - 1) / kSortTile;
+  if (tile == tiles - 1 && threadIdx.x == 0) {
+    seg_start[prefix + total] = (unsigned)n;
+    *seg_total = prefix + total;
+  }
+}
+
 template <typename KeyT>
 __global__ void __launch_bounds__(kThreads) segment_heads(const KeyT* keys, unsigned long long n,
                                                           unsigned* seg_start, unsigned* seg_total,
@@ -339,6 +426,13 @@ cudaError_t run_heads(const SegmentLaunch& p, cudaStream_t s) {
   unsigned* counter = p.scratch;
   unsigned long long* status = reinterpret_cast<unsigned long long*>(
       reinterpret_cast<char*>(p.scratch) + 256);
+  if (tiles <= kDirectTiles) {
+    unsigned* tile_cnt = reinterpret_cast<unsigned*>(status);   // tiles x 8 bytes available
+    segment_counts<KeyT><<<tiles, kThreads, 0, s>>>(static_cast<const KeyT*>(p.keys), p.n, tile_cnt);
+    segment_write<KeyT><<<tiles, kThreads, 0, s>>>(static_cast<const KeyT*>(p.keys), p.n, tile_cnt,
+                                                   p.seg_start, p.seg_total);
+    return cudaGetLastError();
+  }
   segment_heads<KeyT><<<tiles, kThreads, 0, s>>>(static_cast<const KeyT*>(p.keys), p.n,
                                                  p.seg_start, p.seg_total, status, counter,
                                                  p.error);
@@ -441,6 +535,11 @@ cudaError_t run_plan(const PlanLaunch& p, cudaStream_t s) {
 
 size_t segment_scratch_bytes(unsigned long long n) {
   return 256 + (size_t)((n + kSortTile - 1) / kSortTile) * sizeof(unsigned long long);
+}
+
+unsigned segment_launch_count(unsigned long long n) {
+  if (n == 0) return 0;
+  return (n + kSortTile - 1) / kSortTile <= kDirectTiles ? 2u : 1u;
 }
 
 cudaError_t launch_segments(const SegmentLaunch& p, cudaStream_t stream) {
