@@ -172,6 +172,29 @@ class Clocks:
         except Exception:
             self.proc = None
 
+    def wait_first(self, timeout=15.0):
+        """Blocks until nvidia-smi has written its first sample, so that its
+        start-up (process spawn, driver library initialisation, first query),
+        which can hold up this process's own driver calls for tens of
+        milliseconds, is over before any timed round."""
+        if not self.proc:
+            return
+        t0 = time.time()
+        while time.time() - t0 < timeout and self.proc.poll() is None:
+            self.out.flush()
+            if os.path.getsize(self.path) > 0:
+                return
+            time.sleep(0.02)
+
+    def mark(self):
+        """Samples before this call (sampler start-up, allocator priming) are
+        left out of the summary."""
+        self.skip = 0
+        if self.proc:
+            self.out.flush()
+            with open(self.path) as f:
+                self.skip = sum(1 for _ in f)
+
     def stop(self):
         if not self.proc:
             return None
@@ -182,9 +205,9 @@ class Clocks:
             self.proc.kill()
         self.out.close()
         rows = []
-        for line in open(self.path):
+        for i, line in enumerate(open(self.path)):
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 8:
+            if i >= getattr(self, "skip", 0) and len(parts) >= 8:
                 rows.append(parts)
         os.unlink(self.path)
         if not rows:
@@ -326,6 +349,10 @@ def run_b200(args):
             ticket = lookup(stream)
             push(ticket, stream, wait=False)
 
+    # the clock sampler first: its start-up must be over before timed work
+    clocks = Clocks(local_rank)
+    clocks.start()
+    clocks.wait_first()
     # allocator priming (untimed): more rounds in flight than the library's
     # limit of enqueued pushes, so that the stream-ordered memory pool reaches
     # its steady size before the warm-up and never grows (maps new memory, a
@@ -333,8 +360,7 @@ def run_b200(args):
     for _ in range(8):
         one_round()
     store.synchronize()
-    clocks = Clocks(local_rank)
-    clocks.start()
+    clocks.mark()
     for _ in range(args.warmup):
         flush.zero_()
         one_round()
@@ -521,7 +547,9 @@ def run_b200(args):
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,
         "host_us_per_round": {"median": 1e6 * float(np.median(host_s)),
-                              "max": 1e6 * max(host_s)},
+                              "max": 1e6 * max(host_s),
+                              "argmax": int(np.argmax(host_s)),
+                              "rounds_ms": [round(a.elapsed_time(b), 4) for a, b in events]},
         "clocks": clk,
     }
     print(json.dumps(line))
