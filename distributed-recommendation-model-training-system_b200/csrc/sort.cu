@@ -59,8 +59,7 @@ __global__ void __launch_bounds__(kThreads) digit_histograms(const KeyT* keys, u
 
 // Order-preserving compaction of segment heads of the sorted keys:
 // seg_start[u] = position of the u-th run of equal keys, seg_start[U] = n,
-// *seg_total = U.  Tiles of 4096 positions (16 consecutive per thread), taken
-// in launch order; a warp-wide look-back reads 32 predecessors per step.
+// *seg_total = U, over tiles of 4096 positions (16 consecutive per thread).
 // Segment heads without a look-back chain, for up to kDirectTiles tiles: the
 // first launch counts each tile's run heads, the second gives every tile the
 // sum of its predecessors' counts (read directly, at most kDirectTiles values)
@@ -148,6 +147,8 @@ __global__ void __launch_bounds__(kThreads) segment_write(const KeyT* keys, unsi
   }
 }
 
+// The look-back variant: tiles taken in launch order; a warp-wide look-back
+// reads 32 predecessors per step.
 template <typename KeyT>
 __global__ void __launch_bounds__(kThreads) segment_heads(const KeyT* keys, unsigned long long n,
                                                           unsigned* seg_start, unsigned* seg_total,
