@@ -361,6 +361,12 @@ def run_b200(args):
         one_round()
     store.synchronize()
     clocks.mark()
+    # no Python collector pauses inside the warm-up and the timed rounds (a pause
+    # longer than the rounds queued ahead of the host would leave the device
+    # idle); collecting here, before the warm-up, keeps the device busy right up
+    # to the first timed round
+    gc.collect()
+    gc.disable()
     for _ in range(args.warmup):
         flush.zero_()
         one_round()
@@ -372,10 +378,6 @@ def run_b200(args):
     events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in range(args.steps)]
     torch.cuda.synchronize()
-    # no Python collector pauses inside the timed rounds (a pause longer than the
-    # rounds queued ahead of the host would leave the device idle)
-    gc.collect()
-    gc.disable()
     host_s = []
     for a, b in events:
         flush.zero_()
