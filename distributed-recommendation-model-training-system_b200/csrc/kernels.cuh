@@ -12,11 +12,6 @@
 
 namespace eps_b200 {
 
-template <int VEC> struct VecT;
-template <> struct VecT<1> { using type = float; };
-template <> struct VecT<2> { using type = float2; };
-template <> struct VecT<4> { using type = float4; };
-
 template <int VEC>
 __device__ __forceinline__ void load_vec(const float* p, float (&r)[VEC]) {
   if constexpr (VEC == 4) {
@@ -66,10 +61,6 @@ __device__ __forceinline__ void store_vec_stream(float* p, const float (&r)[VEC]
   }
 }
 
-__device__ __forceinline__ unsigned lane_id() { return threadIdx.x & 31u; }
-
-__device__ __forceinline__ bool finitef(float x) { return isfinite(x); }
-
 // Clamp with std::clamp semantics (src/common/optimizer_bounds.hpp:14-18).
 __device__ __forceinline__ float clamp_weight(float v, int has, float lo, float hi) {
   if (!has) return v;
@@ -77,22 +68,6 @@ __device__ __forceinline__ float clamp_weight(float v, int has, float lo, float 
 }
 
 __device__ __forceinline__ unsigned abs_bits(float x) { return __float_as_uint(fabsf(x)); }
-
-// Asynchronous global -> shared copies (sm_80+ cp.async): VEC floats per lane.
-template <int VEC>
-__device__ __forceinline__ void cp_async_vec(float* smem, const float* gmem) {
-  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
-  if constexpr (VEC == 4) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
-  } else if constexpr (VEC == 2) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(s), "l"(gmem));
-  } else {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem));
-  }
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
 
 // Launch shape of the row kernels: a group of `group` lanes owns one row, each
 // lane `vec` consecutive floats, `iters` times.  128-bit accesses (vec = 4) need

@@ -45,17 +45,13 @@
 
 namespace cg = cooperative_groups;
 
-#ifndef EPS_PUSH_DEPTH_REGS
-#define EPS_PUSH_DEPTH_REGS 16        // registers per lane for gradient rows in flight
-#endif
 #ifndef EPS_PUSH_MIN_BLOCKS
-#define EPS_PUSH_MIN_BLOCKS 2         // resident 256-thread blocks per SM (C <= 4)
+#define EPS_PUSH_MIN_BLOCKS 2         // resident 256-thread blocks per SM of the register
+                                      // stages (C <= 4)
 #endif
 #ifndef EPS_PIECE_DEPTH_REGS
-#define EPS_PIECE_DEPTH_REGS 32       // the same for the long rows' pieces
-#endif
-#ifndef EPS_PIECE_MIN_BLOCKS
-#define EPS_PIECE_MIN_BLOCKS 3
+#define EPS_PIECE_DEPTH_REGS 32       // registers per lane for gradient rows in flight
+                                      // in the register stage's piece sums
 #endif
 
 namespace eps_b200 {
