@@ -378,6 +378,11 @@ def run_b200(args):
     events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in range(args.steps)]
     torch.cuda.synchronize()
+    # after the synchronize the device queue is empty: three extra L2 flushes
+    # (untimed, ~40 us each) give the host the head start it has in steady
+    # state, so that round 0 does not wait for its own enqueue
+    for _ in range(3):
+        flush.zero_()
     host_s = []
     for a, b in events:
         flush.zero_()
