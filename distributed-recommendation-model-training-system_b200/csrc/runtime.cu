@@ -810,6 +810,17 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       ev = s.Begin(stream);
       Cuda(launch_lookup(lp, stream));
       s.End(EPS_B200_PHASE_LOOKUP, ev, stream, bag_base ? 1u : 0u);
+      // ---- host outputs: final once the gather ends, so their copies are queued
+      // before the stream joins the sort and overlap the sort's remaining work
+      hoff = 0;
+      for (uint64_t i = 0; i < count; ++i) {
+        if (outputs[i].device >= 0) continue;
+        const unsigned long long n = outputs[i].rows * outputs[i].columns;
+        if (n)
+          Cuda(cudaMemcpyAsync(outputs[i].data, reinterpret_cast<float*>(P(at_hostout)) + hoff,
+                               n * 4, cudaMemcpyDeviceToHost, stream));
+        hoff += n;
+      }
       if (!read_only) {
         cudaStream_t sort_stream = s.side;
         Cuda(cudaStreamWaitEvent(s.side, s.fork, 0));
@@ -867,16 +878,6 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         t.push_features = reinterpret_cast<PushFeature*>(P(at_pfeat));
         t.grad_prefix = reinterpret_cast<unsigned long long*>(P(at_gpre));
         t.stage_end = P(at_end);
-      }
-      // ---- host outputs
-      hoff = 0;
-      for (uint64_t i = 0; i < count; ++i) {
-        if (outputs[i].device >= 0) continue;
-        const unsigned long long n = outputs[i].rows * outputs[i].columns;
-        if (n)
-          Cuda(cudaMemcpyAsync(outputs[i].data, reinterpret_cast<float*>(P(at_hostout)) + hoff,
-                               n * 4, cudaMemcpyDeviceToHost, stream));
-        hoff += n;
       }
       const bool synchronous = !input_on_device || any_host_out;
       int slot = -1;
