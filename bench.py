@@ -354,10 +354,10 @@ def run_b200(args):
     clocks.start()
     clocks.wait_first()
     # allocator priming (untimed): more rounds in flight than the library's
-    # limit of enqueued pushes, so that the stream-ordered memory pool reaches
-    # its steady size before the warm-up and never grows (maps new memory, a
-    # host stall of milliseconds) inside the timed rounds
-    for _ in range(8):
+    # limit of enqueued pushes (16), so that the stream-ordered memory pool
+    # reaches its steady size before the warm-up and never grows (maps new
+    # memory, a host stall of milliseconds) inside the timed rounds
+    for _ in range(20):
         one_round()
     store.synchronize()
     clocks.mark()

@@ -368,7 +368,7 @@ struct EpsB200Store {
   // for the oldest before the next lookup allocates its ticket, so that the
   // ticket memory of a steady stream of rounds stays bounded (and the
   // stream-ordered pool stops growing after the first rounds).
-  static constexpr size_t kMaxInflight = 6;
+  static constexpr size_t kMaxInflight = 16;
   void Throttle(cudaStream_t stream) {
     while (inflight.size() >= kMaxInflight) {
       auto it = tickets.find(inflight.front());
