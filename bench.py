@@ -129,6 +129,14 @@ def byte_model(w):
             "U_long": sum(long_rows.values())}
 
 
+def dominant_kernel(prof, bm):
+    """The roofline's kernel: the phase with the longest time per call among
+    those with compulsory HBM bytes in the byte model (gather, row updates, long
+    rows, prescan)."""
+    cands = [p for p in prof if bm.get(p) and prof[p]["ms"]]
+    return max(cands, key=lambda p: prof[p]["ms"] / max(1, prof[p]["calls"]))
+
+
 def load_peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -433,9 +441,7 @@ def run_b200(args):
 
     # ---- roofline of the dominant phase
     peak, peak_kind = load_peaks()
-    # the dominant kernel: the longest phase with compulsory HBM bytes (the
-    # gather, the row updates, the long rows or the prescan: each one launch)
-    dom = max((p for p in prof if bm.get(p) and prof[p]["ms"]), key=lambda p: prof[p]["ms"])
+    dom = dominant_kernel(prof, bm)
     calls = max(1, prof[dom]["calls"])
     per_call_ms = prof[dom]["ms"] / calls
     alg = bm[dom]

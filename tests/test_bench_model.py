@@ -1,0 +1,51 @@
+"""bench.py's byte model and roofline-kernel choice (CPU): the compulsory HBM
+bytes per round, recomputed here independently on a multi-table workload with
+mixed dimensions, pooling modes and rows hot enough to take the long-row path."""
+import importlib.util
+import os
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def load_bench():
+    spec = importlib.util.spec_from_file_location("eps_bench_under_test", os.path.join(ROOT, "bench.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_byte_model_matches_an_independent_count(workloads):
+    bench = load_bench()
+    w = workloads.small(5, rows=40)
+    bm = bench.byte_model(w)
+    dims = {t.id: t.dimension for t in w.tables}
+    n = sum(len(f.keys) for f in w.features)
+    uniq, longs = {}, {}
+    for t in w.tables:
+        ks = np.concatenate([f.keys for f in w.features if f.table == t.id])
+        u, c = np.unique(ks, return_counts=True)
+        uniq[t.id], longs[t.id] = len(u), int((c > 64).sum())
+    outs = sum(4 * dims[f.table] * f.output_rows for f in w.features)
+    offs = sum(len(f.offsets) for f in w.features if f.pooling != 2)
+    rows_u = sum(4 * dims[t] * u for t, u in uniq.items())
+    assert bm["N"] == n and bm["U"] == sum(uniq.values())
+    assert bm["pull"] == 8 * n + 8 * offs + rows_u + outs
+    assert bm["push"] == outs + 8 * n + 8 * offs + 6 * rows_u + 16 * sum(uniq.values())
+    assert bm["apply"] == sum((24 * dims[t] + 16) * (uniq[t] - longs[t]) for t in uniq)
+    assert bm["long"] == sum((24 * dims[t] + 16) * longs[t] for t in uniq)
+    assert sum(longs.values()) > 0 and bm["U_long"] == sum(longs.values())
+    assert bm["prescan"] == outs and bm["sort"] == 0 and bm["pieces"] == 0
+
+
+def test_dominant_kernel_is_the_longest_phase_with_bytes():
+    bench = load_bench()
+    bm = {"lookup": 10, "apply": 20, "long": 5, "prescan": 1, "sort": 0, "pieces": 0, "emit": 0}
+    prof = {"lookup": {"ms": 2.0, "calls": 20}, "sort": {"ms": 9.0, "calls": 20},
+            "apply": {"ms": 1.9, "calls": 20}, "pieces": {"ms": 3.0, "calls": 20},
+            "long": {"ms": 0.5, "calls": 20}, "prescan": {"ms": 0.3, "calls": 20},
+            "emit": {"ms": 0.4, "calls": 20}, "finalize": {"ms": 0.0, "calls": 0}}
+    assert bench.dominant_kernel(prof, bm) == "lookup"      # the sort and pieces have no bytes
+    prof["apply"]["ms"] = 2.5
+    assert bench.dominant_kernel(prof, bm) == "apply"
