@@ -12,7 +12,11 @@
 //      with the agent attached (AttachAgent, include/eps/runtime.hpp:133) and a
 //      DistributedClient resolving cached rows through GatherHost, in the flow
 //      of the reference's tests/cache_tests.cpp -- the same rounds against a
-//      service with a HostCacheBackend attached.
+//      service with a HostCacheBackend attached;
+//   3. under the reference's AgentRuntime (include/eps/agent_runtime.hpp), the
+//      command layer its BRPC agent server dispatches to: retried commands
+//      replay their first result without applying twice, older commands are
+//      retired, and eviction reclaims the slots -- the same with either backend.
 // Linked against the real library it checks the B200 path; linked against
 // oracle/fake_b200_abi.cpp it checks the adapter's host logic without a GPU.
 // Prints "agent_check: PASS ..." and exits 0, or names the first difference.
@@ -28,6 +32,7 @@
 #include <vector>
 
 #include "b200_cache_agent.hpp"
+#include "eps/agent_runtime.hpp"
 #include "eps/cache_backend.hpp"
 #include "eps/distributed_client.hpp"
 #include "eps/runtime.hpp"
@@ -476,14 +481,70 @@ void ServiceDropIn() {
   Take(cb.Release(b), "release");
 }
 
+// ---- the agent process's command layer over each backend
+template <typename T>
+T Both(std::future<Result<T>> a, std::future<Result<T>> b, const std::string& what) {
+  auto x = Take(std::move(a), "b200 " + what);
+  Take(std::move(b), "host " + what);
+  return x;
+}
+
+void RuntimeReplay() {
+  const TableDefinition table{1, 2, 1, 1, {0.1f, 0.9f, 0.999f, 1e-8f, 0.9f, 0.999f}, 0, 0, 42};
+  B200CacheOptions o;
+  o.rows_per_table = 2;                         // two slots, as the host budget below holds
+  auto agent = std::make_shared<B200CacheAgent>(o);
+  auto host = std::make_shared<HostCacheBackend>(0, 2 * (2 * 12 + 8));
+  AgentRuntime ra("agent-runtime", agent), rb("agent-runtime", host);
+  auto id = [](std::uint64_t n) { return AgentCommand{"agent-runtime", 0, n}; };
+  Both(ra.Define(id(0), table), rb.Define(id(0), table), "define");
+  Both(ra.Define(id(0), table), rb.Define(id(0), table), "define replay");
+  const MigrationPlan load{"load", 0, {{{1, 4}, 0, Placement::loading, 0, 1, 0}}, Placement::gpu, 32, 0};
+  const RowState state{{1, 4}, {0.125f, -0.25f}, {0.0f, 0.0f}, {0.0f, 0.0f}, 0};
+  auto first_a = Take(ra.Load(id(1), load, {state}), "b200 load");
+  auto first_b = Take(rb.Load(id(1), load, {state}), "host load");
+  auto again_a = Take(ra.Load(id(1), load, {state}), "b200 load replay");
+  Take(rb.Load(id(1), load, {state}), "host load replay");
+  Check(first_a[0].slot == again_a[0].slot, "load replay allocated a second slot");
+  Check(Take(agent->FreeSlots(1), "free slots") == 1, "load replay consumed a slot");
+  UpdateContext c{{"agent-runtime", 0, 0, Phase::push}, 0, 1, 0, 0.1f, 0.9f, 0.999f};
+  const RowGradients g{{{1, 4}}, {1.0f, -0.5f}};
+  Both(ra.Apply(id(2), c, g), rb.Apply(id(2), c, g), "apply");
+  Both(ra.Apply(id(2), c, g), rb.Apply(id(2), c, g), "apply replay");
+  SameRejection(ra.Load(id(1), load, {state}), rb.Load(id(1), load, {state}),
+                "retired load after an update");
+  c.original_request.sequence = 1;
+  c.optimizer_sequence = 1;
+  c.beta1_power *= 0.9f;
+  c.beta2_power *= 0.999f;
+  const CompactGradients p{{{1, 4}}, 2, {0.5f, 0.25f, -1.0f, 2.0f}, {0, 3}, {0, 1, 0}, {1.0f, 0.5f, 0.25f}};
+  Both(ra.ApplyCompact(id(3), c, p), rb.ApplyCompact(id(3), c, p), "compact apply");
+  Both(ra.ApplyCompact(id(3), c, p), rb.ApplyCompact(id(3), c, p), "compact apply replay");
+  const MigrationPlan evict_a{"evict", 0, first_a, Placement::cpu, 32, 0};
+  const MigrationPlan evict_b{"evict", 0, first_b, Placement::cpu, 32, 0};
+  auto sa = Take(ra.ReadBack(id(4), evict_a), "b200 readback");
+  auto sb = Take(rb.ReadBack(id(4), evict_b), "host readback");
+  auto replay = Take(ra.ReadBack(id(4), evict_a), "b200 readback replay");
+  Check(sa[0].row_updates == 2 && sb[0].row_updates == 2, "replayed updates applied twice");
+  Check(SameBits(sa[0].weights, sb[0].weights) && SameBits(sa[0].first_moment, sb[0].first_moment) &&
+            SameBits(sa[0].second_moment, sb[0].second_moment) && SameBits(replay[0].weights, sa[0].weights),
+        "runtime state differs from the host backend");
+  Both(ra.CommitEviction(id(5), evict_a), rb.CommitEviction(id(5), evict_b), "eviction");
+  Both(ra.CommitEviction(id(5), evict_a), rb.CommitEviction(id(5), evict_b), "eviction replay");
+  Check(Take(agent->FreeSlots(1), "free slots") == 2, "eviction did not reclaim the slot");
+  Both(ra.Define(id(7), table), rb.Define(id(7), table), "define after a skip");
+  SameRejection(ra.Define(id(6), table), rb.Define(id(6), table), "command older than a skip");
+}
+
 }  // namespace
 
 int main() {
   try {
     BackendContract();
     ServiceDropIn();
-    std::cout << "agent_check: PASS backend contract and service drop-in, bit-exact vs "
-                 "HostCacheBackend\n";
+    RuntimeReplay();
+    std::cout << "agent_check: PASS backend contract, service drop-in and agent runtime, "
+                 "bit-exact vs HostCacheBackend\n";
     return 0;
   } catch (const std::exception& e) {
     std::cerr << "agent_check: FAIL " << e.what() << "\n";
