@@ -29,6 +29,7 @@
 #include <memory>
 #include <stdexcept>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 #include "b200_cache_agent.hpp"
@@ -36,8 +37,15 @@
 #include "eps/cache_backend.hpp"
 #include "eps/distributed_client.hpp"
 #include "eps/runtime.hpp"
+#include "eps/worker_cache_agent.hpp"
 
 using namespace eps;
+
+// The training process's owner of a cache agent (include/eps/worker_cache_agent.hpp,
+// served over BRPC, which is not built here) takes the adapter unchanged.
+static_assert(std::is_constructible_v<WorkerCacheAgent, WorkerCacheOptions,
+                                      std::shared_ptr<B200CacheAgent>>);
+static_assert(std::is_convertible_v<std::shared_ptr<B200CacheAgent>, std::shared_ptr<GpuCacheAgent>>);
 
 namespace {
 
