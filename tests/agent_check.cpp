@@ -32,6 +32,8 @@
 #include <type_traits>
 #include <vector>
 
+#include <cuda_runtime_api.h>
+
 #include "b200_cache_agent.hpp"
 #include "eps/agent_runtime.hpp"
 #include "eps/cache_backend.hpp"
@@ -90,12 +92,15 @@ bool SameBits(const std::vector<float>& a, const std::vector<float>& b) {
   return a.size() == b.size() && (a.empty() || !std::memcmp(a.data(), b.data(), a.size() * 4));
 }
 
+// The shapes of the reference's CUDA-backend test (tests/cuda_tests.cpp:73-151).
+constexpr std::uint32_t kDim1 = 128, kDim2 = 64;
+
 TableDefinition Table1() {
-  return {1, 8, 2, 1, {0.01f, 0.9f, 0.999f, 1e-8f, 0.9f, 0.999f}, -0.05f, 0.05f, 7};
+  return {1, kDim1, 2, 1, {0.01f, 0.9f, 0.999f, 1e-8f, 0.9f, 0.999f}, -0.05f, 0.05f, 7};
 }
 TableDefinition Table2() {
   OptimizerConfig o{0.05f, 0.8f, 0.99f, 1e-7f, 0.8f, 0.99f, WeightBounds{-0.03f, 0.03f}};
-  return {2, 4, 2, 1, o, -0.05f, 0.05f, 11};
+  return {2, kDim2, 2, 1, o, -0.05f, 0.05f, 11};
 }
 
 // Resident rows of one backend: its own LocatedRow per key (slots differ).
@@ -148,7 +153,7 @@ std::vector<AgentWork> MakeWork(std::vector<Feature>& features, const Residency&
     AgentWork w{f.input.feature, f.route, 0, {}, {}, {}};
     std::map<Key, std::uint64_t> index;
     const bool transfer = f.route == AccessRoute::transfer_unique;
-    const auto dim = f.input.table == 1 ? 8u : 4u;
+    const auto dim = f.input.table == 1 ? kDim1 : kDim2;
     for (auto key : f.input.keys) {
       auto it = resident.find({f.input.table, key});
       const bool served = transfer ? key % 5 != 0 : it != resident.end();
@@ -268,11 +273,11 @@ void BackendContract() {
   std::vector<RowState> states;
   for (Key k = 0; k < 30; ++k) {
     plan_rows.push_back({{1, k}, 0, Placement::loading, 0, 1 + k % 3, 0});
-    states.push_back(RandomState(r, {1, k}, 8));
+    states.push_back(RandomState(r, {1, k}, kDim1));
   }
   for (Key k = 100; k < 118; ++k) {
     plan_rows.push_back({{2, k}, 0, Placement::loading, 0, 2, 0});
-    states.push_back(RandomState(r, {2, k}, 4));
+    states.push_back(RandomState(r, {2, k}, kDim2));
   }
   auto la = Take(a.Load(Plan(plan_rows, Placement::gpu), states), "b200 load");
   auto lb = Take(b.Load(Plan(plan_rows, Placement::gpu), states), "host load");
@@ -289,7 +294,7 @@ void BackendContract() {
   SameRejection(a.Load(Plan({plan_rows[0]}, Placement::gpu), {states[0]}),
                 b.Load(Plan({plan_rows[0]}, Placement::gpu), {states[0]}), "load of a resident row");
   {
-    auto bad = RandomState(r, {1, 35}, 8);
+    auto bad = RandomState(r, {1, 35}, kDim1);
     bad.second_moment[3] = -1.0f;
     LocatedRow loc{{1, 35}, 0, Placement::loading, 0, 1, 0};
     SameRejection(a.Load(Plan({loc}, Placement::gpu), {bad}), b.Load(Plan({loc}, Placement::gpu), {bad}),
@@ -297,8 +302,8 @@ void BackendContract() {
   }
   CompareStates(a, b, ra, rb, "after load");
 
-  // ---- gathers, updates and gathers again
-  for (int round = 0; round < 4; ++round) {
+  // ---- gathers and 9 update steps per table: 7 ApplyHost, 2 ApplyCompact
+  for (int round = 0; round < 9; ++round) {
     Rng fr{1000u + round};
     auto features = MakeFeatures(fr);
     Rng wa{77u + round}, wb{77u + round};
@@ -308,17 +313,20 @@ void BackendContract() {
                   Take(b.GatherHost(work_b, Layouts(features)), "host gather"),
                   "gather round " + std::to_string(round));
     for (TableId t : {1u, 2u}) {
-      const auto dim = t == 1 ? 8u : 4u;
+      const auto dim = t == 1 ? kDim1 : kDim2;
       const auto def = t == 1 ? Table1() : Table2();
-      Rng ga{500u + round * 7 + t};
-      auto g = Gradients(ga, ra, t, dim, t == 1 ? 0.01f : 0.5f);
       auto c = Context(t, round + 1, def.optimizer.learning_rate, def.optimizer.beta1, def.optimizer.beta2);
-      Take(a.ApplyHost(c, g), "b200 apply");
-      Take(b.ApplyHost(c, g), "host apply");
-      Rng ca{900u + round * 7 + t};
-      auto p = Compact(ca, ra, t, dim);
-      Take(a.ApplyCompact(c, p), "b200 compact apply");
-      Take(b.ApplyCompact(c, p), "host compact apply");
+      if (round == 2 || round == 6) {
+        Rng ca{900u + round * 7 + t};
+        auto p = Compact(ca, ra, t, dim);
+        Take(a.ApplyCompact(c, p), "b200 compact apply");
+        Take(b.ApplyCompact(c, p), "host compact apply");
+      } else {
+        Rng ga{500u + round * 7 + t};
+        auto g = Gradients(ga, ra, t, dim, t == 1 ? 0.01f : 0.5f);
+        Take(a.ApplyHost(c, g), "b200 apply");
+        Take(b.ApplyHost(c, g), "host apply");
+      }
     }
     CompareStates(a, b, ra, rb, "after update round " + std::to_string(round));
   }
@@ -327,10 +335,10 @@ void BackendContract() {
   {
     auto c = Context(1, 9, 0.01f, 0.9f, 0.999f);
     Rng g1{31};
-    auto g = Gradients(g1, ra, 1, 8, 0.01f);
+    auto g = Gradients(g1, ra, 1, kDim1, 0.01f);
     auto dup = g;
     dup.rows.push_back(g.rows.front());
-    dup.values.insert(dup.values.end(), g.values.begin(), g.values.begin() + 8);
+    dup.values.insert(dup.values.end(), g.values.begin(), g.values.begin() + kDim1);
     SameRejection(a.ApplyHost(c, dup), b.ApplyHost(c, dup), "duplicate gradient row");
     auto overflow = g;
     overflow.values[5] = 1e30f;                 // (1 - beta2) g^2 overflows the second moment
@@ -341,7 +349,7 @@ void BackendContract() {
     auto other = c;
     other.shard = 1;
     SameRejection(a.ApplyHost(other, g), b.ApplyHost(other, g), "gradient for another shard");
-    RowGradients absent{{{1, 33}}, std::vector<float>(8, 0.001f)};
+    RowGradients absent{{{1, 33}}, std::vector<float>(kDim1, 0.001f)};
     SameRejection(a.ApplyHost(c, absent), b.ApplyHost(c, absent), "gradient of a row not resident");
     auto bad_power = c;
     bad_power.beta1_power = 1.0f;
@@ -489,6 +497,66 @@ void ServiceDropIn() {
   Take(cb.Release(b), "release");
 }
 
+// ---- GatherDevice (GPU only): the device results equal the host backend's
+// gather, are ready on a consumer stream after WaitOnStream, and outlive the
+// agent that made them (tests/cuda_tests.cpp checks the same lifetime).
+bool DeviceResults() {
+  int devices = 0;
+  if (cudaGetDeviceCount(&devices) != cudaSuccess || devices == 0) {
+    cudaGetLastError();
+    return false;
+  }
+  Rng r{2468};
+  B200CacheOptions o;
+  o.rows_per_table = 64;
+  auto a = std::make_shared<B200CacheAgent>(o);
+  HostCacheBackend b(0, 1 << 20);
+  for (auto t : {Table1(), Table2()}) {
+    Take(a->Define(t), "b200 define");
+    Take(b.Define(t), "host define");
+  }
+  std::vector<LocatedRow> plan_rows;
+  std::vector<RowState> states;
+  for (Key k = 0; k < 25; ++k) {
+    plan_rows.push_back({{1, k}, 0, Placement::loading, 0, 1, 0});
+    states.push_back(RandomState(r, {1, k}, kDim1));
+  }
+  for (Key k = 100; k < 112; ++k) {
+    plan_rows.push_back({{2, k}, 0, Placement::loading, 0, 1, 0});
+    states.push_back(RandomState(r, {2, k}, kDim2));
+  }
+  auto la = Take(a->Load(Plan(plan_rows, Placement::gpu), states), "b200 load");
+  auto lb = Take(b.Load(Plan(plan_rows, Placement::gpu), states), "host load");
+  Residency ra, rb;
+  for (std::size_t i = 0; i < la.size(); ++i) {
+    ra[{la[i].row.table, la[i].row.key}] = la[i];
+    rb[{lb[i].row.table, lb[i].row.key}] = lb[i];
+  }
+  Rng fr{31337};
+  auto features = MakeFeatures(fr);
+  Rng wa{3}, wb{3};
+  auto work_a = MakeWork(features, ra, wa);
+  auto work_b = MakeWork(features, rb, wb);
+  auto device = Take(a->GatherDevice(work_a, Layouts(features)), "b200 device gather");
+  auto expected = Take(b.GatherHost(work_b, Layouts(features)), "host gather");
+  cudaStream_t consumer = nullptr;
+  Check(cudaStreamCreateWithFlags(&consumer, cudaStreamNonBlocking) == cudaSuccess, "stream");
+  std::vector<TensorBlock> got;
+  for (const auto& d : device) {
+    d.tensor->WaitOnStream(consumer);
+    Check(d.tensor->elements() == d.shape[0] * d.shape[1], "device tensor size");
+    got.push_back({d.feature, d.shape, d.tensor->CopyToHost()});
+  }
+  Check(cudaStreamSynchronize(consumer) == cudaSuccess, "consumer stream");
+  cudaStreamDestroy(consumer);
+  CompareBlocks(got, expected, "device gather");
+  a.reset();                                     // the results outlive the agent
+  got.clear();
+  for (const auto& d : device) got.push_back({d.feature, d.shape, d.tensor->CopyToHost()});
+  CompareBlocks(got, expected, "device gather after the agent is gone");
+  return true;
+}
+
 // ---- the agent process's command layer over each backend
 template <typename T>
 T Both(std::future<Result<T>> a, std::future<Result<T>> b, const std::string& what) {
@@ -551,6 +619,7 @@ int main() {
     BackendContract();
     ServiceDropIn();
     RuntimeReplay();
+    if (!DeviceResults()) std::cout << "agent_check: no GPU, device results not checked\n";
     std::cout << "agent_check: PASS backend contract, service drop-in and agent runtime, "
                  "bit-exact vs HostCacheBackend\n";
     return 0;
