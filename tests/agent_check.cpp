@@ -30,6 +30,8 @@
 #include <stdexcept>
 #include <string>
 #include <type_traits>
+#include <utility>
+#include <variant>
 #include <vector>
 
 #include <cuda_runtime_api.h>
@@ -497,6 +499,50 @@ void ServiceDropIn() {
   Take(cb.Release(b), "release");
 }
 
+// ---- slot and budget limits, as the reference's CUDA backend enforces them
+// (src/cuda/cache_backend.cu:353-371,378-404): a load that does not fit, or
+// that would eat the plan's reserve, is refused whole and changes nothing.
+void Capacity() {
+  B200CacheOptions o;
+  o.rows_per_table = 4;
+  o.state_bytes = 4 * (std::uint64_t(kDim1) * 12 + 8) + 100;   // one table of 4 slots
+  B200CacheAgent a(o);
+  Take(a.Define(Table1()), "define");
+  auto refused = a.Define(Table2()).get();
+  Check(std::holds_alternative<Error>(refused) &&
+            std::get<Error>(refused).code == Error::Code::capacity_exceeded,
+        "a table over the state budget was accepted");
+  Rng r{99};
+  auto plan = [&](Key first, Key count, std::uint64_t reserve) {
+    std::vector<LocatedRow> rows;
+    std::vector<RowState> states;
+    for (Key k = first; k < first + count; ++k) {
+      rows.push_back({{1, k}, 0, Placement::loading, 0, 1, 0});
+      states.push_back(RandomState(r, {1, k}, kDim1));
+    }
+    auto p = Plan(rows, Placement::gpu);
+    p.reserve_slots = reserve;
+    return std::make_pair(p, states);
+  };
+  auto [five, five_states] = plan(0, 5, 0);
+  auto over = a.Load(five, five_states).get();
+  Check(std::holds_alternative<Error>(over) &&
+            std::get<Error>(over).code == Error::Code::capacity_exceeded,
+        "a load over the slot count was accepted");
+  Check(Take(a.FreeSlots(1), "free slots") == 4, "a refused load kept slots");
+  auto [three, three_states] = plan(10, 3, 2);
+  auto reserved = a.Load(three, three_states).get();
+  Check(std::holds_alternative<Error>(reserved) &&
+            std::get<Error>(reserved).code == Error::Code::capacity_exceeded,
+        "a load into the reserve was accepted");
+  auto [two, two_states] = plan(10, 2, 2);
+  auto loaded = Take(a.Load(two, two_states), "load within the reserve");
+  Check(Take(a.FreeSlots(1), "free slots") == 2, "slots after a load");
+  auto back = Take(a.ReadBack(Plan(loaded, Placement::cpu)), "readback");
+  Check(SameBits(back[1].weights, two_states[1].weights) && back[1].row_updates == two_states[1].row_updates,
+        "loaded state differs");
+}
+
 // ---- GatherDevice (GPU only): the device results equal the host backend's
 // gather, are ready on a consumer stream after WaitOnStream, and outlive the
 // agent that made them (tests/cuda_tests.cpp checks the same lifetime).
@@ -619,6 +665,7 @@ int main() {
     BackendContract();
     ServiceDropIn();
     RuntimeReplay();
+    Capacity();
     if (!DeviceResults()) std::cout << "agent_check: no GPU, device results not checked\n";
     std::cout << "agent_check: PASS backend contract, service drop-in and agent runtime, "
                  "bit-exact vs HostCacheBackend\n";
