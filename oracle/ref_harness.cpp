@@ -9,6 +9,7 @@
 // the product.
 //
 // Exposes a small C interface so Python (ctypes) can call it.
+#include <algorithm>
 #include <chrono>
 #include <cstring>
 #include <map>
@@ -20,6 +21,10 @@
 #include "eps/distributed_client.hpp"
 #include "eps/prepared_lookup.hpp"
 #include "eps/runtime.hpp"
+#ifdef EPS_REF_CUDA
+#include "eps/cache_resolver.hpp"
+#include "eps/cuda_cache_backend.hpp"
+#endif
 
 using namespace eps;
 
@@ -31,6 +36,7 @@ struct Harness {
   std::uint64_t sequence = 0;
   std::string run = "oracle";
   std::uint32_t learner = 0;
+  std::shared_ptr<CacheBackend> agent;   // the reference's CUDA backend, when attached
 };
 
 void Message(char* err, const std::string& text) {
@@ -212,5 +218,48 @@ int rh_stats(void* p, std::uint64_t* out4, char* err) {
   }
   return 0;
 }
+
+
+#ifdef EPS_REF_CUDA
+// The reference's own GPU path on one GPU (libeps_ref_cuda.so only): its
+// CudaCacheBackend (src/cuda/cache_backend.cu, compiled from the reference
+// sources for sm_100a) attached to the single shard as agent 0, the given rows
+// of `table` migrated to it with MoveRows, and the client's gathers resolved
+// through the reference's MakeCacheResolver -- the wiring of the reference's
+// tests/cache_tests.cpp:45-49 with the CUDA backend in place of the host one.
+// Lookups and pushes of those rows then run the reference's CUDA kernels.
+int rh_attach_cuda(void* p, std::int32_t device, std::uint64_t rows_per_table,
+                   std::uint64_t state_bytes, std::uint32_t table, std::uint32_t dimension,
+                   const std::uint64_t* keys, std::uint64_t key_count, char* err) {
+  auto& h = *static_cast<Harness*>(p);
+  if (h.shards.size() != 1) { Message(err, "the CUDA agent path runs one shard"); return 1; }
+  try {
+    CudaCacheOptions o;
+    o.agent = 0;
+    o.device = device;
+    o.state_bytes = state_bytes;
+    o.rows_per_table = rows_per_table;
+    o.transfer_bytes = 64ULL << 20;               // the backend's maximum staging
+    o.outstanding_output_bytes = 1ULL << 30;
+    auto backend = std::make_shared<CudaCacheBackend>(o);
+    Ack ack;
+    if (int rc = Take(h.shards[0]->AttachAgent(0, backend).get(), &ack, err)) return rc;
+    if (int rc = Take(h.shards[0]->ConfigureAccess(0, AccessRoute::transfer_unique).get(), &ack, err))
+      return rc;
+    h.agent = backend;
+    h.client->SetCacheResolver(MakeCacheResolver({{0, backend}}));
+    // migrate in chunks that fit the backend's staging buffer
+    const std::uint64_t chunk = std::max<std::uint64_t>(1, (16ULL << 20) / (12ULL * dimension + 8));
+    for (std::uint64_t i = 0; i < key_count; i += chunk) {
+      std::vector<RowKey> rows;
+      for (std::uint64_t k = i; k < std::min(key_count, i + chunk); ++k) rows.push_back({table, keys[k]});
+      MoveRowsRequest move{h.run, std::move(rows), 0, Placement::gpu, {1ULL << 40, 64ULL << 20, 8, 0}};
+      std::vector<LocatedRow> moved;
+      if (int rc = Take(h.shards[0]->MoveRows(std::move(move)).get(), &moved, err)) return rc;
+    }
+    return 0;
+  } catch (const std::exception& e) { Message(err, e.what()); return int(Error::Code::run_failed) + 1; }
+}
+#endif
 
 }  // extern "C"

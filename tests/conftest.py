@@ -1,6 +1,8 @@
 """Shared test setup.
 
-* registers the ``gpu`` marker (tests that need a B200; run with ``-m gpu``);
+* registers the ``gpu`` marker (tests that need a B200; run with ``-m gpu``) and
+  the ``refgpu`` marker (the reference's own CUDA backend measured on a GPU;
+  run with ``-m refgpu``);
 * imports the package directory ``distributed-recommendation-model-training-system_b200``
   (its name is not a Python identifier) under the module name ``eps_b200``;
 * makes the CPU checkers (oracle/) importable as ``oracle_lib``.
@@ -21,6 +23,8 @@ sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA B200 GPU")
+    config.addinivalue_line("markers", "refgpu: measures the reference's own CUDA backend on a "
+                            "GPU (run explicitly with -m refgpu; skipped without a GPU)")
 
 
 def import_package():

@@ -18,6 +18,8 @@ import numpy as np
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 ORACLE_SO = os.path.join(ROOT, "oracle", "_build", "libeps_oracle.so")
 REF_SO = os.path.join(ROOT, "oracle", "_ref", "libeps_ref.so")
+# the same harness with the reference's CUDA cache backend linked in (make ref-cuda)
+REF_CUDA_SO = os.path.join(ROOT, "oracle", "_ref", "libeps_ref_cuda.so")
 
 SUM, MEAN, SEQUENCE = 0, 1, 2
 
@@ -261,8 +263,9 @@ class Reference:
     """The reference's own CPU path (CpuParameterService x n + DistributedClient)."""
 
     def __init__(self, tables: list[TableDef], shards: int = 1, state_bytes: int = 8 << 30,
-                 run: str | None = None, snapshot_dir: str | None = None, define: bool = True):
-        self.lib = _load(REF_SO)
+                 run: str | None = None, snapshot_dir: str | None = None, define: bool = True,
+                 library: str = REF_SO):
+        self.lib = _load(library)
         self.lib.rh_create_run.restype = C.c_void_p
         self.lib.rh_create_run.argtypes = [C.c_uint32, C.c_uint64, C.c_char_p, C.c_char_p,
                                            C.c_char_p]
@@ -289,6 +292,18 @@ class Reference:
                           1 if t.bounds else 0, *(t.bounds if t.bounds else (0.0, 0.0)),
                           t.init_min, t.init_max, t.init_seed)
             self._check(self.lib.rh_create_table(C.c_void_p(self.h), C.byref(rt), self.err))
+
+    def attach_cuda(self, tid, keys, device=0, rows_per_table=1 << 24, state_bytes=64 << 30):
+        """The reference's GPU path (library=REF_CUDA_SO, one shard): its
+        CudaCacheBackend attached as agent 0 and the rows `keys` of table `tid`
+        moved to it; the rows must exist (a lookup has touched them)."""
+        fn = self.lib.rh_attach_cuda
+        fn.restype = C.c_int
+        fn.argtypes = [C.c_void_p, C.c_int32, C.c_uint64, C.c_uint64, C.c_uint32, C.c_uint32,
+                       C.c_void_p, C.c_uint64, C.c_char_p]
+        k = _u64(keys)
+        self._check(fn(C.c_void_p(self.h), device, rows_per_table, state_bytes, tid,
+                       self._defs[tid].dimension, k.ctypes.data, len(k), self.err))
 
     def close(self):
         if self.h:
