@@ -227,27 +227,31 @@ int rh_stats(void* p, std::uint64_t* out4, char* err) {
 // of `table` migrated to it with MoveRows, and the client's gathers resolved
 // through the reference's MakeCacheResolver -- the wiring of the reference's
 // tests/cache_tests.cpp:45-49 with the CUDA backend in place of the host one.
-// Lookups and pushes of those rows then run the reference's CUDA kernels.
+// Lookups and pushes of those rows then run the reference's CUDA kernels.  The
+// backend is attached by the first call; later calls migrate more rows (of any
+// table) to it.
 int rh_attach_cuda(void* p, std::int32_t device, std::uint64_t rows_per_table,
                    std::uint64_t state_bytes, std::uint32_t table, std::uint32_t dimension,
                    const std::uint64_t* keys, std::uint64_t key_count, char* err) {
   auto& h = *static_cast<Harness*>(p);
   if (h.shards.size() != 1) { Message(err, "the CUDA agent path runs one shard"); return 1; }
   try {
-    CudaCacheOptions o;
-    o.agent = 0;
-    o.device = device;
-    o.state_bytes = state_bytes;
-    o.rows_per_table = rows_per_table;
-    o.transfer_bytes = 64ULL << 20;               // the backend's maximum staging
-    o.outstanding_output_bytes = 1ULL << 30;
-    auto backend = std::make_shared<CudaCacheBackend>(o);
-    Ack ack;
-    if (int rc = Take(h.shards[0]->AttachAgent(0, backend).get(), &ack, err)) return rc;
-    if (int rc = Take(h.shards[0]->ConfigureAccess(0, AccessRoute::transfer_unique).get(), &ack, err))
-      return rc;
-    h.agent = backend;
-    h.client->SetCacheResolver(MakeCacheResolver({{0, backend}}));
+    if (!h.agent) {                               // attached once; later calls only migrate
+      CudaCacheOptions o;
+      o.agent = 0;
+      o.device = device;
+      o.state_bytes = state_bytes;
+      o.rows_per_table = rows_per_table;
+      o.transfer_bytes = 64ULL << 20;             // the backend's maximum staging
+      o.outstanding_output_bytes = 1ULL << 30;
+      auto backend = std::make_shared<CudaCacheBackend>(o);
+      Ack ack;
+      if (int rc = Take(h.shards[0]->AttachAgent(0, backend).get(), &ack, err)) return rc;
+      if (int rc = Take(h.shards[0]->ConfigureAccess(0, AccessRoute::transfer_unique).get(), &ack, err))
+        return rc;
+      h.agent = backend;
+      h.client->SetCacheResolver(MakeCacheResolver({{0, backend}}));
+    }
     // migrate in chunks that fit the backend's staging buffer
     const std::uint64_t chunk = std::max<std::uint64_t>(1, (16ULL << 20) / (12ULL * dimension + 8));
     for (std::uint64_t i = 0; i < key_count; i += chunk) {

@@ -9,13 +9,13 @@ the B200 path is compared with.
 * CPU: the library builds, and without a GPU attaching the backend fails with
   the reference's own CUDA error.
 * ``refgpu`` marker (run explicitly, ``-m refgpu``, on a B200; not part of
-  ``-m gpu``): pull + push rounds of cfg2 sub-batches (batch 1024: the backend
+  ``-m gpu``): pull + push rounds of cfg1 and of cfg2 sub-batches (batch 1024: the backend
   stages at most 64 MiB and 16 MiB compact packets per call,
   src/cuda/cache_backend.cu:212-214, src/access/compact_gradients.cpp:15) through
   that path, timed on the host clock as the API is synchronous; the pulls must
   match the reference's CPU path within the reference CUDA test's tolerance
-  (1e-5, tests/cuda_tests.cpp:14).  Prints one JSON line, also written to
-  $EPS_REF_CUDA_OUT/ref_cuda.json when that variable names a folder."""
+  (1e-5, tests/cuda_tests.cpp:14).  Prints one JSON line per config, also written
+  to $EPS_REF_CUDA_OUT/ref_cuda_<config>.json when that variable names a folder."""
 import json
 import os
 import subprocess
@@ -47,41 +47,50 @@ def library():
     return REF_CUDA_SO
 
 
-def cfg2_subbatch(workloads, batch, seed=2):
-    w = workloads.config2(seed=seed, batch=batch)
-    t = w.tables[0]
-    table = TableDef(id=t.id, dimension=t.dimension, learning_rate=1e-3, init_min=-0.05,
-                     init_max=0.05, init_seed=7, rows=t.rows)
+def as_reference(w):
+    tables = [TableDef(id=t.id, dimension=t.dimension, learning_rate=1e-3, init_min=-0.05,
+                       init_max=0.05, init_seed=7, rows=t.rows) for t in w.tables]
     feats = [Feature(f.table, f.feature, f.pooling, f.keys, f.offsets) for f in w.features]
-    return w, table, feats
+    return w, tables, feats
+
+
+def cfg2_subbatch(workloads, batch, seed=2):
+    return as_reference(workloads.config2(seed=seed, batch=batch))
 
 
 def test_reference_cuda_backend_fails_loudly_without_a_gpu(workloads):
     if gpu_present():
         pytest.skip("a GPU is present: the measurement runs under -m refgpu")
     lib = library()
-    w, table, feats = cfg2_subbatch(workloads, 16)
-    ref = Reference([table], shards=1, library=lib)
+    w, tables, feats = cfg2_subbatch(workloads, 16)
+    ref = Reference(tables, shards=1, library=lib)
     batch, _ = ref.lookup(feats, read_only=True)
     ref.release(batch)
     with pytest.raises(ValueError, match="reference rejected"):
-        ref.attach_cuda(table.id, np.unique(np.concatenate([f.keys for f in feats]))[:8])
+        ref.attach_cuda(tables[0].id, np.unique(np.concatenate([f.keys for f in feats]))[:8])
     ref.close()
 
 
 @pytest.mark.refgpu
-def test_reference_cuda_backend_rounds(workloads):
+@pytest.mark.parametrize("config", ["cfg1", "cfg2-1024"])
+def test_reference_cuda_backend_rounds(workloads, config):
     if not gpu_present():
         pytest.skip("needs a GPU")
     lib = library()
-    batch_size, warmup, steps = 1024, 3, 10
-    w, table, feats = cfg2_subbatch(workloads, batch_size)
-    keys = np.unique(np.concatenate([f.keys for f in feats]))
-    ref = Reference([table], shards=1, library=lib)
-    cpu = Reference([table], shards=1)
+    warmup, steps = 3, (100 if config == "cfg1" else 10)
+    if config == "cfg1":
+        w, tables, feats = as_reference(workloads.config1())
+    else:
+        w, tables, feats = cfg2_subbatch(workloads, 1024)
+    ref = Reference(tables, shards=1, library=lib)
+    cpu = Reference(tables, shards=1)
     b0, _ = ref.lookup(feats, read_only=True)     # creates the rows on the shard
     ref.release(b0)
-    ref.attach_cuda(table.id, keys)
+    unique = 0
+    for t in tables:
+        keys = np.unique(np.concatenate([f.keys for f in feats if f.table == t.id]))
+        ref.attach_cuda(t.id, keys)
+        unique += len(keys)
     # first round against the CPU path
     b1, outs_gpu = ref.lookup(feats)
     c1, outs_cpu = cpu.lookup(feats)
@@ -109,13 +118,13 @@ def test_reference_cuda_backend_rounds(workloads):
         np.testing.assert_allclose(g, c, rtol=1e-5, atol=1e-5)
     line = {"impl": "reference-cuda-backend", "metric": "embedding rows/s per round (pull+push+Adam)",
             "value": w.occurrences / dt, "unit": "rows/s", "ms_per_round": dt * 1e3,
-            "workload": f"cfg2 sub-batch: batch {batch_size}, {w.occurrences} occurrences, "
-                        f"{len(keys)} unique rows, all resident on the GPU",
+            "workload": f"{config}: {w.occurrences} occurrences, {unique} unique rows, "
+                        f"all resident on the GPU ({w.name})",
             "steps": steps, "warmup": warmup, "timing": "host clock around synchronous API calls"}
     print(json.dumps(line))
     out = os.environ.get("EPS_REF_CUDA_OUT")
     if out and os.path.isdir(out):
-        with open(os.path.join(out, "ref_cuda.json"), "w") as f:
+        with open(os.path.join(out, f"ref_cuda_{config}.json"), "w") as f:
             f.write(json.dumps(line) + "\n")
     ref.close()
     cpu.close()
