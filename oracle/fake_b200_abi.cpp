@@ -16,7 +16,8 @@
 //   load_state        finite state, v >= 0, all-or-nothing
 //   read_state
 //   apply_rows        host values, external powers (eo_apply_host), all-or-nothing
-//   apply_compact     ExpandCompactGradients then apply_rows
+//   apply_compact     packet checks of ValidateCompactGradients, ExpandCompactGradients,
+//                     then apply_rows
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -207,8 +208,11 @@ int eps_b200_apply_compact(EpsB200Store* s, const EpsB200UpdateContext* c,
     if (g->row_offsets[r] > g->row_offsets[r + 1])
       return Fail(st, EPS_B200_INVALID_ARGUMENT, "invalid compact gradient packet");
   for (uint64_t k = 0; k < g->refs; ++k)
-    if (g->source_rows[k] >= g->sources || !std::isfinite(g->scales[k]))
+    if (g->source_rows[k] >= g->sources || !std::isfinite(g->scales[k]) || g->scales[k] < 0)
       return Fail(st, EPS_B200_INVALID_ARGUMENT, "invalid compact gradient packet");
+  for (uint64_t j = 0; j < g->sources * g->dimension; ++j)
+    if (!std::isfinite(g->source_values[j]))
+      return Fail(st, EPS_B200_INVALID_ARGUMENT, "non-finite compact gradient value");
   std::vector<float> expanded(g->rows * g->dimension);
   if (eo_expand_compact(g->dimension, g->rows, g->source_values, g->sources, g->row_offsets,
                         g->source_rows, g->scales, expanded.data()))

@@ -372,6 +372,28 @@ void BackendContract() {
         if (task.route == AccessRoute::resident_gpu && !task.rows.empty()) ++task.rows[0].generation;
     SameRejection(a.GatherHost(work_a, Layouts(features)), b.GatherHost(work_b, Layouts(features)),
                   "gather of a stale generation");
+    // malformed compact packets (src/access/compact_gradients.cpp:10-22)
+    Rng pr{57};
+    const auto good = Compact(pr, ra, 1, kDim1);
+    Check(good.rows.size() >= 2 && good.source_rows.size() >= 2, "compact packet too small");
+    auto bad = [&](const char* what, auto mutate) {
+      auto p = good;
+      mutate(p);
+      SameRejection(a.ApplyCompact(c, p), b.ApplyCompact(c, p), std::string("compact: ") + what);
+    };
+    bad("offsets not from 0", [](CompactGradients& p) { p.row_offsets[0] = 1; });
+    bad("decreasing offsets", [](CompactGradients& p) { std::swap(p.row_offsets[1], p.row_offsets[2]); });
+    bad("offsets short", [](CompactGradients& p) { p.row_offsets.pop_back(); });
+    bad("source out of range", [](CompactGradients& p) { p.source_rows[1] = 7; });
+    bad("negative scale", [](CompactGradients& p) { p.scales[0] = -0.5f; });
+    bad("non-finite scale", [](CompactGradients& p) { p.scales[1] = std::nanf(""); });
+    bad("non-finite value", [](CompactGradients& p) { p.source_values[3] = INFINITY; });
+    bad("dimension mismatch", [](CompactGradients& p) { p.dimension = kDim1 / 2; });
+    bad("duplicate row", [](CompactGradients& p) {
+      p.rows.push_back(p.rows.front());
+      p.row_offsets.push_back(p.row_offsets.back());
+    });
+    CompareStates(a, b, ra, rb, "after rejected compact packets");
     SameRejection(a.CommitEviction(Plan({ra.begin()->second, ra.begin()->second}, Placement::cpu)),
                   b.CommitEviction(Plan({rb.begin()->second, rb.begin()->second}, Placement::cpu)),
                   "duplicate eviction row");
