@@ -16,7 +16,11 @@
 //   3. under the reference's AgentRuntime (include/eps/agent_runtime.hpp), the
 //      command layer its BRPC agent server dispatches to: retried commands
 //      replay their first result without applying twice, older commands are
-//      retired, and eviction reclaims the slots -- the same with either backend.
+//      retired, and eviction reclaims the slots -- the same with either backend;
+//   4. the adapter alone: slot, reserve and state-budget limits refused whole;
+//      calls from four threads (each result equals the single-thread one); and,
+//      on a machine with a GPU, GatherDevice results (equal to the host
+//      backend's gather, ordered on a consumer stream, outliving the agent).
 // Linked against the real library it checks the B200 path; linked against
 // oracle/fake_b200_abi.cpp it checks the adapter's host logic without a GPU.
 // Prints "agent_check: PASS ..." and exits 0, or names the first difference.
@@ -29,6 +33,7 @@
 #include <memory>
 #include <stdexcept>
 #include <string>
+#include <thread>
 #include <type_traits>
 #include <utility>
 #include <variant>
@@ -565,6 +570,54 @@ void Capacity() {
         "loaded state differs");
 }
 
+// ---- calls from several threads: the agent runs them one at a time in
+// submission order, so every thread's gathers equal the single-thread result
+void Concurrent() {
+  Rng r{4711};
+  B200CacheOptions o;
+  o.rows_per_table = 64;
+  auto a = std::make_shared<B200CacheAgent>(o);
+  for (auto t : {Table1(), Table2()}) Take(a->Define(t), "define");
+  std::vector<LocatedRow> plan_rows;
+  std::vector<RowState> states;
+  for (Key k = 0; k < 40; ++k) {
+    plan_rows.push_back({{1, k}, 0, Placement::loading, 0, 1, 0});
+    states.push_back(RandomState(r, {1, k}, kDim1));
+  }
+  for (Key k = 100; k < 124; ++k) {
+    plan_rows.push_back({{2, k}, 0, Placement::loading, 0, 1, 0});
+    states.push_back(RandomState(r, {2, k}, kDim2));
+  }
+  auto loaded = Take(a->Load(Plan(plan_rows, Placement::gpu), states), "load");
+  Residency ra;
+  for (const auto& loc : loaded) ra[{loc.row.table, loc.row.key}] = loc;
+  Rng fr{8}, wr{8};
+  auto features = MakeFeatures(fr);
+  auto work = MakeWork(features, ra, wr);
+  const auto expected = Take(a->GatherHost(work, Layouts(features)), "gather");
+  const auto state = Take(a->ReadBack(Plan(Rows(ra), Placement::cpu)), "readback");
+  std::vector<std::string> failures(4);
+  std::vector<std::thread> threads;
+  for (int t = 0; t < 4; ++t)
+    threads.emplace_back([&, t] {
+      try {
+        for (int i = 0; i < 25; ++i) {
+          CompareBlocks(Take(a->GatherHost(work, Layouts(features)), "gather"), expected,
+                        "concurrent gather");
+          if (i % 5 == 0) {
+            auto again = Take(a->ReadBack(Plan(Rows(ra), Placement::cpu)), "readback");
+            Check(again.size() == state.size() && SameBits(again.back().weights, state.back().weights),
+                  "concurrent readback");
+          }
+        }
+      } catch (const std::exception& e) {
+        failures[t] = e.what();
+      }
+    });
+  for (auto& th : threads) th.join();
+  for (const auto& f : failures) Check(f.empty(), f);
+}
+
 // ---- GatherDevice (GPU only): the device results equal the host backend's
 // gather, are ready on a consumer stream after WaitOnStream, and outlive the
 // agent that made them (tests/cuda_tests.cpp checks the same lifetime).
@@ -688,6 +741,7 @@ int main() {
     ServiceDropIn();
     RuntimeReplay();
     Capacity();
+    Concurrent();
     if (!DeviceResults()) std::cout << "agent_check: no GPU, device results not checked\n";
     std::cout << "agent_check: PASS backend contract, service drop-in and agent runtime, "
                  "bit-exact vs HostCacheBackend\n";
