@@ -235,12 +235,14 @@ struct B200CacheAgent::Impl {
   }
   ~Impl() {
     if (worker) worker->Stop();
+    // the store synchronizes the last stream it ran on when it is destroyed, so
+    // that stream (GatherDevice's) must outlive the store
+    eps_b200_destroy(store);
     if (stream) {
       cudaSetDevice(options.device);
       cudaStreamSynchronize(stream);
       cudaStreamDestroy(stream);
     }
-    eps_b200_destroy(store);
   }
 
   Table& Get(TableId id) {

@@ -155,6 +155,9 @@ EPS_B200_EXPORT uint32_t eps_b200_abi_version(void);
  * eps::CpuParameterService (include/eps/runtime.hpp:104) /
  * eps::CudaCacheBackend (include/eps/cuda_cache_backend.hpp:19). */
 EPS_B200_EXPORT int eps_b200_create(const EpsB200Options* options, EpsB200Store** out, EpsB200Status* status);
+/* Waits for the store's work, on its own streams and on the last caller stream
+ * it ran on, then frees it: a stream passed to the store must stay valid until
+ * the store is destroyed (or a later call has run on another stream). */
 EPS_B200_EXPORT void eps_b200_destroy(EpsB200Store* store);
 
 /* ParameterService::CreateTable (include/eps/parameter_service.hpp:16),

@@ -24,7 +24,11 @@
 // Linked against the real library it checks the B200 path; linked against
 // oracle/fake_b200_abi.cpp it checks the adapter's host logic without a GPU.
 // Prints "agent_check: PASS ..." and exits 0, or names the first difference.
+#include <execinfo.h>
+#include <unistd.h>
+
 #include <cmath>
+#include <csignal>
 #include <cstdint>
 #include <cstring>
 #include <future>
@@ -735,14 +739,36 @@ void RuntimeReplay() {
 
 }  // namespace
 
+// A crash prints the stack (addresses resolve with addr2line against this
+// binary and the libraries it loads) instead of ending the run silently.
+void OnFatalSignal(int sig) {
+  void* frames[64];
+  const int n = backtrace(frames, 64);
+  const char head[] = "agent_check: fatal signal, stack:\n";
+  (void)!write(2, head, sizeof(head) - 1);
+  backtrace_symbols_fd(frames, n, 2);
+  _exit(128 + sig);
+}
+
+void Part(const char* name) { std::cerr << "agent_check: " << name << std::endl; }
+
 int main() {
+  std::signal(SIGSEGV, OnFatalSignal);
+  std::signal(SIGABRT, OnFatalSignal);
   try {
+    Part("backend contract");
     BackendContract();
+    Part("service drop-in");
     ServiceDropIn();
+    Part("agent runtime");
     RuntimeReplay();
+    Part("capacity");
     Capacity();
+    Part("concurrent calls");
     Concurrent();
+    Part("device results");
     if (!DeviceResults()) std::cout << "agent_check: no GPU, device results not checked\n";
+    Part("done");
     std::cout << "agent_check: PASS backend contract, service drop-in and agent runtime, "
                  "bit-exact vs HostCacheBackend\n";
     return 0;

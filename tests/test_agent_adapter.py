@@ -8,8 +8,9 @@ bit-identical results and equal error codes.  Here it is linked against
 oracle/fake_b200_abi.cpp, a CPU stand-in of the C ABI built on the oracle, so
 the adapter's host logic (residency map, slots, generations, budgets, skipped
 occurrences as padding keys, error mapping) is checked without a GPU.  Linked
-against the real libeps_b200.so on a machine without a GPU, the adapter must
-fail loudly at construction (no CPU fallback).
+against the real libeps_b200.so it is the GPU test of the adapter (``-m gpu``:
+the same calls plus GatherDevice on a B200); on a machine without a GPU that
+build must fail loudly at construction (no CPU fallback).
 
 The programs link the reference compiled from its sources (oracle/_ref), so
 they are built only where the reference's headers are present."""
@@ -54,3 +55,16 @@ def test_adapter_on_the_real_library_fails_loudly_without_a_gpu():
     r = subprocess.run([exe], capture_output=True, text=True, timeout=300)
     assert r.returncode == 1
     assert "agent_check: FAIL B200 cache agent:" in r.stderr, r.stdout + r.stderr
+
+
+@pytest.mark.gpu
+def test_adapter_on_the_real_library_matches_host_cache_backend():
+    exe = os.path.join(OUT, "agent_check")
+    if os.path.isdir(os.path.join(REF, "include", "eps")):
+        exe = build("agent", "agent_check")
+    if not os.path.exists(exe):
+        pytest.skip("agent_check is built where the reference's headers are present")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "agent_check: PASS" in r.stdout
+    assert "device results not checked" not in r.stdout      # GatherDevice ran
