@@ -252,8 +252,10 @@ int rh_attach_cuda(void* p, std::int32_t device, std::uint64_t rows_per_table,
       h.agent = backend;
       h.client->SetCacheResolver(MakeCacheResolver({{0, backend}}));
     }
-    // migrate in chunks that fit the backend's staging buffer
-    const std::uint64_t chunk = std::max<std::uint64_t>(1, (16ULL << 20) / (12ULL * dimension + 8));
+    // migrate in chunks within the service's 4096 rows per MoveRows
+    // (src/server/service.cpp:394) and the backend's staging buffer
+    const std::uint64_t chunk = std::min<std::uint64_t>(
+        4096, std::max<std::uint64_t>(1, (16ULL << 20) / (12ULL * dimension + 8)));
     for (std::uint64_t i = 0; i < key_count; i += chunk) {
       std::vector<RowKey> rows;
       for (std::uint64_t k = i; k < std::min(key_count, i + chunk); ++k) rows.push_back({table, keys[k]});

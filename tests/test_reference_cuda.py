@@ -16,6 +16,7 @@ the B200 path is compared with.
   match the reference's CPU path within the reference CUDA test's tolerance
   (1e-5, tests/cuda_tests.cpp:14).  Prints one JSON line per config, also written
   to $EPS_REF_CUDA_OUT/ref_cuda_<config>.json when that variable names a folder."""
+import ctypes
 import json
 import os
 import subprocess
@@ -31,10 +32,13 @@ REF = os.environ.get("EPS_REFERENCE", "/root/reference")
 
 
 def gpu_present():
+    """A CUDA device answers (asked of the driver directly: no framework start-up)."""
     try:
-        import torch
-        return torch.cuda.is_available()
-    except ImportError:
+        cuda = ctypes.CDLL("libcuda.so.1")
+        count = ctypes.c_int(0)
+        return cuda.cuInit(0) == 0 and cuda.cuDeviceGetCount(ctypes.byref(count)) == 0 \
+            and count.value > 0
+    except OSError:
         return False
 
 
