@@ -5,30 +5,41 @@ One *round* (= one bench step) over the configured synthetic batch is: one
 lookup (gather + sum/mean pooling of every feature, occurrence list and its
 coalescing sort) and one push (gradient prescan, coalesced segment-sum fused
 with the sparse LazyAdam update, finalize).  rows = id occurrences processed per
-round (each is pulled once and contributes one gradient).
+round (each is pulled once and contributes one gradient).  Config 4 is the
+push-heavy stress: at N = 1 its round is timed without the gather (a push-only
+lookup builds the occurrence list and the coalescing sort -- the dedup -- then
+the push runs), as BASELINE.json specifies (dedup + segment-sum + Adam only).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--config 1|2|4]
+                    [--config 1|2|3|4|5] [--no-check] [--no-cpu-baseline]
 
-value  : rows/s with inputs resident in HBM, device-timed with CUDA events on
-         the launching stream, L2 flushed (256 MiB write) before every timed
-         round, summed over the K rounds; max over ranks when N > 1.
-e2e    : the same rounds through the C ABI with HOST (pinned) buffers: keys and
-         offsets copied in, pooled outputs copied out, gradients copied in and
-         the push status read back, all inside the timed region.
+value  : rows/s of the whole job (every rank's batch) with inputs resident in
+         HBM, device-timed with CUDA events on the launching stream, L2 flushed
+         (256 MiB write) before every timed round; max over ranks when N > 1.
+e2e    : the same rounds through the public API with HOST (pinned) buffers:
+         keys and offsets copied in, pooled outputs copied out, gradients copied
+         in and the push status read back, all inside the timed region.
 roofline: the dominant kernel (the longest single-launch phase with compulsory
-         HBM bytes: gather, row updates or prescan) -- its algorithmic bytes per
-         launch (byte_model) over its CUDA-event duration, timed by the
+         HBM bytes: gather, row updates or prescan) -- the bytes it must move per
+         launch (owner-side at N > 1) over its CUDA-event duration, timed by the
          library's phase events in a separate profiled pass of the same rounds,
          against the measured HBM copy bandwidth in MEASURED_PEAKS.json.
+parity : one round from freshly initialised tables checked against the
+         unmodified reference CPU parameter server (oracle/_ref) serving the same
+         job with the same shard count (tests/round_check.py): outputs and the
+         rows with <= 64 occurrences bit-exact, longer rows within 1e-6 of their
+         sum of |terms|; at N = 1 also the bit-exact mode
+         (EPS_B200_FLAG_REFERENCE_ORDER), every row bit-exact.  Runs after all
+         timing, never inside a timed region.
 cpu_baseline / --impl reference: the UNMODIFIED reference CPU parameter server
          (oracle/_ref, compiled from its own sources) with one shard per host
-         core behind its DistributedClient, timed wall-clock on the same batch.
+         core behind its DistributedClient, timed wall-clock on the same job.
 """
 from __future__ import annotations
 
 import argparse
 import gc
+import importlib.util
 import json
 import os
 import statistics
@@ -40,30 +51,32 @@ import time
 import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "distributed-recommendation-model-training-system_b200")
 sys.path.insert(0, os.path.join(ROOT, "tests"))
 METRIC = "embedding rows/s per round (pull+push+Adam)"
 UNIT = "rows/s"
 FALLBACK_HBM_GBS = 6650.0
+LONG_RUN = 64
 
 
-def _import_package():
-    import importlib.util
-    pkg = os.path.join(ROOT, "distributed-recommendation-model-training-system_b200")
+def _load(name, path, package=False):
+    if name in sys.modules:
+        return sys.modules[name]
+    kw = {"submodule_search_locations": [PKG]} if package else {}
+    spec = importlib.util.spec_from_file_location(name, path, **kw)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
 
-    def load(name, path, package=False):
-        if name in sys.modules:
-            return sys.modules[name]
-        kw = {"submodule_search_locations": [pkg]} if package else {}
-        spec = importlib.util.spec_from_file_location(name, path, **kw)
-        mod = importlib.util.module_from_spec(spec)
-        sys.modules[name] = mod
-        spec.loader.exec_module(mod)
-        return mod
 
-    workloads = load("eps_b200_workloads", os.path.join(pkg, "workloads.py"))
-    if os.environ.get("EPS_B200_NO_PACKAGE"):
-        return workloads, None
-    return workloads, load("eps_b200", os.path.join(pkg, "__init__.py"), package=True)
+def load_workloads():
+    """The synthetic input generators only (no library)."""
+    return _load("eps_b200_workloads", os.path.join(PKG, "workloads.py"))
+
+
+def load_package():
+    return _load("eps_b200", os.path.join(PKG, "__init__.py"), package=True)
 
 
 def parse():
@@ -72,10 +85,14 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 4])
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-check", action="store_true",
+                    help="skip the parity check against the reference after the timed rounds")
+    ap.add_argument("--no-bitexact", action="store_true",
+                    help="skip timing the bit-exact summation mode at N = 1")
     ap.add_argument("--rows", type=int, default=0,
-                    help="override the table rows of config 2 (smaller profiling captures)")
+                    help="override the table rows of config 2/4/5 (smaller profiling captures)")
     return ap.parse_args()
 
 
@@ -84,56 +101,118 @@ def dist_env():
             int(os.environ.get("WORLD_SIZE", 1)))
 
 
-def workload_for(wl, config, rank, rows=0):
+def cfg5_rows(world: int) -> int:
+    """Config 5's table: 1e9 x 32 when it fits, else the largest subset whose
+    state ([w|m|v] + counter, 392 B per row) split over `world` GPUs stays
+    within 150 GB per GPU."""
+    return int(min(1_000_000_000, world * 150_000_000_000 // 392))
+
+
+def workload_for(wl, config, rank, world, rows=0):
+    """Rank `rank`'s batch: every rank draws its own batch (seed per rank) from
+    the same id distribution (the config's shared id map and tables)."""
     if config == 1:
         return wl.config1(seed=1 + 1000 * rank)
+    if config == 2:
+        return wl.config2(seed=2 + 1000 * rank, rows=rows or 10_000_000)
+    if config == 3:
+        return wl.config3(seed=3 + 1000 * rank)
     if config == 4:
-        return wl.config4(seed=4 + 1000 * rank)
-    if rows:
-        return wl.config2(seed=2 + 1000 * rank, rows=rows)
-    return wl.config2(seed=2 + 1000 * rank)
+        return wl.config4(seed=4 + 1000 * rank, rows=rows or 100_000_000)
+    return wl.config5(seed=5 + 1000 * rank, rows=rows or cfg5_rows(world))
 
 
-def byte_model(w):
-    """Compulsory bytes (each byte that must cross HBM once; sort scratch excluded)."""
-    N = w.occurrences
-    rows_out = w.bags                                    # output / gradient rows
-    pooled_offsets = sum(len(f.offsets) for f in w.features if f.pooling != 2)
-    dims = {t.id: t.dimension for t in w.tables}
-    U_by_dim = {}
-    for t in w.tables:
-        ks = [f.keys for f in w.features if f.table == t.id]
-        if ks:
-            U_by_dim[t.id] = len(np.unique(np.concatenate(ks)))
-    U = sum(U_by_dim.values())
-    row_bytes_u = sum(4 * dims[t] * u for t, u in U_by_dim.items())        # 4D per unique row
-    out_bytes = sum(4 * dims[f.table] * f.output_rows for f in w.features)  # 4D per output row
-    pull = 8 * N + 8 * pooled_offsets + row_bytes_u + out_bytes
-    push = out_bytes + 8 * N + 8 * pooled_offsets + 6 * row_bytes_u + 16 * U
-    # per kernel: the gather moves the pull's bytes; the row-update kernel moves
-    # the read + write of [w|m|v] (12D each way) and the u64 counter of every
-    # row it updates (all rows except those with > 64 occurrences, which the
-    # long-row kernel updates); the prescan reads every gradient value once
-    long_rows = {}
-    for t in w.tables:
-        ks = [f.keys for f in w.features if f.table == t.id]
-        if ks:
-            _, c = np.unique(np.concatenate(ks), return_counts=True)
-            long_rows[t.id] = int((c > 64).sum())
-    rmw = {t: 24 * dims[t] + 16 for t in U_by_dim}
-    apply_kernel = sum(rmw[t] * (U_by_dim[t] - long_rows[t]) for t in U_by_dim)
-    long_kernel = sum(rmw[t] * long_rows[t] for t in U_by_dim)
-    return {"N": N, "U": U, "B": rows_out, "pull": pull, "push": push,
-            "lookup": pull, "apply": apply_kernel, "long": long_kernel, "prescan": out_bytes,
-            "sort": 0, "emit": 0, "pieces": 0, "finalize": 0,
-            "U_long": sum(long_rows.values())}
+def push_only(config, world):
+    return config == 4 and world == 1
 
 
-def dominant_kernel(prof, bm):
+# ------------------------------------------------------------------ byte model
+def _feature_rows(f):
+    return len(f.keys) if f.pooling == 2 else len(f.offsets) - 1
+
+
+def byte_model(tables, feats, world=1, rank=0):
+    """Compulsory bytes of one round (each byte that must cross HBM once; sort
+    scratch, exchange copies and re-reads excluded) of the job whose features
+    are `feats` (every rank's, rank-major), and the bytes the kernels of owner
+    `rank` move per launch: its keys, its unique rows, the partial rows it
+    serves (kept bags) and their gradients."""
+    dims = {t.id: t.dimension for t in tables}
+    N = sum(len(f.keys) for f in feats)
+    B = sum(_feature_rows(f) for f in feats)
+    pooled_offsets = sum(len(f.offsets) for f in feats if f.pooling != 2)
+    out_bytes = sum(4 * dims[f.table] * _feature_rows(f) for f in feats)
+    U, u_row_bytes = 0, 0
+    own = {"N": 0, "U": 0, "long": 0, "kept": 0, "kept_bytes": 0, "offsets": 0, "rows": 0,
+           "apply": 0, "longb": 0}
+    for t in tables:
+        ks = [f.keys for f in feats if f.table == t.id]
+        if not ks:
+            continue
+        uk, cnt = np.unique(np.concatenate(ks), return_counts=True)
+        U += len(uk)
+        u_row_bytes += 4 * t.dimension * len(uk)
+        mine = (uk % np.uint64(world)) == np.uint64(rank)
+        nu, nl = int(mine.sum()), int((mine & (cnt > LONG_RUN)).sum())
+        own["U"] += nu
+        own["long"] += nl
+        own["rows"] += 4 * t.dimension * nu
+        own["apply"] += (24 * t.dimension + 16) * (nu - nl)
+        own["longb"] += (24 * t.dimension + 16) * nl
+    for f in feats:
+        d = dims[f.table]
+        sel = (f.keys % np.uint64(world)) == np.uint64(rank)
+        own["N"] += int(sel.sum())
+        if f.pooling == 2:
+            kept = int(sel.sum())
+        elif world == 1:
+            kept = len(f.offsets) - 1
+            own["offsets"] += len(f.offsets)
+        else:
+            lengths = np.diff(f.offsets.astype(np.int64))
+            bag = np.repeat(np.arange(len(lengths)), lengths)
+            kept = len(np.unique(bag[sel]))
+            own["offsets"] += kept + 1
+        own["kept"] += kept
+        own["kept_bytes"] += 4 * d * kept
+    pull = 8 * N + 8 * pooled_offsets + u_row_bytes + out_bytes
+    push = out_bytes + 8 * N + 8 * pooled_offsets + 6 * u_row_bytes + 16 * U
+    owner = {"lookup": 8 * own["N"] + 8 * own["offsets"] + own["rows"] + own["kept_bytes"],
+             "apply": own["apply"], "long": own["longb"], "prescan": own["kept_bytes"]}
+    return {"N": N, "U": U, "B": B, "pull": pull, "push": push, "owner": owner,
+            "owner_U": own["U"], "owner_U_long": own["long"], "owner_N": own["N"]}
+
+
+def job_parts(wl, args, world):
+    return [workload_for(wl, args.config, r, world, args.rows) for r in range(world)]
+
+
+def job_features(parts):
+    """Every rank's features as the one combined request (ids r * F + f)."""
+    F = len(parts[0].features)
+    feats, grads = [], []
+    for r, p in enumerate(parts):
+        for f, g in zip(p.features, p.gradients):
+            feats.append(type(f)(f.table, r * F + f.feature, f.pooling, f.keys, f.offsets))
+            grads.append(g)
+    return feats, grads
+
+
+def job_config(parts, bm, config, world):
+    """The `config` object both arms print (identical for the same job)."""
+    only_push = push_only(config, world)
+    return {"workload": parts[0].name, "config": config, "batches": len(parts),
+            "occurrences_per_round": bm["N"], "unique_rows_per_round": bm["U"],
+            "output_rows_per_round": bm["B"],
+            "compulsory_bytes_per_round": bm["push"] if only_push else bm["pull"] + bm["push"],
+            "timed": ("push only: dedup (coalescing sort) + segment-sum + LazyAdam, no gather"
+                      if only_push else "pull + push + LazyAdam")}
+
+
+def dominant_kernel(prof, owner):
     """The roofline's kernel: the phase with the longest time per call among
-    those with compulsory HBM bytes in the byte model (gather, row updates, long
-    rows, prescan)."""
-    cands = [p for p in prof if bm.get(p) and prof[p]["ms"]]
+    those with compulsory HBM bytes (gather, row updates, long rows, prescan)."""
+    cands = [p for p in prof if owner.get(p) and prof[p]["ms"]]
     return max(cands, key=lambda p: prof[p]["ms"] / max(1, prof[p]["calls"]))
 
 
@@ -154,6 +233,24 @@ def load_traffic():
             return json.load(f)
     except Exception:
         return {}
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
 
 
 class Clocks:
@@ -231,71 +328,115 @@ class Clocks:
 
 
 # --------------------------------------------------------------- reference arm
-def reference_rounds(w, steps, warmup, threads):
-    """Times the reference's CPU path (oracle/_ref) on the batch; returns seconds per round."""
-    from oracle_lib import Feature, Reference, TableDef, reference_available
+def reference_rounds(parts, config, world, steps, warmup, threads, budget_s=60.0):
+    """Times the reference's CPU path (oracle/_ref: DistributedClient over
+    `threads` CpuParameterService shards) on the job: every rank's batch as one
+    combined request.  Push-only configs time the push alone.  Stops early (at
+    least 2 timed rounds) once `budget_s` of timed work is done.  Returns the
+    seconds of each timed round, or None without the reference build."""
+    from oracle_lib import Feature, Reference, reference_available
+    import round_check
     if not reference_available():
         return None
-    tables = [TableDef(id=t.id, dimension=t.dimension, learning_rate=1e-3, init_min=-0.05,
-                       init_max=0.05, init_seed=42, rows=t.rows) for t in w.tables]
-    feats = [Feature(f.table, f.feature, f.pooling, f.keys, f.offsets) for f in w.features]
-    ref = Reference(tables, shards=threads, state_bytes=64 << 30)
-    times = []
+    feats, grads = job_features(parts)
+    feats = [Feature(f.table, f.feature, f.pooling, f.keys, f.offsets) for f in feats]
+    ref = Reference(round_check.table_defs(parts[0]), shards=threads, state_bytes=256 << 30)
+    only_push = push_only(config, world)
+    times, spent = [], 0.0
     for i in range(warmup + steps):
         t0 = time.perf_counter()
         batch, _ = ref.lookup(feats)
-        ref.push(batch, feats, w.gradients)
+        if only_push:
+            t0 = time.perf_counter()
+        ref.push(batch, feats, grads)
         dt = time.perf_counter() - t0
         if i >= warmup:
             times.append(dt)
+            spent += dt
+            if spent > budget_s and len(times) >= 2:
+                break
     ref.close()
     return times
-
-
-def host_threads():
-    try:
-        return len(os.sched_getaffinity(0))
-    except Exception:
-        return os.cpu_count() or 1
 
 
 def run_reference(args):
     rank, local_rank, world = dist_env()
     if rank != 0:
         return
-    wl, _ = _import_package()
-    w = workload_for(wl, args.config, 0, args.rows)
-    if world > 1:
-        # the same job as the GPU arm at this N: every rank's batch, served as one
-        # combined request (features rank-major, ids r * F + f) by the CPU shards
-        parts = [workload_for(wl, args.config, r, args.rows) for r in range(world)]
-        F = len(w.features)
-        feats = [type(f)(f.table, r * F + f.feature, f.pooling, f.keys, f.offsets)
-                 for r, p in enumerate(parts) for f in p.features]
-        grads = [g for p in parts for g in p.gradients]
-        w = type(w)(f"{w.name}, {world} batches (one per GPU of the sharded run)", w.tables,
-                    feats, grads, w.seed, dict(w.meta))
+    wl = load_workloads()              # the generators only: no repo library is loaded
+    parts = job_parts(wl, args, world)
+    feats, _ = job_features(parts)
+    bm = byte_model(parts[0].tables, feats, world, 0)
     threads = host_threads()
-    times = reference_rounds(w, args.steps, args.warmup, threads)
+    times = reference_rounds(parts, args.config, world, args.steps, args.warmup, threads)
     if times is None:
         print(json.dumps({"impl": "reference", "unavailable":
                           "reference CPU build oracle/_ref/libeps_ref.so is missing"}))
         return
     total = sum(times)
-    value = w.occurrences * len(times) / total
-    sample = (f"{len(times)} full rounds of {w.name} ({w.occurrences} occurrences each) after "
-              f"{args.warmup} warm-up rounds, {threads} shards/threads")
+    value = bm["N"] * len(times) / total
+    what = "push" if push_only(args.config, world) else "lookup + push"
+    sample = (f"{len(times)} rounds ({what}) of the job ({bm['N']} occurrences each, "
+              f"{len(parts)} batch(es) as one request) after {args.warmup} warm-up rounds; "
+              f"DistributedClient over {threads} CpuParameterService shards")
     print(json.dumps({
         "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
         "steps": len(times), "warmup": args.warmup, "ms_per_step": 1e3 * total / len(times),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": {"workload": w.name, "parallelism": f"cpu x{threads}"},
+        "data": "synthetic", "config": job_config(parts, bm, args.config, world),
+        "parallelism": f"cpu x{threads}",
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
-                         "sample": sample},
+                         "cpu_model": cpu_model(), "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
 
 
 # ------------------------------------------------------------------- B200 arm
+def _create_tables(eps, store, w, world):
+    for t in w.tables:
+        store.create_table(eps.TableDefinition(id=t.id, dimension=t.dimension, key_space=t.rows,
+                                               learning_rate=1e-3, shard_count=world))
+
+
+def parity_check(eps, torch, parts, rank, world, dev, comms, bitexact):
+    """One round from fresh tables against the reference (tests/round_check.py).
+    Returns this rank's reports (default order; at N = 1 also the bit-exact
+    mode)."""
+    import round_check as rc
+    w = parts[rank]
+    ref_result = rc.reference_round(parts)
+    reports = []
+    modes = [False, True] if (world == 1 and bitexact) else [False]
+    for reference_order in modes:
+        store = eps.ParameterStore(device=dev.index, shard_id=rank, shard_count=world,
+                                   state_bytes=170 << 30, reference_order=reference_order)
+        try:
+            _create_tables(eps, store, w, world)
+            feats = [eps.FeatureInput(f.table, f.feature, f.pooling,
+                                      torch.from_numpy(f.keys.astype(np.int64)).to(dev),
+                                      torch.from_numpy(f.offsets.astype(np.int64)).to(dev))
+                     for f in w.features]
+            grads = [torch.from_numpy(g).to(dev) for g in w.gradients]
+            if world == 1:
+                ticket, outs = store.lookup(feats)
+                store.push(ticket, grads)
+            else:
+                import importlib
+                D = importlib.import_module("eps_b200.distributed")
+                client = D.NativeClient(store, comms[0], comms[1])
+                handle, outs = client.lookup(feats)
+                client.push(handle, grads, wait=True)
+                torch.cuda.synchronize()
+                client.close()
+            outs = [o.cpu().numpy() for o in outs]
+            rep = rc.check_round(parts, rank, outs, store.read_state,
+                                 reference_order=reference_order, ref_result=ref_result)
+        finally:
+            store.close()
+        reports.append(rep)
+    ref_result[0].close()
+    return reports
+
+
 def run_b200(args):
     import torch
     rank, local_rank, world = dist_env()
@@ -304,18 +445,20 @@ def run_b200(args):
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device(f"cuda:{local_rank}"))
-    wl, eps = _import_package()
-    w = workload_for(wl, args.config, rank, args.rows)
-    bm = byte_model(w)
+    wl = load_workloads()
+    eps = load_package()
+    parts = job_parts(wl, args, world)
+    w = parts[rank]
+    jfeats, _ = job_features(parts)
+    bm = byte_model(w.tables, jfeats, world, rank)
+    only_push = push_only(args.config, world)
     dev = torch.device(f"cuda:{local_rank}")
     # one shard per rank: keys k with k % world == rank (the table's rows are split)
     store = eps.ParameterStore(device=local_rank, shard_id=rank, shard_count=world,
-                               state_bytes=150 << 30)
-    for t in w.tables:
-        store.create_table(eps.TableDefinition(id=t.id, dimension=t.dimension, key_space=t.rows,
-                                               learning_rate=1e-3, shard_count=world))
+                               state_bytes=170 << 30)
+    _create_tables(eps, store, w, world)
     stream = torch.cuda.Stream(device=dev)
     torch.cuda.set_stream(stream)          # flushes and events run on the store's stream
 
@@ -325,16 +468,19 @@ def run_b200(args):
                               torch.from_numpy(f.offsets.astype(np.int64)).to(dev))
              for f in w.features]
     dims = {t.id: t.dimension for t in w.tables}
-    outs = [torch.empty((f.output_rows, dims[f.table]), dtype=torch.float32, device=dev)
-            for f in w.features]
+    outs = None if only_push else [
+        torch.empty((f.output_rows, dims[f.table]), dtype=torch.float32, device=dev)
+        for f in w.features]
     grads = [torch.from_numpy(g).to(dev) for g in w.gradients]
     flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)   # 256 MiB > 126 MB L2
+    comms = (None, None)
     if dist:
         # every rank's batch is routed to the owners over NCCL all-to-all
         import importlib
         D = importlib.import_module("eps_b200.distributed")
         comm = D.NcclComm.from_process_group(local_rank)    # NCCL group calls on our streams
         comm_in = D.NcclComm.from_process_group(local_rank)  # the prepare phase's exchanges
+        comms = (comm, comm_in)
         client = D.NativeClient(store, comm, comm_in)        # the round's host side in C++
         # the next batch's partition + key exchange (prepare) is issued before this
         # round's push, on a high-priority input stream, as a training loop whose
@@ -429,30 +575,27 @@ def run_b200(args):
     if dist:
         dist.barrier()
     total_ms = sum(a.elapsed_time(b) for a, b in events)
-    job_N, job_U = bm["N"], bm["U"]          # occurrences / unique rows of the whole job
     if dist:
         t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms = float(t.item())
-        t = torch.tensor([bm["N"], bm["U"]], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        job_N, job_U = int(t[0].item()), int(t[1].item())
-    value = job_N * args.steps / (total_ms / 1e3)
+    value = bm["N"] * args.steps / (total_ms / 1e3)
 
-    # ---- roofline of the dominant phase
+    # ---- roofline of the dominant phase (bytes the owner's kernels move)
     peak, peak_kind = load_peaks()
-    dom = dominant_kernel(prof, bm)
+    owner = bm["owner"]
+    dom = dominant_kernel(prof, owner)
     calls = max(1, prof[dom]["calls"])
     per_call_ms = prof[dom]["ms"] / calls
-    alg = bm[dom]
+    alg = owner[dom]
     achieved = alg / (per_call_ms / 1e3) / 1e9 if alg else 0.0
-    traffic = load_traffic().get(f"cfg{args.config}", {}).get(dom)
+    traffic = load_traffic().get(f"cfg{args.config}", {}).get(dom) if world == 1 else None
     phases = {p: {"ms_per_round": prof[p]["ms"] / max(1, prof[p]["calls"]),
                   "launches_per_round": prof[p]["launches"] / max(1, prof[p]["calls"]),
-                  "alg_GBps": (bm[p] / (prof[p]["ms"] / max(1, prof[p]["calls"]) / 1e3) / 1e9)
-                  if bm.get(p) and prof[p]["ms"] else None} for p in prof}
+                  "alg_GBps": (owner[p] / (prof[p]["ms"] / max(1, prof[p]["calls"]) / 1e3) / 1e9)
+                  if owner.get(p) and prof[p]["ms"] else None} for p in prof}
 
-    # ---- e2e through the C ABI with pinned host buffers
+    # ---- e2e through the public API with pinned host buffers
     def pinned(a):
         t = torch.empty(a.shape, dtype=torch.from_numpy(a[:0]).dtype, pin_memory=True)
         t.numpy()[...] = a
@@ -460,10 +603,11 @@ def run_b200(args):
 
     hfeats = [eps.FeatureInput(f.table, f.feature, f.pooling, pinned(f.keys), pinned(f.offsets))
               for f in w.features]
-    houts = [pinned(np.zeros((f.output_rows, dims[f.table]), np.float32)) for f in w.features]
+    houts = None if only_push else [pinned(np.zeros((f.output_rows, dims[f.table]), np.float32))
+                                    for f in w.features]
     hgrads = [pinned(g) for g in w.gradients]
     if dist:
-        # host buffers: pinned copies in, the round through ShardedClient, outputs out
+        # host buffers: pinned copies in, the round through the C++ client, outputs out
         tk = [torch.from_numpy(f.keys.view(np.int64)) for f in hfeats]
         to = [torch.from_numpy(f.offsets.view(np.int64)) for f in hfeats]
         th = [torch.from_numpy(o) for o in houts]
@@ -508,30 +652,89 @@ def run_b200(args):
         t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
-    e2e_value = job_N * e2e_steps / (e2e_ms / 1e3)
+    e2e_value = bm["N"] * e2e_steps / (e2e_ms / 1e3)
     h2d = sum(f.keys.nbytes + f.offsets.nbytes for f in w.features) + \
         sum(g.nbytes for g in w.gradients)
-    d2h = sum(o.nbytes for o in houts) + 36      # pooled outputs + push status
+    d2h = (0 if houts is None else sum(o.nbytes for o in houts)) + 36  # outputs + push status
     if dist:
         if nxt[0] is not None:
             client.discard(nxt[0])
         torch.cuda.synchronize()
         client.close()
-        comm.close()
-        comm_in.close()
     store.close()
+    del flush
+
+    # ---- the bit-exact summation mode (EPS_B200_FLAG_REFERENCE_ORDER) at N = 1:
+    # the same timed rounds on a fresh store that sums every row serially
+    bitexact = None
+    if world == 1 and not args.no_bitexact:
+        store = eps.ParameterStore(device=local_rank, state_bytes=170 << 30, reference_order=True)
+        _create_tables(eps, store, w, world)
+        flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
+        lookup = store.prepare_lookup(feats, outs)
+        push = store.prepare_push(grads)
+        for _ in range(args.warmup + 4):
+            flush.zero_()
+            push(lookup(stream), stream, wait=False)
+        store.synchronize()
+        bev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        torch.cuda.synchronize()
+        for a, b in bev:
+            flush.zero_()
+            a.record(stream)
+            push(lookup(stream), stream, wait=False)
+            b.record(stream)
+        torch.cuda.synchronize()
+        store.synchronize()
+        bms = sum(a.elapsed_time(b) for a, b in bev) / args.steps
+        bitexact = {"ms_per_step": bms, "value": bm["N"] / (bms / 1e3), "unit": UNIT,
+                    "mode": "EPS_B200_FLAG_REFERENCE_ORDER: every row summed serially in "
+                            "occurrence order (bit-exact on every row)"}
+        store.close()
+        del flush
+
+    # ---- parity: one round from fresh tables against the reference (checker only)
+    parity = None
+    if not args.no_check:
+        reports = parity_check(eps, torch, parts, rank, world, dev, comms,
+                               bitexact=not args.no_bitexact)
+        ok = all(r["parity"] for r in reports)
+        if dist:
+            t = torch.tensor([1.0 if ok else 0.0], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MIN)
+            ok = bool(t.item() == 1.0)
+            gathered = [None] * world
+            dist.all_gather_object(gathered, reports)
+            reports = [r for g in gathered for r in g]
+        parity = {"parity": ok,
+                  "outputs_bitexact": all(r["outputs_bitexact"] for r in reports),
+                  "rows_bitexact": all(r["rows_bitexact"] for r in reports),
+                  "rows_checked": sum(r["rows_checked"] for r in reports
+                                      if not r["reference_order"]),
+                  "long_rows": sum(r["long_rows"] for r in reports),
+                  "long_max_norm_err": {k: max(r["long_max_norm_err"][k] for r in reports)
+                                        for k in ("w", "m", "v")},
+                  "long_max_rel_err": {k: max(r["long_max_rel_err"][k] for r in reports)
+                                       for k in ("w", "m", "v")},
+                  "bitexact_mode_checked": any(r["reference_order"] for r in reports)}
+    if dist:
+        comms[0].close()
+        comms[1].close()
 
     # ---- CPU baseline (rank 0, N = 1): reference CPU path, bounded sample
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = host_threads()
-        times = reference_rounds(w, steps=2, warmup=1, threads=threads)
+        times = reference_rounds(parts, args.config, world, steps=args.steps, warmup=1,
+                                 threads=threads, budget_s=20.0)
         if times:
-            cpu = {"value": w.occurrences * len(times) / sum(times), "unit": UNIT,
-                   "cores": threads, "kind": "reference",
-                   "sample": f"{len(times)} full rounds of the same batch after 1 warm-up round "
-                             f"(reference DistributedClient over {threads} CpuParameterService "
-                             f"shards, one per host thread)"}
+            what = "push" if only_push else "lookup + push"
+            cpu = {"value": bm["N"] * len(times) / sum(times), "unit": UNIT,
+                   "cores": threads, "kind": "reference", "cpu_model": cpu_model(),
+                   "sample": f"{len(times)} rounds ({what}) of the same batch after 1 warm-up "
+                             f"round, at most ~20 s (reference DistributedClient over {threads} "
+                             f"CpuParameterService shards, one per host thread)"}
 
     if dist:
         dist.barrier()
@@ -542,19 +745,23 @@ def run_b200(args):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": w.name, "occurrences_per_round": job_N,
-                   "unique_rows_per_round": bm["U"], "output_rows_per_round": bm["B"],
-                   "compulsory_bytes_per_round": bm["pull"] + bm["push"],
-                   "l2": "flushed (256 MiB write) before every timed round",
-                   "parallelism": "single GPU" if world == 1 else
-                   f"{world} shards (rows by key % {world}), NCCL all-to-all of keys, "
-                   f"partials and gradients; one batch per GPU"},
-        "unique_rows_per_s": job_U * args.steps / (total_ms / 1e3),
-        "round_hbm_frac": ((bm["pull"] + bm["push"]) * args.steps / (total_ms / 1e3) / 1e9) / peak,
+        "config": job_config(parts, bm, args.config, world),
+        "parallelism": "single GPU" if world == 1 else
+        f"{world} shards (rows by key % {world}), NCCL all-to-all of keys, partials and "
+        f"gradients; one batch per GPU",
+        "l2": "flushed (256 MiB write) before every timed round",
+        "unique_rows_per_s": bm["U"] * args.steps / (total_ms / 1e3),
+        "round_hbm_frac": ((bm["push"] if only_push else bm["pull"] + bm["push"]) * args.steps /
+                           (total_ms / 1e3) / 1e9) / (peak * world),
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": traffic, "alg_bytes_per_launch": alg},
+                     "traffic": traffic, "alg_bytes_per_launch": alg,
+                     "bytes": "owner-side" if world > 1 else "single GPU"},
         "phases": phases,
+        "owner": {"occurrences": bm["owner_N"], "unique_rows": bm["owner_U"],
+                  "long_rows": bm["owner_U_long"]},
+        "parity": parity,
+        "bitexact_mode": bitexact,
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},

@@ -130,7 +130,7 @@ class SnapshotTable(C.Structure):
 
 ENTRY_POINTS = ("eps_b200_abi_version", "eps_b200_create", "eps_b200_destroy",
                 "eps_b200_create_table", "eps_b200_lookup", "eps_b200_lookup_noalloc",
-                "eps_b200_push", "eps_b200_release",
+                "eps_b200_push", "eps_b200_release", "eps_b200_ticket_coalesced",
                 "eps_b200_synchronize", "eps_b200_read_state", "eps_b200_load_state",
                 "eps_b200_optimizer_state", "eps_b200_profile", "eps_b200_stats",
                 "eps_b200_route", "eps_b200_route_scatter", "eps_b200_route_merge",
@@ -165,6 +165,8 @@ def load_library() -> C.CDLL:
     lib.eps_b200_lookup_noalloc.argtypes = [vp, P(Feature), C.c_uint64, P(Buffer), vp, P(Status)]
     lib.eps_b200_push.argtypes = [vp, C.c_uint64, P(Buffer), C.c_uint64, vp, C.c_int32, P(Status)]
     lib.eps_b200_release.argtypes = [vp, C.c_uint64, P(Status)]
+    lib.eps_b200_ticket_coalesced.argtypes = [vp, C.c_uint64, vp, vp, vp, vp, vp, vp, C.c_uint64,
+                                              C.c_uint64, P(C.c_uint64), P(C.c_uint64), P(Status)]
     lib.eps_b200_synchronize.argtypes = [vp, P(Status)]
     lib.eps_b200_read_state.argtypes = [vp, C.c_uint32, vp, C.c_uint64, vp, vp, vp, vp, P(Status)]
     lib.eps_b200_load_state.argtypes = [vp, C.c_uint32, vp, C.c_uint64, vp, vp, vp, vp, P(Status)]
@@ -409,13 +411,17 @@ class ParameterStore:
     def prepare_lookup(self, feats: Sequence[FeatureInput], outputs, read_only=False,
                        shard_partial=False):
         """Binds inputs/outputs once; the returned callable runs eps_b200_lookup
-        with no per-call Python marshalling (for steady-state loops)."""
+        with no per-call Python marshalling (for steady-state loops).
+        outputs=None binds a push-only lookup (occurrence list and coalescing
+        sort, no gather)."""
         arr, on_device, keep = self._features(feats)
-        bufs = (Buffer * len(feats))()
-        for i, (f, o) in enumerate(zip(feats, outputs)):
-            dev = _is_device(o)
-            bufs[i] = Buffer(f.feature, 0, int(o.shape[0]), int(o.shape[1]), _ptr(o),
-                             self.device if dev else -1, 0)
+        bufs = None
+        if outputs is not None:
+            bufs = (Buffer * len(feats))()
+            for i, (f, o) in enumerate(zip(feats, outputs)):
+                dev = _is_device(o)
+                bufs[i] = Buffer(f.feature, 0, int(o.shape[0]), int(o.shape[1]), _ptr(o),
+                                 self.device if dev else -1, 0)
         ticket = C.c_uint64(0)
         st = Status()
         lib, h, n = self.lib, self._h, len(feats)
@@ -476,6 +482,25 @@ class ParameterStore:
     def release(self, ticket: int):
         st = Status()
         _check(self.lib.eps_b200_release(self._h, ticket, C.byref(st)), st)
+
+    def coalesced(self, ticket: int):
+        """The ticket's coalesced rows as CompactGradients CSR
+        (eps_b200_ticket_coalesced): dict of tables, keys, row_offsets and per
+        reference feature, source row and scale."""
+        rows, refs = C.c_uint64(0), C.c_uint64(0)
+        st = Status()
+        _check(self.lib.eps_b200_ticket_coalesced(self._h, ticket, None, None, None, None, None,
+                                                  None, 0, 0, C.byref(rows), C.byref(refs),
+                                                  C.byref(st)), st)
+        U, R = rows.value, refs.value
+        out = {"tables": np.zeros(U, np.uint32), "keys": np.zeros(U, np.uint64),
+               "row_offsets": np.zeros(U + 1, np.uint64), "features": np.zeros(R, np.uint32),
+               "sources": np.zeros(R, np.uint64), "scales": np.zeros(R, np.float32)}
+        _check(self.lib.eps_b200_ticket_coalesced(
+            self._h, ticket, _ptr(out["tables"]), _ptr(out["keys"]), _ptr(out["row_offsets"]),
+            _ptr(out["features"]), _ptr(out["sources"]), _ptr(out["scales"]), U, R,
+            C.byref(rows), C.byref(refs), C.byref(st)), st)
+        return out
 
     def synchronize(self):
         st = Status()

@@ -321,5 +321,10 @@ constexpr int kNoAllocMaxDevices = 64;
 // Device address of this GPU's descriptor array; the first call on a GPU looks it
 // up (with that GPU current) and caches it.
 cudaError_t noalloc_feature_table(int device, LookupFeature** out);
+// Writes `count` descriptors into that array on `stream` (by kernel parameters,
+// so `desc` may be released once this returns); *launches receives the kernels
+// launched.
+cudaError_t noalloc_store_features(const LookupFeature* desc, unsigned count, cudaStream_t stream,
+                                   unsigned* launches);
 
 }  // namespace eps_b200

@@ -434,6 +434,22 @@ bool SameTable(const EpsB200Table& a, const EpsB200Table& b) {
          a.initialization_seed == b.initialization_seed && a.key_space == b.key_space;
 }
 
+// Per-feature shape checks shared by every lookup entry point: the host half of
+// ValidateFeature (src/access/batch_access.cpp:10-23); the keys and offsets
+// themselves are checked by the kernels.  Returns the feature's output rows.
+unsigned long long CheckFeatureShape(const EpsB200Feature& f) {
+  Require(f.pooling <= 2, "unsupported pooling mode");
+  Require(f.offset_count >= 1 && f.offsets, "invalid bag offsets");
+  Require(f.offset_count > 1 || f.key_count == 0, "invalid bag offsets");
+  Require(!f.key_count || f.keys, "null feature keys");
+  Require(!f.has_padding || !f.valid_lengths,
+          "valid lengths are derived from the padding key; pass one or the other");
+  const unsigned long long rows = f.pooling == 2 ? f.key_count : f.offset_count - 1;
+  Require(rows < (1ull << kRowBits) && f.key_count < (1ull << 31),
+          "feature exceeds the per-feature row limit", EPS_B200_CAPACITY_EXCEEDED);
+  return rows;
+}
+
 }  // namespace
 
 extern "C" {
@@ -494,7 +510,11 @@ void eps_b200_destroy(EpsB200Store* s) {
   if (!s) return;
   try {
     cudaSetDevice(s->opt.device);
-    if (s->last) cudaStreamSynchronize(s->last);
+    // the store's own completion event (recorded after every call's work, on
+    // whatever stream the caller passed) and the store's own streams: no caller
+    // stream is touched, so callers may destroy theirs first
+    if (s->last && s->last_done) cudaEventSynchronize(s->last_done);
+    if (s->side) cudaStreamSynchronize(s->side);
     if (s->own) cudaStreamSynchronize(s->own);
     for (auto& [id, t] : s->tickets) if (t.slab) cudaFree(t.slab);
     for (auto& [id, r] : s->routes) if (r.slab) cudaFree(r.slab);
@@ -510,7 +530,7 @@ void eps_b200_destroy(EpsB200Store* s) {
     if (s->sticky_error) cudaFree(s->sticky_error);
     if (s->host_status) cudaFreeHost(s->host_status);
     if (s->last_done) cudaEventDestroy(s->last_done);
-    if (s->side) { cudaStreamSynchronize(s->side); cudaStreamDestroy(s->side); }
+    if (s->side) cudaStreamDestroy(s->side);
     if (s->fork) cudaEventDestroy(s->fork);
     if (s->join) cudaEventDestroy(s->join);
     if (s->push_fork) cudaEventDestroy(s->push_fork);
@@ -582,8 +602,11 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
                     EpsB200Status* status) {
   return Boundary(status, [&] {
     auto& s = *Checked(store);
-    Require(features && outputs && count > 0 && count <= kMaxFeatures,
-            "invalid native feature count");
+    Require(features && count > 0 && count <= kMaxFeatures, "invalid native feature count");
+    // no outputs: a push-only lookup (the occurrence list and its coalescing
+    // sort, no gather) for a caller that pushes gradients of rows it already holds
+    const bool gather = outputs != nullptr;
+    Require(gather || !read_only, "a read-only lookup needs output buffers");
     Require(read_only || ticket_out, "null ticket output");
     std::lock_guard lock(s.mutex);
     s.Activate();
@@ -605,25 +628,19 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       const auto& f = features[i];
       Require(ids.insert(f.feature).second, "duplicate feature ID");
       const Table& t = s.Get(f.table);
-      Require(f.pooling <= 2, "unsupported pooling mode");
-      Require(f.offset_count >= 1 && f.offsets, "invalid bag offsets");
-      Require(f.offset_count > 1 || f.key_count == 0, "invalid bag offsets");
-      Require(!f.key_count || f.keys, "null feature keys");
-      Require(!f.has_padding || !f.valid_lengths,
-              "valid lengths are derived from the padding key; pass one or the other");
+      const unsigned long long rows = CheckFeatureShape(f);
       any_padding |= f.has_padding != 0;
-      const unsigned long long rows = f.pooling == 2 ? f.key_count : f.offset_count - 1;
-      Require(rows < (1ull << kRowBits) && f.key_count < (1ull << 31),
-              "feature exceeds the per-feature row limit", EPS_B200_CAPACITY_EXCEEDED);
-      const auto& o = outputs[i];
-      Require(o.feature == f.feature && o.rows == rows && o.columns == t.def.dimension,
-              "output buffer layout mismatch");
-      Require(!rows || o.data, "null output buffer");
-      Require(o.device < 0 || o.device == s.opt.device, "output device mismatch");
-      if (o.device < 0) { any_host_out = true; host_out_values += rows * t.def.dimension; }
-      else {
-        out16 &= (reinterpret_cast<uintptr_t>(o.data) & 15) == 0;
-        out8 &= (reinterpret_cast<uintptr_t>(o.data) & 7) == 0;
+      if (gather) {
+        const auto& o = outputs[i];
+        Require(o.feature == f.feature && o.rows == rows && o.columns == t.def.dimension,
+                "output buffer layout mismatch");
+        Require(!rows || o.data, "null output buffer");
+        Require(o.device < 0 || o.device == s.opt.device, "output device mismatch");
+        if (o.device < 0) { any_host_out = true; host_out_values += rows * t.def.dimension; }
+        else {
+          out16 &= (reinterpret_cast<uintptr_t>(o.data) & 15) == 0;
+          out8 &= (reinterpret_cast<uintptr_t>(o.data) & 7) == 0;
+        }
       }
       ranks.emplace(f.table, 0);
       total_keys += f.key_count;
@@ -747,7 +764,9 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
           koff += f.key_count;
           ooff += f.offset_count;
         }
-        if (outputs[i].device < 0) {
+        if (!gather) {
+          L.out = nullptr;
+        } else if (outputs[i].device < 0) {
           L.out = reinterpret_cast<float*>(P(at_hostout)) + hoff;
           hoff += rows * D;
         } else {
@@ -807,13 +826,15 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         s.End(EPS_B200_PHASE_EMIT, ev, stream, bag_base ? 1u : 0u);
         Cuda(cudaEventRecord(s.fork, stream));
       }
-      ev = s.Begin(stream);
-      Cuda(launch_lookup(lp, stream));
-      s.End(EPS_B200_PHASE_LOOKUP, ev, stream, bag_base ? 1u : 0u);
+      if (gather) {
+        ev = s.Begin(stream);
+        Cuda(launch_lookup(lp, stream));
+        s.End(EPS_B200_PHASE_LOOKUP, ev, stream, bag_base ? 1u : 0u);
+      }
       // ---- host outputs: final once the gather ends, so their copies are queued
       // before the stream joins the sort and overlap the sort's remaining work
       hoff = 0;
-      for (uint64_t i = 0; i < count; ++i) {
+      for (uint64_t i = 0; gather && i < count; ++i) {
         if (outputs[i].device >= 0) continue;
         const unsigned long long n = outputs[i].rows * outputs[i].columns;
         if (n)
@@ -947,11 +968,7 @@ int eps_b200_lookup_noalloc(EpsB200Store* store, const EpsB200Feature* features,
       const auto& f = features[i];
       for (uint64_t j = 0; j < i; ++j) Require(features[j].feature != f.feature, "duplicate feature ID");
       const Table& t = s.Get(f.table);
-      Require(f.pooling <= 2, "unsupported pooling mode");
-      Require(f.offset_count >= 1 && f.offsets, "invalid bag offsets");
-      Require(f.offset_count > 1 || f.key_count == 0, "invalid bag offsets");
-      Require(!f.key_count || f.keys, "null feature keys");
-      const unsigned long long rows = f.pooling == 2 ? f.key_count : f.offset_count - 1;
+      const unsigned long long rows = CheckFeatureShape(f);
       const unsigned D = t.def.dimension;
       const auto& o = outputs[i];
       Require(o.feature == f.feature && o.rows == rows && o.columns == D,
@@ -992,8 +1009,9 @@ int eps_b200_lookup_noalloc(EpsB200Store* store, const EpsB200Feature* features,
     LookupFeature* table = nullptr;
     Cuda(noalloc_feature_table(s.opt.device, &table));
     cudaStream_t stream = s.Use(stream_arg);
-    // desc is pageable: the copy has consumed it when cudaMemcpyAsync returns
-    Cuda(cudaMemcpyAsync(table, desc, count * sizeof(LookupFeature), cudaMemcpyHostToDevice, stream));
+    unsigned stores = 0;
+    Cuda(noalloc_store_features(desc, (unsigned)count, stream, &stores));
+    s.stats.kernel_launches += stores;
     LookupLaunch lp{};
     lp.features = table;
     lp.feature_count = (unsigned)count;
@@ -1257,6 +1275,74 @@ int eps_b200_release(EpsB200Store* store, uint64_t ticket, EpsB200Status* status
     }
     s.FreeTicket(it, stream);
     s.Done(stream);
+  });
+}
+
+int eps_b200_ticket_coalesced(EpsB200Store* store, uint64_t ticket, uint32_t* tables,
+                              uint64_t* keys, uint64_t* row_offsets, uint32_t* features,
+                              uint64_t* sources, float* scales, uint64_t row_capacity,
+                              uint64_t reference_capacity, uint64_t* rows_out,
+                              uint64_t* references_out, EpsB200Status* status) {
+  return Boundary(status, [&] {
+    auto& s = *Checked(store);
+    Require(rows_out && references_out, "null count outputs");
+    std::lock_guard lock(s.mutex);
+    s.Activate();
+    auto it = s.tickets.find(ticket);
+    Require(it != s.tickets.end(), "unknown lookup ticket");
+    const Ticket& t = it->second;
+    Require(!t.read_only, "ticket does not belong to update");
+    // the ticket's lookup, its sort included, ended before the store's latest call did
+    Cuda(cudaEventSynchronize(s.last_done));
+    unsigned lookup_error = 0, seg_total = 0;
+    Cuda(cudaMemcpy(&lookup_error, t.lookup_error, sizeof(unsigned), cudaMemcpyDeviceToHost));
+    Require(!lookup_error, EpsB200Store::LookupMessage(lookup_error).c_str());
+    Cuda(cudaMemcpy(&seg_total, t.seg_total, sizeof(unsigned), cudaMemcpyDeviceToHost));
+    const unsigned long long n = t.n;
+    std::vector<unsigned long long> ck(n);
+    if (t.key64) {
+      Cuda(cudaMemcpy(ck.data(), t.keys, n * 8, cudaMemcpyDeviceToHost));
+    } else {
+      std::vector<unsigned> k32(n);
+      Cuda(cudaMemcpy(k32.data(), t.keys, n * 4, cudaMemcpyDeviceToHost));
+      for (unsigned long long i = 0; i < n; ++i) ck[i] = k32[i];
+    }
+    std::vector<unsigned> src(n), seg(seg_total + 1ull);
+    Cuda(cudaMemcpy(src.data(), t.srcs, n * 4, cudaMemcpyDeviceToHost));
+    Cuda(cudaMemcpy(seg.data(), t.seg_start, seg.size() * 4, cudaMemcpyDeviceToHost));
+    const unsigned long long grad_rows =
+        t.scale_base.empty() ? 0 : t.scale_base.back() + t.grad_rows.back();
+    std::vector<float> scale(grad_rows);
+    if (grad_rows)
+      Cuda(cudaMemcpy(scale.data(), t.row_scale, grad_rows * 4, cudaMemcpyDeviceToHost));
+    // runs of padding occurrences (table rank past the lookup's tables) are not rows
+    const unsigned long long slot_mask = (1ull << t.slot_bits) - 1ull;
+    unsigned long long rows = 0, refs = 0;
+    for (unsigned u = 0; u < seg_total; ++u)
+      if ((ck[seg[u]] >> t.slot_bits) < t.table_ids.size()) { ++rows; refs += seg[u + 1] - seg[u]; }
+    *rows_out = rows;
+    *references_out = refs;
+    if (!tables) return;
+    Require(keys && row_offsets && features && sources && scales, "null coalesced outputs");
+    Require(row_capacity >= rows && reference_capacity >= refs, "coalesced output capacity too small",
+            EPS_B200_CAPACITY_EXCEEDED);
+    unsigned long long r = 0, q = 0;
+    row_offsets[0] = 0;
+    for (unsigned u = 0; u < seg_total; ++u) {
+      const unsigned long long rank = ck[seg[u]] >> t.slot_bits;
+      if (rank >= t.table_ids.size()) continue;
+      tables[r] = t.table_ids[rank];
+      keys[r] = (ck[seg[u]] & slot_mask) * s.opt.shard_count + s.opt.shard_id;
+      for (unsigned i = seg[u]; i < seg[u + 1]; ++i, ++q) {
+        const unsigned f = src[i] >> kRowBits, row = src[i] & ((1u << kRowBits) - 1u);
+        Require(f < t.feature_ids.size() && row < t.grad_rows[f], "corrupt occurrence list",
+                EPS_B200_RUN_FAILED);
+        features[q] = t.feature_ids[f];
+        sources[q] = row;
+        scales[q] = scale[t.scale_base[f] + row];
+      }
+      row_offsets[++r] = q;
+    }
   });
 }
 

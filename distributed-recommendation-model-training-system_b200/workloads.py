@@ -128,11 +128,16 @@ def config1(seed: int = 1) -> Workload:
 
 
 def config2(seed: int = 2, batch: int = 4096, rows: int = 10_000_000, dim: int = 64,
-            features: int = 8, alpha: float = 1.05, max_bag: int = 64) -> Workload:
+            features: int = 8, alpha: float = 1.05, max_bag: int = 64,
+            map_seed: int | None = 2) -> Workload:
     """One 10M x 64 table, 8 multi-hot features, bags U[1,64], Zipf(1.05),
-    features 0-3 sum and 4-7 mean."""
+    features 0-3 sum and 4-7 mean.  The rank -> id map comes from `map_seed`
+    (shared by every worker of a data-parallel job, so all workers draw from the
+    same id distribution and share its hot rows); the batch from `seed`."""
     rng = np.random.Generator(np.random.Philox(seed))
     a, b = affine(rng, rows)
+    if map_seed is not None and map_seed != seed:
+        a, b = affine(np.random.Generator(np.random.Philox(map_seed)), rows)
     feats = []
     for fi in range(features):
         lengths = rng.integers(1, max_bag + 1, size=batch).astype(np.uint64)
@@ -148,11 +153,13 @@ def config2(seed: int = 2, batch: int = 4096, rows: int = 10_000_000, dim: int =
 
 
 def config4(seed: int = 4, rows: int = 100_000_000, dim: int = 64, n: int = 262_144,
-            alpha: float = 1.2) -> Workload:
+            alpha: float = 1.2, map_seed: int | None = 4) -> Workload:
     """Push-heavy: one 100M x 64 table, 262,144 gradient rows, Zipf(1.2)
-    (one id per sequence position)."""
+    (one id per sequence position).  Id map from `map_seed`, as config2."""
     rng = np.random.Generator(np.random.Philox(seed))
     a, b = affine(rng, rows)
+    if map_seed is not None and map_seed != seed:
+        a, b = affine(np.random.Generator(np.random.Philox(map_seed)), rows)
     keys = to_ids(zipf_ranks(rng, rows, alpha, n), rows, a, b)
     feats = [FeatureSpec(1, 0, SEQUENCE, keys, np.array([0, n], np.uint64))]
     grads = gradients_for(rng, feats, {1: dim})
@@ -160,21 +167,72 @@ def config4(seed: int = 4, rows: int = 100_000_000, dim: int = 64, n: int = 262_
                     [TableSpec(1, dim, rows)], feats, grads, seed, {"a": a, "b": b})
 
 
-def config3(seed: int = 3, batch: int = 65536, tables: int = 26, dim: int = 128,
-            alpha: float = 1.1, row_scale: float = 1.0) -> Workload:
-    """26 tables x 128, rows log-uniform in [1e3, 4e7], one id per table, Zipf(1.1)."""
-    rng = np.random.Generator(np.random.Philox(seed))
-    specs, feats = [], []
+# The table-size draw of config 3.  Row counts are log-uniform in [1e3, 4e7], so
+# the expected total is 26 * (4e7 - 1e3) / ln(4e4) = 9.81e7 rows (151 GB of
+# [w|m|v] + counter state at D = 128).  Seed 9 is the draw among seeds 1..29
+# whose total (9.64e7 rows, 149 GB) lies nearest that expectation; it fits one
+# B200, so the same tables are measured at 1, 2, 4 and 8 GPUs.
+CONFIG3_TABLE_SEED = 9
+
+
+def config3_tables(table_seed: int = CONFIG3_TABLE_SEED, tables: int = 26, dim: int = 128,
+                   row_scale: float = 1.0):
+    rng = np.random.Generator(np.random.Philox(table_seed))
+    specs, maps = [], []
     for t in range(tables):
-        rows = int(np.exp(rng.uniform(np.log(1e3), np.log(4e7))) * row_scale)
-        rows = max(rows, 1)
+        rows = max(1, int(np.exp(rng.uniform(np.log(1e3), np.log(4e7))) * row_scale))
         specs.append(TableSpec(t + 1, dim, rows))
-        a, b = affine(rng, rows)
-        keys = to_ids(zipf_ranks(rng, rows, alpha, batch), rows, a, b)
-        feats.append(FeatureSpec(t + 1, t, SUM, keys, np.arange(batch + 1, dtype=np.uint64)))
+    for s in specs:
+        maps.append(affine(rng, s.rows))
+    return specs, maps
+
+
+def config3(seed: int = 3, batch: int = 65536, tables: int = 26, dim: int = 128,
+            alpha: float = 1.1, row_scale: float = 1.0,
+            table_seed: int = CONFIG3_TABLE_SEED) -> Workload:
+    """26 tables x 128, rows log-uniform in [1e3, 4e7] (drawn from `table_seed`,
+    with the id maps), one id per table per sample, Zipf(1.1); the batch from
+    `seed`."""
+    specs, maps = config3_tables(table_seed, tables, dim, row_scale)
+    rng = np.random.Generator(np.random.Philox(seed))
+    feats = []
+    for t, (s, (a, b)) in enumerate(zip(specs, maps)):
+        keys = to_ids(zipf_ranks(rng, s.rows, alpha, batch), s.rows, a, b)
+        feats.append(FeatureSpec(s.id, t, SUM, keys, np.arange(batch + 1, dtype=np.uint64)))
     grads = gradients_for(rng, feats, {s.id: s.dimension for s in specs})
-    return Workload(f"cfg3: {tables} tables x {dim}, batch {batch}, one id per table, Zipf({alpha})",
-                    specs, feats, grads, seed)
+    return Workload(f"cfg3: {tables} tables x {dim} ({sum(s.rows for s in specs)} rows), "
+                    f"batch {batch}, one id per table, Zipf({alpha})", specs, feats, grads, seed,
+                    {"table_seed": table_seed})
+
+
+def zipf_ranks_continuous(rng, rows: int, alpha: float, n: int) -> np.ndarray:
+    """Zipf ranks in [1, rows] for tables too large for an exact CDF: the
+    continuous density x^-alpha on [1, rows + 1) inverted in closed form and
+    floored."""
+    u = rng.random(n)
+    e = 1.0 - alpha
+    top = (rows + 1.0) ** e - 1.0
+    x = np.power(1.0 + u * top, 1.0 / e)
+    return np.clip(np.floor(x), 1, rows).astype(np.uint64)
+
+
+def config5(seed: int = 5, rows: int = 1_000_000_000, dim: int = 32, batch: int = 131072,
+            hot: int = 20, alpha: float = 1.05, map_seed: int | None = 5) -> Workload:
+    """Large pooled workload: one 1e9 x 32 table, batch 131,072 x 20-hot sum
+    pooling, Zipf(1.05) (continuous inverse CDF: the exact one would need a
+    1e9-entry table).  `rows` below 1e9 is the largest fitting subset of the
+    table for fewer GPUs."""
+    rng = np.random.Generator(np.random.Philox(seed))
+    mrng = rng if map_seed is None or map_seed == seed else \
+        np.random.Generator(np.random.Philox(map_seed))
+    a, b = affine(mrng, rows)
+    n = batch * hot
+    keys = to_ids(zipf_ranks_continuous(rng, rows, alpha, n), rows, a, b)
+    offsets = np.arange(0, n + 1, hot, dtype=np.uint64)
+    feats = [FeatureSpec(1, 0, SUM, keys, offsets)]
+    grads = gradients_for(rng, feats, {1: dim})
+    return Workload(f"cfg5: {rows}x{dim}, batch {batch} x {hot}-hot sum, Zipf({alpha})",
+                    [TableSpec(1, dim, rows)], feats, grads, seed, {"a": a, "b": b})
 
 
 def small(seed: int, dims=(2, 32, 64, 128), bags: int = 64, max_bag: int = 12,

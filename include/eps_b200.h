@@ -155,9 +155,9 @@ EPS_B200_EXPORT uint32_t eps_b200_abi_version(void);
  * eps::CpuParameterService (include/eps/runtime.hpp:104) /
  * eps::CudaCacheBackend (include/eps/cuda_cache_backend.hpp:19). */
 EPS_B200_EXPORT int eps_b200_create(const EpsB200Options* options, EpsB200Store** out, EpsB200Status* status);
-/* Waits for the store's work, on its own streams and on the last caller stream
- * it ran on, then frees it: a stream passed to the store must stay valid until
- * the store is destroyed (or a later call has run on another stream). */
+/* Waits for the store's work (its own completion event, recorded after every
+ * call on whatever stream the call ran on, and its own streams), then frees it.
+ * No caller stream is used, so callers may destroy their streams first. */
 EPS_B200_EXPORT void eps_b200_destroy(EpsB200Store* store);
 
 /* ParameterService::CreateTable (include/eps/parameter_service.hpp:16),
@@ -179,7 +179,10 @@ EPS_B200_EXPORT int eps_b200_create_table(EpsB200Store* store, const EpsB200Tabl
  * eps_b200_push or eps_b200_release (LookupReply::ticket, types.hpp:151-156).
  * Device inputs are validated on the GPU; such errors are reported by the next
  * push / release / synchronize of the ticket.  Host outputs imply a synchronous
- * call that reports them directly. */
+ * call that reports them directly.  outputs == NULL (read_only == 0 only) is a
+ * push-only lookup: the ticket's occurrence list and coalescing sort are built,
+ * nothing is gathered -- for a caller that pushes gradients of rows it already
+ * holds (the Lookup + Push of a push-heavy round, whose Push alone is timed). */
 EPS_B200_EXPORT int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_t count,
                     int32_t input_on_device, int32_t read_only, int32_t shard_partial,
                     EpsB200Buffer* outputs, void* stream, uint64_t* ticket,
@@ -194,12 +197,16 @@ EPS_B200_EXPORT int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* f
  * Limits and sharing:
  *  - 1 to 256 features per call (larger counts fail with CAPACITY_EXCEEDED);
  *    inputs and outputs must be device buffers on the store's GPU;
- *  - the feature descriptors go to one fixed ~26 KiB array per GPU, created when
+ *  - the feature descriptors go to one fixed ~30 KiB array per GPU, created when
  *    the library is loaded on that GPU and kept until the process exits; every
- *    call on that GPU reuses it, so calls that overlap on the GPU (two streams, or
- *    two stores on one GPU) race; calls of one store on one stream are ordered;
- *  - the first call on a GPU looks up that array's device address, so make the
- *    first call before any CUDA stream capture starts;
+ *    call on that GPU reuses it.  The calls of one store are ordered on the GPU
+ *    whatever their streams, so only calls of different stores on one GPU (or of
+ *    other users of the library in the process) can overlap, and those race;
+ *  - the descriptors are handed to the GPU as kernel parameters, so the caller's
+ *    `features` array may be reused as soon as the call returns;
+ *  - the first call on a GPU looks up that array's device address (cached for
+ *    the life of the process), so make the first call before any CUDA stream
+ *    capture starts;
  *  - invalid keys or offsets are reported by the next eps_b200_synchronize. */
 EPS_B200_EXPORT int eps_b200_lookup_noalloc(EpsB200Store* store, const EpsB200Feature* features,
                                             uint64_t count, EpsB200Buffer* outputs, void* stream,
@@ -217,6 +224,24 @@ EPS_B200_EXPORT int eps_b200_push(EpsB200Store* store, uint64_t ticket, const Ep
 
 /* ParameterService::Release (include/eps/parameter_service.hpp:20). */
 EPS_B200_EXPORT int eps_b200_release(EpsB200Store* store, uint64_t ticket, EpsB200Status* status);
+
+/* The coalesced rows of a lookup ticket -- what a Push reduces -- as the
+ * reference's CompactGradients CSR (BuildCompactGradients,
+ * src/access/compact_gradients.cpp:41-72; ReduceGradients' unique rows and their
+ * ordered occurrences, src/access/batch_access.cpp:99-121): per unique row its
+ * table id and key, row_offsets[rows + 1] into the references, and per reference
+ * (in the order the row's gradients are summed) the feature id, the gradient row
+ * (bag, or position for sequence features) and its scale (1/length for mean).
+ * Rows come in ascending (table, key) order; the reference lists them in first
+ * occurrence order, which no result depends on.  Waits for the ticket's lookup.
+ * *rows_out / *references_out always receive the counts; with tables == NULL
+ * nothing else is written. */
+EPS_B200_EXPORT int eps_b200_ticket_coalesced(EpsB200Store* store, uint64_t ticket, uint32_t* tables,
+                                              uint64_t* keys, uint64_t* row_offsets,
+                                              uint32_t* features, uint64_t* sources, float* scales,
+                                              uint64_t row_capacity, uint64_t reference_capacity,
+                                              uint64_t* rows_out, uint64_t* references_out,
+                                              EpsB200Status* status);
 
 /* Waits for all queued work and reports the first deferred error
  * (DeviceTensor::WaitOnStream contract, include/eps/cache_agent.hpp:7-14). */

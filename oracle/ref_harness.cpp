@@ -204,6 +204,41 @@ int rh_read(void* p, std::uint32_t table, std::uint64_t key, float* w, float* m,
   return 0;
 }
 
+// ParameterService::ReadState of many rows of one table: the keys are grouped by
+// home shard (key % n) and read in chunks of 4096 rows per call, within the
+// service's request byte budget.  w / m / v are [count][dimension].
+int rh_read_many(void* p, std::uint32_t table, const std::uint64_t* keys, std::uint64_t count,
+                 std::uint32_t dimension, float* w, float* m, float* v, std::uint64_t* updates,
+                 char* err) {
+  auto& h = *static_cast<Harness*>(p);
+  const std::size_t n = h.shards.size();
+  std::vector<std::vector<std::uint64_t>> by_shard(n);
+  for (std::uint64_t i = 0; i < count; ++i) by_shard[keys[i] % n].push_back(i);
+  for (std::size_t s = 0; s < n; ++s) {
+    const auto& idx = by_shard[s];
+    for (std::size_t at = 0; at < idx.size(); at += 4096) {
+      const std::size_t end = std::min(idx.size(), at + 4096);
+      std::vector<LocatedRow> req;
+      req.reserve(end - at);
+      for (std::size_t j = at; j < end; ++j)
+        req.push_back({{table, keys[idx[j]]}, ShardId(s), Placement::cpu, 0, 0, 0});
+      std::vector<RowState> rows;
+      if (int rc = Take(h.shards[s]->ReadState(std::move(req)).get(), &rows, err)) return rc;
+      if (rows.size() != end - at) { Message(err, "short ReadState reply"); return 6; }
+      for (std::size_t j = at; j < end; ++j) {
+        const auto& r = rows[j - at];
+        const std::uint64_t i = idx[j];
+        if (r.weights.size() != dimension) { Message(err, "dimension mismatch"); return 1; }
+        std::memcpy(w + i * dimension, r.weights.data(), dimension * 4);
+        std::memcpy(m + i * dimension, r.first_moment.data(), dimension * 4);
+        std::memcpy(v + i * dimension, r.second_moment.data(), dimension * 4);
+        updates[i] = r.row_updates;
+      }
+    }
+  }
+  return 0;
+}
+
 // Shard-level phase counters (include/eps/runtime.hpp:76-80) summed over shards.
 int rh_stats(void* p, std::uint64_t* out4, char* err) {
   auto& h = *static_cast<Harness*>(p);

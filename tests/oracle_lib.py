@@ -352,6 +352,21 @@ class Reference:
                                      _ptr(m, f32p), _ptr(v, f32p), C.byref(upd), self.err))
         return w, m, v, upd.value
 
+    def read_many(self, tid, keys):
+        """ReadState of many rows of table `tid` (rh_read_many): (w, m, v, updates)."""
+        keys = _u64(keys)
+        d = self._defs[tid].dimension
+        n = len(keys)
+        w, m, v = (np.zeros((n, d), np.float32) for _ in range(3))
+        upd = np.zeros(n, np.uint64)
+        fn = self.lib.rh_read_many
+        fn.restype = C.c_int
+        fn.argtypes = [C.c_void_p, C.c_uint32, u64p, C.c_uint64, C.c_uint32, f32p, f32p, f32p,
+                       u64p, C.c_char_p]
+        self._check(fn(C.c_void_p(self.h), tid, _ptr(keys, u64p), n, d, _ptr(w, f32p),
+                       _ptr(m, f32p), _ptr(v, f32p), _ptr(upd, u64p), self.err))
+        return w, m, v, upd
+
     def snapshot(self, snapshot_id: str, shard: int = 0) -> str:
         """DrainAndFlush of one shard; returns the state file path."""
         out = C.create_string_buffer(1024)

@@ -20,7 +20,8 @@ import subprocess
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF = os.environ.get("EPS_REFERENCE", "/root/reference")
+REF = os.environ.get("EPS_REFERENCE", os.path.join(
+    os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))), "reference"))
 OUT = os.path.join(ROOT, "oracle", "_ref")
 
 

@@ -19,7 +19,7 @@ def load_bench():
 def test_byte_model_matches_an_independent_count(workloads):
     bench = load_bench()
     w = workloads.small(5, rows=40)
-    bm = bench.byte_model(w)
+    bm = bench.byte_model(w.tables, w.features)
     dims = {t.id: t.dimension for t in w.tables}
     n = sum(len(f.keys) for f in w.features)
     uniq, longs = {}, {}
@@ -33,10 +33,38 @@ def test_byte_model_matches_an_independent_count(workloads):
     assert bm["N"] == n and bm["U"] == sum(uniq.values())
     assert bm["pull"] == 8 * n + 8 * offs + rows_u + outs
     assert bm["push"] == outs + 8 * n + 8 * offs + 6 * rows_u + 16 * sum(uniq.values())
-    assert bm["apply"] == sum((24 * dims[t] + 16) * (uniq[t] - longs[t]) for t in uniq)
-    assert bm["long"] == sum((24 * dims[t] + 16) * longs[t] for t in uniq)
-    assert sum(longs.values()) > 0 and bm["U_long"] == sum(longs.values())
-    assert bm["prescan"] == outs and bm["sort"] == 0 and bm["pieces"] == 0
+    own = bm["owner"]
+    assert own["apply"] == sum((24 * dims[t] + 16) * (uniq[t] - longs[t]) for t in uniq)
+    assert own["long"] == sum((24 * dims[t] + 16) * longs[t] for t in uniq)
+    assert sum(longs.values()) > 0 and bm["owner_U_long"] == sum(longs.values())
+    assert own["prescan"] == outs and own["lookup"] == bm["pull"]
+    assert "sort" not in own and "pieces" not in own
+
+
+def test_owner_bytes_split_the_job_across_shards(workloads):
+    """At n shards each owner's kernels move its own keys, its own unique rows
+    and the partial rows of the bags that have keys on it; the owners' shares
+    add up to the job's keys and rows."""
+    bench = load_bench()
+    parts = [workloads.small(7 + r, rows=60) for r in range(2)]
+    feats, _ = bench.job_features(parts)
+    job = bench.byte_model(parts[0].tables, feats)
+    owners = [bench.byte_model(parts[0].tables, feats, 2, r) for r in range(2)]
+    assert all(o["N"] == job["N"] and o["U"] == job["U"] for o in owners)
+    assert sum(o["owner_N"] for o in owners) == job["N"]
+    assert sum(o["owner_U"] for o in owners) == job["U"]
+    dims = {t.id: t.dimension for t in parts[0].tables}
+    for r, o in enumerate(owners):
+        kept = 0
+        for f in feats:
+            own = (f.keys % np.uint64(2)) == np.uint64(r)
+            if f.pooling == 2:
+                kept += 4 * dims[f.table] * int(own.sum())
+            else:
+                lengths = np.diff(f.offsets.astype(np.int64))
+                bag = np.repeat(np.arange(len(lengths)), lengths)
+                kept += 4 * dims[f.table] * len(np.unique(bag[own]))
+        assert o["owner"]["prescan"] == kept
 
 
 def test_dominant_kernel_is_the_longest_phase_with_bytes():

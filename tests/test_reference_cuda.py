@@ -28,7 +28,8 @@ import pytest
 from oracle_lib import REF_CUDA_SO, Feature, Reference, TableDef
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF = os.environ.get("EPS_REFERENCE", "/root/reference")
+REF = os.environ.get("EPS_REFERENCE", os.path.join(
+    os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))), "reference"))
 
 
 def gpu_present():

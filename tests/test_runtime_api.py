@@ -29,7 +29,9 @@ from conftest import ROOT, gpu_available
 from oracle_lib import MEAN, SEQUENCE, SUM, Feature, Oracle, TableDef
 
 HEADER = os.path.join(ROOT, "include", "eps_b200_runtime_c.h")
-REFERENCE_HEADER_DIR = "/root/reference/include"
+REFERENCE_HEADER_DIR = os.path.join(os.environ.get("EPS_REFERENCE", os.path.join(
+    os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))), "reference")),
+    "include")
 U64_MAX = (1 << 64) - 1
 
 F32 = np.float32

@@ -19,7 +19,9 @@ import pytest
 from conftest import import_package
 from oracle_lib import SEQUENCE, SUM, MEAN, Feature, Oracle, Reference, TableDef, reference_available
 
-FIXTURE = "/root/reference/tests/fixtures/snapshot-v1-unbounded.bin"
+REFERENCE = os.environ.get("EPS_REFERENCE", os.path.join(
+    os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))), "reference"))
+FIXTURE = os.path.join(REFERENCE, "tests", "fixtures", "snapshot-v1-unbounded.bin")
 
 
 def bits(a):
