@@ -93,6 +93,9 @@ def parse():
                     help="skip timing the bit-exact summation mode at N = 1")
     ap.add_argument("--rows", type=int, default=0,
                     help="override the table rows of config 2/4/5 (smaller profiling captures)")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="override the batch of config 2/3/5 or the gradient rows of config 4 "
+                         "(sub-batches within the reference CUDA backend's staging limits)")
     return ap.parse_args()
 
 
@@ -108,18 +111,18 @@ def cfg5_rows(world: int) -> int:
     return int(min(1_000_000_000, world * 150_000_000_000 // 392))
 
 
-def workload_for(wl, config, rank, world, rows=0):
+def workload_for(wl, config, rank, world, rows=0, batch=0):
     """Rank `rank`'s batch: every rank draws its own batch (seed per rank) from
     the same id distribution (the config's shared id map and tables)."""
     if config == 1:
         return wl.config1(seed=1 + 1000 * rank)
     if config == 2:
-        return wl.config2(seed=2 + 1000 * rank, rows=rows or 10_000_000)
+        return wl.config2(seed=2 + 1000 * rank, rows=rows or 10_000_000, batch=batch or 4096)
     if config == 3:
-        return wl.config3(seed=3 + 1000 * rank)
+        return wl.config3(seed=3 + 1000 * rank, batch=batch or 65536)
     if config == 4:
-        return wl.config4(seed=4 + 1000 * rank, rows=rows or 100_000_000)
-    return wl.config5(seed=5 + 1000 * rank, rows=rows or cfg5_rows(world))
+        return wl.config4(seed=4 + 1000 * rank, rows=rows or 100_000_000, n=batch or 262_144)
+    return wl.config5(seed=5 + 1000 * rank, rows=rows or cfg5_rows(world), batch=batch or 131072)
 
 
 def push_only(config, world):
@@ -184,7 +187,7 @@ def byte_model(tables, feats, world=1, rank=0):
 
 
 def job_parts(wl, args, world):
-    return [workload_for(wl, args.config, r, world, args.rows) for r in range(world)]
+    return [workload_for(wl, args.config, r, world, args.rows, args.batch) for r in range(world)]
 
 
 def job_features(parts):
@@ -272,7 +275,7 @@ class Clocks:
             os.close(fd)
             self.out = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", "-i", self.index, f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
                                          stdout=self.out, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -482,18 +485,21 @@ def run_b200(args):
         comm_in = D.NcclComm.from_process_group(local_rank)  # the prepare phase's exchanges
         comms = (comm, comm_in)
         client = D.NativeClient(store, comm, comm_in)        # the round's host side in C++
-        # the next batch's partition + key exchange (prepare) is issued before this
-        # round's push, on a high-priority input stream, as a training loop whose
-        # loader holds the next batch would; every timed step contains exactly one
-        # prepare, one lookup and one push
+        # batches are prepared (partition + count exchange) two rounds ahead on a
+        # high-priority input stream, as a training loop whose loader holds the
+        # next batches would: a prepare issues the key exchange of the batch
+        # before it, whose counts arrived a round earlier, so the host never
+        # waits for the device; every timed step contains exactly one prepare,
+        # one lookup and one push
         ids_stream = torch.cuda.Stream(device=dev, priority=-1)
-        nxt = [None]
+        from collections import deque
+        nxt = deque()
 
         def one_round():
-            if nxt[0] is None:
-                nxt[0] = client.prepare(feats, input_stream=ids_stream)
-            handle, _ = client.lookup_prepared(nxt[0], outputs=outs)
-            nxt[0] = client.prepare(feats, input_stream=ids_stream)
+            while len(nxt) < 2:
+                nxt.append(client.prepare(feats, input_stream=ids_stream))
+            handle, _ = client.lookup_prepared(nxt.popleft(), outputs=outs)
+            nxt.append(client.prepare(feats, input_stream=ids_stream))
             client.push(handle, grads)
     else:
         lookup = store.prepare_lookup(feats, outs)
@@ -657,8 +663,8 @@ def run_b200(args):
         sum(g.nbytes for g in w.gradients)
     d2h = (0 if houts is None else sum(o.nbytes for o in houts)) + 36  # outputs + push status
     if dist:
-        if nxt[0] is not None:
-            client.discard(nxt[0])
+        while nxt:
+            client.discard(nxt.popleft())
         torch.cuda.synchronize()
         client.close()
     store.close()

@@ -4,10 +4,17 @@
 // keys k with k % n == rank.
 //
 //   prepare   route (partition by key % n, src/access/prepared_lookup.cpp:47-83)
-//             -> count rows all-to-all -> ONE wait for the counts -> payload
-//             (keys, kept-bag offsets, valid lengths) all-to-all; on the input
-//             stream and the input communicator, so the next batch can be
-//             prepared while the current round's push runs
+//             -> count rows all-to-all -> an asynchronous copy of the counts to
+//             the host; on the input stream and the input communicator, so the
+//             next batch can be prepared while the current round's push runs.
+//             The prepare returns at once: the batch's payload exchange (keys,
+//             kept-bag offsets, valid lengths), which needs its counts on the
+//             host, is issued by the NEXT prepare call (for every earlier batch
+//             still pending) or by the batch's own lookup, whichever comes
+//             first.  Both points are the same on every rank, so every rank
+//             issues the same collectives in the same order; a caller that
+//             prepares two batches ahead finds the counts long arrived and the
+//             host never waits on fresh device work.
 //   lookup    shard lookup over every requester's part (eps_b200_serve) ->
 //             partial all-to-all -> shard-ordered merge and mean
 //             (src/client/distributed_client.cpp:173-188,227-232)
@@ -18,8 +25,9 @@
 //
 // One round of n ranks is what a reference shard serves for ONE combined
 // request: the features of every rank, rank-major (ids r * F + f).  Input
-// errors travel in the count rows, so every rank raises the same error before
-// any data moves.  Exchange buffers come from the stream-ordered allocator.
+// errors travel in the count rows, so every rank sees the same error, at the
+// batch's payload exchange, before any of its data moves; it is reported by
+// the batch's lookup.  Exchange buffers come from the stream-ordered allocator.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -90,6 +98,17 @@ struct Prepared {
   uint64_t route = 0;
   unsigned F = 0;
   std::vector<unsigned> dims, pools, tables;
+  // first phase (prepare): the count rows, on their way to the host
+  long long* counts = nullptr;      // pinned [2][n][4F + 1]: rows sent | rows received
+  size_t counts_words = 0;
+  cudaEvent_t counts_ready = nullptr;
+  cudaStream_t in = nullptr;        // the input stream of the first phase
+  int host_code = 0;                // this rank's shape error found on the host
+  std::string host_error;
+  // second phase (payload exchange)
+  bool exchanged = false;
+  int fail_code = 0;                // the batch's input error, reported by its lookup
+  std::string fail_message;
   std::vector<uint64_t> mine;       // [n][F][2] keys, kept bags of this rank's batch per owner
   std::vector<uint64_t> peer;       // [n][F][2] of every requester's part on this shard
   uint64_t* rpay = nullptr;         // received payload (device)
@@ -123,8 +142,7 @@ struct EpsB200Client {
   std::map<uint64_t, Prepared> prepared;
   std::map<uint64_t, Round> rounds;
   uint64_t next = 1;
-  long long* pinned = nullptr;
-  size_t pinned_words = 0;
+  std::vector<std::pair<long long*, size_t>> pinned;   // free pinned count buffers
   std::vector<cudaEvent_t> events;
 
   cudaEvent_t Event() {
@@ -133,20 +151,101 @@ struct EpsB200Client {
     Cu(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     return e;
   }
-  void Pinned(size_t words) {
-    if (pinned_words >= words) return;
-    if (pinned) Cu(cudaFreeHost(pinned));
-    pinned = nullptr;
-    pinned_words = 0;
-    Cu(cudaMallocHost(reinterpret_cast<void**>(&pinned), words * sizeof(long long)));
-    pinned_words = words;
+  // A pinned buffer of at least `words` (reused: allocating pinned memory is slow).
+  std::pair<long long*, size_t> TakePinned(size_t words) {
+    for (size_t i = 0; i < pinned.size(); ++i)
+      if (pinned[i].second >= words) {
+        auto b = pinned[i];
+        pinned.erase(pinned.begin() + (long)i);
+        return b;
+      }
+    long long* p = nullptr;
+    Cu(cudaMallocHost(reinterpret_cast<void**>(&p), words * sizeof(long long)));
+    return {p, words};
   }
+  void GivePinned(Prepared& P) {
+    if (P.counts) pinned.push_back({P.counts, P.counts_words});
+    P.counts = nullptr;
+    if (P.counts_ready) { events.push_back(P.counts_ready); P.counts_ready = nullptr; }
+  }
+  // The second phase of a prepared batch on `s` (which the count copy is
+  // ordered before): read its counts, check the inputs of every rank, then the
+  // payload exchange.  An input error is kept for the batch's lookup.
+  void Exchange(Prepared& P, cudaStream_t s);
   void Alltoall(EpsB200Comm* c, const void* send, const std::vector<uint64_t>& sc, void* recv,
                 const std::vector<uint64_t>& rc, unsigned elem, cudaStream_t s) {
     EpsB200Status st;
     Call(eps_b200_comm_alltoallv(c, send, sc.data(), recv, rc.data(), elem, s, &st), st);
   }
 };
+
+void EpsB200Client::Exchange(Prepared& P, cudaStream_t s) {
+  P.exchanged = true;
+  Cu(cudaEventSynchronize(P.counts_ready));   // recorded a call ago: normally long done
+  const unsigned F = P.F, width = 4 * F + 1;
+  const long long* mine = P.counts;
+  const long long* recv = P.counts + (size_t)n * width;
+  bool peer_error = false, bad_schema = false;
+  for (unsigned r = 0; r < n; ++r) {
+    peer_error |= recv[(size_t)r * width + 4 * F] != 0;
+    for (unsigned f = 0; f < F; ++f)
+      bad_schema |= recv[(size_t)r * width + 2 * F + f] != P.tables[f] ||
+                    recv[(size_t)r * width + 3 * F + f] != P.pools[f];
+  }
+  const long long own_bits = mine[4 * F];
+  if (P.host_code || own_bits || peer_error || bad_schema) {
+    EpsB200Status st;
+    if (P.route) eps_b200_route_release(store, P.route, &st);
+    P.route = 0;
+    if (P.host_code) { P.fail_code = P.host_code; P.fail_message = P.host_error; }
+    else if (own_bits) { P.fail_code = EPS_B200_INVALID_ARGUMENT; P.fail_message = InputMessage(own_bits); }
+    else {
+      P.fail_code = EPS_B200_INVALID_ARGUMENT;
+      P.fail_message = bad_schema ? "ranks disagree on the feature schema"
+                                  : "a peer rank rejected its lookup inputs";
+    }
+    GivePinned(P);
+    return;
+  }
+  P.mine.resize((size_t)n * F * 2);
+  P.peer.resize((size_t)n * F * 2);
+  std::vector<uint64_t> send_words(n, 0), recv_words(n, 0);
+  for (unsigned o = 0; o < n; ++o)
+    for (unsigned f = 0; f < F; ++f)
+      for (unsigned k = 0; k < 2; ++k) {
+        P.mine[((size_t)o * F + f) * 2 + k] = (uint64_t)mine[(size_t)o * width + 2 * f + k];
+        P.peer[((size_t)o * F + f) * 2 + k] = (uint64_t)recv[(size_t)o * width + 2 * f + k];
+      }
+  GivePinned(P);
+  for (unsigned o = 0; o < n; ++o)
+    for (unsigned f = 0; f < F; ++f) {
+      send_words[o] += P.mine[((size_t)o * F + f) * 2] + 2 * P.mine[((size_t)o * F + f) * 2 + 1] + 1;
+      recv_words[o] += P.peer[((size_t)o * F + f) * 2] + 2 * P.peer[((size_t)o * F + f) * 2 + 1] + 1;
+    }
+  // ---- 3. payload: keys / kept-bag offsets / valid lengths per owner
+  uint64_t total_send = 0, total_recv = 0;
+  for (unsigned o = 0; o < n; ++o) { total_send += send_words[o]; total_recv += recv_words[o]; }
+  uint64_t* pay = nullptr;
+  try {
+    pay = DevAlloc<uint64_t>(total_send, s);
+    P.rpay = DevAlloc<uint64_t>(total_recv, s);
+    EpsB200Status st;
+    Call(eps_b200_route_scatter(store, P.route, pay, s, &st), st);
+    Alltoall(input_comm, pay, send_words, P.rpay, recv_words, 8, s);
+    Cu(cudaFreeAsync(pay, s));
+    pay = nullptr;
+    P.ready = Event();
+    Cu(cudaEventRecord(P.ready, s));
+  } catch (...) {
+    EpsB200Status st;
+    eps_b200_route_release(store, P.route, &st);
+    P.route = 0;
+    if (pay) cudaFreeAsync(pay, s);
+    if (P.rpay) cudaFreeAsync(P.rpay, s);
+    P.rpay = nullptr;
+    throw;
+  }
+}
 
 extern "C" {
 
@@ -179,16 +278,19 @@ void eps_b200_client_destroy(EpsB200Client* c) {
   cudaSetDevice(c->device);
   EpsB200Status st;
   for (auto& [id, p] : c->prepared) {
-    eps_b200_route_release(c->store, p.route, &st);
+    if (p.counts_ready) cudaEventSynchronize(p.counts_ready);
+    if (p.route) eps_b200_route_release(c->store, p.route, &st);
     if (p.rpay) cudaFree(p.rpay);
     if (p.ready) cudaEventDestroy(p.ready);
+    if (p.counts_ready) cudaEventDestroy(p.counts_ready);
+    if (p.counts) cudaFreeHost(p.counts);
   }
   for (auto& [id, r] : c->rounds) {
     if (r.route) eps_b200_route_release(c->store, r.route, &st);
     if (r.ticket) eps_b200_release(c->store, r.ticket, &st);
   }
   for (auto e : c->events) cudaEventDestroy(e);
-  if (c->pinned) cudaFreeHost(c->pinned);
+  for (auto& b : c->pinned) cudaFreeHost(b.first);
   delete c;
 }
 
@@ -202,6 +304,7 @@ int eps_b200_client_prepare(EpsB200Client* c, const EpsB200Feature* features, ui
     const cudaStream_t in = static_cast<cudaStream_t>(input_stream);
     Prepared P;
     P.F = F;
+    P.in = in;
     for (unsigned f = 0; f < F; ++f) {
       unsigned d = 0;
       if (!eps_b200::store_table_dimension(c->store, features[f].table, &d)) d = 0;
@@ -211,14 +314,12 @@ int eps_b200_client_prepare(EpsB200Client* c, const EpsB200Feature* features, ui
     }
     // ---- 1./2. partition and count rows [send | recv], one row per peer
     int64_t* rows = DevAlloc<int64_t>(2ull * n * width, in);
-    std::string host_error;
-    int host_code = 0;
     {
       EpsB200Status st;
       const int rc = eps_b200_route(c->store, features, count, n, in, &P.route, rows, &st);
       if (rc) {                      // shape error found on the host: still exchange
-        host_code = rc;
-        host_error = st.message;
+        P.host_code = rc;
+        P.host_error = st.message;
         P.route = 0;
         std::vector<int64_t> h((size_t)n * width, 0);
         for (unsigned o = 0; o < n; ++o) {
@@ -229,14 +330,18 @@ int eps_b200_client_prepare(EpsB200Client* c, const EpsB200Feature* features, ui
           h[(size_t)o * width + 4 * F] = -1;
         }
         Cu(cudaMemcpyAsync(rows, h.data(), h.size() * 8, cudaMemcpyHostToDevice, in));
+        Cu(cudaStreamSynchronize(in));          // h is pageable and local
       }
     }
     try {
       c->Alltoall(c->input_comm, rows, std::vector<uint64_t>(n, width), rows + (size_t)n * width,
                   std::vector<uint64_t>(n, width), 8, in);
-      c->Pinned(2ull * n * width);
-      Cu(cudaMemcpyAsync(c->pinned, rows, 2ull * n * width * 8, cudaMemcpyDeviceToHost, in));
-      Cu(cudaStreamSynchronize(in));            // the one wait of a round
+      auto buf = c->TakePinned(2ull * n * width);
+      P.counts = buf.first;
+      P.counts_words = buf.second;
+      Cu(cudaMemcpyAsync(P.counts, rows, 2ull * n * width * 8, cudaMemcpyDeviceToHost, in));
+      P.counts_ready = c->Event();
+      Cu(cudaEventRecord(P.counts_ready, in));
     } catch (...) {
       EpsB200Status st;
       if (P.route) eps_b200_route_release(c->store, P.route, &st);
@@ -244,59 +349,9 @@ int eps_b200_client_prepare(EpsB200Client* c, const EpsB200Feature* features, ui
       throw;
     }
     Cu(cudaFreeAsync(rows, in));
-    const long long* mine = c->pinned;
-    const long long* recv = c->pinned + (size_t)n * width;
-    bool peer_error = false, bad_schema = false;
-    for (unsigned r = 0; r < n; ++r) {
-      peer_error |= recv[(size_t)r * width + 4 * F] != 0;
-      for (unsigned f = 0; f < F; ++f)
-        bad_schema |= recv[(size_t)r * width + 2 * F + f] != P.tables[f] ||
-                      recv[(size_t)r * width + 3 * F + f] != P.pools[f];
-    }
-    const long long own_bits = mine[4 * F];
-    if (host_code || own_bits || peer_error || bad_schema) {
-      EpsB200Status st;
-      if (P.route) eps_b200_route_release(c->store, P.route, &st);
-      if (host_code) throw Fail(host_code, host_error);
-      if (own_bits) throw Fail(EPS_B200_INVALID_ARGUMENT, InputMessage(own_bits));
-      throw Fail(EPS_B200_INVALID_ARGUMENT, bad_schema ? "ranks disagree on the feature schema"
-                                                      : "a peer rank rejected its lookup inputs");
-    }
-    P.mine.resize((size_t)n * F * 2);
-    P.peer.resize((size_t)n * F * 2);
-    std::vector<uint64_t> send_words(n, 0), recv_words(n, 0);
-    for (unsigned o = 0; o < n; ++o)
-      for (unsigned f = 0; f < F; ++f)
-        for (unsigned k = 0; k < 2; ++k) {
-          P.mine[((size_t)o * F + f) * 2 + k] = (uint64_t)mine[(size_t)o * width + 2 * f + k];
-          P.peer[((size_t)o * F + f) * 2 + k] = (uint64_t)recv[(size_t)o * width + 2 * f + k];
-        }
-    for (unsigned o = 0; o < n; ++o)
-      for (unsigned f = 0; f < F; ++f) {
-        send_words[o] += P.mine[((size_t)o * F + f) * 2] + 2 * P.mine[((size_t)o * F + f) * 2 + 1] + 1;
-        recv_words[o] += P.peer[((size_t)o * F + f) * 2] + 2 * P.peer[((size_t)o * F + f) * 2 + 1] + 1;
-      }
-    // ---- 3. payload: keys / kept-bag offsets / valid lengths per owner
-    uint64_t total_send = 0, total_recv = 0;
-    for (unsigned o = 0; o < n; ++o) { total_send += send_words[o]; total_recv += recv_words[o]; }
-    uint64_t* pay = nullptr;
-    try {
-      pay = DevAlloc<uint64_t>(total_send, in);
-      P.rpay = DevAlloc<uint64_t>(total_recv, in);
-      EpsB200Status st;
-      Call(eps_b200_route_scatter(c->store, P.route, pay, in, &st), st);
-      c->Alltoall(c->input_comm, pay, send_words, P.rpay, recv_words, 8, in);
-      Cu(cudaFreeAsync(pay, in));
-      pay = nullptr;
-      P.ready = c->Event();
-      Cu(cudaEventRecord(P.ready, in));
-    } catch (...) {
-      EpsB200Status st;
-      eps_b200_route_release(c->store, P.route, &st);
-      if (pay) cudaFreeAsync(pay, in);
-      if (P.rpay) cudaFreeAsync(P.rpay, in);
-      throw;
-    }
+    // the payload exchanges of earlier batches still pending, oldest first
+    for (auto& [id, Q] : c->prepared)
+      if (!Q.exchanged) c->Exchange(Q, in);
     const uint64_t id = c->next++;
     c->prepared.emplace(id, std::move(P));
     *prepared_out = id;
@@ -312,8 +367,10 @@ int eps_b200_client_lookup(EpsB200Client* c, uint64_t prepared, EpsB200Buffer* o
     Cu(cudaSetDevice(c->device));
     auto it = c->prepared.find(prepared);
     Require(it != c->prepared.end(), "unknown prepared batch");
+    if (!it->second.exchanged) c->Exchange(it->second, it->second.in);
     Prepared P = std::move(it->second);
     c->prepared.erase(it);
+    if (P.fail_code) throw Fail(P.fail_code, P.fail_message);
     const unsigned n = c->n, F = P.F;
     const cudaStream_t s = static_cast<cudaStream_t>(stream_arg);
     Cu(cudaStreamWaitEvent(s, P.ready, 0));
@@ -419,10 +476,15 @@ int eps_b200_client_release(EpsB200Client* c, uint64_t handle, EpsB200Status* st
     Cu(cudaSetDevice(c->device));
     EpsB200Status st;
     if (auto it = c->prepared.find(handle); it != c->prepared.end()) {
-      Call(eps_b200_route_release(c->store, it->second.route, &st), st);
-      Cu(cudaStreamWaitEvent(nullptr, it->second.ready, 0));
-      Cu(cudaFreeAsync(it->second.rpay, nullptr));
-      c->events.push_back(it->second.ready);
+      Prepared& P = it->second;
+      if (P.counts_ready) Cu(cudaEventSynchronize(P.counts_ready));
+      if (P.route) Call(eps_b200_route_release(c->store, P.route, &st), st);
+      if (P.ready) {
+        Cu(cudaStreamWaitEvent(nullptr, P.ready, 0));
+        c->events.push_back(P.ready);
+      }
+      if (P.rpay) Cu(cudaFreeAsync(P.rpay, nullptr));
+      c->GivePinned(P);
       c->prepared.erase(it);
       return;
     }

@@ -59,10 +59,40 @@ struct LookupFeature {
   unsigned int table_rank;             // rank of the table inside this lookup
   unsigned int feature_index;          // index inside the lookup (gradient slot)
   unsigned int has_padding;            // keys equal to padding_key are dropped
-  unsigned int pad_reserved;
+  unsigned int unit_bags;              // bags per work unit (pooled features)
   unsigned long long padding_key;
+  // work units of the emit and gather kernels: unit_bags consecutive bags of a
+  // pooled feature, or kUnitPositions consecutive positions (and the same span
+  // of offsets, which the unit validates) of a sequence feature
+  unsigned long long unit_base;        // prefix of units over features
+  unsigned long long units;
 };
 constexpr unsigned int kPadSlot = 0xFFFFFFFEu;   // slot marker of a padding key
+constexpr unsigned int kUnitBags = 8;
+constexpr unsigned int kUnitPositions = 256;
+constexpr unsigned int kUnitSlices = kUnitPositions / 32;   // 32-position slices of a unit
+
+// Bags per work unit of a pooled feature: one bag when bags hold 8 or more keys
+// on average (enough work and parallelism per bag), else kUnitBags, so that the
+// chain of dependent loads (offsets, keys, rows) is paid once per unit.
+inline unsigned feature_unit_bags(unsigned pooling, unsigned long long key_count,
+                                  unsigned long long bag_count) {
+  if (pooling == 2) return 0;
+  return (bag_count && key_count >= 8ull * bag_count) ? 1u : kUnitBags;
+}
+
+// Work units of one feature (see LookupFeature::units).
+inline unsigned long long feature_units(unsigned pooling, unsigned long long key_count,
+                                        unsigned long long bag_count) {
+  if (pooling != 2) {
+    const unsigned ub = feature_unit_bags(pooling, key_count, bag_count);
+    return (bag_count + ub - 1) / ub;
+  }
+  const unsigned long long by_keys = (key_count + kUnitPositions - 1) / kUnitPositions;
+  if (bag_count == 0) return by_keys;
+  const unsigned long long by_offsets = (bag_count + 1 + kUnitPositions - 1) / kUnitPositions;
+  return by_keys > by_offsets ? by_keys : by_offsets;
+}
 
 // Gradient source of one feature for a Push.
 struct PushFeature {

@@ -44,10 +44,10 @@ namespace {
 
 template <int G, int VEC, int ITERS, typename KeyT>
 __global__ void __launch_bounds__(256, EPS_LOOKUP_MIN_BLOCKS) lookup_kernel(LookupLaunch p) {
-  __shared__ unsigned long long s_bag_base[kMaxFeatures + 1];
+  __shared__ unsigned long long s_unit_base[kMaxFeatures + 1];
   const unsigned fc = p.feature_count;
-  for (unsigned i = threadIdx.x; i < fc; i += blockDim.x) s_bag_base[i] = p.features[i].bag_base;
-  if (threadIdx.x == 0) s_bag_base[fc] = p.bag_total;
+  for (unsigned i = threadIdx.x; i < fc; i += blockDim.x) s_unit_base[i] = p.features[i].unit_base;
+  if (threadIdx.x == 0) s_unit_base[fc] = p.unit_total;
   __syncthreads();
 
   const auto grp = cg::tiled_partition<G>(cg::this_thread_block());
@@ -56,22 +56,16 @@ __global__ void __launch_bounds__(256, EPS_LOOKUP_MIN_BLOCKS) lookup_kernel(Look
   const unsigned long long ngroups = (gridDim.x * (unsigned long long)blockDim.x) / G;
   constexpr int C = VEC * ITERS;
   constexpr int DEPTH = G < EPS_LOOKUP_DEPTH_REGS / C ? G : EPS_LOOKUP_DEPTH_REGS / C;
+  static_assert(G >= (int)kUnitBags, "a lane per bag of a unit");
   unsigned int err = 0;
 
-  for (unsigned long long g = gid; g < p.bag_total; g += ngroups) {
-    // feature owning bag g: largest f with bag_base[f] <= g
+  for (unsigned long long u = gid; u < p.unit_total; u += ngroups) {
+    // feature owning unit u: largest f with unit_base[f] <= u
     unsigned lo = 0, hi = fc;
-    while (hi - lo > 1) { const unsigned mid = (lo + hi) >> 1; if (s_bag_base[mid] <= g) lo = mid; else hi = mid; }
+    while (hi - lo > 1) { const unsigned mid = (lo + hi) >> 1; if (s_unit_base[mid] <= u) lo = mid; else hi = mid; }
     const LookupFeature* F = p.features + lo;
-    const unsigned long long b = g - s_bag_base[lo];
-    const unsigned long long key_count = F->key_count;
-    // offsets[b] and offsets[b + 1] by lanes 0 and 1
-    unsigned long long o = 0;
-    if (gl < 2) o = F->offsets[b + gl];
-    unsigned long long s = grp.shfl(o, 0), e = grp.shfl(o, 1);
-    if (b == 0 && s != 0) err |= kLookupBadOffsets;
-    if (b + 1 == F->bag_count && e != key_count) err |= kLookupBadOffsets;
-    if (s > e || e > key_count) { err |= kLookupBadOffsets; s = e = 0; }
+    const unsigned long long lu = u - s_unit_base[lo];
+    const unsigned long long key_count = F->key_count, B = F->bag_count;
     const unsigned long long* const keys = F->keys;
     const float* const state = F->state;
     float* const out = F->out;
@@ -79,107 +73,161 @@ __global__ void __launch_bounds__(256, EPS_LOOKUP_MIN_BLOCKS) lookup_kernel(Look
     const unsigned long long rows = F->rows;
     const unsigned long long row_stride = 3ull * D;
     const bool sequence = F->pooling == 2;
-
-    float acc[C];
-#pragma unroll
-    for (int k = 0; k < C; ++k) acc[k] = 0.0f;
-
     // padding keys (PrepareAdapterInput, src/access/prepare_queue.cpp:69-77) are
     // dropped: no row, no gradient; mean bags divide by the kept count and
     // sequence positions holding padding read as zeros
     const bool has_pad = F->has_padding != 0;
     const unsigned long long pad_key = F->padding_key;
-    unsigned long long kept = 0;
-    unsigned long long key = (s + gl < e) ? keys[s + gl] : 0ull;
-    for (unsigned long long c0 = s; c0 < e; c0 += G) {
-      const unsigned long long i = c0 + gl;
-      unsigned slot = ~0u;              // slots fit 32 bits: rows < 2^32 - 2 per shard
-      if (i < e && has_pad && key == pad_key) {
-        slot = kPadSlot;
-      } else if (i < e) {
-        unsigned long long sl, sh;
-        if (p.shard_count == 1) { sl = key; sh = 0; }
-        else { sl = key / p.shard_count; sh = key - sl * p.shard_count; }
-        if (sh == p.shard_id && sl < rows) slot = (unsigned)sl;
-        else err |= kLookupBadKey;
-      }
-      // next chunk's keys in flight while this chunk's rows load
-      if (i + G < e) key = keys[i + G];
-      const int cnt = (int)min((unsigned long long)G, e - c0);
-      if (has_pad) kept += __popc(grp.ballot(i < e && slot != kPadSlot));
+
+    // the unit's bags (pooled: unit_bags bags; sequence: one run of up to
+    // kUnitPositions positions), lane k holding bag k's first occurrence and end
+    // (32-bit: a feature holds fewer than 2^31 keys)
+    unsigned long long b0 = 0;
+    unsigned s_mine = 0, e_mine = 0, nb = 0;
+    if (sequence) {
+      b0 = lu * kUnitPositions;
+      nb = b0 < key_count ? 1u : 0u;
+      s_mine = (unsigned)b0;
+      e_mine = nb ? (unsigned)min(key_count, b0 + kUnitPositions) : (unsigned)b0;
+      // this unit's span of offsets (a sequence feature's bags do not shape its outputs)
 #pragma unroll 1
-      for (int j0 = 0; j0 < cnt; j0 += DEPTH) {
-        float r[DEPTH][C];
-        bool use[DEPTH], padrow[DEPTH];
-#pragma unroll
-        for (int u = 0; u < DEPTH; ++u) {
-          const unsigned su = grp.shfl(slot, (j0 + u) & (G - 1));
-          padrow[u] = (j0 + u < cnt) && su == kPadSlot;
-          use[u] = (j0 + u < cnt) && su < kPadSlot;
-          const float* row = state + (unsigned long long)su * row_stride;
-#pragma unroll
-          for (int it = 0; it < ITERS; ++it) {
-            const unsigned col = (it * G + gl) * VEC;
-            float t[VEC];
-            if (use[u] && col < D) load_vec<VEC>(row + col, t);
-            else {
-#pragma unroll
-              for (int v = 0; v < VEC; ++v) t[v] = -0.0f;
-            }
-#pragma unroll
-            for (int v = 0; v < VEC; ++v) r[u][it * VEC + v] = t[v];
-          }
+      for (unsigned q = gl; q < kUnitPositions; q += G) {
+        const unsigned long long i = b0 + q;
+        if (B > 0 && i <= B) {
+          const unsigned long long o = F->offsets[i];
+          if (i == 0 && o != 0) err |= kLookupBadOffsets;
+          if (i == B && o != key_count) err |= kLookupBadOffsets;
+          if (o > key_count || (i > 0 && F->offsets[i - 1] > o)) err |= kLookupBadOffsets;
         }
-        if (sequence) {
-          // one output row per position: 0 + w (batch_access.cpp:74-76)
+      }
+    } else {
+      b0 = lu * F->unit_bags;
+      nb = (unsigned)min((unsigned long long)F->unit_bags, B - b0);
+      if (gl < nb) {
+        const unsigned long long b = b0 + gl;
+        unsigned long long s = F->offsets[b], e = F->offsets[b + 1];
+        if (b == 0 && s != 0) err |= kLookupBadOffsets;
+        if (b + 1 == B && e != key_count) err |= kLookupBadOffsets;
+        if (s > e || e > key_count) { err |= kLookupBadOffsets; s = e = 0; }
+        s_mine = (unsigned)s;
+        e_mine = (unsigned)e;
+      }
+    }
+    unsigned s = grp.shfl(s_mine, 0), e = grp.shfl(e_mine, 0);
+    unsigned long long key = (s + gl < e) ? keys[s + gl] : 0ull;
+#pragma unroll 1
+    for (unsigned k = 0; k < nb; ++k) {
+      // bag k's range [s, e); its first chunk's keys were requested before
+      float acc[C];
 #pragma unroll
-          for (int u = 0; u < DEPTH; ++u) {
-            if (!use[u] && !padrow[u]) continue;
-            const unsigned long long pos = c0 + j0 + u;
+      for (int q = 0; q < C; ++q) acc[q] = 0.0f;
+      unsigned kept = 0;
+      if (s == e && k + 1 < nb) {
+        const unsigned ns = grp.shfl(s_mine, (k + 1) & (G - 1));
+        const unsigned ne = grp.shfl(e_mine, (k + 1) & (G - 1));
+        key = (ns + gl < ne) ? keys[ns + gl] : 0ull;
+      }
+#pragma unroll 1
+      for (unsigned c0 = s; c0 < e; c0 += G) {
+        const unsigned i = c0 + gl;
+        unsigned slot = ~0u;              // slots fit 32 bits: rows < 2^32 - 2 per shard
+        if (i < e && has_pad && key == pad_key) {
+          slot = kPadSlot;
+        } else if (i < e) {
+          unsigned long long sl, sh;
+          if (p.shard_count == 1) { sl = key; sh = 0; }
+          else { sl = key / p.shard_count; sh = key - sl * p.shard_count; }
+          if (sh == p.shard_id && sl < rows) slot = (unsigned)sl;
+          else err |= kLookupBadKey;
+        }
+        // the next chunk's keys -- of this bag, or of the next one -- in flight
+        // while this chunk's rows load
+        if (c0 + G < e) {
+          if (i + G < e) key = keys[i + G];
+        } else if (k + 1 < nb) {
+          const unsigned ns = grp.shfl(s_mine, (k + 1) & (G - 1));
+          const unsigned ne = grp.shfl(e_mine, (k + 1) & (G - 1));
+          key = (ns + gl < ne) ? keys[ns + gl] : 0ull;
+        }
+        const int cnt = (int)min((unsigned)G, e - c0);
+        if (has_pad) kept += __popc(grp.ballot(i < e && slot != kPadSlot));
+#pragma unroll 1
+        for (int j0 = 0; j0 < cnt; j0 += DEPTH) {
+          float r[DEPTH][C];
+          bool use[DEPTH], padrow[DEPTH];
+#pragma unroll
+          for (int uu = 0; uu < DEPTH; ++uu) {
+            const unsigned su = grp.shfl(slot, (j0 + uu) & (G - 1));
+            padrow[uu] = (j0 + uu < cnt) && su == kPadSlot;
+            use[uu] = (j0 + uu < cnt) && su < kPadSlot;
+            const float* row = state + (unsigned long long)su * row_stride;
 #pragma unroll
             for (int it = 0; it < ITERS; ++it) {
               const unsigned col = (it * G + gl) * VEC;
-              if (col >= D) continue;
               float t[VEC];
+              if (use[uu] && col < D) load_vec<VEC>(row + col, t);
+              else {
 #pragma unroll
-              for (int v = 0; v < VEC; ++v) t[v] = padrow[u] ? 0.0f : __fadd_rn(0.0f, r[u][it * VEC + v]);
-              store_vec<VEC>(out + pos * D + col, t);
+                for (int v = 0; v < VEC; ++v) t[v] = -0.0f;
+              }
+#pragma unroll
+              for (int v = 0; v < VEC; ++v) r[uu][it * VEC + v] = t[v];
             }
           }
-        } else {
-          // position order; -0.0f padding leaves acc unchanged
+          if (sequence) {
+            // one output row per position: 0 + w (batch_access.cpp:74-76)
 #pragma unroll
-          for (int u = 0; u < DEPTH; ++u)
+            for (int uu = 0; uu < DEPTH; ++uu) {
+              if (!use[uu] && !padrow[uu]) continue;
+              const unsigned long long pos = (unsigned long long)(c0 + j0 + uu);
 #pragma unroll
-            for (int k = 0; k < C; ++k) acc[k] = __fadd_rn(acc[k], r[u][k]);
-        }
-      }
-    }
-    if (!sequence) {
-      unsigned long long len = has_pad ? kept : e - s;
-      if (F->lengths) {
-        const unsigned long long given = F->lengths[b];
-        if (given < len) err |= kLookupShortLength;
-        len = given;
-      }
-      const bool mean = F->pooling == 1;
-      const float denom = (float)len;   // u64 -> float, round to nearest
+              for (int it = 0; it < ITERS; ++it) {
+                const unsigned col = (it * G + gl) * VEC;
+                if (col >= D) continue;
+                float t[VEC];
 #pragma unroll
-      for (int it = 0; it < ITERS; ++it) {
-        const unsigned col = (it * G + gl) * VEC;
-        if (col >= D) continue;
-        float t[VEC];
+                for (int v = 0; v < VEC; ++v) t[v] = padrow[uu] ? 0.0f : __fadd_rn(0.0f, r[uu][it * VEC + v]);
+                store_vec<VEC>(out + pos * D + col, t);
+              }
+            }
+          } else {
+            // position order; -0.0f padding leaves acc unchanged
 #pragma unroll
-        for (int v = 0; v < VEC; ++v) {
-          float x = acc[it * VEC + v];
-          if (p.client) {
-            x = __fadd_rn(0.0f, x);
-            if (mean && len) x = __fdiv_rn(x, denom);
+            for (int uu = 0; uu < DEPTH; ++uu)
+#pragma unroll
+              for (int q = 0; q < C; ++q) acc[q] = __fadd_rn(acc[q], r[uu][q]);
           }
-          t[v] = x;
         }
-        store_vec<VEC>(out + b * D + col, t);
       }
+      if (!sequence) {
+        const unsigned long long b = b0 + k;
+        unsigned long long len = has_pad ? kept : (unsigned long long)(e - s);
+        if (F->lengths) {
+          const unsigned long long given = F->lengths[b];
+          if (given < len) err |= kLookupShortLength;
+          len = given;
+        }
+        const bool mean = F->pooling == 1;
+        const float denom = (float)len;   // u64 -> float, round to nearest
+#pragma unroll
+        for (int it = 0; it < ITERS; ++it) {
+          const unsigned col = (it * G + gl) * VEC;
+          if (col >= D) continue;
+          float t[VEC];
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) {
+            float x = acc[it * VEC + v];
+            if (p.client) {
+              x = __fadd_rn(0.0f, x);
+              if (mean && len) x = __fdiv_rn(x, denom);
+            }
+            t[v] = x;
+          }
+          store_vec<VEC>(out + b * D + col, t);
+        }
+      }
+      s = grp.shfl(s_mine, (k + 1) & (G - 1));
+      e = grp.shfl(e_mine, (k + 1) & (G - 1));
     }
   }
   err = cg::reduce(grp, err, cg::bit_or<unsigned>());
@@ -188,72 +236,162 @@ __global__ void __launch_bounds__(256, EPS_LOOKUP_MIN_BLOCKS) lookup_kernel(Look
 
 // Occurrence list of a lookup that will be pushed, ahead of (and independent
 // of) the gather, so that the coalescing sort can run concurrently with the
-// gather: one warp per bag writes every occurrence's composite key (table
-// rank, slot) and gradient source (feature, bag or position) and the gradient
-// row scales (1.0f / valid length for mean, src/access/batch_access.cpp:107-108).
-// Validation matches the gather kernel's.
+// gather: every occurrence's composite key (table rank, slot) and gradient
+// source (feature, bag or position), and the gradient row scales (1.0f / valid
+// length for mean, src/access/batch_access.cpp:107-108).  Validation matches the
+// gather kernel's.
+//
+// One warp per work unit (LookupFeature::units), 32 occurrences per step: a
+// pooled unit is unit_bags consecutive bags -- their offsets are read once, and
+// lane j of a step finds its bag among them -- and a sequence unit is
+// kUnitPositions consecutive positions plus the same span of offsets, which it
+// validates (a sequence feature's bags do not shape its outputs).  So neither a
+// very long bag nor many one-key bags serialise on one warp.
 template <typename KeyT>
 __global__ void __launch_bounds__(256) emit_kernel(LookupLaunch p) {
-  __shared__ unsigned long long s_bag_base[kMaxFeatures + 1];
+  __shared__ unsigned long long s_unit_base[kMaxFeatures + 1];
+  __shared__ unsigned s_kept[8][kUnitBags];
   const unsigned fc = p.feature_count;
-  for (unsigned i = threadIdx.x; i < fc; i += blockDim.x) s_bag_base[i] = p.features[i].bag_base;
-  if (threadIdx.x == 0) s_bag_base[fc] = p.bag_total;
+  for (unsigned i = threadIdx.x; i < fc; i += blockDim.x) s_unit_base[i] = p.features[i].unit_base;
+  if (threadIdx.x == 0) s_unit_base[fc] = p.unit_total;
   __syncthreads();
-  const unsigned lane = threadIdx.x & 31;
+  const unsigned lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const unsigned long long warp = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) >> 5;
   const unsigned long long nwarps = (gridDim.x * (unsigned long long)blockDim.x) >> 5;
   unsigned err = 0;
-  for (unsigned long long g = warp; g < p.bag_total; g += nwarps) {
+  for (unsigned long long u = warp; u < p.unit_total; u += nwarps) {
     unsigned lo = 0, hi = fc;
-    while (hi - lo > 1) { const unsigned mid = (lo + hi) >> 1; if (s_bag_base[mid] <= g) lo = mid; else hi = mid; }
+    while (hi - lo > 1) { const unsigned mid = (lo + hi) >> 1; if (s_unit_base[mid] <= u) lo = mid; else hi = mid; }
     const LookupFeature* F = p.features + lo;
-    const unsigned long long b = g - s_bag_base[lo];
-    const unsigned long long key_count = F->key_count;
-    unsigned long long o = 0;
-    if (lane < 2) o = F->offsets[b + lane];
-    unsigned long long s = __shfl_sync(~0u, o, 0), e = __shfl_sync(~0u, o, 1);
-    if (b == 0 && s != 0) err |= kLookupBadOffsets;
-    if (b + 1 == F->bag_count && e != key_count) err |= kLookupBadOffsets;
-    if (s > e || e > key_count) { err |= kLookupBadOffsets; s = e = 0; }
-    const bool sequence = F->pooling == 2;
+    const unsigned long long lu = u - s_unit_base[lo];
+    const unsigned long long key_count = F->key_count, B = F->bag_count;
     const bool has_pad = F->has_padding != 0;
     const unsigned long long pad_key = F->padding_key;
     const unsigned long long rows = F->rows, occ_base = F->occ_base;
     const unsigned src_hi = F->feature_index << kRowBits;
     const KeyT rank_bits = KeyT(F->table_rank) << p.slot_bits;
-    unsigned long long kept = 0;
-    for (unsigned long long c0 = s; c0 < e; c0 += 32) {
-      const unsigned long long i = c0 + lane;
-      bool pad = false;
-      if (i < e) {
-        const unsigned long long key = F->keys[i];
-        KeyT ck = KeyT(0);
-        if (has_pad && key == pad_key) {
-          pad = true;
-          ck = KeyT(p.pad_key);        // sorts after every row key; the push skips it
-        } else {
-          unsigned long long sl, sh;
-          if (p.shard_count == 1) { sl = key; sh = 0; }
-          else { sl = key / p.shard_count; sh = key - sl * p.shard_count; }
-          if (sh == p.shard_id && sl < rows) ck = rank_bits | KeyT(sl);
-          else err |= kLookupBadKey;
+    // composite key of one occurrence; pad / bad reported through the flags
+    auto composite = [&](unsigned long long key, bool* pad) -> KeyT {
+      *pad = false;
+      if (has_pad && key == pad_key) { *pad = true; return KeyT(p.pad_key); }
+      unsigned long long sl, sh;
+      if (p.shard_count == 1) { sl = key; sh = 0; }
+      else { sl = key / p.shard_count; sh = key - sl * p.shard_count; }
+      if (sh == p.shard_id && sl < rows) return rank_bits | KeyT(sl);
+      err |= kLookupBadKey;
+      return KeyT(0);
+    };
+    if (F->pooling == 2) {
+      // positions [lu * kUnitPositions, ...) and the offsets with the same indices
+      const unsigned long long base = lu * kUnitPositions;
+#pragma unroll 1
+      for (unsigned q = 0; q < kUnitSlices; ++q) {
+        const unsigned long long i = base + q * 32 + lane;
+        if (i < key_count) {
+          bool pad;
+          const KeyT ck = composite(F->keys[i], &pad);
+          static_cast<KeyT*>(p.occ_key)[occ_base + i] = ck;
+          p.occ_src[occ_base + i] = src_hi | (unsigned)i;
+          p.row_scale[F->scale_base + i] = 1.0f;
         }
-        static_cast<KeyT*>(p.occ_key)[occ_base + i] = ck;
-        p.occ_src[occ_base + i] = src_hi | (unsigned)(sequence ? i : b);
-        if (sequence) p.row_scale[F->scale_base + i] = 1.0f;
+        if (B > 0 && i <= B) {
+          const unsigned long long o = F->offsets[i];
+          if (i == 0 && o != 0) err |= kLookupBadOffsets;
+          if (i == B && o != key_count) err |= kLookupBadOffsets;
+          if (o > key_count || (i > 0 && F->offsets[i - 1] > o)) err |= kLookupBadOffsets;
+        }
       }
-      kept += __popc(__ballot_sync(~0u, i < e && !pad));
+      continue;
     }
-    if (!sequence && lane == 0) {
-      unsigned long long len = has_pad ? kept : e - s;
+    if (F->unit_bags == 1) {
+      // one long bag: the warp walks it 32 keys at a time
+      const unsigned long long b = lu;
+      unsigned long long o = 0;
+      if (lane < 2) o = F->offsets[b + lane];
+      unsigned long long s = __shfl_sync(~0u, o, 0), e = __shfl_sync(~0u, o, 1);
+      if (b == 0 && s != 0) err |= kLookupBadOffsets;
+      if (b + 1 == B && e != key_count) err |= kLookupBadOffsets;
+      if (s > e || e > key_count) { err |= kLookupBadOffsets; s = e = 0; }
+      unsigned long long kept = 0;
+      for (unsigned long long c0 = s; c0 < e; c0 += 32) {
+        const unsigned long long i = c0 + lane;
+        bool pad = false;
+        if (i < e) {
+          const KeyT ck = composite(F->keys[i], &pad);
+          static_cast<KeyT*>(p.occ_key)[occ_base + i] = ck;
+          p.occ_src[occ_base + i] = src_hi | (unsigned)b;
+        }
+        kept += __popc(__ballot_sync(~0u, i < e && !pad));
+      }
+      if (lane == 0) {
+        unsigned long long len = has_pad ? kept : e - s;
+        if (F->lengths) {
+          const unsigned long long given = F->lengths[b];
+          if (given < len) err |= kLookupShortLength;
+          len = given;
+        }
+        const bool mean = F->pooling == 1;
+        p.row_scale[F->scale_base + b] = (mean && len) ? __fdiv_rn(1.0f, (float)len) : 1.0f;
+      }
+      continue;
+    }
+    // pooled: bags b0 .. b0 + nb - 1
+    const unsigned long long b0 = lu * F->unit_bags;
+    const unsigned nb = (unsigned)min((unsigned long long)F->unit_bags, B - b0);
+    unsigned long long o = 0;
+    if (lane <= nb) o = F->offsets[b0 + lane];
+    unsigned long long s = o, e = __shfl_down_sync(0xffffffffu, o, 1);
+    unsigned n = 0;
+    if (lane < nb) {
+      const unsigned long long b = b0 + lane;
+      if (b == 0 && s != 0) err |= kLookupBadOffsets;
+      if (b + 1 == B && e != key_count) err |= kLookupBadOffsets;
+      if (s > e || e > key_count) { err |= kLookupBadOffsets; s = e = 0; }
+      n = (unsigned)(e - s);
+    }
+    unsigned incl = n;
+#pragma unroll
+    for (int d = 1; d < (int)kUnitBags; d <<= 1) {
+      const unsigned y = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= (unsigned)d) incl += y;
+    }
+    const unsigned total = __shfl_sync(0xffffffffu, incl, kUnitBags - 1);
+    const unsigned excl = incl - n;
+    unsigned ex[kUnitBags];
+#pragma unroll
+    for (unsigned k = 0; k < kUnitBags; ++k) ex[k] = __shfl_sync(0xffffffffu, excl, k);
+    if (lane < kUnitBags) s_kept[w][lane] = 0;
+    __syncwarp();
+    for (unsigned c0 = 0; c0 < total; c0 += 32) {
+      const unsigned i = c0 + lane;
+      unsigned k = 0;
+#pragma unroll
+      for (unsigned kk = 1; kk < kUnitBags; ++kk)
+        if (kk < nb && ex[kk] <= i) k = kk;
+      // bag k's first occurrence and entry offset, from lane k (a per-lane source)
+      const unsigned long long sk = __shfl_sync(0xffffffffu, s, k);
+      const unsigned ek = __shfl_sync(0xffffffffu, excl, k);
+      if (i < total) {
+        const unsigned long long occ = sk + (i - ek);
+        bool pad;
+        const KeyT ck = composite(F->keys[occ], &pad);
+        static_cast<KeyT*>(p.occ_key)[occ_base + occ] = ck;
+        p.occ_src[occ_base + occ] = src_hi | (unsigned)(b0 + k);
+        if (has_pad && !pad) atomicAdd(&s_kept[w][k], 1u);
+      }
+    }
+    __syncwarp();
+    if (lane < nb) {
+      unsigned long long len = has_pad ? s_kept[w][lane] : n;
       if (F->lengths) {
-        const unsigned long long given = F->lengths[b];
+        const unsigned long long given = F->lengths[b0 + lane];
         if (given < len) err |= kLookupShortLength;
         len = given;
       }
       const bool mean = F->pooling == 1;
-      p.row_scale[F->scale_base + b] = (mean && len) ? __fdiv_rn(1.0f, (float)len) : 1.0f;
+      p.row_scale[F->scale_base + b0 + lane] = (mean && len) ? __fdiv_rn(1.0f, (float)len) : 1.0f;
     }
+    __syncwarp();
   }
   err = __reduce_or_sync(~0u, err);
   if (err && lane == 0) atomicOr(p.error, err);
@@ -262,7 +400,7 @@ __global__ void __launch_bounds__(256) emit_kernel(LookupLaunch p) {
 template <int G, int VEC, int ITERS>
 cudaError_t launch_key(const LookupLaunch& p, cudaStream_t s) {
   const unsigned long long groups_per_block = 256 / G;
-  const unsigned long long want = (p.bag_total + groups_per_block - 1) / groups_per_block;
+  const unsigned long long want = (p.unit_total + groups_per_block - 1) / groups_per_block;
   const unsigned long long cap = 148ull * EPS_LOOKUP_MIN_BLOCKS * 4;   // 4 waves
   const unsigned grid = (unsigned)(want < cap ? want : cap);
   if (p.key64) lookup_kernel<G, VEC, ITERS, unsigned long long><<<grid, 256, 0, s>>>(p);
@@ -272,8 +410,8 @@ cudaError_t launch_key(const LookupLaunch& p, cudaStream_t s) {
 }  // namespace
 
 cudaError_t launch_emit(const LookupLaunch& p, cudaStream_t stream) {
-  if (p.bag_total == 0) return cudaSuccess;
-  const unsigned long long want = (p.bag_total + 7) / 8;
+  if (p.unit_total == 0) return cudaSuccess;
+  const unsigned long long want = (p.unit_total + 7) / 8;
   const unsigned grid = (unsigned)(want < 148ull * 8 * 2 ? want : 148ull * 8 * 2);
   if (p.key64) emit_kernel<unsigned long long><<<grid, 256, 0, stream>>>(p);
   else emit_kernel<unsigned int><<<grid, 256, 0, stream>>>(p);
@@ -281,7 +419,7 @@ cudaError_t launch_emit(const LookupLaunch& p, cudaStream_t stream) {
 }
 
 cudaError_t launch_lookup(const LookupLaunch& p, cudaStream_t stream) {
-  if (p.bag_total == 0) return cudaSuccess;
+  if (p.unit_total == 0) return cudaSuccess;
   if (p.vec == 4) {
     switch (p.group) {
       case 8: return launch_key<8, 4, 1>(p, stream);

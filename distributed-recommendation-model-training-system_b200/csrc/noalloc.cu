@@ -19,7 +19,7 @@
 // overlap and race on it.
 //
 // The descriptors reach the array through the parameters of a small kernel
-// (up to 32 per launch): the launch copies its parameters when it is enqueued,
+// (up to 24 per launch): the launch copies its parameters when it is enqueued,
 // so no host memory is read after the entry point returns.
 #include <mutex>
 
@@ -30,7 +30,7 @@ namespace eps_b200 {
 static __device__ __align__(256) LookupFeature g_noalloc_features[kNoAllocFeatures];
 
 namespace {
-constexpr unsigned kNoAllocChunk = 32;
+constexpr unsigned kNoAllocChunk = 24;
 struct NoAllocChunk {
   unsigned first, count;
   LookupFeature f[kNoAllocChunk];

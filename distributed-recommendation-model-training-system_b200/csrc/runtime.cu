@@ -733,7 +733,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       Ticket t;
       t.read_only = read_only != 0;
       unsigned long long bag_base = 0, occ_base = 0, scale_base = 0, koff = 0,
-                         ooff = 0, loff = 0, hoff = 0;
+                         ooff = 0, loff = 0, hoff = 0, unit_base = 0;
       t.table_ids.resize(ranks.size());
       t.table_occ.assign(ranks.size(), 0);
       for (auto& [id, rank] : ranks) t.table_ids[rank] = id;
@@ -785,6 +785,10 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         L.feature_index = (unsigned)i;
         L.has_padding = f.has_padding ? 1u : 0u;
         L.padding_key = f.padding_key;
+        L.unit_base = unit_base;
+        L.units = feature_units(f.pooling, f.key_count, L.bag_count);
+        L.unit_bags = feature_unit_bags(f.pooling, f.key_count, L.bag_count);
+        unit_base += L.units;
         bag_base += L.bag_count;
         occ_base += f.key_count;
         scale_base += rows;
@@ -801,6 +805,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       lp.features = reinterpret_cast<const LookupFeature*>(P(at_desc));
       lp.feature_count = (unsigned)count;
       lp.bag_total = bag_base;
+      lp.unit_total = unit_base;
       lp.shard_count = s.opt.shard_count;
       lp.shard_id = s.opt.shard_id;
       lp.client = shard_partial ? 0 : 1;
@@ -823,13 +828,13 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         // stream concurrently with the gather
         ev = s.Begin(stream);
         Cuda(launch_emit(lp, stream));
-        s.End(EPS_B200_PHASE_EMIT, ev, stream, bag_base ? 1u : 0u);
+        s.End(EPS_B200_PHASE_EMIT, ev, stream, unit_base ? 1u : 0u);
         Cuda(cudaEventRecord(s.fork, stream));
       }
       if (gather) {
         ev = s.Begin(stream);
         Cuda(launch_lookup(lp, stream));
-        s.End(EPS_B200_PHASE_LOOKUP, ev, stream, bag_base ? 1u : 0u);
+        s.End(EPS_B200_PHASE_LOOKUP, ev, stream, unit_base ? 1u : 0u);
       }
       // ---- host outputs: final once the gather ends, so their copies are queued
       // before the stream joins the sort and overlap the sort's remaining work
@@ -961,7 +966,7 @@ int eps_b200_lookup_noalloc(EpsB200Store* store, const EpsB200Feature* features,
     s.Activate();
     Require(s.opt.shard_count == 1, "a client-level lookup needs a single-shard store");
     LookupFeature desc[kNoAllocFeatures];
-    unsigned long long bag_base = 0;
+    unsigned long long bag_base = 0, unit_base = 0;
     unsigned dmax = 1;
     bool all4 = true, all2 = true, out16 = true, out8 = true;
     for (uint64_t i = 0; i < count; ++i) {
@@ -998,6 +1003,10 @@ int eps_b200_lookup_noalloc(EpsB200Store* store, const EpsB200Feature* features,
       L.feature_index = (unsigned)i;
       L.has_padding = f.has_padding ? 1u : 0u;
       L.padding_key = f.padding_key;
+      L.unit_base = unit_base;
+      L.units = feature_units(f.pooling, f.key_count, L.bag_count);
+        L.unit_bags = feature_unit_bags(f.pooling, f.key_count, L.bag_count);
+      unit_base += L.units;
       bag_base += L.bag_count;
     }
     // launch shape as in the regular lookup (no heap use here)
@@ -1016,6 +1025,7 @@ int eps_b200_lookup_noalloc(EpsB200Store* store, const EpsB200Feature* features,
     lp.features = table;
     lp.feature_count = (unsigned)count;
     lp.bag_total = bag_base;
+    lp.unit_total = unit_base;
     lp.shard_count = 1;
     lp.shard_id = 0;
     lp.client = 1;
@@ -1027,7 +1037,7 @@ int eps_b200_lookup_noalloc(EpsB200Store* store, const EpsB200Feature* features,
     lp.iters = sh.iters;
     Cuda(launch_lookup(lp, stream));
     ++s.stats.lookups;
-    if (bag_base) ++s.stats.kernel_launches;
+    if (unit_base) ++s.stats.kernel_launches;
     s.Done(stream);
   });
 }

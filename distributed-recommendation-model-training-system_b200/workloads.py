@@ -161,7 +161,8 @@ def config4(seed: int = 4, rows: int = 100_000_000, dim: int = 64, n: int = 262_
     if map_seed is not None and map_seed != seed:
         a, b = affine(np.random.Generator(np.random.Philox(map_seed)), rows)
     keys = to_ids(zipf_ranks(rng, rows, alpha, n), rows, a, b)
-    feats = [FeatureSpec(1, 0, SEQUENCE, keys, np.array([0, n], np.uint64))]
+    # n samples of one id each; sequence pooling: one gradient row per id
+    feats = [FeatureSpec(1, 0, SEQUENCE, keys, np.arange(n + 1, dtype=np.uint64))]
     grads = gradients_for(rng, feats, {1: dim})
     return Workload(f"cfg4: {rows}x{dim}, {n} gradient rows, Zipf({alpha})",
                     [TableSpec(1, dim, rows)], feats, grads, seed, {"a": a, "b": b})

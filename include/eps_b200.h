@@ -388,7 +388,12 @@ EPS_B200_EXPORT int eps_b200_client_create(EpsB200Store* store, EpsB200Comm* com
 EPS_B200_EXPORT void eps_b200_client_destroy(EpsB200Client* client);
 /* PrepareLookupInputs + the key exchange (DistributedClient::LookupPrepared's
  * input), on input_stream; device inputs that stay valid until the lookup.
- * Waits once, for the partition counts. */
+ * Returns without waiting: it enqueues the partition and the count exchange;
+ * the key exchange, which needs the counts on the host, is issued by the next
+ * eps_b200_client_prepare (for every earlier batch still pending) or by this
+ * batch's lookup, whichever comes first -- the same point on every rank.
+ * Preparing two batches ahead therefore never waits on fresh device work.
+ * Input errors of any rank are reported by the batch's lookup, on every rank. */
 EPS_B200_EXPORT int eps_b200_client_prepare(EpsB200Client* client, const EpsB200Feature* features,
                                             uint64_t count, void* input_stream, uint64_t* prepared,
                                             EpsB200Status* status);

@@ -9,9 +9,10 @@ the B200 path is compared with.
 * CPU: the library builds, and without a GPU attaching the backend fails with
   the reference's own CUDA error.
 * ``refgpu`` marker (run explicitly, ``-m refgpu``, on a B200; not part of
-  ``-m gpu``): pull + push rounds of cfg1 and of cfg2 sub-batches (batch 1024: the backend
+  ``-m gpu``): pull + push rounds of cfg1, of cfg2 sub-batches (batch 1024: the backend
   stages at most 64 MiB and 16 MiB compact packets per call,
-  src/cuda/cache_backend.cu:212-214, src/access/compact_gradients.cpp:15) through
+  src/cuda/cache_backend.cu:212-214, src/access/compact_gradients.cpp:15) and of
+  cfg4 sub-batches (32,768 gradient rows; the push is also timed alone) through
   that path, timed on the host clock as the API is synchronous; the pulls must
   match the reference's CPU path within the reference CUDA test's tolerance
   (1e-5, tests/cuda_tests.cpp:14).  Prints one JSON line per config, also written
@@ -77,7 +78,7 @@ def test_reference_cuda_backend_fails_loudly_without_a_gpu(workloads):
 
 
 @pytest.mark.refgpu
-@pytest.mark.parametrize("config", ["cfg1", "cfg2-1024"])
+@pytest.mark.parametrize("config", ["cfg1", "cfg2-1024", "cfg4-32768"])
 def test_reference_cuda_backend_rounds(workloads, config):
     if not gpu_present():
         pytest.skip("needs a GPU")
@@ -85,6 +86,8 @@ def test_reference_cuda_backend_rounds(workloads, config):
     warmup, steps = 3, (100 if config == "cfg1" else 10)
     if config == "cfg1":
         w, tables, feats = as_reference(workloads.config1())
+    elif config == "cfg4-32768":
+        w, tables, feats = as_reference(workloads.config4(n=32768))
     else:
         w, tables, feats = cfg2_subbatch(workloads, 1024)
     ref = Reference(tables, shards=1, library=lib)
@@ -107,9 +110,12 @@ def test_reference_cuda_backend_rounds(workloads, config):
         b, _ = ref.lookup(feats)
         ref.push(b, feats, w.gradients)
     t0 = time.perf_counter()
+    push_s = 0.0
     for _ in range(steps):
         b, _ = ref.lookup(feats)
+        p0 = time.perf_counter()
         ref.push(b, feats, w.gradients)
+        push_s += time.perf_counter() - p0
     dt = (time.perf_counter() - t0) / steps
     b2, outs_gpu = ref.lookup(feats, read_only=True)
     ref.release(b2)
@@ -123,6 +129,7 @@ def test_reference_cuda_backend_rounds(workloads, config):
         np.testing.assert_allclose(g, c, rtol=1e-5, atol=1e-5)
     line = {"impl": "reference-cuda-backend", "metric": "embedding rows/s per round (pull+push+Adam)",
             "value": w.occurrences / dt, "unit": "rows/s", "ms_per_round": dt * 1e3,
+            "push_ms_per_round": push_s / steps * 1e3,
             "workload": f"{config}: {w.occurrences} occurrences, {unique} unique rows, "
                         f"all resident on the GPU ({w.name})",
             "steps": steps, "warmup": warmup, "timing": "host clock around synchronous API calls"}
