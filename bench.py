@@ -440,6 +440,110 @@ def parity_check(eps, torch, parts, rank, world, dev, comms, bitexact):
     return reports
 
 
+def e2e_pipelined(eps, torch, store, stream, w, hfeats, houts, hgrads, flush, steps, dev):
+    """End-to-end rounds through the public API from pinned host buffers, with
+    the copies of consecutive rounds overlapped as a training loop overlaps
+    them: round k + 1's keys and offsets are copied in while round k runs; round
+    k's pooled outputs are copied out as soon as its gather ends (its coalescing
+    sort still running); its gradients, which a training step computes from
+    those outputs, are copied in after them; then its push, whose status the
+    library copies back.  Two sets of device buffers alternate.  One window of
+    CUDA events on the store's stream covers every round, the L2 flush before
+    each round included.  Returns the window in milliseconds."""
+    nb = 2
+    dk = [[torch.empty(len(f.keys), dtype=torch.int64, device=dev) for f in hfeats] for _ in range(nb)]
+    do = [[torch.empty(len(f.offsets), dtype=torch.int64, device=dev) for f in hfeats]
+          for _ in range(nb)]
+    dout = None if houts is None else [[torch.empty(o.shape, dtype=torch.float32, device=dev)
+                                         for o in houts] for _ in range(nb)]
+    hout2 = None if houts is None else [
+        houts, [torch.empty(o.shape, dtype=torch.float32, pin_memory=True).numpy() for o in houts]]
+    dg = [[torch.empty(g.shape, dtype=torch.float32, device=dev) for g in hgrads] for _ in range(nb)]
+    tk = [torch.from_numpy(f.keys.view(np.int64)) for f in hfeats]
+    to = [torch.from_numpy(f.offsets.view(np.int64)) for f in hfeats]
+    tg = [torch.from_numpy(g) for g in hgrads]
+    looks, pushes = [], []
+    for b in range(nb):
+        feats_b = [eps.FeatureInput(f.table, f.feature, f.pooling, dk[b][i], do[b][i])
+                   for i, f in enumerate(hfeats)]
+        looks.append(store.prepare_lookup(feats_b, None if dout is None else dout[b]))
+        pushes.append(store.prepare_push(dg[b]))
+    sk = torch.cuda.Stream(device=dev)       # keys / offsets in
+    so = torch.cuda.Stream(device=dev)       # outputs out
+    sg = torch.cuda.Stream(device=dev)       # gradients in
+    E = lambda: torch.cuda.Event()           # noqa: E731
+
+    def copy_keys(b):
+        with torch.cuda.stream(sk):
+            for i in range(len(hfeats)):
+                dk[b][i].copy_(tk[i], non_blocking=True)
+                do[b][i].copy_(to[i], non_blocking=True)
+        e = E()
+        e.record(sk)
+        return e
+
+    def run(nrounds, timed):
+        keys_ready = [None] * nb
+        free_in = [None] * nb                 # the buffer set's lookup has read its inputs
+        free_out = [None] * nb                # its outputs have been copied out
+        free_g = [None] * nb                  # its push has read its gradients
+        keys_ready[0] = copy_keys(0)
+        t0 = t1 = None
+        for k in range(nrounds):
+            b = k % nb
+            flush.zero_()
+            if timed and k == 0:
+                t0 = torch.cuda.Event(enable_timing=True)
+                t0.record(stream)
+            stream.wait_event(keys_ready[b])
+            if free_out[b] is not None:
+                stream.wait_event(free_out[b])
+            ticket = looks[b](stream)
+            looked = E()
+            looked.record(stream)
+            free_in[b] = looked
+            if k + 1 < nrounds:               # the next round's keys, during this round
+                b2 = (k + 1) % nb
+                if free_in[b2] is not None:
+                    sk.wait_event(free_in[b2])
+                keys_ready[b2] = copy_keys(b2)
+            after = looked
+            if dout is not None:
+                so.wait_event(looked)
+                with torch.cuda.stream(so):
+                    for h, o in zip(hout2[b], dout[b]):
+                        torch.from_numpy(h).copy_(o, non_blocking=True)
+                after = E()
+                after.record(so)
+                free_out[b] = after
+            sg.wait_event(after)
+            if free_g[b] is not None:
+                sg.wait_event(free_g[b])
+            with torch.cuda.stream(sg):
+                for d, h in zip(dg[b], tg):
+                    d.copy_(h, non_blocking=True)
+            gready = E()
+            gready.record(sg)
+            stream.wait_event(gready)
+            pushes[b](ticket, stream, wait=False)
+            pushed = E()
+            pushed.record(stream)
+            free_g[b] = pushed
+        if timed:
+            t1 = torch.cuda.Event(enable_timing=True)
+            t1.record(stream)
+        torch.cuda.synchronize()
+        store.synchronize()                    # every push's status, read back
+        return t0, t1
+
+    run(3, False)
+    gc.collect()
+    gc.disable()
+    t0, t1 = run(steps, True)
+    gc.enable()
+    return t0.elapsed_time(t1)
+
+
 def run_b200(args):
     import torch
     rank, local_rank, world = dist_env()
@@ -558,12 +662,15 @@ def run_b200(args):
     # per-phase device time: the same rounds again with the library's phase events
     # (kept out of the timed rounds above, whose stream they would otherwise join)
     store.profile(1)
+    if dist:
+        client.profile(1)
     for _ in range(args.steps):
         flush.zero_()
         one_round()
     torch.cuda.synchronize()
     store.synchronize()
     prof = store.profile(0)
+    exch = client.profile(0) if dist else None
     # the timed rounds last milliseconds, less than one nvidia-smi sample period:
     # keep the same load running (untimed) for 0.5 s so the clock record covers it
     # (a fixed round count, the same on every rank, so that collectives match)
@@ -601,6 +708,41 @@ def run_b200(args):
                   "alg_GBps": (owner[p] / (prof[p]["ms"] / max(1, prof[p]["calls"]) / 1e3) / 1e9)
                   if owner.get(p) and prof[p]["ms"] else None} for p in prof}
 
+    # ---- NVLink: this rank's exchanges per round, against the all-to-all
+    # bandwidth measured here on the same communicator (32 MiB to every peer)
+    nvlink = None
+    if dist:
+        per = 32 << 20
+        src = torch.empty(world * per // 4, dtype=torch.float32, device=dev)
+        dst = torch.empty_like(src)
+        for _ in range(2):
+            comm.all_to_all_single(dst, src)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(5):
+            comm.all_to_all_single(dst, src)
+        b.record(stream)
+        torch.cuda.synchronize()
+        a2a_ms = a.elapsed_time(b) / 5
+        t = torch.tensor([a2a_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        peak_nv = per * (world - 1) / (float(t.item()) / 1e3) / 1e9
+        del src, dst
+        calls = max(1, args.steps)
+        ex = {k: {"ms_per_round": v["ms"] / calls, "bytes_out_per_round": v["bytes"] / calls,
+                  "GBps_out": (v["bytes"] / (v["ms"] / 1e3) / 1e9) if v["ms"] else None}
+              for k, v in exch.items()}
+        out_bytes = sum(v["bytes"] for v in exch.values()) / calls
+        out_ms = sum(v["ms"] for v in exch.values()) / calls
+        nvlink = {"bytes_out_per_round": out_bytes, "exchange_ms_per_round": out_ms,
+                  "achieved_GBps_out": out_bytes / (out_ms / 1e3) / 1e9 if out_ms else None,
+                  "alltoall_peak_GBps_out": peak_nv,
+                  "frac": (out_bytes / (out_ms / 1e3) / 1e9) / peak_nv if out_ms else None,
+                  "exchanges": ex,
+                  "peak": f"NCCL all-to-all of {per >> 20} MiB to every peer on the round's "
+                          f"communicator, this rank's outgoing bytes / time (max over ranks)"}
+
     # ---- e2e through the public API with pinned host buffers
     def pinned(a):
         t = torch.empty(a.shape, dtype=torch.from_numpy(a[:0]).dtype, pin_memory=True)
@@ -630,30 +772,27 @@ def run_b200(args):
                 h.copy_(o, non_blocking=True)
             client.push(handle, [g.to(dev, non_blocking=True) for g in tg])
             torch.cuda.current_stream(dev).synchronize()
-    else:
-        hlookup = store.prepare_lookup(hfeats, houts)
-        hpush = store.prepare_push(hgrads)
-
-        def e2e_round():
-            hpush(hlookup(stream), stream, wait=True)
     e2e_steps = max(3, args.steps // 2)
-    for _ in range(2):
-        e2e_round()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(e2e_steps)]
-    torch.cuda.synchronize()
     if dist:
+        for _ in range(2):
+            e2e_round()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(e2e_steps)]
+        torch.cuda.synchronize()
         dist.barrier()
-    gc.collect()
-    gc.disable()
-    for a, b in ev:
-        flush.zero_()
-        a.record(stream)
-        e2e_round()
-        b.record(stream)
-    torch.cuda.synchronize()
-    gc.enable()
-    e2e_ms = sum(a.elapsed_time(b) for a, b in ev)
+        gc.collect()
+        gc.disable()
+        for a, b in ev:
+            flush.zero_()
+            a.record(stream)
+            e2e_round()
+            b.record(stream)
+        torch.cuda.synchronize()
+        gc.enable()
+        e2e_ms = sum(a.elapsed_time(b) for a, b in ev)
+    else:
+        e2e_ms = e2e_pipelined(eps, torch, store, stream, w, hfeats, houts, hgrads, flush,
+                               e2e_steps, dev)
     if dist:
         t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -764,6 +903,7 @@ def run_b200(args):
                      "traffic": traffic, "alg_bytes_per_launch": alg,
                      "bytes": "owner-side" if world > 1 else "single GPU"},
         "phases": phases,
+        "nvlink": nvlink,
         "owner": {"occurrences": bm["owner_N"], "unique_rows": bm["owner_U"],
                   "long_rows": bm["owner_U_long"]},
         "parity": parity,

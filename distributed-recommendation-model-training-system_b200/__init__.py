@@ -139,6 +139,7 @@ ENTRY_POINTS = ("eps_b200_abi_version", "eps_b200_create", "eps_b200_destroy",
                 "eps_b200_comm_destroy", "eps_b200_comm_alltoallv", "eps_b200_comm_allreduce_max",
                 "eps_b200_client_create", "eps_b200_client_destroy", "eps_b200_client_prepare",
                 "eps_b200_client_lookup", "eps_b200_client_push", "eps_b200_client_release",
+                "eps_b200_client_profile",
                 "eps_b200_sync_reduce", "eps_b200_apply_rows", "eps_b200_apply_compact",
                 "eps_b200_snapshot_write", "eps_b200_snapshot_read", "eps_b200_snapshot_inspect",
                 "eps_b200_snapshot_rows")
@@ -199,6 +200,8 @@ def load_library() -> C.CDLL:
                                            P(C.c_uint64), P(Status)]
     lib.eps_b200_client_push.argtypes = [vp, C.c_uint64, P(Buffer), vp, C.c_int32, P(Status)]
     lib.eps_b200_client_release.argtypes = [vp, C.c_uint64, P(Status)]
+    lib.eps_b200_client_profile.argtypes = [vp, C.c_int32, P(C.c_double), P(C.c_uint64),
+                                            P(C.c_uint64), P(Status)]
     lib.eps_b200_sync_reduce.argtypes = [vp, C.c_uint32, vp, C.c_uint32, C.c_int32, vp, vp,
                                          C.c_uint64, P(C.c_uint64), vp, P(Status)]
     lib.eps_b200_apply_rows.argtypes = [vp, P(UpdateContext), vp, C.c_uint64, vp, C.c_int32, vp,

@@ -172,10 +172,47 @@ struct EpsB200Client {
   // ordered before): read its counts, check the inputs of every rank, then the
   // payload exchange.  An input error is kept for the batch's lookup.
   void Exchange(Prepared& P, cudaStream_t s);
+  // ---- exchange profile: CUDA events around every all-to-all on its stream,
+  // and the bytes this rank sends to other ranks (EPS_B200_EXCHANGE_*)
+  bool profiling = false;
+  struct Pending { int kind; cudaEvent_t a, b; };
+  std::vector<Pending> pending;
+  std::vector<cudaEvent_t> timing_events;
+  double ex_ms[EPS_B200_EXCHANGES] = {};
+  uint64_t ex_bytes[EPS_B200_EXCHANGES] = {}, ex_calls[EPS_B200_EXCHANGES] = {};
+  cudaEvent_t TimingEvent() {
+    if (!timing_events.empty()) { cudaEvent_t e = timing_events.back(); timing_events.pop_back(); return e; }
+    cudaEvent_t e;
+    Cu(cudaEventCreate(&e));
+    return e;
+  }
+  void Collect() {
+    for (auto& x : pending) {
+      Cu(cudaEventSynchronize(x.b));
+      float ms = 0;
+      Cu(cudaEventElapsedTime(&ms, x.a, x.b));
+      ex_ms[x.kind] += ms;
+      timing_events.push_back(x.a);
+      timing_events.push_back(x.b);
+    }
+    pending.clear();
+  }
   void Alltoall(EpsB200Comm* c, const void* send, const std::vector<uint64_t>& sc, void* recv,
-                const std::vector<uint64_t>& rc, unsigned elem, cudaStream_t s) {
+                const std::vector<uint64_t>& rc, unsigned elem, cudaStream_t s, int kind) {
     EpsB200Status st;
+    cudaEvent_t a = nullptr;
+    if (profiling) { a = TimingEvent(); Cu(cudaEventRecord(a, s)); }
     Call(eps_b200_comm_alltoallv(c, send, sc.data(), recv, rc.data(), elem, s, &st), st);
+    uint64_t out = 0;
+    for (unsigned o = 0; o < sc.size(); ++o)
+      if (o != rank) out += sc[o] * elem;
+    ex_bytes[kind] += out;
+    ++ex_calls[kind];
+    if (a) {
+      cudaEvent_t b = TimingEvent();
+      Cu(cudaEventRecord(b, s));
+      pending.push_back({kind, a, b});
+    }
   }
 };
 
@@ -231,7 +268,7 @@ void EpsB200Client::Exchange(Prepared& P, cudaStream_t s) {
     P.rpay = DevAlloc<uint64_t>(total_recv, s);
     EpsB200Status st;
     Call(eps_b200_route_scatter(store, P.route, pay, s, &st), st);
-    Alltoall(input_comm, pay, send_words, P.rpay, recv_words, 8, s);
+    Alltoall(input_comm, pay, send_words, P.rpay, recv_words, 8, s, EPS_B200_EXCHANGE_KEYS);
     Cu(cudaFreeAsync(pay, s));
     pay = nullptr;
     P.ready = Event();
@@ -290,6 +327,8 @@ void eps_b200_client_destroy(EpsB200Client* c) {
     if (r.ticket) eps_b200_release(c->store, r.ticket, &st);
   }
   for (auto e : c->events) cudaEventDestroy(e);
+  for (auto& x : c->pending) { cudaEventDestroy(x.a); cudaEventDestroy(x.b); }
+  for (auto e : c->timing_events) cudaEventDestroy(e);
   for (auto& b : c->pinned) cudaFreeHost(b.first);
   delete c;
 }
@@ -335,7 +374,7 @@ int eps_b200_client_prepare(EpsB200Client* c, const EpsB200Feature* features, ui
     }
     try {
       c->Alltoall(c->input_comm, rows, std::vector<uint64_t>(n, width), rows + (size_t)n * width,
-                  std::vector<uint64_t>(n, width), 8, in);
+                  std::vector<uint64_t>(n, width), 8, in, EPS_B200_EXCHANGE_COUNTS);
       auto buf = c->TakePinned(2ull * n * width);
       P.counts = buf.first;
       P.counts_words = buf.second;
@@ -402,7 +441,7 @@ int eps_b200_client_lookup(EpsB200Client* c, uint64_t prepared, EpsB200Buffer* o
       Call(eps_b200_serve(c->store, P.rpay, P.peer.data(), P.tables.data(), P.pools.data(), n, F,
                           read_only, part_send, s, &R.ticket, &st), st);
       have_ticket = !read_only;
-      c->Alltoall(c->comm, part_send, R.send_f, part_recv, R.recv_f, 4, s);
+      c->Alltoall(c->comm, part_send, R.send_f, part_recv, R.recv_f, 4, s, EPS_B200_EXCHANGE_PARTIALS);
       Call(eps_b200_route_merge(c->store, R.route, part_recv, outputs, s, &st), st);
     } catch (...) {
       EpsB200Status st;
@@ -451,7 +490,7 @@ int eps_b200_client_push(EpsB200Client* c, uint64_t round, const EpsB200Buffer* 
       Call(eps_b200_route_gather(c->store, R.route, gradients, send, flag, s, &st), st);
       Call(eps_b200_comm_allreduce_max(c->comm, flag, 1, s, &st), st);
       // gradient rows travel in the layout the partials came back in
-      c->Alltoall(c->comm, send, R.recv_f, recv, R.send_f, 4, s);
+      c->Alltoall(c->comm, send, R.recv_f, recv, R.send_f, 4, s, EPS_B200_EXCHANGE_GRADIENTS);
       rc = eps_b200_serve_push(c->store, R.ticket, recv, R.peer.data(), R.tables.data(),
                                R.pools.data(), n, R.F, flag, s, wait, &st);
     } catch (...) {
@@ -466,6 +505,28 @@ int eps_b200_client_push(EpsB200Client* c, uint64_t round, const EpsB200Buffer* 
     EpsB200Status st2;
     Call(eps_b200_route_release(c->store, R.route, &st2), st2);
     c->rounds.erase(it);
+  });
+}
+
+int eps_b200_client_profile(EpsB200Client* c, int32_t mode, double* exchange_ms,
+                            uint64_t* exchange_bytes, uint64_t* exchange_calls,
+                            EpsB200Status* status) {
+  return Guard(status, [&] {
+    Require(c != nullptr, "invalid client");
+    std::lock_guard lock(c->mutex);
+    Cu(cudaSetDevice(c->device));
+    c->Collect();
+    for (int k = 0; k < EPS_B200_EXCHANGES; ++k) {
+      if (exchange_ms) exchange_ms[k] = c->ex_ms[k];
+      if (exchange_bytes) exchange_bytes[k] = c->ex_bytes[k];
+      if (exchange_calls) exchange_calls[k] = c->ex_calls[k];
+    }
+    if (mode == 1) {
+      for (int k = 0; k < EPS_B200_EXCHANGES; ++k) { c->ex_ms[k] = 0; c->ex_bytes[k] = 0; c->ex_calls[k] = 0; }
+      c->profiling = true;
+    } else if (mode == 0) {
+      c->profiling = false;
+    }
   });
 }
 

@@ -66,6 +66,9 @@ struct LookupFeature {
   // of offsets, which the unit validates) of a sequence feature
   unsigned long long unit_base;        // prefix of units over features
   unsigned long long units;
+  // the emit kernel's units: always kUnitBags bags (or kUnitPositions positions)
+  unsigned long long emit_base;
+  unsigned long long emit_units;
 };
 constexpr unsigned int kPadSlot = 0xFFFFFFFEu;   // slot marker of a padding key
 constexpr unsigned int kUnitBags = 8;
@@ -81,13 +84,11 @@ inline unsigned feature_unit_bags(unsigned pooling, unsigned long long key_count
   return (bag_count && key_count >= 8ull * bag_count) ? 1u : kUnitBags;
 }
 
-// Work units of one feature (see LookupFeature::units).
+// Work units of one feature (see LookupFeature::units); `unit_bags` bags per
+// unit of a pooled feature.
 inline unsigned long long feature_units(unsigned pooling, unsigned long long key_count,
-                                        unsigned long long bag_count) {
-  if (pooling != 2) {
-    const unsigned ub = feature_unit_bags(pooling, key_count, bag_count);
-    return (bag_count + ub - 1) / ub;
-  }
+                                        unsigned long long bag_count, unsigned unit_bags) {
+  if (pooling != 2) return (bag_count + unit_bags - 1) / unit_bags;
   const unsigned long long by_keys = (key_count + kUnitPositions - 1) / kUnitPositions;
   if (bag_count == 0) return by_keys;
   const unsigned long long by_offsets = (bag_count + 1 + kUnitPositions - 1) / kUnitPositions;

@@ -94,7 +94,8 @@ struct LookupLaunch {
   const LookupFeature* features;   // device array
   unsigned int feature_count;
   unsigned long long bag_total;
-  unsigned long long unit_total;   // work units over features (LookupFeature::units)
+  unsigned long long unit_total;   // gather work units over features (LookupFeature::units)
+  unsigned long long emit_total;   // emit work units over features (LookupFeature::emit_units)
   unsigned int shard_count, shard_id;
   int client;                      // 1: merge + mean (DistributedClient), 0: shard partial
   unsigned int slot_bits;

@@ -241,8 +241,8 @@ __global__ void __launch_bounds__(256, EPS_LOOKUP_MIN_BLOCKS) lookup_kernel(Look
 // length for mean, src/access/batch_access.cpp:107-108).  Validation matches the
 // gather kernel's.
 //
-// One warp per work unit (LookupFeature::units), 32 occurrences per step: a
-// pooled unit is unit_bags consecutive bags -- their offsets are read once, and
+// One warp per emit unit (LookupFeature::emit_units), 32 occurrences per step:
+// a pooled unit is kUnitBags consecutive bags -- their offsets are read once, and
 // lane j of a step finds its bag among them -- and a sequence unit is
 // kUnitPositions consecutive positions plus the same span of offsets, which it
 // validates (a sequence feature's bags do not shape its outputs).  So neither a
@@ -252,14 +252,14 @@ __global__ void __launch_bounds__(256) emit_kernel(LookupLaunch p) {
   __shared__ unsigned long long s_unit_base[kMaxFeatures + 1];
   __shared__ unsigned s_kept[8][kUnitBags];
   const unsigned fc = p.feature_count;
-  for (unsigned i = threadIdx.x; i < fc; i += blockDim.x) s_unit_base[i] = p.features[i].unit_base;
-  if (threadIdx.x == 0) s_unit_base[fc] = p.unit_total;
+  for (unsigned i = threadIdx.x; i < fc; i += blockDim.x) s_unit_base[i] = p.features[i].emit_base;
+  if (threadIdx.x == 0) s_unit_base[fc] = p.emit_total;
   __syncthreads();
   const unsigned lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const unsigned long long warp = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) >> 5;
   const unsigned long long nwarps = (gridDim.x * (unsigned long long)blockDim.x) >> 5;
   unsigned err = 0;
-  for (unsigned long long u = warp; u < p.unit_total; u += nwarps) {
+  for (unsigned long long u = warp; u < p.emit_total; u += nwarps) {
     unsigned lo = 0, hi = fc;
     while (hi - lo > 1) { const unsigned mid = (lo + hi) >> 1; if (s_unit_base[mid] <= u) lo = mid; else hi = mid; }
     const LookupFeature* F = p.features + lo;
@@ -303,41 +303,9 @@ __global__ void __launch_bounds__(256) emit_kernel(LookupLaunch p) {
       }
       continue;
     }
-    if (F->unit_bags == 1) {
-      // one long bag: the warp walks it 32 keys at a time
-      const unsigned long long b = lu;
-      unsigned long long o = 0;
-      if (lane < 2) o = F->offsets[b + lane];
-      unsigned long long s = __shfl_sync(~0u, o, 0), e = __shfl_sync(~0u, o, 1);
-      if (b == 0 && s != 0) err |= kLookupBadOffsets;
-      if (b + 1 == B && e != key_count) err |= kLookupBadOffsets;
-      if (s > e || e > key_count) { err |= kLookupBadOffsets; s = e = 0; }
-      unsigned long long kept = 0;
-      for (unsigned long long c0 = s; c0 < e; c0 += 32) {
-        const unsigned long long i = c0 + lane;
-        bool pad = false;
-        if (i < e) {
-          const KeyT ck = composite(F->keys[i], &pad);
-          static_cast<KeyT*>(p.occ_key)[occ_base + i] = ck;
-          p.occ_src[occ_base + i] = src_hi | (unsigned)b;
-        }
-        kept += __popc(__ballot_sync(~0u, i < e && !pad));
-      }
-      if (lane == 0) {
-        unsigned long long len = has_pad ? kept : e - s;
-        if (F->lengths) {
-          const unsigned long long given = F->lengths[b];
-          if (given < len) err |= kLookupShortLength;
-          len = given;
-        }
-        const bool mean = F->pooling == 1;
-        p.row_scale[F->scale_base + b] = (mean && len) ? __fdiv_rn(1.0f, (float)len) : 1.0f;
-      }
-      continue;
-    }
     // pooled: bags b0 .. b0 + nb - 1
-    const unsigned long long b0 = lu * F->unit_bags;
-    const unsigned nb = (unsigned)min((unsigned long long)F->unit_bags, B - b0);
+    const unsigned long long b0 = lu * kUnitBags;
+    const unsigned nb = (unsigned)min((unsigned long long)kUnitBags, B - b0);
     unsigned long long o = 0;
     if (lane <= nb) o = F->offsets[b0 + lane];
     unsigned long long s = o, e = __shfl_down_sync(0xffffffffu, o, 1);
@@ -410,8 +378,8 @@ cudaError_t launch_key(const LookupLaunch& p, cudaStream_t s) {
 }  // namespace
 
 cudaError_t launch_emit(const LookupLaunch& p, cudaStream_t stream) {
-  if (p.unit_total == 0) return cudaSuccess;
-  const unsigned long long want = (p.unit_total + 7) / 8;
+  if (p.emit_total == 0) return cudaSuccess;
+  const unsigned long long want = (p.emit_total + 7) / 8;
   const unsigned grid = (unsigned)(want < 148ull * 8 * 2 ? want : 148ull * 8 * 2);
   if (p.key64) emit_kernel<unsigned long long><<<grid, 256, 0, stream>>>(p);
   else emit_kernel<unsigned int><<<grid, 256, 0, stream>>>(p);

@@ -14,6 +14,11 @@
 //     the full bag gradients of pooled features and the position rows of its
 //     keys for sequence features.
 //
+// Adapter padding (PrepareAdapterInput, src/access/prepare_queue.cpp:58-85, which
+// runs before PrepareLookupInputs): keys equal to a feature's padding key go to
+// no shard; a padded feature's valid length is the bag's kept (non-padding)
+// key count, and its sequence positions holding padding read zeros.
+//
 // Bags without a key on a shard contribute an all-zero partial (0 + nothing) and
 // no gradient term, so they are dropped from that shard's part: a merge that
 // skips them adds +0.0f fewer times, which leaves every value unchanged (a
@@ -68,13 +73,16 @@ __global__ void __launch_bounds__(256) route_count(RouteLaunch p) {
     if (s > e || e > key_count) { err |= kLookupBadOffsets; s = e = 0; }
     if (F->lengths && F->lengths[b] != e - s) err |= kLookupShortLength;
     const unsigned long long key_space = F->rows;
+    const bool has_pad = F->has_padding != 0;
+    const unsigned long long pad_key = F->padding_key;
     unsigned count = 0;
     for (unsigned long long c0 = s; c0 < e; c0 += 32) {
       const unsigned long long i = c0 + lane;
       unsigned owner = ~0u;
       if (i < e) {
         const unsigned long long key = F->keys[i];
-        if (key < key_space) owner = (unsigned)(key % n);
+        if (has_pad && key == pad_key) owner = ~0u;          // dropped, goes nowhere
+        else if (key < key_space) owner = (unsigned)(key % n);
         else err |= kLookupBadKey;
       }
       for (unsigned o = 0; o < n; ++o) {
@@ -278,9 +286,13 @@ __global__ void __launch_bounds__(256) route_scatter(RouteLaunch p) {
     if (lane < 2) o2 = F->offsets[b + lane];
     const unsigned long long s = __shfl_sync(~0u, o2, 0), e = __shfl_sync(~0u, o2, 1);
     // (validated by route_count: s <= e <= key_count)
+    const bool has_pad = F->has_padding != 0;
+    const unsigned long long pad_key = F->padding_key;
     unsigned c = 0, kept = 0, k_at = 0;
+    if (lane < n) c = p.cnt[lane * B + g];
+    // the bag's valid length: its keys, or its non-padding keys (all routed)
+    const unsigned long long valid = has_pad ? __reduce_add_sync(~0u, c) : e - s;
     if (lane < n) {
-      c = p.cnt[lane * B + g];
       k_at = p.pk[lane * B + g];
       kept = p.pb[lane * B + g];
       if (c) {
@@ -289,7 +301,7 @@ __global__ void __launch_bounds__(256) route_scatter(RouteLaunch p) {
         const unsigned long long j = kept - fb;                 // kept index inside (shard, feature)
         const unsigned long long rel = fb - p.pb[lane * B];     // kept bags of earlier features
         p.payload[my_keys_end + rel + f + j + 1] = (unsigned long long)k_at + c - fk;
-        p.payload[my_lens_at + rel + j] = e - s;
+        p.payload[my_lens_at + rel + j] = valid;
         p.bag_map[kept] = (unsigned)b;
       }
     }
@@ -298,7 +310,10 @@ __global__ void __launch_bounds__(256) route_scatter(RouteLaunch p) {
       const unsigned long long i = c0 + lane;
       unsigned long long key = 0;
       unsigned owner = ~0u, rank = 0;
-      if (i < e) { key = F->keys[i]; owner = (unsigned)(key % n); }
+      if (i < e) {
+        key = F->keys[i];
+        owner = (has_pad && key == pad_key) ? ~0u : (unsigned)(key % n);
+      }
       const unsigned before = run;
       for (unsigned o = 0; o < n; ++o) {
         const unsigned m = __ballot_sync(~0u, owner == o);
@@ -343,8 +358,11 @@ __global__ void __launch_bounds__(256) route_merge(RouteLaunch p) {
     float acc[C];
 #pragma unroll
     for (int k = 0; k < C; ++k) acc[k] = 0.0f;
+    unsigned long long routed = 0;          // the bag's keys on all shards
     for (unsigned o = 0; o < n; ++o) {
-      if (!p.cnt[o * B + g]) continue;
+      const unsigned c = p.cnt[o * B + g];
+      routed += c;
+      if (!c) continue;
       const unsigned long long j = p.pb[o * B + g] - p.pb[o * B + s_base[f]];
       const float* row = p.partials + p.part_off[o * fc + f] + j * D;
 #pragma unroll
@@ -358,7 +376,8 @@ __global__ void __launch_bounds__(256) route_merge(RouteLaunch p) {
       }
     }
     const bool mean = F->pooling == 1;
-    const unsigned long long len = F->offsets[b + 1] - F->offsets[b];
+    // the valid length: the bag's keys, or (padding) its non-padding keys
+    const unsigned long long len = F->has_padding ? routed : F->offsets[b + 1] - F->offsets[b];
     const float denom = (float)len;
     float* out = p.outs[f] + b * D;
 #pragma unroll
@@ -373,8 +392,10 @@ __global__ void __launch_bounds__(256) route_merge(RouteLaunch p) {
     }
   }
   if (!p.has_sequence) return;
-  // sequence features: shard-ordered key q -> position pos_map[q]
-  for (unsigned long long q = gid; q < p.key_total; q += ngroups) {
+  // sequence features: shard-ordered key q -> position pos_map[q], over the keys
+  // that were routed (padding keys were not)
+  const unsigned long long routed_total = p.pk[(unsigned long long)n * B];
+  for (unsigned long long q = gid; q < routed_total; q += ngroups) {
     // shard: largest o with pk[o * B] <= q; then feature inside the shard
     unsigned o = 0;
     {
@@ -400,6 +421,25 @@ __global__ void __launch_bounds__(256) route_merge(RouteLaunch p) {
       float t[VEC];
       load_vec<VEC>(row + col, t);
       store_vec<VEC>(out + col, t);
+    }
+  }
+  // positions of padded sequence features that hold the padding key read zeros
+  for (unsigned f = 0; f < fc; ++f) {
+    const LookupFeature* F = p.features + f;
+    if (F->pooling != 2 || !F->has_padding) continue;
+    const unsigned D = F->dim;
+    for (unsigned long long i = gid; i < F->key_count; i += ngroups) {
+      if (F->keys[i] != F->padding_key) continue;
+      float* out = p.outs[f] + i * D;
+#pragma unroll
+      for (int it = 0; it < ITERS; ++it) {
+        const unsigned col = (it * G + gl) * VEC;
+        if (col >= D) continue;
+        float t[VEC];
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) t[v] = 0.0f;
+        store_vec<VEC>(out + col, t);
+      }
     }
   }
 }

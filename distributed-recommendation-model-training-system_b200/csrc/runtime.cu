@@ -101,6 +101,7 @@ struct Ticket {
   bool push_in_flight = false;
   bool lookup_checked = false;
   cudaEvent_t done = nullptr;       // recorded after an enqueued push's status copy
+  cudaEvent_t sorted = nullptr;     // recorded on the side stream after the coalescing sort
   // layout
   std::vector<unsigned> feature_ids, feature_tables, dims, ranks;
   std::vector<unsigned long long> grad_rows, scale_base;
@@ -180,10 +181,10 @@ struct EpsB200Store {
   std::mutex mutex;
   cudaStream_t own = nullptr;
   // the coalescing sort of a lookup runs on `side`, concurrently with the
-  // gather on the caller's stream: fork after the occurrence list, join before
-  // anything that follows the lookup on the caller's stream
+  // gather on the caller's stream: fork after the occurrence list; the ticket's
+  // `sorted` event orders the push (and every call that reads the ticket) after it
   cudaStream_t side = nullptr;
-  cudaEvent_t fork = nullptr, join = nullptr;
+  cudaEvent_t fork = nullptr;
   // a push's piece sums run on `side` concurrently with its prescan
   cudaEvent_t push_fork = nullptr, push_join = nullptr;
   cudaStream_t last = nullptr;
@@ -310,6 +311,12 @@ struct EpsB200Store {
   }
 
   void FreeTicket(std::map<unsigned long long, Ticket>::iterator it, cudaStream_t stream) {
+    if (it->second.sorted) {
+      // the sort on the side stream writes the slab: release it after the sort
+      cudaStreamWaitEvent(stream, it->second.sorted, 0);
+      sync_pool.push_back(it->second.sorted);
+      it->second.sorted = nullptr;
+    }
     if (it->second.slab) cudaFreeAsync(it->second.slab, stream);
     if (it->second.slot >= 0) free_slots.push_back(it->second.slot);
     tickets.erase(it);
@@ -483,7 +490,6 @@ int eps_b200_create(const EpsB200Options* options, EpsB200Store** out, EpsB200St
         Cuda(cudaStreamCreateWithPriority(&s->side, cudaStreamNonBlocking, greatest));
       }
       Cuda(cudaEventCreateWithFlags(&s->fork, cudaEventDisableTiming));
-      Cuda(cudaEventCreateWithFlags(&s->join, cudaEventDisableTiming));
       Cuda(cudaEventCreateWithFlags(&s->push_fork, cudaEventDisableTiming));
       Cuda(cudaEventCreateWithFlags(&s->push_join, cudaEventDisableTiming));
       // one status slot per live ticket plus a scratch slot (index max_live_tickets)
@@ -526,13 +532,15 @@ void eps_b200_destroy(EpsB200Store* s) {
     for (auto& x : s->pending) { cudaEventDestroy(x.a); cudaEventDestroy(x.b); }
     for (auto e : s->event_pool) cudaEventDestroy(e);
     for (auto e : s->sync_pool) cudaEventDestroy(e);
-    for (auto& [id, t] : s->tickets) if (t.done) cudaEventDestroy(t.done);
+    for (auto& [id, t] : s->tickets) {
+      if (t.done) cudaEventDestroy(t.done);
+      if (t.sorted) cudaEventDestroy(t.sorted);
+    }
     if (s->sticky_error) cudaFree(s->sticky_error);
     if (s->host_status) cudaFreeHost(s->host_status);
     if (s->last_done) cudaEventDestroy(s->last_done);
     if (s->side) cudaStreamDestroy(s->side);
     if (s->fork) cudaEventDestroy(s->fork);
-    if (s->join) cudaEventDestroy(s->join);
     if (s->push_fork) cudaEventDestroy(s->push_fork);
     if (s->push_join) cudaEventDestroy(s->push_join);
     if (s->own) cudaStreamDestroy(s->own);
@@ -733,7 +741,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       Ticket t;
       t.read_only = read_only != 0;
       unsigned long long bag_base = 0, occ_base = 0, scale_base = 0, koff = 0,
-                         ooff = 0, loff = 0, hoff = 0, unit_base = 0;
+                         ooff = 0, loff = 0, hoff = 0, unit_base = 0, emit_base = 0;
       t.table_ids.resize(ranks.size());
       t.table_occ.assign(ranks.size(), 0);
       for (auto& [id, rank] : ranks) t.table_ids[rank] = id;
@@ -785,10 +793,13 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         L.feature_index = (unsigned)i;
         L.has_padding = f.has_padding ? 1u : 0u;
         L.padding_key = f.padding_key;
-        L.unit_base = unit_base;
-        L.units = feature_units(f.pooling, f.key_count, L.bag_count);
         L.unit_bags = feature_unit_bags(f.pooling, f.key_count, L.bag_count);
+        L.unit_base = unit_base;
+        L.units = feature_units(f.pooling, f.key_count, L.bag_count, L.unit_bags);
         unit_base += L.units;
+        L.emit_base = emit_base;
+        L.emit_units = feature_units(f.pooling, f.key_count, L.bag_count, kUnitBags);
+        emit_base += L.emit_units;
         bag_base += L.bag_count;
         occ_base += f.key_count;
         scale_base += rows;
@@ -806,6 +817,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       lp.feature_count = (unsigned)count;
       lp.bag_total = bag_base;
       lp.unit_total = unit_base;
+      lp.emit_total = emit_base;
       lp.shard_count = s.opt.shard_count;
       lp.shard_id = s.opt.shard_id;
       lp.client = shard_partial ? 0 : 1;
@@ -828,7 +840,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         // stream concurrently with the gather
         ev = s.Begin(stream);
         Cuda(launch_emit(lp, stream));
-        s.End(EPS_B200_PHASE_EMIT, ev, stream, unit_base ? 1u : 0u);
+        s.End(EPS_B200_PHASE_EMIT, ev, stream, emit_base ? 1u : 0u);
         Cuda(cudaEventRecord(s.fork, stream));
       }
       if (gather) {
@@ -836,8 +848,8 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         Cuda(launch_lookup(lp, stream));
         s.End(EPS_B200_PHASE_LOOKUP, ev, stream, unit_base ? 1u : 0u);
       }
-      // ---- host outputs: final once the gather ends, so their copies are queued
-      // before the stream joins the sort and overlap the sort's remaining work
+      // ---- host outputs: final once the gather ends; their copies overlap the
+      // sort, which runs on the side stream
       hoff = 0;
       for (uint64_t i = 0; gather && i < count; ++i) {
         if (outputs[i].device >= 0) continue;
@@ -881,8 +893,11 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         Cuda(launch_row_plan(pp, sort_stream));
         s.End(EPS_B200_PHASE_SORT, ev, sort_stream,
               sort_launch_count(sp) + segment_launch_count(total_keys) + (total_keys ? 1u : 0u));
-        Cuda(cudaEventRecord(s.join, s.side));
-        Cuda(cudaStreamWaitEvent(stream, s.join, 0));
+        // the caller's stream does not wait for the sort: the lookup's outputs
+        // are final when the gather ends; the push (and every call that reads
+        // the ticket) waits for this event
+        t.sorted = s.SyncEvent();
+        Cuda(cudaEventRecord(t.sorted, s.side));
         t.keys = swapped ? P(at_k1) : P(at_k0);
         t.srcs = reinterpret_cast<unsigned*>(swapped ? P(at_s1) : P(at_s0));
         t.n = total_keys;
@@ -916,6 +931,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
                                cudaMemcpyDeviceToHost, stream));
       }
       unsigned sync_err = 0;
+      if (synchronous && t.sorted) Cuda(cudaStreamWaitEvent(stream, t.sorted, 0));
       if (synchronous) {
         HostStatus& scratch = s.host_status[s.opt.max_live_tickets];
         if (read_only)
@@ -927,6 +943,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       ++s.stats.lookups;
       if (read_only || sync_err) {
         if (slot >= 0) s.free_slots.push_back(slot);
+        if (t.sorted) { s.sync_pool.push_back(t.sorted); t.sorted = nullptr; }
         char* owned = slab;
         slab = nullptr;                 // freed exactly once, here
         Cuda(cudaFreeAsync(owned, stream));
@@ -945,6 +962,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       s.Done(stream);
     } catch (...) {
       cudaStreamSynchronize(stream);
+      cudaStreamSynchronize(s.side);
       if (slab) cudaFreeAsync(slab, stream);
       throw;
     }
@@ -1003,9 +1021,9 @@ int eps_b200_lookup_noalloc(EpsB200Store* store, const EpsB200Feature* features,
       L.feature_index = (unsigned)i;
       L.has_padding = f.has_padding ? 1u : 0u;
       L.padding_key = f.padding_key;
+      L.unit_bags = feature_unit_bags(f.pooling, f.key_count, L.bag_count);
       L.unit_base = unit_base;
-      L.units = feature_units(f.pooling, f.key_count, L.bag_count);
-        L.unit_bags = feature_unit_bags(f.pooling, f.key_count, L.bag_count);
+      L.units = feature_units(f.pooling, f.key_count, L.bag_count, L.unit_bags);
       unit_base += L.units;
       bag_base += L.bag_count;
     }
@@ -1071,6 +1089,8 @@ int PushEntry(EpsB200Store* store, uint64_t ticket, const EpsB200Buffer* gradien
     }
     Ticket& t = it->second;
     Require(!t.read_only, "ticket does not belong to update");
+    // the push reads the ticket's coalesced occurrence list
+    if (t.sorted) Cuda(cudaStreamWaitEvent(stream, t.sorted, 0));
     const size_t nf = t.feature_ids.size();
     Require(gradients && count == nf, "gradient feature count mismatch");
     // gradient index by feature id (src/access/batch_access.cpp:86-96)
@@ -1302,8 +1322,10 @@ int eps_b200_ticket_coalesced(EpsB200Store* store, uint64_t ticket, uint32_t* ta
     Require(it != s.tickets.end(), "unknown lookup ticket");
     const Ticket& t = it->second;
     Require(!t.read_only, "ticket does not belong to update");
-    // the ticket's lookup, its sort included, ended before the store's latest call did
+    // the ticket's lookup ended before the store's latest call did; its sort
+    // (side stream) is waited for separately
     Cuda(cudaEventSynchronize(s.last_done));
+    if (t.sorted) Cuda(cudaEventSynchronize(t.sorted));
     unsigned lookup_error = 0, seg_total = 0;
     Cuda(cudaMemcpy(&lookup_error, t.lookup_error, sizeof(unsigned), cudaMemcpyDeviceToHost));
     Require(!lookup_error, EpsB200Store::LookupMessage(lookup_error).c_str());
@@ -1363,6 +1385,7 @@ int eps_b200_synchronize(EpsB200Store* store, EpsB200Status* status) {
     s.Activate();
     cudaStream_t stream = s.Use(nullptr);
     s.Sync(stream);
+    Cuda(cudaStreamSynchronize(s.side));      // lookups' sorts set their error words too
     std::string first = s.deferred;
     s.deferred.clear();
     s.inflight.clear();
@@ -1599,7 +1622,8 @@ int eps_b200_route(EpsB200Store* store, const EpsB200Feature* features, uint64_t
       Require(f.offset_count >= 1 && f.offsets, "invalid bag offsets");
       Require(f.offset_count > 1 || f.key_count == 0, "invalid bag offsets");
       Require(!f.key_count || f.keys, "null feature keys");
-      Require(!f.has_padding, "padding keys are not supported by the multi-GPU round");
+      Require(!f.has_padding || !f.valid_lengths,
+              "valid lengths are derived from the padding key; pass one or the other");
       const unsigned long long rows = f.pooling == 2 ? f.key_count : f.offset_count - 1;
       Require(rows < (1ull << kRowBits) && f.key_count < (1ull << 31),
               "feature exceeds the per-feature row limit", EPS_B200_CAPACITY_EXCEEDED);
@@ -1615,6 +1639,8 @@ int eps_b200_route(EpsB200Store* store, const EpsB200Feature* features, uint64_t
       L.pooling = f.pooling;
       L.table_rank = f.table;            // a route's descriptors carry the table id
       L.feature_index = (unsigned)i;
+      L.has_padding = f.has_padding ? 1u : 0u;
+      L.padding_key = f.padding_key;
       r.B += L.bag_count;
       r.N += f.key_count;
       r.dims.push_back(t.def.dimension);

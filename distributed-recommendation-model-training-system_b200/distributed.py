@@ -465,6 +465,18 @@ class NativeClient:
         _check(self.lib.eps_b200_client_push(self._h, round_id, self.store._buffers(gradients),
                                              self._stream(stream), int(wait), C.byref(st)), st)
 
+    EXCHANGES = ("counts", "keys", "partials", "gradients")
+
+    def profile(self, mode: int = -1) -> dict:
+        """eps_b200_client_profile: per exchange {ms, bytes, calls} (mode 1
+        resets and starts timing, 0 stops)."""
+        ms = (C.c_double * 4)()
+        by = (C.c_uint64 * 4)()
+        ca = (C.c_uint64 * 4)()
+        st = Status()
+        _check(self.lib.eps_b200_client_profile(self._h, mode, ms, by, ca, C.byref(st)), st)
+        return {k: {"ms": ms[i], "bytes": by[i], "calls": ca[i]} for i, k in enumerate(self.EXCHANGES)}
+
     def release(self, handle: int):
         """Drops a prepared batch or an unpushed round."""
         self._keep.pop(handle, None)

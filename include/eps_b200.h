@@ -109,7 +109,8 @@ typedef struct {
  * pooled bags sum the other keys and mean divides by their count; sequence
  * outputs keep every position, padding positions read 0 and take no gradient.
  * With has_padding, valid_lengths must be NULL (the kept counts are the
- * lengths).  The multi-GPU round does not take padding keys. */
+ * lengths).  The multi-GPU round takes padding keys too: they go to no shard,
+ * and every shard receives the kept counts as the bags' valid lengths. */
 typedef struct {
   uint32_t table, feature, pooling, has_padding;
   const uint64_t* keys; uint64_t key_count;
@@ -410,6 +411,23 @@ EPS_B200_EXPORT int eps_b200_client_lookup(EpsB200Client* client, uint64_t prepa
 EPS_B200_EXPORT int eps_b200_client_push(EpsB200Client* client, uint64_t round,
                                          const EpsB200Buffer* gradients, void* stream, int32_t wait,
                                          EpsB200Status* status);
+/* Exchanges of a round, for eps_b200_client_profile. */
+enum {
+  EPS_B200_EXCHANGE_COUNTS = 0,      /* count rows of a prepared batch */
+  EPS_B200_EXCHANGE_KEYS = 1,        /* keys, kept-bag offsets and valid lengths */
+  EPS_B200_EXCHANGE_PARTIALS = 2,    /* pooled partials / sequence rows back to the requesters */
+  EPS_B200_EXCHANGE_GRADIENTS = 3,   /* gradient rows to the owners */
+  EPS_B200_EXCHANGES = 4
+};
+/* Per-exchange device time (CUDA events around each all-to-all on the stream it
+ * is enqueued on, collected when asked), bytes this rank sent to the other
+ * ranks, and calls.  No counterpart in the reference (its shards talk over
+ * BRPC).  mode 1: reset and start timing, 0: stop, -1: leave as is; bytes and
+ * calls are always counted.  Each output (may be NULL) has EPS_B200_EXCHANGES
+ * entries. */
+EPS_B200_EXPORT int eps_b200_client_profile(EpsB200Client* client, int32_t mode, double* exchange_ms,
+                                            uint64_t* exchange_bytes, uint64_t* exchange_calls,
+                                            EpsB200Status* status);
 /* Drops a prepared batch or an unpushed round (DistributedClient::Release). */
 EPS_B200_EXPORT int eps_b200_client_release(EpsB200Client* client, uint64_t handle,
                                             EpsB200Status* status);

@@ -25,7 +25,7 @@ import pytest
 
 import sharded_harness as H
 from conftest import gpu_available, import_package
-from oracle_lib import Oracle
+from oracle_lib import Feature, Oracle
 
 F32 = np.float32
 
@@ -180,6 +180,95 @@ def test_sharded_round_three_ranks_one_gpu():
             client = D.ShardedClient(stores[rank], device="cuda:0", comm=comm)
             _rank_body(eps, D, stores[rank], client, rank, n, steps, "cuda:0", outputs,
                        threading.Lock())
+        except BaseException as e:          # noqa: BLE001 -- reported below
+            errors.append((rank, e))
+            comm.barrier.abort()
+
+    threads = [threading.Thread(target=run, args=(r,)) for r in range(n)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=300)
+    assert not errors, errors
+    for r, s in enumerate(stores):
+        s.synchronize()
+        _check_state(s, oracle, r, n)
+        assert s.stats()["live_tickets"] == 0
+        s.close()
+
+
+def _drop_padding(f, pad):
+    """PrepareAdapterInput (src/access/prepare_queue.cpp:58-85) on the host: the
+    feature without its padding keys, and the kept positions."""
+    keep = f.keys != np.uint64(pad)
+    lens = np.diff(f.offsets.astype(np.int64))
+    bag = np.repeat(np.arange(len(lens)), lens)
+    kept = np.bincount(bag[keep], minlength=len(lens))
+    offs = np.concatenate([[0], np.cumsum(kept)]).astype(np.uint64)
+    return Feature(f.table, f.feature, f.pooling, f.keys[keep], offs), np.nonzero(keep)[0]
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not gpu_available(), reason="needs a GPU")
+def test_sharded_round_with_padding_three_ranks_one_gpu():
+    """Adapter padding in the multi-GPU round: padding keys go to no shard, every
+    shard gets the kept counts as valid lengths (mean divides by them), sequence
+    positions holding padding read zeros -- bit for bit the reference's adapter
+    (PrepareAdapterInput) followed by its n-shard lookup and push of the
+    combined request."""
+    import torch
+    eps = import_package()
+    D = _client_module()
+    n, steps, pad = 3, 2, 7
+    rng = np.random.default_rng(5)
+    batches = {}
+    for step in range(steps):
+        for r in range(n):
+            feats, grads = H.make_batch(r, step)
+            for f in feats:
+                f.keys[rng.random(len(f.keys)) < 0.3] = pad
+            if len(feats[1].offsets) > 3 and feats[1].offsets[3] > feats[1].offsets[2]:
+                feats[1].keys[int(feats[1].offsets[2]):int(feats[1].offsets[3])] = pad  # all padding
+            batches[(r, step)] = (feats, grads)
+    oracle = Oracle(H.TABLES)
+    expect = {}
+    for step in range(steps):
+        cf, cg = H.concat([batches[(r, step)] for r in range(n)])
+        compact = [_drop_padding(f, pad) for f in cf]
+        outs = oracle.lookup([c for c, _ in compact], shards=n)
+        full = []
+        for f, (c, pos), o in zip(cf, compact, outs):
+            if f.pooling == H.SEQUENCE:
+                z = np.zeros((len(f.keys), o.shape[1]), np.float32)
+                z[pos] = o
+                full.append(z)
+            else:
+                full.append(o)
+        expect[step] = full
+        cgrads = [g[pos] if f.pooling == H.SEQUENCE else g
+                  for f, (c, pos), g in zip(cf, compact, cg)]
+        assert oracle.push([c for c, _ in compact], cgrads) == 0
+    comm = H.ThreadComm(n)
+    stores = [_make_store(eps, r, n) for r in range(n)]
+    errors = []
+
+    def run(rank):
+        try:
+            comm.bind(rank)
+            torch.cuda.set_device(0)
+            client = D.ShardedClient(stores[rank], device="cuda:0", comm=comm)
+            for step in range(steps):
+                feats, grads = batches[(rank, step)]
+                ins = [eps.FeatureInput(f.table, f.feature, f.pooling,
+                                        torch.from_numpy(f.keys.astype(np.int64)).cuda(),
+                                        torch.from_numpy(f.offsets.astype(np.int64)).cuda(),
+                                        padding_key=pad) for f in feats]
+                handle, outs = client.lookup(ins)
+                F = len(feats)
+                for f in range(F):
+                    assert np.array_equal(bits(outs[f].cpu().numpy()),
+                                          bits(expect[step][rank * F + f])), (step, f)
+                client.push(handle, [torch.from_numpy(g).cuda() for g in grads], wait=True)
         except BaseException as e:          # noqa: BLE001 -- reported below
             errors.append((rank, e))
             comm.barrier.abort()
