@@ -70,7 +70,7 @@ class Table(C.Structure):
                 ("initial_beta2_power", C.c_float), ("weight_min", C.c_float),
                 ("weight_max", C.c_float), ("initialization_min", C.c_float),
                 ("initialization_max", C.c_float), ("initialization_seed", C.c_uint64),
-                ("key_space", C.c_uint64)]
+                ("key_space", C.c_uint64), ("capacity", C.c_uint64)]
 
 
 class Feature(C.Structure):
@@ -214,7 +214,7 @@ def load_library() -> C.CDLL:
     for name in ENTRY_POINTS[1:]:
         if name not in ("eps_b200_destroy", "eps_b200_comm_destroy", "eps_b200_client_destroy"):
             getattr(lib, name).restype = C.c_int
-    if lib.eps_b200_abi_version() != 2:
+    if lib.eps_b200_abi_version() != 3:
         raise ImportError("libeps_b200.so ABI version mismatch")
     _lib = lib
     return lib
@@ -226,7 +226,11 @@ load_library()
 # ----------------------------------------------------------- python mirror
 @dataclass
 class TableDefinition:
-    """eps::TableDefinition + OptimizerConfig (include/eps/types.hpp:76-97)."""
+    """eps::TableDefinition + OptimizerConfig (include/eps/types.hpp:76-97).
+
+    key_space > 0: a dense table of keys [0, key_space).  key_space == 0: a hashed
+    table -- any 64-bit key, rows created on first touch (ShardStore::Ensure,
+    src/store/shard_store.cpp:76-115), at most `capacity` rows on this shard."""
     id: int
     dimension: int
     key_space: int
@@ -242,6 +246,7 @@ class TableDefinition:
     initialization_seed: int = 42
     shard_count: int = 1
     partition_epoch: int = 1
+    capacity: int = 0
 
 
 @dataclass
@@ -333,7 +338,7 @@ class ParameterStore:
         ct = Table(t.id, t.dimension, t.shard_count, 1 if b else 0, t.partition_epoch,
                    t.learning_rate, t.beta1, t.beta2, t.epsilon, t.initial_beta1_power,
                    t.initial_beta2_power, *(b if b else (0.0, 0.0)), t.initialization_min,
-                   t.initialization_max, t.initialization_seed, t.key_space)
+                   t.initialization_max, t.initialization_seed, t.key_space, t.capacity)
         st = Status()
         _check(self.lib.eps_b200_create_table(self._h, C.byref(ct), C.byref(st)), st)
         self._tables[t.id] = t

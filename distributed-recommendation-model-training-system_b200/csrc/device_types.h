@@ -24,6 +24,31 @@ struct DeviceTable {
   unsigned int pad;
 };
 
+// The id -> slot index of a hashed table (any u64 key; a row is created on its
+// first touch, as ShardStore::Ensure does, src/store/shard_store.cpp:76-115):
+// open addressing with linear probing over `mask + 1` entries (at most half
+// full), a key entry claimed by one compare-and-swap; the winner takes the next
+// slot and writes the row's initial value.  Device-resident, one per table.
+struct HashIndex {
+  unsigned long long* keys;         // [mask + 1], kEmptyKey = free (key ~0 uses `top`)
+  unsigned int* slots;              // [mask + 2] slot of each entry (entry mask + 1: key ~0)
+  unsigned long long* slot_keys;    // [capacity] key of each slot
+  unsigned long long* used;         // slots handed out (may pass capacity: those failed)
+  unsigned int* top;                // entry of key ~0 claimed
+  unsigned long long mask;
+  unsigned long long capacity;
+  // the row initializer (shard_store.cpp:104-111)
+  float* state;
+  unsigned long long* updates;
+  unsigned int dim, table_id;
+  unsigned long long seed;
+  float init_min, init_max;
+  int has_bounds;
+  float bound_min, bound_max;
+};
+constexpr unsigned long long kEmptyKey = ~0ull;
+constexpr unsigned int kNoSlot = 0xFFFFFFFFu;       // entry without a usable slot
+
 // One table as seen by a Push: constant optimizer parameters plus pointers.
 struct PushTable {
   float* state;
@@ -69,6 +94,10 @@ struct LookupFeature {
   // the emit kernel's units: always kUnitBags bags (or kUnitPositions positions)
   unsigned long long emit_base;
   unsigned long long emit_units;
+  // hashed table: slots[i] is occurrence i's resolved slot (kPadSlot: padding,
+  // kNoSlot: not resolved -- another shard's key or the table is full)
+  const HashIndex* hash;
+  const unsigned int* slots;
 };
 constexpr unsigned int kPadSlot = 0xFFFFFFFEu;   // slot marker of a padding key
 constexpr unsigned int kUnitBags = 8;
@@ -116,6 +145,7 @@ enum LookupErrorBits : unsigned int {
   kLookupBadKey = 2u,           // key routed to another shard / outside the table
   kLookupShortLength = 4u,      // src/access/batch_access.cpp:18-20
   kLookupSortFailed = 8u,       // a coalescing-sort wait ran out (never expected)
+  kLookupCapacity = 64u,        // a hashed table holds its capacity of rows already
 };
 
 // Per-push control block (device).  Zeroed before each push.

@@ -303,6 +303,25 @@ struct InitLaunch {
 };
 cudaError_t launch_init(const InitLaunch& p, cudaStream_t stream);
 
+// Hashed tables (store.cu).  Resolves the keys of every hashed feature of a
+// lookup: each occurrence's slot into LookupFeature::slots, creating rows for
+// unseen keys (two launches: claim / insert, then entry -> slot).  `entries`
+// is scratch of one u32 per occurrence of the lookup.
+struct ResolveLaunch {
+  const LookupFeature* features;   // device
+  unsigned int feature_count;
+  unsigned long long key_total;    // occurrences of the lookup (occ_base prefix)
+  unsigned int shard_count, shard_id;
+  unsigned int* entries;           // [key_total]
+  unsigned int* error;             // LookupErrorBits
+};
+cudaError_t launch_resolve(const ResolveLaunch& p, cudaStream_t stream);   // two launches
+// Keys of one hashed table -> slots (creating rows), for ReadState / Load.
+// `index` is a host copy of the table's HashIndex (its pointers are device memory).
+cudaError_t launch_resolve_keys(const HashIndex* index, const unsigned long long* keys,
+                                unsigned long long n, unsigned int* entries, unsigned int* slots,
+                                unsigned int* error, cudaStream_t stream);
+
 // Row state gather/scatter for ReadState / Load (src/cuda/cache_backend.cu
 // ReadStateKernel / ScatterState contract, slots from keys).
 cudaError_t launch_read_rows(const float* state, const unsigned long long* updates,
@@ -315,6 +334,15 @@ cudaError_t launch_write_rows(float* state, unsigned long long* updates, unsigne
                               const unsigned long long* keys, unsigned long long n,
                               const float* packed, const unsigned long long* upd_in,
                               DeviceTable* dtable, cudaStream_t stream);
+// The same by resolved slots (hashed tables): slots[r] instead of keys[r] / shards.
+cudaError_t launch_read_slots(const float* state, const unsigned long long* updates,
+                              unsigned int dim, const unsigned int* slots, unsigned long long n,
+                              float* packed, unsigned long long* upd_out, unsigned int* error,
+                              cudaStream_t stream);
+cudaError_t launch_write_slots(float* state, unsigned long long* updates, unsigned int dim,
+                               const unsigned int* slots, unsigned long long n, const float* packed,
+                               const unsigned long long* upd_in, DeviceTable* dtable,
+                               cudaStream_t stream);
 
 // Allocation-free lookup (eps_b200_lookup_noalloc): feature descriptors live in
 // a fixed file-scope device array in noalloc.cu instead of an allocated block.

@@ -133,6 +133,10 @@ __global__ void __launch_bounds__(256, EPS_LOOKUP_MIN_BLOCKS) lookup_kernel(Look
         unsigned slot = ~0u;              // slots fit 32 bits: rows < 2^32 - 2 per shard
         if (i < e && has_pad && key == pad_key) {
           slot = kPadSlot;
+        } else if (i < e && F->slots) {
+          const unsigned hs = F->slots[i];      // a hashed table's resolved slot
+          if (hs < kPadSlot) slot = hs;
+          else err |= kLookupBadKey;
         } else if (i < e) {
           unsigned long long sl, sh;
           if (p.shard_count == 1) { sl = key; sh = 0; }
@@ -270,10 +274,17 @@ __global__ void __launch_bounds__(256) emit_kernel(LookupLaunch p) {
     const unsigned long long rows = F->rows, occ_base = F->occ_base;
     const unsigned src_hi = F->feature_index << kRowBits;
     const KeyT rank_bits = KeyT(F->table_rank) << p.slot_bits;
-    // composite key of one occurrence; pad / bad reported through the flags
-    auto composite = [&](unsigned long long key, bool* pad) -> KeyT {
+    // composite key of occurrence `idx` (its key `key`); pad / bad reported
+    // through the flags; a hashed table's slot was resolved before
+    auto composite = [&](unsigned long long key, unsigned long long idx, bool* pad) -> KeyT {
       *pad = false;
       if (has_pad && key == pad_key) { *pad = true; return KeyT(p.pad_key); }
+      if (F->slots) {
+        const unsigned hs = F->slots[idx];
+        if (hs < kPadSlot) return rank_bits | KeyT(hs);
+        err |= kLookupBadKey;
+        return KeyT(0);
+      }
       unsigned long long sl, sh;
       if (p.shard_count == 1) { sl = key; sh = 0; }
       else { sl = key / p.shard_count; sh = key - sl * p.shard_count; }
@@ -289,7 +300,7 @@ __global__ void __launch_bounds__(256) emit_kernel(LookupLaunch p) {
         const unsigned long long i = base + q * 32 + lane;
         if (i < key_count) {
           bool pad;
-          const KeyT ck = composite(F->keys[i], &pad);
+          const KeyT ck = composite(F->keys[i], i, &pad);
           static_cast<KeyT*>(p.occ_key)[occ_base + i] = ck;
           p.occ_src[occ_base + i] = src_hi | (unsigned)i;
           p.row_scale[F->scale_base + i] = 1.0f;
@@ -342,7 +353,7 @@ __global__ void __launch_bounds__(256) emit_kernel(LookupLaunch p) {
       if (i < total) {
         const unsigned long long occ = sk + (i - ek);
         bool pad;
-        const KeyT ck = composite(F->keys[occ], &pad);
+        const KeyT ck = composite(F->keys[occ], occ, &pad);
         static_cast<KeyT*>(p.occ_key)[occ_base + occ] = ck;
         p.occ_src[occ_base + occ] = src_hi | (unsigned)(b0 + k);
         if (has_pad && !pad) atomicAdd(&s_kept[w][k], 1u);

@@ -11,12 +11,12 @@
 //
 // The block below is one file-scope array per GPU, created when the library's
 // device code is loaded on that GPU and held until the process exits.  It
-// holds the descriptors of at most kNoAllocFeatures features (about 26 KiB).
-// Every allocation-free lookup on a GPU reuses it and overwrites what the
-// previous call left there.  The calls of one store are ordered on the GPU
-// (each waits for the store's previous call), so only calls of different stores
-// on one GPU, or of other users of this library in the same process, can
-// overlap and race on it.
+// holds the descriptors of at most kNoAllocFeatures features (168 bytes each,
+// 42 KiB in all).  Every allocation-free lookup on a GPU reuses it and
+// overwrites what the previous call left there.  The calls of one store are
+// ordered on the GPU (each waits for the store's previous call), so only calls
+// of different stores on one GPU, or of other users of this library in the
+// same process, can overlap and race on it.
 //
 // The descriptors reach the array through the parameters of a small kernel
 // (up to 24 per launch): the launch copies its parameters when it is enqueued,
@@ -35,6 +35,7 @@ struct NoAllocChunk {
   unsigned first, count;
   LookupFeature f[kNoAllocChunk];
 };
+static_assert(sizeof(LookupFeature) == 168, "descriptor size stated in eps_b200.h");
 static_assert(sizeof(NoAllocChunk) <= 4096, "descriptor chunk must fit the kernel parameter space");
 
 __global__ void noalloc_store_descriptors(NoAllocChunk c) {

@@ -80,8 +80,29 @@ struct Table {
   float* state = nullptr;
   unsigned long long* updates = nullptr;
   DeviceTable* dtable = nullptr;
-  unsigned long long rows = 0;
+  unsigned long long rows = 0;      // slots (dense: of the key space; hashed: the capacity)
   unsigned long long bytes = 0;
+  // hashed tables (def.key_space == 0): the id -> slot index
+  bool hashed = false;
+  HashIndex index{};                // host copy; its pointers are device memory
+  HashIndex* dindex = nullptr;      // device copy, for the lookup kernels
+  unsigned long long entries = 0;   // index entries (power of two)
+
+  // Frees the table's device memory.
+  void Free() {
+    cudaFree(state); cudaFree(updates); cudaFree(dtable);
+    if (hashed) {
+      cudaFree(index.keys); cudaFree(index.slots); cudaFree(index.slot_keys);
+      cudaFree(index.used); cudaFree(dindex);
+    }
+  }
+  // Empties a hashed table's index (no key, no slot used); stream-ordered.
+  void ClearIndex(cudaStream_t stream) const {
+    if (!hashed) return;
+    Cuda(cudaMemsetAsync(index.keys, 0xFF, entries * 8, stream));
+    Cuda(cudaMemsetAsync(index.slots, 0xFF, (entries + 1) * 4, stream));
+    Cuda(cudaMemsetAsync(index.used, 0, 16, stream));      // used + top
+  }
 };
 
 // Per-ticket status block, laid out identically in the device slab and in the
@@ -335,6 +356,7 @@ struct EpsB200Store {
   // Lookup-input errors recorded by the lookup kernel (LookupErrorBits).
   static std::string LookupMessage(unsigned bits) {
     if (bits & kLookupSortFailed) return "coalescing sort did not complete";
+    if (bits & kLookupCapacity) return "hashed table capacity exceeded";
     if (bits & kLookupBadOffsets) return "invalid bag offsets";
     if (bits & kLookupShortLength) return "original bag length is smaller than shard contribution";
     return "key routed to wrong shard or outside the table";
@@ -425,7 +447,8 @@ void ValidateTable(const EpsB200Store& s, const EpsB200Table& d) {
   Require(std::isfinite(d.initialization_min) && std::isfinite(d.initialization_max) &&
               d.initialization_min <= d.initialization_max,
           "invalid initializer bounds");
-  Require(d.key_space > 0, "invalid key space");
+  Require(d.key_space > 0 || (d.capacity > 0 && d.capacity < 0xFFFFFFF0ull),
+          "invalid key space (a hashed table, key space 0, needs a capacity below 2^32 - 16)");
 }
 
 bool SameTable(const EpsB200Table& a, const EpsB200Table& b) {
@@ -438,7 +461,8 @@ bool SameTable(const EpsB200Table& a, const EpsB200Table& b) {
          (!a.has_weight_bounds || (a.weight_min == b.weight_min && a.weight_max == b.weight_max)) &&
          a.initialization_min == b.initialization_min &&
          a.initialization_max == b.initialization_max &&
-         a.initialization_seed == b.initialization_seed && a.key_space == b.key_space;
+         a.initialization_seed == b.initialization_seed && a.key_space == b.key_space &&
+         (a.key_space != 0 || a.capacity == b.capacity);
 }
 
 // Per-feature shape checks shared by every lookup entry point: the host half of
@@ -524,9 +548,7 @@ void eps_b200_destroy(EpsB200Store* s) {
     if (s->own) cudaStreamSynchronize(s->own);
     for (auto& [id, t] : s->tickets) if (t.slab) cudaFree(t.slab);
     for (auto& [id, r] : s->routes) if (r.slab) cudaFree(r.slab);
-    for (auto& [id, t] : s->tables) {
-      cudaFree(t.state); cudaFree(t.updates); cudaFree(t.dtable);
-    }
+    for (auto& [id, t] : s->tables) t.Free();
     for (auto& f : s->fences) cudaEventDestroy(f.done);
     if (s->ring) cudaFreeHost(s->ring);
     for (auto& x : s->pending) { cudaEventDestroy(x.a); cudaEventDestroy(x.b); }
@@ -563,16 +585,71 @@ int eps_b200_create_table(EpsB200Store* store, const EpsB200Table* table, EpsB20
     }
     Require(s.tables.size() < 1024, "table count exceeds limit", EPS_B200_CAPACITY_EXCEEDED);
     const unsigned long long shard = s.opt.shard_id, n = s.opt.shard_count;
-    const unsigned long long rows = d.key_space > shard ? (d.key_space - 1 - shard) / n + 1 : 0;
+    const bool hashed = d.key_space == 0;
+    const unsigned long long rows =
+        hashed ? d.capacity : d.key_space > shard ? (d.key_space - 1 - shard) / n + 1 : 0;
     Require(rows < 0xffffffffull, "key space exceeds the per-shard slot limit (2^32 - 1)",
             EPS_B200_CAPACITY_EXCEEDED);
-    const unsigned long long bytes = rows * (12ull * d.dimension + 8);
+    unsigned long long entries = 0;
+    if (hashed) {
+      entries = 1;
+      while (entries < 2 * rows) entries <<= 1;        // at most half full
+    }
+    const unsigned long long bytes = rows * (12ull * d.dimension + 8) + entries * 12 + rows * 8;
     Require(s.opt.state_bytes >= s.allocated_state && bytes <= s.opt.state_bytes - s.allocated_state,
             "parameter-state budget exhausted", EPS_B200_CAPACITY_EXCEEDED);
     Table t;
     t.def = d;
     t.rows = rows;
     t.bytes = bytes;
+    t.hashed = hashed;
+    t.entries = entries;
+    if (hashed) {
+      try {
+        Cuda(cudaMalloc(&t.state, std::max<size_t>(rows * 12ull * d.dimension, 16)));
+        Cuda(cudaMalloc(&t.updates, std::max<size_t>(((rows + 1ull) & ~1ull) * 8ull, 16)));
+        Cuda(cudaMalloc(&t.dtable, sizeof(DeviceTable)));
+        HashIndex& h = t.index;
+        Cuda(cudaMalloc(&h.keys, entries * 8));
+        Cuda(cudaMalloc(&h.slots, (entries + 1) * 4));
+        Cuda(cudaMalloc(&h.slot_keys, std::max<size_t>(rows * 8, 8)));
+        Cuda(cudaMalloc(&h.used, 16));               // used (u64) | top (u32)
+        h.top = reinterpret_cast<unsigned*>(h.used + 1);
+        h.mask = entries - 1;
+        h.capacity = rows;
+        h.state = t.state;
+        h.updates = t.updates;
+        h.dim = d.dimension;
+        h.table_id = d.id;
+        h.seed = d.initialization_seed;
+        h.init_min = d.initialization_min;
+        h.init_max = d.initialization_max;
+        h.has_bounds = d.has_weight_bounds;
+        h.bound_min = d.weight_min;
+        h.bound_max = d.weight_max;
+        Cuda(cudaMalloc(&t.dindex, sizeof(HashIndex)));
+        Cuda(cudaMemcpy(t.dindex, &h, sizeof(HashIndex), cudaMemcpyHostToDevice));
+        t.ClearIndex(s.own);
+        DeviceTable dt{};
+        dt.beta1_power = d.initial_beta1_power;
+        dt.beta2_power = d.initial_beta2_power;
+        float bound = std::max(std::fabs(d.initialization_min), std::fabs(d.initialization_max));
+        if (d.has_weight_bounds)
+          bound = std::max(bound, std::max(std::fabs(d.weight_min), std::fabs(d.weight_max)));
+        std::memcpy(&dt.state_absmax_bits, &bound, sizeof(bound));
+        Cuda(cudaMemcpy(t.dtable, &dt, sizeof(dt), cudaMemcpyHostToDevice));
+        Cuda(cudaStreamSynchronize(s.own));
+      } catch (...) {
+        t.Free();
+        throw;
+      }
+      s.allocated_state += bytes;
+      s.stats.state_bytes = s.allocated_state;
+      s.stats.rows += rows;
+      s.stats.tables = s.tables.size() + 1;
+      s.tables.emplace(d.id, t);
+      return;
+    }
     try {
       Cuda(cudaMalloc(&t.state, std::max<size_t>(rows * 12ull * d.dimension, 16)));
       // an even number of counters: the ring push reads the 16-byte block of two
@@ -593,7 +670,7 @@ int eps_b200_create_table(EpsB200Store* store, const EpsB200Table* table, EpsB20
       Cuda(launch_init(p, s.own));
       Cuda(cudaStreamSynchronize(s.own));
     } catch (...) {
-      cudaFree(t.state); cudaFree(t.updates); cudaFree(t.dtable);
+      t.Free();
       throw;
     }
     s.allocated_state += bytes;
@@ -631,13 +708,14 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
     unsigned long long total_keys = 0, total_offsets = 0, total_lengths = 0, total_rows = 0,
                        host_out_values = 0, bags = 0;
     std::vector<unsigned> dims;
-    bool out16 = true, out8 = true, any_host_out = false, any_padding = false;
+    bool out16 = true, out8 = true, any_host_out = false, any_padding = false, any_hashed = false;
     for (uint64_t i = 0; i < count; ++i) {
       const auto& f = features[i];
       Require(ids.insert(f.feature).second, "duplicate feature ID");
       const Table& t = s.Get(f.table);
       const unsigned long long rows = CheckFeatureShape(f);
       any_padding |= f.has_padding != 0;
+      any_hashed |= t.hashed;
       if (gather) {
         const auto& o = outputs[i];
         Require(o.feature == f.feature && o.rows == rows && o.columns == t.def.dimension,
@@ -690,6 +768,8 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       at_lengths = c.take<unsigned long long>(total_lengths);
     }
     if (any_host_out) at_hostout = c.take<float>(host_out_values);
+    // the resolved slots of hashed features' occurrences
+    const size_t at_slots = any_hashed ? c.take<unsigned>(total_keys) : 0;
     const unsigned stiles = sort_tiles(total_keys);
     // pieces: one per row with 2..kLongRun occurrences (at most total_keys / 2
     // rows) and ceil(len / kPiece) per longer row
@@ -793,6 +873,8 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         L.feature_index = (unsigned)i;
         L.has_padding = f.has_padding ? 1u : 0u;
         L.padding_key = f.padding_key;
+        L.hash = tab.hashed ? tab.dindex : nullptr;
+        L.slots = tab.hashed ? reinterpret_cast<unsigned*>(P(at_slots)) + occ_base : nullptr;
         L.unit_bags = feature_unit_bags(f.pooling, f.key_count, L.bag_count);
         L.unit_base = unit_base;
         L.units = feature_units(f.pooling, f.key_count, L.bag_count, L.unit_bags);
@@ -828,6 +910,13 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       lp.vec = vec;
       lp.group = group;
       lp.iters = iters;
+      if (any_hashed) {
+        // keys of hashed tables -> slots, creating the rows of unseen keys
+        ResolveLaunch rp{lp.features, (unsigned)count, total_keys, s.opt.shard_count,
+                         s.opt.shard_id, reinterpret_cast<unsigned*>(P(at_slots)), lp.error};
+        Cuda(launch_resolve(rp, stream));
+        s.stats.kernel_launches += total_keys ? 2 : 0;
+      }
       if (!read_only) {
         lp.occ_key = P(at_k0);
         lp.occ_src = reinterpret_cast<unsigned*>(P(at_s0));
@@ -948,7 +1037,9 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         slab = nullptr;                 // freed exactly once, here
         Cuda(cudaFreeAsync(owned, stream));
         s.Done(stream);
-        Require(!sync_err, EpsB200Store::LookupMessage(sync_err).c_str());
+        Require(!sync_err, EpsB200Store::LookupMessage(sync_err).c_str(),
+                (sync_err & kLookupCapacity) ? EPS_B200_CAPACITY_EXCEEDED
+                                             : EPS_B200_INVALID_ARGUMENT);
         return;
       }
       t.slab = slab;
@@ -991,6 +1082,7 @@ int eps_b200_lookup_noalloc(EpsB200Store* store, const EpsB200Feature* features,
       const auto& f = features[i];
       for (uint64_t j = 0; j < i; ++j) Require(features[j].feature != f.feature, "duplicate feature ID");
       const Table& t = s.Get(f.table);
+      Require(!t.hashed, "the allocation-free lookup serves dense tables (key_space > 0)");
       const unsigned long long rows = CheckFeatureShape(f);
       const unsigned D = t.def.dimension;
       const auto& o = outputs[i];
@@ -1003,7 +1095,10 @@ int eps_b200_lookup_noalloc(EpsB200Store* store, const EpsB200Feature* features,
       all2 &= D % 2 == 0;
       out16 &= (reinterpret_cast<uintptr_t>(o.data) & 15) == 0;
       out8 &= (reinterpret_cast<uintptr_t>(o.data) & 7) == 0;
+      // value-initialised: every field this path does not set (hash index,
+      // slot list, emit units) must read as null / zero in the kernel
       LookupFeature& L = desc[i];
+      L = LookupFeature{};
       L.keys = reinterpret_cast<const unsigned long long*>(f.keys);
       L.offsets = reinterpret_cast<const unsigned long long*>(f.offsets);
       L.lengths = reinterpret_cast<const unsigned long long*>(f.valid_lengths);
@@ -1013,7 +1108,7 @@ int eps_b200_lookup_noalloc(EpsB200Store* store, const EpsB200Feature* features,
       L.key_count = f.key_count;
       L.bag_count = f.offset_count - 1;
       L.bag_base = bag_base;
-        L.occ_base = 0;
+      L.occ_base = 0;
       L.scale_base = 0;
       L.dim = D;
       L.pooling = f.pooling;
@@ -1424,10 +1519,17 @@ std::vector<unsigned long long> CheckedKeys(const EpsB200Store& s, const Table& 
   std::unordered_set<unsigned long long> seen;
   for (auto k : out) {
     Require(k % s.opt.shard_count == s.opt.shard_id, "key belongs to another shard");
-    Require(k / s.opt.shard_count < t.rows, "unknown parameter row");
+    Require(t.hashed || k / s.opt.shard_count < t.rows, "unknown parameter row");
     Require(seen.insert(k).second, "duplicate row");
   }
   return out;
+}
+
+// A hashed table's keys (on the device) -> slots (on the device), creating the
+// rows of unseen keys; `scratch` holds n u32.  Errors land in *err.
+void ResolveKeys(const Table& t, const unsigned long long* keys, unsigned long long n,
+                 unsigned* scratch, unsigned* slots, unsigned* err, cudaStream_t stream) {
+  Cuda(launch_resolve_keys(&t.index, keys, n, scratch, slots, err, stream));
 }
 }  // namespace
 
@@ -1444,20 +1546,30 @@ int eps_b200_read_state(EpsB200Store* store, uint32_t table, const uint64_t* key
     const unsigned D = t.def.dimension;
     cudaStream_t stream = s.Use(nullptr);
     char* buf = nullptr;
-    const size_t kb = align256(count * 8), pb = align256(count * 12ull * D);
-    Cuda(cudaMallocAsync(reinterpret_cast<void**>(&buf), kb + pb + align256(count * 8) + 256, stream));
+    const size_t kb = align256(count * 8), pb = align256(count * 12ull * D), ub = align256(count * 8);
+    const size_t hb = t.hashed ? align256(count * 4) : 0;      // entries, slots (hashed)
+    Cuda(cudaMallocAsync(reinterpret_cast<void**>(&buf), kb + pb + ub + 2 * hb + 256, stream));
     std::vector<float> packed(count * 3ull * D);
     std::vector<unsigned long long> upd(count);
-    unsigned* err = reinterpret_cast<unsigned*>(buf + kb + pb + align256(count * 8));
+    unsigned* err = reinterpret_cast<unsigned*>(buf + kb + pb + ub + 2 * hb);
+    unsigned herr = 0;
     try {
       Cuda(cudaMemsetAsync(err, 0, 4, stream));
       Cuda(cudaMemcpyAsync(buf, k.data(), count * 8, cudaMemcpyHostToDevice, stream));
-      Cuda(launch_read_rows(t.state, t.updates, D, t.rows, s.opt.shard_count,
-                            reinterpret_cast<unsigned long long*>(buf), count,
-                            reinterpret_cast<float*>(buf + kb),
-                            reinterpret_cast<unsigned long long*>(buf + kb + pb), err, stream));
+      const auto* dkeys = reinterpret_cast<unsigned long long*>(buf);
+      if (t.hashed) {
+        auto* slots = reinterpret_cast<unsigned*>(buf + kb + pb + ub + hb);
+        ResolveKeys(t, dkeys, count, reinterpret_cast<unsigned*>(buf + kb + pb + ub), slots, err, stream);
+        Cuda(launch_read_slots(t.state, t.updates, D, slots, count, reinterpret_cast<float*>(buf + kb),
+                               reinterpret_cast<unsigned long long*>(buf + kb + pb), err, stream));
+      } else {
+        Cuda(launch_read_rows(t.state, t.updates, D, t.rows, s.opt.shard_count, dkeys, count,
+                              reinterpret_cast<float*>(buf + kb),
+                              reinterpret_cast<unsigned long long*>(buf + kb + pb), err, stream));
+      }
       Cuda(cudaMemcpyAsync(packed.data(), buf + kb, count * 12ull * D, cudaMemcpyDeviceToHost, stream));
       Cuda(cudaMemcpyAsync(upd.data(), buf + kb + pb, count * 8, cudaMemcpyDeviceToHost, stream));
+      Cuda(cudaMemcpyAsync(&herr, err, 4, cudaMemcpyDeviceToHost, stream));
       char* owned = buf;
       buf = nullptr;
       Cuda(cudaFreeAsync(owned, stream));
@@ -1468,6 +1580,7 @@ int eps_b200_read_state(EpsB200Store* store, uint32_t table, const uint64_t* key
       throw;
     }
     s.Done(stream);
+    Require(!(herr & kLookupCapacity), "hashed table capacity exceeded", EPS_B200_CAPACITY_EXCEEDED);
     for (uint64_t r = 0; r < count; ++r) {
       const float* row = packed.data() + r * 3ull * D;
       if (weights) std::memcpy(weights + r * D, row, D * 4);
@@ -1504,16 +1617,28 @@ int eps_b200_load_state(EpsB200Store* store, uint32_t table, const uint64_t* key
     }
     cudaStream_t stream = s.Use(nullptr);
     char* buf = nullptr;
-    const size_t kb = align256(count * 8), pb = align256(count * 12ull * D);
-    Cuda(cudaMallocAsync(reinterpret_cast<void**>(&buf), kb + pb + align256(count * 8), stream));
+    const size_t kb = align256(count * 8), pb = align256(count * 12ull * D), ub = align256(count * 8);
+    const size_t hb = t.hashed ? align256(count * 4) : 0;      // entries, slots (hashed)
+    Cuda(cudaMallocAsync(reinterpret_cast<void**>(&buf), kb + pb + ub + 2 * hb + 256, stream));
+    unsigned* err = reinterpret_cast<unsigned*>(buf + kb + pb + ub + 2 * hb);
+    unsigned herr = 0;
     try {
+      Cuda(cudaMemsetAsync(err, 0, 4, stream));
       Cuda(cudaMemcpyAsync(buf, k.data(), count * 8, cudaMemcpyHostToDevice, stream));
       Cuda(cudaMemcpyAsync(buf + kb, packed.data(), count * 12ull * D, cudaMemcpyHostToDevice, stream));
       Cuda(cudaMemcpyAsync(buf + kb + pb, upd.data(), count * 8, cudaMemcpyHostToDevice, stream));
-      Cuda(launch_write_rows(t.state, t.updates, D, t.rows, s.opt.shard_count,
-                             reinterpret_cast<unsigned long long*>(buf), count,
-                             reinterpret_cast<float*>(buf + kb),
-                             reinterpret_cast<unsigned long long*>(buf + kb + pb), t.dtable, stream));
+      const auto* dkeys = reinterpret_cast<unsigned long long*>(buf);
+      if (t.hashed) {
+        auto* slots = reinterpret_cast<unsigned*>(buf + kb + pb + ub + hb);
+        ResolveKeys(t, dkeys, count, reinterpret_cast<unsigned*>(buf + kb + pb + ub), slots, err, stream);
+        Cuda(launch_write_slots(t.state, t.updates, D, slots, count, reinterpret_cast<float*>(buf + kb),
+                                reinterpret_cast<unsigned long long*>(buf + kb + pb), t.dtable, stream));
+      } else {
+        Cuda(launch_write_rows(t.state, t.updates, D, t.rows, s.opt.shard_count, dkeys, count,
+                               reinterpret_cast<float*>(buf + kb),
+                               reinterpret_cast<unsigned long long*>(buf + kb + pb), t.dtable, stream));
+      }
+      Cuda(cudaMemcpyAsync(&herr, err, 4, cudaMemcpyDeviceToHost, stream));
       char* owned = buf;
       buf = nullptr;
       Cuda(cudaFreeAsync(owned, stream));
@@ -1524,6 +1649,7 @@ int eps_b200_load_state(EpsB200Store* store, uint32_t table, const uint64_t* key
       throw;
     }
     s.Done(stream);
+    Require(!(herr & kLookupCapacity), "hashed table capacity exceeded", EPS_B200_CAPACITY_EXCEEDED);
   });
 }
 
@@ -1631,7 +1757,7 @@ int eps_b200_route(EpsB200Store* store, const EpsB200Feature* features, uint64_t
       L.keys = reinterpret_cast<const unsigned long long*>(f.keys);
       L.offsets = reinterpret_cast<const unsigned long long*>(f.offsets);
       L.lengths = reinterpret_cast<const unsigned long long*>(f.valid_lengths);
-      L.rows = t.def.key_space;
+      L.rows = t.hashed ? ~0ull : t.def.key_space;   // route checks keys against it
       L.key_count = f.key_count;
       L.bag_count = f.offset_count - 1;
       L.bag_base = r.B;
@@ -1911,6 +2037,7 @@ void ApplyWithContext(EpsB200Store& s, const EpsB200UpdateContext& c, const uint
   std::lock_guard lock(s.mutex);
   s.Activate();
   const Table& t = s.Get(c.table);
+  Require(!t.hashed, "cache updates address slots of a dense table (key_space > 0)");
   const auto& d = t.def;
   const unsigned D = d.dimension;
   Require(rows == 0 || keys, "null gradient rows");
@@ -2085,7 +2212,7 @@ int eps_b200_sync_reduce(EpsB200Store* store, uint32_t table, const EpsB200Worke
     Require(capacity >= n && (!n || (keys_out && values_out)), "reduce output capacity too small");
     cudaStream_t stream = s.Use(stream_arg);
     if (n == 0) { *rows_out = 0; return; }
-    const unsigned bits = std::max(1u, bits_for(t.def.key_space - 1));
+    const unsigned bits = t.hashed ? 64u : std::max(1u, bits_for(t.def.key_space - 1));
     Carver c;
     const size_t at_w = c.take<SyncWorker>(worker_count);
     const size_t at_base = c.take<unsigned long long>(worker_count + 1);
@@ -2113,7 +2240,7 @@ int eps_b200_sync_reduce(EpsB200Store* store, uint32_t table, const EpsB200Worke
       lp.scale = reinterpret_cast<const double*>(P(at_scale));
       lp.total_rows = n;
       lp.dim = D;
-      lp.key_space = t.def.key_space;
+      lp.key_space = t.hashed ? ~0ull : t.def.key_space;
       lp.shard_count = s.opt.shard_count;
       lp.shard_id = s.opt.shard_id;
       lp.keys = reinterpret_cast<unsigned long long*>(P(at_k0));
@@ -2413,15 +2540,26 @@ int eps_b200_snapshot_write(EpsB200Store* store, const char* path, const char* r
         w.U64(dt.optimizer_sequence); w.F32(dt.beta1_power); w.F32(dt.beta2_power);
         // rows: every updated row (rows never updated hold their initial value,
         // which a restore reproduces), or every row with all_rows
-        std::vector<unsigned long long> upd(t.rows);
-        if (t.rows) Cuda(cudaMemcpy(upd.data(), t.updates, t.rows * 8, cudaMemcpyDeviceToHost));
+        // a hashed table's rows are its slots in use, with their keys
+        uint64_t nslots = t.rows;
+        std::vector<unsigned long long> skeys;
+        if (t.hashed) {
+          unsigned long long used = 0;
+          Cuda(cudaMemcpy(&used, t.index.used, 8, cudaMemcpyDeviceToHost));
+          nslots = std::min<uint64_t>(used, t.rows);
+          skeys.resize(nslots);
+          if (nslots)
+            Cuda(cudaMemcpy(skeys.data(), t.index.slot_keys, nslots * 8, cudaMemcpyDeviceToHost));
+        }
+        std::vector<unsigned long long> upd(nslots);
+        if (nslots) Cuda(cudaMemcpy(upd.data(), t.updates, nslots * 8, cudaMemcpyDeviceToHost));
         uint64_t rows = 0;
         for (auto u : upd) rows += (all_rows || u) ? 1 : 0;
         w.U64(rows);
         const uint64_t chunk = std::max<uint64_t>(1, (64ull << 20) / (12ull * D));
         std::vector<float> st;
-        for (uint64_t b = 0; b < t.rows; b += chunk) {
-          const uint64_t e = std::min<uint64_t>(t.rows, b + chunk);
+        for (uint64_t b = 0; b < nslots; b += chunk) {
+          const uint64_t e = std::min<uint64_t>(nslots, b + chunk);
           bool any = all_rows != 0;
           for (uint64_t i = b; i < e && !any; ++i) any = upd[i] != 0;
           if (!any) continue;
@@ -2429,7 +2567,7 @@ int eps_b200_snapshot_write(EpsB200Store* store, const char* path, const char* r
           Cuda(cudaMemcpy(st.data(), t.state + b * 3ull * D, st.size() * 4, cudaMemcpyDeviceToHost));
           for (uint64_t i = b; i < e; ++i) {
             if (!all_rows && !upd[i]) continue;
-            w.U64(i * s.opt.shard_count + s.opt.shard_id);     // key of slot i
+            w.U64(t.hashed ? skeys[i] : i * s.opt.shard_count + s.opt.shard_id);   // slot i's key
             w.U64(upd[i]);
             const float* row = st.data() + (i - b) * 3ull * D;
             for (unsigned k = 0; k < 3 * D; ++k) w.F32(row[k]);
@@ -2486,9 +2624,12 @@ int eps_b200_snapshot_read(EpsB200Store* store, const char* path, const char* ne
       Require(it != s.tables.end(), "snapshot table is not defined in the store");
       Require(SameOptimizer(t.def, it->second.def) && t.def.shard_count == count &&
               t.def.partition_epoch == epoch, "snapshot table definition differs from the store's");
+      const Table& tab = it->second;
       for (auto k : t.keys)
-        Require(k % count == shard && k < it->second.def.key_space,
+        Require(k % count == shard && (tab.hashed || k < tab.def.key_space),
                 "snapshot row outside this shard's key space");
+      Require(!tab.hashed || t.keys.size() <= tab.rows, "snapshot rows exceed the table's capacity",
+              EPS_B200_CAPACITY_EXCEEDED);
     }
     // every check passed: re-initialise, then write the snapshot's rows and powers
     cudaStream_t stream = s.Use(nullptr);
@@ -2496,10 +2637,14 @@ int eps_b200_snapshot_read(EpsB200Store* store, const char* path, const char* ne
       Table& tab = s.tables.at(t.def.id);
       const unsigned D = tab.def.dimension;
       const auto& d = tab.def;
-      InitLaunch ip{tab.state, tab.updates, tab.rows, D, s.opt.shard_count, s.opt.shard_id,
-                    d.id, d.initialization_seed, d.initialization_min, d.initialization_max,
-                    d.has_weight_bounds, d.weight_min, d.weight_max};
-      Cuda(launch_init(ip, stream));
+      if (tab.hashed) {
+        tab.ClearIndex(stream);              // rows are created again as their keys return
+      } else {
+        InitLaunch ip{tab.state, tab.updates, tab.rows, D, s.opt.shard_count, s.opt.shard_id,
+                      d.id, d.initialization_seed, d.initialization_min, d.initialization_max,
+                      d.has_weight_bounds, d.weight_min, d.weight_max};
+        Cuda(launch_init(ip, stream));
+      }
       DeviceTable dt{};
       dt.beta1_power = t.beta1_power;
       dt.beta2_power = t.beta2_power;
@@ -2515,17 +2660,30 @@ int eps_b200_snapshot_read(EpsB200Store* store, const char* path, const char* ne
       std::vector<unsigned long long> slots(rows);
       for (uint64_t j = 0; j < rows; ++j) slots[j] = t.keys[j];
       char* buf = nullptr;
-      const size_t kb = align256(rows * 8), pb = align256(rows * 12ull * D);
-      Cuda(cudaMallocAsync(reinterpret_cast<void**>(&buf), kb + pb + align256(rows * 8), stream));
+      const size_t kb = align256(rows * 8), pb = align256(rows * 12ull * D), ub = align256(rows * 8);
+      const size_t hb = tab.hashed ? align256(rows * 4) : 0;
+      Cuda(cudaMallocAsync(reinterpret_cast<void**>(&buf), kb + pb + ub + 2 * hb + 256, stream));
       try {
         Cuda(cudaMemcpyAsync(buf, slots.data(), rows * 8, cudaMemcpyHostToDevice, stream));
         Cuda(cudaMemcpyAsync(buf + kb, t.state.data(), rows * 12ull * D, cudaMemcpyHostToDevice, stream));
         Cuda(cudaMemcpyAsync(buf + kb + pb, t.updates.data(), rows * 8, cudaMemcpyHostToDevice, stream));
-        Cuda(launch_write_rows(tab.state, tab.updates, D, tab.rows, s.opt.shard_count,
-                               reinterpret_cast<unsigned long long*>(buf), rows,
-                               reinterpret_cast<float*>(buf + kb),
-                               reinterpret_cast<unsigned long long*>(buf + kb + pb), tab.dtable,
-                               stream));
+        const auto* dkeys = reinterpret_cast<unsigned long long*>(buf);
+        if (tab.hashed) {
+          auto* rslots = reinterpret_cast<unsigned*>(buf + kb + pb + ub + hb);
+          auto* err = reinterpret_cast<unsigned*>(buf + kb + pb + ub + 2 * hb);
+          Cuda(cudaMemsetAsync(err, 0, 4, stream));
+          ResolveKeys(tab, dkeys, rows, reinterpret_cast<unsigned*>(buf + kb + pb + ub), rslots, err,
+                      stream);
+          Cuda(launch_write_slots(tab.state, tab.updates, D, rslots, rows,
+                                  reinterpret_cast<float*>(buf + kb),
+                                  reinterpret_cast<unsigned long long*>(buf + kb + pb), tab.dtable,
+                                  stream));
+        } else {
+          Cuda(launch_write_rows(tab.state, tab.updates, D, tab.rows, s.opt.shard_count, dkeys, rows,
+                                 reinterpret_cast<float*>(buf + kb),
+                                 reinterpret_cast<unsigned long long*>(buf + kb + pb), tab.dtable,
+                                 stream));
+        }
         char* owned = buf;
         buf = nullptr;
         Cuda(cudaFreeAsync(owned, stream));

@@ -301,8 +301,15 @@ EpsB200Table TableOf(const Json& t, uint64_t epoch) {
   d.initialization_min = (float)i.At("min").Num();
   d.initialization_max = (float)i.At("max").Num();
   d.initialization_seed = i.At("seed").U64();
-  Require(t.Has("key_space"), "a B200 table needs its dense key space (\"key_space\")");
-  d.key_space = t.At("key_space").U64();
+  // "key_space": a dense table of keys [0, key_space); without it (the reference's
+  // own table JSON) a hashed table of any 64-bit keys, "capacity" rows (default
+  // 2^20) created on first touch
+  if (t.Has("key_space")) {
+    d.key_space = t.At("key_space").U64();
+  } else {
+    d.key_space = 0;
+    d.capacity = t.Has("capacity") ? t.At("capacity").U64() : (1ull << 20);
+  }
   return d;
 }
 

@@ -14,7 +14,9 @@ Configuration keys of the B200 runtime (JSON passed to ``create``):
 ``release_read_only``, ``snapshot_directory``, ``restore`` (a snapshot file
 loaded after the tables are created) and ``tables`` -- each table as the
 reference's runtime reads it (``id``, ``dimension``, ``dtype``, ``optimizer``,
-``initialization``) plus ``key_space``, the dense row count of the table.
+``initialization``) plus, optionally, ``key_space`` (a dense table of keys
+[0, key_space); without it a hashed table of any 64-bit keys, ``capacity`` rows,
+default 2^20, created on first touch).
 """
 from __future__ import annotations
 

@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define EPS_B200_ABI 2
+#define EPS_B200_ABI 3
 
 #if defined(_WIN32)
 #define EPS_B200_EXPORT __declspec(dllexport)
@@ -84,9 +84,15 @@ typedef struct {
 #define EPS_B200_FLAG_REGISTER_ROWS 2u
 
 /* eps::TableDefinition + eps::OptimizerConfig (include/eps/types.hpp:76-97).
- * key_space: keys of this table lie in [0, key_space); the shard holds the slots
- * of keys k with k % shard_count == shard_id (src/store/shard_store.cpp:77),
- * initialised up front with the reference initializer. */
+ * key_space > 0: a dense table -- keys lie in [0, key_space); the shard holds the
+ * slots of keys k with k % shard_count == shard_id (src/store/shard_store.cpp:77),
+ * at slot k / shard_count, initialised up front with the reference initializer.
+ * key_space == 0: a hashed table -- any 64-bit key owned by the shard; a row is
+ * created on the key's first touch (any lookup, read_state or load_state), with
+ * the same initializer, as ShardStore::Ensure does (src/store/shard_store.cpp:
+ * 76-115); the shard holds at most `capacity` rows (then lookups of unseen keys
+ * fail with "hashed table capacity exceeded").  An open-addressing index of
+ * 2 x capacity entries (rounded up to a power of two) maps keys to rows. */
 typedef struct {
   uint32_t id;
   uint32_t dimension;
@@ -99,6 +105,7 @@ typedef struct {
   float initialization_min, initialization_max;
   uint64_t initialization_seed;
   uint64_t key_space;
+  uint64_t capacity;             /* hashed tables (key_space == 0): rows on this shard */
 } EpsB200Table;
 
 /* eps::FeatureInput (include/eps/types.hpp:99-107).  valid_lengths may be NULL
@@ -197,8 +204,10 @@ EPS_B200_EXPORT int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* f
  * or a latency-critical loop that must never wait on an allocator).
  * Limits and sharing:
  *  - 1 to 256 features per call (larger counts fail with CAPACITY_EXCEEDED);
- *    inputs and outputs must be device buffers on the store's GPU;
- *  - the feature descriptors go to one fixed ~30 KiB array per GPU, created when
+ *    inputs and outputs must be device buffers on the store's GPU; every
+ *    feature must read a dense table (key_space > 0): a hashed table's rows are
+ *    found through per-call slot lists, which would need device memory;
+ *  - the feature descriptors go to one fixed ~42 KiB array per GPU, created when
  *    the library is loaded on that GPU and kept until the process exits; every
  *    call on that GPU reuses it.  The calls of one store are ordered on the GPU
  *    whatever their streams, so only calls of different stores on one GPU (or of

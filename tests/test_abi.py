@@ -40,7 +40,7 @@ def test_python_binding_lists_entry_points(eps):
 
 
 def test_abi_version(eps):
-    assert eps.load_library().eps_b200_abi_version() == 2
+    assert eps.load_library().eps_b200_abi_version() == 3
 
 
 def test_struct_sizes_match_header(eps):
