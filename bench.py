@@ -85,7 +85,16 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5])
+    ap.add_argument("--config", type=int, default=None, choices=[1, 2, 3, 4, 5],
+                    help="BASELINE.json config; default 2 (the single-GPU config) at N = 1 "
+                         "and 3 (the config measured at 1/2/4/8 GPUs) at N > 1")
+    ap.add_argument("--check-occurrences", type=int, default=1 << 22,
+                    help="largest job (occurrences over all ranks) the parity round checks "
+                         "at full batch; larger jobs are checked at a proportionally smaller "
+                         "batch per rank of the same config")
+    ap.add_argument("--no-scale-base", action="store_true",
+                    help="at N = 1 with the default config, skip timing the N > 1 default "
+                         "config (3) on this GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-check", action="store_true",
                     help="skip the parity check against the reference after the timed rounds")
@@ -111,18 +120,37 @@ def cfg5_rows(world: int) -> int:
     return int(min(1_000_000_000, world * 150_000_000_000 // 392))
 
 
-def workload_for(wl, config, rank, world, rows=0, batch=0):
+# per-rank batch of each config (config 4: gradient rows; config 1 is fixed)
+DEFAULT_BATCH = {1: 128, 2: 4096, 3: 65536, 4: 262_144, 5: 131072}
+
+
+def resolve_config(args, world):
+    """The config to run: --config, else 2 at N = 1 (the single-GPU config) and
+    3 at N > 1 (the 26-table config BASELINE.json measures at 1/2/4/8 GPUs).
+    Both arms resolve it the same way."""
+    args.config_default = args.config is None
+    if args.config is None:
+        args.config = 2 if world == 1 else 3
+    return args.config
+
+
+def workload_for(wl, config, rank, world, rows=0, batch=0, gradients=True):
     """Rank `rank`'s batch: every rank draws its own batch (seed per rank) from
-    the same id distribution (the config's shared id map and tables)."""
+    the same id distribution (the config's shared id map and tables).  Without
+    `gradients` the batch's keys are the same and its gradients are None."""
+    g = gradients
     if config == 1:
-        return wl.config1(seed=1 + 1000 * rank)
+        return wl.config1(seed=1 + 1000 * rank, gradients=g)
     if config == 2:
-        return wl.config2(seed=2 + 1000 * rank, rows=rows or 10_000_000, batch=batch or 4096)
+        return wl.config2(seed=2 + 1000 * rank, rows=rows or 10_000_000, batch=batch or 4096,
+                          gradients=g)
     if config == 3:
-        return wl.config3(seed=3 + 1000 * rank, batch=batch or 65536)
+        return wl.config3(seed=3 + 1000 * rank, batch=batch or 65536, gradients=g)
     if config == 4:
-        return wl.config4(seed=4 + 1000 * rank, rows=rows or 100_000_000, n=batch or 262_144)
-    return wl.config5(seed=5 + 1000 * rank, rows=rows or cfg5_rows(world), batch=batch or 131072)
+        return wl.config4(seed=4 + 1000 * rank, rows=rows or 100_000_000, n=batch or 262_144,
+                          gradients=g)
+    return wl.config5(seed=5 + 1000 * rank, rows=rows or cfg5_rows(world), batch=batch or 131072,
+                      gradients=g)
 
 
 def push_only(config, world):
@@ -186,8 +214,19 @@ def byte_model(tables, feats, world=1, rank=0):
             "owner_U": own["U"], "owner_U_long": own["long"], "owner_N": own["N"]}
 
 
-def job_parts(wl, args, world):
-    return [workload_for(wl, args.config, r, world, args.rows, args.batch) for r in range(world)]
+def job_parts(wl, args, world, grads_for=None, batch=0):
+    """Every rank's batch.  Only the ranks in `grads_for` (all when None) carry
+    gradients; the others' keys describe the job (byte model, config)."""
+    return [workload_for(wl, args.config, r, world, args.rows, batch or args.batch,
+                         gradients=grads_for is None or r in grads_for) for r in range(world)]
+
+
+def scaled_batch(args, frac):
+    """The per-rank batch that is `frac` of the configured one (at least 1)."""
+    full = args.batch or DEFAULT_BATCH[args.config]
+    if args.config == 1 or frac >= 1.0:
+        return 0 if not args.batch else args.batch
+    return max(1, int(full * frac))
 
 
 def job_features(parts):
@@ -331,20 +370,41 @@ class Clocks:
 
 
 # --------------------------------------------------------------- reference arm
-def reference_rounds(parts, config, world, steps, warmup, threads, budget_s=60.0):
+def reference_rounds(wl, args, world, steps, warmup, threads, budget_s=60.0, round_s=2.0):
     """Times the reference's CPU path (oracle/_ref: DistributedClient over
-    `threads` CpuParameterService shards) on the job: every rank's batch as one
-    combined request.  Push-only configs time the push alone.  Stops early (at
-    least 2 timed rounds) once `budget_s` of timed work is done.  Returns the
-    seconds of each timed round, or None without the reference build."""
+    `threads` CpuParameterService shards) on a bounded sample of the job: every
+    rank's batch as one combined request -- at the configured batch when one
+    round of the whole job takes about `round_s` seconds or less, else at a
+    proportionally smaller batch per rank of the same config (same tables, id
+    distribution and seeds), sized from one untimed probe round of at most 2^18
+    occurrences.  Push-only configs time the push alone.  Stops early (at least
+    2 timed rounds) once `budget_s` of timed work is done.  Returns (seconds of
+    each timed round, the sampled parts), or None without the reference build."""
     from oracle_lib import Feature, Reference, reference_available
     import round_check
     if not reference_available():
         return None
-    feats, grads = job_features(parts)
-    feats = [Feature(f.table, f.feature, f.pooling, f.keys, f.offsets) for f in feats]
-    ref = Reference(round_check.table_defs(parts[0]), shards=threads, state_bytes=256 << 30)
-    only_push = push_only(config, world)
+    full = job_parts(wl, args, world, grads_for=())
+    n_full = sum(p.occurrences for p in full)
+    tables = round_check.table_defs(full[0])
+    del full
+    ref = Reference(tables, shards=threads, state_bytes=256 << 30)
+    only_push = push_only(args.config, world)
+
+    def request(parts):
+        feats, grads = job_features(parts)
+        return [Feature(f.table, f.feature, f.pooling, f.keys, f.offsets) for f in feats], grads
+
+    probe_frac = min(1.0, (1 << 18) / n_full)
+    probe = job_parts(wl, args, world, batch=scaled_batch(args, probe_frac))
+    feats, grads = request(probe)
+    t0 = time.perf_counter()
+    batch, _ = ref.lookup(feats)
+    ref.push(batch, feats, grads)
+    cost = (time.perf_counter() - t0) / max(1, sum(p.occurrences for p in probe))
+    frac = min(1.0, round_s / max(cost * n_full, 1e-9))
+    sample = job_parts(wl, args, world, batch=scaled_batch(args, frac))
+    feats, grads = request(sample)
     times, spent = [], 0.0
     for i in range(warmup + steps):
         t0 = time.perf_counter()
@@ -359,7 +419,18 @@ def reference_rounds(parts, config, world, steps, warmup, threads, budget_s=60.0
             if spent > budget_s and len(times) >= 2:
                 break
     ref.close()
-    return times
+    return times, sample
+
+
+def sample_text(sample, n_job, rounds, warmup, what, threads):
+    n = sum(p.occurrences for p in sample)
+    per = len(sample[0].features[0].offsets) - 1
+    part = ("the whole job" if n >= n_job else
+            f"a sample of the job: {per} samples per rank of the same config "
+            f"({n} of its {n_job} occurrences)")
+    return (f"{rounds} rounds ({what}) of {part}, {len(sample)} batch(es) as one request, "
+            f"after {warmup} warm-up rounds; DistributedClient over {threads} "
+            f"CpuParameterService shards (one per host thread)")
 
 
 def run_reference(args):
@@ -367,21 +438,22 @@ def run_reference(args):
     if rank != 0:
         return
     wl = load_workloads()              # the generators only: no repo library is loaded
-    parts = job_parts(wl, args, world)
+    resolve_config(args, world)
+    parts = job_parts(wl, args, world, grads_for=())
     feats, _ = job_features(parts)
     bm = byte_model(parts[0].tables, feats, world, 0)
+    del feats
     threads = host_threads()
-    times = reference_rounds(parts, args.config, world, args.steps, args.warmup, threads)
-    if times is None:
+    got = reference_rounds(wl, args, world, args.steps, args.warmup, threads)
+    if got is None:
         print(json.dumps({"impl": "reference", "unavailable":
                           "reference CPU build oracle/_ref/libeps_ref.so is missing"}))
         return
+    times, smp = got
     total = sum(times)
-    value = bm["N"] * len(times) / total
+    value = sum(p.occurrences for p in smp) * len(times) / total
     what = "push" if push_only(args.config, world) else "lookup + push"
-    sample = (f"{len(times)} rounds ({what}) of the job ({bm['N']} occurrences each, "
-              f"{len(parts)} batch(es) as one request) after {args.warmup} warm-up rounds; "
-              f"DistributedClient over {threads} CpuParameterService shards")
+    sample = sample_text(smp, bm["N"], len(times), args.warmup, what, threads)
     print(json.dumps({
         "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
         "steps": len(times), "warmup": args.warmup, "ms_per_step": 1e3 * total / len(times),
@@ -400,13 +472,23 @@ def _create_tables(eps, store, w, world):
                                                learning_rate=1e-3, shard_count=world))
 
 
-def parity_check(eps, torch, parts, rank, world, dev, comms, bitexact):
-    """One round from fresh tables against the reference (tests/round_check.py).
-    Returns this rank's reports (default order; at N = 1 also the bit-exact
-    mode)."""
+def parity_check(eps, torch, wl, args, parts, rank, world, dev, comms, bitexact):
+    """One round from fresh tables against the reference (tests/round_check.py),
+    through the same path as the timed rounds (the NCCL round at N > 1).  The
+    job is the timed one when it has at most --check-occurrences occurrences,
+    else the same config at a proportionally smaller batch per rank (every rank
+    runs the reference on the whole job).  Returns this rank's reports (default
+    order; at N = 1 also the bit-exact mode)."""
     import round_check as rc
+    n_job = sum(p.occurrences for p in parts)
+    frac = min(1.0, args.check_occurrences / n_job)
+    if world > 1 or frac < 1.0:
+        parts = job_parts(wl, args, world, batch=scaled_batch(args, frac))
     w = parts[rank]
     ref_result = rc.reference_round(parts)
+    checked = {"check_occurrences": sum(p.occurrences for p in parts),
+               "check_samples_per_rank": len(parts[0].features[0].offsets) - 1,
+               "job_occurrences": n_job}
     reports = []
     modes = [False, True] if (world == 1 and bitexact) else [False]
     for reference_order in modes:
@@ -433,6 +515,7 @@ def parity_check(eps, torch, parts, rank, world, dev, comms, bitexact):
             outs = [o.cpu().numpy() for o in outs]
             rep = rc.check_round(parts, rank, outs, store.read_state,
                                  reference_order=reference_order, ref_result=ref_result)
+            rep.update(checked)
         finally:
             store.close()
         reports.append(rep)
@@ -544,6 +627,50 @@ def e2e_pipelined(eps, torch, store, stream, w, hfeats, houts, hgrads, flush, st
     return t0.elapsed_time(t1)
 
 
+def scale_base_rounds(eps, torch, wl, args, dev, local_rank):
+    """Config 3 -- the default at N > 1 -- timed on this one GPU as the main
+    rounds are (inputs resident, L2 flushed before every round, CUDA events on
+    the store's stream): the N = 1 point of the scaling curve that the N > 1
+    lines measure."""
+    w = workload_for(wl, 3, 0, 1)
+    store = eps.ParameterStore(device=local_rank, state_bytes=170 << 30)
+    try:
+        _create_tables(eps, store, w, 1)
+        stream = torch.cuda.current_stream(dev)
+        dims = {t.id: t.dimension for t in w.tables}
+        feats = [eps.FeatureInput(f.table, f.feature, f.pooling,
+                                  torch.from_numpy(f.keys.astype(np.int64)).to(dev),
+                                  torch.from_numpy(f.offsets.astype(np.int64)).to(dev))
+                 for f in w.features]
+        outs = [torch.empty((f.output_rows, dims[f.table]), dtype=torch.float32, device=dev)
+                for f in w.features]
+        grads = [torch.from_numpy(g).to(dev) for g in w.gradients]
+        flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
+        lookup = store.prepare_lookup(feats, outs)
+        push = store.prepare_push(grads)
+        for _ in range(20 + args.warmup):
+            flush.zero_()
+            push(lookup(stream), stream, wait=False)
+        store.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+        torch.cuda.synchronize()
+        for a, b in ev:
+            flush.zero_()
+            a.record(stream)
+            push(lookup(stream), stream, wait=False)
+            b.record(stream)
+        torch.cuda.synchronize()
+        store.synchronize()
+        ms = sum(a.elapsed_time(b) for a, b in ev) / args.steps
+        return {"workload": w.name, "config": 3, "n_gpus": 1, "steps": args.steps,
+                "ms_per_step": ms, "value": w.occurrences / (ms / 1e3), "unit": UNIT,
+                "note": "config 3 (the default at N > 1) on one GPU, timed like the main "
+                        "rounds: the N = 1 point of the curve the N > 1 lines continue"}
+    finally:
+        store.close()
+
+
 def run_b200(args):
     import torch
     rank, local_rank, world = dist_env()
@@ -556,7 +683,8 @@ def run_b200(args):
                                 device_id=torch.device(f"cuda:{local_rank}"))
     wl = load_workloads()
     eps = load_package()
-    parts = job_parts(wl, args, world)
+    resolve_config(args, world)
+    parts = job_parts(wl, args, world, grads_for={rank})
     w = parts[rank]
     jfeats, _ = job_features(parts)
     bm = byte_model(w.tables, jfeats, world, rank)
@@ -709,10 +837,11 @@ def run_b200(args):
                   if owner.get(p) and prof[p]["ms"] else None} for p in prof}
 
     # ---- NVLink: this rank's exchanges per round, against the all-to-all
-    # bandwidth measured here on the same communicator (32 MiB to every peer)
+    # bandwidth measured here on the same communicator (256 MiB to every peer:
+    # smaller messages do not reach the links' rate)
     nvlink = None
     if dist:
-        per = 32 << 20
+        per = 256 << 20
         src = torch.empty(world * per // 4, dtype=torch.float32, device=dev)
         dst = torch.empty_like(src)
         for _ in range(2):
@@ -842,7 +971,7 @@ def run_b200(args):
     # ---- parity: one round from fresh tables against the reference (checker only)
     parity = None
     if not args.no_check:
-        reports = parity_check(eps, torch, parts, rank, world, dev, comms,
+        reports = parity_check(eps, torch, wl, args, parts, rank, world, dev, comms,
                                bitexact=not args.no_bitexact)
         ok = all(r["parity"] for r in reports)
         if dist:
@@ -862,7 +991,13 @@ def run_b200(args):
                                         for k in ("w", "m", "v")},
                   "long_max_rel_err": {k: max(r["long_max_rel_err"][k] for r in reports)
                                        for k in ("w", "m", "v")},
-                  "bitexact_mode_checked": any(r["reference_order"] for r in reports)}
+                  "bitexact_mode_checked": any(r["reference_order"] for r in reports),
+                  "job_occurrences_checked": reports[0]["check_occurrences"],
+                  "samples_per_rank_checked": reports[0]["check_samples_per_rank"],
+                  "job": ("the timed job" if reports[0]["check_occurrences"] ==
+                          reports[0]["job_occurrences"] else
+                          "the same config at a smaller batch per rank (every rank runs the "
+                          "reference on the whole job)")}
     if dist:
         comms[0].close()
         comms[1].close()
@@ -871,15 +1006,21 @@ def run_b200(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = host_threads()
-        times = reference_rounds(parts, args.config, world, steps=args.steps, warmup=1,
-                                 threads=threads, budget_s=20.0)
-        if times:
+        got = reference_rounds(wl, args, world, steps=args.steps, warmup=1, threads=threads,
+                               budget_s=15.0, round_s=1.0)
+        if got:
+            times, smp = got
             what = "push" if only_push else "lookup + push"
-            cpu = {"value": bm["N"] * len(times) / sum(times), "unit": UNIT,
-                   "cores": threads, "kind": "reference", "cpu_model": cpu_model(),
-                   "sample": f"{len(times)} rounds ({what}) of the same batch after 1 warm-up "
-                             f"round, at most ~20 s (reference DistributedClient over {threads} "
-                             f"CpuParameterService shards, one per host thread)"}
+            cpu = {"value": sum(p.occurrences for p in smp) * len(times) / sum(times),
+                   "unit": UNIT, "cores": threads, "kind": "reference", "cpu_model": cpu_model(),
+                   "sample": sample_text(smp, bm["N"], len(times), 1, what, threads) +
+                   "; at most ~15 s of timed rounds"}
+
+    # ---- at N = 1 with the default config: the N > 1 default config (3) on this
+    # GPU, device-timed as above, the base of its weak-scaling curve
+    scale_base = None
+    if world == 1 and args.config_default and not args.no_scale_base:
+        scale_base = scale_base_rounds(eps, torch, wl, args, dev, local_rank)
 
     if dist:
         dist.barrier()
@@ -909,6 +1050,7 @@ def run_b200(args):
         "parity": parity,
         "bitexact_mode": bitexact,
         "cpu_baseline": cpu,
+        "scale_base": scale_base,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,

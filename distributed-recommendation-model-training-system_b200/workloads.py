@@ -50,7 +50,7 @@ class Workload:
     name: str
     tables: list
     features: list
-    gradients: list           # float32 [output_rows, dim] per feature
+    gradients: list           # float32 [output_rows, dim] per feature (None: not drawn)
     seed: int
     meta: dict = field(default_factory=dict)
 
@@ -109,12 +109,16 @@ def to_ids(ranks: np.ndarray, rows: int, a: int, b: int) -> np.ndarray:
     return np.array([(a * int(x) + b) % rows for x in r], dtype=np.uint64)
 
 
-def gradients_for(rng, features, dims, sigma=1e-2):
+def gradients_for(rng, features, dims, sigma=1e-2, draw=True):
+    """Pooled-output gradients N(0, sigma), drawn after every key of the batch
+    (so `draw=False`, which leaves them out as None, does not change the keys)."""
+    if not draw:
+        return [None] * len(features)
     return [rng.normal(0.0, sigma, size=(f.output_rows, dims[f.table])).astype(np.float32)
             for f in features]
 
 
-def config1(seed: int = 1) -> Workload:
+def config1(seed: int = 1, gradients: bool = True) -> Workload:
     """Two tables (943 x 32, 1682 x 32), batch 128, one uniform id per table, no pooling."""
     rng = np.random.Generator(np.random.Philox(seed))
     tables = [TableSpec(1, 32, 943), TableSpec(2, 32, 1682)]
@@ -122,14 +126,14 @@ def config1(seed: int = 1) -> Workload:
     for i, t in enumerate(tables):
         keys = rng.integers(0, t.rows, size=128).astype(np.uint64)
         feats.append(FeatureSpec(t.id, i, SEQUENCE, keys, np.array([0, 128], np.uint64)))
-    grads = gradients_for(rng, feats, {t.id: t.dimension for t in tables})
+    grads = gradients_for(rng, feats, {t.id: t.dimension for t in tables}, draw=gradients)
     return Workload("cfg1: 943x32 + 1682x32, batch 128, one id per table, sequence", tables,
                     feats, grads, seed)
 
 
 def config2(seed: int = 2, batch: int = 4096, rows: int = 10_000_000, dim: int = 64,
             features: int = 8, alpha: float = 1.05, max_bag: int = 64,
-            map_seed: int | None = 2) -> Workload:
+            map_seed: int | None = 2, gradients: bool = True) -> Workload:
     """One 10M x 64 table, 8 multi-hot features, bags U[1,64], Zipf(1.05),
     features 0-3 sum and 4-7 mean.  The rank -> id map comes from `map_seed`
     (shared by every worker of a data-parallel job, so all workers draw from the
@@ -146,14 +150,15 @@ def config2(seed: int = 2, batch: int = 4096, rows: int = 10_000_000, dim: int =
         n = int(offsets[-1])
         keys = to_ids(zipf_ranks(rng, rows, alpha, n), rows, a, b)
         feats.append(FeatureSpec(1, fi, SUM if fi < features // 2 else MEAN, keys, offsets))
-    grads = gradients_for(rng, feats, {1: dim})
+    grads = gradients_for(rng, feats, {1: dim}, draw=gradients)
     return Workload(f"cfg2: {rows}x{dim}, {features} features, batch {batch}, bags U[1,{max_bag}], "
                     f"Zipf({alpha}), f0-3 sum / f4-7 mean", [TableSpec(1, dim, rows)], feats, grads,
                     seed, {"a": a, "b": b, "alpha": alpha})
 
 
 def config4(seed: int = 4, rows: int = 100_000_000, dim: int = 64, n: int = 262_144,
-            alpha: float = 1.2, map_seed: int | None = 4) -> Workload:
+            alpha: float = 1.2, map_seed: int | None = 4,
+            gradients: bool = True) -> Workload:
     """Push-heavy: one 100M x 64 table, 262,144 gradient rows, Zipf(1.2)
     (one id per sequence position).  Id map from `map_seed`, as config2."""
     rng = np.random.Generator(np.random.Philox(seed))
@@ -163,7 +168,7 @@ def config4(seed: int = 4, rows: int = 100_000_000, dim: int = 64, n: int = 262_
     keys = to_ids(zipf_ranks(rng, rows, alpha, n), rows, a, b)
     # n samples of one id each; sequence pooling: one gradient row per id
     feats = [FeatureSpec(1, 0, SEQUENCE, keys, np.arange(n + 1, dtype=np.uint64))]
-    grads = gradients_for(rng, feats, {1: dim})
+    grads = gradients_for(rng, feats, {1: dim}, draw=gradients)
     return Workload(f"cfg4: {rows}x{dim}, {n} gradient rows, Zipf({alpha})",
                     [TableSpec(1, dim, rows)], feats, grads, seed, {"a": a, "b": b})
 
@@ -190,7 +195,7 @@ def config3_tables(table_seed: int = CONFIG3_TABLE_SEED, tables: int = 26, dim: 
 
 def config3(seed: int = 3, batch: int = 65536, tables: int = 26, dim: int = 128,
             alpha: float = 1.1, row_scale: float = 1.0,
-            table_seed: int = CONFIG3_TABLE_SEED) -> Workload:
+            table_seed: int = CONFIG3_TABLE_SEED, gradients: bool = True) -> Workload:
     """26 tables x 128, rows log-uniform in [1e3, 4e7] (drawn from `table_seed`,
     with the id maps), one id per table per sample, Zipf(1.1); the batch from
     `seed`."""
@@ -200,7 +205,7 @@ def config3(seed: int = 3, batch: int = 65536, tables: int = 26, dim: int = 128,
     for t, (s, (a, b)) in enumerate(zip(specs, maps)):
         keys = to_ids(zipf_ranks(rng, s.rows, alpha, batch), s.rows, a, b)
         feats.append(FeatureSpec(s.id, t, SUM, keys, np.arange(batch + 1, dtype=np.uint64)))
-    grads = gradients_for(rng, feats, {s.id: s.dimension for s in specs})
+    grads = gradients_for(rng, feats, {s.id: s.dimension for s in specs}, draw=gradients)
     return Workload(f"cfg3: {tables} tables x {dim} ({sum(s.rows for s in specs)} rows), "
                     f"batch {batch}, one id per table, Zipf({alpha})", specs, feats, grads, seed,
                     {"table_seed": table_seed})
@@ -218,7 +223,8 @@ def zipf_ranks_continuous(rng, rows: int, alpha: float, n: int) -> np.ndarray:
 
 
 def config5(seed: int = 5, rows: int = 1_000_000_000, dim: int = 32, batch: int = 131072,
-            hot: int = 20, alpha: float = 1.05, map_seed: int | None = 5) -> Workload:
+            hot: int = 20, alpha: float = 1.05, map_seed: int | None = 5,
+            gradients: bool = True) -> Workload:
     """Large pooled workload: one 1e9 x 32 table, batch 131,072 x 20-hot sum
     pooling, Zipf(1.05) (continuous inverse CDF: the exact one would need a
     1e9-entry table).  `rows` below 1e9 is the largest fitting subset of the
@@ -231,7 +237,7 @@ def config5(seed: int = 5, rows: int = 1_000_000_000, dim: int = 32, batch: int 
     keys = to_ids(zipf_ranks_continuous(rng, rows, alpha, n), rows, a, b)
     offsets = np.arange(0, n + 1, hot, dtype=np.uint64)
     feats = [FeatureSpec(1, 0, SUM, keys, offsets)]
-    grads = gradients_for(rng, feats, {1: dim})
+    grads = gradients_for(rng, feats, {1: dim}, draw=gradients)
     return Workload(f"cfg5: {rows}x{dim}, batch {batch} x {hot}-hot sum, Zipf({alpha})",
                     [TableSpec(1, dim, rows)], feats, grads, seed, {"a": a, "b": b})
 
