@@ -567,7 +567,7 @@ class ParameterStore:
     def route(self, feats: Sequence[FeatureInput], shard_count: int, counts, stream=None):
         """Partitions device features by key % shard_count (eps_b200_route,
         asynchronous).  `counts` is a device int64 tensor [shard_count,
-        4 * len(feats) + 1] that receives the per-shard count rows.  Returns the
+        5 * len(feats) + 1] that receives the per-shard count rows.  Returns the
         route id."""
         arr, on_device, keep = self._features(feats)
         if not on_device:

@@ -99,7 +99,7 @@ struct Prepared {
   unsigned F = 0;
   std::vector<unsigned> dims, pools, tables;
   // first phase (prepare): the count rows, on their way to the host
-  long long* counts = nullptr;      // pinned [2][n][4F + 1]: rows sent | rows received
+  long long* counts = nullptr;      // pinned [2][n][5F + 1]: rows sent | rows received
   size_t counts_words = 0;
   cudaEvent_t counts_ready = nullptr;
   cudaStream_t in = nullptr;        // the input stream of the first phase
@@ -109,8 +109,8 @@ struct Prepared {
   bool exchanged = false;
   int fail_code = 0;                // the batch's input error, reported by its lookup
   std::string fail_message;
-  std::vector<uint64_t> mine;       // [n][F][2] keys, kept bags of this rank's batch per owner
-  std::vector<uint64_t> peer;       // [n][F][2] of every requester's part on this shard
+  std::vector<uint64_t> mine;       // [n][F][3] keys, kept bags, distinct keys of this rank's batch per owner
+  std::vector<uint64_t> peer;       // [n][F][3] of every requester's part on this shard
   uint64_t* rpay = nullptr;         // received payload (device)
   cudaEvent_t ready = nullptr;      // on the input stream, after the payload exchange
 };
@@ -121,6 +121,7 @@ struct Round {
   std::vector<unsigned> dims, pools, tables;
   std::vector<uint64_t> peer;
   std::vector<uint64_t> send_f, recv_f;   // floats of partials sent to requester r / from owner o
+  std::vector<uint64_t> gsend_f, grecv_f; // floats of gradients sent to owner o / from requester r
 };
 
 template <typename T>
@@ -219,17 +220,17 @@ struct EpsB200Client {
 void EpsB200Client::Exchange(Prepared& P, cudaStream_t s) {
   P.exchanged = true;
   Cu(cudaEventSynchronize(P.counts_ready));   // recorded a call ago: normally long done
-  const unsigned F = P.F, width = 4 * F + 1;
+  const unsigned F = P.F, width = 5 * F + 1;
   const long long* mine = P.counts;
   const long long* recv = P.counts + (size_t)n * width;
   bool peer_error = false, bad_schema = false;
   for (unsigned r = 0; r < n; ++r) {
-    peer_error |= recv[(size_t)r * width + 4 * F] != 0;
+    peer_error |= recv[(size_t)r * width + 5 * F] != 0;
     for (unsigned f = 0; f < F; ++f)
       bad_schema |= recv[(size_t)r * width + 2 * F + f] != P.tables[f] ||
                     recv[(size_t)r * width + 3 * F + f] != P.pools[f];
   }
-  const long long own_bits = mine[4 * F];
+  const long long own_bits = mine[5 * F];
   if (P.host_code || own_bits || peer_error || bad_schema) {
     EpsB200Status st;
     if (P.route) eps_b200_route_release(store, P.route, &st);
@@ -244,20 +245,26 @@ void EpsB200Client::Exchange(Prepared& P, cudaStream_t s) {
     GivePinned(P);
     return;
   }
-  P.mine.resize((size_t)n * F * 2);
-  P.peer.resize((size_t)n * F * 2);
+  P.mine.resize((size_t)n * F * 3);
+  P.peer.resize((size_t)n * F * 3);
   std::vector<uint64_t> send_words(n, 0), recv_words(n, 0);
   for (unsigned o = 0; o < n; ++o)
-    for (unsigned f = 0; f < F; ++f)
+    for (unsigned f = 0; f < F; ++f) {
       for (unsigned k = 0; k < 2; ++k) {
-        P.mine[((size_t)o * F + f) * 2 + k] = (uint64_t)mine[(size_t)o * width + 2 * f + k];
-        P.peer[((size_t)o * F + f) * 2 + k] = (uint64_t)recv[(size_t)o * width + 2 * f + k];
+        P.mine[((size_t)o * F + f) * 3 + k] = (uint64_t)mine[(size_t)o * width + 2 * f + k];
+        P.peer[((size_t)o * F + f) * 3 + k] = (uint64_t)recv[(size_t)o * width + 2 * f + k];
       }
+      P.mine[((size_t)o * F + f) * 3 + 2] = (uint64_t)mine[(size_t)o * width + 4 * F + f];
+      P.peer[((size_t)o * F + f) * 3 + 2] = (uint64_t)recv[(size_t)o * width + 4 * F + f];
+    }
   GivePinned(P);
+  // payload words per (owner, feature): keys, kept-bag offsets (+1), lengths, and
+  // [0, U, U distinct keys] for a deduplicated group
+  auto words = [](const uint64_t* c) { return c[0] + 2 * c[1] + 1 + (c[2] ? c[2] + 2 : 0); };
   for (unsigned o = 0; o < n; ++o)
     for (unsigned f = 0; f < F; ++f) {
-      send_words[o] += P.mine[((size_t)o * F + f) * 2] + 2 * P.mine[((size_t)o * F + f) * 2 + 1] + 1;
-      recv_words[o] += P.peer[((size_t)o * F + f) * 2] + 2 * P.peer[((size_t)o * F + f) * 2 + 1] + 1;
+      send_words[o] += words(&P.mine[((size_t)o * F + f) * 3]);
+      recv_words[o] += words(&P.peer[((size_t)o * F + f) * 3]);
     }
   // ---- 3. payload: keys / kept-bag offsets / valid lengths per owner
   uint64_t total_send = 0, total_recv = 0;
@@ -339,7 +346,7 @@ int eps_b200_client_prepare(EpsB200Client* c, const EpsB200Feature* features, ui
     Require(c && features && prepared_out && count > 0 && count <= 1024, "invalid client prepare");
     std::lock_guard lock(c->mutex);
     Cu(cudaSetDevice(c->device));
-    const unsigned n = c->n, F = (unsigned)count, width = 4 * F + 1;
+    const unsigned n = c->n, F = (unsigned)count, width = 5 * F + 1;
     const cudaStream_t in = static_cast<cudaStream_t>(input_stream);
     Prepared P;
     P.F = F;
@@ -366,7 +373,7 @@ int eps_b200_client_prepare(EpsB200Client* c, const EpsB200Feature* features, ui
             h[(size_t)o * width + 2 * F + f] = P.tables[f];
             h[(size_t)o * width + 3 * F + f] = P.pools[f];
           }
-          h[(size_t)o * width + 4 * F] = -1;
+          h[(size_t)o * width + 5 * F] = -1;
         }
         Cu(cudaMemcpyAsync(rows, h.data(), h.size() * 8, cudaMemcpyHostToDevice, in));
         Cu(cudaStreamSynchronize(in));          // h is pageable and local
@@ -423,11 +430,19 @@ int eps_b200_client_lookup(EpsB200Client* c, uint64_t prepared, EpsB200Buffer* o
     R.peer = P.peer;
     R.send_f.assign(n, 0);
     R.recv_f.assign(n, 0);
+    R.gsend_f.assign(n, 0);
+    R.grecv_f.assign(n, 0);
     for (unsigned o = 0; o < n; ++o)
       for (unsigned f = 0; f < F; ++f) {
-        const size_t i = ((size_t)o * F + f) * 2 + (P.pools[f] == 2 ? 0 : 1);
-        R.send_f[o] += P.peer[i] * P.dims[f];     // partials this shard returns to requester o
-        R.recv_f[o] += P.mine[i] * P.dims[f];     // partials owner o returns to this rank
+        // rows of a (shard, feature) block: its keys (sequence) or kept bags;
+        // the partials of a deduplicated group: its distinct keys
+        const uint64_t* pe = &P.peer[((size_t)o * F + f) * 3];
+        const uint64_t* mi = &P.mine[((size_t)o * F + f) * 3];
+        const unsigned k = P.pools[f] == 2 ? 0 : 1;
+        R.send_f[o] += (pe[2] ? pe[2] : pe[k]) * P.dims[f];   // partials returned to requester o
+        R.recv_f[o] += (mi[2] ? mi[2] : mi[k]) * P.dims[f];   // partials owner o returns here
+        R.gsend_f[o] += mi[k] * P.dims[f];                    // gradients sent to owner o
+        R.grecv_f[o] += pe[k] * P.dims[f];                    // gradients received from requester o
       }
     uint64_t ts = 0, tr = 0;
     for (unsigned o = 0; o < n; ++o) { ts += R.send_f[o]; tr += R.recv_f[o]; }
@@ -479,7 +494,7 @@ int eps_b200_client_push(EpsB200Client* c, uint64_t round, const EpsB200Buffer* 
     const unsigned n = c->n;
     const cudaStream_t s = static_cast<cudaStream_t>(stream_arg);
     uint64_t ts = 0, tr = 0;
-    for (unsigned o = 0; o < n; ++o) { ts += R.recv_f[o]; tr += R.send_f[o]; }
+    for (unsigned o = 0; o < n; ++o) { ts += R.gsend_f[o]; tr += R.grecv_f[o]; }
     float* send = DevAlloc<float>(ts, s);
     float* recv = DevAlloc<float>(tr, s);
     uint32_t* flag = DevAlloc<uint32_t>(1, s);
@@ -489,8 +504,8 @@ int eps_b200_client_push(EpsB200Client* c, uint64_t round, const EpsB200Buffer* 
       Cu(cudaMemsetAsync(flag, 0, sizeof(uint32_t), s));
       Call(eps_b200_route_gather(c->store, R.route, gradients, send, flag, s, &st), st);
       Call(eps_b200_comm_allreduce_max(c->comm, flag, 1, s, &st), st);
-      // gradient rows travel in the layout the partials came back in
-      c->Alltoall(c->comm, send, R.recv_f, recv, R.send_f, 4, s, EPS_B200_EXCHANGE_GRADIENTS);
+      // gradient rows: one per kept bag (or key) of every (shard, feature) block
+      c->Alltoall(c->comm, send, R.gsend_f, recv, R.grecv_f, 4, s, EPS_B200_EXCHANGE_GRADIENTS);
       rc = eps_b200_serve_push(c->store, R.ticket, recv, R.peer.data(), R.tables.data(),
                                R.pools.data(), n, R.F, flag, s, wait, &st);
     } catch (...) {

@@ -104,13 +104,28 @@ constexpr unsigned int kUnitBags = 8;
 constexpr unsigned int kUnitPositions = 256;
 constexpr unsigned int kUnitSlices = kUnitPositions / 32;   // 32-position slices of a unit
 
-// Bags per work unit of a pooled feature: one bag when bags hold 8 or more keys
-// on average (enough work and parallelism per bag), else kUnitBags, so that the
-// chain of dependent loads (offsets, keys, rows) is paid once per unit.
+constexpr unsigned int kEmitShortBags = 32;
+
+// Bags per gather unit of a pooled feature: one bag when bags hold 8 or more
+// keys on average (enough work and parallelism per bag), else `group` bags (the
+// gather's lanes per group, 8..32: a lane holds one bag's range), whose keys the
+// group walks as one run, so that the chain of dependent loads (offsets, keys,
+// rows) is paid once per unit and rows load back to back across bags.
 inline unsigned feature_unit_bags(unsigned pooling, unsigned long long key_count,
-                                  unsigned long long bag_count) {
+                                  unsigned long long bag_count, unsigned group) {
   if (pooling == 2) return 0;
-  return (bag_count && key_count >= 8ull * bag_count) ? 1u : kUnitBags;
+  if (bag_count && key_count >= 8ull * bag_count) return 1u;
+  return group < kUnitBags ? kUnitBags : (group > 32u ? 32u : group);
+}
+
+// Bags per emit unit of a pooled feature (one warp per unit, one occurrence per
+// lane and step): kUnitBags for long bags, kEmitShortBags for short ones, so a
+// step of one-key bags still fills the warp.
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+inline unsigned emit_unit_bags(unsigned unit_bags) {
+  return unit_bags == 1u ? kUnitBags : kEmitShortBags;
 }
 
 // Work units of one feature (see LookupFeature::units); `unit_bags` bags per

@@ -138,7 +138,19 @@ struct RouteLaunch {
   unsigned int* nonfinite;         // gather: set to 1 if any gradient value is not finite
   unsigned long long* row_pre;          // [shard_count * feature_count] row prefix
   unsigned long long* row_total_dev;    // rows of all blocks (device)
-  long long* counts_out;                // [shard_count][4F + 1] count rows (route_layout)
+  long long* counts_out;                // [shard_count][5F + 1] count rows (route_layout)
+  // Distinct rows of one-key groups.  A (shard, feature) group g = o * F + f of a
+  // dense table whose kept bags hold one key each on shard o (or a sequence
+  // feature) is deduplicated when it has fewer distinct keys than keys: the
+  // owner gathers each distinct row once and the merge reads it by rank.
+  unsigned long long* dd_keys;          // [dd_mask + 1] (key << 10 | g); ~0 = free
+  unsigned int* dd_rank;                // [dd_mask + 1] the key's rank among g's distinct keys
+  unsigned long long dd_mask;
+  unsigned int* dd_count;               // [cells F-major: o * F + f] distinct keys of group g
+  unsigned int* dd_used;                // [o * F + f] distinct keys if g is deduplicated, else 0
+  unsigned long long* dd_off;           // [o * F + f] float offsets of the partials received
+  unsigned long long* dd_words;         // [o * F + f + 1] prefix of the unique-key words (U + 2)
+  unsigned int* dd_idx;                 // [N] shard-ordered key -> rank (deduplicated groups)
   int has_sequence;
   int vec, group, iters;           // launch shape (see choose_shape)
 };

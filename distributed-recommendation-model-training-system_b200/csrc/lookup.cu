@@ -12,11 +12,13 @@
 // bit-identical to the reference's.
 //
 // Work decomposition: a group of G lanes (G = D/4 for D = 32/64/128, so a row
-// is read with one 128-bit load per lane) owns one bag at a time; a warp holds
-// 32/G bags.  The group fetches G keys with one coalesced load (the next chunk's
-// keys are requested before the current chunk's rows), broadcasts the slots by
-// shuffle and issues up to DEPTH row loads back to back before the dependent
-// adds.  Rows past the end of a chunk are added as -0.0f, the additive identity
+// is read with one 128-bit load per lane) owns one work unit at a time -- one
+// long bag, G consecutive short bags (walked as one run of keys, rows loaded
+// back to back across bag boundaries) or 256 positions of a sequence feature;
+// a warp holds 32/G groups.  The group fetches G keys with one coalesced load
+// (the next chunk's keys are requested before the current chunk's rows),
+// broadcasts the slots by shuffle and issues up to DEPTH row loads back to back
+// before the dependent adds.  Rows past the end of a chunk are added as -0.0f, the additive identity
 // of round-to-nearest addition, so the add loop carries no predicates.
 // When the lookup will be pushed (non-read-only), `emit_kernel` writes the
 // occurrence list consumed by the coalescing sort before the gather runs:
@@ -40,6 +42,9 @@ namespace {
 #endif
 #ifndef EPS_LOOKUP_MIN_BLOCKS
 #define EPS_LOOKUP_MIN_BLOCKS 4
+#endif
+#ifndef EPS_LOOKUP_GRID_PER_SM
+#define EPS_LOOKUP_GRID_PER_SM (EPS_LOOKUP_MIN_BLOCKS * 4)   // blocks per SM in the grid (4 waves)
 #endif
 
 template <int G, int VEC, int ITERS, typename KeyT>
@@ -112,6 +117,110 @@ __global__ void __launch_bounds__(256, EPS_LOOKUP_MIN_BLOCKS) lookup_kernel(Look
         s_mine = (unsigned)s;
         e_mine = (unsigned)e;
       }
+    }
+    if (!sequence && F->unit_bags > 1) {
+      // short bags: the unit's keys [S, E) walked as one run in position order,
+      // DEPTH rows in flight across bag boundaries.  Bag `cur`'s sum is stored
+      // when the run reaches its end: the adds per bag stay in position order,
+      // so the sums equal the per-bag loop's.  Everything here is uniform over
+      // the group (positions, bag ends and slots come by shuffle).
+      const unsigned S = grp.shfl(s_mine, 0);
+      const unsigned E = grp.shfl(e_mine, (nb - 1) & (G - 1));
+      unsigned cur = 0, kept = 0;
+      unsigned e_cur = grp.shfl(e_mine, 0);
+      float acc[C];
+#pragma unroll
+      for (int q = 0; q < C; ++q) acc[q] = 0.0f;
+      auto close_bag = [&]() {
+        const unsigned long long b = b0 + cur;
+        const unsigned s_cur = grp.shfl(s_mine, cur & (G - 1));
+        unsigned long long len = has_pad ? kept : (unsigned long long)(e_cur - s_cur);
+        if (F->lengths) {
+          const unsigned long long given = F->lengths[b];
+          if (given < len) err |= kLookupShortLength;
+          len = given;
+        }
+        const bool mean = F->pooling == 1;
+        const float denom = (float)len;   // u64 -> float, round to nearest
+#pragma unroll
+        for (int it = 0; it < ITERS; ++it) {
+          const unsigned col = (it * G + gl) * VEC;
+          if (col >= D) continue;
+          float t[VEC];
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) {
+            float x = acc[it * VEC + v];
+            if (p.client) {
+              x = __fadd_rn(0.0f, x);
+              if (mean && len) x = __fdiv_rn(x, denom);
+            }
+            t[v] = x;
+          }
+          store_vec<VEC>(out + b * D + col, t);
+        }
+#pragma unroll
+        for (int q = 0; q < C; ++q) acc[q] = 0.0f;
+        kept = 0;
+        ++cur;
+        e_cur = grp.shfl(e_mine, cur & (G - 1));
+      };
+      unsigned long long key = (S + gl < E) ? keys[S + gl] : 0ull;
+#pragma unroll 1
+      for (unsigned c0 = S; c0 < E; c0 += G) {
+        const unsigned i = c0 + gl;
+        unsigned slot = ~0u;
+        if (i < E && has_pad && key == pad_key) {
+          slot = kPadSlot;
+        } else if (i < E && F->slots) {
+          const unsigned hs = F->slots[i];
+          if (hs < kPadSlot) slot = hs;
+          else err |= kLookupBadKey;
+        } else if (i < E) {
+          unsigned long long sl, sh;
+          if (p.shard_count == 1) { sl = key; sh = 0; }
+          else { sl = key / p.shard_count; sh = key - sl * p.shard_count; }
+          if (sh == p.shard_id && sl < rows) slot = (unsigned)sl;
+          else err |= kLookupBadKey;
+        }
+        if (i + G < E) key = keys[i + G];   // the next chunk's keys in flight
+        const int cnt = (int)min((unsigned)G, E - c0);
+#pragma unroll 1
+        for (int j0 = 0; j0 < cnt; j0 += DEPTH) {
+          float r[DEPTH][C];
+          bool use[DEPTH];
+#pragma unroll
+          for (int uu = 0; uu < DEPTH; ++uu) {
+            const unsigned su = grp.shfl(slot, (j0 + uu) & (G - 1));
+            use[uu] = (j0 + uu < cnt) && su < kPadSlot;
+            const float* row = state + (unsigned long long)su * row_stride;
+#pragma unroll
+            for (int it = 0; it < ITERS; ++it) {
+              const unsigned col = (it * G + gl) * VEC;
+              float t[VEC];
+              if (use[uu] && col < D) load_vec<VEC>(row + col, t);
+              else {
+#pragma unroll
+                for (int v = 0; v < VEC; ++v) t[v] = -0.0f;
+              }
+#pragma unroll
+              for (int v = 0; v < VEC; ++v) r[uu][it * VEC + v] = t[v];
+            }
+          }
+#pragma unroll
+          for (int uu = 0; uu < DEPTH; ++uu) {
+            if (j0 + uu >= cnt) break;
+            const unsigned pos = c0 + (unsigned)(j0 + uu);
+            while (cur < nb && pos >= e_cur) close_bag();
+            if (cur < nb) {
+#pragma unroll
+              for (int q = 0; q < C; ++q) acc[q] = __fadd_rn(acc[q], r[uu][q]);
+              kept += use[uu] ? 1u : 0u;
+            }
+          }
+        }
+      }
+      while (cur < nb) close_bag();      // bags ending at E, empty bags included
+      continue;
     }
     unsigned s = grp.shfl(s_mine, 0), e = grp.shfl(e_mine, 0);
     unsigned long long key = (s + gl < e) ? keys[s + gl] : 0ull;
@@ -246,15 +355,16 @@ __global__ void __launch_bounds__(256, EPS_LOOKUP_MIN_BLOCKS) lookup_kernel(Look
 // gather kernel's.
 //
 // One warp per emit unit (LookupFeature::emit_units), 32 occurrences per step:
-// a pooled unit is kUnitBags consecutive bags -- their offsets are read once, and
-// lane j of a step finds its bag among them -- and a sequence unit is
+// a pooled unit is kUnitBags consecutive bags of a long-bag feature, or
+// kEmitShortBags of a short-bag one -- their offsets are read once, and lane j of
+// a step finds its bag among them -- and a sequence unit is
 // kUnitPositions consecutive positions plus the same span of offsets, which it
 // validates (a sequence feature's bags do not shape its outputs).  So neither a
 // very long bag nor many one-key bags serialise on one warp.
 template <typename KeyT>
 __global__ void __launch_bounds__(256) emit_kernel(LookupLaunch p) {
   __shared__ unsigned long long s_unit_base[kMaxFeatures + 1];
-  __shared__ unsigned s_kept[8][kUnitBags];
+  __shared__ unsigned s_kept[8][kEmitShortBags];
   const unsigned fc = p.feature_count;
   for (unsigned i = threadIdx.x; i < fc; i += blockDim.x) s_unit_base[i] = p.features[i].emit_base;
   if (threadIdx.x == 0) s_unit_base[fc] = p.emit_total;
@@ -314,15 +424,16 @@ __global__ void __launch_bounds__(256) emit_kernel(LookupLaunch p) {
       }
       continue;
     }
-    // pooled: bags b0 .. b0 + nb - 1
-    const unsigned long long b0 = lu * kUnitBags;
-    const unsigned nb = (unsigned)min((unsigned long long)kUnitBags, B - b0);
-    unsigned long long o = 0;
-    if (lane <= nb) o = F->offsets[b0 + lane];
-    unsigned long long s = o, e = __shfl_down_sync(0xffffffffu, o, 1);
+    // pooled: bags b0 .. b0 + nb - 1 (ub <= 32 bags per unit, lane k holding bag k)
+    const unsigned ub = emit_unit_bags(F->unit_bags);
+    const unsigned long long b0 = lu * ub;
+    const unsigned nb = (unsigned)min((unsigned long long)ub, B - b0);
+    unsigned long long s = 0, e = 0;
     unsigned n = 0;
     if (lane < nb) {
       const unsigned long long b = b0 + lane;
+      s = F->offsets[b];
+      e = F->offsets[b + 1];
       if (b == 0 && s != 0) err |= kLookupBadOffsets;
       if (b + 1 == B && e != key_count) err |= kLookupBadOffsets;
       if (s > e || e > key_count) { err |= kLookupBadOffsets; s = e = 0; }
@@ -330,24 +441,23 @@ __global__ void __launch_bounds__(256) emit_kernel(LookupLaunch p) {
     }
     unsigned incl = n;
 #pragma unroll
-    for (int d = 1; d < (int)kUnitBags; d <<= 1) {
+    for (int d = 1; d < 32; d <<= 1) {
       const unsigned y = __shfl_up_sync(0xffffffffu, incl, d);
       if (lane >= (unsigned)d) incl += y;
     }
-    const unsigned total = __shfl_sync(0xffffffffu, incl, kUnitBags - 1);
-    const unsigned excl = incl - n;
-    unsigned ex[kUnitBags];
-#pragma unroll
-    for (unsigned k = 0; k < kUnitBags; ++k) ex[k] = __shfl_sync(0xffffffffu, excl, k);
-    if (lane < kUnitBags) s_kept[w][lane] = 0;
+    const unsigned total = __shfl_sync(0xffffffffu, incl, 31);
+    const unsigned excl = incl - n;       // bag's first entry in the unit's run
+    s_kept[w][lane] = 0;
     __syncwarp();
     for (unsigned c0 = 0; c0 < total; c0 += 32) {
       const unsigned i = c0 + lane;
+      // bag of entry i: the last bag whose first entry is <= i (binary lifting
+      // over the lanes' non-decreasing first entries; bag 0's is 0)
       unsigned k = 0;
-#pragma unroll
-      for (unsigned kk = 1; kk < kUnitBags; ++kk)
-        if (kk < nb && ex[kk] <= i) k = kk;
-      // bag k's first occurrence and entry offset, from lane k (a per-lane source)
+      for (unsigned step = ub >> 1; step; step >>= 1) {
+        const unsigned ek = __shfl_sync(0xffffffffu, excl, k + step);
+        if (k + step < nb && ek <= i) k += step;
+      }
       const unsigned long long sk = __shfl_sync(0xffffffffu, s, k);
       const unsigned ek = __shfl_sync(0xffffffffu, excl, k);
       if (i < total) {
@@ -380,7 +490,7 @@ template <int G, int VEC, int ITERS>
 cudaError_t launch_key(const LookupLaunch& p, cudaStream_t s) {
   const unsigned long long groups_per_block = 256 / G;
   const unsigned long long want = (p.unit_total + groups_per_block - 1) / groups_per_block;
-  const unsigned long long cap = 148ull * EPS_LOOKUP_MIN_BLOCKS * 4;   // 4 waves
+  const unsigned long long cap = 148ull * EPS_LOOKUP_GRID_PER_SM;
   const unsigned grid = (unsigned)(want < cap ? want : cap);
   if (p.key64) lookup_kernel<G, VEC, ITERS, unsigned long long><<<grid, 256, 0, s>>>(p);
   else lookup_kernel<G, VEC, ITERS, unsigned int><<<grid, 256, 0, s>>>(p);

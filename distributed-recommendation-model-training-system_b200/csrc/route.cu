@@ -47,6 +47,62 @@ __device__ __forceinline__ unsigned feature_of(const unsigned long long* s_base,
   return lo;
 }
 
+// ---------------------------------------------------------- distinct rows
+// A group (shard o, feature f) whose kept bags hold exactly one key each on
+// shard o -- or a sequence feature's keys on o -- has a partial per kept bag
+// that is just 0 + the key's row.  When such a group (dense table) has fewer
+// distinct keys than keys, the owner returns each distinct row once and the
+// merge reads a bag's row by its key's rank: the bytes change, the values and
+// their order of addition do not.  The ranks come from a hash set of
+// (key << 10 | group) built while the batch is prepared.
+constexpr unsigned long long kDedupFree = ~0ull;
+
+__device__ __forceinline__ unsigned long long dd_mix(unsigned long long x) {
+  // MurmurHash3's 64-bit finaliser
+  x ^= x >> 33;
+  x *= 0xff51afd7ed558ccdull;
+  x ^= x >> 33;
+  x *= 0xc4ceb9fe1a85ec53ull;
+  x ^= x >> 33;
+  return x;
+}
+
+// keys and kept bags of group (o, f), from route_bounds
+__device__ __forceinline__ void group_counts(const RouteLaunch& p, unsigned o, unsigned f,
+                                             unsigned& keys, unsigned& kept) {
+  const unsigned* a = p.bounds + 2 * (o * (p.feature_count + 1) + f);
+  keys = a[2] - a[0];
+  kept = a[3] - a[1];
+}
+
+__device__ __forceinline__ bool dedup_eligible(const RouteLaunch& p, const LookupFeature* F,
+                                               unsigned o, unsigned f) {
+  unsigned keys, kept;
+  group_counts(p, o, f, keys, kept);
+  return p.dd_mask && F->rows <= (1ull << 53) && keys > 0 && (F->pooling == 2 || keys == kept);
+}
+
+__device__ __forceinline__ void dd_claim(const RouteLaunch& p, unsigned long long comp, unsigned g) {
+  unsigned long long h = dd_mix(comp) & p.dd_mask;
+  for (unsigned long long probe = 0; probe <= p.dd_mask; ++probe) {
+    const unsigned long long old = atomicCAS(p.dd_keys + h, kDedupFree, comp);
+    if (old == kDedupFree) { p.dd_rank[h] = atomicAdd(p.dd_count + g, 1u); return; }
+    if (old == comp) return;
+    h = (h + 1) & p.dd_mask;
+  }
+}
+
+__device__ __forceinline__ unsigned dd_find(const RouteLaunch& p, unsigned long long comp) {
+  unsigned long long h = dd_mix(comp) & p.dd_mask;
+  for (unsigned long long probe = 0; probe <= p.dd_mask; ++probe) {
+    const unsigned long long k = p.dd_keys[h];
+    if (k == comp) return p.dd_rank[h];
+    if (k == kDedupFree) return 0u;      // not reached: every key was claimed
+    h = (h + 1) & p.dd_mask;
+  }
+  return 0u;
+}
+
 // ------------------------------------------------------------------ count
 // One warp per bag: validates the bag and counts its keys per shard (lane o
 // holds shard o's count; n <= 32).
@@ -94,6 +150,38 @@ __global__ void __launch_bounds__(256) route_count(RouteLaunch p) {
   }
   err = __reduce_or_sync(~0u, err);
   if (err && lane == 0) atomicOr(p.error, err);
+}
+
+// One warp per bag (after route_bounds): every key of an eligible group joins
+// the group's distinct-key set; the key that inserts an entry takes the next rank.
+__global__ void __launch_bounds__(256) route_dedup_claim(RouteLaunch p) {
+  __shared__ unsigned long long s_base[kMaxFeatures + 1];
+  const unsigned fc = p.feature_count;
+  for (unsigned i = threadIdx.x; i < fc; i += blockDim.x) s_base[i] = p.features[i].bag_base;
+  if (threadIdx.x == 0) s_base[fc] = p.bag_total;
+  __syncthreads();
+  const unsigned lane = threadIdx.x & 31;
+  const unsigned long long warp = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) >> 5;
+  const unsigned long long nwarps = (gridDim.x * (unsigned long long)blockDim.x) >> 5;
+  const unsigned n = p.shard_count;
+  for (unsigned long long g = warp; g < p.bag_total; g += nwarps) {
+    const unsigned f = feature_of(s_base, fc, g);
+    const LookupFeature* F = p.features + f;
+    const unsigned long long b = g - F->bag_base;
+    unsigned long long o2 = 0;
+    if (lane < 2) o2 = F->offsets[b + lane];
+    const unsigned long long s = __shfl_sync(~0u, o2, 0), e = __shfl_sync(~0u, o2, 1);
+    if (s > e || e > F->key_count) continue;      // reported by route_count
+    const bool has_pad = F->has_padding != 0;
+    for (unsigned long long c0 = s; c0 < e; c0 += 32) {
+      const unsigned long long i = c0 + lane;
+      if (i >= e) continue;
+      const unsigned long long key = F->keys[i];
+      if ((has_pad && key == F->padding_key) || key >= F->rows) continue;
+      const unsigned o = (unsigned)(key % n);
+      if (dedup_eligible(p, F, o, f)) dd_claim(p, (key << 10) | (o * fc + f), o * fc + f);
+    }
+  }
 }
 
 // --------------------------------------------------------- three-phase scan
@@ -200,53 +288,70 @@ __global__ void route_bounds(RouteLaunch p) {
   p.bounds[2 * t + 1] = p.pb[idx];
 }
 
-// One block: the (shard, feature) row blocks of the partial / gradient exchange
-// (part_off: float offsets, row_pre: row prefix, shard-major) and the count rows
-// sent to every shard before the payload: [keys(F) kept(F) interleaved as
-// (keys, kept) per feature | table ids (F) | poolings (F) | error], int64.
+// One block: the (shard, feature) row blocks of the gradient exchange (part_off:
+// float offsets, row_pre: row prefix, shard-major), of the partials received
+// (dd_off: distinct rows for deduplicated groups), the unique-key words of the
+// payload (dd_words) and the count rows sent to every shard before the payload:
+// [keys(F) kept(F) interleaved as (keys, kept) per feature | table ids (F) |
+// poolings (F) | distinct keys (F, 0 = not deduplicated) | error], int64.
 __global__ void __launch_bounds__(1024) route_layout(RouteLaunch p) {
   __shared__ unsigned s_warp[33];
-  __shared__ unsigned long long s_carry[2];
+  __shared__ unsigned long long s_carry[4];
   const unsigned F = p.feature_count, cells = p.shard_count * F;
-  if (threadIdx.x == 0) { s_carry[0] = 0; s_carry[1] = 0; }
+  if (threadIdx.x < 4) s_carry[threadIdx.x] = 0;
   __syncthreads();
   const unsigned err = *(volatile const unsigned*)p.error;
   for (unsigned base = 0; base < cells; base += blockDim.x) {
     const unsigned c = base + threadIdx.x;
-    unsigned rows = 0, floats = 0;
+    unsigned rows = 0, floats = 0, dfloats = 0, words = 0;
     if (c < cells) {
       const unsigned o = c / F, f = c % F;
-      const unsigned* a = p.bounds + 2 * (o * (F + 1) + f);
-      const unsigned keys = a[2] - a[0], kept = a[3] - a[1];
+      unsigned keys, kept;
+      group_counts(p, o, f, keys, kept);
       const LookupFeature* X = p.features + f;
       rows = X->pooling == 2 ? keys : kept;
       floats = rows * X->dim;
-      long long* row = p.counts_out + (unsigned long long)o * (4 * F + 1);
+      const bool dd = dedup_eligible(p, X, o, f) && p.dd_count[c] < keys;
+      const unsigned U = dd ? p.dd_count[c] : 0u;
+      p.dd_used[c] = U;
+      dfloats = (dd ? U : rows) * X->dim;
+      words = dd ? U + 2 : 0u;
+      long long* row = p.counts_out + (unsigned long long)o * (5 * F + 1);
       row[2 * f] = keys;
       row[2 * f + 1] = kept;
       row[2 * F + f] = X->table_rank;        // the table id, in a route's descriptors
       row[3 * F + f] = X->pooling;
-      if (f == 0) row[4 * F] = err;
+      row[4 * F + f] = U;
+      if (f == 0) row[5 * F] = err;
     }
-    unsigned tr, tf;
+    unsigned tr, tf, td, tw;
     const unsigned er = block_exclusive(rows, s_warp, tr);
     const unsigned ef = block_exclusive(floats, s_warp, tf);
+    const unsigned ed = block_exclusive(dfloats, s_warp, td);
+    const unsigned ew = block_exclusive(words, s_warp, tw);
     if (c < cells) {
       p.row_pre[c] = s_carry[0] + er;
       p.part_off[c] = s_carry[1] + ef;
+      p.dd_off[c] = s_carry[2] + ed;
+      p.dd_words[c] = s_carry[3] + ew;
     }
     __syncthreads();
-    if (threadIdx.x == 0) { s_carry[0] += tr; s_carry[1] += tf; }
+    if (threadIdx.x == 0) { s_carry[0] += tr; s_carry[1] += tf; s_carry[2] += td; s_carry[3] += tw; }
     __syncthreads();
   }
-  if (threadIdx.x == 0) *p.row_total_dev = s_carry[0];
+  if (threadIdx.x == 0) {
+    *p.row_total_dev = s_carry[0];
+    p.dd_words[cells] = s_carry[3];
+  }
 }
 
 // ---------------------------------------------------------------- scatter
 __device__ __forceinline__ unsigned long long extra_of(const RouteLaunch& p, unsigned o) {
-  // u64 words before shard o's keys that are not keys: the offsets and lengths
-  // regions of shards 0 .. o-1 (2 per kept bag + 1 per feature)
-  return 2ull * p.pb[o * p.bag_total] + (unsigned long long)o * p.feature_count;
+  // u64 words before shard o's keys that are not keys: the offsets, lengths and
+  // unique-key regions of shards 0 .. o-1 (2 per kept bag + 1 per feature, and
+  // U + 2 per deduplicated group)
+  return 2ull * p.pb[o * p.bag_total] + (unsigned long long)o * p.feature_count +
+         p.dd_words[o * p.feature_count];
 }
 
 __global__ void __launch_bounds__(256) route_scatter(RouteLaunch p) {
@@ -257,7 +362,8 @@ __global__ void __launch_bounds__(256) route_scatter(RouteLaunch p) {
   __syncthreads();
   const unsigned n = p.shard_count;
   const unsigned long long B = p.bag_total;
-  // leading zero of every (shard, feature) offsets region
+  // leading zero of every (shard, feature) offsets region, and the offsets
+  // [0, U] heading a deduplicated group's unique keys
   {
     const unsigned long long t = blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x;
     if (t < (unsigned long long)n * fc) {
@@ -265,6 +371,13 @@ __global__ void __launch_bounds__(256) route_scatter(RouteLaunch p) {
       const unsigned long long keys_end = p.pk[(o + 1ull) * B] + extra_of(p, o);
       const unsigned long long at = keys_end + (p.pb[o * B + s_base[f]] - p.pb[o * B]) + f;
       p.payload[at] = 0ull;
+      const unsigned U = p.dd_used[t];
+      if (U) {
+        const unsigned long long kept_o = p.pb[(o + 1ull) * B] - p.pb[o * B];
+        const unsigned long long u_at = keys_end + 2 * kept_o + fc + (p.dd_words[t] - p.dd_words[o * fc]);
+        p.payload[u_at] = 0ull;
+        p.payload[u_at + 1] = U;
+      }
     }
   }
   const unsigned lane = threadIdx.x & 31;
@@ -272,11 +385,12 @@ __global__ void __launch_bounds__(256) route_scatter(RouteLaunch p) {
   const unsigned long long nwarps = (gridDim.x * (unsigned long long)blockDim.x) >> 5;
   const unsigned lt = (1u << lane) - 1u;
   // per-lane constants of shard `lane`
-  unsigned long long my_extra = 0, my_keys_end = 0, my_lens_at = 0;
+  unsigned long long my_extra = 0, my_keys_end = 0, my_lens_at = 0, my_uniq_at = 0;
   if (lane < n) {
     my_extra = extra_of(p, lane);
     my_keys_end = p.pk[(lane + 1ull) * B] + my_extra;
     my_lens_at = my_keys_end + (p.pb[(lane + 1ull) * B] - p.pb[lane * B]) + fc;
+    my_uniq_at = my_lens_at + (p.pb[(lane + 1ull) * B] - p.pb[lane * B]);
   }
   for (unsigned long long g = warp; g < B; g += nwarps) {
     const unsigned f = feature_of(s_base, fc, g);
@@ -323,10 +437,19 @@ __global__ void __launch_bounds__(256) route_scatter(RouteLaunch p) {
       const unsigned o_safe = owner < n ? owner : 0u;
       const unsigned base = __shfl_sync(~0u, before, o_safe);
       const unsigned long long ex = __shfl_sync(~0u, my_extra, o_safe);
+      const unsigned long long ua = __shfl_sync(~0u, my_uniq_at, o_safe);
       if (owner < n) {
         const unsigned q = base + rank;    // shard-ordered key index
         p.payload[q + ex] = key;
         p.pos_map[q] = (unsigned)i;
+        const unsigned grp = owner * fc + f;
+        if (p.dd_used[grp]) {
+          // the key's rank among its group's distinct keys, and the key in the
+          // group's unique list (every occurrence writes the same word)
+          const unsigned r = dd_find(p, (key << 10) | grp);
+          p.dd_idx[q] = r;
+          p.payload[ua + (p.dd_words[grp] - p.dd_words[owner * fc]) + 2 + r] = key;
+        }
       }
     }
   }
@@ -363,8 +486,10 @@ __global__ void __launch_bounds__(256) route_merge(RouteLaunch p) {
       const unsigned c = p.cnt[o * B + g];
       routed += c;
       if (!c) continue;
-      const unsigned long long j = p.pb[o * B + g] - p.pb[o * B + s_base[f]];
-      const float* row = p.partials + p.part_off[o * fc + f] + j * D;
+      // a deduplicated group's row is its key's distinct row
+      const unsigned long long j = p.dd_used[o * fc + f] ? p.dd_idx[p.pk[o * B + g]]
+                                                          : p.pb[o * B + g] - p.pb[o * B + s_base[f]];
+      const float* row = p.partials + p.dd_off[o * fc + f] + j * D;
 #pragma unroll
       for (int it = 0; it < ITERS; ++it) {
         const unsigned col = (it * G + gl) * VEC;
@@ -412,7 +537,8 @@ __global__ void __launch_bounds__(256) route_merge(RouteLaunch p) {
     const LookupFeature* F = p.features + f;
     if (F->pooling != 2) continue;
     const unsigned D = F->dim;
-    const float* row = p.partials + p.part_off[o * fc + f] + (q - ob[2 * f]) * (unsigned long long)D;
+    const unsigned long long j = p.dd_used[o * fc + f] ? p.dd_idx[q] : q - ob[2 * f];
+    const float* row = p.partials + p.dd_off[o * fc + f] + j * (unsigned long long)D;
     float* out = p.outs[f] + (unsigned long long)p.pos_map[q] * D;
 #pragma unroll
     for (int it = 0; it < ITERS; ++it) {
@@ -558,13 +684,18 @@ cudaError_t launch_route_count(const RouteLaunch& p, cudaStream_t stream) {
   route_bounds<<<(nb + 255) / 256, 256, 0, stream>>>(p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
+  if (p.dd_mask && p.bag_total) {
+    route_dedup_claim<<<grid_for(p.bag_total, 8), 256, 0, stream>>>(p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
   route_layout<<<1, 1024, 0, stream>>>(p);
   return cudaGetLastError();
 }
 
 unsigned route_count_launches(const RouteLaunch& p) {
   const unsigned tiles = route_tiles(p.cells);
-  return (p.bag_total ? 1u : 0u) + (tiles ? 2u : 0u) + 3u;
+  return (p.bag_total ? 1u : 0u) + (tiles ? 2u : 0u) + 3u + (p.dd_mask && p.bag_total ? 1u : 0u);
 }
 
 cudaError_t launch_route_scatter(const RouteLaunch& p, cudaStream_t stream) {

@@ -167,6 +167,12 @@ struct Route {
   unsigned long long *part_off = nullptr, *row_pre = nullptr;
   float** outs = nullptr;
   const float** grads = nullptr;
+  // distinct rows of one-key groups (see RouteLaunch::dd_*)
+  unsigned long long* dd_keys = nullptr;
+  unsigned* dd_rank = nullptr;
+  unsigned long long dd_mask = 0;
+  unsigned *dd_count = nullptr, *dd_used = nullptr, *dd_idx = nullptr;
+  unsigned long long *dd_off = nullptr, *dd_words = nullptr;
 };
 
 // Slab carve-out helper.
@@ -720,9 +726,12 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         const auto& o = outputs[i];
         Require(o.feature == f.feature && o.rows == rows && o.columns == t.def.dimension,
                 "output buffer layout mismatch");
-        Require(!rows || o.data, "null output buffer");
+        // a null buffer in a lookup that will be pushed makes that feature
+        // push-only (its occurrences are listed, nothing is gathered)
+        Require(!rows || o.data || !read_only, "null output buffer");
         Require(o.device < 0 || o.device == s.opt.device, "output device mismatch");
-        if (o.device < 0) { any_host_out = true; host_out_values += rows * t.def.dimension; }
+        if (!o.data) {
+        } else if (o.device < 0) { any_host_out = true; host_out_values += rows * t.def.dimension; }
         else {
           out16 &= (reinterpret_cast<uintptr_t>(o.data) & 15) == 0;
           out8 &= (reinterpret_cast<uintptr_t>(o.data) & 7) == 0;
@@ -852,7 +861,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
           koff += f.key_count;
           ooff += f.offset_count;
         }
-        if (!gather) {
+        if (!gather || !outputs[i].data) {
           L.out = nullptr;
         } else if (outputs[i].device < 0) {
           L.out = reinterpret_cast<float*>(P(at_hostout)) + hoff;
@@ -875,12 +884,13 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         L.padding_key = f.padding_key;
         L.hash = tab.hashed ? tab.dindex : nullptr;
         L.slots = tab.hashed ? reinterpret_cast<unsigned*>(P(at_slots)) + occ_base : nullptr;
-        L.unit_bags = feature_unit_bags(f.pooling, f.key_count, L.bag_count);
+        L.unit_bags = feature_unit_bags(f.pooling, f.key_count, L.bag_count, (unsigned)group);
         L.unit_base = unit_base;
-        L.units = feature_units(f.pooling, f.key_count, L.bag_count, L.unit_bags);
+        L.units = L.out ? feature_units(f.pooling, f.key_count, L.bag_count, L.unit_bags) : 0;
         unit_base += L.units;
         L.emit_base = emit_base;
-        L.emit_units = feature_units(f.pooling, f.key_count, L.bag_count, kUnitBags);
+        L.emit_units = feature_units(f.pooling, f.key_count, L.bag_count,
+                                     emit_unit_bags(L.unit_bags));
         emit_base += L.emit_units;
         bag_base += L.bag_count;
         occ_base += f.key_count;
@@ -941,7 +951,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
       // sort, which runs on the side stream
       hoff = 0;
       for (uint64_t i = 0; gather && i < count; ++i) {
-        if (outputs[i].device >= 0) continue;
+        if (outputs[i].device >= 0 || !outputs[i].data) continue;
         const unsigned long long n = outputs[i].rows * outputs[i].columns;
         if (n)
           Cuda(cudaMemcpyAsync(outputs[i].data, reinterpret_cast<float*>(P(at_hostout)) + hoff,
@@ -1116,16 +1126,20 @@ int eps_b200_lookup_noalloc(EpsB200Store* store, const EpsB200Feature* features,
       L.feature_index = (unsigned)i;
       L.has_padding = f.has_padding ? 1u : 0u;
       L.padding_key = f.padding_key;
-      L.unit_bags = feature_unit_bags(f.pooling, f.key_count, L.bag_count);
-      L.unit_base = unit_base;
-      L.units = feature_units(f.pooling, f.key_count, L.bag_count, L.unit_bags);
-      unit_base += L.units;
       bag_base += L.bag_count;
     }
-    // launch shape as in the regular lookup (no heap use here)
+    // launch shape as in the regular lookup (no heap use here), then the work
+    // units, whose size for short bags follows the shape's group
     Shape sh;
     Require(choose_shape(dmax, all4, out16, &sh),
             "embedding dimension/alignment not supported by this build", EPS_B200_CAPACITY_EXCEEDED);
+    for (uint64_t i = 0; i < count; ++i) {
+      LookupFeature& L = desc[i];
+      L.unit_bags = feature_unit_bags(L.pooling, L.key_count, L.bag_count, (unsigned)sh.group);
+      L.unit_base = unit_base;
+      L.units = feature_units(L.pooling, L.key_count, L.bag_count, L.unit_bags);
+      unit_base += L.units;
+    }
     (void)all2;
     (void)out8;
     LookupFeature* table = nullptr;
@@ -1453,13 +1467,29 @@ int eps_b200_ticket_coalesced(EpsB200Store* store, uint64_t ticket, uint32_t* ta
     Require(keys && row_offsets && features && sources && scales, "null coalesced outputs");
     Require(row_capacity >= rows && reference_capacity >= refs, "coalesced output capacity too small",
             EPS_B200_CAPACITY_EXCEEDED);
+    // a row's key: slot * shards + shard in a dense table; in a hashed table the
+    // key its slot was created for (the index's slot -> key array, read once)
+    std::vector<std::vector<unsigned long long>> slot_keys(t.table_ids.size());
+    auto key_of = [&](unsigned long long rank, unsigned long long slot) {
+      const Table& tab = s.Get(t.table_ids[rank]);
+      if (!tab.hashed) return slot * s.opt.shard_count + s.opt.shard_id;
+      auto& v = slot_keys[rank];
+      if (v.empty()) {
+        unsigned long long used = 0;
+        Cuda(cudaMemcpy(&used, tab.index.used, 8, cudaMemcpyDeviceToHost));
+        v.resize(std::max(1ull, std::min(used, tab.rows)));
+        Cuda(cudaMemcpy(v.data(), tab.index.slot_keys, v.size() * 8, cudaMemcpyDeviceToHost));
+      }
+      Require(slot < v.size(), "corrupt occurrence list", EPS_B200_RUN_FAILED);
+      return v[slot];
+    };
     unsigned long long r = 0, q = 0;
     row_offsets[0] = 0;
     for (unsigned u = 0; u < seg_total; ++u) {
       const unsigned long long rank = ck[seg[u]] >> t.slot_bits;
       if (rank >= t.table_ids.size()) continue;
       tables[r] = t.table_ids[rank];
-      keys[r] = (ck[seg[u]] & slot_mask) * s.opt.shard_count + s.opt.shard_id;
+      keys[r] = key_of(rank, ck[seg[u]] & slot_mask);
       for (unsigned i = seg[u]; i < seg[u + 1]; ++i, ++q) {
         const unsigned f = src[i] >> kRowBits, row = src[i] & ((1u << kRowBits) - 1u);
         Require(f < t.feature_ids.size() && row < t.grad_rows[f], "corrupt occurrence list",
@@ -1717,6 +1747,14 @@ RouteLaunch RouteParams(const Route& r) {
   lp.part_off = r.part_off;
   lp.row_pre = r.row_pre;
   lp.row_total_dev = r.row_total;
+  lp.dd_keys = r.dd_keys;
+  lp.dd_rank = r.dd_rank;
+  lp.dd_mask = r.dd_mask;
+  lp.dd_count = r.dd_count;
+  lp.dd_used = r.dd_used;
+  lp.dd_off = r.dd_off;
+  lp.dd_words = r.dd_words;
+  lp.dd_idx = r.dd_idx;
   lp.has_sequence = r.has_sequence;
   return lp;
 }
@@ -1795,6 +1833,17 @@ int eps_b200_route(EpsB200Store* store, const EpsB200Feature* features, uint64_t
     const size_t at_rpre = c.take<unsigned long long>((size_t)r.n * r.F + 1);   // + row total
     const size_t at_outs = c.take<float*>(count);
     const size_t at_grads = c.take<float*>(count);
+    // the distinct-key set: a power of two of at least 2N entries (half full at most)
+    unsigned long long dd_cap = 0;
+    if (r.N) { dd_cap = 2; while (dd_cap < 2 * r.N) dd_cap <<= 1; }
+    const size_t groups = (size_t)r.n * r.F;
+    const size_t at_ddk = c.take<unsigned long long>(dd_cap);
+    const size_t at_ddr = c.take<unsigned>(dd_cap);
+    const size_t at_ddc = c.take<unsigned>(groups);
+    const size_t at_ddu = c.take<unsigned>(groups);
+    const size_t at_ddo = c.take<unsigned long long>(groups);
+    const size_t at_ddw = c.take<unsigned long long>(groups + 1);
+    const size_t at_ddi = c.take<unsigned>(r.N);
     cudaStream_t stream = s.RouteStream(stream_arg);
     Cuda(cudaMallocAsync(reinterpret_cast<void**>(&r.slab), std::max<size_t>(c.offset, 256), stream));
     try {
@@ -1814,7 +1863,17 @@ int eps_b200_route(EpsB200Store* store, const EpsB200Feature* features, uint64_t
       r.row_total = r.row_pre + (size_t)r.n * r.F;
       r.outs = reinterpret_cast<float**>(P(at_outs));
       r.grads = reinterpret_cast<const float**>(P(at_grads));
+      r.dd_keys = reinterpret_cast<unsigned long long*>(P(at_ddk));
+      r.dd_rank = reinterpret_cast<unsigned*>(P(at_ddr));
+      r.dd_mask = dd_cap ? dd_cap - 1 : 0;
+      r.dd_count = reinterpret_cast<unsigned*>(P(at_ddc));
+      r.dd_used = reinterpret_cast<unsigned*>(P(at_ddu));
+      r.dd_off = reinterpret_cast<unsigned long long*>(P(at_ddo));
+      r.dd_words = reinterpret_cast<unsigned long long*>(P(at_ddw));
+      r.dd_idx = reinterpret_cast<unsigned*>(P(at_ddi));
       Cuda(cudaMemsetAsync(r.error, 0, sizeof(unsigned), stream));
+      if (dd_cap) Cuda(cudaMemsetAsync(r.dd_keys, 0xFF, dd_cap * 8, stream));
+      Cuda(cudaMemsetAsync(r.dd_count, 0, groups * 4, stream));
       s.Stage(r.desc, desc.data(), count * sizeof(LookupFeature), stream);
       RouteLaunch lp = RouteParams(r);
       lp.tile_k = r.tile_k;
@@ -1935,14 +1994,20 @@ int eps_b200_route_release(EpsB200Store* store, uint64_t route, EpsB200Status* s
 
 namespace {
 // Owner-side layout of a sharded round: requester r's payload region and the
-// (requester, feature) row blocks of the partial / gradient buffers.
+// (requester, feature) row blocks of the partial / gradient buffers.  Peer
+// counts are [requester][feature][keys, kept bags, distinct keys]; a group with
+// distinct keys U > 0 is deduplicated: its payload ends with [0, U, U keys] and
+// its partial block holds U rows (its gradient block, as any other, one row per
+// kept bag or key).
 struct ServeLayout {
   std::vector<EpsB200Feature> feats;
-  std::vector<EpsB200Buffer> blocks;     // rows x dim views (data = byte offset until bound)
+  std::vector<EpsB200Buffer> blocks;     // rows x dim views
+  std::vector<EpsB200Feature> uniq;      // deduplicated groups: their distinct keys
+  std::vector<EpsB200Buffer> uniq_blocks;
 };
 ServeLayout MakeServeLayout(EpsB200Store& s, const uint64_t* payload, const uint64_t* peer_counts,
                             const uint32_t* tables, const uint32_t* poolings, uint32_t n,
-                            uint32_t F, const float* rows_base) {
+                            uint32_t F, const float* rows_base, bool partials) {
   Require(peer_counts && tables && poolings && n >= 1 && n <= 32 && F >= 1 &&
           (uint64_t)n * F <= kMaxFeatures, "invalid sharded round layout");
   std::vector<unsigned> dims(F);
@@ -1958,12 +2023,16 @@ ServeLayout MakeServeLayout(EpsB200Store& s, const uint64_t* payload, const uint
   L.blocks.resize((size_t)n * F);
   unsigned long long base = 0, floats = 0;
   for (uint32_t r = 0; r < n; ++r) {
-    const uint64_t* c = peer_counts + (size_t)r * F * 2;
-    unsigned long long NK = 0, KB = 0;
-    for (uint32_t f = 0; f < F; ++f) { NK += c[2 * f]; KB += c[2 * f + 1]; }
-    unsigned long long ko = 0, oo = 0, lo = 0;
+    const uint64_t* c = peer_counts + (size_t)r * F * 3;
+    unsigned long long NK = 0, KB = 0, UW = 0;
     for (uint32_t f = 0; f < F; ++f) {
-      const unsigned long long nk = c[2 * f], kb = c[2 * f + 1];
+      NK += c[3 * f]; KB += c[3 * f + 1];
+      UW += c[3 * f + 2] ? c[3 * f + 2] + 2 : 0;
+    }
+    unsigned long long ko = 0, oo = 0, lo = 0, uo = 0;
+    for (uint32_t f = 0; f < F; ++f) {
+      const unsigned long long nk = c[3 * f], kb = c[3 * f + 1], U = c[3 * f + 2];
+      Require(U <= nk, "invalid sharded round layout");
       EpsB200Feature& x = L.feats[(size_t)r * F + f];
       x.table = tables[f];
       x.feature = r * F + f;
@@ -1977,6 +2046,7 @@ ServeLayout MakeServeLayout(EpsB200Store& s, const uint64_t* payload, const uint
       x.valid_lengths = payload + base + NK + KB + F + lo;
       ko += nk; oo += kb + 1; lo += kb;
       const unsigned long long rows = poolings[f] == 2 ? nk : kb;
+      const unsigned long long block_rows = partials && U ? U : rows;
       EpsB200Buffer& b = L.blocks[(size_t)r * F + f];
       b.feature = r * F + f;
       b.reserved = 0;
@@ -1985,9 +2055,27 @@ ServeLayout MakeServeLayout(EpsB200Store& s, const uint64_t* payload, const uint
       b.data = const_cast<float*>(rows_base) + floats;
       b.device = s.opt.device;
       b.reserved2 = 0;
-      floats += rows * dims[f];
+      if (partials && U) {
+        // the group's distinct rows: a sequence feature over its unique keys,
+        // gathered into the partial block; the per-bag feature gathers nothing
+        EpsB200Feature u{};
+        u.table = tables[f];
+        u.feature = r * F + f;
+        u.pooling = 2;
+        u.keys = payload + base + NK + 2 * KB + F + uo + 2;
+        u.key_count = U;
+        u.offsets = payload + base + NK + 2 * KB + F + uo;
+        u.offset_count = 2;
+        L.uniq.push_back(u);
+        EpsB200Buffer ub = b;
+        ub.rows = U;
+        L.uniq_blocks.push_back(ub);
+        b.data = nullptr;
+        uo += U + 2;
+      }
+      floats += block_rows * dims[f];
     }
-    base += NK + 2 * KB + F;
+    base += NK + 2 * KB + F + UW;
   }
   return L;
 }
@@ -2001,11 +2089,34 @@ int eps_b200_serve(EpsB200Store* store, const uint64_t* payload, const uint64_t*
     auto& s = *Checked(store);
     Require(payload != nullptr && partials != nullptr, "null sharded round buffer");
     ServeLayout L = MakeServeLayout(s, payload, peer_counts, tables, poolings, requesters,
-                                    feature_count, partials);
+                                    feature_count, partials, true);
     EpsB200Status inner;
-    const int rc = eps_b200_lookup(store, L.feats.data(), L.feats.size(), 1, read_only, 1,
-                                   L.blocks.data(), stream, ticket, &inner);
-    if (rc) throw Failure(rc, inner.message);
+    if (!read_only) {
+      // every occurrence joins the ticket (the push sums them in order)
+      const int rc = eps_b200_lookup(store, L.feats.data(), L.feats.size(), 1, 0, 1,
+                                     L.blocks.data(), stream, ticket, &inner);
+      if (rc) throw Failure(rc, inner.message);
+    } else {
+      // a read-only round gathers only the groups that are not deduplicated
+      std::vector<EpsB200Feature> fs;
+      std::vector<EpsB200Buffer> bs;
+      for (size_t i = 0; i < L.feats.size(); ++i)
+        if (L.blocks[i].data) { fs.push_back(L.feats[i]); bs.push_back(L.blocks[i]); }
+      if (!fs.empty()) {
+        const int rc = eps_b200_lookup(store, fs.data(), fs.size(), 1, 1, 1, bs.data(), stream,
+                                       ticket, &inner);
+        if (rc) throw Failure(rc, inner.message);
+      }
+    }
+    if (!L.uniq.empty()) {
+      uint64_t none = 0;
+      const int rc = eps_b200_lookup(store, L.uniq.data(), L.uniq.size(), 1, 1, 1,
+                                     L.uniq_blocks.data(), stream, &none, &inner);
+      if (rc) {
+        if (!read_only) { EpsB200Status st; eps_b200_release(store, *ticket, &st); }
+        throw Failure(rc, inner.message);
+      }
+    }
   });
 }
 
@@ -2018,7 +2129,7 @@ int eps_b200_serve_push(EpsB200Store* store, uint64_t ticket, const float* gradi
     Require(gradients != nullptr, "null sharded round buffer");
     static const uint64_t kNoPayload = 0;
     ServeLayout L = MakeServeLayout(s, &kNoPayload, peer_counts, tables, poolings, requesters,
-                                    feature_count, gradients);
+                                    feature_count, gradients, false);
     EpsB200Status inner;
     const int rc = PushEntry(store, ticket, L.blocks.data(), L.blocks.size(), stream, wait,
                              reject, &inner);

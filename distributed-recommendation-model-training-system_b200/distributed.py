@@ -7,13 +7,17 @@ the shard that owns keys k with k % n == rank:
 
   lookup  1. route      keys bucketed by owner on the device (eps_b200_route:
                         PrepareLookupInputs, src/access/prepared_lookup.cpp:47-83)
-          2. counts     all-to-all of (keys, kept bags) per (owner, feature)
-          3. payload    all-to-all of keys / bag offsets / valid lengths
+          2. counts     all-to-all of (keys, kept bags, distinct keys) per
+                        (owner, feature)
+          3. payload    all-to-all of keys / bag offsets / valid lengths, and the
+                        distinct keys of deduplicated groups
           4. shard      one eps_b200_lookup(shard_partial=1) per rank over the
                         features of ALL requesters (requester-major), which is
                         the reference shard's Lookup of that combined request
-          5. partials   all-to-all back; eps_b200_route_merge adds them in shard
-                        order and divides mean bags (distributed_client.cpp:173-188,227-232)
+          5. partials   all-to-all back (a deduplicated group -- one key per kept
+                        bag, dense table -- returns each distinct row once);
+                        eps_b200_route_merge adds them in shard order and divides
+                        mean bags (distributed_client.cpp:173-188,227-232)
   push    6. gather     eps_b200_route_gather: the gradient rows each owner needs
                         (distributed_client.cpp:252-265)
           7. gradients  all-to-all; each owner runs ONE eps_b200_push over all
@@ -49,14 +53,16 @@ class RoundHandle:
     """State of one sharded lookup until its push (DistributedBatch)."""
     route: int | None
     ticket: int | None
-    counts: np.ndarray        # [owner, feature, (keys, kept)] of this rank's batch
-    peer_counts: np.ndarray   # [requester, feature, (keys, kept)] received by this shard
+    counts: np.ndarray        # [owner, feature, (keys, kept, distinct)] of this rank's batch
+    peer_counts: np.ndarray   # [requester, feature, (keys, kept, distinct)] received here
     dims: list
     poolings: list
     read_only: bool
     tables: list
     send_f: np.ndarray = None   # floats of partials sent to each requester
     recv_f: np.ndarray = None   # floats of partials received from each owner
+    gsend_f: np.ndarray = None  # floats of gradients sent to each owner
+    grecv_f: np.ndarray = None  # floats of gradients received from each requester
     mrow: np.ndarray = None
     prow: np.ndarray = None
 
@@ -105,16 +111,27 @@ def _input_message(bits: int) -> str:
 
 
 def payload_layout(counts_row: np.ndarray):
-    """Word offsets of one shard's payload: (keys_at[f], offsets_at[f], lengths_at[f], total)."""
+    """Word offsets of one shard's payload: (keys_at[f], offsets_at[f],
+    lengths_at[f], uniq_at[f], total).  counts_row[f] = (keys, kept bags,
+    distinct keys); a deduplicated group (distinct > 0) ends the payload with
+    [0, U, U distinct keys] at uniq_at[f]."""
     nk = counts_row[:, 0].astype(np.int64)
     kb = counts_row[:, 1].astype(np.int64)
+    uw = np.where(counts_row[:, 2] > 0, counts_row[:, 2].astype(np.int64) + 2, 0)
     F = len(nk)
     keys_at = np.concatenate([[0], np.cumsum(nk)[:-1]]) if F else np.zeros(0, np.int64)
     NK = int(nk.sum())
     off_at = NK + np.concatenate([[0], np.cumsum(kb + 1)[:-1]])
     KB = int(kb.sum())
     len_at = NK + KB + F + np.concatenate([[0], np.cumsum(kb)[:-1]])
-    return keys_at, off_at, len_at, NK + 2 * KB + F
+    uniq_at = NK + 2 * KB + F + np.concatenate([[0], np.cumsum(uw)[:-1]])
+    return keys_at, off_at, len_at, uniq_at, NK + 2 * KB + F + int(uw.sum())
+
+
+def _words(counts: np.ndarray) -> np.ndarray:
+    """Payload words per owner (or requester) of counts [n, F, (keys, kept, distinct)]."""
+    uw = np.where(counts[:, :, 2] > 0, counts[:, :, 2] + 2, 0)
+    return (counts[:, :, 0] + 2 * counts[:, :, 1] + 1 + uw).sum(axis=1)
 
 
 class ShardedClient:
@@ -176,7 +193,7 @@ class ShardedClient:
         tables = [int(f.table) for f in feats]
         with self._on(side):
             # ---- 1./2. partition (asynchronous) and the count rows, one per peer
-            width = 4 * F + 1
+            width = 5 * F + 1
             send_t = torch.empty((n, width), dtype=torch.int64, device=self.device)
             err, route = None, None
             try:
@@ -186,7 +203,7 @@ class ShardedClient:
                 host = np.zeros((n, width), np.int64)
                 host[:, 2 * F:3 * F] = tables
                 host[:, 3 * F:4 * F] = pools
-                host[:, 4 * F] = -1
+                host[:, 5 * F] = -1
                 send_t.copy_(torch.from_numpy(host))
             recv_t = torch.empty_like(send_t)
             self._a2a(recv_t, send_t, comm=self.input_dist)
@@ -194,8 +211,8 @@ class ShardedClient:
             mine, recv = both[0], both[1]
             schema = np.array(tables + pools, np.int64)
             bad_schema = bool((recv[:, 2 * F:4 * F] != schema[None, :]).any())
-            own_bits = int(mine[0, 4 * F])
-            if err is not None or own_bits or recv[:, 4 * F].any() or bad_schema:
+            own_bits = int(mine[0, 5 * F])
+            if err is not None or own_bits or recv[:, 5 * F].any() or bad_schema:
                 if route is not None:
                     self.store.route_release(route)
                 if err is not None:
@@ -204,11 +221,14 @@ class ShardedClient:
                     raise EpsError(INVALID_ARGUMENT, _input_message(own_bits))
                 raise EpsError(INVALID_ARGUMENT, "a peer rank rejected its lookup inputs"
                                if not bad_schema else "ranks disagree on the feature schema")
-            counts = mine[:, :2 * F].reshape(n, F, 2)   # [owner, f, (keys, kept)]
-            peer = recv[:, :2 * F].reshape(n, F, 2)     # [requester, f, (keys, kept)]
-            # ---- 3. payload: keys / offsets / valid lengths per owner
-            send_words = (counts[:, :, 0] + 2 * counts[:, :, 1] + 1).sum(axis=1)
-            recv_words = (peer[:, :, 0] + 2 * peer[:, :, 1] + 1).sum(axis=1)
+            # [owner, f, (keys, kept, distinct)] / [requester, f, (...)]
+            counts = np.concatenate([mine[:, :2 * F].reshape(n, F, 2),
+                                     mine[:, 4 * F:5 * F].reshape(n, F, 1)], axis=2)
+            peer = np.concatenate([recv[:, :2 * F].reshape(n, F, 2),
+                                   recv[:, 4 * F:5 * F].reshape(n, F, 1)], axis=2)
+            # ---- 3. payload: keys / offsets / valid lengths (/ distinct keys) per owner
+            send_words = _words(counts)
+            recv_words = _words(peer)
             payload = torch.empty(int(send_words.sum()), dtype=torch.int64, device=self.device)
             self.store.route_scatter(route, payload, side)
             rpay = torch.empty(int(recv_words.sum()), dtype=torch.int64, device=self.device)
@@ -235,8 +255,11 @@ class ShardedClient:
         seq = np.array([p == SEQUENCE for p in pools])
         prow = np.where(seq[None, :], prep.peer[:, :, 0], prep.peer[:, :, 1]).astype(np.int64)
         mrow = np.where(seq[None, :], prep.counts[:, :, 0], prep.counts[:, :, 1]).astype(np.int64)
-        send_f = (prow * dims[None, :]).sum(axis=1)
-        recv_f = (mrow * dims[None, :]).sum(axis=1)
+        # partial rows: a deduplicated group returns its distinct rows
+        pprow = np.where(prep.peer[:, :, 2] > 0, prep.peer[:, :, 2], prow).astype(np.int64)
+        pmrow = np.where(prep.counts[:, :, 2] > 0, prep.counts[:, :, 2], mrow).astype(np.int64)
+        send_f = (pprow * dims[None, :]).sum(axis=1)
+        recv_f = (pmrow * dims[None, :]).sum(axis=1)
         # ---- 4. this shard's lookup over every requester's part (C++ layout)
         part_send = torch.empty(max(1, int(send_f.sum())), dtype=torch.float32, device=self.device)
         ticket = self.store.serve(prep.payload, prep.peer, prep.tables, pools, part_send,
@@ -250,7 +273,9 @@ class ShardedClient:
                        for r, d in zip(prep.output_rows, dims)]
         self.store.route_merge(prep.route, part_recv, outputs, main)
         handle = RoundHandle(prep.route, ticket, prep.counts, prep.peer, list(dims), pools,
-                             read_only, prep.tables, send_f, recv_f, mrow, prow)
+                             read_only, prep.tables, send_f, recv_f,
+                             (mrow * dims[None, :]).sum(axis=1), (prow * dims[None, :]).sum(axis=1),
+                             mrow, prow)
         prep.route = None
         if read_only:
             self.store.route_release(handle.route)
@@ -278,8 +303,8 @@ class ShardedClient:
             raise EpsError(INVALID_ARGUMENT, "read-only lookups cannot be pushed")
         torch = self.torch
         main = self._stream()
-        # gradient rows go out in the layout the partials came back in
-        send_f, recv_f = handle.recv_f, handle.send_f
+        # one gradient row per kept bag (or key) of every (shard, feature) block
+        send_f, recv_f = handle.gsend_f, handle.grecv_f
         send = torch.empty(max(1, int(send_f.sum())), dtype=torch.float32, device=self.device)
         flag = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.store.route_gather(handle.route, gradients, send, flag, main)

@@ -190,7 +190,9 @@ EPS_B200_EXPORT int eps_b200_create_table(EpsB200Store* store, const EpsB200Tabl
  * call that reports them directly.  outputs == NULL (read_only == 0 only) is a
  * push-only lookup: the ticket's occurrence list and coalescing sort are built,
  * nothing is gathered -- for a caller that pushes gradients of rows it already
- * holds (the Lookup + Push of a push-heavy round, whose Push alone is timed). */
+ * holds (the Lookup + Push of a push-heavy round, whose Push alone is timed).
+ * Likewise, with read_only == 0, a single output whose data is NULL makes that
+ * feature push-only (its layout fields are still checked). */
 EPS_B200_EXPORT int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_t count,
                     int32_t input_on_device, int32_t read_only, int32_t shard_partial,
                     EpsB200Buffer* outputs, void* stream, uint64_t* ticket,
@@ -295,12 +297,18 @@ EPS_B200_EXPORT int eps_b200_profile(EpsB200Store* store, int32_t mode, double* 
  * original (global) bag lengths as valid lengths, so the shard's
  * eps_b200_lookup(shard_partial = 1) returns the reference's shard contribution
  * for exactly those bags (bags without keys there contribute zeros).
- * Asynchronous: `counts` (device, int64 [shard_count][4 * count + 1]) receives,
+ * Asynchronous: `counts` (device, int64 [shard_count][5 * count + 1]) receives,
  * for every shard o, the row sent to o before the payload: (keys, kept bags)
- * of every feature, then the features' table ids, then their poolings, then the
- * input-error bits (nonzero: offsets not monotone from 0 to key_count, a valid
- * length that differs from the offset difference, or a key >= the table's
- * key_space).  The inputs must stay valid until eps_b200_route_release. */
+ * of every feature, then the features' table ids, then their poolings, then
+ * their distinct keys U, then the input-error bits (nonzero: offsets not
+ * monotone from 0 to key_count, a valid length that differs from the offset
+ * difference, or a key >= the table's key_space).  U > 0 marks a deduplicated
+ * group: feature f of a dense table whose kept bags on o hold one key each (or
+ * a sequence feature), with U distinct keys among its keys (U < keys).  Its
+ * owner returns each distinct row once (U partial rows) and the merge reads a
+ * bag's row by its key's rank; the values and their order of addition are
+ * those of the per-bag partials.  Gradients are not deduplicated.  The inputs
+ * must stay valid until eps_b200_route_release. */
 EPS_B200_EXPORT int eps_b200_route(EpsB200Store* store, const EpsB200Feature* features, uint64_t count,
                                    uint32_t shard_count, void* stream, uint64_t* route,
                                    int64_t* counts, EpsB200Status* status);
@@ -308,14 +316,15 @@ EPS_B200_EXPORT int eps_b200_route(EpsB200Store* store, const EpsB200Feature* fe
  * reference's DistributedClient sends in each shard's LookupRequest,
  * src/client/distributed_client.cpp:96-104): for shard o, the keys of every
  * feature, then every feature's kept-bag offsets (kept + 1 words), then every
- * feature's kept-bag valid lengths.  Shard o's part has
- * sum_f (keys + 2 * kept + 1) words. */
+ * feature's kept-bag valid lengths, then for every deduplicated feature
+ * [0, U, its U distinct keys] (the offsets and keys of one sequence bag).
+ * Shard o's part has sum_f (keys + 2 * kept + 1 + (U ? U + 2 : 0)) words. */
 EPS_B200_EXPORT int eps_b200_route_scatter(EpsB200Store* store, uint64_t route, uint64_t* payload,
                                            void* stream, EpsB200Status* status);
 /* Client merge (src/client/distributed_client.cpp:173-188,227-232): partials holds the
  * shard contributions received from every shard, shard after shard, each
- * feature after feature as [kept bags, dim] (sum/mean) or [keys, dim]
- * (sequence); outputs[i] ([bags, dim] or [keys, dim], device) receives the
+ * feature after feature as [kept bags, dim] (sum/mean), [keys, dim]
+ * (sequence) or [U, dim] (deduplicated: the distinct rows); outputs[i] ([bags, dim] or [keys, dim], device) receives the
  * zero-initialised shard-ordered sum, mean bags divided by (float)length, and
  * sequence rows at their positions. */
 EPS_B200_EXPORT int eps_b200_route_merge(EpsB200Store* store, uint64_t route, const float* partials,
@@ -324,7 +333,8 @@ EPS_B200_EXPORT int eps_b200_route_merge(EpsB200Store* store, uint64_t route, co
 /* Push split (src/client/distributed_client.cpp:252-265): gathers into `send`
  * (device, the layout of route_merge's partials) the gradient rows each shard
  * needs: the kept bags' rows of pooled features, the keys' rows of sequence
- * features.  If `nonfinite` (device u32, may be NULL) is given, 1 is stored
+ * features (deduplicated groups too), shard after shard, feature after feature.
+ * If `nonfinite` (device u32, may be NULL) is given, 1 is stored
  * there when any value of any gradient tensor is not finite (the client check
  * of src/client/distributed_client.cpp:249); the caller zeroes it. */
 EPS_B200_EXPORT int eps_b200_route_gather(EpsB200Store* store, uint64_t route,
@@ -333,13 +343,15 @@ EPS_B200_EXPORT int eps_b200_route_gather(EpsB200Store* store, uint64_t route,
 /* Owner side of a sharded round: ParameterService::Lookup of the combined
  * request of `requesters` clients (include/eps/parameter_service.hpp:17).
  * payload (device) holds the words every requester's route_scatter sent to this
- * shard, requester after requester; peer_counts (host, [requesters][F][2]) the
- * (keys, kept bags) of each part; tables / poolings (host, [F]) the feature
- * schema shared by all requesters.  Runs eps_b200_lookup(shard_partial = 1) on
- * the requesters' features (ids r * F + f), writing the contributions into
- * `partials` (device), requester after requester, feature after feature, as
- * [kept bags, dim] (sum/mean) or [keys, dim] (sequence).  *ticket as for
- * eps_b200_lookup. */
+ * shard, requester after requester; peer_counts (host, [requesters][F][3]) the
+ * (keys, kept bags, distinct keys U) of each part; tables / poolings (host,
+ * [F]) the feature schema shared by all requesters.  Runs
+ * eps_b200_lookup(shard_partial = 1) on the requesters' features (ids r * F +
+ * f), writing the contributions into `partials` (device), requester after
+ * requester, feature after feature, as [kept bags, dim] (sum/mean), [keys, dim]
+ * (sequence) or, for a deduplicated part (U > 0), [U, dim]: the rows of its
+ * distinct keys, gathered by a read-only lookup while the ticketed lookup only
+ * lists the part's occurrences.  *ticket as for eps_b200_lookup. */
 EPS_B200_EXPORT int eps_b200_serve(EpsB200Store* store, const uint64_t* payload,
                                    const uint64_t* peer_counts, const uint32_t* tables,
                                    const uint32_t* poolings, uint32_t requesters,
@@ -347,7 +359,9 @@ EPS_B200_EXPORT int eps_b200_serve(EpsB200Store* store, const uint64_t* payload,
                                    void* stream, uint64_t* ticket, EpsB200Status* status);
 /* Owner side of the push of a served round (ParameterService::Push,
  * include/eps/parameter_service.hpp:18): gradients (device) hold the rows every
- * requester's route_gather sent, in the layout of eps_b200_serve's partials.
+ * requester's route_gather sent: one row per kept bag (sum/mean) or key
+ * (sequence) of every part, requester after requester, feature after feature;
+ * peer_counts as for eps_b200_serve.
  * If `reject` (device u32, may be NULL) is nonzero when the push runs, the push
  * is rejected on the device as a non-finite input (state unchanged, ticket
  * live); with wait == 0 that outcome is reported by eps_b200_synchronize. */

@@ -28,15 +28,20 @@ TABLES = [TableDef(id=1, dimension=8, learning_rate=0.01, init_min=-0.05, init_m
 SCHEMA = [(1, SUM), (1, MEAN), (2, SEQUENCE), (2, SUM)]
 
 
-def make_batch(rank: int, step: int, bags: int = 9):
-    """Features of one rank (ids 0..F-1) and matching gradients."""
-    rng = np.random.default_rng(1000 * rank + step)
+def make_batch(rank: int, step: int, bags: int = 9, onehot: bool = False):
+    """Features of one rank (ids 0..F-1) and matching gradients.  With
+    `onehot`, the first two features (sum, mean) hold one key per bag over many
+    duplicate keys: the groups the multi-GPU round returns distinct rows for."""
+    rng = np.random.default_rng(1000 * rank + step + (500 if onehot else 0))
     rows = {t.id: t.rows for t in TABLES}
     dims = {t.id: t.dimension for t in TABLES}
     feats, grads = [], []
     for fi, (tid, pool) in enumerate(SCHEMA):
-        lens = rng.integers(0, 6, size=bags)
-        lens[rng.integers(0, bags)] = 0                       # at least one empty bag
+        if onehot and fi < 2:
+            lens = np.ones(4 * bags, np.int64)
+        else:
+            lens = rng.integers(0, 6, size=bags)
+            lens[rng.integers(0, bags)] = 0                   # at least one empty bag
         offs = np.concatenate([[0], np.cumsum(lens)]).astype(np.uint64)
         hot = rng.integers(0, rows[tid], size=3)
         keys = np.where(rng.random(int(offs[-1])) < 0.4,
@@ -90,10 +95,11 @@ class FakeShardStore:
 
     # ---- route: PrepareLookupInputs with the bags that have keys on each shard
     def route(self, feats, n, counts, stream=None):
-        """Writes the count rows [n][4F + 1] into `counts` (tables, poolings,
+        """Writes the count rows [n][5F + 1] into `counts` (tables, poolings,
+        distinct keys -- always 0: this stand-in deduplicates no group --
         input-error bits last) and keeps the partition."""
         F = len(feats)
-        rows = np.zeros((n, 4 * F + 1), np.int64)
+        rows = np.zeros((n, 5 * F + 1), np.int64)
         rows[:, 2 * F:3 * F] = [f.table for f in feats]
         rows[:, 3 * F:4 * F] = [f.pooling for f in feats]
         parts, bits = [], 0
@@ -122,7 +128,7 @@ class FakeShardStore:
                 rows[o, 2 * fi] = len(per[o]["keys"])
                 rows[o, 2 * fi + 1] = len(per[o]["kept"])
             parts.append(per)
-        rows[:, 4 * F] = bits
+        rows[:, 5 * F] = bits
         counts.copy_(__import__("torch").from_numpy(rows))
         rid = self._next
         self._next += 1

@@ -55,10 +55,17 @@ def _inputs(eps, feats, device):
 
 def test_payload_layout():
     D = _client_module()
-    counts = np.array([[3, 2], [0, 0], [4, 1]], np.uint64)
-    keys_at, off_at, len_at, total = D.payload_layout(counts)
+    counts = np.array([[3, 2, 0], [0, 0, 0], [4, 1, 0]], np.uint64)
+    keys_at, off_at, len_at, uniq_at, total = D.payload_layout(counts)
     assert list(keys_at) == [0, 3, 3] and list(off_at) == [7, 10, 11]
     assert list(len_at) == [7 + 3 + 3, 7 + 3 + 3 + 2, 7 + 3 + 3 + 2] and total == 7 + 2 * 3 + 3
+    # a deduplicated group (4 keys in 4 one-key bags, 2 distinct): [0, 2, k, k]
+    # after the lengths region
+    counts = np.array([[3, 2, 0], [4, 4, 2]], np.uint64)
+    keys_at, off_at, len_at, uniq_at, total = D.payload_layout(counts)
+    assert list(keys_at) == [0, 3] and list(off_at) == [7, 10]
+    assert list(len_at) == [7 + 6 + 2, 7 + 6 + 2 + 2] and list(uniq_at) == [21, 21]
+    assert total == 7 + 2 * 6 + 2 + (2 + 2)
 
 
 # ------------------------------------------------------------------ gloo, CPU
@@ -142,10 +149,11 @@ def _check_state(store, oracle, rank, n):
         assert store.optimizer_state(t.id)[0] == oracle.powers(t.id)[2]
 
 
-def _rank_body(eps, D, store, client, rank, n, steps, device, oracle_outputs, oracle_lock):
+def _rank_body(eps, D, store, client, rank, n, steps, device, oracle_outputs, oracle_lock,
+               onehot=False):
     import torch
     for step in range(steps):
-        batches = [H.make_batch(r, step) for r in range(n)]
+        batches = [H.make_batch(r, step, onehot=onehot) for r in range(n)]
         feats, grads = batches[rank]
         handle, outs = client.lookup(_inputs(eps, feats, device))
         with oracle_lock:
@@ -158,7 +166,12 @@ def _rank_body(eps, D, store, client, rank, n, steps, device, oracle_outputs, or
 
 @pytest.mark.gpu
 @pytest.mark.skipif(not gpu_available(), reason="needs a GPU")
-def test_sharded_round_three_ranks_one_gpu():
+@pytest.mark.parametrize("onehot", [False, True])
+def test_sharded_round_three_ranks_one_gpu(onehot):
+    """Three ranks as threads on one GPU against the oracle serving the combined
+    request.  The sequence feature's groups (and, with `onehot`, the one-key sum
+    and mean features') hold duplicate keys, so their owners return distinct
+    rows only; outputs and state must still be bit-exact."""
     import torch
     eps = import_package()
     D = _client_module()
@@ -166,7 +179,7 @@ def test_sharded_round_three_ranks_one_gpu():
     oracle = Oracle(H.TABLES)
     outputs = {}
     for step in range(steps):                     # the combined requests, in order
-        cf, cg = H.concat([H.make_batch(r, step) for r in range(n)])
+        cf, cg = H.concat([H.make_batch(r, step, onehot=onehot) for r in range(n)])
         outputs[step] = oracle.lookup(cf, shards=n)
         assert oracle.push(cf, cg) == 0
     comm = H.ThreadComm(n)
@@ -179,7 +192,7 @@ def test_sharded_round_three_ranks_one_gpu():
             torch.cuda.set_device(0)
             client = D.ShardedClient(stores[rank], device="cuda:0", comm=comm)
             _rank_body(eps, D, stores[rank], client, rank, n, steps, "cuda:0", outputs,
-                       threading.Lock())
+                       threading.Lock(), onehot=onehot)
         except BaseException as e:          # noqa: BLE001 -- reported below
             errors.append((rank, e))
             comm.barrier.abort()

@@ -6,8 +6,11 @@ for every lookup, read-only ones included).
 Checked against the unmodified reference CPU parameter server (oracle/_ref),
 which keeps its rows in a hash map and creates them lazily:
 * lookups + pushes with random 64-bit keys (the all-ones key included): pooled
-  outputs and every touched row's w / m / v / updates bit-exact, on one shard
-  and as the owner of one of three shards (keys of other shards refused);
+  outputs, the coalesced occurrence lists (eps_b200_ticket_coalesced: each key's
+  occurrences, sources and scales in reference order; rows sorted by key, as a
+  hashed table's rows come in slot order) and every touched row's w / m / v /
+  updates bit-exact, on one shard and as the owner of one of three shards (keys
+  of other shards refused);
 * a read-only lookup creates the rows it touches (their initial values);
 * a table that is full refuses new keys with capacity_exceeded, keeping the
   keys it holds;
@@ -20,6 +23,7 @@ import tempfile
 import numpy as np
 import pytest
 
+import round_check as rc
 from oracle_lib import MEAN, SEQUENCE, SUM, Feature, Reference, TableDef, reference_available
 
 pytestmark = [pytest.mark.gpu,
@@ -43,6 +47,19 @@ def key_pool(rng, n, shards=1, shard=0):
         if k % shards == shard:
             keys.add(k)
     return np.array(sorted(keys), dtype=np.uint64)
+
+
+def rows_by_key(got):
+    """A coalesced CSR with its rows reordered by (table, key)."""
+    order = np.lexsort((got["keys"], got["tables"]))
+    ro = got["row_offsets"].astype(np.int64)
+    idx = (np.concatenate([np.arange(ro[i], ro[i + 1]) for i in order]) if len(order)
+           else np.zeros(0, np.int64))
+    out = {"tables": got["tables"][order], "keys": got["keys"][order],
+           "row_offsets": np.concatenate([[0], np.cumsum(np.diff(ro)[order])]).astype(np.uint64)}
+    for k in ("features", "sources", "scales"):
+        out[k] = got[k][idx]
+    return out
 
 
 def features(rng, pool, dim, bags=64):
@@ -79,6 +96,9 @@ def test_hashed_round_against_reference(eps, dim):
         batch, want = ref.lookup(feats)
         for a, b in zip(outs, want):
             assert np.array_equal(bits(a), bits(b)), step
+        got = store.coalesced(ticket)
+        assert len(got["keys"]) == len(np.unique(np.concatenate([f.keys for f in feats])))
+        assert rc.check_coalesced(rows_by_key(got), feats), step
         grads = [rng.normal(0, 0.01, size=o.shape).astype(np.float32) for o in outs]
         store.push(ticket, grads)
         ref.push(batch, feats, grads)

@@ -7,7 +7,9 @@ reference's header (a C consumer compiled against either header reads the same
 offsets); configuration errors are reported with the reference's codes before
 any GPU work; without a GPU, create fails loudly.
 GPU: pull / push through the table bit-exact against the oracle (padding, all
-poolings, weight bounds, host and device buffers), the adapter's batch
+poolings, weight bounds, host and device buffers), a table given as the
+reference writes it (no key_space: any 64-bit key, rows created on first touch)
+bit-exact against the reference CPU parameter server, the adapter's batch
 lifecycle (handles, read-only batches, prepared inputs, live-batch limit,
 retired handles), frozen save -> checkpoint export -> resume, restore of the
 saved file into a fresh runtime, table modes and control commands.
@@ -26,7 +28,8 @@ import numpy as np
 import pytest
 
 from conftest import ROOT, gpu_available
-from oracle_lib import MEAN, SEQUENCE, SUM, Feature, Oracle, TableDef
+from oracle_lib import (MEAN, SEQUENCE, SUM, Feature, Oracle, Reference, TableDef,
+                        reference_available)
 
 HEADER = os.path.join(ROOT, "include", "eps_b200_runtime_c.h")
 REFERENCE_HEADER_DIR = os.path.join(os.environ.get("EPS_REFERENCE", os.path.join(
@@ -474,3 +477,47 @@ def test_read_only_release_and_table_modes(rt, eps):
     r.command("abort")
     with pytest.raises(eps.EpsError):
         r.pull(feats)
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not reference_available(), reason="oracle/_ref not built")
+def test_reference_table_json_takes_any_64bit_key(rt):
+    """A table in the reference's own JSON (no key_space) is a hashed table:
+    random 64-bit keys, the all-ones key among them, rows created on first
+    touch; three pull / push rounds and the final weights equal the reference's
+    CPU parameter server (oracle/_ref) bit for bit."""
+    rng = np.random.default_rng(21)
+    t = TableDef(id=1, dimension=32, learning_rate=0.01, init_min=-0.05, init_max=0.05,
+                 init_seed=42)
+    j = table_json(t)
+    del j["key_space"]
+    j["capacity"] = 4096
+    r = rt.NativeRuntime({"run": "hashed", "device": 0, "state_bytes": 1 << 28, "tables": [j]})
+    ref = Reference([t], shards=1)
+    pool = np.unique(np.concatenate([rng.integers(0, 2**63, size=600, dtype=np.int64)
+                                     .astype(np.uint64) * np.uint64(2),
+                                     np.array([U64_MAX], np.uint64)]))
+    touched = set()
+    for step in range(3):
+        feats = []
+        for fi, pooling in enumerate((SUM, MEAN, SEQUENCE)):
+            lens = rng.integers(0, 7, size=32)
+            offs = np.concatenate([[0], np.cumsum(lens)]).astype(np.uint64)
+            keys = pool[rng.integers(0, len(pool), size=int(offs[-1]))]
+            touched.update(int(k) for k in keys)
+            feats.append(Feature(1, 20 + fi, pooling, keys, offs))
+        b = r.pull(feats)
+        batch, want = ref.lookup(feats)
+        for f, got, w in zip(feats, b.outputs, want):
+            assert np.array_equal(bits(got), bits(w)), (step, f.feature)
+        grads = _grads(b.outputs, 300 + step)
+        r.push(b.handle, [(f.feature, g) for f, g in zip(feats, grads)])
+        ref.push(batch, feats, grads)
+    keys = np.array(sorted(touched), np.uint64)
+    got = r.pull([types.SimpleNamespace(table=1, feature=99, pooling=SEQUENCE, keys=keys,
+                                        offsets=np.array([0, len(keys)], np.uint64))],
+                 read_only=True).outputs[0]
+    rw, _, _, _ = ref.read_many(1, keys)
+    assert np.array_equal(bits(got), bits(rw))
+    ref.close()
+    r.close()
