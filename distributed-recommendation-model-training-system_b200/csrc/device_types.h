@@ -119,13 +119,13 @@ inline unsigned feature_unit_bags(unsigned pooling, unsigned long long key_count
 }
 
 // Bags per emit unit of a pooled feature (one warp per unit, one occurrence per
-// lane and step): kUnitBags for long bags, kEmitShortBags for short ones, so a
-// step of one-key bags still fills the warp.
+// lane and step): kUnitBags for long bags (8 or more keys on average),
+// kEmitShortBags for short ones, so a step of one-key bags still fills the warp.
 #ifdef __CUDACC__
 __host__ __device__
 #endif
-inline unsigned emit_unit_bags(unsigned unit_bags) {
-  return unit_bags == 1u ? kUnitBags : kEmitShortBags;
+inline unsigned emit_unit_bags(unsigned long long key_count, unsigned long long bag_count) {
+  return (bag_count && key_count >= 8ull * bag_count) ? kUnitBags : kEmitShortBags;
 }
 
 // Work units of one feature (see LookupFeature::units); `unit_bags` bags per

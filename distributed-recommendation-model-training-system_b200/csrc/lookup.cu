@@ -425,7 +425,7 @@ __global__ void __launch_bounds__(256) emit_kernel(LookupLaunch p) {
       continue;
     }
     // pooled: bags b0 .. b0 + nb - 1 (ub <= 32 bags per unit, lane k holding bag k)
-    const unsigned ub = emit_unit_bags(F->unit_bags);
+    const unsigned ub = emit_unit_bags(key_count, B);
     const unsigned long long b0 = lu * ub;
     const unsigned nb = (unsigned)min((unsigned long long)ub, B - b0);
     unsigned long long s = 0, e = 0;

@@ -890,7 +890,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         unit_base += L.units;
         L.emit_base = emit_base;
         L.emit_units = feature_units(f.pooling, f.key_count, L.bag_count,
-                                     emit_unit_bags(L.unit_bags));
+                                     emit_unit_bags(f.key_count, L.bag_count));
         emit_base += L.emit_units;
         bag_base += L.bag_count;
         occ_base += f.key_count;
