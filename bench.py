@@ -57,6 +57,10 @@ METRIC = "embedding rows/s per round (pull+push+Adam)"
 UNIT = "rows/s"
 FALLBACK_HBM_GBS = 6650.0
 LONG_RUN = 64
+# pushes the library keeps enqueued before a lookup waits for the oldest: a
+# host hiccup shorter than this many queued rounds (23 ms at cfg2) leaves the
+# GPU busy; each enqueued round keeps its lookup's slab (~50 MB at cfg2)
+ENQUEUED = 64
 
 
 def _load(name, path, package=False):
@@ -92,6 +96,10 @@ def parse():
                     help="largest job (occurrences over all ranks) the parity round checks "
                          "at full batch; larger jobs are checked at a proportionally smaller "
                          "batch per rank of the same config")
+    ap.add_argument("--probe-nvlink", action="store_true",
+                    help="instead of a round: under torchrun, the NCCL all-to-all bandwidth "
+                         "of this job's ranks at 32/128/512 MiB per peer (max over ranks); "
+                         "in one process, a copy-engine copy from GPU 0 to GPU 1; one JSON line")
     ap.add_argument("--no-scale-base", action="store_true",
                     help="at N = 1 with the default config, skip timing the N > 1 default "
                          "config (3) on this GPU")
@@ -296,19 +304,27 @@ def host_threads():
 
 
 class Clocks:
-    """nvidia-smi samples during the timed region."""
+    """nvidia-smi samples during the timed region: SM clocks and throttle
+    reasons of every GPU of the job, by ONE sampler (local rank 0's).  A query
+    can hold up driver calls for tens of milliseconds: one sampler per rank (8
+    queries per period at N = 8) showed as host stalls of 13-60 ms inside timed
+    rounds, and the power reading is left out for the same reason."""
 
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("index,clocks.sm,clocks.max.sm,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, local_rank):
+    def __init__(self, local_rank, local_world=1):
         vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-        self.index = vis.split(",")[local_rank] if vis else str(local_rank)
+        ids = vis.split(",") if vis else [str(i) for i in range(local_world)]
+        self.index = ",".join(ids[:local_world])
+        self.owner = local_rank == 0
         self.proc = None
         self.path = None
 
     def start(self):
+        if not self.owner:
+            return
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
@@ -359,13 +375,13 @@ class Clocks:
         os.unlink(self.path)
         if not rows:
             return None
-        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
-        mx = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({n for r in rows for n, v in zip(names, r[4:8]) if v.lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(rows),
+                "gpus": self.index, "samples": len(rows),
                 "window": "warm-up start to the end of a 0.5 s untimed soak of the same rounds"}
 
 
@@ -633,7 +649,8 @@ def scale_base_rounds(eps, torch, wl, args, dev, local_rank):
     the store's stream): the N = 1 point of the scaling curve that the N > 1
     lines measure."""
     w = workload_for(wl, 3, 0, 1)
-    store = eps.ParameterStore(device=local_rank, state_bytes=170 << 30)
+    store = eps.ParameterStore(device=local_rank, state_bytes=170 << 30,
+                               max_enqueued_pushes=ENQUEUED)
     try:
         _create_tables(eps, store, w, 1)
         stream = torch.cuda.current_stream(dev)
@@ -648,7 +665,7 @@ def scale_base_rounds(eps, torch, wl, args, dev, local_rank):
         flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
         lookup = store.prepare_lookup(feats, outs)
         push = store.prepare_push(grads)
-        for _ in range(20 + args.warmup):
+        for _ in range(ENQUEUED + 4 + args.warmup):
             flush.zero_()
             push(lookup(stream), stream, wait=False)
         store.synchronize()
@@ -692,7 +709,7 @@ def run_b200(args):
     dev = torch.device(f"cuda:{local_rank}")
     # one shard per rank: keys k with k % world == rank (the table's rows are split)
     store = eps.ParameterStore(device=local_rank, shard_id=rank, shard_count=world,
-                               state_bytes=170 << 30)
+                               state_bytes=170 << 30, max_enqueued_pushes=ENQUEUED)
     _create_tables(eps, store, w, world)
     stream = torch.cuda.Stream(device=dev)
     torch.cuda.set_stream(stream)          # flushes and events run on the store's stream
@@ -742,14 +759,14 @@ def run_b200(args):
             push(ticket, stream, wait=False)
 
     # the clock sampler first: its start-up must be over before timed work
-    clocks = Clocks(local_rank)
+    clocks = Clocks(local_rank, int(os.environ.get("LOCAL_WORLD_SIZE", world)))
     clocks.start()
     clocks.wait_first()
     # allocator priming (untimed): more rounds in flight than the library's
-    # limit of enqueued pushes (16), so that the stream-ordered memory pool
-    # reaches its steady size before the warm-up and never grows (maps new
-    # memory, a host stall of milliseconds) inside the timed rounds
-    for _ in range(20):
+    # limit of enqueued pushes, so that the stream-ordered memory pool reaches
+    # its steady size before the warm-up and never grows (maps new memory, a
+    # host stall of milliseconds) inside the timed rounds
+    for _ in range(ENQUEUED + 4):
         one_round()
     store.synchronize()
     clocks.mark()
@@ -759,9 +776,12 @@ def run_b200(args):
     # to the first timed round
     gc.collect()
     gc.disable()
+    warm_host = []
     for _ in range(args.warmup):
         flush.zero_()
+        h0 = time.perf_counter()
         one_round()
+        warm_host.append(time.perf_counter() - h0)
     store.synchronize()
     torch.cuda.synchronize()
     if dist:
@@ -770,10 +790,17 @@ def run_b200(args):
     events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in range(args.steps)]
     torch.cuda.synchronize()
-    # after the synchronize the device queue is empty: three extra L2 flushes
-    # (untimed, ~40 us each) give the host the head start it has in steady
-    # state, so that round 0 does not wait for its own enqueue
-    for _ in range(3):
+    # after the synchronize the device queue is empty: extra L2 flushes (untimed,
+    # ~40 us of device work each, queued before round 0's start event) give the
+    # host the head start it has in steady state, so that round 0 does not wait
+    # for its own enqueue: enough to cover one round's host time (the warm-up's
+    # median), at least 3, at most 150
+    head = int(min(150, max(3, np.ceil(1e3 * float(np.median(warm_host)) / 0.04))))
+    if dist:
+        t = torch.tensor([head], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)      # the same count on every rank
+        head = int(t.item())
+    for _ in range(head):
         flush.zero_()
     host_s = []
     for a, b in events:
@@ -830,7 +857,9 @@ def run_b200(args):
     per_call_ms = prof[dom]["ms"] / calls
     alg = owner[dom]
     achieved = alg / (per_call_ms / 1e3) / 1e9 if alg else 0.0
-    traffic = load_traffic().get(f"cfg{args.config}", {}).get(dom) if world == 1 else None
+    tr = load_traffic().get(f"cfg{args.config}", {}).get(dom) if world == 1 else None
+    traffic = tr.get("bytes") if tr else None
+    traffic_capture = tr.get("capture") if tr else None
     phases = {p: {"ms_per_round": prof[p]["ms"] / max(1, prof[p]["calls"]),
                   "launches_per_round": prof[p]["launches"] / max(1, prof[p]["calls"]),
                   "alg_GBps": (owner[p] / (prof[p]["ms"] / max(1, prof[p]["calls"]) / 1e3) / 1e9)
@@ -1036,12 +1065,14 @@ def run_b200(args):
         f"{world} shards (rows by key % {world}), NCCL all-to-all of keys, partials and "
         f"gradients; one batch per GPU",
         "l2": "flushed (256 MiB write) before every timed round",
+        "head_start_flushes": head,
         "unique_rows_per_s": bm["U"] * args.steps / (total_ms / 1e3),
         "round_hbm_frac": ((bm["push"] if only_push else bm["pull"] + bm["push"]) * args.steps /
                            (total_ms / 1e3) / 1e9) / (peak * world),
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": traffic, "alg_bytes_per_launch": alg,
+                     "traffic": traffic, "traffic_capture": traffic_capture,
+                     "alg_bytes_per_launch": alg,
                      "bytes": "owner-side" if world > 1 else "single GPU"},
         "phases": phases,
         "nvlink": nvlink,
@@ -1063,8 +1094,74 @@ def run_b200(args):
     print(json.dumps(line))
 
 
+def probe_nvlink(args):
+    """NVLink bandwidth available to the round's exchanges.  Under torchrun: the
+    NCCL all-to-all of this job's ranks at 32 / 128 / 512 MiB to every peer
+    (CUDA events, 5 calls after 3, max over ranks).  Without it (one process
+    seeing two or more GPUs): a copy-engine copy of 128 / 512 MiB from GPU 0 to
+    GPU 1 with peer access enabled."""
+    import torch
+    rank, local_rank, world = dist_env()
+
+    def timed(fn, stream, k=5):
+        for _ in range(3):
+            fn()
+        stream.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(k):
+            fn()
+        b.record(stream)
+        stream.synchronize()
+        return a.elapsed_time(b) / k
+
+    if "WORLD_SIZE" not in os.environ:
+        if torch.cuda.device_count() < 2 or not torch.cuda.can_device_access_peer(0, 1):
+            print(json.dumps({"probe": "peer_copy", "unavailable": "needs two GPUs with peer access"}))
+            return
+        ce = {}
+        with torch.cuda.device(0):
+            s0 = torch.cuda.Stream(device=0)
+            for mib in (128, 512):
+                x = torch.empty((mib << 20) // 4, device="cuda:0")
+                y = torch.empty_like(x, device="cuda:1")
+                with torch.cuda.stream(s0):
+                    ms = timed(lambda: y.copy_(x, non_blocking=True), s0)
+                torch.cuda.synchronize(1)
+                ce[mib] = (mib << 20) / (ms / 1e3) / 1e9
+                del x, y
+        print(json.dumps({"probe": "peer_copy", "copy_engine_GBps_by_MiB": ce,
+                          "path": "GPU 0 -> GPU 1, one process, peer access enabled"}))
+        return
+    import datetime
+    import torch.distributed as dist
+    torch.cuda.set_device(local_rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device(f"cuda:{local_rank}"))
+    a2a = {}
+    stream = torch.cuda.current_stream()
+    for mib in (32, 128, 512):
+        per = mib << 20
+        src = torch.empty(world * per // 4, device="cuda")
+        dst = torch.empty_like(src)
+        ms = timed(lambda: dist.all_to_all_single(dst, src), stream)
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        a2a[mib] = per * (world - 1) / (t.item() / 1e3) / 1e9
+        del src, dst
+    dist.barrier()
+    dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps({"probe": "nvlink", "n_gpus": world,
+                          "nccl_env": {k: v for k, v in os.environ.items() if k.startswith("NCCL_")},
+                          "alltoall_GBps_out_by_MiB_per_peer": a2a}))
+
+
 def main():
     args = parse()
+    if args.probe_nvlink:
+        probe_nvlink(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -55,7 +55,8 @@ class Status(C.Structure):
 class Options(C.Structure):
     _fields_ = [("device", C.c_int32), ("shard_id", C.c_uint32), ("shard_count", C.c_uint32),
                 ("max_live_tickets", C.c_uint32), ("partition_epoch", C.c_uint64),
-                ("state_bytes", C.c_uint64), ("flags", C.c_uint32), ("reserved", C.c_uint32)]
+                ("state_bytes", C.c_uint64), ("flags", C.c_uint32),
+                ("max_enqueued_pushes", C.c_uint32)]
 
 
 FLAG_REFERENCE_ORDER = 1
@@ -302,14 +303,14 @@ class ParameterStore:
     def __init__(self, device: int = 0, shard_id: int = 0, shard_count: int = 1,
                  state_bytes: int = 64 << 30, max_live_tickets: int = 1024,
                  partition_epoch: int = 1, reference_order: bool = False,
-                 register_rows: bool = False):
+                 register_rows: bool = False, max_enqueued_pushes: int = 0):
         self.lib = load_library()
         self.device = device
         self.shard_count = shard_count
         self._tables: dict[int, TableDefinition] = {}
         opt = Options(device, shard_id, shard_count, max_live_tickets, partition_epoch, state_bytes,
                       (FLAG_REFERENCE_ORDER if reference_order else 0) |
-                      (FLAG_REGISTER_ROWS if register_rows else 0), 0)
+                      (FLAG_REGISTER_ROWS if register_rows else 0), max_enqueued_pushes)
         st = Status()
         h = C.c_void_p()
         _check(self.lib.eps_b200_create(C.byref(opt), C.byref(h), C.byref(st)), st)

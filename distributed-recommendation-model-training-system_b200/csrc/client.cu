@@ -497,13 +497,13 @@ int eps_b200_client_push(EpsB200Client* c, uint64_t round, const EpsB200Buffer* 
     for (unsigned o = 0; o < n; ++o) { ts += R.gsend_f[o]; tr += R.grecv_f[o]; }
     float* send = DevAlloc<float>(ts, s);
     float* recv = DevAlloc<float>(tr, s);
-    uint32_t* flag = DevAlloc<uint32_t>(1, s);
+    uint32_t* flag = DevAlloc<uint32_t>(2, s);       // non-finite flag, max |g| bits
     int rc = 0;
     EpsB200Status st;
     try {
-      Cu(cudaMemsetAsync(flag, 0, sizeof(uint32_t), s));
+      Cu(cudaMemsetAsync(flag, 0, 2 * sizeof(uint32_t), s));
       Call(eps_b200_route_gather(c->store, R.route, gradients, send, flag, s, &st), st);
-      Call(eps_b200_comm_allreduce_max(c->comm, flag, 1, s, &st), st);
+      Call(eps_b200_comm_allreduce_max(c->comm, flag, 2, s, &st), st);
       // gradient rows: one per kept bag (or key) of every (shard, feature) block
       c->Alltoall(c->comm, send, R.gsend_f, recv, R.grecv_f, 4, s, EPS_B200_EXCHANGE_GRADIENTS);
       rc = eps_b200_serve_push(c->store, R.ticket, recv, R.peer.data(), R.tables.data(),

@@ -135,7 +135,7 @@ struct RouteLaunch {
   float* const* outs;              // [feature_count] merge outputs
   const float* const* grads;       // [feature_count] gradient inputs of the gather
   float* send;                     // gather output (same layout as partials)
-  unsigned int* nonfinite;         // gather: set to 1 if any gradient value is not finite
+  unsigned int* nonfinite;         // gather: [0] set to 1 if a gradient value is not finite, [1] max |g| bits
   unsigned long long* row_pre;          // [shard_count * feature_count] row prefix
   unsigned long long* row_total_dev;    // rows of all blocks (device)
   long long* counts_out;                // [shard_count][5F + 1] count rows (route_layout)
@@ -286,7 +286,9 @@ struct PushLaunch {
   unsigned int dim_max;
   PushControl* control;
   const unsigned int* lookup_error;
-  const unsigned int* external_reject;  // optional device word: nonzero rejects (non-finite input)
+  // optional device words of a sharded round: [0] nonzero rejects (non-finite
+  // input), [1] an upper bound of every |g| (float bits) that replaces the scan
+  const unsigned int* external_reject;
   unsigned long long long_run;     // segments longer than this are reduced in pieces
   int vec, group, iters;           // launch shape (see choose_shape)
   int ring_dim;                    // 32 / 64 / 128: rows updated through the async ring

@@ -63,34 +63,59 @@ __device__ __forceinline__ KeyT key_at(const void* keys, unsigned long long i) {
 }
 
 // ------------------------------------------------------------------ prescan
-// Grid (x, features): blocks of row y scan feature y's gradient values.
+// The gradient values of every feature, in feature order, form one array of
+// grad_values values (grad_prefix[f]: where feature f starts).  Block b scans
+// the contiguous span [b * span, (b + 1) * span) of it, feature after feature,
+// so the grid's parallelism does not depend on how many features the push has
+// (a shard serving 8 requesters x 26 features pushes 208 small tensors).
 __global__ void __launch_bounds__(256) push_prescan(PushLaunch p, PushTable* tables_rw) {
   __shared__ unsigned s_bad, s_max, s_last;
   if (threadIdx.x == 0) { s_bad = 0; s_max = 0; }
   __syncthreads();
-  const PushFeature& F = p.features[blockIdx.y];
-  const unsigned long long nvals = F.rows * (unsigned long long)F.dim;
-  const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
+  const unsigned long long total = p.grad_values;
+  const unsigned fc = p.feature_count;
+  // a multiple of 4 values: with grad_vec4 every feature starts at one too
+  const unsigned long long span = ((total + gridDim.x - 1) / gridDim.x + 3) & ~3ull;
+  unsigned long long lo = blockIdx.x * span;
+  // a sharded round's requesters reduced every gradient value already
+  // (external_reject[1]: their largest |g|): nothing to read here
+  const unsigned long long hi = p.external_reject ? lo : min(total, lo + span);
   unsigned bad = 0;
   float mx = 0.0f;
-  if (p.grad_vec4) {
-    const float4* g4 = reinterpret_cast<const float4*>(F.grad);
-    const unsigned long long n4 = nvals / 4;
+  // the feature holding value `lo`: the last f with grad_prefix[f] <= lo
+  unsigned f = 0;
+  {
+    unsigned a = 0, b = fc;
+    while (b - a > 1) { const unsigned m = (a + b) >> 1; if (p.grad_prefix[m] <= lo) a = m; else b = m; }
+    f = a;
+  }
+  for (; lo < hi && f < fc; ++f) {
+    const unsigned long long f0 = p.grad_prefix[f], f1 = p.grad_prefix[f + 1];
+    const unsigned long long a = max(lo, f0), b = min(hi, f1);
+    if (a < b) {
+      const float* g = p.features[f].grad + (a - f0);
+      if (p.grad_vec4) {
+        const float4* g4 = reinterpret_cast<const float4*>(g);
+        const unsigned long long n4 = (b - a) / 4;
 #pragma unroll 4
-    for (unsigned long long i = blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x; i < n4; i += stride) {
-      const float4 x = __ldg(g4 + i);
-      bad |= !isfinite(x.x) | !isfinite(x.y) | !isfinite(x.z) | !isfinite(x.w);
-      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+        for (unsigned long long i = threadIdx.x; i < n4; i += blockDim.x) {
+          const float4 x = __ldg(g4 + i);
+          bad |= !isfinite(x.x) | !isfinite(x.y) | !isfinite(x.z) | !isfinite(x.w);
+          mx = fmaxf(mx, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+        }
+      } else {
+        for (unsigned long long i = threadIdx.x; i < b - a; i += blockDim.x) {
+          const float x = __ldg(g + i);
+          bad |= !isfinite(x);
+          mx = fmaxf(mx, fabsf(x));
+        }
+      }
     }
-  } else {
-    for (unsigned long long i = blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x; i < nvals; i += stride) {
-      const float x = __ldg(F.grad + i);
-      bad |= !isfinite(x);
-      mx = fmaxf(mx, fabsf(x));
-    }
+    lo = max(lo, b);
   }
   bad = __reduce_or_sync(0xffffffffu, bad);
   unsigned mb = __reduce_max_sync(0xffffffffu, __float_as_uint(mx));
+  if (p.external_reject && threadIdx.x == 0) mb = *(volatile const unsigned*)(p.external_reject + 1);
   if ((threadIdx.x & 31) == 0) {
     if (bad) atomicOr(&s_bad, 1u);
     atomicMax(&s_max, mb);
@@ -100,7 +125,7 @@ __global__ void __launch_bounds__(256) push_prescan(PushLaunch p, PushTable* tab
     if (s_bad) atomicOr(&p.control->nonfinite, 1u);
     atomicMax(&p.control->maxabs_bits, s_max);
     __threadfence();
-    s_last = atomicAdd(&p.control->blocks_done, 1u) == gridDim.x * gridDim.y - 1;
+    s_last = atomicAdd(&p.control->blocks_done, 1u) == gridDim.x - 1;
   }
   __syncthreads();
   if (!s_last || threadIdx.x != 0) return;
@@ -1178,14 +1203,11 @@ cudaError_t run_key(const PushLaunch& p, cudaStream_t s, int part) {
 }  // namespace
 
 cudaError_t launch_push_prescan(const PushLaunch& p, cudaStream_t stream) {
-  // one grid row per feature; enough columns to stream the largest feature, with
-  // about 592 blocks in all: every block ends with atomics on the same words of
-  // the control block, which serialise (cfg3, 26 features: 15,392 blocks, 314 us)
-  const unsigned long long per = 256ull * (p.grad_vec4 ? 16 : 4);
-  const unsigned long long want = (p.grad_max_values + per - 1) / per;
-  const unsigned long long cap = max(1ull, 148ull * 4 / max(1u, p.feature_count));
-  const unsigned gx = (unsigned)max(1ull, min(want, cap));
-  const dim3 grid(gx, max(1u, p.feature_count));
+  // at least 16 values per thread, at most 592 blocks (four per SM): every block
+  // ends with atomics on the same words of the control block, which serialise
+  // (15,392 blocks took 314 us)
+  const unsigned long long want = (p.grad_values + 256ull * 16 - 1) / (256ull * 16);
+  const unsigned grid = p.external_reject ? 1u : (unsigned)max(1ull, min(want, 148ull * 4));
   push_prescan<<<grid, 256, 0, stream>>>(p, const_cast<PushTable*>(p.tables));
   return cudaGetLastError();
 }

@@ -605,19 +605,30 @@ __global__ void __launch_bounds__(256) route_gather(RouteLaunch p) {
     }
   }
   if (!p.nonfinite) return;
-  // every gradient value must be finite, sent or not (distributed_client.cpp:249)
+  // every gradient value must be finite, sent or not (distributed_client.cpp:249);
+  // the largest |g| too, which the owners' pushes take as their overflow bound
+  // instead of reading the received rows again
   const unsigned long long tid = blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x;
   const unsigned long long nthreads = gridDim.x * (unsigned long long)blockDim.x;
   unsigned bad = 0;
+  float mx = 0.0f;
   for (unsigned f = 0; f < fc; ++f) {
     const LookupFeature* F = p.features + f;
     const unsigned long long rows = F->pooling == 2 ? F->key_count : F->bag_count;
     const unsigned long long total = rows * F->dim;
     const float* g = p.grads[f];
-    for (unsigned long long i = tid; i < total; i += nthreads) bad |= !isfinite(g[i]);
+    for (unsigned long long i = tid; i < total; i += nthreads) {
+      const float x = g[i];
+      bad |= !isfinite(x);
+      mx = fmaxf(mx, fabsf(x));
+    }
   }
   bad = __reduce_or_sync(~0u, bad);
-  if (bad && (threadIdx.x & 31) == 0) atomicOr(p.nonfinite, 1u);
+  const unsigned mb = __reduce_max_sync(~0u, __float_as_uint(mx));
+  if ((threadIdx.x & 31) == 0) {
+    if (bad) atomicOr(p.nonfinite, 1u);
+    if (mb) atomicMax(p.nonfinite + 1, mb);
+  }
 }
 
 unsigned grid_for(unsigned long long groups, unsigned per_block) {

@@ -403,9 +403,10 @@ struct EpsB200Store {
   // for the oldest before the next lookup allocates its ticket, so that the
   // ticket memory of a steady stream of rounds stays bounded (and the
   // stream-ordered pool stops growing after the first rounds).
-  static constexpr size_t kMaxInflight = 16;
+  static constexpr size_t kMaxInflight = 16;   // default of max_enqueued_pushes
   void Throttle(cudaStream_t stream) {
-    while (inflight.size() >= kMaxInflight) {
+    const size_t limit = opt.max_enqueued_pushes ? opt.max_enqueued_pushes : kMaxInflight;
+    while (inflight.size() >= limit) {
       auto it = tickets.find(inflight.front());
       if (it == tickets.end() || !it->second.push_in_flight) { inflight.pop_front(); continue; }
       Cuda(cudaEventSynchronize(it->second.done));

@@ -306,7 +306,7 @@ class ShardedClient:
         # one gradient row per kept bag (or key) of every (shard, feature) block
         send_f, recv_f = handle.gsend_f, handle.grecv_f
         send = torch.empty(max(1, int(send_f.sum())), dtype=torch.float32, device=self.device)
-        flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+        flag = torch.zeros(2, dtype=torch.int32, device=self.device)   # non-finite, max |g| bits
         self.store.route_gather(handle.route, gradients, send, flag, main)
         self.dist.all_reduce(flag, op=self.dist.ReduceOp.MAX, group=self.group)
         recv = torch.empty(max(1, int(recv_f.sum())), dtype=torch.float32, device=self.device)

@@ -66,7 +66,10 @@ typedef struct {
   uint64_t partition_epoch;
   uint64_t state_bytes;          /* HBM budget for table state (runtime.hpp:20) */
   uint32_t flags;                /* EPS_B200_FLAG_* */
-  uint32_t reserved;
+  /* Pushes left enqueued (wait == 0) before the next lookup waits for the
+   * oldest: bounds the ticket memory of a caller that runs ahead of the device
+   * (each enqueued push keeps its lookup's slab).  0 = 16. */
+  uint32_t max_enqueued_pushes;
 } EpsB200Options;
 
 /* Sum every coalesced row's gradients serially in occurrence order, as the
@@ -334,9 +337,10 @@ EPS_B200_EXPORT int eps_b200_route_merge(EpsB200Store* store, uint64_t route, co
  * (device, the layout of route_merge's partials) the gradient rows each shard
  * needs: the kept bags' rows of pooled features, the keys' rows of sequence
  * features (deduplicated groups too), shard after shard, feature after feature.
- * If `nonfinite` (device u32, may be NULL) is given, 1 is stored
- * there when any value of any gradient tensor is not finite (the client check
- * of src/client/distributed_client.cpp:249); the caller zeroes it. */
+ * If `nonfinite` (device u32[2], may be NULL) is given, 1 is stored in [0] when
+ * any value of any gradient tensor is not finite (the client check of
+ * src/client/distributed_client.cpp:249) and the largest |value| (float bits)
+ * is max-ed into [1]; the caller zeroes both. */
 EPS_B200_EXPORT int eps_b200_route_gather(EpsB200Store* store, uint64_t route,
                                           const EpsB200Buffer* gradients, float* send,
                                           uint32_t* nonfinite, void* stream, EpsB200Status* status);
@@ -362,9 +366,12 @@ EPS_B200_EXPORT int eps_b200_serve(EpsB200Store* store, const uint64_t* payload,
  * requester's route_gather sent: one row per kept bag (sum/mean) or key
  * (sequence) of every part, requester after requester, feature after feature;
  * peer_counts as for eps_b200_serve.
- * If `reject` (device u32, may be NULL) is nonzero when the push runs, the push
+ * `reject` (device u32[2], may be NULL): the requesters' route_gather words
+ * max-reduced over every rank.  If [0] is nonzero when the push runs, the push
  * is rejected on the device as a non-finite input (state unchanged, ticket
- * live); with wait == 0 that outcome is reported by eps_b200_synchronize. */
+ * live); [1], an upper bound of every |g| of the round, then replaces the
+ * push's own scan of the gradients in its overflow check.  With wait == 0 the
+ * outcome is reported by eps_b200_synchronize. */
 EPS_B200_EXPORT int eps_b200_serve_push(EpsB200Store* store, uint64_t ticket, const float* gradients,
                                         const uint64_t* peer_counts, const uint32_t* tables,
                                         const uint32_t* poolings, uint32_t requesters,
