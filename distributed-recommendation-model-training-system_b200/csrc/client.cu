@@ -348,6 +348,12 @@ int eps_b200_client_prepare(EpsB200Client* c, const EpsB200Feature* features, ui
     Cu(cudaSetDevice(c->device));
     const unsigned n = c->n, F = (unsigned)count, width = 5 * F + 1;
     const cudaStream_t in = static_cast<cudaStream_t>(input_stream);
+    // first the payload exchanges of earlier batches still pending, oldest first
+    // (their counts arrived a call ago): queued ahead of this batch's partition
+    // and count exchange, so that the next lookup, which waits for its batch's
+    // payload, does not also wait behind this batch's count all-to-all
+    for (auto& [pid, Q] : c->prepared)
+      if (!Q.exchanged) c->Exchange(Q, in);
     Prepared P;
     P.F = F;
     P.in = in;
@@ -395,9 +401,6 @@ int eps_b200_client_prepare(EpsB200Client* c, const EpsB200Feature* features, ui
       throw;
     }
     Cu(cudaFreeAsync(rows, in));
-    // the payload exchanges of earlier batches still pending, oldest first
-    for (auto& [id, Q] : c->prepared)
-      if (!Q.exchanged) c->Exchange(Q, in);
     const uint64_t id = c->next++;
     c->prepared.emplace(id, std::move(P));
     *prepared_out = id;
