@@ -797,6 +797,11 @@ def run_b200(args):
     # median), at least 3, at most 150
     head = int(min(150, max(3, np.ceil(1e3 * float(np.median(warm_host)) / 0.04))))
     if dist:
+        # a sharded round runs at about twice its steady time for ~50 ms after
+        # the synchronize (measured at N = 2: the same ~50 ms whether 1, 2 or 3
+        # batches are prepared ahead; a longer head start shortens it by its own
+        # length): at N > 1 the head start covers 60 ms
+        head = max(head, 1500)
         t = torch.tensor([head], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)      # the same count on every rank
         head = int(t.item())
