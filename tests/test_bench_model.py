@@ -77,3 +77,41 @@ def test_dominant_kernel_is_the_longest_phase_with_bytes():
     assert bench.dominant_kernel(prof, bm) == "lookup"      # the sort and pieces have no bytes
     prof["apply"]["ms"] = 2.5
     assert bench.dominant_kernel(prof, bm) == "apply"
+
+
+def test_default_config_per_world_size():
+    """Config 2 at N = 1 (the single-GPU config), config 3 at N > 1 (the one
+    BASELINE measures at 1/2/4/8 GPUs); an explicit --config wins."""
+    bench = load_bench()
+    import argparse
+    for world, want in ((1, 2), (2, 3), (8, 3)):
+        a = argparse.Namespace(config=None)
+        assert bench.resolve_config(a, world) == want and a.config_default
+    a = argparse.Namespace(config=5)
+    assert bench.resolve_config(a, 8) == 5 and not a.config_default
+
+
+def test_gradient_free_parts_keep_the_keys(workloads):
+    """Other ranks' parts are generated without gradients; their keys (drawn
+    first from the same seeded stream) must equal the full generation's."""
+    for make in (lambda g: workloads.config2(seed=7, rows=100_000, batch=64, gradients=g),
+                 lambda g: workloads.config3(seed=7, batch=64, row_scale=1e-3, gradients=g),
+                 lambda g: workloads.config4(seed=7, rows=100_000, n=256, gradients=g),
+                 lambda g: workloads.config5(seed=7, rows=100_000, batch=64, gradients=g)):
+        full, keys_only = make(True), make(False)
+        assert all(g is None for g in keys_only.gradients)
+        for a, b in zip(full.features, keys_only.features):
+            assert np.array_equal(a.keys, b.keys) and np.array_equal(a.offsets, b.offsets)
+
+
+def test_scaled_batch_and_samples():
+    """The parity and reference samples shrink the per-rank batch in proportion,
+    never below one sample; config 1's fixed batch is never scaled."""
+    bench = load_bench()
+    import argparse
+    a = argparse.Namespace(config=3, batch=0)
+    assert bench.scaled_batch(a, 1.0) == 0                    # 0: the configured batch
+    assert bench.scaled_batch(a, 0.25) == 65536 // 4
+    assert bench.scaled_batch(a, 1e-9) == 1
+    a = argparse.Namespace(config=1, batch=0)
+    assert bench.scaled_batch(a, 0.1) == 0
