@@ -8,8 +8,8 @@ through its DistributedClient over `world` CpuParameterService shards, i.e. with
 the same shard count, so that pooled outputs merge the same shard partials in the
 same order (src/client/distributed_client.cpp:173-188,227-232).
 
-Bars (gather and coalescing bit-exact, Adam within the
-tolerance of a different summation order):
+Bars (the path's parity target: gather and coalescing bit-exact, Adam within
+the tolerance of a different summation order):
   * pooled / sequence outputs of this rank's features: bit-exact;
   * w, m, v and row_updates of every touched row this rank owns (key % world ==
     rank): bit-exact for rows whose occurrences in the combined request number

@@ -80,8 +80,8 @@ def test_dominant_kernel_is_the_longest_phase_with_bytes():
 
 
 def test_default_config_per_world_size():
-    """Config 2 at N = 1 (the single-GPU config), config 3 at N > 1 (the one
-    BASELINE measures at 1/2/4/8 GPUs); an explicit --config wins."""
+    """Config 2 at N = 1 (the single-GPU config), config 3 at N > 1 (the
+    26-table config measured at 1/2/4/8 GPUs); an explicit --config wins."""
     bench = load_bench()
     import argparse
     for world, want in ((1, 2), (2, 3), (8, 3)):
