@@ -106,6 +106,10 @@ struct LookupLaunch {
   float* row_scale;                // [gradient rows]
   unsigned int* error;             // LookupErrorBits
   int vec, group, iters;           // launch shape (see choose_shape)
+  // emit only: the coalescing sort's digit histograms (hist[pass][256] of the
+  // composite keys, zeroed), counted as the keys are written; null: not counted
+  unsigned int* digit_hist;
+  unsigned int digit_passes;
 };
 cudaError_t launch_lookup(const LookupLaunch& p, cudaStream_t stream);
 // Occurrence list of a non-read-only lookup (one launch, before the gather).
@@ -170,6 +174,7 @@ struct SortLaunch {
   unsigned int* scratch;           // sort_scratch_bytes(n, bits), 256-byte aligned, zeroed
   unsigned int tiles;              // sort_tiles(n)
   unsigned int* error;             // set (kLookupSortFailed) if a look-back wait ran out
+  int hist_ready;                  // the scratch's digit histograms are already counted
 };
 // Stable LSD radix sort; returns in *swapped whether the result is in the alt
 // buffers.

@@ -361,14 +361,28 @@ __global__ void __launch_bounds__(256, EPS_LOOKUP_MIN_BLOCKS) lookup_kernel(Look
 // kUnitPositions consecutive positions plus the same span of offsets, which it
 // validates (a sequence feature's bags do not shape its outputs).  So neither a
 // very long bag nor many one-key bags serialise on one warp.
+constexpr int kEmitSteps = 4;   // 32-entry steps whose keys load together
+
 template <typename KeyT>
-__global__ void __launch_bounds__(256) emit_kernel(LookupLaunch p) {
+__global__ void __launch_bounds__(256, 4) emit_kernel(LookupLaunch p) {
   __shared__ unsigned long long s_unit_base[kMaxFeatures + 1];
   __shared__ unsigned s_kept[8][kEmitShortBags];
+  __shared__ unsigned s_hist[8][256];   // the sort's digit histograms, block part
   const unsigned fc = p.feature_count;
+  const unsigned passes = p.digit_hist ? p.digit_passes : 0u;
   for (unsigned i = threadIdx.x; i < fc; i += blockDim.x) s_unit_base[i] = p.features[i].emit_base;
+  for (unsigned i = threadIdx.x; i < passes * 256u; i += blockDim.x) (&s_hist[0][0])[i] = 0;
   if (threadIdx.x == 0) s_unit_base[fc] = p.emit_total;
   __syncthreads();
+  // the sort's digits of a key this lane wrote (shared-memory atomics; warp
+  // aggregation by __match_any_sync, or a vote for digits shared by the whole
+  // step, measured slower on every config)
+  auto count_digits = [&](KeyT ck, bool valid) {
+    if (valid)
+      for (unsigned q = 0; q < passes; ++q) atomicAdd(&s_hist[q][(unsigned)(ck >> (8 * q)) & 255u], 1u);
+  };
+
+
   const unsigned lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const unsigned long long warp = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) >> 5;
   const unsigned long long nwarps = (gridDim.x * (unsigned long long)blockDim.x) >> 5;
@@ -403,18 +417,28 @@ __global__ void __launch_bounds__(256) emit_kernel(LookupLaunch p) {
       return KeyT(0);
     };
     if (F->pooling == 2) {
-      // positions [lu * kUnitPositions, ...) and the offsets with the same indices
+      // positions [lu * kUnitPositions, ...) and the offsets with the same indices;
+      // every slice's keys are requested before the first store (a store might
+      // alias the keys, so the compiler would not move a later load above it)
       const unsigned long long base = lu * kUnitPositions;
-#pragma unroll 1
+      unsigned long long kq[kUnitSlices];
+#pragma unroll
       for (unsigned q = 0; q < kUnitSlices; ++q) {
         const unsigned long long i = base + q * 32 + lane;
+        kq[q] = i < key_count ? F->keys[i] : 0ull;
+      }
+#pragma unroll
+      for (unsigned q = 0; q < kUnitSlices; ++q) {
+        const unsigned long long i = base + q * 32 + lane;
+        KeyT ck = KeyT(0);
         if (i < key_count) {
           bool pad;
-          const KeyT ck = composite(F->keys[i], i, &pad);
+          ck = composite(kq[q], i, &pad);
           static_cast<KeyT*>(p.occ_key)[occ_base + i] = ck;
           p.occ_src[occ_base + i] = src_hi | (unsigned)i;
           p.row_scale[F->scale_base + i] = 1.0f;
         }
+        count_digits(ck, i < key_count);
         if (B > 0 && i <= B) {
           const unsigned long long o = F->offsets[i];
           if (i == 0 && o != 0) err |= kLookupBadOffsets;
@@ -449,24 +473,40 @@ __global__ void __launch_bounds__(256) emit_kernel(LookupLaunch p) {
     const unsigned excl = incl - n;       // bag's first entry in the unit's run
     s_kept[w][lane] = 0;
     __syncwarp();
-    for (unsigned c0 = 0; c0 < total; c0 += 32) {
-      const unsigned i = c0 + lane;
-      // bag of entry i: the last bag whose first entry is <= i (binary lifting
-      // over the lanes' non-decreasing first entries; bag 0's is 0)
-      unsigned k = 0;
-      for (unsigned step = ub >> 1; step; step >>= 1) {
-        const unsigned ek = __shfl_sync(0xffffffffu, excl, k + step);
-        if (k + step < nb && ek <= i) k += step;
+    // kEmitSteps steps of 32 entries at a time: their keys are requested
+    // before the first store (see the sequence branch)
+#pragma unroll 1
+    for (unsigned c0 = 0; c0 < total; c0 += 32 * kEmitSteps) {
+      unsigned long long kq[kEmitSteps];
+      unsigned occ[kEmitSteps], kb[kEmitSteps];   // a feature holds fewer than 2^31 keys
+#pragma unroll
+      for (int q = 0; q < kEmitSteps; ++q) {
+        const unsigned i = c0 + q * 32 + lane;
+        // bag of entry i: the last bag whose first entry is <= i (binary lifting
+        // over the lanes' non-decreasing first entries; bag 0's is 0)
+        unsigned k = 0;
+        for (unsigned step = ub >> 1; step; step >>= 1) {
+          const unsigned ek = __shfl_sync(0xffffffffu, excl, k + step);
+          if (k + step < nb && ek <= i) k += step;
+        }
+        const unsigned long long sk = __shfl_sync(0xffffffffu, s, k);
+        const unsigned ek = __shfl_sync(0xffffffffu, excl, k);
+        kb[q] = k;
+        occ[q] = (unsigned)(sk + (i - ek));
+        kq[q] = i < total ? F->keys[occ[q]] : 0ull;
       }
-      const unsigned long long sk = __shfl_sync(0xffffffffu, s, k);
-      const unsigned ek = __shfl_sync(0xffffffffu, excl, k);
-      if (i < total) {
-        const unsigned long long occ = sk + (i - ek);
-        bool pad;
-        const KeyT ck = composite(F->keys[occ], occ, &pad);
-        static_cast<KeyT*>(p.occ_key)[occ_base + occ] = ck;
-        p.occ_src[occ_base + occ] = src_hi | (unsigned)(b0 + k);
-        if (has_pad && !pad) atomicAdd(&s_kept[w][k], 1u);
+#pragma unroll
+      for (int q = 0; q < kEmitSteps; ++q) {
+        const bool valid = c0 + q * 32 + lane < total;
+        KeyT ck = KeyT(0);
+        if (valid) {
+          bool pad;
+          ck = composite(kq[q], occ[q], &pad);
+          static_cast<KeyT*>(p.occ_key)[occ_base + occ[q]] = ck;
+          p.occ_src[occ_base + occ[q]] = src_hi | (unsigned)(b0 + kb[q]);
+          if (has_pad && !pad) atomicAdd(&s_kept[w][kb[q]], 1u);
+        }
+        count_digits(ck, valid);
       }
     }
     __syncwarp();
@@ -484,6 +524,13 @@ __global__ void __launch_bounds__(256) emit_kernel(LookupLaunch p) {
   }
   err = __reduce_or_sync(~0u, err);
   if (err && lane == 0) atomicOr(p.error, err);
+  if (passes) {
+    __syncthreads();
+    for (unsigned i = threadIdx.x; i < passes * 256u; i += blockDim.x) {
+      const unsigned c = (&s_hist[0][0])[i];
+      if (c) atomicAdd(p.digit_hist + i, c);
+    }
+  }
 }
 
 template <int G, int VEC, int ITERS>

@@ -932,6 +932,10 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         lp.occ_key = P(at_k0);
         lp.occ_src = reinterpret_cast<unsigned*>(P(at_s0));
         lp.row_scale = reinterpret_cast<float*>(P(at_scale));
+        // the sort's digit histograms are counted by the emit kernel (the sort
+        // scratch they start was zeroed above)
+        lp.digit_hist = reinterpret_cast<unsigned*>(P(at_hist));
+        lp.digit_passes = (key_bits + 7) / 8;
       }
       cudaEvent_t ev = nullptr;
       if (!read_only) {
@@ -964,7 +968,7 @@ int eps_b200_lookup(EpsB200Store* store, const EpsB200Feature* features, uint64_
         Cuda(cudaStreamWaitEvent(s.side, s.fork, 0));
         SortLaunch sp{P(at_k0), P(at_k1), reinterpret_cast<unsigned*>(P(at_s0)),
                       reinterpret_cast<unsigned*>(P(at_s1)), total_keys, key_bits,
-                      key64, reinterpret_cast<unsigned*>(P(at_hist)), stiles, err};
+                      key64, reinterpret_cast<unsigned*>(P(at_hist)), stiles, err, 1};
         int swapped = 0;
         ev = s.Begin(sort_stream);
         Cuda(launch_sort(sp, sort_stream, &swapped));

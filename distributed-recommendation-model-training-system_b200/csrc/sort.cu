@@ -38,7 +38,8 @@ constexpr unsigned long long kFlagAggregate = 1ull << 32;
 constexpr unsigned long long kFlagPrefix = 2ull << 32;
 constexpr unsigned kSpinLimit = 1u << 22;
 
-// Global digit histograms of all passes: hist[pass][256].
+// Global digit histograms of all passes: hist[pass][256] (a lookup's emit kernel
+// counts them as it writes the keys; this kernel serves the other sorts).
 template <typename KeyT>
 __global__ void __launch_bounds__(kThreads) digit_histograms(const KeyT* keys, unsigned long long n,
                                                              unsigned passes, unsigned* hist) {
@@ -394,8 +395,10 @@ cudaError_t run_sort(const SortLaunch& p, cudaStream_t s, int* swapped) {
   unsigned long long* status = reinterpret_cast<unsigned long long*>(
       reinterpret_cast<char*>(p.scratch) + sort_scratch_header(passes));
   // the caller hands over zeroed scratch (sort_scratch_bytes)
-  const unsigned long long hist_grid = min(148ull * EPS_HIST_BLOCKS_PER_SM, (p.n + kThreads - 1) / kThreads);
-  digit_histograms<KeyT><<<(unsigned)hist_grid, kThreads, 0, s>>>(k0, p.n, passes, hist);
+  if (!p.hist_ready) {
+    const unsigned long long hist_grid = min(148ull * EPS_HIST_BLOCKS_PER_SM, (p.n + kThreads - 1) / kThreads);
+    digit_histograms<KeyT><<<(unsigned)hist_grid, kThreads, 0, s>>>(k0, p.n, passes, hist);
+  }
   const size_t smem = sizeof(OnesweepSmem<KeyT>);
   static bool attr_set[64] = {};
   int dev = 0;
@@ -567,7 +570,7 @@ size_t sort_scratch_bytes(unsigned long long n, unsigned bits) {
 }
 
 unsigned int sort_launch_count(const SortLaunch& p) {
-  return p.n <= 1 ? 0u : 1u + (p.bits + 7) / 8;
+  return p.n <= 1 ? 0u : (p.hist_ready ? 0u : 1u) + (p.bits + 7) / 8;
 }
 
 cudaError_t launch_sort(const SortLaunch& p, cudaStream_t stream, int* swapped) {
