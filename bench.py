@@ -672,6 +672,8 @@ def scale_base_rounds(eps, torch, wl, args, dev, local_rank):
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in range(args.steps)]
         torch.cuda.synchronize()
+        for _ in range(250):          # the main rounds' head start (10 ms of flushes)
+            flush.zero_()
         for a, b in ev:
             flush.zero_()
             a.record(stream)
@@ -794,8 +796,12 @@ def run_b200(args):
     # ~40 us of device work each, queued before round 0's start event) give the
     # host the head start it has in steady state, so that round 0 does not wait
     # for its own enqueue: enough to cover one round's host time (the warm-up's
-    # median), at least 3, at most 150
-    head = int(min(150, max(3, np.ceil(1e3 * float(np.median(warm_host)) / 0.04))))
+    # median), and at least 250 (10 ms): the timed rounds' whole enqueue (~2 ms
+    # at N = 1) then ends before the first of them starts, so that a host stall
+    # of a few milliseconds (an nvidia-smi query holds the driver; one of 8.5 ms
+    # fell on the third timed round of a default run) cannot leave the device idle
+    # inside a timed round
+    head = int(min(1500, max(250, np.ceil(1e3 * float(np.median(warm_host)) / 0.04))))
     if dist:
         # a sharded round runs at about twice its steady time for ~50 ms after
         # the synchronize (measured at N = 2: the same ~50 ms whether 1, 2 or 3
