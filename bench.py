@@ -237,6 +237,26 @@ def scaled_batch(args, frac):
     return max(1, int(full * frac))
 
 
+FLUSH_S = 40e-6   # device time of one L2 flush (a 256 MiB fill)
+
+
+def head_start_flushes(round_host_s, world):
+    """L2 flushes queued (untimed) before the first timed round, so that the host
+    starts the timed rounds with the lead it has in steady state.
+
+    At least one round's host time, and at least 250 (10 ms): the timed rounds'
+    whole enqueue (~2 ms at N = 1) then ends before the first of them starts, so
+    that a host stall of a few milliseconds (an nvidia-smi query holds the
+    driver; one of 8.5 ms fell on the third timed round of a default run with a
+    3-flush head start) cannot leave the device idle inside a timed round; at
+    most 1,500.  At N > 1 exactly 1,500 (60 ms): after the synchronize a sharded
+    round runs at about twice its steady time for ~50 ms (measured at N = 2, the
+    same whether 1, 2 or 3 batches are prepared ahead), and a longer head start
+    shortens that transient by its own length."""
+    head = int(min(1500, max(250, np.ceil(round_host_s / FLUSH_S))))
+    return max(head, 1500) if world > 1 else head
+
+
 def job_features(parts):
     """Every rank's features as the one combined request (ids r * F + f)."""
     F = len(parts[0].features)
@@ -672,7 +692,7 @@ def scale_base_rounds(eps, torch, wl, args, dev, local_rank):
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in range(args.steps)]
         torch.cuda.synchronize()
-        for _ in range(250):          # the main rounds' head start (10 ms of flushes)
+        for _ in range(head_start_flushes(0.0, 1)):   # the main rounds' head start
             flush.zero_()
         for a, b in ev:
             flush.zero_()
@@ -793,21 +813,10 @@ def run_b200(args):
               for _ in range(args.steps)]
     torch.cuda.synchronize()
     # after the synchronize the device queue is empty: extra L2 flushes (untimed,
-    # ~40 us of device work each, queued before round 0's start event) give the
-    # host the head start it has in steady state, so that round 0 does not wait
-    # for its own enqueue: enough to cover one round's host time (the warm-up's
-    # median), and at least 250 (10 ms): the timed rounds' whole enqueue (~2 ms
-    # at N = 1) then ends before the first of them starts, so that a host stall
-    # of a few milliseconds (an nvidia-smi query holds the driver; one of 8.5 ms
-    # fell on the third timed round of a default run) cannot leave the device idle
-    # inside a timed round
-    head = int(min(1500, max(250, np.ceil(1e3 * float(np.median(warm_host)) / 0.04))))
+    # queued before round 0's start event) give the host its steady-state head
+    # start (see head_start_flushes)
+    head = head_start_flushes(float(np.median(warm_host)), world)
     if dist:
-        # a sharded round runs at about twice its steady time for ~50 ms after
-        # the synchronize (measured at N = 2: the same ~50 ms whether 1, 2 or 3
-        # batches are prepared ahead; a longer head start shortens it by its own
-        # length): at N > 1 the head start covers 60 ms
-        head = max(head, 1500)
         t = torch.tensor([head], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)      # the same count on every rank
         head = int(t.item())

@@ -115,3 +115,17 @@ def test_scaled_batch_and_samples():
     assert bench.scaled_batch(a, 1e-9) == 1
     a = argparse.Namespace(config=1, batch=0)
     assert bench.scaled_batch(a, 0.1) == 0
+
+
+def test_head_start_covers_host_stalls():
+    """The untimed flushes queued before the first timed round: at N = 1 at least
+    10 ms (250 flushes of 40 us), more when one round's host time is longer, at
+    most 60 ms; at N > 1 always 60 ms (1,500 flushes)."""
+    bench = load_bench()
+    assert bench.head_start_flushes(90e-6, 1) == 250            # a cfg2 round's host time
+    assert bench.head_start_flushes(0.0, 1) == 250
+    assert bench.head_start_flushes(20e-3, 1) == 500            # 20 ms of host time per round
+    assert bench.head_start_flushes(1.0, 1) == 1500
+    for world in (2, 8):
+        assert bench.head_start_flushes(90e-6, world) == 1500
+    assert 250 * bench.FLUSH_S >= 10e-3
